@@ -1,0 +1,14 @@
+"""B200 (sm_100a) MoE block forward for AGILLM4.1.
+
+Import as ``agillm41_b200`` (the repository-root alias for this directory).
+
+* :class:`MoEFFN` - drop-in for the reference ``MoEFFN`` (agillm41.py:4323-4460)
+* :func:`install` - rebind the reference runtime's ``MoEFFN`` to the B200 forward
+* :mod:`.ops`     - one Python entry point per kernel stage, plus the fused forward
+* :mod:`._lib`    - the ctypes binding of ``lib/libagillm_moe.so``
+"""
+from ._lib import LIB_PATH, MoEKernelError, load  # noqa: F401
+from .moe import MoEFFN, install, uninstall  # noqa: F401
+from . import ops  # noqa: F401
+
+__all__ = ["MoEFFN", "install", "uninstall", "ops", "load", "LIB_PATH", "MoEKernelError"]

@@ -1,0 +1,107 @@
+"""ctypes binding of ``lib/libagillm_moe.so`` (the C ABI in ``include/agillm_moe.h``).
+
+The library is the only compute path: there is no CPU or PyTorch fallback.
+If it cannot be loaded, or a tensor is not a CUDA tensor, the call raises.
+Torch tensors cross the boundary as raw device pointers; every launch goes on
+the current torch CUDA stream.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Optional
+
+import torch
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libagillm_moe.so")
+
+AGM_F32, AGM_BF16, AGM_F16 = 0, 1, 2
+AGM_OK = 0
+AGM_TILE_M = 128
+AGM_DISPATCH_BLOCK = 256
+AGM_MAX_EXPERTS = 16
+AGM_FLAG_TIE_SWAP = 0x1
+AGM_STAGE_EVENTS = 8
+
+_DTYPE_CODE = {torch.float32: AGM_F32, torch.bfloat16: AGM_BF16, torch.float16: AGM_F16}
+
+# Exported entry points and their C signatures (must match include/agillm_moe.h).
+_P, _I, _I64, _SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t
+SIGNATURES = {
+    "agm_last_error": (ctypes.c_char_p, []),
+    "agm_abi_version": (_I, []),
+    "agm_dispatch_blocks": (_I64, [_I64]),
+    "agm_max_rows": (_I64, [_I64, _I, _I]),
+    "agm_router_topk": (_I, [_P, _P, _I, _I64, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P]),
+    "agm_dispatch_plan": (_I, [_P, _I64, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "agm_permute": (_I, [_P, _I, _I64, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "agm_grouped_gemm": (_I, [_P, _I64, _P, _P, _I, _I, _I, _I, _P, _P, _I64, _I, _I, _P, _I64, _P, _P]),
+    "agm_combine": (_I, [_P, _P, _P, _I, _I64, _I, _I, _P, _I, _I64, _P, _P]),
+    "agm_moe_workspace_bytes": (_SZ, [_I64, _I, _I, _I, _I, _I, _I, _I]),
+    "agm_moe_forward": (_I, [_P, _I, _I64, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _P, _P,
+                             _P, _SZ, _I, _P, _P, _P, _P, _P, _P]),
+    "agm_read_device_error": (_I, [_P, _P, _P]),
+}
+
+
+class MoEKernelError(RuntimeError):
+    """A C-ABI call returned an error (bad argument, CUDA error, device error word)."""
+
+
+_lib: Optional[ctypes.CDLL] = None
+
+
+def load() -> ctypes.CDLL:
+    """Load the shared library (once). Raises if it is missing."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise MoEKernelError(
+                f"{LIB_PATH} is missing: build it with `python agillm4.1_b200/build.py` "
+                "(nvcc, sm_100a). There is no fallback path.")
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        if lib.agm_abi_version() != 1:
+            raise MoEKernelError("libagillm_moe.so ABI version mismatch")
+        _lib = lib
+    return _lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != AGM_OK:
+        msg = load().agm_last_error().decode(errors="replace")
+        raise MoEKernelError(f"{what} failed ({rc}): {msg}")
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    try:
+        return _DTYPE_CODE[dt]
+    except KeyError:
+        raise MoEKernelError(f"unsupported dtype {dt}; expected float32, bfloat16 or float16") from None
+
+
+def ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise MoEKernelError("CUDA tensors only: the MoE kernels have no CPU path")
+    if not t.is_contiguous():
+        raise MoEKernelError("tensors passed to the MoE kernels must be contiguous")
+    return t.data_ptr()
+
+
+def stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def read_device_error(err: torch.Tensor) -> int:
+    """Synchronise the current stream and return (and clear) a device error word."""
+    code = ctypes.c_int(0)
+    lib = load()
+    rc = lib.agm_read_device_error(ptr(err), ctypes.byref(code), stream_handle(err.device))
+    if rc != AGM_OK and code.value == 0:
+        check(rc, "agm_read_device_error")
+    return int(code.value)

@@ -1,0 +1,135 @@
+// K4: gate-weighted combine back to token order (+ shared experts).
+//
+// Replaces agillm41.py:4420-4430:
+//   out = zeros_like(flat)
+//   for rank: out.index_add_(0, rows, expert(x[rows]) * w[rows])   (4428)
+//   out = out + (shared[0](flat) + shared[1](flat) + ...)          (4429-4430)
+// In bf16/fp16 mode every op rounds to the activation dtype: the product
+// y*w, each index_add_ accumulation (rank 0 first, then rank 1, ...), each
+// shared-expert sum and the final add. This kernel keeps exactly that chain
+// (fp32 arithmetic, rounded to T after every op), so with identical expert
+// outputs it reproduces the reference bit for bit.
+//
+// Layout: a warp per token (grid-stride); lanes stream 16-byte chunks of the
+// k gathered rows of y_perm and write the token's output row once.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace agm {
+
+template <typename T, int K_MAX>
+__global__ void __launch_bounds__(256) combine_kernel(const T* __restrict__ y_perm, const int32_t* __restrict__ row_of,
+                                                      const T* __restrict__ gates, int64_t n_tokens, int d, int k,
+                                                      const T* __restrict__ shared_y, int n_shared,
+                                                      int64_t shared_stride, T* __restrict__ out) {
+  constexpr int CH = 16 / sizeof(T);
+  const int nchunk = d / CH;
+  const int lane = lane_id();
+  const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
+  for (int64_t tok = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + warp_id(); tok < n_tokens;
+       tok += warps_total) {
+    int rows[K_MAX];
+    float g[K_MAX];
+#pragma unroll
+    for (int r = 0; r < K_MAX; ++r) {
+      if (r < k) {
+        rows[r] = row_of[tok * k + r];
+        g[r] = Traits<T>::to_f(gates[tok * k + r]);
+      } else {
+        rows[r] = -1;
+        g[r] = 0.f;
+      }
+    }
+    for (int c = lane; c < nchunk; c += 32) {
+      float acc[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+      uint4 v[K_MAX];
+#pragma unroll
+      for (int r = 0; r < K_MAX; ++r)
+        if (r < k && rows[r] >= 0) v[r] = __ldg(reinterpret_cast<const uint4*>(y_perm + static_cast<int64_t>(rows[r]) * d) + c);
+#pragma unroll
+      for (int r = 0; r < K_MAX; ++r) {
+        if (r < k && rows[r] >= 0) {
+          float f[8];
+          if constexpr (sizeof(T) == 4) {
+            f[0] = __uint_as_float(v[r].x); f[1] = __uint_as_float(v[r].y);
+            f[2] = __uint_as_float(v[r].z); f[3] = __uint_as_float(v[r].w);
+          } else {
+            unpack8<T>(v[r], f);
+          }
+#pragma unroll
+          for (int j = 0; j < CH; ++j) acc[j] = round_to<T>(acc[j] + round_to<T>(f[j] * g[r]));
+        }
+      }
+      if (n_shared > 0) {
+        float s[8];
+        for (int si = 0; si < n_shared; ++si) {
+          const uint4 u = __ldg(reinterpret_cast<const uint4*>(shared_y + si * shared_stride + tok * d) + c);
+          float f[8];
+          if constexpr (sizeof(T) == 4) {
+            f[0] = __uint_as_float(u.x); f[1] = __uint_as_float(u.y);
+            f[2] = __uint_as_float(u.z); f[3] = __uint_as_float(u.w);
+          } else {
+            unpack8<T>(u, f);
+          }
+#pragma unroll
+          for (int j = 0; j < CH; ++j) s[j] = (si == 0) ? f[j] : round_to<T>(s[j] + f[j]);
+        }
+#pragma unroll
+        for (int j = 0; j < CH; ++j) acc[j] = round_to<T>(acc[j] + s[j]);
+      }
+      uint4 o;
+      if constexpr (sizeof(T) == 4) {
+        o = make_uint4(__float_as_uint(acc[0]), __float_as_uint(acc[1]), __float_as_uint(acc[2]),
+                       __float_as_uint(acc[3]));
+      } else {
+        o = make_uint4(pack2<T>(acc[0], acc[1]), pack2<T>(acc[2], acc[3]), pack2<T>(acc[4], acc[5]),
+                       pack2<T>(acc[6], acc[7]));
+      }
+      reinterpret_cast<uint4*>(out + tok * d)[c] = o;
+    }
+  }
+}
+
+template <typename T>
+static cudaError_t launch_combine(const void* y, const int32_t* row_of, const void* gates, int64_t n, int d, int k,
+                                  const void* shared_y, int n_shared, int64_t shared_stride, void* out, int num_sms,
+                                  cudaStream_t stream) {
+  const int64_t warps_needed = n;
+  const int64_t blocks = std::min<int64_t>((warps_needed + 7) / 8, static_cast<int64_t>(num_sms) * 8);
+  if (blocks <= 0) return cudaSuccess;
+  const T* ys = static_cast<const T*>(y);
+  const T* gs = static_cast<const T*>(gates);
+  const T* sh = static_cast<const T*>(shared_y);
+  T* o = static_cast<T*>(out);
+  if (k <= 2)
+    combine_kernel<T, 2><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(ys, row_of, gs, n, d, k, sh, n_shared,
+                                                                            shared_stride, o);
+  else if (k <= 4)
+    combine_kernel<T, 4><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(ys, row_of, gs, n, d, k, sh, n_shared,
+                                                                            shared_stride, o);
+  else
+    combine_kernel<T, 16><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(ys, row_of, gs, n, d, k, sh, n_shared,
+                                                                             shared_stride, o);
+  return cudaGetLastError();
+}
+
+cudaError_t combine(int dtype, const void* y, const int32_t* row_of, const void* gates, int64_t n, int d, int k,
+                    const void* shared_y, int n_shared, int64_t shared_stride, void* out, int num_sms,
+                    cudaStream_t stream) {
+  switch (dtype) {
+    case AGM_F32:
+      return launch_combine<float>(y, row_of, gates, n, d, k, shared_y, n_shared, shared_stride, out, num_sms, stream);
+    case AGM_BF16:
+      return launch_combine<__nv_bfloat16>(y, row_of, gates, n, d, k, shared_y, n_shared, shared_stride, out, num_sms,
+                                           stream);
+    case AGM_F16:
+      return launch_combine<__half>(y, row_of, gates, n, d, k, shared_y, n_shared, shared_stride, out, num_sms,
+                                    stream);
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace agm

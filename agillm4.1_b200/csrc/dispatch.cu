@@ -1,0 +1,209 @@
+// K2: expert histogram -> prefix sums -> stable scatter permutation.
+//
+// Replaces the reference's dispatch loop (agillm41.py:4421-4428): for every
+// (rank, expert) it runs `nonzero` (a device->host sync) and `index_select`.
+// Here the whole dispatch is two kernels and no host sync:
+//
+// * dispatch_plan_kernel (one CTA): per expert, an exclusive scan of the
+//   per-block histograms written by the router kernel gives each dispatch
+//   block its base offset inside the expert's segment; per-expert counts;
+//   segment starts padded to the GEMM row tile; the row-tile -> expert table
+//   and the number of row tiles (read by the persistent GEMM on the device).
+// * permute_kernel (one CTA per dispatch block of 256 tokens, plus one CTA per
+//   expert that zero-fills the segment's padding rows): warp ballots give each
+//   (token, rank) its rank among the block's tokens routed to the same expert,
+//   in ascending token order, so the permutation is deterministic and equals
+//   the reference's ascending `nonzero` order. Rows of x are copied with
+//   16-byte vector loads/stores to every destination row of the token.
+//
+// Output layout in HBM: x_perm [max_rows, d] (expert segments back to back,
+// each padded to a multiple of 128 rows), row_of [N, k] (destination row of
+// each (token, rank)), token_of [max_rows] (source token of each row, -1 for
+// padding rows).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace agm {
+
+constexpr int kTile = AGM_TILE_M;
+constexpr int kBlk = AGM_DISPATCH_BLOCK;
+constexpr int kPlanThreads = 512;
+
+__global__ void __launch_bounds__(kPlanThreads) dispatch_plan_kernel(
+    const int32_t* __restrict__ block_hist, int n_blocks, int E, int64_t max_rows, int max_tiles,
+    int32_t* __restrict__ block_off, int32_t* __restrict__ counts, int32_t* __restrict__ seg_start,
+    int32_t* __restrict__ tile_expert, int32_t* __restrict__ num_tiles, int32_t* __restrict__ token_of, int* err) {
+  __shared__ int tot_s[32];
+  __shared__ int seg_s[33];
+  const int warp = warp_id(), lane = lane_id();
+  const int nwarps = blockDim.x / 32;
+  // 1. Per-expert exclusive scan over blocks (one warp per expert).
+  for (int e = warp; e < E; e += nwarps) {
+    int carry = 0;
+    for (int b0 = 0; b0 < n_blocks; b0 += 32) {
+      const int b = b0 + lane;
+      const int v = (b < n_blocks) ? block_hist[static_cast<int64_t>(b) * E + e] : 0;
+      int incl = v;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += n;
+      }
+      if (b < n_blocks) block_off[static_cast<int64_t>(b) * E + e] = carry + incl - v;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) tot_s[e] = carry;
+  }
+  __syncthreads();
+  // 2. Padded segment starts.
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int e = 0; e < E; ++e) {
+      seg_s[e] = acc;
+      acc += (tot_s[e] + kTile - 1) / kTile * kTile;
+    }
+    seg_s[E] = acc;
+    if (acc > max_rows || acc / kTile > max_tiles) raise_error(err, kErrRowOverflow);
+  }
+  __syncthreads();
+  const int total_rows = min(static_cast<int64_t>(seg_s[E]), max_rows);
+  const int ntiles = total_rows / kTile;
+  if (threadIdx.x < E) counts[threadIdx.x] = tot_s[threadIdx.x];
+  if (threadIdx.x <= E) seg_start[threadIdx.x] = seg_s[threadIdx.x];
+  if (threadIdx.x == 0) *num_tiles = ntiles;
+  // 3. Tile table and padding rows of token_of.
+  for (int m = threadIdx.x; m < ntiles; m += blockDim.x) {
+    const int row = m * kTile;
+    int e = 0;
+    while (e + 1 < E && seg_s[e + 1] <= row) ++e;
+    tile_expert[m] = e;
+  }
+  for (int e = 0; e < E; ++e) {
+    const int p0 = seg_s[e] + tot_s[e], p1 = min(seg_s[e + 1], total_rows);
+    for (int r = p0 + threadIdx.x; r < p1; r += blockDim.x) token_of[r] = -1;
+  }
+}
+
+template <int K_MAX>
+__global__ void __launch_bounds__(kBlk) permute_kernel(
+    const uint4* __restrict__ x, int64_t n_tokens, int nchunk /* 16-byte chunks per row */, int k, int E,
+    int n_blocks, const int32_t* __restrict__ idx, const int32_t* __restrict__ block_off,
+    const int32_t* __restrict__ seg_start, const int32_t* __restrict__ counts, int64_t max_rows,
+    uint4* __restrict__ x_perm, int32_t* __restrict__ row_of, int32_t* __restrict__ token_of, int* err) {
+  const int warp = warp_id(), lane = lane_id();
+  if (static_cast<int>(blockIdx.x) >= n_blocks) {
+    // Zero-fill the padding rows of one expert segment.
+    const int e = blockIdx.x - n_blocks;
+    const int64_t r0 = seg_start[e] + counts[e];
+    const int64_t r1 = min(static_cast<int64_t>(seg_start[e + 1]), max_rows);
+    const int64_t nvec = (r1 - r0) * nchunk;
+    uint4* base = x_perm + r0 * nchunk;
+    for (int64_t i = threadIdx.x; i < nvec; i += blockDim.x) base[i] = make_uint4(0, 0, 0, 0);
+    return;
+  }
+  __shared__ uint32_t mask_s[kBlk / 32][32];
+  __shared__ int cnt_s[kBlk / 32][32];
+  __shared__ int off_s[kBlk / 32][32];
+  const int64_t tok = static_cast<int64_t>(blockIdx.x) * kBlk + threadIdx.x;
+  const bool valid = tok < n_tokens;
+  int my_e[K_MAX];
+#pragma unroll
+  for (int r = 0; r < K_MAX; ++r) my_e[r] = (valid && r < k) ? idx[tok * k + r] : -1;
+  // Per-warp masks: lanes whose token picked expert e (at any rank).
+  for (int e = 0; e < E; ++e) {
+    bool hit = false;
+#pragma unroll
+    for (int r = 0; r < K_MAX; ++r) hit |= (my_e[r] == e);
+    const uint32_t m = __ballot_sync(0xffffffffu, hit);
+    if (lane == 0) {
+      mask_s[warp][e] = m;
+      cnt_s[warp][e] = __popc(m);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < E) {
+    const int e = threadIdx.x;
+    int acc = 0;
+    for (int w = 0; w < kBlk / 32; ++w) {
+      off_s[w][e] = acc;
+      acc += cnt_s[w][e];
+    }
+  }
+  __syncthreads();
+  const uint32_t lt = (1u << lane) - 1u;
+  int dest[K_MAX];
+#pragma unroll
+  for (int r = 0; r < K_MAX; ++r) {
+    dest[r] = -1;
+    const int e = my_e[r];
+    if (e >= 0 && e < E) {
+      const int64_t row = static_cast<int64_t>(seg_start[e]) + block_off[static_cast<int64_t>(blockIdx.x) * E + e] +
+                          off_s[warp][e] + __popc(mask_s[warp][e] & lt);
+      if (row >= 0 && row < max_rows) {
+        dest[r] = static_cast<int>(row);
+        row_of[tok * k + r] = static_cast<int32_t>(row);
+        token_of[row] = static_cast<int32_t>(tok);
+      } else {
+        raise_error(err, kErrRowOverflow);
+      }
+    } else if (e >= E) {
+      raise_error(err, kErrBadExpert);
+    }
+  }
+  // Copy rows: the warp walks its 32 tokens; all lanes stream the row.
+  const int64_t warp_tok0 = static_cast<int64_t>(blockIdx.x) * kBlk + warp * 32;
+  for (int i = 0; i < 32; ++i) {
+    const int64_t t = warp_tok0 + i;
+    if (t >= n_tokens) break;
+    int drow[K_MAX];
+#pragma unroll
+    for (int r = 0; r < K_MAX; ++r) drow[r] = __shfl_sync(0xffffffffu, dest[r], i);
+    const uint4* src = x + t * nchunk;
+    for (int c = lane; c < nchunk; c += 64) {
+      const uint4 v0 = __ldg(src + c);
+      const bool two = (c + 32) < nchunk;
+      uint4 v1 = make_uint4(0, 0, 0, 0);
+      if (two) v1 = __ldg(src + c + 32);
+#pragma unroll
+      for (int r = 0; r < K_MAX; ++r) {
+        if (r < k && drow[r] >= 0) {
+          uint4* dst = x_perm + static_cast<int64_t>(drow[r]) * nchunk;
+          dst[c] = v0;
+          if (two) dst[c + 32] = v1;
+        }
+      }
+    }
+  }
+}
+
+cudaError_t dispatch_plan(const int32_t* block_hist, int n_blocks, int E, int64_t max_rows, int max_tiles,
+                          int32_t* block_off, int32_t* counts, int32_t* seg_start, int32_t* tile_expert,
+                          int32_t* num_tiles, int32_t* token_of, int* err, cudaStream_t stream) {
+  dispatch_plan_kernel<<<1, kPlanThreads, 0, stream>>>(block_hist, n_blocks, E, max_rows, max_tiles, block_off,
+                                                       counts, seg_start, tile_expert, num_tiles, token_of, err);
+  return cudaGetLastError();
+}
+
+cudaError_t permute_rows(const void* x, int elem_bytes, int64_t n_tokens, int d, int k, int E, const int32_t* idx,
+                         const int32_t* block_off, const int32_t* seg_start, const int32_t* counts, int64_t max_rows,
+                         void* x_perm, int32_t* row_of, int32_t* token_of, int* err, cudaStream_t stream) {
+  const int n_blocks = static_cast<int>((n_tokens + kBlk - 1) / kBlk);
+  const int nchunk = d * elem_bytes / 16;
+  const unsigned grid = static_cast<unsigned>(n_blocks + E);
+  if (grid == 0) return cudaSuccess;
+  const uint4* xs = static_cast<const uint4*>(x);
+  uint4* xp = static_cast<uint4*>(x_perm);
+  if (k <= 2) {
+    permute_kernel<2><<<grid, kBlk, 0, stream>>>(xs, n_tokens, nchunk, k, E, n_blocks, idx, block_off, seg_start,
+                                                 counts, max_rows, xp, row_of, token_of, err);
+  } else if (k <= 4) {
+    permute_kernel<4><<<grid, kBlk, 0, stream>>>(xs, n_tokens, nchunk, k, E, n_blocks, idx, block_off, seg_start,
+                                                 counts, max_rows, xp, row_of, token_of, err);
+  } else {
+    permute_kernel<16><<<grid, kBlk, 0, stream>>>(xs, n_tokens, nchunk, k, E, n_blocks, idx, block_off, seg_start,
+                                                  counts, max_rows, xp, row_of, token_of, err);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace agm

@@ -1,0 +1,41 @@
+// Internal launch interface shared by the kernel files and the C ABI layer.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace agm {
+
+// Arguments of the grouped GEMM  c[r, :] = act(a[r, :] @ w[g]^T + bias[g]).
+struct GemmArgs {
+  void* c;
+  int64_t ldc;
+  int64_t c_rows;             // rows of c that exist (rows beyond are not stored)
+  const void* bias;           // [groups, n] or nullptr
+  int n;
+  int k;
+  int groups;
+  const int32_t* tile_group;  // [max_tiles] or nullptr (all tiles -> group 0)
+  const int32_t* num_tiles;   // device count of valid row tiles, or nullptr
+  int max_tiles;              // host bound (and the count when num_tiles is null)
+  int* err;
+};
+
+cudaError_t router_topk(int dtype, const void* x, const void* w, int64_t n_tokens, int d, int E, int k,
+                        int tie_swap, const float* logits_in, float* logits_out, int32_t* idx, void* gates,
+                        int32_t* block_hist, int* err, cudaStream_t stream);
+size_t router_smem_bytes(int d, int E);
+cudaError_t dispatch_plan(const int32_t* block_hist, int n_blocks, int E, int64_t max_rows, int max_tiles,
+                          int32_t* block_off, int32_t* counts, int32_t* seg_start, int32_t* tile_expert,
+                          int32_t* num_tiles, int32_t* token_of, int* err, cudaStream_t stream);
+cudaError_t permute_rows(const void* x, int elem_bytes, int64_t n_tokens, int d, int k, int E, const int32_t* idx,
+                         const int32_t* block_off, const int32_t* seg_start, const int32_t* counts, int64_t max_rows,
+                         void* x_perm, int32_t* row_of, int32_t* token_of, int* err, cudaStream_t stream);
+cudaError_t grouped_gemm(int dtype, const void* a, int64_t a_rows, const void* w, const GemmArgs& args, bool relu,
+                         int num_sms, cudaStream_t stream, int force_bn);
+cudaError_t combine(int dtype, const void* y, const int32_t* row_of, const void* gates, int64_t n, int d, int k,
+                    const void* shared_y, int n_shared, int64_t shared_stride, void* out, int num_sms,
+                    cudaStream_t stream);
+
+}  // namespace agm

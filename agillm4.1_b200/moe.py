@@ -1,0 +1,194 @@
+"""Drop-in MoE block for AGILLM4.1 whose forward runs on the sm_100a kernels.
+
+``MoEFFN`` keeps the reference class's interface (agillm41.py:4323-4460):
+
+* constructor ``MoEFFN(d, mlp_mult=4, experts=4, top_k=1, shared_experts=0,
+  shared_mlp_mult=0)`` and the same submodules, so the same state-dict keys:
+  ``router.weight``, ``experts.{e}.{0,2}.{weight,bias}``,
+  ``shared.{s}.{0,2}.{weight,bias}`` (4324-4351);
+* attributes ``d, mlp_mult, num_experts, top_k, num_shared,
+  last_router_input, expert_stream, expert_stream_empty_cache,
+  expert_stream_stats`` and ``set_expert_stream`` (4353-4365);
+* the legacy dense-FFN state-dict seeding of ``_load_from_state_dict``
+  (4433-4460);
+* ``forward(x[..., d]) -> Tensor[same shape, same dtype]``: the FFN output
+  only (the caller adds the residual, agillm41.py:4542, 4547).
+
+The forward calls the fused C-ABI entry point ``agm_moe_forward`` (router ->
+dispatch plan -> permute -> grouped FC1/FC2 -> combine) on the current CUDA
+stream with no host synchronisation. It refuses CPU tensors (there is no CPU
+fallback) and autograd (training keeps the reference class).
+
+``install(agillm41)`` rebinds the reference module's ``MoEFFN`` to a subclass
+of the reference class that uses this forward, so ``Block`` (4533-4537), the
+AR/SAT/NAT inference paths and the pipeline-stage runtime construct it, and
+``isinstance(m, agillm41.MoEFFN)`` checks (4475, 7657, 7674, 7685, 7694) hold.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.nn as nn
+
+from . import ops
+from ._lib import MoEKernelError
+
+
+class _B200Forward:
+    """Forward of the MoE block on the B200 kernels (mixed into the module classes)."""
+
+    # Set to True to synchronise and check the device error word after each
+    # forward (tests do; the hot path does not).
+    check_device_errors = False
+
+    def _packed_weights(self, device: torch.device, dtype: torch.dtype):
+        """Expert weights as contiguous [E, ...] device tensors, with the
+        module's parameters re-pointed at views of them so that in-place
+        updates (load_state_dict, optimiser steps) keep the pack current."""
+        experts = list(self.experts)
+        params = [p for ex in experts for p in (ex[0].weight, ex[0].bias, ex[2].weight, ex[2].bias)]
+        shared = list(self.shared) if getattr(self, "shared", None) is not None else []
+        sparams = [p for ex in shared for p in (ex[0].weight, ex[0].bias, ex[2].weight, ex[2].bias)]
+        key = (device, dtype) + tuple(p.data_ptr() for p in params + sparams)
+        cache = getattr(self, "_b200_pack", None)
+        if cache is not None and cache[0] == key:
+            return cache[1]
+        for p in params + sparams:
+            if p.device != device or p.dtype != dtype:
+                raise MoEKernelError(f"expert parameters must be on {device} in {dtype}, found {p.device}/{p.dtype}")
+
+        def stack(mods, i, attr):
+            return torch.stack([getattr(m[i], attr).detach() for m in mods]).contiguous()
+
+        with torch.no_grad():
+            w1, b1, w2, b2 = stack(experts, 0, "weight"), stack(experts, 0, "bias"), \
+                stack(experts, 2, "weight"), stack(experts, 2, "bias")
+            for e, ex in enumerate(experts):
+                ex[0].weight.data = w1[e]
+                ex[0].bias.data = b1[e]
+                ex[2].weight.data = w2[e]
+                ex[2].bias.data = b2[e]
+            sh = None
+            if shared:
+                sw1, sb1, sw2, sb2 = stack(shared, 0, "weight"), stack(shared, 0, "bias"), \
+                    stack(shared, 2, "weight"), stack(shared, 2, "bias")
+                for s, ex in enumerate(shared):
+                    ex[0].weight.data = sw1[s]
+                    ex[0].bias.data = sb1[s]
+                    ex[2].weight.data = sw2[s]
+                    ex[2].bias.data = sb2[s]
+                sh = (sw1, sb1, sw2, sb2)
+        packed = (w1, b1, w2, b2, sh)
+        key = (device, dtype) + tuple(p.data_ptr() for p in params + sparams)
+        self._b200_pack = (key, packed)
+        return packed
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:  # agillm41.py:4389-4431
+        orig_shape = x.shape
+        flat = x.reshape(-1, orig_shape[-1])
+        if self.training:
+            # agillm41.py:4392-4397: stash the detached input for _collect_moe_aux.
+            self.last_router_input = flat.detach()
+        if not flat.is_cuda:
+            raise MoEKernelError("MoEFFN (B200) runs on CUDA tensors only; there is no CPU path")
+        if torch.is_grad_enabled() and (flat.requires_grad or any(p.requires_grad for p in self.parameters())):
+            raise MoEKernelError("MoEFFN (B200) implements the inference forward only; run it under "
+                                 "torch.no_grad()/inference_mode or keep the reference module for training")
+        if self.expert_stream:
+            raise MoEKernelError("expert_stream (CPU-resident experts) is not supported by the B200 forward")
+        wr = self.router.weight
+        if flat.dtype != wr.dtype:
+            raise MoEKernelError(f"input dtype {flat.dtype} differs from the weight dtype {wr.dtype}")
+        w1, b1, w2, b2, sh = self._packed_weights(flat.device, flat.dtype)
+        out = ops.moe_forward(flat.contiguous(), wr.detach().contiguous(), w1, b1, w2, b2, self.top_k,
+                              shared=sh, check_errors=self.check_device_errors)
+        return out.reshape(orig_shape)
+
+
+class MoEFFN(_B200Forward, nn.Module):
+    """AGILLM4.1 MoE feed-forward block (reference interface, B200 forward)."""
+
+    def __init__(self, d: int, mlp_mult: int = 4, experts: int = 4, top_k: int = 1,
+                 shared_experts: int = 0, shared_mlp_mult: int = 0):
+        super().__init__()
+        # agillm41.py:4324-4360
+        self.d = int(d)
+        self.mlp_mult = max(1, int(mlp_mult))
+        self.num_experts = max(1, int(experts))
+        self.top_k = min(max(1, int(top_k)), self.num_experts)
+        hidden = self.mlp_mult * self.d
+        self.router = nn.Linear(self.d, self.num_experts, bias=False)
+        self.experts = nn.ModuleList([
+            nn.Sequential(nn.Linear(self.d, hidden), nn.ReLU(), nn.Linear(hidden, self.d))
+            for _ in range(self.num_experts)
+        ])
+        self.num_shared = max(0, int(shared_experts))
+        if self.num_shared > 0:
+            shidden = max(1, int(shared_mlp_mult) or self.mlp_mult) * self.d
+            self.shared = nn.ModuleList([
+                nn.Sequential(nn.Linear(self.d, shidden), nn.ReLU(), nn.Linear(shidden, self.d))
+                for _ in range(self.num_shared)
+            ])
+            for blk in self.shared:  # zero-initialised output layer: a no-op at step 0
+                nn.init.zeros_(blk[2].weight)
+                nn.init.zeros_(blk[2].bias)
+        else:
+            self.shared = None
+        self.last_router_input = None
+        self.expert_stream = False
+        self.expert_stream_empty_cache = True
+        self.expert_stream_stats = {"loads": 0, "tokens": 0}
+
+    def set_expert_stream(self, enabled: bool, empty_cache: bool = True):  # agillm41.py:4362-4365
+        self.expert_stream = bool(enabled)
+        self.expert_stream_empty_cache = bool(empty_cache)
+        return self
+
+    def _load_from_state_dict(self, state_dict, prefix, local_metadata, strict, missing_keys, unexpected_keys,
+                              error_msgs):
+        # agillm41.py:4433-4460: a dense FFN checkpoint (`ff.0.*`, `ff.2.*`)
+        # seeds every expert with the same weights; the router keeps its init.
+        legacy = ("0.weight", "0.bias", "2.weight", "2.bias")
+        seeded = False
+        for e, expert in enumerate(self.experts):
+            expert_state = expert.state_dict()
+            for suffix in legacy:
+                src = state_dict.get(prefix + suffix)
+                dst_key = prefix + f"experts.{e}." + suffix
+                tgt = expert_state.get(suffix)
+                if dst_key not in state_dict and torch.is_tensor(src) and torch.is_tensor(tgt) \
+                        and tuple(src.shape) == tuple(tgt.shape):
+                    state_dict[dst_key] = src
+                    seeded = True
+        if seeded and prefix + "router.weight" not in state_dict:
+            state_dict[prefix + "router.weight"] = self.router.weight.detach().clone()
+        if seeded:
+            for suffix in legacy:
+                state_dict.pop(prefix + suffix, None)
+        return super()._load_from_state_dict(state_dict, prefix, local_metadata, strict, missing_keys,
+                                             unexpected_keys, error_msgs)
+
+
+def install(agillm41_module, name: str = "MoEFFN"):
+    """Rebind ``agillm41_module.MoEFFN`` to a subclass of the reference class
+    whose forward runs on the B200 kernels. Returns the new class.
+
+    Everything except ``forward`` (constructor, state-dict shim, expert
+    streaming toggles, aux-loss stash) is inherited from the reference class.
+    Modules built after the call (``Block``, ``Encoder``, the inference and
+    pipeline-stage runtimes) use it.
+    """
+    ref_cls = getattr(agillm41_module, name)
+    if getattr(ref_cls, "_is_b200", False):
+        return ref_cls
+    cls = type(name, (_B200Forward, ref_cls), {"_is_b200": True, "_reference_class": ref_cls,
+                                               "__module__": ref_cls.__module__})
+    setattr(agillm41_module, name, cls)
+    return cls
+
+
+def uninstall(agillm41_module, name: str = "MoEFFN") -> None:
+    cls = getattr(agillm41_module, name)
+    if getattr(cls, "_is_b200", False):
+        setattr(agillm41_module, name, cls._reference_class)

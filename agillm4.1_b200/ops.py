@@ -1,0 +1,225 @@
+"""Python entry points over the C ABI, one per kernel stage plus the fused forward.
+
+Each function takes torch CUDA tensors, allocates its outputs with torch's
+caching allocator and launches on the current stream. They mirror the stages
+of the reference forward (agillm41.py:4389-4431):
+
+* :func:`router_topk`      router logits, top-k / top-1, gates (4398-4419)
+* :func:`dispatch_plan`    expert counts and segment layout (replaces `nonzero`, 4425)
+* :func:`permute`          stable scatter of token rows (replaces `index_select`, 4428)
+* :func:`grouped_gemm`     expert Linear layers over all segments (4428, 4332-4336)
+* :func:`combine`          gate-weighted `index_add_` + shared experts (4420-4430)
+* :func:`moe_forward`      all of the above in one call, no host sync
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Dict, Optional
+
+import torch
+
+from . import _lib
+from ._lib import AGM_FLAG_TIE_SWAP, AGM_TILE_M, check, dtype_code, load, ptr, stream_handle
+
+# Order of two exactly-equal top-k values. The reference selects with
+# torch.topk on the device it runs on; `tie_swap=True` reverses the order of
+# an exactly-equal adjacent pair relative to ascending expert index.
+DEFAULT_TIE_SWAP = False
+
+
+def _flags(tie_swap: Optional[bool]) -> int:
+    return AGM_FLAG_TIE_SWAP if (DEFAULT_TIE_SWAP if tie_swap is None else tie_swap) else 0
+
+
+def dispatch_blocks(n_tokens: int) -> int:
+    return int(load().agm_dispatch_blocks(n_tokens))
+
+
+def max_rows(n_tokens: int, top_k: int, n_experts: int) -> int:
+    return int(load().agm_max_rows(n_tokens, top_k, n_experts))
+
+
+def router_topk(x: torch.Tensor, w_router: torch.Tensor, top_k: int, *, logits_in: Optional[torch.Tensor] = None,
+                want_logits: bool = False, tie_swap: Optional[bool] = None, err: Optional[torch.Tensor] = None):
+    """Returns (idx int32 [N,k], gates [N,k], block_hist int32 [nb,E], logits fp32 [N,E] or None)."""
+    lib = load()
+    n, d = x.shape
+    E = w_router.shape[0]
+    dev = x.device
+    idx = torch.empty(n, top_k, dtype=torch.int32, device=dev)
+    gates = torch.empty(n, top_k, dtype=x.dtype, device=dev)
+    hist = torch.empty(dispatch_blocks(n), E, dtype=torch.int32, device=dev)
+    logits = torch.empty(n, E, dtype=torch.float32, device=dev) if want_logits else None
+    if logits_in is not None:
+        logits_in = logits_in.to(dtype=torch.float32).contiguous()
+    rc = lib.agm_router_topk(ptr(x), ptr(w_router), dtype_code(x.dtype), n, d, E, top_k, _flags(tie_swap),
+                             ptr(logits_in), ptr(logits), ptr(idx), ptr(gates), ptr(hist), ptr(err),
+                             stream_handle(dev))
+    check(rc, "agm_router_topk")
+    return idx, gates, hist, logits
+
+
+def dispatch_plan(block_hist: torch.Tensor, n_tokens: int, top_k: int, err: Optional[torch.Tensor] = None
+                  ) -> Dict[str, torch.Tensor]:
+    lib = load()
+    E = block_hist.shape[1]
+    dev = block_hist.device
+    rows = max_rows(n_tokens, top_k, E)
+    out = dict(
+        block_off=torch.empty_like(block_hist),
+        counts=torch.empty(E, dtype=torch.int32, device=dev),
+        seg_start=torch.empty(E + 1, dtype=torch.int32, device=dev),
+        tile_expert=torch.empty(max(rows // AGM_TILE_M, 1), dtype=torch.int32, device=dev),
+        num_tiles=torch.empty(1, dtype=torch.int32, device=dev),
+        token_of=torch.empty(max(rows, 1), dtype=torch.int32, device=dev),
+    )
+    rc = lib.agm_dispatch_plan(ptr(block_hist), n_tokens, E, top_k, ptr(out["block_off"]), ptr(out["counts"]),
+                               ptr(out["seg_start"]), ptr(out["tile_expert"]), ptr(out["num_tiles"]),
+                               ptr(out["token_of"]), ptr(err), stream_handle(dev))
+    check(rc, "agm_dispatch_plan")
+    return out
+
+
+def permute(x: torch.Tensor, idx: torch.Tensor, plan: Dict[str, torch.Tensor], n_experts: int,
+            err: Optional[torch.Tensor] = None):
+    """Returns (x_perm [max_rows, d], row_of int32 [N,k]); fills plan['token_of']."""
+    lib = load()
+    n, d = x.shape
+    k = idx.shape[1]
+    rows = max_rows(n, k, n_experts)
+    x_perm = torch.empty(max(rows, 1), d, dtype=x.dtype, device=x.device)
+    row_of = torch.empty(n, k, dtype=torch.int32, device=x.device)
+    rc = lib.agm_permute(ptr(x), dtype_code(x.dtype), n, d, n_experts, k, ptr(idx), ptr(plan["block_off"]),
+                         ptr(plan["seg_start"]), ptr(plan["counts"]), ptr(x_perm), ptr(row_of),
+                         ptr(plan["token_of"]), ptr(err), stream_handle(x.device))
+    check(rc, "agm_permute")
+    return x_perm, row_of
+
+
+def grouped_gemm(a: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor], *, relu: bool,
+                 tile_group: Optional[torch.Tensor] = None, num_tiles: Optional[torch.Tensor] = None,
+                 max_tiles: Optional[int] = None, c_rows: Optional[int] = None, force_bn: int = 0,
+                 err: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """c = act(a @ w[g]^T + bias[g]) per 128-row tile; w is [G, N, K] (nn.Linear layout)."""
+    lib = load()
+    a_rows, k_in = a.shape
+    if w.dim() == 2:
+        w = w.unsqueeze(0)
+        bias = None if bias is None else bias.unsqueeze(0)
+    G, n_out, k_w = w.shape
+    if k_w != k_in:
+        raise ValueError(f"a has {k_in} features, w expects {k_w}")
+    if max_tiles is None:
+        max_tiles = (a_rows + AGM_TILE_M - 1) // AGM_TILE_M
+    if c_rows is None:
+        c_rows = a_rows
+    c = torch.empty(c_rows, n_out, dtype=a.dtype, device=a.device)
+    rc = lib.agm_grouped_gemm(ptr(a), a_rows, ptr(w), ptr(bias), dtype_code(a.dtype), G, n_out, k_in,
+                              ptr(tile_group), ptr(num_tiles), max_tiles, int(relu), force_bn, ptr(c), c_rows,
+                              ptr(err), stream_handle(a.device))
+    check(rc, "agm_grouped_gemm")
+    return c
+
+
+def combine(y_perm: torch.Tensor, row_of: torch.Tensor, gates: torch.Tensor,
+            shared_y: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out[t] = sum_r y_perm[row_of[t,r]] * gates[t,r] (+ sum_s shared_y[s, t]), reference rounding order."""
+    lib = load()
+    n, k = row_of.shape
+    d = y_perm.shape[1]
+    out = torch.empty(n, d, dtype=y_perm.dtype, device=y_perm.device)
+    n_shared = 0 if shared_y is None else shared_y.shape[0]
+    stride = 0 if shared_y is None else shared_y.shape[1]
+    rc = lib.agm_combine(ptr(y_perm), ptr(row_of), ptr(gates), dtype_code(y_perm.dtype), n, d, k, ptr(shared_y),
+                         n_shared, stride, ptr(out), stream_handle(y_perm.device))
+    check(rc, "agm_combine")
+    return out
+
+
+def _event_array(events):
+    if events is None:
+        return None
+    if len(events) != _lib.AGM_STAGE_EVENTS:
+        raise ValueError(f"stage_events needs {_lib.AGM_STAGE_EVENTS} events")
+    return (ctypes.c_void_p * len(events))(*[ev.cuda_event for ev in events])
+
+
+class Workspace:
+    """Device scratch for :func:`moe_forward`, grown on demand and reused.
+
+    One workspace per (device, stream): forwards on the same stream run one
+    after another, so they can share it.
+    """
+
+    _cache: Dict[tuple, torch.Tensor] = {}
+
+    @classmethod
+    def get(cls, device: torch.device, nbytes: int) -> torch.Tensor:
+        key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+        buf = cls._cache.get(key)
+        if buf is None or buf.numel() < nbytes:
+            cls._cache.pop(key, None)
+            buf = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
+            cls._cache[key] = buf
+        return buf
+
+    @classmethod
+    def clear(cls) -> None:
+        cls._cache.clear()
+
+
+def workspace_bytes(n_tokens: int, d: int, n_experts: int, top_k: int, hidden: int, n_shared: int,
+                    shared_hidden: int, dtype: torch.dtype) -> int:
+    return int(load().agm_moe_workspace_bytes(n_tokens, d, n_experts, top_k, hidden, n_shared, shared_hidden,
+                                              dtype_code(dtype)))
+
+
+def moe_forward(x: torch.Tensor, w_router: torch.Tensor, w1: torch.Tensor, b1: torch.Tensor, w2: torch.Tensor,
+                b2: torch.Tensor, top_k: int, *, shared: Optional[tuple] = None, out: Optional[torch.Tensor] = None,
+                want: tuple = (), tie_swap: Optional[bool] = None, workspace: Optional[torch.Tensor] = None,
+                check_errors: bool = False, stage_events=None):
+    """Fused forward: x [N, d] -> out [N, d]. ``want`` may hold 'idx', 'gates', 'counts', 'logits'.
+
+    Weights: w_router [E, d]; w1 [E, H, d]; b1 [E, H]; w2 [E, d, H]; b2 [E, d];
+    shared = (ws1 [S,Hs,d], sb1 [S,Hs], ws2 [S,d,Hs], sb2 [S,d]) or None.
+    ``stage_events``: optional list of AGM_STAGE_EVENTS torch.cuda.Event
+    (timing enabled) recorded around each kernel stage on the current stream.
+    Returns out, or (out, extras dict) when ``want`` is not empty.
+    """
+    lib = load()
+    n, d = x.shape
+    E = w_router.shape[0]
+    H = w1.shape[1]
+    dev = x.device
+    if shared is not None:
+        ws1, sb1, ws2, sb2 = shared
+        S, Hs = ws1.shape[0], ws1.shape[1]
+    else:
+        ws1 = sb1 = ws2 = sb2 = None
+        S, Hs = 0, 0
+    if out is None:
+        out = torch.empty_like(x)
+    nbytes = workspace_bytes(n, d, E, top_k, H, S, max(Hs, 1), x.dtype)
+    if workspace is None:
+        workspace = Workspace.get(dev, nbytes)
+    extras = {}
+    if "idx" in want:
+        extras["idx"] = torch.empty(n, top_k, dtype=torch.int32, device=dev)
+    if "gates" in want:
+        extras["gates"] = torch.empty(n, top_k, dtype=x.dtype, device=dev)
+    if "counts" in want:
+        extras["counts"] = torch.empty(E, dtype=torch.int32, device=dev)
+    if "logits" in want:
+        extras["logits"] = torch.empty(n, E, dtype=torch.float32, device=dev)
+    ev_arr = _event_array(stage_events)  # kept alive across the call
+    rc = lib.agm_moe_forward(
+        ptr(x), dtype_code(x.dtype), n, d, E, top_k, H, ptr(w_router), ptr(w1), ptr(b1), ptr(w2), ptr(b2), S,
+        max(Hs, 1), ptr(ws1), ptr(sb1), ptr(ws2), ptr(sb2), ptr(out), ptr(workspace), workspace.numel(),
+        _flags(tie_swap), ptr(extras.get("idx")), ptr(extras.get("gates")), ptr(extras.get("counts")),
+        ptr(extras.get("logits")), None if ev_arr is None else ctypes.addressof(ev_arr), stream_handle(dev))
+    check(rc, "agm_moe_forward")
+    if check_errors:
+        code = _lib.read_device_error(workspace[:4].view(torch.int32))
+        if code:
+            raise _lib.MoEKernelError(f"device error word 0x{code:x} after agm_moe_forward")
+    return (out, extras) if want else out

@@ -1,0 +1,381 @@
+"""Benchmark of the AGILLM4.1 MoE block forward on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one MoE block forward (router -> top-2 -> dispatch -> expert FFNs
+-> combine) over the whole batch. Workload at one GPU: B=48, L=1536 tokens
+(73,728), d_model=1280, 14 experts with hidden 3200, top-2, bf16, random-init
+weights N(0, 0.02^2), x ~ N(0, 1), seed 1. Inputs (x: 189 MB, expert
+weights: 229 MB) are larger than the 126 MB L2, so no flush is needed between
+steps.
+
+With N > 1 (one process per GPU under torchrun) every rank runs the same
+workload on its own tokens (weak scaling, replicas); tokens/s is the sum over
+ranks and the time is the max over ranks.
+
+The JSON line carries the whole-job tokens/s (device-timed, inputs resident
+in HBM), the end-to-end tokens/s through the public module API with host
+buffers (pinned host -> device copy of x and device -> host copy of the
+output inside the timed region), the per-stage kernel times measured live
+with CUDA events around each kernel stage, the roofline of the dominant
+kernel (the tcgen05 grouped GEMM), the CPU baseline (the oracle, i.e. the
+reference's torch op sequence, on the host cores) and the SM clocks seen
+during the timed region.
+
+``--impl reference`` times the reference's CPU implementation of the path
+(the oracle) on the host cores instead, on the same workload shapes.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+D, HIDDEN, EXPERTS, TOP_K, BATCH, SEQ, SEED = 1280, 3200, 14, 2, 48, 1536, 1
+METRIC = "MoE tokens/s (d1280, 14 exp, top-2) at 1/2/4/8 B200; % of roofline"
+UNIT = "tokens/s"
+FLOP_PER_TOKEN = 4 * D * HIDDEN * TOP_K          # 32,768,000 (FC1 + FC2, k rows per token)
+# Algorithmic HBM bytes per token of the memory-bound stages (bf16):
+ROUTER_BYTES = 2 * D + 4 * TOP_K + 2 * TOP_K      # read x row; write idx (int32) + gates (bf16)
+PERMUTE_BYTES = 2 * D + 4 * TOP_K + 2 * D * TOP_K + 4 * TOP_K + 4 * TOP_K  # x, idx -> k rows, row_of, token_of
+COMBINE_BYTES = 2 * D * TOP_K + 4 * TOP_K + 2 * TOP_K + 2 * D             # k rows, row_of, gates -> out row
+STAGES = ["router", "plan", "permute", "fc1", "fc2", "shared", "combine"]
+KERNELS_PER_STEP = 6   # router, plan, permute, fc1, fc2, combine
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return dict(hbm=float(j["hbm_gbs"]), tf=float(j["bf16_tflops"]),
+                    tf_sus=float(j.get("bf16_tflops_sustained", j["bf16_tflops"])), src="measured")
+    return dict(hbm=6650.0, tf=1590.0, tf_sus=1400.0, src="fallback")
+
+
+def load_traffic():
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f)
+    return {}
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        # nvidia-smi numbers GPUs differently from CUDA under CUDA_VISIBLE_DEVICES: use the UUID.
+        try:
+            self.gpu = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
+        except Exception:
+            self.gpu = str(device.index if isinstance(device, torch.device) else device)
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            import tempfile
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or not self.path or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        loaded = [s for s in sm if mx and s > 0.3 * max(mx)] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows),
+                "power_w_max": max((float(r[3]) for r in rows if r[3].replace(".", "").isdigit()), default=None)}
+
+
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def cpu_oracle_rate(n_tokens, budget_s=12.0, min_reps=2, threads=None):
+    """Tokens/s of the reference's torch op sequence on the host CPU (fp32)."""
+    from oracle import reference_moe
+    threads = threads or (os.cpu_count() or 1)
+    torch.set_num_threads(threads)
+    sd = reference_moe.make_state(D, HIDDEN, EXPERTS, SEED, dtype=torch.float32)
+    x = reference_moe.make_input(n_tokens, D, SEED)
+    with torch.no_grad():
+        reference_moe.moe_forward(x[: min(256, n_tokens)], sd, TOP_K)   # warm-up
+        reps, t0 = 0, time.perf_counter()
+        while reps < min_reps or time.perf_counter() - t0 < budget_s:
+            reference_moe.moe_forward(x, sd, TOP_K)
+            reps += 1
+        dt = time.perf_counter() - t0
+    return n_tokens * reps / dt, threads, reps, dt
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_reference(args, world, rank):
+    """--impl reference: the reference's CPU path (oracle) on the host cores."""
+    if rank != 0:
+        return
+    from oracle import reference_moe
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    sample = 2048
+    sd = reference_moe.make_state(D, HIDDEN, EXPERTS, SEED, dtype=torch.float32)
+    x = reference_moe.make_input(sample, D, SEED)
+    times = []
+    with torch.no_grad():
+        for i in range(args.warmup + args.steps):
+            t0 = time.perf_counter()
+            reference_moe.moe_forward(x, sd, TOP_K)
+            if i >= args.warmup:
+                times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = sample * len(times) / total
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / len(times),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) input, N(0,0.02^2) weights)",
+        "config": workload_config(world),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{sample} tokens of the workload per step, fp32, torch.set_num_threads({threads}), "
+                                   f"CPU {cpu_model()}"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(world):
+    return {"workload": f"MoE block forward B{BATCH} L{SEQ} d{D} E{EXPERTS} H{HIDDEN} top{TOP_K} bf16 seed{SEED}",
+            "global_batch": BATCH * world, "seq_len": SEQ, "tokens_per_gpu": BATCH * SEQ, "d_model": D,
+            "experts": EXPERTS, "expert_hidden": HIDDEN, "top_k": TOP_K,
+            "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+            "l2": "inputs larger than L2 (x 189 MB + expert weights 229 MB > 126 MB); no flush"}
+
+
+def run_ours(args, world, rank, local):
+    import agillm41_b200
+    from agillm41_b200 import ops, synthetic
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    N = BATCH * SEQ
+    sd = synthetic.make_state(D, HIDDEN, EXPERTS, SEED + rank * 1000, dtype=torch.bfloat16, device=dev)
+    x = synthetic.make_input(N, D, SEED + rank * 1000, dtype=torch.bfloat16, device=dev)
+    w1 = torch.stack([sd[f"experts.{e}.0.weight"] for e in range(EXPERTS)]).contiguous()
+    b1 = torch.stack([sd[f"experts.{e}.0.bias"] for e in range(EXPERTS)]).contiguous()
+    w2 = torch.stack([sd[f"experts.{e}.2.weight"] for e in range(EXPERTS)]).contiguous()
+    b2 = torch.stack([sd[f"experts.{e}.2.bias"] for e in range(EXPERTS)]).contiguous()
+    wr = sd["router.weight"].contiguous()
+    out = torch.empty_like(x)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(events=None):
+        ops.moe_forward(x, wr, w1, b1, w2, b2, TOP_K, out=out, stage_events=events)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    from agillm41_b200._lib import read_device_error
+    err = read_device_error(ops.Workspace.get(dev, 0)[:4].view(torch.int32))
+    if err:
+        raise RuntimeError(f"device error word 0x{err:x} after warm-up")
+
+    # ---- timed region (device time, per-stage events) ----
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(8)] for _ in range(args.steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(dev) as clk:
+        start.record(stream)
+        for i in range(args.steps):
+            step(evs[i])
+        stop.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms_total = start.elapsed_time(stop)
+    ms_total = max_over_ranks(ms_total, world)
+    stage_ms = {s: 0.0 for s in STAGES}
+    for e in evs:
+        for j, s in enumerate(STAGES):
+            stage_ms[s] += e[j].elapsed_time(e[j + 1])
+    stage_ms = {s: v / args.steps for s, v in stage_ms.items()}
+    clocks = clk.summary()
+    value = N * world * args.steps / (ms_total / 1000.0)
+
+    # ---- end to end through the public module API with host buffers ----
+    m = agillm41_b200.MoEFFN(D, mlp_mult=4, experts=EXPERTS, top_k=TOP_K)
+    m.experts = torch.nn.ModuleList([torch.nn.Sequential(torch.nn.Linear(D, HIDDEN), torch.nn.ReLU(),
+                                                         torch.nn.Linear(HIDDEN, D)) for _ in range(EXPERTS)])
+    m = m.to(device=dev, dtype=torch.bfloat16).eval()
+    m.load_state_dict(sd)
+    x_host = x.reshape(BATCH, SEQ, D).cpu().pin_memory()
+    y_host = torch.empty_like(x_host).pin_memory()
+    x_dev = torch.empty(BATCH, SEQ, D, dtype=torch.bfloat16, device=dev)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        with torch.no_grad():
+            y = m(x_dev)
+        y_host.copy_(y, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    e2e_value = N * world * args.steps / (e2e_ms / 1000.0)
+    assert torch.equal(y_host.reshape(N, D).to(dev), out), "module output differs from the timed forward"
+
+    if rank != 0:
+        return
+    peaks = load_peaks()
+    gemm_ms = (stage_ms["fc1"] + stage_ms["fc2"]) / 2.0          # average launch of the grouped GEMM
+    gemm_flop_per_launch = FLOP_PER_TOKEN * N / 2.0
+    achieved_tf = gemm_flop_per_launch / (gemm_ms / 1000.0) / 1e12
+    traffic = load_traffic().get("grouped_gemm_fc1_fc2_avg_bytes_per_launch")
+
+    def hbm(stage, per_tok):
+        gbs = per_tok * N / (stage_ms[stage] / 1000.0) / 1e9
+        return {"ms": round(stage_ms[stage], 4), "achieved_gbs": round(gbs, 1), "frac": round(gbs / peaks["hbm"], 3),
+                "algorithmic_bytes": per_tok * N}
+
+    cpu = None
+    if world == 1:
+        rate, threads, reps, dt = cpu_oracle_rate(2048)
+        cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"2048 tokens of the workload x {reps} forwards ({dt:.1f} s), fp32, "
+                         f"torch.set_num_threads({threads}), CPU {cpu_model()}"}
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_total / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) input, N(0,0.02^2) random-init expert weights)",
+        "config": workload_config(world),
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": x_host.numel() * 2,
+                "d2h_bytes_per_step": y_host.numel() * 2},
+        "gpu_launches": KERNELS_PER_STEP * args.steps,
+        "roofline": {"kernel": "grouped_gemm_tc_kernel (FC1+FC2, tcgen05)", "bound": "tensor",
+                     "achieved": round(achieved_tf, 1), "peak": peaks["tf_sus"], "unit": "TFLOP/s",
+                     "frac": round(achieved_tf / peaks["tf_sus"], 3),
+                     "frac_of_burst_peak": round(achieved_tf / peaks["tf"], 3),
+                     "peak_source": f"{peaks['src']} bf16 sustained (burst {peaks['tf']})",
+                     "traffic": traffic, "flop_per_launch": gemm_flop_per_launch},
+        "stages": {
+            "router": hbm("router", ROUTER_BYTES), "permute": hbm("permute", PERMUTE_BYTES),
+            "combine": hbm("combine", COMBINE_BYTES),
+            "plan_ms": round(stage_ms["plan"], 4), "fc1_ms": round(stage_ms["fc1"], 4),
+            "fc2_ms": round(stage_ms["fc2"], 4), "hbm_peak_gbs": peaks["hbm"],
+        },
+        "cpu_baseline": cpu,
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, world, rank)
+        return
+    world, rank, local = dist_setup(args.gpus)
+    try:
+        run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

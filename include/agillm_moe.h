@@ -1,0 +1,152 @@
+/*
+ * agillm_moe.h - C ABI of the B200 (sm_100a) MoE block forward for AGILLM4.1.
+ *
+ * Drop-in boundary for the reference's `MoEFFN.forward` (agillm41.py:4389-4431).
+ * The reference is a Python/PyTorch module, so its "FFI" is the module's
+ * forward; each entry point below replaces the part of that forward cited in
+ * its comment. All pointers are DEVICE pointers (unless stated), all tensors
+ * are dense row-major, and every call is asynchronous on the CUDA stream
+ * passed as `stream` (a cudaStream_t; NULL = legacy default stream).
+ *
+ * Return value: AGM_OK (0) or a negative AGM_ERR_* code; agm_last_error()
+ * then describes the failure (thread-local). Kernels never trap: device-side
+ * problems (impossible routing, a wait that timed out) are OR-ed into a device
+ * error word that the caller reads with agm_read_device_error().
+ *
+ * dtype: AGM_F32, AGM_BF16 or AGM_F16 for activations, weights, biases and
+ * gates alike (the reference runs the block in one dtype: bf16 when the model
+ * is converted with --infer_dtype, fp32 otherwise).
+ */
+#ifndef AGILLM_MOE_H_
+#define AGILLM_MOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define AGM_API __attribute__((visibility("default")))
+#else
+#define AGM_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define AGM_ABI_VERSION 1
+
+enum { AGM_F32 = 0, AGM_BF16 = 1, AGM_F16 = 2 };
+
+enum {
+  AGM_OK = 0,
+  AGM_ERR_ARG = -1,         /* invalid argument (shape, dtype, alignment, null) */
+  AGM_ERR_UNSUPPORTED = -2, /* valid for the reference, not supported here     */
+  AGM_ERR_CUDA = -3,        /* CUDA runtime error                              */
+  AGM_ERR_DEVICE = -4,      /* device error word was non-zero                  */
+  AGM_ERR_WORKSPACE = -5    /* workspace too small                             */
+};
+
+/* Rows per GEMM tile. Every expert segment of the permuted activations is
+ * padded to a multiple of this. */
+#define AGM_TILE_M 128
+/* Tokens handled by one CTA of the router and permute kernels. */
+#define AGM_DISPATCH_BLOCK 256
+/* Largest supported number of experts (router kernel keeps 16 logits/token). */
+#define AGM_MAX_EXPERTS 16
+
+/* Number of events agm_moe_forward records when stage_events is given. */
+#define AGM_STAGE_EVENTS 8
+
+/* forward flags */
+#define AGM_FLAG_TIE_SWAP 0x1 /* reverse the order of exactly-equal top-k pairs */
+
+AGM_API const char* agm_last_error(void);
+AGM_API int agm_abi_version(void);
+
+/* Number of dispatch blocks for n_tokens tokens: ceil(n / AGM_DISPATCH_BLOCK). */
+AGM_API int64_t agm_dispatch_blocks(int64_t n_tokens);
+/* Upper bound on permuted rows: round_up(k*n + E*(AGM_TILE_M-1), AGM_TILE_M). */
+AGM_API int64_t agm_max_rows(int64_t n_tokens, int top_k, int n_experts);
+
+/* Router + top-k. Replaces agillm41.py:4398-4419 (scores = router(x).float();
+ * top-k: vals, idx = topk(scores, k); w = softmax(vals).to(dtype);
+ * top-1 (4401-4416): idx = argmax(softmax(scores)), gate 1.0).
+ *   x [n, d], w_router [E, d]      -> idx int32 [n, k], gates [n, k] (dtype),
+ *                                     block_hist int32 [agm_dispatch_blocks(n), E]
+ *   logits_in  (nullable) fp32 [n, E]: select from these logits instead of
+ *                                     computing them (bit-exactness checks)
+ *   logits_out (nullable) fp32 [n, E]: the logits (rounded like the reference)
+ *   flags: AGM_FLAG_TIE_SWAP
+ *   err: device int (nullable)                                                */
+AGM_API int agm_router_topk(const void* x, const void* w_router, int dtype, int64_t n_tokens, int d, int n_experts,
+                    int top_k, int flags, const float* logits_in, float* logits_out, int32_t* idx, void* gates,
+                    int32_t* block_hist, int* err, void* stream);
+
+/* Dispatch plan (expert histogram prefix sums). Replaces the `nonzero` calls
+ * of the reference dispatch loop (agillm41.py:4421-4426).
+ *   block_hist [nb, E] -> block_off [nb, E], counts [E], seg_start [E+1]
+ *   (segments padded to AGM_TILE_M), tile_expert [max_rows/AGM_TILE_M],
+ *   num_tiles [1], token_of [max_rows] (padding rows set to -1).          */
+AGM_API int agm_dispatch_plan(const int32_t* block_hist, int64_t n_tokens, int n_experts, int top_k, int32_t* block_off,
+                      int32_t* counts, int32_t* seg_start, int32_t* tile_expert, int32_t* num_tiles,
+                      int32_t* token_of, int* err, void* stream);
+
+/* Stable scatter permutation. Replaces `flat.index_select(0, rows)` of
+ * agillm41.py:4428: x [n, d] -> x_perm [max_rows, d] (expert segments in
+ * ascending token order, padding rows zeroed), row_of [n, k], token_of.  */
+AGM_API int agm_permute(const void* x, int dtype, int64_t n_tokens, int d, int n_experts, int top_k, const int32_t* idx,
+                const int32_t* block_off, const int32_t* seg_start, const int32_t* counts, void* x_perm,
+                int32_t* row_of, int32_t* token_of, int* err, void* stream);
+
+/* Grouped GEMM over row tiles. Replaces the expert Linear layers
+ * (agillm41.py:4332-4336 via `_run_expert`, 4367-4379):
+ *   c[r, :] = act(a[r, :] @ w[g]^T + bias[g])   g = tile_group[r / AGM_TILE_M]
+ *   a [a_rows, k_in], w [groups, n_out, k_in], bias [groups, n_out] (nullable),
+ *   c [c_rows, n_out]; tile_group (nullable: all tiles use group 0);
+ *   num_tiles (nullable device int: valid tiles; else max_tiles are valid).
+ *   relu: 1 = ReLU epilogue (FC1), 0 = none (FC2).  force_bn: 0 = auto,
+ *   128 or 256 = GEMM tile width (bf16/fp16 only).                        */
+AGM_API int agm_grouped_gemm(const void* a, int64_t a_rows, const void* w, const void* bias, int dtype, int groups,
+                     int n_out, int k_in, const int32_t* tile_group, const int32_t* num_tiles, int64_t max_tiles,
+                     int relu, int force_bn, void* c, int64_t c_rows, int* err, void* stream);
+
+/* Gate-weighted combine. Replaces `out.index_add_(0, rows, y * w[rows])`
+ * (agillm41.py:4420-4428) and `out = out + shared(flat)` (4429-4430):
+ *   out[t] = sum_r y_perm[row_of[t, r]] * gates[t, r]  (+ sum_s shared_y[s, t])
+ *   with every op rounded to dtype in the reference's order.
+ *   shared_y (nullable) [n_shared, shared_stride_rows, d].                  */
+AGM_API int agm_combine(const void* y_perm, const int32_t* row_of, const void* gates, int dtype, int64_t n_tokens, int d,
+                int top_k, const void* shared_y, int n_shared, int64_t shared_stride_rows, void* out, void* stream);
+
+/* Workspace needed by agm_moe_forward (bytes). */
+AGM_API size_t agm_moe_workspace_bytes(int64_t n_tokens, int d, int n_experts, int top_k, int hidden, int n_shared,
+                               int shared_hidden, int dtype);
+
+/* Whole MoE block forward. Replaces MoEFFN.forward (agillm41.py:4389-4431)
+ * in eval mode:
+ *   x [n, d]; w_router [E, d]; w1 [E, H, d]; b1 [E, H]; w2 [E, d, H]; b2 [E, d];
+ *   shared experts (n_shared may be 0): ws1 [S, Hs, d]; sb1 [S, Hs];
+ *   ws2 [S, d, Hs]; sb2 [S, d];  out [n, d].
+ *   Optional outputs (nullable): idx_out int32 [n, k], gates_out [n, k],
+ *   counts_out int32 [E], logits_out fp32 [n, E].
+ *   The device error word is the first int of the workspace.
+ *   stage_events (nullable): AGM_STAGE_EVENTS cudaEvent_t handles recorded on
+ *   `stream` before the router and after the router, dispatch plan, permute,
+ *   FC1, FC2, shared experts and combine (for per-kernel timing).
+ * No host synchronisation; every kernel runs on `stream`.                  */
+AGM_API int agm_moe_forward(const void* x, int dtype, int64_t n_tokens, int d, int n_experts, int top_k, int hidden,
+                    const void* w_router, const void* w1, const void* b1, const void* w2, const void* b2, int n_shared,
+                    int shared_hidden, const void* ws1, const void* sb1, const void* ws2, const void* sb2, void* out,
+                    void* workspace, size_t workspace_bytes, int flags, int32_t* idx_out, void* gates_out,
+                    int32_t* counts_out, float* logits_out, void* const* stage_events, void* stream);
+
+/* Synchronise `stream`, read the device error word at `err` (e.g. the first
+ * int of a forward workspace) into *code and reset it to 0. Returns AGM_OK if
+ * the word was 0, AGM_ERR_DEVICE otherwise.                                */
+AGM_API int agm_read_device_error(int* err, int* code, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AGILLM_MOE_H_ */

@@ -1,0 +1,112 @@
+"""Torch restatement of the reference MoE block forward (oracle; test infrastructure).
+
+Follows ``MoEFFN`` in the reference's ``agillm41.py``:
+
+* constructor / parameter structure  agillm41.py:4324-4360
+* expert = Linear(d,H) -> ReLU -> Linear(H,d)  agillm41.py:4332-4336
+* forward                            agillm41.py:4389-4431
+    - flatten                        4390-4391
+    - router logits in weight dtype, then ``.float()``   4398-4399
+    - top-1 branch (softmax, argmax, straight-through gate)  4401-4416
+    - top-k branch: ``topk`` on the fp32 logits, softmax over the k
+      values, cast to the activation dtype                 4418-4419
+    - per (rank, expert) ``nonzero`` / ``index_select`` / expert /
+      ``* weight`` / ``index_add_`` into ``zeros_like(flat)``  4420-4428
+    - shared experts: ``s = shared[0](flat); s = s + shared[i](flat)``,
+      ``out = out + s``                                     4381-4387, 4429-4430
+
+The restatement uses exactly the same torch calls in the same order as the
+reference, so on the same device and dtype it reproduces the reference bit for
+bit (``tests/golden/make_golden.py`` asserts this against the imported
+reference module). Weights are passed as a state-dict mapping with the
+reference's keys (``router.weight``, ``experts.{e}.{0,2}.{weight,bias}``,
+``shared.{s}.{0,2}.{weight,bias}``).
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline
+leg use this module.
+"""
+from __future__ import annotations
+
+from typing import Dict, Mapping, Optional
+
+import torch
+import torch.nn.functional as F
+
+
+def _expert(sd: Mapping[str, torch.Tensor], prefix: str, rows: torch.Tensor) -> torch.Tensor:
+    # nn.Sequential(nn.Linear(d, H), nn.ReLU(), nn.Linear(H, d)): agillm41.py:4332-4336
+    h = F.linear(rows, sd[prefix + "0.weight"], sd[prefix + "0.bias"])
+    h = torch.relu(h)
+    return F.linear(h, sd[prefix + "2.weight"], sd[prefix + "2.bias"])
+
+
+def num_experts_in(sd: Mapping[str, torch.Tensor]) -> int:
+    return int(sd["router.weight"].shape[0])
+
+
+def num_shared_in(sd: Mapping[str, torch.Tensor]) -> int:
+    n = 0
+    while f"shared.{n}.0.weight" in sd:
+        n += 1
+    return n
+
+
+def moe_forward(x: torch.Tensor, sd: Mapping[str, torch.Tensor], top_k: int,
+                aux: Optional[Dict[str, torch.Tensor]] = None) -> torch.Tensor:
+    """Reference MoE forward (agillm41.py:4389-4431), eval mode.
+
+    ``aux`` (optional dict) receives ``logits`` (fp32 [N,E]), ``idx`` (int64
+    [N,k]), ``gates`` ([N,k], activation dtype) and ``counts`` (int64 [E]).
+    """
+    E = num_experts_in(sd)
+    k = min(max(1, int(top_k)), E)                                  # 4329
+    orig_shape = x.shape
+    flat = x.reshape(-1, orig_shape[-1])                             # 4391
+    wr = sd["router.weight"]
+    router_in = flat.to(wr.dtype) if flat.dtype != wr.dtype else flat  # 4398
+    scores = F.linear(router_in, wr).float()                         # 4399
+    n_shared = num_shared_in(sd)
+
+    if k == 1:                                                       # 4401-4416
+        probs = scores.softmax(dim=-1)
+        chosen = probs.argmax(dim=-1)
+        out = torch.zeros_like(flat)
+        for e in range(E):
+            mask = chosen == e
+            if not bool(mask.any()):
+                continue
+            gate = probs[mask, e].to(flat.dtype).clamp_min(1e-6)
+            gate_st = (gate / gate.detach()).unsqueeze(-1)
+            out[mask] = _expert(sd, f"experts.{e}.", flat[mask]) * gate_st
+        idx = chosen.unsqueeze(-1)
+        gates = torch.ones_like(idx, dtype=flat.dtype)
+    else:
+        vals, idx = torch.topk(scores, k=k, dim=-1)                  # 4418
+        weights = vals.softmax(dim=-1).to(flat.dtype)                # 4419
+        out = torch.zeros_like(flat)                                 # 4420
+        for rank in range(k):                                        # 4421
+            chosen = idx[:, rank]
+            weight = weights[:, rank].unsqueeze(-1)
+            for e in range(E):                                       # 4424
+                rows = (chosen == e).nonzero(as_tuple=False).flatten()
+                if rows.numel() == 0:
+                    continue
+                out.index_add_(0, rows, _expert(sd, f"experts.{e}.", flat.index_select(0, rows))
+                               * weight.index_select(0, rows))       # 4428
+        gates = weights
+    if n_shared > 0:                                                 # 4429-4430, 4381-4387
+        s = _expert(sd, "shared.0.", flat)
+        for i in range(1, n_shared):
+            s = s + _expert(sd, f"shared.{i}.", flat)
+        out = out + s
+    if aux is not None:
+        aux["logits"] = scores
+        aux["idx"] = idx
+        aux["gates"] = gates
+        aux["counts"] = torch.bincount(idx.reshape(-1), minlength=E)
+    return out.reshape(orig_shape)
+
+
+# Seeded synthetic weights and inputs (the workload definitions) live in the
+# package so that the benchmark can build its workload without the oracle.
+from agillm41_b200.synthetic import BIAS_ALPHA, make_input, make_state, zipf_logit_bias  # noqa: E402,F401

@@ -1,0 +1,69 @@
+"""Loading helpers for the golden vectors in tests/golden/*.npz."""
+import glob
+import hashlib
+import os
+
+import numpy as np
+import torch
+
+from oracle.golden_cases import case_by_name, case_inputs
+
+GOLDEN_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+DTYPES = {"float32": torch.float32, "bfloat16": torch.bfloat16, "float16": torch.float16}
+
+
+def names():
+    return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz")))
+
+
+def _to_np(t):
+    t = t.detach().cpu().contiguous()
+    if t.dtype == torch.bfloat16:
+        return t.view(torch.int16).numpy().view(np.uint16)
+    return t.numpy()
+
+
+def sha(t):
+    return hashlib.sha256(_to_np(t).tobytes()).hexdigest()
+
+
+def state_sha(sd):
+    h = hashlib.sha256()
+    for k in sorted(sd):
+        h.update(k.encode())
+        h.update(_to_np(sd[k]).tobytes())
+    return h.hexdigest()
+
+
+def from_np(a, dtype):
+    if dtype == torch.bfloat16:
+        return torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).view(torch.bfloat16)
+    return torch.from_numpy(np.ascontiguousarray(a))
+
+
+class Golden:
+    """One golden case: regenerated inputs (hash-checked) and reference outputs."""
+
+    def __init__(self, name):
+        self.name = name
+        self.z = np.load(os.path.join(GOLDEN_DIR, name + ".npz"))
+        z = self.z
+        self.case = case_by_name(name)
+        self.dtype = DTYPES[str(z["dtype"])]
+        self.top_k = int(z["top_k"])
+        self.E = int(z["experts"])
+        self.d = int(z["d"])
+        self.H = int(z["hidden"])
+        self.N = int(z["n_tokens"])
+        self.shared = int(z["shared"])
+        sd32, x32 = case_inputs(self.case)
+        self.sd = {k: v.to(self.dtype) for k, v in sd32.items()}
+        self.x = x32.to(self.dtype)
+        self.out = from_np(z["out"], self.dtype)
+        self.logits = torch.from_numpy(z["logits"])
+        self.idx = torch.from_numpy(z["idx"].astype(np.int64))
+        self.gates = from_np(z["gates"], self.dtype)
+        self.counts = torch.from_numpy(z["counts"].astype(np.int64))
+
+    def inputs_match(self):
+        return sha(self.x) == str(self.z["x_sha256"]) and state_sha(self.sd) == str(self.z["state_sha256"])

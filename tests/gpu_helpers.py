@@ -1,0 +1,47 @@
+"""Shared helpers for the GPU parity tests."""
+import torch
+
+from oracle import reference_moe
+
+BF16_RTOL, BF16_ATOL = 2e-2, 1e-2   # bf16 output tolerance (reference parity rule)
+F32_TOL = 1e-4                      # fp32 mode tolerance
+
+
+def packed(sd, E, device):
+    """Stack the reference state dict into the kernel's [E, ...] layout."""
+    w1 = torch.stack([sd[f"experts.{e}.0.weight"] for e in range(E)]).to(device).contiguous()
+    b1 = torch.stack([sd[f"experts.{e}.0.bias"] for e in range(E)]).to(device).contiguous()
+    w2 = torch.stack([sd[f"experts.{e}.2.weight"] for e in range(E)]).to(device).contiguous()
+    b2 = torch.stack([sd[f"experts.{e}.2.bias"] for e in range(E)]).to(device).contiguous()
+    S = reference_moe.num_shared_in(sd)
+    shared = None
+    if S:
+        shared = tuple(torch.stack([sd[f"shared.{s}.{i}.{p}"] for s in range(S)]).to(device).contiguous()
+                       for i, p in ((0, "weight"), (0, "bias"), (2, "weight"), (2, "bias")))
+    return w1, b1, w2, b2, shared
+
+
+def explained_index_mismatches(our_idx, ref_idx, our_logits, ref_logits, k):
+    """Rows whose top-k indices differ; each must coincide with a logit that
+    differs from the reference's (fp32 summation order can flip a bf16
+    rounding) or with an exact tie among the reference's top k+1 logits."""
+    diff = (our_idx.long() != ref_idx.long()).any(dim=1)
+    rows = diff.nonzero().flatten()
+    unexplained = []
+    E = ref_logits.shape[1]
+    kk = min(k + 1, E)
+    for t in rows.tolist():
+        if not torch.equal(our_logits[t], ref_logits[t]):
+            continue
+        top = torch.topk(ref_logits[t], kk).values
+        if (top[1:] == top[:-1]).any():
+            continue
+        unexplained.append(t)
+    return rows, unexplained
+
+
+def assert_close_rows(ours, ref, rows_ok, dtype):
+    if dtype == torch.float32:
+        torch.testing.assert_close(ours[rows_ok], ref[rows_ok], rtol=F32_TOL, atol=F32_TOL)
+    else:
+        torch.testing.assert_close(ours[rows_ok].float(), ref[rows_ok].float(), rtol=BF16_RTOL, atol=BF16_ATOL)

@@ -1,0 +1,94 @@
+"""The C-ABI library loads on a host without a GPU and exports exactly the
+entry points that include/agillm_moe.h declares; argument errors are reported
+without touching a device."""
+import ctypes
+import os
+import re
+
+import pytest
+
+import agillm41_b200
+from agillm41_b200 import _lib
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "agillm_moe.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"AGM_API\s+[\w\s\*]+?\b(agm_\w+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    syms = declared_symbols()
+    assert "agm_moe_forward" in syms and "agm_router_topk" in syms
+    assert set(syms) == set(_lib.SIGNATURES), "ctypes signature table out of sync with the header"
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for s in declared_symbols():
+        assert hasattr(lib, s), s
+    assert lib.agm_abi_version() == 1
+
+
+def test_library_has_no_driver_link_dependency():
+    # The driver is resolved at run time; the .so must load where no libcuda exists.
+    ctypes.CDLL(_lib.LIB_PATH)
+
+
+def test_size_helpers():
+    lib = _lib.load()
+    assert lib.agm_dispatch_blocks(0) == 0
+    assert lib.agm_dispatch_blocks(1) == 1
+    assert lib.agm_dispatch_blocks(256) == 1
+    assert lib.agm_dispatch_blocks(257) == 2
+    assert lib.agm_max_rows(73728, 2, 14) == ((2 * 73728 + 14 * 127 + 127) // 128) * 128
+    assert lib.agm_max_rows(0, 2, 14) == 0
+    ws = lib.agm_moe_workspace_bytes(73728, 1280, 14, 2, 3200, 0, 1, _lib.AGM_BF16)
+    rows = lib.agm_max_rows(73728, 2, 14)
+    # x_perm/y and h dominate: rows * (d + H) * 2 bytes.
+    assert ws >= rows * (1280 + 3200) * 2
+    assert ws < rows * (1280 + 3200) * 2 + 64 * 1024 * 1024
+
+
+@pytest.mark.parametrize("call,code", [
+    ("bad_dtype", _lib.AGM_OK - 1),
+    ("bad_topk", _lib.AGM_OK - 1),
+    ("too_many_experts", _lib.AGM_OK - 2),
+    ("odd_d", _lib.AGM_OK - 2),
+    ("null_ptrs", _lib.AGM_OK - 1),
+])
+def test_argument_errors_are_reported(call, code):
+    lib = _lib.load()
+    fake = ctypes.c_void_p(4096)  # never dereferenced: validation fails first
+    args = dict(x=fake, w=fake, dtype=_lib.AGM_BF16, n=16, d=64, E=14, k=2)
+    if call == "bad_dtype":
+        args["dtype"] = 7
+    elif call == "bad_topk":
+        args["k"] = 15
+    elif call == "too_many_experts":
+        args["E"] = 17
+    elif call == "odd_d":
+        args["d"] = 60
+    if call == "null_ptrs":
+        rc = lib.agm_router_topk(fake, fake, args["dtype"], 16, 64, 14, 2, 0, None, None, None, None, None, None,
+                                 None)
+    else:
+        rc = lib.agm_router_topk(args["x"], args["w"], args["dtype"], args["n"], args["d"], args["E"], args["k"], 0,
+                                 None, None, fake, fake, fake, None, None)
+    assert rc == code
+    assert lib.agm_last_error().decode()
+
+
+def test_forward_rejects_small_workspace():
+    lib = _lib.load()
+    fake = ctypes.c_void_p(4096)
+    rc = lib.agm_moe_forward(fake, _lib.AGM_BF16, 1024, 64, 14, 2, 128, fake, fake, fake, fake, fake, 0, 1, None,
+                             None, None, None, fake, fake, 1024, 0, None, None, None, None, None, None)
+    assert rc == -5
+    assert "workspace" in lib.agm_last_error().decode()
+
+
+def test_package_exports():
+    assert agillm41_b200.MoEFFN is not None
+    assert os.path.exists(agillm41_b200.LIB_PATH)
