@@ -97,15 +97,17 @@ __global__ void __launch_bounds__(kDispatchBlock) router_topk_kernel(
   extern __shared__ __align__(16) float smem_f[];
   constexpr int CH = 16 / sizeof(T);  // elements per 16-byte chunk
   const int nchunk = d / CH;
-  float* w_s = smem_f;                                      // [E][d] fp32
-  float* logit_s = smem_f + E * d;                          // [8 warps][32 tok][16]
+  const bool compute = (logits_in == nullptr);
+  // Dynamic smem: [E][d] fp32 router weight (only when computing logits),
+  // then [8 warps][32 tokens][16] fp32 logits.
+  float* w_s = smem_f;
+  float* logit_s = smem_f + (compute ? E * d : 0);
   __shared__ int hist_s[kMaxExperts];
 
   const int warp = warp_id(), lane = lane_id();
   const int64_t blk_tok0 = static_cast<int64_t>(blockIdx.x) * kDispatchBlock;
   if (threadIdx.x < kMaxExperts) hist_s[threadIdx.x] = 0;
 
-  const bool compute = (logits_in == nullptr);
   if (compute) {
     // Stage W (vectorised, 16 B per thread per step), converting to fp32.
     const int total_chunks = E * nchunk;
