@@ -20,7 +20,7 @@ AGM_OK = 0
 AGM_TILE_M = 128
 AGM_DISPATCH_BLOCK = 256
 AGM_MAX_EXPERTS = 16
-AGM_FLAG_TIE_SWAP = 0x1
+AGM_FLAG_TIE_LOW_FIRST = 0x1
 AGM_STAGE_EVENTS = 8
 
 _DTYPE_CODE = {torch.float32: AGM_F32, torch.bfloat16: AGM_BF16, torch.float16: AGM_F16}
@@ -39,7 +39,7 @@ SIGNATURES = {
     "agm_combine": (_I, [_P, _P, _P, _I, _I64, _I, _I, _P, _I, _I64, _P, _P]),
     "agm_moe_workspace_bytes": (_SZ, [_I64, _I, _I, _I, _I, _I, _I, _I]),
     "agm_moe_forward": (_I, [_P, _I, _I64, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _P, _P,
-                             _P, _SZ, _I, _P, _P, _P, _P, _P, _P]),
+                             _P, _SZ, _I, _P, _P, _P, _P, _P, _P, _P]),
     "agm_read_device_error": (_I, [_P, _P, _P]),
 }
 

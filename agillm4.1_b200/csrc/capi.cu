@@ -147,7 +147,7 @@ int agm_router_topk(const void* x, const void* w_router, int dtype, int64_t n_to
     return fail(AGM_ERR_ARG, "x and w_router must be 16-byte aligned");
   if (!logits_in && agm::router_smem_bytes(d, n_experts) > 227 * 1024)
     return fail(AGM_ERR_UNSUPPORTED, "router weight does not fit in shared memory (E * d * 4 bytes > 211 KB)");
-  cudaError_t e = agm::router_topk(dtype, x, w_router, n_tokens, d, n_experts, top_k, flags & AGM_FLAG_TIE_SWAP,
+  cudaError_t e = agm::router_topk(dtype, x, w_router, n_tokens, d, n_experts, top_k, flags & AGM_FLAG_TIE_LOW_FIRST,
                                    logits_in, logits_out, idx, gates, block_hist, err,
                                    static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? AGM_OK : cuda_fail(e, "router_topk");
@@ -242,7 +242,8 @@ int agm_moe_forward(const void* x, int dtype, int64_t n_tokens, int d, int n_exp
                     const void* w_router, const void* w1, const void* b1, const void* w2, const void* b2, int n_shared,
                     int shared_hidden, const void* ws1, const void* sb1, const void* ws2, const void* sb2, void* out,
                     void* workspace, size_t workspace_bytes, int flags, int32_t* idx_out, void* gates_out,
-                    int32_t* counts_out, float* logits_out, void* const* stage_events, void* stream_) {
+                    int32_t* counts_out, float* logits_out, const float* logits_in, void* const* stage_events,
+                    void* stream_) {
   int rc = check_common(dtype, d, n_experts, top_k);
   if (rc) return rc;
   const int eb = elem_bytes(dtype);
@@ -282,8 +283,8 @@ int agm_moe_forward(const void* x, int dtype, int64_t n_tokens, int d, int n_exp
   const int64_t max_tiles = rows / AGM_TILE_M;
 
   if ((e = mark(0)) != cudaSuccess) return cuda_fail(e, "event record");
-  e = agm::router_topk(dtype, x, w_router, n_tokens, d, n_experts, top_k, flags & AGM_FLAG_TIE_SWAP, nullptr,
-                       logits_out, idx, gates, L.block_hist, L.err, stream);
+  e = agm::router_topk(dtype, x, w_router, n_tokens, d, n_experts, top_k, flags & AGM_FLAG_TIE_LOW_FIRST,
+                       logits_in, logits_out, idx, gates, L.block_hist, L.err, stream);
   if (e != cudaSuccess) return cuda_fail(e, "router_topk");
   if ((e = mark(1)) != cudaSuccess) return cuda_fail(e, "event record");
   e = agm::dispatch_plan(L.block_hist, static_cast<int>(agm_dispatch_blocks(n_tokens)), n_experts, rows,

@@ -59,7 +59,9 @@ __global__ void __launch_bounds__(256) combine_kernel(const T* __restrict__ y_pe
             unpack8<T>(v[r], f);
           }
 #pragma unroll
-          for (int j = 0; j < CH; ++j) acc[j] = round_to<T>(acc[j] + round_to<T>(f[j] * g[r]));
+          // __fmul_rn/__fadd_rn: never contracted into an FMA, so the product
+          // is rounded on its own as in the reference's `y * w` tensor.
+          for (int j = 0; j < CH; ++j) acc[j] = round_to<T>(__fadd_rn(acc[j], round_to<T>(__fmul_rn(f[j], g[r]))));
         }
       }
       if (n_shared > 0) {
@@ -74,10 +76,10 @@ __global__ void __launch_bounds__(256) combine_kernel(const T* __restrict__ y_pe
             unpack8<T>(u, f);
           }
 #pragma unroll
-          for (int j = 0; j < CH; ++j) s[j] = (si == 0) ? f[j] : round_to<T>(s[j] + f[j]);
+          for (int j = 0; j < CH; ++j) s[j] = (si == 0) ? f[j] : round_to<T>(__fadd_rn(s[j], f[j]));
         }
 #pragma unroll
-        for (int j = 0; j < CH; ++j) acc[j] = round_to<T>(acc[j] + s[j]);
+        for (int j = 0; j < CH; ++j) acc[j] = round_to<T>(__fadd_rn(acc[j], s[j]));
       }
       uint4 o;
       if constexpr (sizeof(T) == 4) {

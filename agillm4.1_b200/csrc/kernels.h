@@ -23,7 +23,7 @@ struct GemmArgs {
 };
 
 cudaError_t router_topk(int dtype, const void* x, const void* w, int64_t n_tokens, int d, int E, int k,
-                        int tie_swap, const float* logits_in, float* logits_out, int32_t* idx, void* gates,
+                        int tie_low_first, const float* logits_in, float* logits_out, int32_t* idx, void* gates,
                         int32_t* block_hist, int* err, cudaStream_t stream);
 size_t router_smem_bytes(int d, int E);
 cudaError_t dispatch_plan(const int32_t* block_hist, int n_blocks, int E, int64_t max_rows, int max_tiles,

@@ -41,6 +41,15 @@ class _B200Forward:
     # Set to True to synchronise and check the device error word after each
     # forward (tests do; the hot path does not).
     check_device_errors = False
+    # Where the router logits come from:
+    #   "kernel"         - the router kernel: fp32 accumulation of the bf16/fp16
+    #                      products, one rounding to the activation dtype;
+    #   "reference_gemm" - the reference's own call, `router(x).float()`
+    #                      (agillm41.py:4398-4399, a library GEMM), then the
+    #                      same selection kernel. On the same GPU this gives
+    #                      routing bit-identical to the reference, whose
+    #                      library GEMM may round its split-K partial sums.
+    router_logits = "kernel"
 
     def _packed_weights(self, device: torch.device, dtype: torch.dtype):
         """Expert weights as contiguous [E, ...] device tensors, with the
@@ -101,8 +110,14 @@ class _B200Forward:
         if flat.dtype != wr.dtype:
             raise MoEKernelError(f"input dtype {flat.dtype} differs from the weight dtype {wr.dtype}")
         w1, b1, w2, b2, sh = self._packed_weights(flat.device, flat.dtype)
-        out = ops.moe_forward(flat.contiguous(), wr.detach().contiguous(), w1, b1, w2, b2, self.top_k,
-                              shared=sh, check_errors=self.check_device_errors)
+        flat = flat.contiguous()
+        logits_in = None
+        if self.router_logits == "reference_gemm":
+            logits_in = self.router(flat).float()
+        elif self.router_logits != "kernel":
+            raise MoEKernelError(f"router_logits must be 'kernel' or 'reference_gemm', not {self.router_logits!r}")
+        out = ops.moe_forward(flat, wr.detach().contiguous(), w1, b1, w2, b2, self.top_k, shared=sh,
+                              check_errors=self.check_device_errors, logits_in=logits_in)
         return out.reshape(orig_shape)
 
 

@@ -19,16 +19,13 @@ from typing import Dict, Optional
 import torch
 
 from . import _lib
-from ._lib import AGM_FLAG_TIE_SWAP, AGM_TILE_M, check, dtype_code, load, ptr, stream_handle
+from ._lib import AGM_FLAG_TIE_LOW_FIRST, AGM_TILE_M, check, dtype_code, load, ptr, stream_handle
 
-# Order of two exactly-equal top-k values. The reference selects with
-# torch.topk on the device it runs on; `tie_swap=True` reverses the order of
-# an exactly-equal adjacent pair relative to ascending expert index.
-DEFAULT_TIE_SWAP = False
-
-
-def _flags(tie_swap: Optional[bool]) -> int:
-    return AGM_FLAG_TIE_SWAP if (DEFAULT_TIE_SWAP if tie_swap is None else tie_swap) else 0
+# Order of exactly-equal top-k values. The default follows torch.topk on a
+# CUDA device (descending expert index among equal values); `tie_low_first`
+# orders them by ascending index instead.
+def _flags(tie_low_first: bool) -> int:
+    return AGM_FLAG_TIE_LOW_FIRST if tie_low_first else 0
 
 
 def dispatch_blocks(n_tokens: int) -> int:
@@ -40,7 +37,7 @@ def max_rows(n_tokens: int, top_k: int, n_experts: int) -> int:
 
 
 def router_topk(x: torch.Tensor, w_router: torch.Tensor, top_k: int, *, logits_in: Optional[torch.Tensor] = None,
-                want_logits: bool = False, tie_swap: Optional[bool] = None, err: Optional[torch.Tensor] = None):
+                want_logits: bool = False, tie_low_first: bool = False, err: Optional[torch.Tensor] = None):
     """Returns (idx int32 [N,k], gates [N,k], block_hist int32 [nb,E], logits fp32 [N,E] or None)."""
     lib = load()
     n, d = x.shape
@@ -52,7 +49,7 @@ def router_topk(x: torch.Tensor, w_router: torch.Tensor, top_k: int, *, logits_i
     logits = torch.empty(n, E, dtype=torch.float32, device=dev) if want_logits else None
     if logits_in is not None:
         logits_in = logits_in.to(dtype=torch.float32).contiguous()
-    rc = lib.agm_router_topk(ptr(x), ptr(w_router), dtype_code(x.dtype), n, d, E, top_k, _flags(tie_swap),
+    rc = lib.agm_router_topk(ptr(x), ptr(w_router), dtype_code(x.dtype), n, d, E, top_k, _flags(tie_low_first),
                              ptr(logits_in), ptr(logits), ptr(idx), ptr(gates), ptr(hist), ptr(err),
                              stream_handle(dev))
     check(rc, "agm_router_topk")
@@ -176,12 +173,14 @@ def workspace_bytes(n_tokens: int, d: int, n_experts: int, top_k: int, hidden: i
 
 def moe_forward(x: torch.Tensor, w_router: torch.Tensor, w1: torch.Tensor, b1: torch.Tensor, w2: torch.Tensor,
                 b2: torch.Tensor, top_k: int, *, shared: Optional[tuple] = None, out: Optional[torch.Tensor] = None,
-                want: tuple = (), tie_swap: Optional[bool] = None, workspace: Optional[torch.Tensor] = None,
-                check_errors: bool = False, stage_events=None):
+                want: tuple = (), tie_low_first: bool = False, workspace: Optional[torch.Tensor] = None,
+                check_errors: bool = False, stage_events=None, logits_in: Optional[torch.Tensor] = None):
     """Fused forward: x [N, d] -> out [N, d]. ``want`` may hold 'idx', 'gates', 'counts', 'logits'.
 
     Weights: w_router [E, d]; w1 [E, H, d]; b1 [E, H]; w2 [E, d, H]; b2 [E, d];
     shared = (ws1 [S,Hs,d], sb1 [S,Hs], ws2 [S,d,Hs], sb2 [S,d]) or None.
+    ``logits_in``: optional fp32 [N, E] router logits to route with instead
+    of computing them in the router kernel.
     ``stage_events``: optional list of AGM_STAGE_EVENTS torch.cuda.Event
     (timing enabled) recorded around each kernel stage on the current stream.
     Returns out, or (out, extras dict) when ``want`` is not empty.
@@ -215,8 +214,9 @@ def moe_forward(x: torch.Tensor, w_router: torch.Tensor, w1: torch.Tensor, b1: t
     rc = lib.agm_moe_forward(
         ptr(x), dtype_code(x.dtype), n, d, E, top_k, H, ptr(w_router), ptr(w1), ptr(b1), ptr(w2), ptr(b2), S,
         max(Hs, 1), ptr(ws1), ptr(sb1), ptr(ws2), ptr(sb2), ptr(out), ptr(workspace), workspace.numel(),
-        _flags(tie_swap), ptr(extras.get("idx")), ptr(extras.get("gates")), ptr(extras.get("counts")),
-        ptr(extras.get("logits")), None if ev_arr is None else ctypes.addressof(ev_arr), stream_handle(dev))
+        _flags(tie_low_first), ptr(extras.get("idx")), ptr(extras.get("gates")), ptr(extras.get("counts")),
+        ptr(extras.get("logits")), ptr(logits_in), None if ev_arr is None else ctypes.addressof(ev_arr),
+        stream_handle(dev))
     check(rc, "agm_moe_forward")
     if check_errors:
         code = _lib.read_device_error(workspace[:4].view(torch.int32))

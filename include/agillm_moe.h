@@ -58,7 +58,8 @@ enum {
 #define AGM_STAGE_EVENTS 8
 
 /* forward flags */
-#define AGM_FLAG_TIE_SWAP 0x1 /* reverse the order of exactly-equal top-k pairs */
+#define AGM_FLAG_TIE_LOW_FIRST 0x1 /* order exactly-equal top-k values by ascending expert index
+                                      (default: descending, as torch.topk does on CUDA) */
 
 AGM_API const char* agm_last_error(void);
 AGM_API int agm_abi_version(void);
@@ -76,7 +77,7 @@ AGM_API int64_t agm_max_rows(int64_t n_tokens, int top_k, int n_experts);
  *   logits_in  (nullable) fp32 [n, E]: select from these logits instead of
  *                                     computing them (bit-exactness checks)
  *   logits_out (nullable) fp32 [n, E]: the logits (rounded like the reference)
- *   flags: AGM_FLAG_TIE_SWAP
+ *   flags: AGM_FLAG_TIE_LOW_FIRST
  *   err: device int (nullable)                                                */
 AGM_API int agm_router_topk(const void* x, const void* w_router, int dtype, int64_t n_tokens, int d, int n_experts,
                     int top_k, int flags, const float* logits_in, float* logits_out, int32_t* idx, void* gates,
@@ -129,6 +130,9 @@ AGM_API size_t agm_moe_workspace_bytes(int64_t n_tokens, int d, int n_experts, i
  *   ws2 [S, d, Hs]; sb2 [S, d];  out [n, d].
  *   Optional outputs (nullable): idx_out int32 [n, k], gates_out [n, k],
  *   counts_out int32 [E], logits_out fp32 [n, E].
+ *   logits_in (nullable) fp32 [n, E]: route with these router logits instead
+ *   of computing them (e.g. the logits of the library GEMM the reference
+ *   calls, for routing that is bit-exact with it on the same GPU).
  *   The device error word is the first int of the workspace.
  *   stage_events (nullable): AGM_STAGE_EVENTS cudaEvent_t handles recorded on
  *   `stream` before the router and after the router, dispatch plan, permute,
@@ -138,7 +142,8 @@ AGM_API int agm_moe_forward(const void* x, int dtype, int64_t n_tokens, int d, i
                     const void* w_router, const void* w1, const void* b1, const void* w2, const void* b2, int n_shared,
                     int shared_hidden, const void* ws1, const void* sb1, const void* ws2, const void* sb2, void* out,
                     void* workspace, size_t workspace_bytes, int flags, int32_t* idx_out, void* gates_out,
-                    int32_t* counts_out, float* logits_out, void* const* stage_events, void* stream);
+                    int32_t* counts_out, float* logits_out, const float* logits_in, void* const* stage_events,
+                    void* stream);
 
 /* Synchronise `stream`, read the device error word at `err` (e.g. the first
  * int of a forward workspace) into *code and reset it to 0. Returns AGM_OK if

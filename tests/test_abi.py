@@ -84,7 +84,7 @@ def test_forward_rejects_small_workspace():
     lib = _lib.load()
     fake = ctypes.c_void_p(4096)
     rc = lib.agm_moe_forward(fake, _lib.AGM_BF16, 1024, 64, 14, 2, 128, fake, fake, fake, fake, fake, 0, 1, None,
-                             None, None, None, fake, fake, 1024, 0, None, None, None, None, None, None)
+                             None, None, None, fake, fake, 1024, 0, None, None, None, None, None, None, None)
     assert rc == -5
     assert "workspace" in lib.agm_last_error().decode()
 
