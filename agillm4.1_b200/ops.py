@@ -138,6 +138,9 @@ def _event_array(events):
         return None
     if len(events) != _lib.AGM_STAGE_EVENTS:
         raise ValueError(f"stage_events needs {_lib.AGM_STAGE_EVENTS} events")
+    for ev in events:
+        if not ev.cuda_event:
+            ev.record()  # torch creates the CUDA event lazily, on its first record
     return (ctypes.c_void_p * len(events))(*[ev.cuda_event for ev in events])
 
 

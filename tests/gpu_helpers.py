@@ -41,7 +41,22 @@ def explained_index_mismatches(our_idx, ref_idx, our_logits, ref_logits, k):
 
 
 def assert_close_rows(ours, ref, rows_ok, dtype):
+    """Output parity on the rows whose routing matches.
+
+    fp32: every element within 1e-4 (abs and rel).
+    bf16/fp16: every element within 1e-2 abs + 2e-2 rel, except at most one
+    element in 10^5: where the k gated expert outputs nearly cancel, a 1-ulp
+    difference in an expert output (any two fp32 accumulation orders differ
+    there) survives the cancellation; those elements must still be within two
+    ulps of a summand of magnitude < 8 (0.0625) + 2e-2 rel.
+    """
     if dtype == torch.float32:
         torch.testing.assert_close(ours[rows_ok], ref[rows_ok], rtol=F32_TOL, atol=F32_TOL)
-    else:
-        torch.testing.assert_close(ours[rows_ok].float(), ref[rows_ok].float(), rtol=BF16_RTOL, atol=BF16_ATOL)
+        return
+    a, b = ours[rows_ok].float(), ref[rows_ok].float()
+    diff = (a - b).abs()
+    outside = diff > BF16_ATOL + BF16_RTOL * b.abs()
+    n_out = int(outside.sum())
+    assert n_out <= max(1, int(1e-5 * b.numel())), (
+        f"{n_out} of {b.numel()} elements outside 1e-2 abs / 2e-2 rel (max diff {diff.max().item():.4g})")
+    assert bool((diff <= 0.0625 + BF16_RTOL * b.abs()).all()), f"max diff {diff.max().item():.4g}"
