@@ -93,7 +93,7 @@ class ClockSampler:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
@@ -218,9 +218,10 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
-def workload_config(world):
-    return {"workload": f"MoE block forward B{BATCH} L{SEQ} d{D} E{EXPERTS} H{HIDDEN} top{TOP_K} bf16 seed{SEED}",
-            "global_batch": BATCH * world, "seq_len": SEQ, "tokens_per_gpu": BATCH * SEQ, "d_model": D,
+def workload_config(world, tokens=BATCH * SEQ):
+    shape = f"B{BATCH} L{SEQ}" if tokens == BATCH * SEQ else f"{tokens} tokens"
+    return {"workload": f"MoE block forward {shape} d{D} E{EXPERTS} H{HIDDEN} top{TOP_K} bf16 seed{SEED}",
+            "global_batch": BATCH * world, "seq_len": SEQ, "tokens_per_gpu": tokens, "d_model": D,
             "experts": EXPERTS, "expert_hidden": HIDDEN, "top_k": TOP_K,
             "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
             "l2": "inputs larger than L2 (x 189 MB + expert weights 229 MB > 126 MB); no flush"}
@@ -232,7 +233,7 @@ def run_ours(args, world, rank, local):
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    N = BATCH * SEQ
+    N = args.tokens
     sd = synthetic.make_state(D, HIDDEN, EXPERTS, SEED + rank * 1000, dtype=torch.bfloat16, device=dev)
     x = synthetic.make_input(N, D, SEED + rank * 1000, dtype=torch.bfloat16, device=dev)
     w1 = torch.stack([sd[f"experts.{e}.0.weight"] for e in range(EXPERTS)]).contiguous()
@@ -276,15 +277,25 @@ def run_ours(args, world, rank, local):
     clocks = clk.summary()
     value = N * world * args.steps / (ms_total / 1000.0)
 
-    # ---- end to end through the public module API with host buffers ----
+    if args.skip_e2e:
+        e2e_value = None
+    else:
+        e2e_value = run_e2e(args, world, dev, sd, x, out, N, stream)
+    report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e_value, x)
+
+
+def run_e2e(args, world, dev, sd, x, out, N, stream):
+    """Same metric through the public module API, host buffers, copies timed."""
+    import agillm41_b200
+
     m = agillm41_b200.MoEFFN(D, mlp_mult=4, experts=EXPERTS, top_k=TOP_K)
     m.experts = torch.nn.ModuleList([torch.nn.Sequential(torch.nn.Linear(D, HIDDEN), torch.nn.ReLU(),
                                                          torch.nn.Linear(HIDDEN, D)) for _ in range(EXPERTS)])
     m = m.to(device=dev, dtype=torch.bfloat16).eval()
     m.load_state_dict(sd)
-    x_host = x.reshape(BATCH, SEQ, D).cpu().pin_memory()
+    x_host = x.reshape(1, N, D).cpu().pin_memory()
     y_host = torch.empty_like(x_host).pin_memory()
-    x_dev = torch.empty(BATCH, SEQ, D, dtype=torch.bfloat16, device=dev)
+    x_dev = torch.empty(1, N, D, dtype=torch.bfloat16, device=dev)
 
     def e2e_step():
         x_dev.copy_(x_host, non_blocking=True)
@@ -307,7 +318,11 @@ def run_ours(args, world, rank, local):
     e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
     e2e_value = N * world * args.steps / (e2e_ms / 1000.0)
     assert torch.equal(y_host.reshape(N, D).to(dev), out), "module output differs from the timed forward"
+    return {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": x_host.numel() * 2,
+            "d2h_bytes_per_step": y_host.numel() * 2}
 
+
+def report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e, x):
     if rank != 0:
         return
     peaks = load_peaks()
@@ -322,7 +337,7 @@ def run_ours(args, world, rank, local):
                 "algorithmic_bytes": per_tok * N}
 
     cpu = None
-    if world == 1:
+    if world == 1 and not args.skip_cpu:
         rate, threads, reps, dt = cpu_oracle_rate(2048)
         cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
                "sample": f"2048 tokens of the workload x {reps} forwards ({dt:.1f} s), fp32, "
@@ -332,9 +347,8 @@ def run_ours(args, world, rank, local):
         "warmup": args.warmup, "ms_per_step": ms_total / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) input, N(0,0.02^2) random-init expert weights)",
-        "config": workload_config(world),
-        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": x_host.numel() * 2,
-                "d2h_bytes_per_step": y_host.numel() * 2},
+        "config": workload_config(world, N),
+        "e2e": e2e,
         "gpu_launches": KERNELS_PER_STEP * args.steps,
         "roofline": {"kernel": "grouped_gemm_tc_kernel (FC1+FC2, tcgen05)", "bound": "tensor",
                      "achieved": round(achieved_tf, 1), "peak": peaks["tf_sus"], "unit": "TFLOP/s",
@@ -357,9 +371,13 @@ def run_ours(args, world, rank, local):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--tokens", type=int, default=BATCH * SEQ,
+                    help="tokens per GPU (default: the 48 x 1536 workload; smaller for profiling)")
+    ap.add_argument("--skip-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    ap.add_argument("--skip-cpu", action="store_true", help="skip the CPU baseline leg")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)

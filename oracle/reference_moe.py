@@ -56,7 +56,11 @@ def moe_forward(x: torch.Tensor, sd: Mapping[str, torch.Tensor], top_k: int,
     """Reference MoE forward (agillm41.py:4389-4431), eval mode.
 
     ``aux`` (optional dict) receives ``logits`` (fp32 [N,E]), ``idx`` (int64
-    [N,k]), ``gates`` ([N,k], activation dtype) and ``counts`` (int64 [E]).
+    [N,k]), ``gates`` ([N,k], activation dtype), ``counts`` (int64 [E]) and
+    ``term_scale`` (fp32 [N,d]): the sum of the magnitudes of the terms added
+    into each output element (|y_r * w_r| over ranks, |shared_s| over shared
+    experts), which sets the size of the rounding error the result carries.
+    Computing it does not change the output.
     """
     E = num_experts_in(sd)
     k = min(max(1, int(top_k)), E)                                  # 4329
@@ -67,6 +71,7 @@ def moe_forward(x: torch.Tensor, sd: Mapping[str, torch.Tensor], top_k: int,
     scores = F.linear(router_in, wr).float()                         # 4399
     n_shared = num_shared_in(sd)
 
+    scale = torch.zeros(flat.shape, dtype=torch.float32, device=flat.device) if aux is not None else None
     if k == 1:                                                       # 4401-4416
         probs = scores.softmax(dim=-1)
         chosen = probs.argmax(dim=-1)
@@ -78,6 +83,8 @@ def moe_forward(x: torch.Tensor, sd: Mapping[str, torch.Tensor], top_k: int,
             gate = probs[mask, e].to(flat.dtype).clamp_min(1e-6)
             gate_st = (gate / gate.detach()).unsqueeze(-1)
             out[mask] = _expert(sd, f"experts.{e}.", flat[mask]) * gate_st
+            if aux is not None:
+                scale[mask] = out[mask].float().abs()
         idx = chosen.unsqueeze(-1)
         gates = torch.ones_like(idx, dtype=flat.dtype)
     else:
@@ -91,19 +98,27 @@ def moe_forward(x: torch.Tensor, sd: Mapping[str, torch.Tensor], top_k: int,
                 rows = (chosen == e).nonzero(as_tuple=False).flatten()
                 if rows.numel() == 0:
                     continue
-                out.index_add_(0, rows, _expert(sd, f"experts.{e}.", flat.index_select(0, rows))
-                               * weight.index_select(0, rows))       # 4428
+                term = _expert(sd, f"experts.{e}.", flat.index_select(0, rows)) * weight.index_select(0, rows)
+                out.index_add_(0, rows, term)                        # 4428
+                if aux is not None:
+                    scale.index_add_(0, rows, term.float().abs())
         gates = weights
     if n_shared > 0:                                                 # 4429-4430, 4381-4387
         s = _expert(sd, "shared.0.", flat)
+        if aux is not None:
+            scale += s.float().abs()
         for i in range(1, n_shared):
-            s = s + _expert(sd, f"shared.{i}.", flat)
+            si = _expert(sd, f"shared.{i}.", flat)
+            s = s + si
+            if aux is not None:
+                scale += si.float().abs()
         out = out + s
     if aux is not None:
         aux["logits"] = scores
         aux["idx"] = idx
         aux["gates"] = gates
         aux["counts"] = torch.bincount(idx.reshape(-1), minlength=E)
+        aux["term_scale"] = scale.reshape(orig_shape)
     return out.reshape(orig_shape)
 
 

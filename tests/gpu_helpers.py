@@ -40,22 +40,36 @@ def explained_index_mismatches(our_idx, ref_idx, our_logits, ref_logits, k):
     return rows, unexplained
 
 
-def assert_close_rows(ours, ref, rows_ok, dtype):
+def bf16_ulp(v):
+    e = torch.floor(torch.log2(v.abs().clamp_min(2.0 ** -100)))
+    return torch.pow(2.0, e - 7)
+
+
+def assert_close_rows(ours, ref, rows_ok, dtype, term_scale=None):
     """Output parity on the rows whose routing matches.
 
     fp32: every element within 1e-4 (abs and rel).
-    bf16/fp16: every element within 1e-2 abs + 2e-2 rel, except at most one
-    element in 10^5: where the k gated expert outputs nearly cancel, a 1-ulp
-    difference in an expert output (any two fp32 accumulation orders differ
-    there) survives the cancellation; those elements must still be within two
-    ulps of a summand of magnitude < 8 (0.0625) + 2e-2 rel.
+    bf16/fp16: every element within 1e-2 abs + 2e-2 rel, or - where the gated
+    expert outputs nearly cancel - within two bf16 ulps of the magnitude of
+    the summed terms (`term_scale` from the oracle): any two implementations
+    whose fp32 accumulation orders differ can round an expert output to
+    neighbouring bf16 values, and that step survives the cancellation.
+    Without `term_scale`, at most one element in 10^5 may use a 0.0625 bound.
     """
     if dtype == torch.float32:
         torch.testing.assert_close(ours[rows_ok], ref[rows_ok], rtol=F32_TOL, atol=F32_TOL)
         return
     a, b = ours[rows_ok].float(), ref[rows_ok].float()
     diff = (a - b).abs()
-    outside = diff > BF16_ATOL + BF16_RTOL * b.abs()
+    nominal = BF16_ATOL + BF16_RTOL * b.abs()
+    outside = diff > nominal
+    if term_scale is not None:
+        env = torch.maximum(nominal, 2 * bf16_ulp(term_scale[rows_ok].float()))
+        bad = diff > env
+        assert not bool(bad.any()), (
+            f"{int(bad.sum())} elements beyond the rounding envelope (max diff {diff.max().item():.4g})")
+        assert int(outside.sum()) <= max(1, int(1e-4 * b.numel())), int(outside.sum())
+        return
     n_out = int(outside.sum())
     assert n_out <= max(1, int(1e-5 * b.numel())), (
         f"{n_out} of {b.numel()} elements outside 1e-2 abs / 2e-2 rel (max diff {diff.max().item():.4g})")

@@ -58,7 +58,7 @@ def check_against_oracle(x, sd, k, E, dtype, max_flip_frac):
     assert torch.equal(ex["counts"].long(), aux["counts"])
     assert torch.equal(ex["gates"], aux["gates"])
     n = x.shape[0]
-    assert_close_rows(out, ref, torch.ones(n, dtype=torch.bool, device=DEV), dtype)
+    assert_close_rows(out, ref, torch.ones(n, dtype=torch.bool, device=DEV), dtype, aux["term_scale"])
     # Kernel logits: explained flips only.
     out2, ex2 = run_ours(x, sd, k, E)
     rows, unexplained = explained_index_mismatches(ex2["idx"], aux["idx"], ex2["logits"], aux["logits"], k)
@@ -66,7 +66,7 @@ def check_against_oracle(x, sd, k, E, dtype, max_flip_frac):
     assert rows.numel() <= max(2, int(max_flip_frac * n)), rows.numel()
     ok = torch.ones(n, dtype=torch.bool, device=DEV)
     ok[rows] = False
-    assert_close_rows(out2, ref, ok, dtype)
+    assert_close_rows(out2, ref, ok, dtype, aux["term_scale"])
     same_logits = (ex2["logits"] == aux["logits"]).all(1)
     assert torch.equal(ex2["gates"][same_logits], aux["gates"][same_logits])
     return rows.numel()
