@@ -41,6 +41,8 @@ SIGNATURES = {
     "agm_moe_forward": (_I, [_P, _I, _I64, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _P, _P,
                              _P, _SZ, _I, _P, _P, _P, _P, _P, _P, _P]),
     "agm_read_device_error": (_I, [_P, _P, _P]),
+    "agm_moe_forward_noalloc": (_I, [_P, _I, _I64, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _P, _P,
+                                     _I, _P]),
 }
 
 

@@ -118,6 +118,10 @@ FwdLayout carve(void* ws, int64_t n, int d, int E, int k, int H, int S, int Hs, 
 
 }  // namespace
 
+namespace agm {
+void set_last_error(const std::string& msg) { g_err = msg; }
+}  // namespace agm
+
 extern "C" {
 
 const char* agm_last_error(void) { return g_err.c_str(); }

@@ -5,6 +5,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <string>
+
 namespace agm {
 
 // Arguments of the grouped GEMM  c[r, :] = act(a[r, :] @ w[g]^T + bias[g]).
@@ -21,6 +23,9 @@ struct GemmArgs {
   int max_tiles;              // host bound (and the count when num_tiles is null)
   int* err;
 };
+
+// Set the message returned by agm_last_error() (thread-local).
+void set_last_error(const std::string& msg);
 
 cudaError_t router_topk(int dtype, const void* x, const void* w, int64_t n_tokens, int d, int E, int k,
                         int tie_low_first, const float* logits_in, float* logits_out, int32_t* idx, void* gates,

@@ -145,6 +145,27 @@ AGM_API int agm_moe_forward(const void* x, int dtype, int64_t n_tokens, int d, i
                     int32_t* counts_out, float* logits_out, const float* logits_in, void* const* stage_events,
                     void* stream);
 
+/* Size of the scratch area compiled into the library for
+ * agm_moe_forward_noalloc (32 MiB; e.g. up to about 950 tokens at d=1280,
+ * H=3200, 14 experts, top-2, bf16). */
+#define AGM_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+/* agm_moe_forward for callers that cannot allocate device memory (no
+ * counterpart in the reference): a host that owns all GPU memory through its
+ * own pool and passes only input/output buffers, or a process that must not
+ * grow its GPU footprint at run time. Same arguments and results as
+ * agm_moe_forward without the workspace; the scratch is a fixed array of
+ * AGM_NOALLOC_SCRATCH_BYTES inside the library, held by every GPU that loads
+ * it until the process exits. A problem needing more scratch is rejected with
+ * AGM_ERR_WORKSPACE. The first call on each device looks up the array's device
+ * address (with that device current); make that first call before any stream
+ * capture. All calls share the array: calls that overlap on the GPU race. The
+ * device error word is the array's first int, cleared by every call.       */
+AGM_API int agm_moe_forward_noalloc(const void* x, int dtype, int64_t n_tokens, int d, int n_experts, int top_k,
+                                    int hidden, const void* w_router, const void* w1, const void* b1, const void* w2,
+                                    const void* b2, int n_shared, int shared_hidden, const void* ws1, const void* sb1,
+                                    const void* ws2, const void* sb2, void* out, int flags, void* stream);
+
 /* Synchronise `stream`, read the device error word at `err` (e.g. the first
  * int of a forward workspace) into *code and reset it to 0. Returns AGM_OK if
  * the word was 0, AGM_ERR_DEVICE otherwise.                                */
