@@ -24,7 +24,7 @@ import torch.nn.functional as F
 
 import agillm41_b200
 from agillm41_b200 import ops
-from gpu_helpers import assert_close_rows, explained_index_mismatches, packed
+from gpu_helpers import assert_close_rows, explained_index_mismatches, gate_slack, packed
 from golden_io import Golden, names
 from oracle import reference_moe
 
@@ -66,7 +66,9 @@ def check_against_oracle(x, sd, k, E, dtype, max_flip_frac):
     assert rows.numel() <= max(2, int(max_flip_frac * n)), rows.numel()
     ok = torch.ones(n, dtype=torch.bool, device=DEV)
     ok[rows] = False
-    assert_close_rows(out2, ref, ok, dtype, aux["term_scale"])
+    # Where a logit differs without flipping the choice, the gates differ too.
+    assert_close_rows(out2, ref, ok, dtype, aux["term_scale"],
+                      slack=gate_slack(ex2["gates"], aux["gates"], aux["term_scale"]))
     same_logits = (ex2["logits"] == aux["logits"]).all(1)
     assert torch.equal(ex2["gates"][same_logits], aux["gates"][same_logits])
     return rows.numel()
