@@ -18,7 +18,7 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "liba
 AGM_F32, AGM_BF16, AGM_F16 = 0, 1, 2
 AGM_OK = 0
 AGM_TILE_M = 128
-AGM_DISPATCH_BLOCK = 256
+AGM_DISPATCH_BLOCK = 128
 AGM_MAX_EXPERTS = 16
 AGM_FLAG_TIE_LOW_FIRST = 0x1
 AGM_STAGE_EVENTS = 8

@@ -59,6 +59,15 @@ int check_common(int dtype, int d, int n_experts, int top_k) {
   return AGM_OK;
 }
 
+// The router keeps its weight in shared memory: the tensor-core router (bf16,
+// fp16) holds it as 16-bit tiles, the SIMT router (fp32, or routing from
+// caller-supplied logits) as fp32.
+bool router_fits(int dtype, int d, int n_experts, bool logits_in) {
+  if (logits_in) return agm::router_smem_bytes(0, n_experts) <= 227 * 1024;
+  if (dtype != AGM_F32 && agm::router_tc_supported(d)) return true;
+  return agm::router_smem_bytes(d, n_experts) <= 227 * 1024;
+}
+
 struct Carver {
   uint8_t* base;
   size_t off = 0;
@@ -149,10 +158,10 @@ int agm_router_topk(const void* x, const void* w_router, int dtype, int64_t n_to
     return fail(AGM_ERR_ARG, "null pointer argument");
   if (!logits_in && (!aligned16(x) || !aligned16(w_router)))
     return fail(AGM_ERR_ARG, "x and w_router must be 16-byte aligned");
-  if (!logits_in && agm::router_smem_bytes(d, n_experts) > 227 * 1024)
-    return fail(AGM_ERR_UNSUPPORTED, "router weight does not fit in shared memory (E * d * 4 bytes > 211 KB)");
+  if (!router_fits(dtype, d, n_experts, logits_in != nullptr))
+    return fail(AGM_ERR_UNSUPPORTED, "router weight does not fit in shared memory for this d and dtype");
   cudaError_t e = agm::router_topk(dtype, x, w_router, n_tokens, d, n_experts, top_k, flags & AGM_FLAG_TIE_LOW_FIRST,
-                                   logits_in, logits_out, idx, gates, block_hist, err,
+                                   logits_in, logits_out, idx, gates, block_hist, err, num_sms_current(),
                                    static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? AGM_OK : cuda_fail(e, "router_topk");
 }
@@ -265,8 +274,8 @@ int agm_moe_forward(const void* x, int dtype, int64_t n_tokens, int d, int n_exp
     if (!aligned16(p)) return fail(AGM_ERR_ARG, "all tensors must be 16-byte aligned");
   if (n_shared > 0 && (!aligned16(ws1) || !aligned16(sb1) || !aligned16(ws2) || !aligned16(sb2)))
     return fail(AGM_ERR_ARG, "all tensors must be 16-byte aligned");
-  if (agm::router_smem_bytes(d, n_experts) > 227 * 1024)
-    return fail(AGM_ERR_UNSUPPORTED, "router weight does not fit in shared memory (E * d * 4 bytes > 211 KB)");
+  if (!router_fits(dtype, d, n_experts, logits_in != nullptr))
+    return fail(AGM_ERR_UNSUPPORTED, "router weight does not fit in shared memory for this d and dtype");
   const int64_t rows = agm_max_rows(n_tokens, top_k, n_experts);
   if (rows > INT32_MAX) return fail(AGM_ERR_UNSUPPORTED, "too many permuted rows for int32 indices");
   FwdLayout L = carve(workspace, n_tokens, d, n_experts, top_k, hidden, n_shared, std::max(1, shared_hidden), eb);
@@ -288,7 +297,7 @@ int agm_moe_forward(const void* x, int dtype, int64_t n_tokens, int d, int n_exp
 
   if ((e = mark(0)) != cudaSuccess) return cuda_fail(e, "event record");
   e = agm::router_topk(dtype, x, w_router, n_tokens, d, n_experts, top_k, flags & AGM_FLAG_TIE_LOW_FIRST,
-                       logits_in, logits_out, idx, gates, L.block_hist, L.err, stream);
+                       logits_in, logits_out, idx, gates, L.block_hist, L.err, sms, stream);
   if (e != cudaSuccess) return cuda_fail(e, "router_topk");
   if ((e = mark(1)) != cudaSuccess) return cuda_fail(e, "event record");
   e = agm::dispatch_plan(L.block_hist, static_cast<int>(agm_dispatch_blocks(n_tokens)), n_experts, rows,

@@ -17,6 +17,66 @@
 
 namespace agm {
 
+// Rows up to kMaxChunks x 32 x 16 bytes keep every chunk of the k gathered
+// rows in registers (all loads issued before any use); longer rows loop.
+constexpr int kMaxChunks = 5;
+
+template <typename T>
+__device__ __forceinline__ void load8(const uint4& u, float (&f)[8]) {
+  if constexpr (sizeof(T) == 4) {
+    f[0] = __uint_as_float(u.x); f[1] = __uint_as_float(u.y);
+    f[2] = __uint_as_float(u.z); f[3] = __uint_as_float(u.w);
+  } else {
+    unpack8<T>(u, f);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 store8(const float (&acc)[8]) {
+  if constexpr (sizeof(T) == 4) {
+    return make_uint4(__float_as_uint(acc[0]), __float_as_uint(acc[1]), __float_as_uint(acc[2]),
+                      __float_as_uint(acc[3]));
+  } else {
+    return make_uint4(pack2<T>(acc[0], acc[1]), pack2<T>(acc[2], acc[3]), pack2<T>(acc[4], acc[5]),
+                      pack2<T>(acc[6], acc[7]));
+  }
+}
+
+// out chunk = ((0 + round(y_0 g_0)) + round(y_1 g_1) + ...) [+ shared sum], each
+// op rounded to T. __fmul_rn/__fadd_rn are never contracted into an FMA, so
+// the product is rounded on its own as in the reference's `y * w` tensor.
+template <typename T, int K_MAX>
+__device__ __forceinline__ uint4 combine_chunk(const uint4 (&v)[K_MAX], const float (&g)[K_MAX], int k,
+                                               const T* __restrict__ shared_y, int n_shared,
+                                               int64_t shared_stride, int64_t tok, int d, int c) {
+  constexpr int CH = 16 / sizeof(T);
+  float acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+#pragma unroll
+  for (int r = 0; r < K_MAX; ++r) {
+    if (r < k) {
+      float f[8];
+      load8<T>(v[r], f);
+#pragma unroll
+      for (int j = 0; j < CH; ++j) acc[j] = round_to<T>(__fadd_rn(acc[j], round_to<T>(__fmul_rn(f[j], g[r]))));
+    }
+  }
+  if (n_shared > 0) {
+    float s[8];
+    for (int si = 0; si < n_shared; ++si) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(shared_y + si * shared_stride + tok * d) + c);
+      float f[8];
+      load8<T>(u, f);
+#pragma unroll
+      for (int j = 0; j < CH; ++j) s[j] = (si == 0) ? f[j] : round_to<T>(__fadd_rn(s[j], f[j]));
+    }
+#pragma unroll
+    for (int j = 0; j < CH; ++j) acc[j] = round_to<T>(__fadd_rn(acc[j], s[j]));
+  }
+  return store8<T>(acc);
+}
+
 template <typename T, int K_MAX>
 __global__ void __launch_bounds__(256) combine_kernel(const T* __restrict__ y_perm, const int32_t* __restrict__ row_of,
                                                       const T* __restrict__ gates, int64_t n_tokens, int d, int k,
@@ -28,68 +88,49 @@ __global__ void __launch_bounds__(256) combine_kernel(const T* __restrict__ y_pe
   const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
   for (int64_t tok = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + warp_id(); tok < n_tokens;
        tok += warps_total) {
-    int rows[K_MAX];
+    const uint4* src[K_MAX];
     float g[K_MAX];
 #pragma unroll
     for (int r = 0; r < K_MAX; ++r) {
       if (r < k) {
-        rows[r] = row_of[tok * k + r];
+        src[r] = reinterpret_cast<const uint4*>(y_perm + static_cast<int64_t>(row_of[tok * k + r]) * d);
         g[r] = Traits<T>::to_f(gates[tok * k + r]);
       } else {
-        rows[r] = -1;
+        src[r] = nullptr;
         g[r] = 0.f;
       }
     }
-    for (int c = lane; c < nchunk; c += 32) {
-      float acc[8];
+    uint4* dst = reinterpret_cast<uint4*>(out + tok * d);
+    bool done = false;
+    if constexpr (K_MAX <= 4) {
+      if (nchunk <= 32 * kMaxChunks) {
+      done = true;
+      uint4 v[kMaxChunks][K_MAX];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-      uint4 v[K_MAX];
+      for (int j = 0; j < kMaxChunks; ++j) {
+        const int c = lane + 32 * j;
+        if (c < nchunk) {
 #pragma unroll
-      for (int r = 0; r < K_MAX; ++r)
-        if (r < k && rows[r] >= 0) v[r] = __ldg(reinterpret_cast<const uint4*>(y_perm + static_cast<int64_t>(rows[r]) * d) + c);
-#pragma unroll
-      for (int r = 0; r < K_MAX; ++r) {
-        if (r < k && rows[r] >= 0) {
-          float f[8];
-          if constexpr (sizeof(T) == 4) {
-            f[0] = __uint_as_float(v[r].x); f[1] = __uint_as_float(v[r].y);
-            f[2] = __uint_as_float(v[r].z); f[3] = __uint_as_float(v[r].w);
-          } else {
-            unpack8<T>(v[r], f);
-          }
-#pragma unroll
-          // __fmul_rn/__fadd_rn: never contracted into an FMA, so the product
-          // is rounded on its own as in the reference's `y * w` tensor.
-          for (int j = 0; j < CH; ++j) acc[j] = round_to<T>(__fadd_rn(acc[j], round_to<T>(__fmul_rn(f[j], g[r]))));
+          for (int r = 0; r < K_MAX; ++r)
+            if (r < k) v[j][r] = __ldg(src[r] + c);
         }
       }
-      if (n_shared > 0) {
-        float s[8];
-        for (int si = 0; si < n_shared; ++si) {
-          const uint4 u = __ldg(reinterpret_cast<const uint4*>(shared_y + si * shared_stride + tok * d) + c);
-          float f[8];
-          if constexpr (sizeof(T) == 4) {
-            f[0] = __uint_as_float(u.x); f[1] = __uint_as_float(u.y);
-            f[2] = __uint_as_float(u.z); f[3] = __uint_as_float(u.w);
-          } else {
-            unpack8<T>(u, f);
-          }
 #pragma unroll
-          for (int j = 0; j < CH; ++j) s[j] = (si == 0) ? f[j] : round_to<T>(__fadd_rn(s[j], f[j]));
-        }
+      for (int j = 0; j < kMaxChunks; ++j) {
+        const int c = lane + 32 * j;
+        if (c < nchunk)
+          dst[c] = combine_chunk<T, K_MAX>(v[j], g, k, shared_y, n_shared, shared_stride, tok, d, c);
+      }
+      }
+    }
+    if (!done) {
+      for (int c = lane; c < nchunk; c += 32) {
+        uint4 v[K_MAX];
 #pragma unroll
-        for (int j = 0; j < CH; ++j) acc[j] = round_to<T>(__fadd_rn(acc[j], s[j]));
+        for (int r = 0; r < K_MAX; ++r)
+          if (r < k) v[r] = __ldg(src[r] + c);
+        dst[c] = combine_chunk<T, K_MAX>(v, g, k, shared_y, n_shared, shared_stride, tok, d, c);
       }
-      uint4 o;
-      if constexpr (sizeof(T) == 4) {
-        o = make_uint4(__float_as_uint(acc[0]), __float_as_uint(acc[1]), __float_as_uint(acc[2]),
-                       __float_as_uint(acc[3]));
-      } else {
-        o = make_uint4(pack2<T>(acc[0], acc[1]), pack2<T>(acc[2], acc[3]), pack2<T>(acc[4], acc[5]),
-                       pack2<T>(acc[6], acc[7]));
-      }
-      reinterpret_cast<uint4*>(out + tok * d)[c] = o;
     }
   }
 }

@@ -28,6 +28,7 @@ namespace agm {
 constexpr int kTile = AGM_TILE_M;
 constexpr int kBlk = AGM_DISPATCH_BLOCK;
 constexpr int kPlanThreads = 512;
+constexpr int kMaxChunks = 8;  // 16-byte chunks per lane held in registers (rows up to 4 KB)
 
 __global__ void __launch_bounds__(kPlanThreads) dispatch_plan_kernel(
     const int32_t* __restrict__ block_hist, int n_blocks, int E, int64_t max_rows, int max_tiles,
@@ -150,27 +151,59 @@ __global__ void __launch_bounds__(kBlk) permute_kernel(
       raise_error(err, kErrBadExpert);
     }
   }
-  // Copy rows: the warp walks its 32 tokens; all lanes stream the row.
+  // Copy rows: the warp walks its 32 tokens two at a time; every lane loads
+  // all of its 16-byte chunks of both rows before storing them to the k
+  // destination rows, so up to 2 x kMaxChunks loads per lane are in flight.
   const int64_t warp_tok0 = static_cast<int64_t>(blockIdx.x) * kBlk + warp * 32;
-  for (int i = 0; i < 32; ++i) {
-    const int64_t t = warp_tok0 + i;
-    if (t >= n_tokens) break;
-    int drow[K_MAX];
-#pragma unroll
-    for (int r = 0; r < K_MAX; ++r) drow[r] = __shfl_sync(0xffffffffu, dest[r], i);
-    const uint4* src = x + t * nchunk;
-    for (int c = lane; c < nchunk; c += 64) {
-      const uint4 v0 = __ldg(src + c);
-      const bool two = (c + 32) < nchunk;
-      uint4 v1 = make_uint4(0, 0, 0, 0);
-      if (two) v1 = __ldg(src + c + 32);
+  if (nchunk <= 32 * kMaxChunks) {
+    for (int i = 0; i < 32; i += 2) {
+      const int64_t t0 = warp_tok0 + i, t1 = t0 + 1;
+      if (t0 >= n_tokens) break;
+      const bool has1 = t1 < n_tokens;
+      int d0[K_MAX], d1[K_MAX];
 #pragma unroll
       for (int r = 0; r < K_MAX; ++r) {
-        if (r < k && drow[r] >= 0) {
-          uint4* dst = x_perm + static_cast<int64_t>(drow[r]) * nchunk;
-          dst[c] = v0;
-          if (two) dst[c + 32] = v1;
+        d0[r] = __shfl_sync(0xffffffffu, dest[r], i);
+        d1[r] = __shfl_sync(0xffffffffu, dest[r], i + 1);
+      }
+      const uint4* s0 = x + t0 * nchunk;
+      const uint4* s1 = x + t1 * nchunk;
+      uint4 v0[kMaxChunks], v1[kMaxChunks];
+#pragma unroll
+      for (int j = 0; j < kMaxChunks; ++j) {
+        const int c = lane + 32 * j;
+        if (c < nchunk) {
+          v0[j] = __ldg(s0 + c);
+          if (has1) v1[j] = __ldg(s1 + c);
         }
+      }
+#pragma unroll
+      for (int r = 0; r < K_MAX; ++r) {
+        if (r >= k) break;
+        uint4* o0 = d0[r] >= 0 ? x_perm + static_cast<int64_t>(d0[r]) * nchunk : nullptr;
+        uint4* o1 = (has1 && d1[r] >= 0) ? x_perm + static_cast<int64_t>(d1[r]) * nchunk : nullptr;
+#pragma unroll
+        for (int j = 0; j < kMaxChunks; ++j) {
+          const int c = lane + 32 * j;
+          if (c < nchunk) {
+            if (o0) o0[c] = v0[j];
+            if (o1) o1[c] = v1[j];
+          }
+        }
+      }
+    }
+  } else {
+    for (int i = 0; i < 32; ++i) {
+      const int64_t t = warp_tok0 + i;
+      if (t >= n_tokens) break;
+      int drow[K_MAX];
+#pragma unroll
+      for (int r = 0; r < K_MAX; ++r) drow[r] = __shfl_sync(0xffffffffu, dest[r], i);
+      const uint4* src = x + t * nchunk;
+      for (int c = lane; c < nchunk; c += 32) {
+        const uint4 v = __ldg(src + c);
+        for (int r = 0; r < k && r < K_MAX; ++r)
+          if (drow[r] >= 0) x_perm[static_cast<int64_t>(drow[r]) * nchunk + c] = v;
       }
     }
   }

@@ -14,13 +14,15 @@
 // kernel writes on the device, together with the number of valid tiles, so
 // the forward needs no host sync.
 //
-// bf16/fp16 path (tcgen05, sm_100a): persistent CTAs (one per SM), 192
+// bf16/fp16 path (tcgen05, sm_100a): persistent CTAs (one per SM), 320
 // threads: warp 0 issues TMA loads (128x64 A tile + BNx64 W tile per stage,
 // 128-byte swizzle, no multicast), warp 1 owns the TMEM allocation and issues
-// tcgen05.mma (M=128, N=BN, K=16, fp32 accumulation in TMEM), warps 2-5 drain
-// the accumulator (tcgen05.ld), add the bias, apply ReLU, round to the
-// activation dtype and store. The accumulator is double-buffered in TMEM
-// (2 x BN columns) so the epilogue of one tile overlaps the MMAs of the next.
+// tcgen05.mma (M=128, N=BN, K=16, fp32 accumulation in TMEM), warps 2-9 drain
+// the accumulator (tcgen05.ld; two warps per TMEM lane quarter, alternate
+// 64-column chunks), add the bias, apply ReLU, round to the activation dtype,
+// stage each 32x64 chunk in shared memory (128-byte swizzle) and write it with
+// a TMA store. The accumulator is double-buffered in TMEM (2 x BN columns) so
+// the epilogue of one tile overlaps the MMAs of the next.
 // Every mbarrier wait is bounded; on time-out the kernel records an error
 // code, drains its in-flight copies and MMAs, frees TMEM and returns.
 //
@@ -37,7 +39,9 @@ namespace agm {
 constexpr int BM = AGM_TILE_M;  // 128 rows per tile
 constexpr int BK = 64;          // 64 x 16-bit = 128 B: one swizzle atom row
 constexpr int kGroupM = 16;     // tile rasterisation: 16 row tiles per group
-constexpr int kGemmThreads = 192;
+constexpr int kEpiWarps = 8;     // two epilogue warps per TMEM lane quarter
+constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
+constexpr int kStgBytes = 32 * 64 * 2;  // one 32-row x 64-column output chunk (TMA store source)
 
 
 template <int BN>
@@ -47,8 +51,9 @@ struct TcCfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (BN >= 256) ? 4 : 6;
   static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int STG_BYTES = kEpiWarps * kStgBytes;
   static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STG_BYTES + BAR_BYTES + 1024;
 };
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& m_blk, int& n_blk) {
@@ -64,14 +69,15 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& m_
 template <typename T, int BN, bool RELU>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     grouped_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                           GemmArgs args) {
+                           const __grid_constant__ CUtensorMap tmC, GemmArgs args) {
   using Cfg = TcCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint8_t* sStg = smem + STAGES * Cfg::STAGE_BYTES;  // [8 warps][32 rows][128 B], 128-byte swizzled
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sStg + Cfg::STG_BYTES);
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
   uint64_t* acc_full = bars + 2 * STAGES;
@@ -101,13 +107,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 128);
+      mbar_init(&acc_empty[i], 32 * kEpiWarps);
     }
     mbar_init(drain, 1);
     *abort_s = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
@@ -204,10 +211,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncwarp();
     mbar_wait(drain, 0, args.err, kErrTimeoutDrain);
   } else {
-    // ---------------- Epilogue (warps 2..5) ----------------
-    const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32)
+    // ---------------- Epilogue (warps 2..9) ----------------
+    // Warp w reads TMEM lanes [32*(w%4), +32) (its quarter of the 128 rows);
+    // warps 2-5 take the even 64-column chunks of the tile, warps 6-9 the odd
+    // ones. A chunk (32 rows x 64 columns) is biased, activated, rounded,
+    // written to this warp's staging buffer in the 128-byte swizzled layout
+    // (conflict-free 16-byte stores) and sent to global memory with one TMA
+    // store, which also clips rows/columns outside C.
+    const int ew = warp - 2;
+    const int quarter = warp & 3;
+    const int half = ew >> 2;
+    uint8_t* stg = sStg + ew * kStgBytes;
+    const uint32_t stg_row = lane * 128;
     int it = 0;
-    T* C = static_cast<T*>(args.c);
     const T* bias = static_cast<const T*>(args.bias);
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
       int m_blk, n_blk;
@@ -221,23 +237,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         break;
       }
       tc_fence_after();
-      const int64_t row = static_cast<int64_t>(m_blk) * BM + quarter * 32 + lane;
       const int n0 = n_blk * BN;
       const int n_valid = min(BN, args.n - n0);
-      const bool row_ok = row < args.c_rows;
-      T* crow = C + row * args.ldc + n0;
       const T* brow = bias ? bias + static_cast<int64_t>(g) * args.n + n0 : nullptr;
-      for (int c = 0; c < n_valid; c += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN + c, r);
+      for (int c64 = half; c64 * 64 < n_valid; c64 += 2) {
+        const int col = c64 * 64;
+        uint32_t r[64];
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN + col;
+        tmem_ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+        tmem_ld_32x32b_x32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
         tmem_ld_wait();
+        // The staging buffer is free once the previous chunk's TMA store has read it.
+        if (lane == 0) bulk_wait_group_read0();
+        __syncwarp();
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int col = c + q * 8;
-          if (col >= n_valid) break;
+        for (int q = 0; q < 8; ++q) {
           float bv[8];
-          if (brow) {
-            const uint4 bu = __ldg(reinterpret_cast<const uint4*>(brow + col));
+          if (brow && col + q * 8 < n_valid) {
+            const uint4 bu = __ldg(reinterpret_cast<const uint4*>(brow + col + q * 8));
             unpack8<T>(bu, bv);
           } else {
 #pragma unroll
@@ -249,16 +266,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             v[j] = __uint_as_float(r[q * 8 + j]) + bv[j];
             if (RELU) v[j] = fmaxf(v[j], 0.f);
           }
-          if (row_ok) {
-            uint4 o = make_uint4(pack2<T>(v[0], v[1]), pack2<T>(v[2], v[3]), pack2<T>(v[4], v[5]),
-                                 pack2<T>(v[6], v[7]));
-            *reinterpret_cast<uint4*>(crow + col) = o;
-          }
+          const uint4 o = make_uint4(pack2<T>(v[0], v[1]), pack2<T>(v[2], v[3]), pack2<T>(v[4], v[5]),
+                                     pack2<T>(v[6], v[7]));
+          // 128-byte swizzle: 16-byte chunk q of row `lane` lives at chunk q ^ (lane % 8).
+          *reinterpret_cast<uint4*>(stg + stg_row + ((q ^ (lane & 7)) << 4)) = o;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, stg, n0 + col, m_blk * BM + quarter * 32);
+          bulk_commit_group();
         }
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[acc]);
     }
+    if (lane == 0) bulk_wait_group0();
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -351,7 +375,7 @@ static EncodeTiledFn get_encode_fn() {
 }
 
 // 2-D/3-D row-major tensor of 16-bit elements: dims innermost first.
-static bool encode_tmap(CUtensorMap* m, const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
+bool encode_tmap(CUtensorMap* m, const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
                         const uint32_t* box, CUtensorMapDataType dt) {
   EncodeTiledFn fn = get_encode_fn();
   if (!fn) return false;
@@ -388,13 +412,20 @@ static cudaError_t launch_tc(const void* a, int64_t a_rows, const void* w, const
     const uint32_t box[3] = {BK, static_cast<uint32_t>(BN), 1};
     if (!encode_tmap(&tmB, w, 3, dims, str, box, dt)) return cudaErrorInvalidValue;
   }
+  CUtensorMap tmC;
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(args.n), static_cast<uint64_t>(args.c_rows)};
+    const uint64_t str[1] = {static_cast<uint64_t>(args.ldc) * 2};
+    const uint32_t box[2] = {64, 32};
+    if (!encode_tmap(&tmC, args.c, 2, dims, str, box, dt)) return cudaErrorInvalidValue;
+  }
   cudaError_t e = cudaFuncSetAttribute(grouped_gemm_tc_kernel<T, BN, RELU>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
   if (e != cudaSuccess) return e;
   const int num_n = (args.n + BN - 1) / BN;
   const int64_t max_total = static_cast<int64_t>(args.max_tiles) * num_n;
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(num_sms, max_total)));
-  grouped_gemm_tc_kernel<T, BN, RELU><<<grid, kGemmThreads, Cfg::SMEM_BYTES, stream>>>(tmA, tmB, args);
+  grouped_gemm_tc_kernel<T, BN, RELU><<<grid, kGemmThreads, Cfg::SMEM_BYTES, stream>>>(tmA, tmB, tmC, args);
   return cudaGetLastError();
 }
 

@@ -1,6 +1,7 @@
 // Internal launch interface shared by the kernel files and the C ABI layer.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -24,13 +25,21 @@ struct GemmArgs {
   int* err;
 };
 
+// Tiled TMA descriptor (128-byte swizzle, zero OOB fill) for a row-major
+// tensor of rank 2 or 3; dims and box innermost first, strides in bytes.
+bool encode_tmap(CUtensorMap* m, const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
+                 const uint32_t* box, CUtensorMapDataType dt);
+
 // Set the message returned by agm_last_error() (thread-local).
 void set_last_error(const std::string& msg);
 
 cudaError_t router_topk(int dtype, const void* x, const void* w, int64_t n_tokens, int d, int E, int k,
                         int tie_low_first, const float* logits_in, float* logits_out, int32_t* idx, void* gates,
-                        int32_t* block_hist, int* err, cudaStream_t stream);
+                        int32_t* block_hist, int* err, int num_sms, cudaStream_t stream);
+// Shared memory of the SIMT router (fp32, or caller-supplied logits).
 size_t router_smem_bytes(int d, int E);
+// Whether the tensor-core router (bf16/fp16) handles this d.
+bool router_tc_supported(int d);
 cudaError_t dispatch_plan(const int32_t* block_hist, int n_blocks, int E, int64_t max_rows, int max_tiles,
                           int32_t* block_off, int32_t* counts, int32_t* seg_start, int32_t* tile_expert,
                           int32_t* num_tiles, int32_t* token_of, int* err, cudaStream_t stream);

@@ -4,24 +4,33 @@
 // fp32 logits and `softmax` over the k chosen values cast to the activation
 // dtype; top-1: `softmax` over all experts and `argmax`, agillm41.py:4401-4416).
 //
-// Layout: one CTA per dispatch block of 256 tokens (8 warps x 32 tokens).
-// The router weight [E, d] is staged once per CTA in shared memory as fp32.
-// A warp computes 4 tokens at a time: lane l owns the 16-byte chunks
-// l, l+32, ... of each row (vectorised loads, fully coalesced), accumulates
-// 4 x 16 partial dot products, and a transpose-reduce over the 32 lanes (16
-// shuffles per token) leaves each expert's sum in two lanes. The logits are
-// rounded like the reference's router output (bf16/fp16 GEMM result, then
-// `.float()`), staged in shared memory, and then one thread per token does
-// the selection and the softmax with the same reduction order as torch's
-// warp softmax, so gates match bit for bit when the logits do.
+// bf16 / fp16 (router_tc_kernel): the logits are a [N, d] x [d, E] product, so
+// they run on the 5th-generation tensor cores while x streams from HBM once:
+// persistent CTAs (one per SM) walk 128-token tiles; warp 0 streams 128x64
+// tiles of x through an 8-stage TMA ring, the router weight [E <= 16, d]
+// stays resident in shared memory (TMA zero-fills rows E..15), warp 1 issues
+// tcgen05.mma M=128 N=16 K=16 with fp32 accumulation into TMEM (two 16-column
+// buffers), and each of the 128 epilogue threads reads the 16 logits of its
+// token (its TMEM lane) with one tcgen05.ld, rounds them like the reference's
+// bf16/fp16 GEMM output and selects top-k in registers.
+//
+// fp32, or logits supplied by the caller (router_topk_kernel): a SIMT kernel,
+// one CTA per 128 tokens, 4 tokens per warp iteration, 16-byte vector loads
+// and a transpose-reduce over the lanes.
+//
+// Both kernels share the per-token selection (route_token): it follows
+// torch.topk and torch's warp softmax so gates match bit for bit when the
+// logits do, and writes one histogram row per 128-token dispatch block.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
 namespace agm {
 
-constexpr int kDispatchBlock = AGM_DISPATCH_BLOCK;  // tokens per CTA
+constexpr int kDispatchBlock = AGM_DISPATCH_BLOCK;  // 128 tokens
 constexpr int kRouterWarps = kDispatchBlock / 32;
-constexpr int kMaxExperts = 16;
+constexpr int kMaxExperts = AGM_MAX_EXPERTS;       // 16
 constexpr int kTokGroup = 4;
 
 // Sum of e[0..W) in the order of a butterfly (xor) reduction over W lanes,
@@ -94,6 +103,61 @@ __device__ __forceinline__ void select_topk(const float* logit, int E, int k, bo
   }
 }
 
+// Selection, gates and histogram for one token whose fp32 logits (already
+// rounded like the reference's router output) are lg[0..E).
+template <typename T>
+__device__ __forceinline__ void route_token(const float* lg, int E, int k, bool low_first, int64_t tok,
+                                            float* __restrict__ logits_out, int32_t* __restrict__ idx_out,
+                                            T* __restrict__ gates_out, int* hist_s, int* err) {
+  if (logits_out) {
+    for (int e = 0; e < E; ++e) logits_out[tok * E + e] = lg[e];
+  }
+  int sel[kMaxExperts];
+  float gate[kMaxExperts];
+  if (k == 1) {
+    // probs = softmax(scores) (warp softmax over next_pow2(E) lanes, padding
+    // contributes exp(-inf) = 0), chosen = argmax(probs), first index on ties.
+    float m = lg[0];
+    for (int e = 1; e < E; ++e) m = fmaxf(m, lg[e]);
+    float ex[kMaxExperts];
+#pragma unroll
+    for (int e = 0; e < kMaxExperts; ++e) ex[e] = (e < E) ? expf(lg[e] - m) : 0.f;
+    const float s = butterfly_sum_rt(ex, next_pow2_le32(E));
+    int best = 0;
+    float bp = ex[0] / s;
+    for (int e = 1; e < E; ++e) {
+      const float p = ex[e] / s;
+      if (p > bp || (isnan(p) && !isnan(bp))) { bp = p; best = e; }
+    }
+    sel[0] = best;
+    gate[0] = 1.f;  // straight-through gate: gate / gate.detach() == 1
+  } else {
+    float val[kMaxExperts];
+    select_topk(lg, E, k, low_first, sel, val);
+    // softmax over the k values (sorted descending, so val[0] is the max).
+    float m = val[0];
+    for (int r = 1; r < k; ++r) m = fmaxf(m, val[r]);
+    float ex[kMaxExperts];
+#pragma unroll
+    for (int r = 0; r < kMaxExperts; ++r) ex[r] = (r < k) ? expf(val[r] - m) : 0.f;
+    const float s = butterfly_sum_rt(ex, next_pow2_le32(k));
+    for (int r = 0; r < k; ++r) gate[r] = ex[r] / s;
+  }
+  for (int r = 0; r < k; ++r) {
+    const int e = sel[r];
+    if (e < 0 || e >= E) {
+      raise_error(err, kErrBadExpert);
+      continue;
+    }
+    idx_out[tok * k + r] = e;
+    gates_out[tok * k + r] = Traits<T>::from_f(gate[r]);
+    atomicAdd(&hist_s[e], 1);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// SIMT router (fp32, or caller-supplied logits)
+// ---------------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(kDispatchBlock) router_topk_kernel(
     const T* __restrict__ x, const T* __restrict__ w, int64_t n_tokens, int d, int E, int k, int tie_low_first,
@@ -104,7 +168,7 @@ __global__ void __launch_bounds__(kDispatchBlock) router_topk_kernel(
   const int nchunk = d / CH;
   const bool compute = (logits_in == nullptr);
   // Dynamic smem: [E][d] fp32 router weight (only when computing logits),
-  // then [8 warps][32 tokens][16] fp32 logits.
+  // then [warps][32 tokens][16] fp32 logits.
   float* w_s = smem_f;
   float* logit_s = smem_f + (compute ? E * d : 0);
   __shared__ int hist_s[kMaxExperts];
@@ -224,59 +288,223 @@ __global__ void __launch_bounds__(kDispatchBlock) router_topk_kernel(
     float lg[kMaxExperts];
 #pragma unroll
     for (int e = 0; e < kMaxExperts; ++e) lg[e] = (e < E) ? my_logits[lane * kMaxExperts + e] : 0.f;
-    if (logits_out) {
-      for (int e = 0; e < E; ++e) logits_out[tok * E + e] = lg[e];
-    }
-    int sel[kMaxExperts];
-    float gate[kMaxExperts];
-    if (k == 1) {
-      // probs = softmax(scores) (warp softmax over next_pow2(E) lanes, padding
-      // contributes exp(-inf) = 0), chosen = argmax(probs), first index on ties.
-      float m = lg[0];
-      for (int e = 1; e < E; ++e) m = fmaxf(m, lg[e]);
-      float ex[kMaxExperts];
-#pragma unroll
-      for (int e = 0; e < kMaxExperts; ++e) ex[e] = (e < E) ? expf(lg[e] - m) : 0.f;
-      const float s = butterfly_sum_rt(ex, next_pow2_le32(E));
-      int best = 0;
-      float bp = ex[0] / s;
-      for (int e = 1; e < E; ++e) {
-        const float p = ex[e] / s;
-        if (p > bp || (isnan(p) && !isnan(bp))) { bp = p; best = e; }
-      }
-      sel[0] = best;
-      gate[0] = 1.f;  // straight-through gate: gate / gate.detach() == 1
-    } else {
-      float val[kMaxExperts];
-      select_topk(lg, E, k, tie_low_first != 0, sel, val);
-      // softmax over the k values (sorted descending, so val[0] is the max).
-      float m = val[0];
-      for (int r = 1; r < k; ++r) m = fmaxf(m, val[r]);
-      float ex[kMaxExperts];
-#pragma unroll
-      for (int r = 0; r < kMaxExperts; ++r) ex[r] = (r < k) ? expf(val[r] - m) : 0.f;
-      const float s = butterfly_sum_rt(ex, next_pow2_le32(k));
-      for (int r = 0; r < k; ++r) gate[r] = ex[r] / s;
-    }
-    for (int r = 0; r < k; ++r) {
-      const int e = sel[r];
-      if (e < 0 || e >= E) {
-        raise_error(err, kErrBadExpert);
-        continue;
-      }
-      idx_out[tok * k + r] = e;
-      gates_out[tok * k + r] = Traits<T>::from_f(gate[r]);
-      atomicAdd(&hist_s[e], 1);
-    }
+    route_token<T>(lg, E, k, tie_low_first != 0, tok, logits_out, idx_out, gates_out, hist_s, err);
   }
   __syncthreads();
   if (threadIdx.x < E) block_hist[static_cast<int64_t>(blockIdx.x) * E + threadIdx.x] = hist_s[threadIdx.x];
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core router (bf16 / fp16): TMA-fed tcgen05, thread-per-token epilogue
+// ---------------------------------------------------------------------------
+constexpr int kRtStages = 8;
+constexpr int kRtThreads = 192;
+constexpr int kRtABytes = 128 * 64 * 2;   // one 128-token x 64-feature tile
+constexpr int kRtWBytes = 16 * 64 * 2;    // one 16-expert x 64-feature tile of the router weight
+
+__host__ __device__ constexpr int rt_smem_bytes(int nkb) {
+  return kRtStages * kRtABytes + nkb * kRtWBytes + 256 + 1024;
+}
+
 template <typename T>
-static cudaError_t launch_router(const void* x, const void* w, int64_t n_tokens, int d, int E, int k, int tie_low_first,
-                                 const float* logits_in, float* logits_out, int32_t* idx, void* gates,
-                                 int32_t* block_hist, int* err, cudaStream_t stream) {
+__global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(
+    const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, int64_t n_tokens, int d,
+    int E, int k, int tie_low_first, float* __restrict__ logits_out, int32_t* __restrict__ idx_out,
+    T* __restrict__ gates_out, int32_t* __restrict__ block_hist, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int nkb = (d + 63) / 64;
+  uint8_t* sA = smem;
+  uint8_t* sW = smem + kRtStages * kRtABytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sW + nkb * kRtWBytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kRtStages;
+  uint64_t* acc_full = empty + kRtStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* w_full = acc_empty + 2;
+  uint64_t* drain = w_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_s = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* hist_s = const_cast<int*>(abort_s) + 1;  // [16]
+
+  const int warp = warp_id(), lane = lane_id();
+  const int num_tiles = static_cast<int>((n_tokens + 127) / 128);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kRtStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 128);
+    }
+    mbar_init(w_full, 1);
+    mbar_init(drain, 1);
+    *abort_s = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmX);
+    tma_prefetch_desc(&tmW);
+  }
+  if (threadIdx.x < kMaxExperts) hist_s[threadIdx.x] = 0;
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 32);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      mbar_arrive_expect_tx(w_full, nkb * kRtWBytes);
+      for (int kb = 0; kb < nkb; ++kb) tma_load_2d(sW + kb * kRtWBytes, &tmW, kb * 64, 0, w_full);
+    }
+    int stage = 0;
+    uint32_t phase = 0, armed = 0, armed_parity = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      for (int kb = 0; kb < nkb; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1, err, kErrTimeoutEmpty) || *abort_s) {
+          *abort_s = 1;
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&full[stage], kRtABytes);
+          tma_load_2d(sA + stage * kRtABytes, &tmX, kb * 64, t * 128, &full[stage]);
+        }
+        armed |= 1u << stage;
+        armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
+        __syncwarp();
+        if (++stage == kRtStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+    for (int s = 0; s < kRtStages; ++s)
+      if (armed & (1u << s)) mbar_wait(&full[s], (armed_parity >> s) & 1, err, kErrTimeoutDrain);
+    mbar_wait(w_full, 0, err, kErrTimeoutDrain);
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    const uint32_t idesc = idesc_f16(Traits<T>::code == AGM_BF16, 128, 16);
+    const uint32_t sA_addr = smem_u32(sA), sW_addr = smem_u32(sW);
+    int stage = 0, it = 0;
+    uint32_t phase = 0;
+    bool ok = mbar_wait(w_full, 0, err, kErrTimeoutFull);
+    if (!ok) *abort_s = 1;
+    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
+      const int acc = it & 1;
+      if (!mbar_wait(&acc_empty[acc], ((it >> 1) & 1) ^ 1, err, kErrTimeoutAcc) || *abort_s) {
+        *abort_s = 1;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * 16;
+      for (int kb = 0; kb < nkb; ++kb) {
+        if (!mbar_wait(&full[stage], phase, err, kErrTimeoutFull) || *abort_s) {
+          *abort_s = 1;
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint64_t a_desc = smem_desc_k_sw128(sA_addr + stage * kRtABytes);
+          const uint64_t w_desc = smem_desc_k_sw128(sW_addr + kb * kRtWBytes);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_f16(d_tmem, a_desc + 2 * kk, w_desc + 2 * kk, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&empty[stage]);
+          if (kb == nkb - 1) umma_commit(&acc_full[acc]);
+        }
+        __syncwarp();
+        if (++stage == kRtStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+    if (lane == 0) umma_commit(drain);
+    __syncwarp();
+    mbar_wait(drain, 0, err, kErrTimeoutDrain);
+  } else {
+    // ---------------- Epilogue: one thread per token ----------------
+    const int quarter = warp & 3;
+    int it = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
+      const int acc = it & 1;
+      if (!mbar_wait(&acc_full[acc], (it >> 1) & 1, err, kErrTimeoutAcc) || *abort_s) {
+        *abort_s = 1;
+        break;
+      }
+      tc_fence_after();
+      uint32_t r[16];
+      tmem_ld_32x32b_x16(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * 16, r);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(&acc_empty[acc]);  // the accumulator is in registers: release it
+      const int64_t tok = static_cast<int64_t>(t) * 128 + quarter * 32 + lane;
+      if (tok < n_tokens) {
+        float lg[kMaxExperts];
+#pragma unroll
+        for (int e = 0; e < kMaxExperts; ++e) lg[e] = round_to<T>(__uint_as_float(r[e]));
+        route_token<T>(lg, E, k, tie_low_first != 0, tok, logits_out, idx_out, gates_out, hist_s, err);
+      }
+      named_bar_sync(1, 128);
+      const int et = threadIdx.x - 64;  // epilogue thread index 0..127
+      if (et < E) {
+        block_hist[static_cast<int64_t>(t) * E + et] = hist_s[et];
+        hist_s[et] = 0;
+      }
+      named_bar_sync(1, 128);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 32);
+  }
+}
+
+template <typename T>
+static cudaError_t launch_router_tc(const void* x, const void* w, int64_t n_tokens, int d, int E, int k,
+                                    int tie_low_first, float* logits_out, int32_t* idx, void* gates,
+                                    int32_t* block_hist, int* err, int num_sms, cudaStream_t stream) {
+  const CUtensorMapDataType dt = (Traits<T>::code == AGM_BF16) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                                : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap tmX, tmW;
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(d), static_cast<uint64_t>(n_tokens)};
+    const uint64_t str[1] = {static_cast<uint64_t>(d) * 2};
+    const uint32_t box[2] = {64, 128};
+    if (!encode_tmap(&tmX, x, 2, dims, str, box, dt)) return cudaErrorInvalidValue;
+  }
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(d), static_cast<uint64_t>(E)};
+    const uint64_t str[1] = {static_cast<uint64_t>(d) * 2};
+    const uint32_t box[2] = {64, 16};
+    if (!encode_tmap(&tmW, w, 2, dims, str, box, dt)) return cudaErrorInvalidValue;
+  }
+  const int nkb = (d + 63) / 64;
+  const int smem = rt_smem_bytes(nkb);
+  cudaError_t e = cudaFuncSetAttribute(router_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  const int64_t tiles = (n_tokens + 127) / 128;
+  const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms));
+  router_tc_kernel<T><<<grid, kRtThreads, smem, stream>>>(tmX, tmW, n_tokens, d, E, k, tie_low_first, logits_out,
+                                                          idx, static_cast<T*>(gates), block_hist, err);
+  return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t launch_router(const void* x, const void* w, int64_t n_tokens, int d, int E, int k,
+                                 int tie_low_first, const float* logits_in, float* logits_out, int32_t* idx,
+                                 void* gates, int32_t* block_hist, int* err, cudaStream_t stream) {
   const int64_t nblk = (n_tokens + kDispatchBlock - 1) / kDispatchBlock;
   const size_t smem = (logits_in ? 0 : static_cast<size_t>(E) * d * sizeof(float)) +
                       static_cast<size_t>(kRouterWarps) * 32 * kMaxExperts * sizeof(float);
@@ -284,25 +512,36 @@ static cudaError_t launch_router(const void* x, const void* w, int64_t n_tokens,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   router_topk_kernel<T><<<static_cast<unsigned>(nblk), kDispatchBlock, smem, stream>>>(
-      static_cast<const T*>(x), static_cast<const T*>(w), n_tokens, d, E, k, tie_low_first, logits_in, logits_out, idx,
-      static_cast<T*>(gates), block_hist, err);
+      static_cast<const T*>(x), static_cast<const T*>(w), n_tokens, d, E, k, tie_low_first, logits_in, logits_out,
+      idx, static_cast<T*>(gates), block_hist, err);
   return cudaGetLastError();
 }
 
+// The tensor-core router keeps the whole router weight resident next to its
+// 8-stage x ring: d up to 4096 (64 k-blocks of 2 KB) fits in shared memory.
+bool router_tc_supported(int d) { return d > 0 && d % 8 == 0 && rt_smem_bytes((d + 63) / 64) <= 227 * 1024; }
+
 cudaError_t router_topk(int dtype, const void* x, const void* w, int64_t n_tokens, int d, int E, int k,
                         int tie_low_first, const float* logits_in, float* logits_out, int32_t* idx, void* gates,
-                        int32_t* block_hist, int* err, cudaStream_t stream) {
+                        int32_t* block_hist, int* err, int num_sms, cudaStream_t stream) {
   if (n_tokens == 0) return cudaSuccess;
+  const bool tc = !logits_in && router_tc_supported(d);
   switch (dtype) {
     case AGM_F32:
-      return launch_router<float>(x, w, n_tokens, d, E, k, tie_low_first, logits_in, logits_out, idx, gates, block_hist,
-                                  err, stream);
+      return launch_router<float>(x, w, n_tokens, d, E, k, tie_low_first, logits_in, logits_out, idx, gates,
+                                  block_hist, err, stream);
     case AGM_BF16:
+      if (tc)
+        return launch_router_tc<__nv_bfloat16>(x, w, n_tokens, d, E, k, tie_low_first, logits_out, idx, gates,
+                                               block_hist, err, num_sms, stream);
       return launch_router<__nv_bfloat16>(x, w, n_tokens, d, E, k, tie_low_first, logits_in, logits_out, idx, gates,
                                           block_hist, err, stream);
     case AGM_F16:
-      return launch_router<__half>(x, w, n_tokens, d, E, k, tie_low_first, logits_in, logits_out, idx, gates, block_hist,
-                                   err, stream);
+      if (tc)
+        return launch_router_tc<__half>(x, w, n_tokens, d, E, k, tie_low_first, logits_out, idx, gates, block_hist,
+                                        err, num_sms, stream);
+      return launch_router<__half>(x, w, n_tokens, d, E, k, tie_low_first, logits_in, logits_out, idx, gates,
+                                   block_hist, err, stream);
     default:
       return cudaErrorInvalidValue;
   }

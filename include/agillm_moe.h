@@ -50,7 +50,7 @@ enum {
  * padded to a multiple of this. */
 #define AGM_TILE_M 128
 /* Tokens handled by one CTA of the router and permute kernels. */
-#define AGM_DISPATCH_BLOCK 256
+#define AGM_DISPATCH_BLOCK 128
 /* Largest supported number of experts (router kernel keeps 16 logits/token). */
 #define AGM_MAX_EXPERTS 16
 

@@ -39,9 +39,10 @@ def test_library_has_no_driver_link_dependency():
 def test_size_helpers():
     lib = _lib.load()
     assert lib.agm_dispatch_blocks(0) == 0
+    B = _lib.AGM_DISPATCH_BLOCK
     assert lib.agm_dispatch_blocks(1) == 1
-    assert lib.agm_dispatch_blocks(256) == 1
-    assert lib.agm_dispatch_blocks(257) == 2
+    assert lib.agm_dispatch_blocks(B) == 1
+    assert lib.agm_dispatch_blocks(B + 1) == 2
     assert lib.agm_max_rows(73728, 2, 14) == ((2 * 73728 + 14 * 127 + 127) // 128) * 128
     assert lib.agm_max_rows(0, 2, 14) == 0
     ws = lib.agm_moe_workspace_bytes(73728, 1280, 14, 2, 3200, 0, 1, _lib.AGM_BF16)

@@ -4,7 +4,7 @@ import pytest
 import torch
 import torch.nn.functional as F
 
-from agillm41_b200 import ops
+from agillm41_b200 import _lib, ops
 from agillm41_b200._lib import read_device_error
 from oracle import permute_oracle
 
@@ -134,7 +134,7 @@ def test_dispatch_plan_and_permute_exact(n, E, k):
     nb = ops.dispatch_blocks(n)
     hist = torch.zeros(nb, E, dtype=torch.int32)
     for b in range(nb):
-        seg = idx_np[b * 256:(b + 1) * 256].reshape(-1)
+        seg = idx_np[b * _lib.AGM_DISPATCH_BLOCK:(b + 1) * _lib.AGM_DISPATCH_BLOCK].reshape(-1)
         hist[b] = torch.from_numpy(np.bincount(seg, minlength=E).astype(np.int32))
     hist = hist.to(DEV)
     err = _err()
