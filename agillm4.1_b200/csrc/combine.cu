@@ -45,10 +45,69 @@ __device__ __forceinline__ uint4 store8(const float (&acc)[8]) {
 // out chunk = ((0 + round(y_0 g_0)) + round(y_1 g_1) + ...) [+ shared sum], each
 // op rounded to T. __fmul_rn/__fadd_rn are never contracted into an FMA, so
 // the product is rounded on its own as in the reference's `y * w` tensor.
+// 16-bit types: the same chain on packed pairs. For bf16/fp16 operands a
+// correctly rounded 16-bit multiply or add equals the fp32 operation followed
+// by one rounding (the fp32 product is exact; an fp32 sum can only round where
+// the smaller addend is below half a 16-bit ulp of the larger), and the _rn
+// intrinsics are never contracted into an FMA.
+template <typename T> struct Pair;
+template <> struct Pair<__nv_bfloat16> {
+  using V = __nv_bfloat162;
+  __device__ __forceinline__ static V mul(V a, V b) { return __hmul2_rn(a, b); }
+  __device__ __forceinline__ static V add(V a, V b) { return __hadd2_rn(a, b); }
+  __device__ __forceinline__ static V splat(float g) { return __float2bfloat162_rn(g); }
+  __device__ __forceinline__ static V zero() { return __float2bfloat162_rn(0.f); }
+};
+template <> struct Pair<__half> {
+  using V = __half2;
+  __device__ __forceinline__ static V mul(V a, V b) { return __hmul2_rn(a, b); }
+  __device__ __forceinline__ static V add(V a, V b) { return __hadd2_rn(a, b); }
+  __device__ __forceinline__ static V splat(float g) { return __float2half2_rn(g); }
+  __device__ __forceinline__ static V zero() { return __float2half2_rn(0.f); }
+};
+
+template <typename T, int K_MAX>
+__device__ __forceinline__ uint4 combine_chunk16(const uint4 (&v)[K_MAX], const float (&g)[K_MAX], int k,
+                                                 const T* __restrict__ shared_y, int n_shared,
+                                                 int64_t shared_stride, int64_t tok, int d, int c) {
+  using P = Pair<T>;
+  using V = typename P::V;
+  V acc[4] = {P::zero(), P::zero(), P::zero(), P::zero()};
+#pragma unroll
+  for (int r = 0; r < K_MAX; ++r) {
+    if (r < k) {
+      const V gg = P::splat(g[r]);  // exact: g is a T value
+      const V* y = reinterpret_cast<const V*>(&v[r]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[j] = P::add(acc[j], P::mul(y[j], gg));
+    }
+  }
+  if (n_shared > 0) {
+    V s[4];
+    for (int si = 0; si < n_shared; ++si) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(shared_y + si * shared_stride + tok * d) + c);
+      const V* f = reinterpret_cast<const V*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s[j] = (si == 0) ? f[j] : P::add(s[j], f[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[j] = P::add(acc[j], s[j]);
+  }
+  uint4 o;
+  o.x = *reinterpret_cast<uint32_t*>(&acc[0]);
+  o.y = *reinterpret_cast<uint32_t*>(&acc[1]);
+  o.z = *reinterpret_cast<uint32_t*>(&acc[2]);
+  o.w = *reinterpret_cast<uint32_t*>(&acc[3]);
+  return o;
+}
+
 template <typename T, int K_MAX>
 __device__ __forceinline__ uint4 combine_chunk(const uint4 (&v)[K_MAX], const float (&g)[K_MAX], int k,
                                                const T* __restrict__ shared_y, int n_shared,
                                                int64_t shared_stride, int64_t tok, int d, int c) {
+  if constexpr (sizeof(T) == 2) {
+    return combine_chunk16<T, K_MAX>(v, g, k, shared_y, n_shared, shared_stride, tok, d, c);
+  }
   constexpr int CH = 16 / sizeof(T);
   float acc[8];
 #pragma unroll

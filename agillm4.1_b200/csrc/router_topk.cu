@@ -6,8 +6,8 @@
 //
 // bf16 / fp16 (router_tc_kernel): the logits are a [N, d] x [d, E] product, so
 // they run on the 5th-generation tensor cores while x streams from HBM once:
-// persistent CTAs (one per SM) walk 128-token tiles; warp 0 streams 128x64
-// tiles of x through an 8-stage TMA ring, the router weight [E <= 16, d]
+// persistent CTAs (two per SM) walk 128-token tiles; warp 0 streams 128x64
+// tiles of x through a 4-stage TMA ring, the router weight [E <= 16, d]
 // stays resident in shared memory (TMA zero-fills rows E..15), warp 1 issues
 // tcgen05.mma M=128 N=16 K=16 with fp32 accumulation into TMEM (two 16-column
 // buffers), and each of the 128 epilogue threads reads the 16 logits of its
@@ -297,7 +297,7 @@ __global__ void __launch_bounds__(kDispatchBlock) router_topk_kernel(
 // ---------------------------------------------------------------------------
 // Tensor-core router (bf16 / fp16): TMA-fed tcgen05, thread-per-token epilogue
 // ---------------------------------------------------------------------------
-constexpr int kRtStages = 8;
+constexpr int kRtStages = 4;   // two CTAs per SM: 8 x 16 KB of x in flight per SM
 constexpr int kRtThreads = 192;
 constexpr int kRtABytes = 128 * 64 * 2;   // one 128-token x 64-feature tile
 constexpr int kRtWBytes = 16 * 64 * 2;    // one 16-expert x 64-feature tile of the router weight
@@ -307,7 +307,7 @@ __host__ __device__ constexpr int rt_smem_bytes(int nkb) {
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(
+__global__ void __launch_bounds__(kRtThreads, 2) router_tc_kernel(
     const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, int64_t n_tokens, int d,
     int E, int k, int tie_low_first, float* __restrict__ logits_out, int32_t* __restrict__ idx_out,
     T* __restrict__ gates_out, int32_t* __restrict__ block_hist, int* err) {
@@ -495,7 +495,7 @@ static cudaError_t launch_router_tc(const void* x, const void* w, int64_t n_toke
   cudaError_t e = cudaFuncSetAttribute(router_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   const int64_t tiles = (n_tokens + 127) / 128;
-  const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms));
+  const int grid = static_cast<int>(std::min<int64_t>(tiles, 2 * num_sms));
   router_tc_kernel<T><<<grid, kRtThreads, smem, stream>>>(tmX, tmW, n_tokens, d, E, k, tie_low_first, logits_out,
                                                           idx, static_cast<T*>(gates), block_hist, err);
   return cudaGetLastError();
