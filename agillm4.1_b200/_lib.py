@@ -21,6 +21,7 @@ AGM_TILE_M = 128
 AGM_DISPATCH_BLOCK = 128
 AGM_MAX_EXPERTS = 16
 AGM_FLAG_TIE_LOW_FIRST = 0x1
+AGM_FLAG_KEEP_ERROR = 0x2
 AGM_STAGE_EVENTS = 8
 
 _DTYPE_CODE = {torch.float32: AGM_F32, torch.bfloat16: AGM_BF16, torch.float16: AGM_F16}
@@ -41,6 +42,9 @@ SIGNATURES = {
     "agm_moe_forward": (_I, [_P, _I, _I64, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _P, _P,
                              _P, _SZ, _I, _P, _P, _P, _P, _P, _P, _P]),
     "agm_read_device_error": (_I, [_P, _P, _P]),
+    "agm_moe_host_workspace_bytes": (_SZ, [_I64, _I, _I, _I, _I, _I, _I, _I]),
+    "agm_moe_forward_host": (_I, [_P, _I, _I64, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _P, _P, _P,
+                                  _SZ, _I64, _I, _P]),
     "agm_moe_forward_noalloc": (_I, [_P, _I, _I64, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _P, _P,
                                      _I, _P]),
 }

@@ -284,8 +284,11 @@ int agm_moe_forward(const void* x, int dtype, int64_t n_tokens, int d, int n_exp
   auto mark = [&](int i) -> cudaError_t {
     return stage_events ? cudaEventRecord(static_cast<cudaEvent_t>(stage_events[i]), stream) : cudaSuccess;
   };
-  cudaError_t e = cudaMemsetAsync(L.err, 0, sizeof(int), stream);
-  if (e != cudaSuccess) return cuda_fail(e, "memset");
+  cudaError_t e = cudaSuccess;
+  if (!(flags & AGM_FLAG_KEEP_ERROR)) {
+    e = cudaMemsetAsync(L.err, 0, sizeof(int), stream);
+    if (e != cudaSuccess) return cuda_fail(e, "memset");
+  }
   if (n_tokens == 0) {
     for (int i = 0; i < AGM_STAGE_EVENTS && e == cudaSuccess; ++i) e = mark(i);
     return e == cudaSuccess ? AGM_OK : cuda_fail(e, "event record");

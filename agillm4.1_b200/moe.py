@@ -121,6 +121,32 @@ class _B200Forward:
         return out.reshape(orig_shape)
 
 
+    def forward_host(self, x_host: torch.Tensor, out_host: Optional[torch.Tensor] = None,
+                     chunk_tokens: int = ops.DEFAULT_CHUNK_TOKENS) -> torch.Tensor:
+        """The forward for activations in host memory: x_host [..., d] on the CPU
+        (page-locked for overlap) -> output on the CPU, same shape and dtype.
+        Copies and compute overlap chunk by chunk on the module's GPU; the
+        result is ready when this returns (it synchronises the stream)."""
+        orig_shape = x_host.shape
+        flat = x_host.reshape(-1, orig_shape[-1])
+        if flat.is_cuda:
+            return self.forward(x_host)
+        if torch.is_grad_enabled() and any(p.requires_grad for p in self.parameters()):
+            raise MoEKernelError("MoEFFN (B200) implements the inference forward only; run it under torch.no_grad()")
+        wr = self.router.weight
+        if not wr.is_cuda:
+            raise MoEKernelError("MoEFFN (B200): move the module to a CUDA device first")
+        if flat.dtype != wr.dtype:
+            raise MoEKernelError(f"input dtype {flat.dtype} differs from the weight dtype {wr.dtype}")
+        w1, b1, w2, b2, sh = self._packed_weights(wr.device, wr.dtype)
+        out = None if out_host is None else out_host.reshape(-1, orig_shape[-1])
+        out = ops.moe_forward_host(flat.contiguous(), wr.detach().contiguous(), w1, b1, w2, b2, self.top_k,
+                                   shared=sh, out_host=out, chunk_tokens=chunk_tokens,
+                                   check_errors=self.check_device_errors)
+        torch.cuda.current_stream(wr.device).synchronize()
+        return out.reshape(orig_shape)
+
+
 class MoEFFN(_B200Forward, nn.Module):
     """AGILLM4.1 MoE feed-forward block (reference interface, B200 forward)."""
 

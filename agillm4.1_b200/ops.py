@@ -226,3 +226,65 @@ def moe_forward(x: torch.Tensor, w_router: torch.Tensor, w1: torch.Tensor, b1: t
         if code:
             raise _lib.MoEKernelError(f"device error word 0x{code:x} after agm_moe_forward")
     return (out, extras) if want else out
+
+
+class HostWorkspace:
+    """Device scratch for :func:`moe_forward_host`, one per (device, stream)."""
+
+    _cache: Dict[tuple, torch.Tensor] = {}
+
+    @classmethod
+    def get(cls, device: torch.device, nbytes: int) -> torch.Tensor:
+        key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+        buf = cls._cache.get(key)
+        if buf is None or buf.numel() < nbytes:
+            cls._cache.pop(key, None)
+            buf = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
+            cls._cache[key] = buf
+        return buf
+
+
+DEFAULT_CHUNK_TOKENS = 8192
+
+
+def moe_forward_host(x_host: torch.Tensor, w_router: torch.Tensor, w1: torch.Tensor, b1: torch.Tensor,
+                     w2: torch.Tensor, b2: torch.Tensor, top_k: int, *, shared: Optional[tuple] = None,
+                     out_host: Optional[torch.Tensor] = None, chunk_tokens: int = DEFAULT_CHUNK_TOKENS,
+                     tie_low_first: bool = False, check_errors: bool = False) -> torch.Tensor:
+    """MoE forward on host tensors: x_host [N, d] (CPU, ideally pinned) -> out_host [N, d] (CPU).
+
+    Weights are on the GPU (the current device). Copies in, the forward and
+    copies out overlap chunk by chunk; on return the current stream is ordered
+    after the last copy, so ``torch.cuda.current_stream().synchronize()``
+    makes ``out_host`` ready.
+    """
+    lib = load()
+    if x_host.is_cuda:
+        raise _lib.MoEKernelError("moe_forward_host takes host (CPU) tensors; use moe_forward for device tensors")
+    if not x_host.is_contiguous():
+        raise _lib.MoEKernelError("x_host must be contiguous")
+    n, d = x_host.shape
+    E = w_router.shape[0]
+    H = w1.shape[1]
+    dev = w1.device
+    if shared is not None:
+        ws1, sb1, ws2, sb2 = shared
+        S, Hs = ws1.shape[0], ws1.shape[1]
+    else:
+        ws1 = sb1 = ws2 = sb2 = None
+        S, Hs = 0, 0
+    if out_host is None:
+        out_host = torch.empty(n, d, dtype=x_host.dtype, pin_memory=True)
+    chunk = max(1, min(int(chunk_tokens), n)) if n else 1
+    nbytes = int(lib.agm_moe_host_workspace_bytes(chunk, d, E, top_k, H, S, max(Hs, 1), dtype_code(x_host.dtype)))
+    ws = HostWorkspace.get(dev, nbytes)
+    rc = lib.agm_moe_forward_host(
+        x_host.data_ptr(), dtype_code(x_host.dtype), n, d, E, top_k, H, ptr(w_router), ptr(w1), ptr(b1), ptr(w2),
+        ptr(b2), S, max(Hs, 1), ptr(ws1), ptr(sb1), ptr(ws2), ptr(sb2), out_host.data_ptr(), ptr(ws), ws.numel(),
+        chunk, _flags(tie_low_first), stream_handle(dev))
+    check(rc, "agm_moe_forward_host")
+    if check_errors:
+        code = _lib.read_device_error(ws[:4].view(torch.int32))
+        if code:
+            raise _lib.MoEKernelError(f"device error word 0x{code:x} after agm_moe_forward_host")
+    return out_host

@@ -60,6 +60,7 @@ enum {
 /* forward flags */
 #define AGM_FLAG_TIE_LOW_FIRST 0x1 /* order exactly-equal top-k values by ascending expert index
                                       (default: descending, as torch.topk does on CUDA) */
+#define AGM_FLAG_KEEP_ERROR 0x2    /* agm_moe_forward: do not clear the device error word first */
 
 AGM_API const char* agm_last_error(void);
 AGM_API int agm_abi_version(void);
@@ -165,6 +166,27 @@ AGM_API int agm_moe_forward_noalloc(const void* x, int dtype, int64_t n_tokens, 
                                     int hidden, const void* w_router, const void* w1, const void* b1, const void* w2,
                                     const void* b2, int n_shared, int shared_hidden, const void* ws1, const void* sb1,
                                     const void* ws2, const void* sb2, void* out, int flags, void* stream);
+
+/* Device workspace for agm_moe_forward_host with chunks of chunk_tokens. */
+AGM_API size_t agm_moe_host_workspace_bytes(int64_t chunk_tokens, int d, int n_experts, int top_k, int hidden,
+                                            int n_shared, int shared_hidden, int dtype);
+
+/* MoEFFN.forward (agillm41.py:4389-4431) on HOST buffers x_host [n, d] ->
+ * out_host [n, d] (page-locked for overlap), for callers whose activations
+ * live in host memory (the reference pages layers between host and device,
+ * agillm41.py:7656-7668). The batch is split into chunks of chunk_tokens;
+ * the host->device copy of one chunk, the forward of the previous one and
+ * the device->host copy of the one before run concurrently (two copy streams
+ * owned by the library, the forward on `stream`). Bit-identical to
+ * agm_moe_forward on the whole batch. Weights are device pointers as for
+ * agm_moe_forward; workspace >= agm_moe_host_workspace_bytes(chunk_tokens,...).
+ * On return `stream` is ordered after the last copy out. The device error
+ * word (first int of the workspace) accumulates over all chunks.            */
+AGM_API int agm_moe_forward_host(const void* x_host, int dtype, int64_t n_tokens, int d, int n_experts, int top_k,
+                                 int hidden, const void* w_router, const void* w1, const void* b1, const void* w2,
+                                 const void* b2, int n_shared, int shared_hidden, const void* ws1, const void* sb1,
+                                 const void* ws2, const void* sb2, void* out_host, void* workspace,
+                                 size_t workspace_bytes, int64_t chunk_tokens, int flags, void* stream);
 
 /* Synchronise `stream`, read the device error word at `err` (e.g. the first
  * int of a forward workspace) into *code and reset it to 0. Returns AGM_OK if

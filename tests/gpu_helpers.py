@@ -49,7 +49,8 @@ def assert_close_rows(ours, ref, rows_ok, dtype, term_scale=None, slack=None):
     """Output parity on the rows whose routing matches.
 
     fp32: every element within 1e-4 (abs and rel).
-    bf16/fp16: every element within 1e-2 abs + 2e-2 rel, or - where the gated
+    bf16/fp16: every element within 1e-2 abs + 2e-2 rel, or (at most 1e-3 of
+    the elements) - where the gated
     expert outputs nearly cancel - within two bf16 ulps of the magnitude of
     the summed terms (`term_scale` from the oracle): any two implementations
     whose fp32 accumulation orders differ can round an expert output to
@@ -72,7 +73,7 @@ def assert_close_rows(ours, ref, rows_ok, dtype, term_scale=None, slack=None):
         bad = diff > env
         assert not bool(bad.any()), (
             f"{int(bad.sum())} elements beyond the rounding envelope (max diff {diff.max().item():.4g})")
-        assert int(outside.sum()) <= max(1, int(1e-4 * b.numel())), int(outside.sum())
+        assert int(outside.sum()) <= max(1, int(1e-3 * b.numel())), int(outside.sum())
         return
     n_out = int(outside.sum())
     assert n_out <= max(1, int(1e-5 * b.numel())), (

@@ -197,3 +197,34 @@ def test_module_production_shape_top1_shared():
         ref = reference_moe.moe_forward(x, sd, 1)
     assert_close_rows(y.reshape(-1, d), ref.reshape(-1, d), torch.ones(300, dtype=torch.bool, device=DEV),
                       torch.bfloat16)
+
+
+@pytest.mark.parametrize("n,chunk", [(5000, 1024), (4096, 4096), (3000, 8192), (777, 100)])
+def test_host_pipeline_bit_identical(n, chunk):
+    """agm_moe_forward_host (host buffers, chunked, copies overlapped with the
+    forward) gives exactly the device forward's result."""
+    d, H, E, k = 1280, 3200, 14, 2
+    sd = reference_moe.make_state(d, H, E, 21, dtype=torch.bfloat16, device=DEV, bias_std=0.02)
+    w1, b1, w2, b2, _ = packed(sd, E, DEV)
+    wr = sd["router.weight"].contiguous()
+    x = reference_moe.make_input(n, d, 21, dtype=torch.bfloat16)
+    ref = ops.moe_forward(x.to(DEV), wr, w1, b1, w2, b2, k)
+    x_host = x.pin_memory()
+    out = ops.moe_forward_host(x_host, wr, w1, b1, w2, b2, k, chunk_tokens=chunk, check_errors=True)
+    torch.cuda.current_stream().synchronize()
+    assert torch.equal(out, ref.cpu())
+
+
+def test_module_forward_host_matches_device():
+    d, H, E, k = 1280, 3200, 14, 2
+    m = agillm41_b200.MoEFFN(d, mlp_mult=4, experts=E, top_k=k)
+    m.experts = torch.nn.ModuleList([torch.nn.Sequential(torch.nn.Linear(d, H), torch.nn.ReLU(),
+                                                         torch.nn.Linear(H, d)) for _ in range(E)])
+    m.load_state_dict(reference_moe.make_state(d, H, E, 22, bias_std=0.02))
+    m = m.to(device=DEV, dtype=torch.bfloat16).eval()
+    x = reference_moe.make_input(2 * 700, d, 22, dtype=torch.bfloat16).reshape(2, 700, d)
+    with torch.no_grad():
+        y_dev = m(x.to(DEV)).cpu()
+        y_host = m.forward_host(x.pin_memory(), chunk_tokens=512)
+    assert y_host.shape == x.shape and not y_host.is_cuda
+    assert torch.equal(y_host, y_dev)
