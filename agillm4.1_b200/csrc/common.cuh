@@ -164,7 +164,7 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
 }
 
 // ---------------------------------------------------------------------------
-// TMA (no multicast anywhere in this library)
+// TMA: every copy is issued by and lands in one CTA of this GPU
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");

@@ -16,7 +16,7 @@
 //
 // bf16/fp16 path (tcgen05, sm_100a): persistent CTAs (one per SM), 320
 // threads: warp 0 issues TMA loads (128x64 A tile + BNx64 W tile per stage,
-// 128-byte swizzle, no multicast), warp 1 owns the TMEM allocation and issues
+// 128-byte swizzle, one CTA per copy), warp 1 owns the TMEM allocation and issues
 // tcgen05.mma (M=128, N=BN, K=16, fp32 accumulation in TMEM), warps 2-9 drain
 // the accumulator (tcgen05.ld; two warps per TMEM lane quarter, alternate
 // 64-column chunks), add the bias, apply ReLU, round to the activation dtype,

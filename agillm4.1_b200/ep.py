@@ -1,0 +1,201 @@
+"""Expert-parallel MoE block forward across the GPUs of one node.
+
+The reference runs the whole MoE block on one device (agillm41.py:4389-4431);
+this module spreads the expert FFN work of a block over P ranks (one process
+per GPU, `torch.distributed` over NCCL) while every rank keeps its own tokens:
+
+1. each rank routes and permutes its tokens (router, dispatch plan, permute
+   kernels): x_perm holds its rows expert-major, each (rank, expert) segment
+   padded to 128-row GEMM tiles;
+2. the ranks all-gather their per-expert counts (E int32 per rank; one
+   device->host read per forward for the all-to-all split sizes);
+3. every rank computes the same plan (:func:`plan_dispatch`) over the global
+   tile sequence ordered by (expert, source rank, tile); rank r computes a
+   contiguous range of it. Along any source's x_perm the destination rank is
+   non-decreasing, so x_perm itself is the all-to-all send buffer;
+4. all-to-all of the rows (NCCL, NVLink/NVSwitch), the grouped FC1/FC2 GEMM
+   on the received tiles (the tile -> expert table comes from the plan), and
+   the reverse all-to-all, which returns y rows to their x_perm positions;
+5. each rank combines its tokens' k rows (the unchanged combine kernel).
+
+Placement:
+* ``"static"``: expert ownership in contiguous ranges (14 experts over 2/4/8
+  ranks: 7/7, 4/4/3/3, 2x6+1x2); a rank holds the weights of its experts only.
+* ``"balanced"``: every rank holds all expert weights and the global tile
+  sequence is cut into P near-equal ranges, so a hot expert's tiles are spread
+  over several ranks (skewed routing stays balanced; results are unchanged
+  because rows are independent).
+
+Rows are independent in the MoE block, so the output of every token is
+bit-identical to the single-GPU forward of the same token.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import List, Optional, Sequence
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+TILE = 128
+
+
+def static_owner_ranges(n_experts: int, world: int) -> List[range]:
+    """Contiguous expert ranges: the first (E mod P) ranks get one more."""
+    base, extra = divmod(n_experts, world)
+    out, e = [], 0
+    for r in range(world):
+        n = base + (1 if r < extra else 0)
+        out.append(range(e, e + n))
+        e += n
+    return out
+
+
+@dataclass
+class DispatchPlan:
+    """Per-rank view of one expert-parallel dispatch.
+
+    send_rows[r]    rows of this rank's x_perm sent to rank r (in order)
+    recv_rows[i]    rows received from source rank i (in order)
+    recv_tile_expert  expert of every received 128-row tile (receive order)
+    tile_ranges     [P+1] boundaries of the ranks' ranges in the global tile sequence
+    """
+
+    send_rows: List[int]
+    recv_rows: List[int]
+    recv_tile_expert: np.ndarray
+    tile_ranges: np.ndarray
+    local_rows: int
+
+
+def plan_dispatch(counts_all: np.ndarray, rank: int, placement: str = "static") -> DispatchPlan:
+    """Plan one forward from the all-gathered counts [P, E] (rows per rank per expert)."""
+    counts_all = np.asarray(counts_all, dtype=np.int64)
+    P, E = counts_all.shape
+    tiles = (counts_all + TILE - 1) // TILE                      # [P, E]
+    # Global tile sequence ordered by (expert, source rank, tile).
+    per_e = tiles.sum(axis=0)                                     # [E]
+    e_start = np.concatenate([[0], np.cumsum(per_e)])             # [E+1]
+    total = int(e_start[-1])
+    if placement == "static":
+        owners = static_owner_ranges(E, P)
+        bounds = np.array([e_start[o.start] for o in owners] + [total], dtype=np.int64)
+    elif placement == "balanced":
+        bounds = np.array([(r * total) // P for r in range(P)] + [total], dtype=np.int64)
+    else:
+        raise ValueError(f"placement must be 'static' or 'balanced', not {placement!r}")
+    # Global position of source i's tiles for expert e: e_start[e] + sum_{i'<i} tiles[i', e].
+    src_off = np.zeros((P, E), dtype=np.int64)
+    src_off[1:] = np.cumsum(tiles, axis=0)[:-1]
+    g0 = e_start[:-1][None, :] + src_off                          # [P, E] first global tile
+    g1 = g0 + tiles                                               # [P, E] one past last
+
+    def overlap(i, r):
+        lo, hi = bounds[r], bounds[r + 1]
+        return np.clip(np.minimum(g1[i], hi) - np.maximum(g0[i], lo), 0, None)  # [E] tiles
+
+    send_rows = [int(overlap(rank, r).sum()) * TILE for r in range(P)]
+    recv_rows = [int(overlap(i, rank).sum()) * TILE for i in range(P)]
+    te = []
+    for i in range(P):
+        ov = overlap(i, rank)
+        for e in range(E):
+            te.extend([e] * int(ov[e]))
+    return DispatchPlan(send_rows, recv_rows, np.asarray(te, dtype=np.int32), bounds,
+                        int(tiles[rank].sum()) * TILE)
+
+
+class LocalOps:
+    """The single-GPU kernel stages used by the expert-parallel forward."""
+
+    def route(self, x, w_router, top_k):
+        """-> (idx, gates, x_perm, row_of, counts[E] int32 on device)."""
+        from . import ops
+        idx, gates, hist, _ = ops.router_topk(x, w_router, top_k)
+        plan = ops.dispatch_plan(hist, x.shape[0], top_k)
+        x_perm, row_of = ops.permute(x, idx, plan, w_router.shape[0])
+        return idx, gates, x_perm, row_of, plan["counts"]
+
+    def ffn(self, rows, w1, b1, w2, b2, tile_expert):
+        from . import ops
+        n_tiles = tile_expert.numel()
+        h = ops.grouped_gemm(rows, w1, b1, relu=True, tile_group=tile_expert, max_tiles=n_tiles)
+        return ops.grouped_gemm(h, w2, b2, relu=False, tile_group=tile_expert, max_tiles=n_tiles)
+
+    def combine(self, y_perm, row_of, gates):
+        from . import ops
+        return ops.combine(y_perm, row_of, gates)
+
+
+class ExpertParallelMoE:
+    """Expert-parallel forward of one MoE block (no autograd).
+
+    ``weights``: (w_router [E, d], w1 [E_w, H, d], b1 [E_w, H], w2 [E_w, d, H],
+    b2 [E_w, d]) on this rank's device, where E_w = E for "balanced" and the
+    rank's owned experts (``static_owner_ranges``) for "static".
+    """
+
+    def __init__(self, weights: Sequence[torch.Tensor], top_k: int, n_experts: int, group=None,
+                 placement: str = "static", local_ops: Optional[LocalOps] = None):
+        self.w_router, self.w1, self.b1, self.w2, self.b2 = weights
+        self.top_k = int(top_k)
+        self.E = int(n_experts)
+        self.group = group
+        self.placement = placement
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.ops = local_ops or LocalOps()
+        self.first_local_expert = static_owner_ranges(self.E, self.world)[self.rank].start \
+            if placement == "static" else 0
+        self.last_plan: Optional[DispatchPlan] = None
+
+    @staticmethod
+    def shard_weights(w1, b1, w2, b2, rank: int, world: int, placement: str):
+        """The expert weights a rank keeps for a placement."""
+        if placement == "balanced":
+            return w1, b1, w2, b2
+        r = static_owner_ranges(w1.shape[0], world)[rank]
+        return (w1[r.start:r.stop].contiguous(), b1[r.start:r.stop].contiguous(),
+                w2[r.start:r.stop].contiguous(), b2[r.start:r.stop].contiguous())
+
+    def forward(self, x: torch.Tensor, events: Optional[Sequence] = None) -> torch.Tensor:
+        """``events``: optional 7 CUDA events recorded on the current stream at
+        the boundaries route | count exchange + plan | dispatch all-to-all |
+        expert FFN | return all-to-all | combine (for timing)."""
+        n, d = x.shape
+
+        def mark(i):
+            if events is not None:
+                events[i].record()
+
+        mark(0)
+        idx, gates, x_perm, row_of, counts = self.ops.route(x, self.w_router, self.top_k)
+        mark(1)
+        # (2) counts of every rank; one device->host read for the split sizes.
+        counts_all = torch.empty(self.world * self.E, dtype=counts.dtype, device=counts.device)
+        dist.all_gather_into_tensor(counts_all, counts.contiguous(), group=self.group)
+        plan = plan_dispatch(counts_all.cpu().numpy().reshape(self.world, self.E), self.rank, self.placement)
+        self.last_plan = plan
+        # (4) dispatch rows, expert FFN on the received tiles, return rows.
+        send = x_perm[:plan.local_rows]
+        recv = torch.empty(sum(plan.recv_rows), d, dtype=x.dtype, device=x.device)
+        tile_expert = torch.from_numpy(plan.recv_tile_expert - self.first_local_expert).to(x.device,
+                                                                                           non_blocking=True)
+        mark(2)
+        dist.all_to_all_single(recv, send, output_split_sizes=plan.recv_rows, input_split_sizes=plan.send_rows,
+                               group=self.group)
+        mark(3)
+        if recv.shape[0] > 0:
+            y_recv = self.ops.ffn(recv, self.w1, self.b1, self.w2, self.b2, tile_expert)
+        else:
+            y_recv = recv
+        mark(4)
+        y_perm = torch.empty_like(x_perm)
+        dist.all_to_all_single(y_perm[:plan.local_rows], y_recv.contiguous(), output_split_sizes=plan.send_rows,
+                               input_split_sizes=plan.recv_rows, group=self.group)
+        mark(5)
+        # (5) combine this rank's tokens.
+        out = self.ops.combine(y_perm, row_of, gates)
+        mark(6)
+        return out

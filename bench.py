@@ -51,6 +51,12 @@ PERMUTE_BYTES = 2 * D + 4 * TOP_K + 2 * D * TOP_K + 4 * TOP_K + 4 * TOP_K  # x, 
 COMBINE_BYTES = 2 * D * TOP_K + 4 * TOP_K + 2 * TOP_K + 2 * D             # k rows, row_of, gates -> out row
 STAGES = ["router", "plan", "permute", "fc1", "fc2", "shared", "combine"]
 KERNELS_PER_STEP = 6   # router, plan, permute, fc1, fc2, combine
+TILE_ROWS = 128
+# Multi-GPU workload: each rank holds B x L tokens; router logits carry a
+# per-expert bias log(p_e) * ZIPF_SCALE with p Zipf(1.2) over a seeded
+# permutation of the experts (seed 3), which gives a ~5:1 max/mean expert load.
+EP_SEED, ZIPF_S, ZIPF_SCALE = 3, 1.2, 0.63
+EP_STAGES = ["route", "counts_plan", "dispatch_a2a", "expert_ffn", "return_a2a", "combine"]
 
 
 def load_peaks():
@@ -284,6 +290,129 @@ def run_ours(args, world, rank, local):
     report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e_value, x)
 
 
+def run_ep(args, world, rank, local):
+    """Expert-parallel forward over `world` GPUs (one process each, NCCL).
+
+    Skewed workload: every rank holds B x L tokens of its own (input seed
+    3 + 1000*rank); all ranks share the weights (seed 3) whose router carries
+    the Zipf logit bias. Headline: "balanced" placement (hot experts' tiles
+    spread over ranks); also reported: the static ownership 7/7, 4/4/3/3,
+    2x6+1x2 ("static"). Per-stage times are CUDA events around each stage.
+    """
+    import torch.distributed as dist
+
+    import agillm41_b200
+    from agillm41_b200 import ep, ops, synthetic
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    N = args.tokens
+    bias = synthetic.zipf_logit_bias(EXPERTS, EP_SEED, s=ZIPF_S, scale=ZIPF_SCALE)
+    sd = synthetic.make_state(D, HIDDEN, EXPERTS, EP_SEED, dtype=torch.bfloat16, device=dev,
+                              router_logit_bias=bias)
+    x = synthetic.make_input(N, D, EP_SEED + 1000 * rank, dtype=torch.bfloat16, device=dev, pin_feature0=True)
+    w1 = torch.stack([sd[f"experts.{e}.0.weight"] for e in range(EXPERTS)]).contiguous()
+    b1 = torch.stack([sd[f"experts.{e}.0.bias"] for e in range(EXPERTS)]).contiguous()
+    w2 = torch.stack([sd[f"experts.{e}.2.weight"] for e in range(EXPERTS)]).contiguous()
+    b2 = torch.stack([sd[f"experts.{e}.2.bias"] for e in range(EXPERTS)]).contiguous()
+    wr = sd["router.weight"].contiguous()
+    stream = torch.cuda.current_stream(dev)
+    ref = ops.moe_forward(x, wr, w1, b1, w2, b2, TOP_K)    # single-GPU forward of this rank's tokens
+
+    results = {}
+    for placement in ("balanced", "static"):
+        mine = ep.ExpertParallelMoE.shard_weights(w1, b1, w2, b2, rank, world, placement)
+        moe = ep.ExpertParallelMoE((wr,) + tuple(mine), TOP_K, EXPERTS, placement=placement)
+        for _ in range(args.warmup):
+            out = moe.forward(x)
+        torch.cuda.synchronize()
+        same = bool(torch.equal(out, ref))
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(7)] for _ in range(args.steps)]
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier(world)
+        torch.cuda.synchronize()
+        with ClockSampler(dev) as clk:
+            start.record(stream)
+            for i in range(args.steps):
+                moe.forward(x, events=evs[i])
+            stop.record(stream)
+            torch.cuda.synchronize()
+        barrier(world)
+        ms = max_over_ranks(start.elapsed_time(stop), world)
+        st = {s_: 0.0 for s_ in EP_STAGES}
+        for e in evs:
+            for j, s_ in enumerate(EP_STAGES):
+                st[s_] += e[j].elapsed_time(e[j + 1])
+        st = {s_: max_over_ranks(v / args.steps, world) for s_, v in st.items()}
+        plan = moe.last_plan
+        work = torch.tensor([plan.recv_tile_expert.size], dtype=torch.float64, device=dev)
+        works = [torch.zeros_like(work) for _ in range(world)]
+        dist.all_gather(works, work)
+        works = [int(w.item()) for w in works]
+        ok = torch.tensor([1.0 if same else 0.0], device=dev)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        results[placement] = dict(value=N * world * args.steps / (ms / 1000.0), ms_per_step=ms / args.steps,
+                                  stages_ms={k_: round(v, 4) for k_, v in st.items()},
+                                  tiles_per_rank=works, max_over_mean_tiles=round(max(works) / (sum(works) / world), 3),
+                                  bit_identical_to_single_gpu=bool(ok.item() > 0), clocks=clk.summary())
+
+    # End to end through the public API with host buffers (copy in, forward, copy out).
+    moe = ep.ExpertParallelMoE((wr, w1, b1, w2, b2), TOP_K, EXPERTS, placement="balanced")
+    x_host = x.cpu().pin_memory()
+    y_host = torch.empty_like(x_host).pin_memory()
+    x_dev = torch.empty_like(x)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        y = moe.forward(x_dev)
+        y_host.copy_(y, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    if rank != 0:
+        return
+    peaks = load_peaks()
+    head = results["balanced"]
+    ffn_ms = head["stages_ms"]["expert_ffn"]
+    # Grouped GEMM roofline: FLOPs this rank's FC1+FC2 launches did (its tiles) / their time.
+    flop = 2 * 2 * TILE_ROWS * max(head["tiles_per_rank"]) * D * HIDDEN
+    achieved = flop / (ffn_ms / 1000.0) / 1e12
+    line = {
+        "metric": METRIC, "value": head["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) input, N(0,0.02^2) random-init expert weights, Zipf(1.2) router bias)",
+        "config": {"workload": f"expert-parallel MoE block forward, {N} tokens/rank d{D} E{EXPERTS} H{HIDDEN} "
+                               f"top{TOP_K} bf16, Zipf(1.2) logit bias x{ZIPF_SCALE} (seed {EP_SEED})",
+                   "global_batch": BATCH * world, "seq_len": SEQ, "tokens_per_gpu": N,
+                   "parallelism": f"expert parallel x{world} (NCCL all-to-all), balanced placement",
+                   "l2": "inputs larger than L2; no flush"},
+        "e2e": {"value": N * world * args.steps / (e2e_ms / 1000.0), "unit": UNIT,
+                "h2d_bytes_per_step": x_host.numel() * 2, "d2h_bytes_per_step": y_host.numel() * 2,
+                "api": "ExpertParallelMoE.forward with host copies"},
+        "gpu_launches": KERNELS_PER_STEP * args.steps,
+        "roofline": {"kernel": "grouped_gemm_tc_kernel (FC1+FC2, busiest rank)", "bound": "tensor",
+                     "achieved": round(achieved, 1), "peak": peaks["tf_sus"], "unit": "TFLOP/s",
+                     "frac": round(achieved / peaks["tf_sus"], 3),
+                     "peak_source": f"{peaks['src']} bf16 sustained", "traffic": None},
+        "placements": results,
+        "cpu_baseline": None,
+        "clocks": head["clocks"],
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_e2e(args, world, dev, sd, x, out, N, stream):
     """Same metric through the public module API on host buffers, copies timed.
 
@@ -404,7 +533,10 @@ def main():
         return
     world, rank, local = dist_setup(args.gpus)
     try:
-        run_ours(args, world, rank, local)
+        if world > 1:
+            run_ep(args, world, rank, local)
+        else:
+            run_ours(args, world, rank, local)
     finally:
         if world > 1:
             import torch.distributed as dist
