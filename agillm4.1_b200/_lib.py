@@ -45,6 +45,15 @@ SIGNATURES = {
     "agm_moe_host_workspace_bytes": (_SZ, [_I64, _I, _I, _I, _I, _I, _I, _I]),
     "agm_moe_forward_host": (_I, [_P, _I, _I64, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _P, _P, _P,
                                   _SZ, _I64, _I, _P]),
+    "agm_ep_comm_bytes": (_SZ, [_I, _I64, _I, _I]),
+    "agm_ep_alloc": (_I, [_SZ, _P]),
+    "agm_ep_free": (_I, [_P]),
+    "agm_ep_ipc_handle": (_I, [_P, _P]),
+    "agm_ep_ipc_open": (_I, [_P, _P]),
+    "agm_ep_ipc_close": (_I, [_P]),
+    "agm_ep_workspace_bytes": (_SZ, [_I64, _I, _I, _I, _I, _I64, _I]),
+    "agm_ep_forward": (_I, [_P, _I, _I64, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _I64,
+                            ctypes.c_uint64, _P, _P, _SZ, _I, _P]),
     "agm_moe_forward_noalloc": (_I, [_P, _I, _I64, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _P, _P,
                                      _I, _P]),
 }

@@ -136,8 +136,37 @@ __device__ __forceinline__ uint4 combine_chunk(const uint4 (&v)[K_MAX], const fl
   return store8<T>(acc);
 }
 
-template <typename T, int K_MAX>
-__global__ void __launch_bounds__(256) combine_kernel(const T* __restrict__ y_perm, const int32_t* __restrict__ row_of,
+// Source of the expert output row for permuted row p: the local y_perm.
+struct LocalY {
+  const uint4* base;
+  int nchunk;
+  __device__ __forceinline__ const uint4* row(int64_t p) const { return base + p * nchunk; }
+  __device__ __forceinline__ static uint4 load(const uint4* p) { return __ldg(p); }
+};
+
+// Expert-parallel source: the row lives in the result buffer of the rank that
+// computed it (read over NVLink for peers).
+struct EpY {
+  const EpRoute* route;
+  int nchunk;
+  __device__ __forceinline__ const uint4* row(int64_t p) const {
+    const int64_t t = p >> 7;
+    const int w = route->world;
+    for (int r = 0; r < w; ++r) {
+      const int64_t lo = route->send_tile_start[r], hi = route->send_tile_start[r + 1];
+      if (t >= lo && t < hi) {
+        const int64_t drow = (route->dest_tile_base[r] + (t - lo)) * 128 + (p & 127);
+        return reinterpret_cast<const uint4*>(route->peer_y[r]) + drow * nchunk;
+      }
+    }
+    return nullptr;
+  }
+  // Rows written by other GPUs: cache in L2 only (ld.global.cg).
+  __device__ __forceinline__ static uint4 load(const uint4* p) { return __ldcg(p); }
+};
+
+template <typename T, int K_MAX, class Src>
+__global__ void __launch_bounds__(256) combine_kernel(Src ysrc, const int32_t* __restrict__ row_of,
                                                       const T* __restrict__ gates, int64_t n_tokens, int d, int k,
                                                       const T* __restrict__ shared_y, int n_shared,
                                                       int64_t shared_stride, T* __restrict__ out) {
@@ -152,7 +181,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const T* __restrict__ y_pe
 #pragma unroll
     for (int r = 0; r < K_MAX; ++r) {
       if (r < k) {
-        src[r] = reinterpret_cast<const uint4*>(y_perm + static_cast<int64_t>(row_of[tok * k + r]) * d);
+        src[r] = ysrc.row(row_of[tok * k + r]);
         g[r] = Traits<T>::to_f(gates[tok * k + r]);
       } else {
         src[r] = nullptr;
@@ -171,7 +200,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const T* __restrict__ y_pe
         if (c < nchunk) {
 #pragma unroll
           for (int r = 0; r < K_MAX; ++r)
-            if (r < k) v[j][r] = __ldg(src[r] + c);
+            if (r < k) v[j][r] = Src::load(src[r] + c);
         }
       }
 #pragma unroll
@@ -187,34 +216,38 @@ __global__ void __launch_bounds__(256) combine_kernel(const T* __restrict__ y_pe
         uint4 v[K_MAX];
 #pragma unroll
         for (int r = 0; r < K_MAX; ++r)
-          if (r < k) v[r] = __ldg(src[r] + c);
+          if (r < k) v[r] = Src::load(src[r] + c);
         dst[c] = combine_chunk<T, K_MAX>(v, g, k, shared_y, n_shared, shared_stride, tok, d, c);
       }
     }
   }
 }
 
-template <typename T>
-static cudaError_t launch_combine(const void* y, const int32_t* row_of, const void* gates, int64_t n, int d, int k,
+template <typename T, class Src>
+static cudaError_t launch_combine(Src ysrc, const int32_t* row_of, const void* gates, int64_t n, int d, int k,
                                   const void* shared_y, int n_shared, int64_t shared_stride, void* out, int num_sms,
                                   cudaStream_t stream) {
-  const int64_t warps_needed = n;
-  const int64_t blocks = std::min<int64_t>((warps_needed + 7) / 8, static_cast<int64_t>(num_sms) * 8);
+  const int64_t blocks = std::min<int64_t>((n + 7) / 8, static_cast<int64_t>(num_sms) * 8);
   if (blocks <= 0) return cudaSuccess;
-  const T* ys = static_cast<const T*>(y);
   const T* gs = static_cast<const T*>(gates);
   const T* sh = static_cast<const T*>(shared_y);
   T* o = static_cast<T*>(out);
+  const unsigned g = static_cast<unsigned>(blocks);
   if (k <= 2)
-    combine_kernel<T, 2><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(ys, row_of, gs, n, d, k, sh, n_shared,
-                                                                            shared_stride, o);
+    combine_kernel<T, 2, Src><<<g, 256, 0, stream>>>(ysrc, row_of, gs, n, d, k, sh, n_shared, shared_stride, o);
   else if (k <= 4)
-    combine_kernel<T, 4><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(ys, row_of, gs, n, d, k, sh, n_shared,
-                                                                            shared_stride, o);
+    combine_kernel<T, 4, Src><<<g, 256, 0, stream>>>(ysrc, row_of, gs, n, d, k, sh, n_shared, shared_stride, o);
   else
-    combine_kernel<T, 16><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(ys, row_of, gs, n, d, k, sh, n_shared,
-                                                                             shared_stride, o);
+    combine_kernel<T, 16, Src><<<g, 256, 0, stream>>>(ysrc, row_of, gs, n, d, k, sh, n_shared, shared_stride, o);
   return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t combine_local(const void* y, const int32_t* row_of, const void* gates, int64_t n, int d, int k,
+                                 const void* shared_y, int n_shared, int64_t shared_stride, void* out, int num_sms,
+                                 cudaStream_t stream) {
+  LocalY src{static_cast<const uint4*>(y), static_cast<int>(d * sizeof(T) / 16)};
+  return launch_combine<T>(src, row_of, gates, n, d, k, shared_y, n_shared, shared_stride, out, num_sms, stream);
 }
 
 cudaError_t combine(int dtype, const void* y, const int32_t* row_of, const void* gates, int64_t n, int d, int k,
@@ -222,12 +255,29 @@ cudaError_t combine(int dtype, const void* y, const int32_t* row_of, const void*
                     cudaStream_t stream) {
   switch (dtype) {
     case AGM_F32:
-      return launch_combine<float>(y, row_of, gates, n, d, k, shared_y, n_shared, shared_stride, out, num_sms, stream);
+      return combine_local<float>(y, row_of, gates, n, d, k, shared_y, n_shared, shared_stride, out, num_sms, stream);
     case AGM_BF16:
-      return launch_combine<__nv_bfloat16>(y, row_of, gates, n, d, k, shared_y, n_shared, shared_stride, out, num_sms,
-                                           stream);
+      return combine_local<__nv_bfloat16>(y, row_of, gates, n, d, k, shared_y, n_shared, shared_stride, out, num_sms,
+                                          stream);
     case AGM_F16:
-      return launch_combine<__half>(y, row_of, gates, n, d, k, shared_y, n_shared, shared_stride, out, num_sms,
+      return combine_local<__half>(y, row_of, gates, n, d, k, shared_y, n_shared, shared_stride, out, num_sms,
+                                   stream);
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t combine_ep(int dtype, const EpRoute* route, const int32_t* row_of, const void* gates, int64_t n, int d,
+                       int k, void* out, int num_sms, cudaStream_t stream) {
+  switch (dtype) {
+    case AGM_F32:
+      return launch_combine<float>(EpY{route, d * 4 / 16}, row_of, gates, n, d, k, nullptr, 0, 0, out, num_sms,
+                                   stream);
+    case AGM_BF16:
+      return launch_combine<__nv_bfloat16>(EpY{route, d * 2 / 16}, row_of, gates, n, d, k, nullptr, 0, 0, out,
+                                           num_sms, stream);
+    case AGM_F16:
+      return launch_combine<__half>(EpY{route, d * 2 / 16}, row_of, gates, n, d, k, nullptr, 0, 0, out, num_sms,
                                     stream);
     default:
       return cudaErrorInvalidValue;

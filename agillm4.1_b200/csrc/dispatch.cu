@@ -85,21 +85,32 @@ __global__ void __launch_bounds__(kPlanThreads) dispatch_plan_kernel(
   }
 }
 
-template <int K_MAX>
+// Destination of permuted row p: the local x_perm buffer.
+struct LocalRows {
+  static constexpr bool kSystemFence = false;
+  uint4* base;
+  int nchunk;
+  __device__ __forceinline__ uint4* row(int64_t p) const { return base + p * nchunk; }
+};
+
+template <int K_MAX, class Dst>
 __global__ void __launch_bounds__(kBlk) permute_kernel(
     const uint4* __restrict__ x, int64_t n_tokens, int nchunk /* 16-byte chunks per row */, int k, int E,
     int n_blocks, const int32_t* __restrict__ idx, const int32_t* __restrict__ block_off,
-    const int32_t* __restrict__ seg_start, const int32_t* __restrict__ counts, int64_t max_rows,
-    uint4* __restrict__ x_perm, int32_t* __restrict__ row_of, int32_t* __restrict__ token_of, int* err) {
+    const int32_t* __restrict__ seg_start, const int32_t* __restrict__ counts, int64_t max_rows, Dst dst,
+    int32_t* __restrict__ row_of, int32_t* __restrict__ token_of, int* err) {
   const int warp = warp_id(), lane = lane_id();
   if (static_cast<int>(blockIdx.x) >= n_blocks) {
     // Zero-fill the padding rows of one expert segment.
     const int e = blockIdx.x - n_blocks;
     const int64_t r0 = seg_start[e] + counts[e];
     const int64_t r1 = min(static_cast<int64_t>(seg_start[e + 1]), max_rows);
-    const int64_t nvec = (r1 - r0) * nchunk;
-    uint4* base = x_perm + r0 * nchunk;
-    for (int64_t i = threadIdx.x; i < nvec; i += blockDim.x) base[i] = make_uint4(0, 0, 0, 0);
+    for (int64_t r = r0 + warp; r < r1; r += blockDim.x / 32) {
+      uint4* o = dst.row(r);
+      if (o)
+        for (int c = lane; c < nchunk; c += 32) o[c] = make_uint4(0, 0, 0, 0);
+    }
+    if constexpr (Dst::kSystemFence) __threadfence_system();
     return;
   }
   __shared__ uint32_t mask_s[kBlk / 32][32];
@@ -143,7 +154,7 @@ __global__ void __launch_bounds__(kBlk) permute_kernel(
       if (row >= 0 && row < max_rows) {
         dest[r] = static_cast<int>(row);
         row_of[tok * k + r] = static_cast<int32_t>(row);
-        token_of[row] = static_cast<int32_t>(tok);
+        if (token_of) token_of[row] = static_cast<int32_t>(tok);
       } else {
         raise_error(err, kErrRowOverflow);
       }
@@ -180,8 +191,8 @@ __global__ void __launch_bounds__(kBlk) permute_kernel(
 #pragma unroll
       for (int r = 0; r < K_MAX; ++r) {
         if (r >= k) break;
-        uint4* o0 = d0[r] >= 0 ? x_perm + static_cast<int64_t>(d0[r]) * nchunk : nullptr;
-        uint4* o1 = (has1 && d1[r] >= 0) ? x_perm + static_cast<int64_t>(d1[r]) * nchunk : nullptr;
+        uint4* o0 = d0[r] >= 0 ? dst.row(d0[r]) : nullptr;
+        uint4* o1 = (has1 && d1[r] >= 0) ? dst.row(d1[r]) : nullptr;
 #pragma unroll
         for (int j = 0; j < kMaxChunks; ++j) {
           const int c = lane + 32 * j;
@@ -203,10 +214,14 @@ __global__ void __launch_bounds__(kBlk) permute_kernel(
       for (int c = lane; c < nchunk; c += 32) {
         const uint4 v = __ldg(src + c);
         for (int r = 0; r < k && r < K_MAX; ++r)
-          if (drow[r] >= 0) x_perm[static_cast<int64_t>(drow[r]) * nchunk + c] = v;
+          if (drow[r] >= 0) {
+            uint4* o = dst.row(drow[r]);
+            if (o) o[c] = v;
+          }
       }
     }
   }
+  if constexpr (Dst::kSystemFence) __threadfence_system();
 }
 
 cudaError_t dispatch_plan(const int32_t* block_hist, int n_blocks, int E, int64_t max_rows, int max_tiles,
@@ -217,26 +232,43 @@ cudaError_t dispatch_plan(const int32_t* block_hist, int n_blocks, int E, int64_
   return cudaGetLastError();
 }
 
-cudaError_t permute_rows(const void* x, int elem_bytes, int64_t n_tokens, int d, int k, int E, const int32_t* idx,
-                         const int32_t* block_off, const int32_t* seg_start, const int32_t* counts, int64_t max_rows,
-                         void* x_perm, int32_t* row_of, int32_t* token_of, int* err, cudaStream_t stream) {
+template <class Dst>
+static cudaError_t launch_permute(const void* x, int elem_bytes, int64_t n_tokens, int d, int k, int E,
+                                  const int32_t* idx, const int32_t* block_off, const int32_t* seg_start,
+                                  const int32_t* counts, int64_t max_rows, Dst dst, int32_t* row_of,
+                                  int32_t* token_of, int* err, cudaStream_t stream) {
   const int n_blocks = static_cast<int>((n_tokens + kBlk - 1) / kBlk);
   const int nchunk = d * elem_bytes / 16;
   const unsigned grid = static_cast<unsigned>(n_blocks + E);
-  if (grid == 0) return cudaSuccess;
+  if (n_tokens <= 0) return cudaSuccess;
   const uint4* xs = static_cast<const uint4*>(x);
-  uint4* xp = static_cast<uint4*>(x_perm);
   if (k <= 2) {
-    permute_kernel<2><<<grid, kBlk, 0, stream>>>(xs, n_tokens, nchunk, k, E, n_blocks, idx, block_off, seg_start,
-                                                 counts, max_rows, xp, row_of, token_of, err);
+    permute_kernel<2, Dst><<<grid, kBlk, 0, stream>>>(xs, n_tokens, nchunk, k, E, n_blocks, idx, block_off,
+                                                      seg_start, counts, max_rows, dst, row_of, token_of, err);
   } else if (k <= 4) {
-    permute_kernel<4><<<grid, kBlk, 0, stream>>>(xs, n_tokens, nchunk, k, E, n_blocks, idx, block_off, seg_start,
-                                                 counts, max_rows, xp, row_of, token_of, err);
+    permute_kernel<4, Dst><<<grid, kBlk, 0, stream>>>(xs, n_tokens, nchunk, k, E, n_blocks, idx, block_off,
+                                                      seg_start, counts, max_rows, dst, row_of, token_of, err);
   } else {
-    permute_kernel<16><<<grid, kBlk, 0, stream>>>(xs, n_tokens, nchunk, k, E, n_blocks, idx, block_off, seg_start,
-                                                  counts, max_rows, xp, row_of, token_of, err);
+    permute_kernel<16, Dst><<<grid, kBlk, 0, stream>>>(xs, n_tokens, nchunk, k, E, n_blocks, idx, block_off,
+                                                       seg_start, counts, max_rows, dst, row_of, token_of, err);
   }
   return cudaGetLastError();
+}
+
+cudaError_t permute_rows(const void* x, int elem_bytes, int64_t n_tokens, int d, int k, int E, const int32_t* idx,
+                         const int32_t* block_off, const int32_t* seg_start, const int32_t* counts, int64_t max_rows,
+                         void* x_perm, int32_t* row_of, int32_t* token_of, int* err, cudaStream_t stream) {
+  LocalRows dst{static_cast<uint4*>(x_perm), d * elem_bytes / 16};
+  return launch_permute(x, elem_bytes, n_tokens, d, k, E, idx, block_off, seg_start, counts, max_rows, dst, row_of,
+                        token_of, err, stream);
+}
+
+cudaError_t permute_rows_ep(const void* x, int elem_bytes, int64_t n_tokens, int d, int k, int E, const int32_t* idx,
+                            const int32_t* block_off, const int32_t* seg_start, const int32_t* counts,
+                            int64_t max_rows, const EpRoute* route, int32_t* row_of, int* err, cudaStream_t stream) {
+  EpRows dst{route, d * elem_bytes / 16};
+  return launch_permute(x, elem_bytes, n_tokens, d, k, E, idx, block_off, seg_start, counts, max_rows, dst, row_of,
+                        nullptr, err, stream);
 }
 
 }  // namespace agm

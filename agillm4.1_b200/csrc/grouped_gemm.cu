@@ -281,7 +281,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_before();
       mbar_arrive(&acc_empty[acc]);
     }
-    if (lane == 0) bulk_wait_group0();
+    if (lane == 0) {
+      bulk_wait_group0();
+      // The output may be read by other GPUs after a flag barrier: make the
+      // async-proxy stores visible to generic and system-scope readers.
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+      __threadfence_system();
+    }
     __syncwarp();
   }
 

@@ -25,6 +25,41 @@ struct GemmArgs {
   int* err;
 };
 
+// Expert-parallel routing of one rank's permuted rows (see ep_p2p.cu). The
+// rank's x_perm tiles [send_tile_start[r], send_tile_start[r+1]) go to rank r,
+// landing at tile dest_tile_base[r] of r's receive buffer; peer_recv/peer_y
+// are the device addresses of every rank's receive and result buffers as
+// mapped into this process.
+constexpr int kEpMaxRanks = 16;
+struct EpRoute {
+  int world;
+  int rank;
+  int64_t send_tile_start[kEpMaxRanks + 1];
+  int64_t dest_tile_base[kEpMaxRanks];
+  uint64_t peer_recv[kEpMaxRanks];
+  uint64_t peer_y[kEpMaxRanks];
+};
+
+// Destination row of permuted row p on its receiving rank (nullptr if p is
+// not sent). Rows are 16-byte chunked (nchunk chunks per row).
+struct EpRows {
+  static constexpr bool kSystemFence = true;  // rows land in other GPUs' memory
+  const EpRoute* route;
+  int nchunk;
+  __device__ __forceinline__ uint4* row(int64_t p) const {
+    const int64_t t = p >> 7;
+    const int w = route->world;
+    for (int r = 0; r < w; ++r) {
+      const int64_t lo = route->send_tile_start[r], hi = route->send_tile_start[r + 1];
+      if (t >= lo && t < hi) {
+        const int64_t drow = (route->dest_tile_base[r] + (t - lo)) * 128 + (p & 127);
+        return reinterpret_cast<uint4*>(route->peer_recv[r]) + drow * nchunk;
+      }
+    }
+    return nullptr;
+  }
+};
+
 // Tiled TMA descriptor (128-byte swizzle, zero OOB fill) for a row-major
 // tensor of rank 2 or 3; dims and box innermost first, strides in bytes.
 bool encode_tmap(CUtensorMap* m, const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
@@ -46,6 +81,11 @@ cudaError_t dispatch_plan(const int32_t* block_hist, int n_blocks, int E, int64_
 cudaError_t permute_rows(const void* x, int elem_bytes, int64_t n_tokens, int d, int k, int E, const int32_t* idx,
                          const int32_t* block_off, const int32_t* seg_start, const int32_t* counts, int64_t max_rows,
                          void* x_perm, int32_t* row_of, int32_t* token_of, int* err, cudaStream_t stream);
+cudaError_t permute_rows_ep(const void* x, int elem_bytes, int64_t n_tokens, int d, int k, int E, const int32_t* idx,
+                            const int32_t* block_off, const int32_t* seg_start, const int32_t* counts,
+                            int64_t max_rows, const EpRoute* route, int32_t* row_of, int* err, cudaStream_t stream);
+cudaError_t combine_ep(int dtype, const EpRoute* route, const int32_t* row_of, const void* gates, int64_t n, int d,
+                       int k, void* out, int num_sms, cudaStream_t stream);
 cudaError_t grouped_gemm(int dtype, const void* a, int64_t a_rows, const void* w, const GemmArgs& args, bool relu,
                          int num_sms, cudaStream_t stream, int force_bn);
 cudaError_t combine(int dtype, const void* y, const int32_t* row_of, const void* gates, int64_t n, int d, int k,

@@ -199,3 +199,111 @@ class ExpertParallelMoE:
         out = self.ops.combine(y_perm, row_of, gates)
         mark(6)
         return out
+
+
+class P2PExpertParallelMoE:
+    """Expert-parallel forward with the all-to-all fused into the kernels.
+
+    Every rank allocates one communication buffer (receive rows, result rows,
+    signal flags, counts inbox) and maps every peer's buffer through CUDA IPC.
+    ``forward`` then runs entirely on the current stream with no host sync:
+    the permute kernel writes each row straight into the receive buffer of
+    the rank that computes it (NVLink stores), three flag barriers in peer
+    memory order the phases, and the combine kernel reads the expert outputs
+    straight from the ranks that computed them (NVLink loads). See the C ABI
+    ``agm_ep_forward``. All ranks must call ``forward`` the same number of
+    times (every call is a collective).
+    """
+
+    def __init__(self, weights: Sequence[torch.Tensor], top_k: int, n_experts: int, max_tokens: int, group=None,
+                 placement: str = "balanced", cap_rows: Optional[int] = None):
+        import ctypes
+
+        from . import _lib, ops
+
+        self._lib = _lib
+        self._ops = ops
+        self.lib = _lib.load()
+        self.w_router, self.w1, self.b1, self.w2, self.b2 = weights
+        self.top_k, self.E = int(top_k), int(n_experts)
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.placement = placement
+        self.pl_code = {"static": 0, "balanced": 1}[placement]
+        if placement == "static":
+            r = static_owner_ranges(self.E, self.world)[self.rank]
+            self.first_local, self.n_local = r.start, len(r)
+        else:
+            self.first_local, self.n_local = 0, self.E
+        if self.w1.shape[0] != self.n_local:
+            raise ValueError(f"rank holds {self.w1.shape[0]} experts, placement {placement} needs {self.n_local}")
+        self.device = self.w1.device
+        self.d = int(self.w_router.shape[1])
+        self.H = int(self.w1.shape[1])
+        self.dtype = self.w1.dtype
+        self.max_tokens = int(max_tokens)
+        rows = ops.max_rows(self.max_tokens, self.top_k, self.E)
+        if cap_rows is None:
+            cap_rows = 2 * rows if placement == "balanced" else self.world * rows
+        self.cap_rows = (int(cap_rows) + TILE - 1) // TILE * TILE
+        code = _lib.dtype_code(self.dtype)
+        nbytes = int(self.lib.agm_ep_comm_bytes(self.E, self.cap_rows, self.d, code))
+        ptr = ctypes.c_void_p()
+        _lib.check(self.lib.agm_ep_alloc(nbytes, ctypes.byref(ptr)), "agm_ep_alloc")
+        self.own = ptr.value
+        handle = (ctypes.c_uint8 * 64)()
+        _lib.check(self.lib.agm_ep_ipc_handle(self.own, handle), "agm_ep_ipc_handle")
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.opened = []
+        ptrs = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                ptrs.append(self.own)
+                continue
+            hb = (ctypes.c_uint8 * 64).from_buffer_copy(h)
+            pp = ctypes.c_void_p()
+            _lib.check(self.lib.agm_ep_ipc_open(hb, ctypes.byref(pp)), "agm_ep_ipc_open")
+            self.opened.append(pp.value)
+            ptrs.append(pp.value)
+        self.peer_comm = (ctypes.c_uint64 * self.world)(*ptrs)
+        self.ws = torch.empty(int(self.lib.agm_ep_workspace_bytes(self.max_tokens, self.d, self.E, self.top_k,
+                                                                   self.H, self.cap_rows, code)),
+                              dtype=torch.uint8, device=self.device)
+        self.epoch = 1
+        dist.barrier(group=group)
+
+    def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        import ctypes
+
+        n = x.shape[0]
+        if n > self.max_tokens:
+            raise ValueError(f"{n} tokens > max_tokens={self.max_tokens}")
+        out = torch.empty_like(x) if out is None else out
+        _lib, ops = self._lib, self._ops
+        rc = self.lib.agm_ep_forward(
+            _lib.ptr(x), _lib.dtype_code(x.dtype), n, self.d, self.E, self.top_k, self.H, _lib.ptr(self.w_router),
+            _lib.ptr(self.w1), _lib.ptr(self.b1), _lib.ptr(self.w2), _lib.ptr(self.b2), self.n_local,
+            self.first_local, self.pl_code, self.world, self.rank, ctypes.addressof(self.peer_comm), self.cap_rows,
+            self.epoch, _lib.ptr(out), _lib.ptr(self.ws), self.ws.numel(), 0,
+            _lib.stream_handle(x.device))
+        _lib.check(rc, "agm_ep_forward")
+        self.epoch += 3
+        return out
+
+    def device_error(self) -> int:
+        return self._lib.read_device_error(self.ws[:4].view(torch.int32))
+
+    def close(self) -> None:
+        """Collective: unmap the peers' buffers and free this rank's buffer."""
+        if self.own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for p in self.opened:
+            self.lib.agm_ep_ipc_close(p)
+        self.opened = []
+        dist.barrier(group=self.group)
+        self.lib.agm_ep_free(self.own)
+        self.own = None

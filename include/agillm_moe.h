@@ -188,6 +188,46 @@ AGM_API int agm_moe_forward_host(const void* x_host, int dtype, int64_t n_tokens
                                  const void* ws2, const void* sb2, void* out_host, void* workspace,
                                  size_t workspace_bytes, int64_t chunk_tokens, int flags, void* stream);
 
+/* ---- Expert parallelism across the GPUs of one node (NVLink peer memory) ----
+ * The reference runs MoEFFN.forward (agillm41.py:4389-4431) on one device; the
+ * entry points below spread its expert FFN work over P ranks (one process per
+ * GPU) and move rows inside the kernels instead of through a collective.
+ * Each rank allocates one communication buffer (agm_ep_alloc, IPC-shareable),
+ * shares its handle (agm_ep_ipc_handle) with the other ranks, which map it
+ * (agm_ep_ipc_open); every rank then calls agm_ep_forward with the same
+ * sequence of epochs (1, 4, 7, ...: each call uses epoch, epoch+1, epoch+2). */
+
+/* Bytes of one rank's communication buffer: signals, counts inbox, receive
+ * rows and result rows for up to cap_rows rows of d features. */
+AGM_API size_t agm_ep_comm_bytes(int n_experts, int64_t cap_rows, int d, int dtype);
+/* cudaMalloc a communication buffer (signals and inbox zeroed). */
+AGM_API int agm_ep_alloc(size_t bytes, void** ptr);
+AGM_API int agm_ep_free(void* ptr);
+/* 64-byte CUDA IPC handle of a buffer from agm_ep_alloc. */
+AGM_API int agm_ep_ipc_handle(void* ptr, void* handle_out);
+/* Map a peer's buffer into this process (device pointer) / unmap it. */
+AGM_API int agm_ep_ipc_open(const void* handle, void** peer_ptr);
+AGM_API int agm_ep_ipc_close(void* peer_ptr);
+/* Local (non-shared) device workspace of agm_ep_forward. */
+AGM_API size_t agm_ep_workspace_bytes(int64_t n_tokens, int d, int n_experts, int top_k, int hidden, int64_t cap_rows,
+                                      int dtype);
+/* Expert-parallel MoEFFN.forward of this rank's tokens x [n, d] -> out [n, d].
+ * w_router [E, d] (all experts); w1/b1/w2/b2 hold n_local_experts experts
+ * starting at first_local_expert. placement 0 = static contiguous ownership
+ * (first E mod P ranks own one more expert), 1 = balanced (every rank holds
+ * all experts; the global tile sequence is split evenly, hot experts span
+ * ranks). peer_comm: HOST array of `world` device addresses of every rank's
+ * communication buffer as mapped here (own buffer at [rank]). The counts
+ * exchange and three barriers are flag writes in peer memory, bounded waits
+ * (a time-out sets the device error word, the first int of the workspace).
+ * No host synchronisation; outputs are bit-identical to agm_moe_forward on
+ * the same tokens.                                                           */
+AGM_API int agm_ep_forward(const void* x, int dtype, int64_t n_tokens, int d, int n_experts, int top_k, int hidden,
+                           const void* w_router, const void* w1, const void* b1, const void* w2, const void* b2,
+                           int n_local_experts, int first_local_expert, int placement, int world, int rank,
+                           const uint64_t* peer_comm, int64_t cap_rows, uint64_t epoch, void* out, void* workspace,
+                           size_t workspace_bytes, int flags, void* stream);
+
 /* Synchronise `stream`, read the device error word at `err` (e.g. the first
  * int of a forward workspace) into *code and reset it to 0. Returns AGM_OK if
  * the word was 0, AGM_ERR_DEVICE otherwise.                                */

@@ -50,6 +50,14 @@ def _worker(rank, world, port, q):
             out2 = moe.forward(x)
             torch.cuda.synchronize()
             res[placement] = (bool(torch.equal(out, ref)), bool(torch.equal(out, out2)))
+        for placement in ("static", "balanced"):
+            mine = ep.ExpertParallelMoE.shard_weights(*w, rank, world, placement)
+            moe = ep.P2PExpertParallelMoE((wr,) + tuple(mine), k, E, max_tokens=4000, placement=placement)
+            outs = [moe.forward(x).clone() for _ in range(3)]
+            torch.cuda.synchronize()
+            err = moe.device_error()
+            res["p2p_" + placement] = (all(bool(torch.equal(o, ref)) for o in outs), err == 0)
+            moe.close()
         q.put((rank, res))
     finally:
         dist.destroy_process_group()
@@ -71,6 +79,38 @@ def test_ep_two_gpus_bit_identical():
         assert p.exitcode == 0
     for _ in range(2):
         rank, res = q.get(timeout=5)
-        for placement, (same_as_single, deterministic) in res.items():
+        for placement, (same_as_single, ok) in res.items():
             assert same_as_single, f"rank {rank} {placement}: differs from the single-GPU forward"
-            assert deterministic
+            assert ok, f"rank {rank} {placement}: not deterministic or device error"
+
+
+def test_p2p_path_single_rank():
+    """The peer-memory expert-parallel path with one rank (no peers): device
+    plan, row mapping, flag barriers and the mapped combine on one GPU."""
+    import datetime
+
+    import torch.distributed as dist
+
+    from agillm41_b200 import ep, ops, synthetic
+
+    dev = torch.device("cuda", 0)
+    store = dist.HashStore()
+    dist.init_process_group("gloo", store=store, rank=0, world_size=1, timeout=datetime.timedelta(seconds=60))
+    try:
+        d, H, E, k = 1280, 3200, 14, 2
+        sd = synthetic.make_state(d, H, E, 9, dtype=torch.bfloat16, device=dev, bias_std=0.02)
+        w = [torch.stack([sd[f"experts.{e}.{i}.{p}"] for e in range(E)]).contiguous()
+             for i, p in ((0, "weight"), (0, "bias"), (2, "weight"), (2, "bias"))]
+        wr = sd["router.weight"].contiguous()
+        for placement in ("static", "balanced"):
+            moe = ep.P2PExpertParallelMoE((wr,) + tuple(w), k, E, max_tokens=5000, placement=placement)
+            for n in (4096, 1, 777, 5000):
+                x = synthetic.make_input(n, d, n, dtype=torch.bfloat16, device=dev)
+                out = moe.forward(x)
+                ref = ops.moe_forward(x, wr, *w, k)
+                torch.cuda.synchronize()
+                assert torch.equal(out, ref), (placement, n)
+            assert moe.device_error() == 0
+            moe.close()
+    finally:
+        dist.destroy_process_group()
