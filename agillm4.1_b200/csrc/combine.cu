@@ -155,6 +155,7 @@ struct EpY {
     for (int r = 0; r < w; ++r) {
       const int64_t lo = route->send_tile_start[r], hi = route->send_tile_start[r + 1];
       if (t >= lo && t < hi) {
+        if (t - lo >= route->send_limit[r]) return nullptr;
         const int64_t drow = (route->dest_tile_base[r] + (t - lo)) * 128 + (p & 127);
         return reinterpret_cast<const uint4*>(route->peer_y[r]) + drow * nchunk;
       }
@@ -200,7 +201,7 @@ __global__ void __launch_bounds__(256) combine_kernel(Src ysrc, const int32_t* _
         if (c < nchunk) {
 #pragma unroll
           for (int r = 0; r < K_MAX; ++r)
-            if (r < k) v[j][r] = Src::load(src[r] + c);
+            if (r < k) v[j][r] = src[r] ? Src::load(src[r] + c) : make_uint4(0, 0, 0, 0);
         }
       }
 #pragma unroll
@@ -216,7 +217,7 @@ __global__ void __launch_bounds__(256) combine_kernel(Src ysrc, const int32_t* _
         uint4 v[K_MAX];
 #pragma unroll
         for (int r = 0; r < K_MAX; ++r)
-          if (r < k) v[r] = Src::load(src[r] + c);
+          if (r < k) v[r] = src[r] ? Src::load(src[r] + c) : make_uint4(0, 0, 0, 0);
         dst[c] = combine_chunk<T, K_MAX>(v, g, k, shared_y, n_shared, shared_stride, tok, d, c);
       }
     }

@@ -155,6 +155,8 @@ __global__ void ep_plan_kernel(PeerComm pc, int world, int rank, int E, int plac
           if (i < rank) base_in_r += ov;
         }
       route->dest_tile_base[r] = base_in_r;
+      // Never write past rank r's receive buffer (its own plan flags the overflow).
+      route->send_limit[r] = max(static_cast<int64_t>(0), cap_rows / 128 - base_in_r);
       route->peer_recv[r] = pc.base[r] + ep_off_recv(E);
       route->peer_y[r] = pc.base[r] + ep_off_y(E, cap_rows, d, eb);
     }

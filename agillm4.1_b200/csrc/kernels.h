@@ -36,6 +36,7 @@ struct EpRoute {
   int rank;
   int64_t send_tile_start[kEpMaxRanks + 1];
   int64_t dest_tile_base[kEpMaxRanks];
+  int64_t send_limit[kEpMaxRanks];  // tiles that fit in rank r's receive buffer from this rank
   uint64_t peer_recv[kEpMaxRanks];
   uint64_t peer_y[kEpMaxRanks];
 };
@@ -52,6 +53,7 @@ struct EpRows {
     for (int r = 0; r < w; ++r) {
       const int64_t lo = route->send_tile_start[r], hi = route->send_tile_start[r + 1];
       if (t >= lo && t < hi) {
+        if (t - lo >= route->send_limit[r]) return nullptr;  // would overflow rank r's buffer
         const int64_t drow = (route->dest_tile_base[r] + (t - lo)) * 128 + (p & 127);
         return reinterpret_cast<uint4*>(route->peer_recv[r]) + drow * nchunk;
       }
