@@ -291,13 +291,15 @@ def run_ours(args, world, rank, local):
 
 
 def run_ep(args, world, rank, local):
-    """Expert-parallel forward over `world` GPUs (one process each, NCCL).
+    """Expert-parallel forward over `world` GPUs (one process each).
 
     Skewed workload: every rank holds B x L tokens of its own (input seed
     3 + 1000*rank); all ranks share the weights (seed 3) whose router carries
-    the Zipf logit bias. Headline: "balanced" placement (hot experts' tiles
-    spread over ranks); also reported: the static ownership 7/7, 4/4/3/3,
-    2x6+1x2 ("static"). Per-stage times are CUDA events around each stage.
+    the Zipf logit bias. Headline: rows moved inside the permute/combine
+    kernels over NVLink peer memory ("p2p"), "balanced" placement (hot
+    experts' tiles spread over ranks). Also reported: the static ownership
+    7/7, 4/4/3/3, 2x6+1x2, and both placements with NCCL all-to-all between
+    the kernels (per-stage CUDA-event times for those).
     """
     import torch.distributed as dist
 
@@ -320,44 +322,62 @@ def run_ep(args, world, rank, local):
     ref = ops.moe_forward(x, wr, w1, b1, w2, b2, TOP_K)    # single-GPU forward of this rank's tokens
 
     results = {}
-    for placement in ("balanced", "static"):
+    # Tiles each rank computes (from the same global plan every variant uses).
+    counts = torch.bincount(ops.moe_forward(x, wr, w1, b1, w2, b2, TOP_K, want=("idx",))[1]["idx"].flatten().long(),
+                            minlength=EXPERTS).to(torch.int32)
+    counts_all = torch.empty(world * EXPERTS, dtype=torch.int32, device=dev)
+    dist.all_gather_into_tensor(counts_all, counts)
+    counts_all = counts_all.cpu().numpy().reshape(world, EXPERTS)
+    for variant in ("p2p_balanced", "p2p_static", "nccl_balanced", "nccl_static"):
+        kind, placement = variant.split("_")
         mine = ep.ExpertParallelMoE.shard_weights(w1, b1, w2, b2, rank, world, placement)
-        moe = ep.ExpertParallelMoE((wr,) + tuple(mine), TOP_K, EXPERTS, placement=placement)
+        if kind == "p2p":
+            moe = ep.P2PExpertParallelMoE((wr,) + tuple(mine), TOP_K, EXPERTS, max_tokens=N, placement=placement)
+            fwd = moe.forward
+        else:
+            moe = ep.ExpertParallelMoE((wr,) + tuple(mine), TOP_K, EXPERTS, placement=placement)
+            fwd = moe.forward
         for _ in range(args.warmup):
-            out = moe.forward(x)
+            out = fwd(x)
         torch.cuda.synchronize()
         same = bool(torch.equal(out, ref))
-        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(7)] for _ in range(args.steps)]
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(7)] for _ in range(args.steps)] \
+            if kind == "nccl" else None
         start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         barrier(world)
         torch.cuda.synchronize()
         with ClockSampler(dev) as clk:
             start.record(stream)
             for i in range(args.steps):
-                moe.forward(x, events=evs[i])
+                if evs is not None:
+                    moe.forward(x, events=evs[i])
+                else:
+                    fwd(x)
             stop.record(stream)
             torch.cuda.synchronize()
         barrier(world)
         ms = max_over_ranks(start.elapsed_time(stop), world)
-        st = {s_: 0.0 for s_ in EP_STAGES}
-        for e in evs:
-            for j, s_ in enumerate(EP_STAGES):
-                st[s_] += e[j].elapsed_time(e[j + 1])
-        st = {s_: max_over_ranks(v / args.steps, world) for s_, v in st.items()}
-        plan = moe.last_plan
-        work = torch.tensor([plan.recv_tile_expert.size], dtype=torch.float64, device=dev)
-        works = [torch.zeros_like(work) for _ in range(world)]
-        dist.all_gather(works, work)
-        works = [int(w.item()) for w in works]
+        st = None
+        if evs is not None:
+            st = {s_: 0.0 for s_ in EP_STAGES}
+            for e in evs:
+                for j, s_ in enumerate(EP_STAGES):
+                    st[s_] += e[j].elapsed_time(e[j + 1])
+            st = {s_: round(max_over_ranks(v / args.steps, world), 4) for s_, v in st.items()}
+        if kind == "p2p":
+            err = moe.device_error()
+            same = same and err == 0
+            moe.close()
+        works = [ep.plan_dispatch(counts_all, r, placement).recv_tile_expert.size for r in range(world)]
         ok = torch.tensor([1.0 if same else 0.0], device=dev)
         dist.all_reduce(ok, op=dist.ReduceOp.MIN)
-        results[placement] = dict(value=N * world * args.steps / (ms / 1000.0), ms_per_step=ms / args.steps,
-                                  stages_ms={k_: round(v, 4) for k_, v in st.items()},
-                                  tiles_per_rank=works, max_over_mean_tiles=round(max(works) / (sum(works) / world), 3),
-                                  bit_identical_to_single_gpu=bool(ok.item() > 0), clocks=clk.summary())
+        results[variant] = dict(value=N * world * args.steps / (ms / 1000.0), ms_per_step=ms / args.steps,
+                                stages_ms=st, tiles_per_rank=works,
+                                max_over_mean_tiles=round(max(works) / (sum(works) / world), 3),
+                                bit_identical_to_single_gpu=bool(ok.item() > 0), clocks=clk.summary())
 
     # End to end through the public API with host buffers (copy in, forward, copy out).
-    moe = ep.ExpertParallelMoE((wr, w1, b1, w2, b2), TOP_K, EXPERTS, placement="balanced")
+    moe = ep.P2PExpertParallelMoE((wr, w1, b1, w2, b2), TOP_K, EXPERTS, max_tokens=N, placement="balanced")
     x_host = x.cpu().pin_memory()
     y_host = torch.empty_like(x_host).pin_memory()
     x_dev = torch.empty_like(x)
@@ -380,12 +400,13 @@ def run_ep(args, world, rank, local):
     torch.cuda.synchronize()
     barrier(world)
     e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    moe.close()
     if rank != 0:
         return
     peaks = load_peaks()
-    head = results["balanced"]
-    ffn_ms = head["stages_ms"]["expert_ffn"]
-    # Grouped GEMM roofline: FLOPs this rank's FC1+FC2 launches did (its tiles) / their time.
+    head = results["p2p_balanced"]
+    ffn_ms = results["nccl_balanced"]["stages_ms"]["expert_ffn"]
+    # Grouped GEMM roofline: FLOPs of the busiest rank's FC1+FC2 launches / their event-timed duration.
     flop = 2 * 2 * TILE_ROWS * max(head["tiles_per_rank"]) * D * HIDDEN
     achieved = flop / (ffn_ms / 1000.0) / 1e12
     line = {
@@ -396,11 +417,12 @@ def run_ep(args, world, rank, local):
         "config": {"workload": f"expert-parallel MoE block forward, {N} tokens/rank d{D} E{EXPERTS} H{HIDDEN} "
                                f"top{TOP_K} bf16, Zipf(1.2) logit bias x{ZIPF_SCALE} (seed {EP_SEED})",
                    "global_batch": BATCH * world, "seq_len": SEQ, "tokens_per_gpu": N,
-                   "parallelism": f"expert parallel x{world} (NCCL all-to-all), balanced placement",
+                   "parallelism": f"expert parallel x{world}: rows moved by the permute/combine kernels over "
+                                  f"NVLink peer memory, balanced placement",
                    "l2": "inputs larger than L2; no flush"},
         "e2e": {"value": N * world * args.steps / (e2e_ms / 1000.0), "unit": UNIT,
                 "h2d_bytes_per_step": x_host.numel() * 2, "d2h_bytes_per_step": y_host.numel() * 2,
-                "api": "ExpertParallelMoE.forward with host copies"},
+                "api": "P2PExpertParallelMoE.forward with host copies"},
         "gpu_launches": KERNELS_PER_STEP * args.steps,
         "roofline": {"kernel": "grouped_gemm_tc_kernel (FC1+FC2, busiest rank)", "bound": "tensor",
                      "achieved": round(achieved, 1), "peak": peaks["tf_sus"], "unit": "TFLOP/s",
