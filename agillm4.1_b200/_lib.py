@@ -23,6 +23,7 @@ AGM_MAX_EXPERTS = 16
 AGM_FLAG_TIE_LOW_FIRST = 0x1
 AGM_FLAG_KEEP_ERROR = 0x2
 AGM_STAGE_EVENTS = 8
+AGM_EP_STAGE_EVENTS = 9
 
 _DTYPE_CODE = {torch.float32: AGM_F32, torch.bfloat16: AGM_BF16, torch.float16: AGM_F16}
 
@@ -53,7 +54,7 @@ SIGNATURES = {
     "agm_ep_ipc_close": (_I, [_P]),
     "agm_ep_workspace_bytes": (_SZ, [_I64, _I, _I, _I, _I, _I64, _I]),
     "agm_ep_forward": (_I, [_P, _I, _I64, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _I64,
-                            ctypes.c_uint64, _P, _P, _SZ, _I, _P]),
+                            ctypes.c_uint64, _P, _P, _SZ, _I, _P, _P]),
     "agm_moe_forward_noalloc": (_I, [_P, _I, _I64, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _P, _P,
                                      _I, _P]),
 }

@@ -320,7 +320,7 @@ AGM_API int agm_ep_forward(const void* x, int dtype, int64_t n_tokens, int d, in
                            const void* w_router, const void* w1, const void* b1, const void* w2, const void* b2,
                            int n_local_experts, int first_local_expert, int placement, int world, int rank,
                            const uint64_t* peer_comm, int64_t cap_rows, uint64_t epoch, void* out, void* workspace,
-                           size_t workspace_bytes, int flags, void* stream_) {
+                           size_t workspace_bytes, int flags, void* const* stage_events, void* stream_) {
   const int eb = eb_of(dtype);
   if (!eb) return ep_fail(AGM_ERR_ARG, "agm_ep_forward: bad dtype");
   if (world < 1 || world > agm::kEpMaxRanks || rank < 0 || rank >= world)
@@ -340,8 +340,12 @@ AGM_API int agm_ep_forward(const void* x, int dtype, int64_t n_tokens, int d, in
   for (int r = 0; r < agm::kEpMaxRanks; ++r) pc.base[r] = r < world ? peer_comm[r] : 0;
   const int sms = num_sms_dev();
   const int64_t rows = agm_max_rows(n_tokens, top_k, n_experts);
+  auto mark = [&](int i) -> cudaError_t {
+    return stage_events ? cudaEventRecord(static_cast<cudaEvent_t>(stage_events[i]), stream) : cudaSuccess;
+  };
   cudaError_t e = cudaMemsetAsync(L.err, 0, sizeof(int), stream);
   if (e != cudaSuccess) return ep_cuda(e, "memset");
+  if ((e = mark(0)) != cudaSuccess) return ep_cuda(e, "event");
   e = cudaMemsetAsync(L.counts, 0, sizeof(int32_t) * n_experts, stream);
   if (e != cudaSuccess) return ep_cuda(e, "memset");
   if (n_tokens > 0) {
@@ -353,19 +357,23 @@ AGM_API int agm_ep_forward(const void* x, int dtype, int64_t n_tokens, int d, in
                            L.num_tiles_local, L.token_of, L.err, stream);
     if (e != cudaSuccess) return ep_cuda(e, "dispatch_plan");
   }
+  if ((e = mark(1)) != cudaSuccess) return ep_cuda(e, "event");
   agm::ep_counts_exchange_kernel<<<1, 256, 0, stream>>>(pc, world, rank, n_experts, L.counts, epoch, L.err);
   if ((e = cudaGetLastError()) != cudaSuccess) return ep_cuda(e, "counts exchange");
   agm::ep_plan_kernel<<<1, 512, 0, stream>>>(pc, world, rank, n_experts, placement, first_local_expert,
                                              n_local_experts, cap_rows, d, eb, L.route, L.recv_tile_expert,
                                              L.recv_num_tiles, L.err);
   if ((e = cudaGetLastError()) != cudaSuccess) return ep_cuda(e, "ep plan");
+  if ((e = mark(2)) != cudaSuccess) return ep_cuda(e, "event");
   if (n_tokens > 0) {
     e = agm::permute_rows_ep(x, eb, n_tokens, d, top_k, n_experts, L.idx, L.block_off, L.seg_start, L.counts, rows,
                              L.route, L.row_of, L.err, stream);
     if (e != cudaSuccess) return ep_cuda(e, "dispatch");
   }
+  if ((e = mark(3)) != cudaSuccess) return ep_cuda(e, "event");
   agm::ep_barrier_kernel<<<1, 32, 0, stream>>>(pc, world, rank, epoch + 1, L.err);
   if ((e = cudaGetLastError()) != cudaSuccess) return ep_cuda(e, "barrier");
+  if ((e = mark(4)) != cudaSuccess) return ep_cuda(e, "event");
   // Expert FFN over the received tiles (count and experts from the device plan).
   void* recv = reinterpret_cast<void*>(peer_comm[rank] + agm::ep_off_recv(n_experts));
   void* y = reinterpret_cast<void*>(peer_comm[rank] + agm::ep_off_y(n_experts, cap_rows, d, eb));
@@ -383,6 +391,7 @@ AGM_API int agm_ep_forward(const void* x, int dtype, int64_t n_tokens, int d, in
   g1.err = L.err;
   e = agm::grouped_gemm(dtype, recv, cap_rows, w1, g1, true, sms, stream, 0);
   if (e != cudaSuccess) return ep_cuda(e, "grouped_gemm fc1");
+  if ((e = mark(5)) != cudaSuccess) return ep_cuda(e, "event");
   agm::GemmArgs g2 = g1;
   g2.c = y;
   g2.ldc = d;
@@ -391,12 +400,15 @@ AGM_API int agm_ep_forward(const void* x, int dtype, int64_t n_tokens, int d, in
   g2.k = hidden;
   e = agm::grouped_gemm(dtype, L.h, cap_rows, w2, g2, false, sms, stream, 0);
   if (e != cudaSuccess) return ep_cuda(e, "grouped_gemm fc2");
+  if ((e = mark(6)) != cudaSuccess) return ep_cuda(e, "event");
   agm::ep_barrier_kernel<<<1, 32, 0, stream>>>(pc, world, rank, epoch + 2, L.err);
   if ((e = cudaGetLastError()) != cudaSuccess) return ep_cuda(e, "barrier");
+  if ((e = mark(7)) != cudaSuccess) return ep_cuda(e, "event");
   if (n_tokens > 0) {
     e = agm::combine_ep(dtype, L.route, L.row_of, L.gates, n_tokens, d, top_k, out, sms, stream);
     if (e != cudaSuccess) return ep_cuda(e, "combine");
   }
+  if ((e = mark(8)) != cudaSuccess) return ep_cuda(e, "event");
   return AGM_OK;
 }
 

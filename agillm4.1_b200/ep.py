@@ -274,7 +274,9 @@ class P2PExpertParallelMoE:
         self.epoch = 1
         dist.barrier(group=group)
 
-    def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None, events=None) -> torch.Tensor:
+        """``events``: optional 9 CUDA events (timing) recorded at the stage
+        boundaries listed for ``agm_ep_forward``."""
         import ctypes
 
         n = x.shape[0]
@@ -282,12 +284,18 @@ class P2PExpertParallelMoE:
             raise ValueError(f"{n} tokens > max_tokens={self.max_tokens}")
         out = torch.empty_like(x) if out is None else out
         _lib, ops = self._lib, self._ops
+        ev_arr = None
+        if events is not None:
+            for ev in events:
+                if not ev.cuda_event:
+                    ev.record()
+            ev_arr = (ctypes.c_void_p * len(events))(*[ev.cuda_event for ev in events])
         rc = self.lib.agm_ep_forward(
             _lib.ptr(x), _lib.dtype_code(x.dtype), n, self.d, self.E, self.top_k, self.H, _lib.ptr(self.w_router),
             _lib.ptr(self.w1), _lib.ptr(self.b1), _lib.ptr(self.w2), _lib.ptr(self.b2), self.n_local,
             self.first_local, self.pl_code, self.world, self.rank, ctypes.addressof(self.peer_comm), self.cap_rows,
             self.epoch, _lib.ptr(out), _lib.ptr(self.ws), self.ws.numel(), 0,
-            _lib.stream_handle(x.device))
+            None if ev_arr is None else ctypes.addressof(ev_arr), _lib.stream_handle(x.device))
         _lib.check(rc, "agm_ep_forward")
         self.epoch += 3
         return out

@@ -57,6 +57,8 @@ TILE_ROWS = 128
 # permutation of the experts (seed 3), which gives a ~5:1 max/mean expert load.
 EP_SEED, ZIPF_S, ZIPF_SCALE = 3, 1.2, 0.63
 EP_STAGES = ["route", "counts_plan", "dispatch_a2a", "expert_ffn", "return_a2a", "combine"]
+P2P_STAGES = ["route", "counts_exchange_plan", "dispatch_to_peers", "barrier", "fc1", "fc2", "barrier2",
+              "combine_from_peers"]
 
 
 def load_peaks():
@@ -341,29 +343,25 @@ def run_ep(args, world, rank, local):
             out = fwd(x)
         torch.cuda.synchronize()
         same = bool(torch.equal(out, ref))
-        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(7)] for _ in range(args.steps)] \
-            if kind == "nccl" else None
+        n_ev = 7 if kind == "nccl" else 9
+        names = EP_STAGES if kind == "nccl" else P2P_STAGES
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(n_ev)] for _ in range(args.steps)]
         start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         barrier(world)
         torch.cuda.synchronize()
         with ClockSampler(dev) as clk:
             start.record(stream)
             for i in range(args.steps):
-                if evs is not None:
-                    moe.forward(x, events=evs[i])
-                else:
-                    fwd(x)
+                moe.forward(x, events=evs[i])
             stop.record(stream)
             torch.cuda.synchronize()
         barrier(world)
         ms = max_over_ranks(start.elapsed_time(stop), world)
-        st = None
-        if evs is not None:
-            st = {s_: 0.0 for s_ in EP_STAGES}
-            for e in evs:
-                for j, s_ in enumerate(EP_STAGES):
-                    st[s_] += e[j].elapsed_time(e[j + 1])
-            st = {s_: round(max_over_ranks(v / args.steps, world), 4) for s_, v in st.items()}
+        st = {s_: 0.0 for s_ in names}
+        for e in evs:
+            for j, s_ in enumerate(names):
+                st[s_] += e[j].elapsed_time(e[j + 1])
+        st = {s_: round(max_over_ranks(v / args.steps, world), 4) for s_, v in st.items()}
         if kind == "p2p":
             err = moe.device_error()
             same = same and err == 0
@@ -405,7 +403,7 @@ def run_ep(args, world, rank, local):
         return
     peaks = load_peaks()
     head = results["p2p_balanced"]
-    ffn_ms = results["nccl_balanced"]["stages_ms"]["expert_ffn"]
+    ffn_ms = head["stages_ms"]["fc1"] + head["stages_ms"]["fc2"]
     # Grouped GEMM roofline: FLOPs of the busiest rank's FC1+FC2 launches / their event-timed duration.
     flop = 2 * 2 * TILE_ROWS * max(head["tiles_per_rank"]) * D * HIDDEN
     achieved = flop / (ffn_ms / 1000.0) / 1e12

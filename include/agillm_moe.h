@@ -220,13 +220,17 @@ AGM_API size_t agm_ep_workspace_bytes(int64_t n_tokens, int d, int n_experts, in
  * communication buffer as mapped here (own buffer at [rank]). The counts
  * exchange and three barriers are flag writes in peer memory, bounded waits
  * (a time-out sets the device error word, the first int of the workspace).
+ * stage_events (nullable): AGM_EP_STAGE_EVENTS cudaEvent_t handles recorded
+ * before the router and after: local plan, counts exchange + global plan,
+ * dispatch (permute into peers), barrier, FC1, FC2, barrier, combine.
  * No host synchronisation; outputs are bit-identical to agm_moe_forward on
  * the same tokens.                                                           */
+#define AGM_EP_STAGE_EVENTS 9
 AGM_API int agm_ep_forward(const void* x, int dtype, int64_t n_tokens, int d, int n_experts, int top_k, int hidden,
                            const void* w_router, const void* w1, const void* b1, const void* w2, const void* b2,
                            int n_local_experts, int first_local_expert, int placement, int world, int rank,
                            const uint64_t* peer_comm, int64_t cap_rows, uint64_t epoch, void* out, void* workspace,
-                           size_t workspace_bytes, int flags, void* stream);
+                           size_t workspace_bytes, int flags, void* const* stage_events, void* stream);
 
 /* Synchronise `stream`, read the device error word at `err` (e.g. the first
  * int of a forward workspace) into *code and reset it to 0. Returns AGM_OK if
