@@ -55,6 +55,11 @@ SIGNATURES = {
     "agm_ep_workspace_bytes": (_SZ, [_I64, _I, _I, _I, _I, _I64, _I]),
     "agm_ep_forward": (_I, [_P, _I, _I64, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _I64,
                             ctypes.c_uint64, _P, _P, _SZ, _I, _P, _P]),
+    "agm_ep_dispatch": (_I, [_P, _I, _I64, _I, _I, _I, _I, _P, _I, _I, _I, _I, _I, _P, _I64, ctypes.c_uint64, _P,
+                             _SZ, _I, _P, _P]),
+    "agm_ep_expert": (_I, [_I, _I64, _I, _I, _I, _I, _P, _P, _P, _P, _I, _I, _I, _P, _I64, ctypes.c_uint64, _P, _SZ,
+                           _I, _P, _P]),
+    "agm_ep_combine": (_I, [_I, _I64, _I, _I, _I, _I, _I64, _P, _P, _SZ, _P]),
     "agm_moe_forward_noalloc": (_I, [_P, _I, _I64, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _P, _P,
                                      _I, _P]),
 }

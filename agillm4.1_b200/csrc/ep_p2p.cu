@@ -316,25 +316,28 @@ AGM_API size_t agm_ep_workspace_bytes(int64_t n_tokens, int d, int n_experts, in
   return ep_carve(nullptr, n_tokens, d, n_experts, top_k, hidden, cap_rows, eb).bytes;
 }
 
-AGM_API int agm_ep_forward(const void* x, int dtype, int64_t n_tokens, int d, int n_experts, int top_k, int hidden,
-                           const void* w_router, const void* w1, const void* b1, const void* w2, const void* b2,
-                           int n_local_experts, int first_local_expert, int placement, int world, int rank,
-                           const uint64_t* peer_comm, int64_t cap_rows, uint64_t epoch, void* out, void* workspace,
-                           size_t workspace_bytes, int flags, void* const* stage_events, void* stream_) {
+// Phase 1 (comm stream): route and permute this rank's tokens into the
+// receive buffers of the ranks that compute them; ends with the barrier after
+// which every rank's received rows are complete.
+AGM_API int agm_ep_dispatch(const void* x, int dtype, int64_t n_tokens, int d, int n_experts, int top_k, int hidden,
+                            const void* w_router, int n_local_experts, int first_local_expert, int placement,
+                            int world, int rank, const uint64_t* peer_comm, int64_t cap_rows, uint64_t epoch,
+                            void* workspace, size_t workspace_bytes, int flags, void* const* stage_events,
+                            void* stream_) {
   const int eb = eb_of(dtype);
-  if (!eb) return ep_fail(AGM_ERR_ARG, "agm_ep_forward: bad dtype");
+  if (!eb) return ep_fail(AGM_ERR_ARG, "agm_ep_dispatch: bad dtype");
   if (world < 1 || world > agm::kEpMaxRanks || rank < 0 || rank >= world)
-    return ep_fail(AGM_ERR_UNSUPPORTED, "agm_ep_forward: world must be in [1, 16] and rank in [0, world)");
+    return ep_fail(AGM_ERR_UNSUPPORTED, "agm_ep_dispatch: world must be in [1, 16] and rank in [0, world)");
   if (n_experts < 1 || n_experts > AGM_MAX_EXPERTS || top_k < 1 || top_k > n_experts)
-    return ep_fail(AGM_ERR_ARG, "agm_ep_forward: bad n_experts / top_k");
-  if (placement != 0 && placement != 1) return ep_fail(AGM_ERR_ARG, "agm_ep_forward: placement must be 0 or 1");
-  if (cap_rows <= 0 || cap_rows % 128) return ep_fail(AGM_ERR_ARG, "agm_ep_forward: cap_rows must be a multiple of 128");
-  if (!peer_comm || !x || !w_router || !w1 || !b1 || !w2 || !b2 || !out || !workspace)
-    return ep_fail(AGM_ERR_ARG, "agm_ep_forward: null pointer argument");
-  if (epoch == 0) return ep_fail(AGM_ERR_ARG, "agm_ep_forward: epoch must start at 1");
-  if (n_tokens < 0) return ep_fail(AGM_ERR_ARG, "agm_ep_forward: n_tokens < 0");
+    return ep_fail(AGM_ERR_ARG, "agm_ep_dispatch: bad n_experts / top_k");
+  if (placement != 0 && placement != 1) return ep_fail(AGM_ERR_ARG, "agm_ep_dispatch: placement must be 0 or 1");
+  if (cap_rows <= 0 || cap_rows % 128)
+    return ep_fail(AGM_ERR_ARG, "agm_ep_dispatch: cap_rows must be a multiple of 128");
+  if (!peer_comm || !x || !w_router || !workspace) return ep_fail(AGM_ERR_ARG, "agm_ep_dispatch: null pointer");
+  if (epoch == 0) return ep_fail(AGM_ERR_ARG, "agm_ep_dispatch: epoch must start at 1");
+  if (n_tokens < 0) return ep_fail(AGM_ERR_ARG, "agm_ep_dispatch: n_tokens < 0");
   EpLayout L = ep_carve(workspace, n_tokens, d, n_experts, top_k, hidden, cap_rows, eb);
-  if (L.bytes > workspace_bytes) return ep_fail(AGM_ERR_WORKSPACE, "agm_ep_forward: workspace too small");
+  if (L.bytes > workspace_bytes) return ep_fail(AGM_ERR_WORKSPACE, "agm_ep_dispatch: workspace too small");
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   agm::PeerComm pc;
   for (int r = 0; r < agm::kEpMaxRanks; ++r) pc.base[r] = r < world ? peer_comm[r] : 0;
@@ -374,7 +377,33 @@ AGM_API int agm_ep_forward(const void* x, int dtype, int64_t n_tokens, int d, in
   agm::ep_barrier_kernel<<<1, 32, 0, stream>>>(pc, world, rank, epoch + 1, L.err);
   if ((e = cudaGetLastError()) != cudaSuccess) return ep_cuda(e, "barrier");
   if ((e = mark(4)) != cudaSuccess) return ep_cuda(e, "event");
-  // Expert FFN over the received tiles (count and experts from the device plan).
+  return AGM_OK;
+}
+
+// Phase 2 (compute stream): FC1/FC2 over the received tiles into this rank's
+// result buffer, then the barrier after which every rank's results are
+// complete. gemm_ctas > 0 caps the GEMM's persistent CTAs (leaving SMs to
+// the other phases of another chunk running concurrently).
+AGM_API int agm_ep_expert(int dtype, int64_t n_tokens, int d, int n_experts, int top_k, int hidden, const void* w1,
+                          const void* b1, const void* w2, const void* b2, int n_local_experts, int world, int rank,
+                          const uint64_t* peer_comm, int64_t cap_rows, uint64_t epoch, void* workspace,
+                          size_t workspace_bytes, int gemm_ctas, void* const* stage_events, void* stream_) {
+  const int eb = eb_of(dtype);
+  if (!eb) return ep_fail(AGM_ERR_ARG, "agm_ep_expert: bad dtype");
+  if (world < 1 || world > agm::kEpMaxRanks || rank < 0 || rank >= world)
+    return ep_fail(AGM_ERR_UNSUPPORTED, "agm_ep_expert: bad world / rank");
+  if (!peer_comm || !w1 || !b1 || !w2 || !b2 || !workspace) return ep_fail(AGM_ERR_ARG, "agm_ep_expert: null pointer");
+  if (cap_rows <= 0 || cap_rows % 128) return ep_fail(AGM_ERR_ARG, "agm_ep_expert: bad cap_rows");
+  EpLayout L = ep_carve(workspace, n_tokens, d, n_experts, top_k, hidden, cap_rows, eb);
+  if (L.bytes > workspace_bytes) return ep_fail(AGM_ERR_WORKSPACE, "agm_ep_expert: workspace too small");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  agm::PeerComm pc;
+  for (int r = 0; r < agm::kEpMaxRanks; ++r) pc.base[r] = r < world ? peer_comm[r] : 0;
+  const int sms = num_sms_dev();
+  auto mark = [&](int i) -> cudaError_t {
+    return stage_events ? cudaEventRecord(static_cast<cudaEvent_t>(stage_events[i]), stream) : cudaSuccess;
+  };
+  cudaError_t e;
   void* recv = reinterpret_cast<void*>(peer_comm[rank] + agm::ep_off_recv(n_experts));
   void* y = reinterpret_cast<void*>(peer_comm[rank] + agm::ep_off_y(n_experts, cap_rows, d, eb));
   agm::GemmArgs g1;
@@ -389,9 +418,10 @@ AGM_API int agm_ep_forward(const void* x, int dtype, int64_t n_tokens, int d, in
   g1.num_tiles = L.recv_num_tiles;
   g1.max_tiles = static_cast<int>(cap_rows / 128);
   g1.err = L.err;
+  g1.max_ctas = gemm_ctas;
   e = agm::grouped_gemm(dtype, recv, cap_rows, w1, g1, true, sms, stream, 0);
   if (e != cudaSuccess) return ep_cuda(e, "grouped_gemm fc1");
-  if ((e = mark(5)) != cudaSuccess) return ep_cuda(e, "event");
+  if ((e = mark(0)) != cudaSuccess) return ep_cuda(e, "event");
   agm::GemmArgs g2 = g1;
   g2.c = y;
   g2.ldc = d;
@@ -400,15 +430,48 @@ AGM_API int agm_ep_forward(const void* x, int dtype, int64_t n_tokens, int d, in
   g2.k = hidden;
   e = agm::grouped_gemm(dtype, L.h, cap_rows, w2, g2, false, sms, stream, 0);
   if (e != cudaSuccess) return ep_cuda(e, "grouped_gemm fc2");
-  if ((e = mark(6)) != cudaSuccess) return ep_cuda(e, "event");
+  if ((e = mark(1)) != cudaSuccess) return ep_cuda(e, "event");
   agm::ep_barrier_kernel<<<1, 32, 0, stream>>>(pc, world, rank, epoch + 2, L.err);
   if ((e = cudaGetLastError()) != cudaSuccess) return ep_cuda(e, "barrier");
-  if ((e = mark(7)) != cudaSuccess) return ep_cuda(e, "event");
-  if (n_tokens > 0) {
-    e = agm::combine_ep(dtype, L.route, L.row_of, L.gates, n_tokens, d, top_k, out, sms, stream);
-    if (e != cudaSuccess) return ep_cuda(e, "combine");
+  if ((e = mark(2)) != cudaSuccess) return ep_cuda(e, "event");
+  return AGM_OK;
+}
+
+// Phase 3 (comm stream): each token's k expert rows, read from the ranks that
+// computed them, gate-weighted into out [n, d].
+AGM_API int agm_ep_combine(int dtype, int64_t n_tokens, int d, int n_experts, int top_k, int hidden,
+                           int64_t cap_rows, void* out, void* workspace, size_t workspace_bytes, void* stream_) {
+  const int eb = eb_of(dtype);
+  if (!eb) return ep_fail(AGM_ERR_ARG, "agm_ep_combine: bad dtype");
+  if (!out || !workspace) return ep_fail(AGM_ERR_ARG, "agm_ep_combine: null pointer");
+  EpLayout L = ep_carve(workspace, n_tokens, d, n_experts, top_k, hidden, cap_rows, eb);
+  if (L.bytes > workspace_bytes) return ep_fail(AGM_ERR_WORKSPACE, "agm_ep_combine: workspace too small");
+  if (n_tokens <= 0) return AGM_OK;
+  cudaError_t e = agm::combine_ep(dtype, L.route, L.row_of, L.gates, n_tokens, d, top_k, out, num_sms_dev(),
+                                  static_cast<cudaStream_t>(stream_));
+  return e == cudaSuccess ? AGM_OK : ep_cuda(e, "combine");
+}
+
+AGM_API int agm_ep_forward(const void* x, int dtype, int64_t n_tokens, int d, int n_experts, int top_k, int hidden,
+                           const void* w_router, const void* w1, const void* b1, const void* w2, const void* b2,
+                           int n_local_experts, int first_local_expert, int placement, int world, int rank,
+                           const uint64_t* peer_comm, int64_t cap_rows, uint64_t epoch, void* out, void* workspace,
+                           size_t workspace_bytes, int flags, void* const* stage_events, void* stream) {
+  if (!w1 || !b1 || !w2 || !b2 || !out) return ep_fail(AGM_ERR_ARG, "agm_ep_forward: null pointer argument");
+  int rc = agm_ep_dispatch(x, dtype, n_tokens, d, n_experts, top_k, hidden, w_router, n_local_experts,
+                           first_local_expert, placement, world, rank, peer_comm, cap_rows, epoch, workspace,
+                           workspace_bytes, flags, stage_events, stream);
+  if (rc != AGM_OK) return rc;
+  rc = agm_ep_expert(dtype, n_tokens, d, n_experts, top_k, hidden, w1, b1, w2, b2, n_local_experts, world, rank,
+                     peer_comm, cap_rows, epoch, workspace, workspace_bytes, 0,
+                     stage_events ? stage_events + 5 : nullptr, stream);
+  if (rc != AGM_OK) return rc;
+  rc = agm_ep_combine(dtype, n_tokens, d, n_experts, top_k, hidden, cap_rows, out, workspace, workspace_bytes, stream);
+  if (rc != AGM_OK) return rc;
+  if (stage_events) {
+    cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(stage_events[8]), static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return ep_cuda(e, "event");
   }
-  if ((e = mark(8)) != cudaSuccess) return ep_cuda(e, "event");
   return AGM_OK;
 }
 

@@ -430,7 +430,8 @@ static cudaError_t launch_tc(const void* a, int64_t a_rows, const void* w, const
   if (e != cudaSuccess) return e;
   const int num_n = (args.n + BN - 1) / BN;
   const int64_t max_total = static_cast<int64_t>(args.max_tiles) * num_n;
-  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(num_sms, max_total)));
+  const int ctas = args.max_ctas > 0 ? std::min(args.max_ctas, num_sms) : num_sms;
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ctas, max_total)));
   grouped_gemm_tc_kernel<T, BN, RELU><<<grid, kGemmThreads, Cfg::SMEM_BYTES, stream>>>(tmA, tmB, tmC, args);
   return cudaGetLastError();
 }

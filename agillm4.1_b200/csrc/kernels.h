@@ -23,6 +23,7 @@ struct GemmArgs {
   const int32_t* num_tiles;   // device count of valid row tiles, or nullptr
   int max_tiles;              // host bound (and the count when num_tiles is null)
   int* err;
+  int max_ctas = 0;           // cap on persistent CTAs (0 = one per SM), leaves SMs to concurrent kernels
 };
 
 // Expert-parallel routing of one rank's permuted rows (see ep_p2p.cu). The

@@ -201,24 +201,73 @@ class ExpertParallelMoE:
         return out
 
 
+class _CommSlot:
+    """One communication buffer (mapped on every rank) plus its workspace and
+    epoch sequence: the resources of one token chunk in flight."""
+
+    def __init__(self, lib, _lib, group, world, rank, n_experts, cap_rows, d, hidden, top_k, max_tokens, dtype,
+                 device):
+        import ctypes
+
+        self.lib, self._lib, self.group = lib, _lib, group
+        code = _lib.dtype_code(dtype)
+        nbytes = int(lib.agm_ep_comm_bytes(n_experts, cap_rows, d, code))
+        ptr = ctypes.c_void_p()
+        _lib.check(lib.agm_ep_alloc(nbytes, ctypes.byref(ptr)), "agm_ep_alloc")
+        self.own = ptr.value
+        handle = (ctypes.c_uint8 * 64)()
+        _lib.check(lib.agm_ep_ipc_handle(self.own, handle), "agm_ep_ipc_handle")
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.opened, ptrs = [], []
+        for r, h in enumerate(handles):
+            if r == rank:
+                ptrs.append(self.own)
+                continue
+            hb = (ctypes.c_uint8 * 64).from_buffer_copy(h)
+            pp = ctypes.c_void_p()
+            _lib.check(lib.agm_ep_ipc_open(hb, ctypes.byref(pp)), "agm_ep_ipc_open")
+            self.opened.append(pp.value)
+            ptrs.append(pp.value)
+        self.peer_comm = (ctypes.c_uint64 * world)(*ptrs)
+        self.ws = torch.empty(int(lib.agm_ep_workspace_bytes(max_tokens, d, n_experts, top_k, hidden, cap_rows,
+                                                              code)), dtype=torch.uint8, device=device)
+        self.epoch = 1
+
+    def close(self):
+        for p in self.opened:
+            self.lib.agm_ep_ipc_close(p)
+        self.opened = []
+
+    def free(self):
+        if self.own is not None:
+            self.lib.agm_ep_free(self.own)
+            self.own = None
+
+
 class P2PExpertParallelMoE:
     """Expert-parallel forward with the all-to-all fused into the kernels.
 
-    Every rank allocates one communication buffer (receive rows, result rows,
+    Every rank allocates a communication buffer (receive rows, result rows,
     signal flags, counts inbox) and maps every peer's buffer through CUDA IPC.
-    ``forward`` then runs entirely on the current stream with no host sync:
-    the permute kernel writes each row straight into the receive buffer of
-    the rank that computes it (NVLink stores), three flag barriers in peer
-    memory order the phases, and the combine kernel reads the expert outputs
-    straight from the ranks that computed them (NVLink loads). See the C ABI
-    ``agm_ep_forward``. All ranks must call ``forward`` the same number of
-    times (every call is a collective).
+    ``forward`` runs with no host sync: the permute kernel writes each row
+    straight into the receive buffer of the rank that computes it (NVLink
+    stores), flag barriers in peer memory order the phases, and the combine
+    kernel reads the expert outputs straight from the ranks that computed them
+    (NVLink loads). See the C ABI ``agm_ep_forward``.
+
+    ``chunks > 1`` splits this rank's tokens into chunks and overlaps them on
+    two streams: chunk j's expert GEMMs (capped at ``num_SMs - reserve_sms``
+    CTAs) run while chunk j+1 is dispatched and chunk j-1 combined on the
+    caller's stream; two communication slots alternate between chunks.
+    Results are bit-identical for any chunking (tokens are independent).
+    All ranks must call ``forward`` the same number of times with the same
+    ``chunks`` (every call is a collective).
     """
 
     def __init__(self, weights: Sequence[torch.Tensor], top_k: int, n_experts: int, max_tokens: int, group=None,
-                 placement: str = "balanced", cap_rows: Optional[int] = None):
-        import ctypes
-
+                 placement: str = "balanced", cap_rows: Optional[int] = None, chunks: int = 1,
+                 reserve_sms: int = 20):
         from . import _lib, ops
 
         self._lib = _lib
@@ -243,75 +292,117 @@ class P2PExpertParallelMoE:
         self.H = int(self.w1.shape[1])
         self.dtype = self.w1.dtype
         self.max_tokens = int(max_tokens)
-        rows = ops.max_rows(self.max_tokens, self.top_k, self.E)
+        self.chunks = max(1, int(chunks))
+        self.chunk_tokens = (self.max_tokens + self.chunks - 1) // self.chunks
+        rows = ops.max_rows(self.chunk_tokens, self.top_k, self.E)
         if cap_rows is None:
             cap_rows = 2 * rows if placement == "balanced" else self.world * rows
         self.cap_rows = (int(cap_rows) + TILE - 1) // TILE * TILE
-        code = _lib.dtype_code(self.dtype)
-        nbytes = int(self.lib.agm_ep_comm_bytes(self.E, self.cap_rows, self.d, code))
-        ptr = ctypes.c_void_p()
-        _lib.check(self.lib.agm_ep_alloc(nbytes, ctypes.byref(ptr)), "agm_ep_alloc")
-        self.own = ptr.value
-        handle = (ctypes.c_uint8 * 64)()
-        _lib.check(self.lib.agm_ep_ipc_handle(self.own, handle), "agm_ep_ipc_handle")
-        handles = [None] * self.world
-        dist.all_gather_object(handles, bytes(handle), group=group)
-        self.opened = []
-        ptrs = []
-        for r, h in enumerate(handles):
-            if r == self.rank:
-                ptrs.append(self.own)
-                continue
-            hb = (ctypes.c_uint8 * 64).from_buffer_copy(h)
-            pp = ctypes.c_void_p()
-            _lib.check(self.lib.agm_ep_ipc_open(hb, ctypes.byref(pp)), "agm_ep_ipc_open")
-            self.opened.append(pp.value)
-            ptrs.append(pp.value)
-        self.peer_comm = (ctypes.c_uint64 * self.world)(*ptrs)
-        self.ws = torch.empty(int(self.lib.agm_ep_workspace_bytes(self.max_tokens, self.d, self.E, self.top_k,
-                                                                   self.H, self.cap_rows, code)),
-                              dtype=torch.uint8, device=self.device)
-        self.epoch = 1
+        n_slots = 1 if self.chunks == 1 else 2
+        self.slots = [_CommSlot(self.lib, _lib, group, self.world, self.rank, self.E, self.cap_rows, self.d, self.H,
+                                self.top_k, self.chunk_tokens, self.dtype, self.device) for _ in range(n_slots)]
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        self.gemm_ctas = 0 if self.chunks == 1 else max(1, sms - int(reserve_sms))
+        self.compute_stream = torch.cuda.Stream(self.device) if self.chunks > 1 else None
         dist.barrier(group=group)
 
-    def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None, events=None) -> torch.Tensor:
-        """``events``: optional 9 CUDA events (timing) recorded at the stage
-        boundaries listed for ``agm_ep_forward``."""
+    # -- phases ------------------------------------------------------------
+    def _dispatch(self, slot, x, events=None):
         import ctypes
+        _lib = self._lib
+        ev = self._event_array(events)
+        rc = self.lib.agm_ep_dispatch(
+            _lib.ptr(x), _lib.dtype_code(x.dtype), x.shape[0], self.d, self.E, self.top_k, self.H,
+            _lib.ptr(self.w_router), self.n_local, self.first_local, self.pl_code, self.world, self.rank,
+            ctypes.addressof(slot.peer_comm), self.cap_rows, slot.epoch, _lib.ptr(slot.ws), slot.ws.numel(), 0,
+            None if ev is None else ctypes.addressof(ev), _lib.stream_handle(x.device))
+        _lib.check(rc, "agm_ep_dispatch")
 
+    def _expert(self, slot, n, events=None):
+        import ctypes
+        _lib = self._lib
+        ev = self._event_array(events)
+        rc = self.lib.agm_ep_expert(
+            _lib.dtype_code(self.dtype), n, self.d, self.E, self.top_k, self.H, _lib.ptr(self.w1),
+            _lib.ptr(self.b1), _lib.ptr(self.w2), _lib.ptr(self.b2), self.n_local, self.world, self.rank,
+            ctypes.addressof(slot.peer_comm), self.cap_rows, slot.epoch, _lib.ptr(slot.ws), slot.ws.numel(),
+            self.gemm_ctas, None if ev is None else ctypes.addressof(ev),
+            torch.cuda.current_stream(self.device).cuda_stream)
+        _lib.check(rc, "agm_ep_expert")
+
+    def _combine(self, slot, n, out):
+        _lib = self._lib
+        rc = self.lib.agm_ep_combine(_lib.dtype_code(self.dtype), n, self.d, self.E, self.top_k, self.H,
+                                     self.cap_rows, _lib.ptr(out), _lib.ptr(slot.ws), slot.ws.numel(),
+                                     torch.cuda.current_stream(self.device).cuda_stream)
+        _lib.check(rc, "agm_ep_combine")
+        slot.epoch += 3
+
+    @staticmethod
+    def _event_array(events):
+        import ctypes
+        if events is None:
+            return None
+        for e in events:
+            if not e.cuda_event:
+                e.record()
+        return (ctypes.c_void_p * len(events))(*[e.cuda_event for e in events])
+
+    # -- forward -----------------------------------------------------------
+    def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None, events=None) -> torch.Tensor:
+        """``events`` (chunks == 1 only): 9 CUDA events recorded at the stage
+        boundaries listed for ``agm_ep_forward``."""
         n = x.shape[0]
         if n > self.max_tokens:
             raise ValueError(f"{n} tokens > max_tokens={self.max_tokens}")
         out = torch.empty_like(x) if out is None else out
-        _lib, ops = self._lib, self._ops
-        ev_arr = None
-        if events is not None:
-            for ev in events:
-                if not ev.cuda_event:
-                    ev.record()
-            ev_arr = (ctypes.c_void_p * len(events))(*[ev.cuda_event for ev in events])
-        rc = self.lib.agm_ep_forward(
-            _lib.ptr(x), _lib.dtype_code(x.dtype), n, self.d, self.E, self.top_k, self.H, _lib.ptr(self.w_router),
-            _lib.ptr(self.w1), _lib.ptr(self.b1), _lib.ptr(self.w2), _lib.ptr(self.b2), self.n_local,
-            self.first_local, self.pl_code, self.world, self.rank, ctypes.addressof(self.peer_comm), self.cap_rows,
-            self.epoch, _lib.ptr(out), _lib.ptr(self.ws), self.ws.numel(), 0,
-            None if ev_arr is None else ctypes.addressof(ev_arr), _lib.stream_handle(x.device))
-        _lib.check(rc, "agm_ep_forward")
-        self.epoch += 3
+        if self.chunks == 1:
+            slot = self.slots[0]
+            self._dispatch(slot, x, None if events is None else events[:5])
+            self._expert(slot, n, None if events is None else events[5:8])
+            self._combine(slot, n, out)
+            if events is not None:
+                events[8].record()
+            return out
+        comm = torch.cuda.current_stream(self.device)
+        comp = self.compute_stream
+        bounds = [min(n, j * self.chunk_tokens) for j in range(self.chunks + 1)]
+        ev_disp = [torch.cuda.Event() for _ in range(self.chunks)]
+        ev_ffn = [torch.cuda.Event() for _ in range(self.chunks)]
+        comp.wait_stream(comm)
+
+        def combine(j):
+            comm.wait_event(ev_ffn[j])
+            self._combine(self.slots[j % 2], bounds[j + 1] - bounds[j], out[bounds[j]:bounds[j + 1]])
+
+        for j in range(self.chunks):
+            slot = self.slots[j % 2]
+            self._dispatch(slot, x[bounds[j]:bounds[j + 1]])
+            ev_disp[j].record(comm)
+            with torch.cuda.stream(comp):
+                comp.wait_event(ev_disp[j])
+                self._expert(slot, bounds[j + 1] - bounds[j])
+                ev_ffn[j].record(comp)
+            if j >= 1:
+                combine(j - 1)
+        combine(self.chunks - 1)
         return out
 
     def device_error(self) -> int:
-        return self._lib.read_device_error(self.ws[:4].view(torch.int32))
+        code = 0
+        for slot in self.slots:
+            code |= self._lib.read_device_error(slot.ws[:4].view(torch.int32))
+        return code
 
     def close(self) -> None:
-        """Collective: unmap the peers' buffers and free this rank's buffer."""
-        if self.own is None:
+        """Collective: unmap the peers' buffers and free this rank's buffers."""
+        if not self.slots:
             return
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)
-        for p in self.opened:
-            self.lib.agm_ep_ipc_close(p)
-        self.opened = []
+        for slot in self.slots:
+            slot.close()
         dist.barrier(group=self.group)
-        self.lib.agm_ep_free(self.own)
-        self.own = None
+        for slot in self.slots:
+            slot.free()
+        self.slots = []

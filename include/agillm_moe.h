@@ -226,6 +226,29 @@ AGM_API size_t agm_ep_workspace_bytes(int64_t n_tokens, int d, int n_experts, in
  * No host synchronisation; outputs are bit-identical to agm_moe_forward on
  * the same tokens.                                                           */
 #define AGM_EP_STAGE_EVENTS 9
+
+/* agm_ep_forward in three phases, so that the phases of consecutive token
+ * chunks can overlap on two streams (chunk j's expert GEMMs on a compute
+ * stream while chunk j+1 is dispatched and chunk j-1 combined on a comm
+ * stream). Each chunk in flight needs its own communication buffer, workspace
+ * and epoch sequence; a chunk's phases must run in order (dispatch, expert,
+ * combine) with the caller ordering them across streams (events).
+ * agm_ep_dispatch: router, local plan, counts exchange, device plan, rows into
+ *   the computing ranks' receive buffers, barrier (stage_events: 5 events).
+ * agm_ep_expert: FC1/FC2 on the received tiles, barrier; gemm_ctas > 0 caps
+ *   the GEMM's persistent CTAs (stage_events: 3 events).
+ * agm_ep_combine: gate-weighted combine from the computing ranks' results.   */
+AGM_API int agm_ep_dispatch(const void* x, int dtype, int64_t n_tokens, int d, int n_experts, int top_k, int hidden,
+                            const void* w_router, int n_local_experts, int first_local_expert, int placement,
+                            int world, int rank, const uint64_t* peer_comm, int64_t cap_rows, uint64_t epoch,
+                            void* workspace, size_t workspace_bytes, int flags, void* const* stage_events,
+                            void* stream);
+AGM_API int agm_ep_expert(int dtype, int64_t n_tokens, int d, int n_experts, int top_k, int hidden, const void* w1,
+                          const void* b1, const void* w2, const void* b2, int n_local_experts, int world, int rank,
+                          const uint64_t* peer_comm, int64_t cap_rows, uint64_t epoch, void* workspace,
+                          size_t workspace_bytes, int gemm_ctas, void* const* stage_events, void* stream);
+AGM_API int agm_ep_combine(int dtype, int64_t n_tokens, int d, int n_experts, int top_k, int hidden,
+                           int64_t cap_rows, void* out, void* workspace, size_t workspace_bytes, void* stream);
 AGM_API int agm_ep_forward(const void* x, int dtype, int64_t n_tokens, int d, int n_experts, int top_k, int hidden,
                            const void* w_router, const void* w1, const void* b1, const void* w2, const void* b2,
                            int n_local_experts, int first_local_expert, int placement, int world, int rank,

@@ -50,13 +50,14 @@ def _worker(rank, world, port, q):
             out2 = moe.forward(x)
             torch.cuda.synchronize()
             res[placement] = (bool(torch.equal(out, ref)), bool(torch.equal(out, out2)))
-        for placement in ("static", "balanced"):
+        for placement, chunks in (("static", 1), ("balanced", 1), ("balanced", 2), ("static", 3)):
             mine = ep.ExpertParallelMoE.shard_weights(*w, rank, world, placement)
-            moe = ep.P2PExpertParallelMoE((wr,) + tuple(mine), k, E, max_tokens=4000, placement=placement)
+            moe = ep.P2PExpertParallelMoE((wr,) + tuple(mine), k, E, max_tokens=4000, placement=placement,
+                                          chunks=chunks)
             outs = [moe.forward(x).clone() for _ in range(3)]
             torch.cuda.synchronize()
             err = moe.device_error()
-            res["p2p_" + placement] = (all(bool(torch.equal(o, ref)) for o in outs), err == 0)
+            res[f"p2p_{placement}_chunks{chunks}"] = (all(bool(torch.equal(o, ref)) for o in outs), err == 0)
             moe.close()
         q.put((rank, res))
     finally:
@@ -102,14 +103,15 @@ def test_p2p_path_single_rank():
         w = [torch.stack([sd[f"experts.{e}.{i}.{p}"] for e in range(E)]).contiguous()
              for i, p in ((0, "weight"), (0, "bias"), (2, "weight"), (2, "bias"))]
         wr = sd["router.weight"].contiguous()
-        for placement in ("static", "balanced"):
-            moe = ep.P2PExpertParallelMoE((wr,) + tuple(w), k, E, max_tokens=5000, placement=placement)
+        for placement, chunks in (("static", 1), ("balanced", 1), ("balanced", 3)):
+            moe = ep.P2PExpertParallelMoE((wr,) + tuple(w), k, E, max_tokens=5000, placement=placement,
+                                          chunks=chunks)
             for n in (4096, 1, 777, 5000):
                 x = synthetic.make_input(n, d, n, dtype=torch.bfloat16, device=dev)
                 out = moe.forward(x)
                 ref = ops.moe_forward(x, wr, *w, k)
                 torch.cuda.synchronize()
-                assert torch.equal(out, ref), (placement, n)
+                assert torch.equal(out, ref), (placement, chunks, n)
             assert moe.device_error() == 0
             moe.close()
     finally:
