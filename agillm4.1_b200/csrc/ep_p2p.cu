@@ -333,7 +333,8 @@ AGM_API int agm_ep_dispatch(const void* x, int dtype, int64_t n_tokens, int d, i
   if (placement != 0 && placement != 1) return ep_fail(AGM_ERR_ARG, "agm_ep_dispatch: placement must be 0 or 1");
   if (cap_rows <= 0 || cap_rows % 128)
     return ep_fail(AGM_ERR_ARG, "agm_ep_dispatch: cap_rows must be a multiple of 128");
-  if (!peer_comm || !x || !w_router || !workspace) return ep_fail(AGM_ERR_ARG, "agm_ep_dispatch: null pointer");
+  if (!peer_comm || !w_router || !workspace || (n_tokens > 0 && !x))
+    return ep_fail(AGM_ERR_ARG, "agm_ep_dispatch: null pointer");
   if (epoch == 0) return ep_fail(AGM_ERR_ARG, "agm_ep_dispatch: epoch must start at 1");
   if (n_tokens < 0) return ep_fail(AGM_ERR_ARG, "agm_ep_dispatch: n_tokens < 0");
   EpLayout L = ep_carve(workspace, n_tokens, d, n_experts, top_k, hidden, cap_rows, eb);
@@ -443,7 +444,7 @@ AGM_API int agm_ep_combine(int dtype, int64_t n_tokens, int d, int n_experts, in
                            int64_t cap_rows, void* out, void* workspace, size_t workspace_bytes, void* stream_) {
   const int eb = eb_of(dtype);
   if (!eb) return ep_fail(AGM_ERR_ARG, "agm_ep_combine: bad dtype");
-  if (!out || !workspace) return ep_fail(AGM_ERR_ARG, "agm_ep_combine: null pointer");
+  if (!workspace || (n_tokens > 0 && !out)) return ep_fail(AGM_ERR_ARG, "agm_ep_combine: null pointer");
   EpLayout L = ep_carve(workspace, n_tokens, d, n_experts, top_k, hidden, cap_rows, eb);
   if (L.bytes > workspace_bytes) return ep_fail(AGM_ERR_WORKSPACE, "agm_ep_combine: workspace too small");
   if (n_tokens <= 0) return AGM_OK;
@@ -457,7 +458,8 @@ AGM_API int agm_ep_forward(const void* x, int dtype, int64_t n_tokens, int d, in
                            int n_local_experts, int first_local_expert, int placement, int world, int rank,
                            const uint64_t* peer_comm, int64_t cap_rows, uint64_t epoch, void* out, void* workspace,
                            size_t workspace_bytes, int flags, void* const* stage_events, void* stream) {
-  if (!w1 || !b1 || !w2 || !b2 || !out) return ep_fail(AGM_ERR_ARG, "agm_ep_forward: null pointer argument");
+  if (!w1 || !b1 || !w2 || !b2 || (n_tokens > 0 && !out))
+    return ep_fail(AGM_ERR_ARG, "agm_ep_forward: null pointer argument");
   int rc = agm_ep_dispatch(x, dtype, n_tokens, d, n_experts, top_k, hidden, w_router, n_local_experts,
                            first_local_expert, placement, world, rank, peer_comm, cap_rows, epoch, workspace,
                            workspace_bytes, flags, stage_events, stream);
