@@ -150,17 +150,9 @@ struct EpY {
   const EpRoute* route;
   int nchunk;
   __device__ __forceinline__ const uint4* row(int64_t p) const {
-    const int64_t t = p >> 7;
-    const int w = route->world;
-    for (int r = 0; r < w; ++r) {
-      const int64_t lo = route->send_tile_start[r], hi = route->send_tile_start[r + 1];
-      if (t >= lo && t < hi) {
-        if (t - lo >= route->send_limit[r]) return nullptr;
-        const int64_t drow = (route->dest_tile_base[r] + (t - lo)) * 128 + (p & 127);
-        return reinterpret_cast<const uint4*>(route->peer_y[r]) + drow * nchunk;
-      }
-    }
-    return nullptr;
+    int r = 0;
+    const int64_t drow = ep_dest_row(route, p, &r);
+    return drow < 0 ? nullptr : reinterpret_cast<const uint4*>(route->peer_y[r]) + drow * nchunk;
   }
   // Rows written by other GPUs: cache in L2 only (ld.global.cg).
   __device__ __forceinline__ static uint4 load(const uint4* p) { return __ldcg(p); }

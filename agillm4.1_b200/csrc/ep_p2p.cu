@@ -30,7 +30,9 @@
 // rank r computes the contiguous range [bounds[r], bounds[r+1])):
 //   0 static   - bounds at expert boundaries of contiguous ownership ranges
 //                (first E mod P ranks own one more expert);
-//   1 balanced - P near-equal ranges (every rank holds all expert weights).
+//   1 balanced - P near-equal ranges (every rank holds all expert weights);
+//   2 local    - every rank holds all expert weights; each rank computes its
+//                own tiles up to an equal share and only the excess moves.
 #include <algorithm>
 #include <string>
 
@@ -104,91 +106,144 @@ __global__ void ep_barrier_kernel(PeerComm pc, int world, int rank, uint64_t epo
 }
 
 // One CTA: the global plan from the counts inbox (identical on every rank),
-// this rank's send route and its receive-side tile table.
+// this rank's send segments and its receive-side tile table.
+//
+// The plan is one contiguous piece of every source's tiles (in its x_perm
+// order) per destination rank, piece(i, r) = [lo, hi):
+//   static / balanced: the global tile sequence is ordered by (expert, source,
+//     tile) and rank r computes the range [bounds[r], bounds[r+1]); since a
+//     source's tiles appear in that sequence in x_perm order, the tiles it
+//     sends to r are contiguous;
+//   local (every rank holds every expert): rank r's quota is an equal share of
+//     all tiles; each source keeps its first min(own, quota) tiles and sends
+//     the rest, in order, to the ranks below quota (lowest rank first).
+// A destination lays its pieces out by source rank.
 __global__ void ep_plan_kernel(PeerComm pc, int world, int rank, int E, int placement, int first_local_expert,
                                int n_local_experts, int64_t cap_rows, int d, int eb, EpRoute* route,
                                int32_t* __restrict__ recv_tile_expert, int32_t* __restrict__ recv_num_tiles,
                                int* err) {
   __shared__ int64_t tiles[kEpMaxRanks][AGM_MAX_EXPERTS];
-  __shared__ int64_t g0[kEpMaxRanks][AGM_MAX_EXPERTS];
-  __shared__ int64_t bounds[kEpMaxRanks + 1];
-  __shared__ int64_t recv_off[kEpMaxRanks][AGM_MAX_EXPERTS];  // where (source i, expert e) lands here
-  __shared__ int64_t n_recv;
+  __shared__ int64_t plo[kEpMaxRanks][kEpMaxRanks];  // piece(i, r) = [plo, phi) of source i's tiles
+  __shared__ int64_t phi[kEpMaxRanks][kEpMaxRanks];
   const int32_t* inbox = reinterpret_cast<const int32_t*>(pc.base[rank] + ep_off_inbox());
   if (threadIdx.x == 0) {
-    for (int i = 0; i < world; ++i)
-      for (int e = 0; e < E; ++e) tiles[i][e] = (static_cast<int64_t>(inbox[i * E + e]) + 127) / 128;
-    int64_t pos = 0;
-    int64_t e_start[AGM_MAX_EXPERTS + 1];
-    for (int e = 0; e < E; ++e) {
-      e_start[e] = pos;
-      for (int i = 0; i < world; ++i) {
-        g0[i][e] = pos;
-        pos += tiles[i][e];
+    int64_t T[kEpMaxRanks];
+    int64_t total = 0;
+    for (int i = 0; i < world; ++i) {
+      T[i] = 0;
+      for (int e = 0; e < E; ++e) {
+        tiles[i][e] = (static_cast<int64_t>(inbox[i * E + e]) + 127) / 128;
+        T[i] += tiles[i][e];
       }
+      total += T[i];
+      for (int r = 0; r < world; ++r) plo[i][r] = phi[i][r] = 0;
     }
-    e_start[E] = pos;
-    const int64_t total = pos;
-    if (placement == 0) {
-      const int base = E / world, extra = E % world;
-      int e = 0;
+    if (placement == 2) {
+      int64_t quota[kEpMaxRanks], keep[kEpMaxRanks], deficit[kEpMaxRanks];
       for (int r = 0; r < world; ++r) {
-        bounds[r] = e_start[e];
-        e += base + (r < extra ? 1 : 0);
+        quota[r] = total / world + (r < total % world ? 1 : 0);
+        keep[r] = min(T[r], quota[r]);
+        deficit[r] = quota[r] - keep[r];
+        plo[r][r] = 0;
+        phi[r][r] = keep[r];
+      }
+      int r = 0;
+      for (int i = 0; i < world; ++i) {
+        int64_t pos = keep[i];
+        while (pos < T[i]) {
+          while (r < world && deficit[r] == 0) ++r;
+          if (r >= world) break;  // cannot happen: quotas sum to the total
+          const int64_t n = min(T[i] - pos, deficit[r]);
+          plo[i][r] = pos;
+          phi[i][r] = pos + n;
+          pos += n;
+          deficit[r] -= n;
+        }
       }
     } else {
-      for (int r = 0; r < world; ++r) bounds[r] = (static_cast<int64_t>(r) * total) / world;
+      // Global sequence (expert, source, tile) and the ranks' ranges in it.
+      int64_t g0[kEpMaxRanks][AGM_MAX_EXPERTS];
+      int64_t e_start[AGM_MAX_EXPERTS + 1];
+      int64_t bounds[kEpMaxRanks + 1];
+      int64_t pos = 0;
+      for (int e = 0; e < E; ++e) {
+        e_start[e] = pos;
+        for (int i = 0; i < world; ++i) {
+          g0[i][e] = pos;
+          pos += tiles[i][e];
+        }
+      }
+      e_start[E] = pos;
+      if (placement == 0) {
+        const int base = E / world, extra = E % world;
+        int e = 0;
+        for (int q = 0; q < world; ++q) {
+          bounds[q] = e_start[min(e, E)];
+          e += base + (q < extra ? 1 : 0);
+        }
+      } else {
+        for (int q = 0; q < world; ++q) bounds[q] = (static_cast<int64_t>(q) * total) / world;
+      }
+      bounds[world] = total;
+      for (int i = 0; i < world; ++i) {
+        int64_t start = 0;
+        for (int q = 0; q < world; ++q) {
+          int64_t n = 0;
+          for (int e = 0; e < E; ++e) {
+            const int64_t lo = max(g0[i][e], bounds[q]), hi = min(g0[i][e] + tiles[i][e], bounds[q + 1]);
+            n += hi > lo ? hi - lo : 0;
+          }
+          plo[i][q] = start;
+          phi[i][q] = start + n;
+          start += n;
+        }
+      }
     }
-    bounds[world] = total;
-    // Send route: my tiles (source = rank) in x_perm order go to ranks in increasing order.
+    // Send segments of this rank.
     route->world = world;
     route->rank = rank;
-    int64_t st = 0;
-    for (int r = 0; r < world; ++r) {
-      route->send_tile_start[r] = st;
-      int64_t base_in_r = 0;  // tiles of lower sources landing in r before mine
-      for (int i = 0; i < world; ++i)
-        for (int e = 0; e < E; ++e) {
-          const int64_t lo = max(g0[i][e], bounds[r]), hi = min(g0[i][e] + tiles[i][e], bounds[r + 1]);
-          const int64_t ov = hi > lo ? hi - lo : 0;
-          if (i == rank) st += ov;
-          if (i < rank) base_in_r += ov;
-        }
-      route->dest_tile_base[r] = base_in_r;
-      // Never write past rank r's receive buffer (its own plan flags the overflow).
-      route->send_limit[r] = max(static_cast<int64_t>(0), cap_rows / 128 - base_in_r);
-      route->peer_recv[r] = pc.base[r] + ep_off_recv(E);
-      route->peer_y[r] = pc.base[r] + ep_off_y(E, cap_rows, d, eb);
+    int ns = 0;
+    const int64_t cap_tiles = cap_rows / 128;
+    for (int q = 0; q < world; ++q) {
+      route->peer_recv[q] = pc.base[q] + ep_off_recv(E);
+      route->peer_y[q] = pc.base[q] + ep_off_y(E, cap_rows, d, eb);
+      if (phi[rank][q] <= plo[rank][q]) continue;
+      int64_t base = 0;
+      for (int i = 0; i < rank; ++i) base += phi[i][q] - plo[i][q];
+      route->seg_rank[ns] = q;
+      route->seg_lo[ns] = plo[rank][q];
+      route->seg_hi[ns] = phi[rank][q];
+      route->seg_base[ns] = base;
+      route->seg_limit[ns] = max(static_cast<int64_t>(0), cap_tiles - base);  // never write past q's buffer
+      ++ns;
     }
-    route->send_tile_start[world] = st;
-    // Receive side: tiles from source i (in order), expert-major within i.
-    int64_t off = 0;
-    for (int i = 0; i < world; ++i)
-      for (int e = 0; e < E; ++e) {
-        const int64_t lo = max(g0[i][e], bounds[rank]), hi = min(g0[i][e] + tiles[i][e], bounds[rank + 1]);
-        recv_off[i][e] = off;
-        off += hi > lo ? hi - lo : 0;
-      }
-    n_recv = off;
-    if (off * 128 > cap_rows) raise_error(err, kErrRowOverflow);
-    *recv_num_tiles = static_cast<int32_t>(min(off, cap_rows / 128));
+    route->n_seg = ns;
+    int64_t n_recv = 0;
+    for (int i = 0; i < world; ++i) n_recv += phi[i][rank] - plo[i][rank];
+    if (n_recv > cap_tiles) raise_error(err, kErrRowOverflow);
+    *recv_num_tiles = static_cast<int32_t>(min(n_recv, cap_tiles));
   }
   __syncthreads();
-  // Tile table (local expert index of every received tile), in parallel.
-  for (int i = 0; i < world; ++i)
-    for (int e = 0; e < E; ++e) {
-      const int64_t lo = max(g0[i][e], bounds[rank]), hi = min(g0[i][e] + tiles[i][e], bounds[rank + 1]);
-      const int64_t n = hi > lo ? hi - lo : 0;
+  // Receive-side tile table: source i's tiles [plo, phi) in order; the expert
+  // of source i's tile t follows from its per-expert tile counts.
+  int64_t off = 0;
+  for (int i = 0; i < world; ++i) {
+    const int64_t lo = plo[i][rank], n = phi[i][rank] - lo;
+    for (int64_t j = threadIdx.x; j < n; j += blockDim.x) {
+      const int64_t t = lo + j;
+      int64_t acc = 0;
+      int e = 0;
+      while (e < E - 1 && acc + tiles[i][e] <= t) acc += tiles[i][e++];
       int le = e - first_local_expert;
       if (le < 0 || le >= n_local_experts) {
-        if (n > 0 && threadIdx.x == 0) raise_error(err, kErrBadExpert);
+        raise_error(err, kErrBadExpert);
         le = 0;
       }
-      for (int64_t t = threadIdx.x; t < n; t += blockDim.x) {
-        const int64_t slot = recv_off[i][e] + t;
-        if (slot * 128 < cap_rows) recv_tile_expert[slot] = le;
-      }
+      const int64_t slot = off + j;
+      if (slot * 128 < cap_rows) recv_tile_expert[slot] = le;
     }
+    off += n;
+  }
 }
 
 }  // namespace agm
@@ -330,7 +385,7 @@ AGM_API int agm_ep_dispatch(const void* x, int dtype, int64_t n_tokens, int d, i
     return ep_fail(AGM_ERR_UNSUPPORTED, "agm_ep_dispatch: world must be in [1, 16] and rank in [0, world)");
   if (n_experts < 1 || n_experts > AGM_MAX_EXPERTS || top_k < 1 || top_k > n_experts)
     return ep_fail(AGM_ERR_ARG, "agm_ep_dispatch: bad n_experts / top_k");
-  if (placement != 0 && placement != 1) return ep_fail(AGM_ERR_ARG, "agm_ep_dispatch: placement must be 0 or 1");
+  if (placement < 0 || placement > 2) return ep_fail(AGM_ERR_ARG, "agm_ep_dispatch: placement must be 0, 1 or 2");
   if (cap_rows <= 0 || cap_rows % 128)
     return ep_fail(AGM_ERR_ARG, "agm_ep_dispatch: cap_rows must be a multiple of 128");
   if (!peer_comm || !w_router || !workspace || (n_tokens > 0 && !x))

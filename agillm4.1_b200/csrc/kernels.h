@@ -26,21 +26,41 @@ struct GemmArgs {
   int max_ctas = 0;           // cap on persistent CTAs (0 = one per SM), leaves SMs to concurrent kernels
 };
 
-// Expert-parallel routing of one rank's permuted rows (see ep_p2p.cu). The
-// rank's x_perm tiles [send_tile_start[r], send_tile_start[r+1]) go to rank r,
-// landing at tile dest_tile_base[r] of r's receive buffer; peer_recv/peer_y
-// are the device addresses of every rank's receive and result buffers as
-// mapped into this process.
+// Expert-parallel routing of one rank's permuted rows (see ep_p2p.cu): a list
+// of segments of its x_perm tiles; segment s sends tiles [seg_lo, seg_hi) to
+// rank seg_rank, landing at tile seg_base of that rank's receive buffer
+// (at most seg_limit tiles fit). peer_recv/peer_y are the device addresses of
+// every rank's receive and result buffers as mapped into this process.
 constexpr int kEpMaxRanks = 16;
+constexpr int kEpMaxSegs = 2 * kEpMaxRanks;
 struct EpRoute {
   int world;
   int rank;
-  int64_t send_tile_start[kEpMaxRanks + 1];
-  int64_t dest_tile_base[kEpMaxRanks];
-  int64_t send_limit[kEpMaxRanks];  // tiles that fit in rank r's receive buffer from this rank
+  int n_seg;
+  int seg_rank[kEpMaxSegs];
+  int64_t seg_lo[kEpMaxSegs];
+  int64_t seg_hi[kEpMaxSegs];
+  int64_t seg_base[kEpMaxSegs];
+  int64_t seg_limit[kEpMaxSegs];
   uint64_t peer_recv[kEpMaxRanks];
   uint64_t peer_y[kEpMaxRanks];
 };
+
+// Address of permuted row p on the rank that computes it: base[] is peer_recv
+// or peer_y. nullptr if the row is not sent (or would overflow).
+__device__ __forceinline__ int64_t ep_dest_row(const EpRoute* route, int64_t p, int* dest_rank) {
+  const int64_t t = p >> 7;
+  const int n = route->n_seg;
+  for (int s = 0; s < n; ++s) {
+    const int64_t lo = route->seg_lo[s], hi = route->seg_hi[s];
+    if (t >= lo && t < hi) {
+      if (t - lo >= route->seg_limit[s]) return -1;
+      *dest_rank = route->seg_rank[s];
+      return (route->seg_base[s] + (t - lo)) * 128 + (p & 127);
+    }
+  }
+  return -1;
+}
 
 // Destination row of permuted row p on its receiving rank (nullptr if p is
 // not sent). Rows are 16-byte chunked (nchunk chunks per row).
@@ -49,17 +69,9 @@ struct EpRows {
   const EpRoute* route;
   int nchunk;
   __device__ __forceinline__ uint4* row(int64_t p) const {
-    const int64_t t = p >> 7;
-    const int w = route->world;
-    for (int r = 0; r < w; ++r) {
-      const int64_t lo = route->send_tile_start[r], hi = route->send_tile_start[r + 1];
-      if (t >= lo && t < hi) {
-        if (t - lo >= route->send_limit[r]) return nullptr;  // would overflow rank r's buffer
-        const int64_t drow = (route->dest_tile_base[r] + (t - lo)) * 128 + (p & 127);
-        return reinterpret_cast<uint4*>(route->peer_recv[r]) + drow * nchunk;
-      }
-    }
-    return nullptr;
+    int r = 0;
+    const int64_t drow = ep_dest_row(route, p, &r);
+    return drow < 0 ? nullptr : reinterpret_cast<uint4*>(route->peer_recv[r]) + drow * nchunk;
   }
 };
 

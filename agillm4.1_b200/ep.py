@@ -25,6 +25,10 @@ Placement:
   sequence is cut into P near-equal ranges, so a hot expert's tiles are spread
   over several ranks (skewed routing stays balanced; results are unchanged
   because rows are independent).
+* ``"local"`` (peer-memory forward only): every rank holds all expert weights
+  and computes its own tiles up to an equal share of the total; only the
+  excess moves (to the ranks below their share), so the exchange carries just
+  the imbalance between the ranks' token counts.
 
 Rows are independent in the MoE block, so the output of every token is
 bit-identical to the single-GPU forward of the same token.
@@ -67,6 +71,48 @@ class DispatchPlan:
     recv_tile_expert: np.ndarray
     tile_ranges: np.ndarray
     local_rows: int
+
+
+def plan_pieces(counts_all: np.ndarray, placement: str) -> np.ndarray:
+    """Pieces [P, P, 2]: source i sends its x_perm tiles [lo, hi) to rank r.
+
+    The same plan the device computes for the peer-memory forward:
+    "static"/"balanced" cut the global (expert, source, tile) sequence into
+    contiguous rank ranges; "local" gives every rank an equal share of all
+    tiles, lets each source keep its first min(own, share) tiles and sends the
+    rest, in order, to the ranks below their share (lowest rank first).
+    """
+    counts_all = np.asarray(counts_all, dtype=np.int64)
+    P, E = counts_all.shape
+    tiles = (counts_all + TILE - 1) // TILE
+    T = tiles.sum(axis=1)
+    total = int(T.sum())
+    pieces = np.zeros((P, P, 2), dtype=np.int64)
+    if placement == "local":
+        quota = np.array([total // P + (1 if r < total % P else 0) for r in range(P)], dtype=np.int64)
+        keep = np.minimum(T, quota)
+        deficit = quota - keep
+        for r in range(P):
+            pieces[r, r] = (0, keep[r])
+        r = 0
+        for i in range(P):
+            pos = int(keep[i])
+            while pos < T[i]:
+                while r < P and deficit[r] == 0:
+                    r += 1
+                n = int(min(T[i] - pos, deficit[r]))
+                pieces[i, r] = (pos, pos + n)
+                pos += n
+                deficit[r] -= n
+        return pieces
+    for i in range(P):
+        plan = plan_dispatch(counts_all, i, placement)
+        start = 0
+        for r in range(P):
+            n = plan.send_rows[r] // TILE
+            pieces[i, r] = (start, start + n)
+            start += n
+    return pieces
 
 
 def plan_dispatch(counts_all: np.ndarray, rank: int, placement: str = "static") -> DispatchPlan:
@@ -153,7 +199,7 @@ class ExpertParallelMoE:
     @staticmethod
     def shard_weights(w1, b1, w2, b2, rank: int, world: int, placement: str):
         """The expert weights a rank keeps for a placement."""
-        if placement == "balanced":
+        if placement in ("balanced", "local"):
             return w1, b1, w2, b2
         r = static_owner_ranges(w1.shape[0], world)[rank]
         return (w1[r.start:r.stop].contiguous(), b1[r.start:r.stop].contiguous(),
@@ -279,7 +325,7 @@ class P2PExpertParallelMoE:
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.placement = placement
-        self.pl_code = {"static": 0, "balanced": 1}[placement]
+        self.pl_code = {"static": 0, "balanced": 1, "local": 2}[placement]
         if placement == "static":
             r = static_owner_ranges(self.E, self.world)[self.rank]
             self.first_local, self.n_local = r.start, len(r)
@@ -296,7 +342,7 @@ class P2PExpertParallelMoE:
         self.chunk_tokens = (self.max_tokens + self.chunks - 1) // self.chunks
         rows = ops.max_rows(self.chunk_tokens, self.top_k, self.E)
         if cap_rows is None:
-            cap_rows = 2 * rows if placement == "balanced" else self.world * rows
+            cap_rows = self.world * rows if placement == "static" else 2 * rows
         self.cap_rows = (int(cap_rows) + TILE - 1) // TILE * TILE
         n_slots = 1 if self.chunks == 1 else 2
         self.slots = [_CommSlot(self.lib, _lib, group, self.world, self.rank, self.E, self.cap_rows, self.d, self.H,

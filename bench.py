@@ -298,11 +298,14 @@ def run_ep(args, world, rank, local):
 
     Skewed workload: every rank holds B x L tokens of its own (input seed
     3 + 1000*rank); all ranks share the weights (seed 3) whose router carries
-    the Zipf logit bias. Headline: rows moved inside the permute/combine
-    kernels over NVLink peer memory ("p2p"), "balanced" placement (hot
-    experts' tiles spread over ranks). Also reported: the static ownership
-    7/7, 4/4/3/3, 2x6+1x2, and both placements with NCCL all-to-all between
-    the kernels (per-stage CUDA-event times for those).
+    the Zipf logit bias. Rows move inside the permute/combine kernels over
+    NVLink peer memory ("p2p"). Headline: the fastest bit-exact p2p variant;
+    reported per variant: "local" (all experts on every rank, each rank keeps
+    its own tiles up to an equal share, only the excess moves), "balanced"
+    (global tile sequence cut evenly: hot experts' tiles spread over all
+    ranks, most rows cross NVLink), "static" (ownership 7/7, 4/4/3/3,
+    2x6+1x2), "balanced_overlap" (4 token chunks overlapped on two streams),
+    and the NCCL all-to-all variants.
     """
     import torch.distributed as dist
 
@@ -331,7 +334,8 @@ def run_ep(args, world, rank, local):
     counts_all = torch.empty(world * EXPERTS, dtype=torch.int32, device=dev)
     dist.all_gather_into_tensor(counts_all, counts)
     counts_all = counts_all.cpu().numpy().reshape(world, EXPERTS)
-    for variant in ("p2p_balanced_overlap", "p2p_balanced", "p2p_static", "nccl_balanced", "nccl_static"):
+    for variant in ("p2p_local", "p2p_balanced", "p2p_static", "p2p_balanced_overlap", "nccl_balanced",
+                    "nccl_static"):
         kind, placement = variant.split("_")[:2]
         overlap = variant.endswith("_overlap")
         mine = ep.ExpertParallelMoE.shard_weights(w1, b1, w2, b2, rank, world, placement)
@@ -375,7 +379,11 @@ def run_ep(args, world, rank, local):
             err = moe.device_error()
             same = same and err == 0
             moe.close()
-        works = [ep.plan_dispatch(counts_all, r, placement).recv_tile_expert.size for r in range(world)]
+        if placement == "local":
+            pieces = ep.plan_pieces(counts_all, "local")
+            works = [int((pieces[:, r, 1] - pieces[:, r, 0]).sum()) for r in range(world)]
+        else:
+            works = [ep.plan_dispatch(counts_all, r, placement).recv_tile_expert.size for r in range(world)]
         ok = torch.tensor([1.0 if same else 0.0], device=dev)
         dist.all_reduce(ok, op=dist.ReduceOp.MIN)
         results[variant] = dict(value=N * world * args.steps / (ms / 1000.0), ms_per_step=ms / args.steps,
@@ -412,7 +420,8 @@ def run_ep(args, world, rank, local):
     if rank != 0:
         return
     peaks = load_peaks()
-    ok_p2p = [k_ for k_ in ("p2p_balanced_overlap", "p2p_balanced") if results[k_]["bit_identical_to_single_gpu"]]
+    ok_p2p = [k_ for k_ in ("p2p_local", "p2p_balanced_overlap", "p2p_balanced")
+              if results[k_]["bit_identical_to_single_gpu"]]
     head_name = max(ok_p2p or ["p2p_balanced"], key=lambda k_: results[k_]["value"])
     head = results[head_name]
     stages = results["p2p_balanced"]["stages_ms"]

@@ -216,7 +216,9 @@ AGM_API size_t agm_ep_workspace_bytes(int64_t n_tokens, int d, int n_experts, in
  * starting at first_local_expert. placement 0 = static contiguous ownership
  * (first E mod P ranks own one more expert), 1 = balanced (every rank holds
  * all experts; the global tile sequence is split evenly, hot experts span
- * ranks). peer_comm: HOST array of `world` device addresses of every rank's
+ * ranks), 2 = local (every rank holds all experts and computes its own tiles
+ * up to an equal share of the total; only the excess moves to ranks below
+ * their share). peer_comm: HOST array of `world` device addresses of every rank's
  * communication buffer as mapped here (own buffer at [rank]). The counts
  * exchange and three barriers are flag writes in peer memory, bounded waits
  * (a time-out sets the device error word, the first int of the workspace).

@@ -92,3 +92,26 @@ def test_plan_static_ownership_and_balance():
         else:
             for r in range(P):
                 assert set(plans[r].recv_tile_expert.tolist()) <= set(owners[r])
+
+
+def test_local_plan_pieces():
+    """Locality-first plan: pieces partition each source's tiles, every rank
+    gets an equal share, and only the excess over a rank's share moves."""
+    rng = np.random.default_rng(1)
+    for P in (2, 3, 8):
+        counts = rng.integers(0, 4000, size=(P, 14))
+        counts[0] *= 3                                    # one rank with many more tokens
+        tiles = ((counts + 127) // 128).sum(axis=1)
+        pieces = ep.plan_pieces(counts, "local")
+        total = tiles.sum()
+        for i in range(P):
+            spans = sorted((lo, hi) for lo, hi in pieces[i] if hi > lo)
+            assert spans[0][0] == 0 and spans[-1][1] == tiles[i]
+            assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+        load = (pieces[:, :, 1] - pieces[:, :, 0]).sum(axis=0)
+        assert load.max() - load.min() <= 1 and load.sum() == total
+        moved = sum(pieces[i, r, 1] - pieces[i, r, 0] for i in range(P) for r in range(P) if r != i)
+        share = total // P
+        assert moved <= np.maximum(tiles - share, 0).sum()
+        same = ep.plan_pieces(np.tile(counts[1], (P, 1)), "local")
+        assert all(same[i, r, 1] == same[i, r, 0] for i in range(P) for r in range(P) if r != i)

@@ -50,7 +50,8 @@ def _worker(rank, world, port, q):
             out2 = moe.forward(x)
             torch.cuda.synchronize()
             res[placement] = (bool(torch.equal(out, ref)), bool(torch.equal(out, out2)))
-        for placement, chunks in (("static", 1), ("balanced", 1), ("balanced", 2), ("static", 3)):
+        for placement, chunks in (("static", 1), ("balanced", 1), ("local", 1), ("balanced", 2), ("static", 3),
+                                  ("local", 2)):
             mine = ep.ExpertParallelMoE.shard_weights(*w, rank, world, placement)
             moe = ep.P2PExpertParallelMoE((wr,) + tuple(mine), k, E, max_tokens=4000, placement=placement,
                                           chunks=chunks)
@@ -103,7 +104,7 @@ def test_p2p_path_single_rank():
         w = [torch.stack([sd[f"experts.{e}.{i}.{p}"] for e in range(E)]).contiguous()
              for i, p in ((0, "weight"), (0, "bias"), (2, "weight"), (2, "bias"))]
         wr = sd["router.weight"].contiguous()
-        for placement, chunks in (("static", 1), ("balanced", 1), ("balanced", 3)):
+        for placement, chunks in (("static", 1), ("balanced", 1), ("local", 1), ("balanced", 3)):
             moe = ep.P2PExpertParallelMoE((wr,) + tuple(w), k, E, max_tokens=5000, placement=placement,
                                           chunks=chunks)
             for n in (4096, 1, 777, 5000):
