@@ -18,7 +18,7 @@
 // one CTA per 128 tokens, 4 tokens per warp iteration, 16-byte vector loads
 // and a transpose-reduce over the lanes.
 //
-// Both kernels share the per-token selection (route_token): it follows
+// Both kernels share the per-token selection (route_warp): it follows
 // torch.topk and torch's warp softmax so gates match bit for bit when the
 // logits do, and writes one histogram row per 128-token dispatch block.
 #include <algorithm>
@@ -65,100 +65,179 @@ __device__ __forceinline__ float butterfly_sum_rt(const float* e, int w) {
   }
 }
 
-// Top-k selection reproducing torch.topk(sorted=True) on a CUDA device:
-// the selected set is every value greater than the k-th largest plus, among
-// the values equal to it, the lowest expert indices; the result is ordered by
-// descending value and, among exactly-equal values, by DESCENDING expert
-// index (measured on B200 with torch 2.11 for k = 2 and 3: 100% of ~120k
-// tied rows). `low_first` orders exactly-equal values by ascending index
-// instead.
-__device__ __forceinline__ void select_topk(const float* logit, int E, int k, bool low_first, int* sel,
-                                            float* val) {
-  uint32_t taken = 0;
-  for (int r = 0; r < k; ++r) {
-    int best = -1;
-    float bv = 0.f;
-    for (int e = 0; e < E; ++e) {
-      if (taken & (1u << e)) continue;
-      const float v = logit[e];
-      // NaN compares greater than everything in torch's topk ordering.
-      const bool better = (best < 0) || (v > bv) || (isnan(v) && !isnan(bv));
-      if (better) { best = e; bv = v; }
-    }
-    taken |= 1u << best;
-    sel[r] = best;
-    val[r] = bv;
-  }
-  if (!low_first) {
-    // Reverse every run of exactly-equal values (ascending -> descending index).
-    int r = 0;
-    while (r < k) {
-      int r2 = r + 1;
-      while (r2 < k && val[r2] == val[r]) ++r2;
-      for (int a = r, b = r2 - 1; a < b; ++a, --b) {
-        const int t = sel[a]; sel[a] = sel[b]; sel[b] = t;
-      }
-      r = r2;
-    }
-  }
-}
+constexpr int pow2_ceil(int n) { return n <= 1 ? 1 : 2 * pow2_ceil((n + 1) / 2); }
 
-// Selection, gates and histogram for one token whose fp32 logits (already
-// rounded like the reference's router output) are lg[0..E).
-template <typename T>
-__device__ __forceinline__ void route_token(const float* lg, int E, int k, bool low_first, int64_t tok,
-                                            float* __restrict__ logits_out, int32_t* __restrict__ idx_out,
-                                            T* __restrict__ gates_out, int* hist_s, int* err) {
-  if (logits_out) {
-    for (int e = 0; e < E; ++e) logits_out[tok * E + e] = lg[e];
+// Per-token selection state: top_k = KC in 1..4 is a compile-time constant
+// (arrays of pow2_ceil(KC)); KC = 0 takes top_k at run time (arrays of 16).
+// Every loop is fully unrolled with predicates so the arrays stay in registers.
+template <int KC>
+struct RouteK {
+  static constexpr int S = KC > 0 ? pow2_ceil(KC) : kMaxExperts;
+};
+constexpr int kFastTopK = 4;
+
+// Selection and gates of one token from its fp32 logits lg[0..E) (already
+// rounded like the reference's router output).
+//
+// top-k (k >= 2) reproduces torch.topk(sorted=True) on a CUDA device: the
+// selected set is every value greater than the k-th largest plus, among the
+// values equal to it, the lowest expert indices; the result is ordered by
+// descending value and, among exactly-equal values, by DESCENDING expert
+// index (measured on B200 with torch 2.11 for k = 2 and 3: 100% of ~120k tied
+// rows). `low_first` orders exactly-equal values by ascending index instead.
+// The gates are softmax over the k chosen values (agillm41.py:4417-4419).
+//
+// top-1: probs = softmax(scores) (torch's warp softmax over next_pow2(E)
+// lanes, padding contributes exp(-inf) = 0), chosen = argmax(probs), first
+// index on ties, straight-through gate 1 (agillm41.py:4401-4416).
+template <int KC>
+__device__ __forceinline__ void select_route(const float (&lg)[kMaxExperts], int E, int k, bool low_first,
+                                             int (&sel)[RouteK<KC>::S], float (&gate)[RouteK<KC>::S]) {
+  constexpr int S = RouteK<KC>::S;
+  if (KC > 0) k = KC;
+#pragma unroll
+  for (int r = 0; r < S; ++r) {
+    sel[r] = -1;
+    gate[r] = 0.f;
   }
-  int sel[kMaxExperts];
-  float gate[kMaxExperts];
   if (k == 1) {
-    // probs = softmax(scores) (warp softmax over next_pow2(E) lanes, padding
-    // contributes exp(-inf) = 0), chosen = argmax(probs), first index on ties.
     float m = lg[0];
-    for (int e = 1; e < E; ++e) m = fmaxf(m, lg[e]);
+#pragma unroll
+    for (int e = 1; e < kMaxExperts; ++e)
+      if (e < E) m = fmaxf(m, lg[e]);
     float ex[kMaxExperts];
 #pragma unroll
     for (int e = 0; e < kMaxExperts; ++e) ex[e] = (e < E) ? expf(lg[e] - m) : 0.f;
     const float s = butterfly_sum_rt(ex, next_pow2_le32(E));
     int best = 0;
     float bp = ex[0] / s;
-    for (int e = 1; e < E; ++e) {
-      const float p = ex[e] / s;
-      if (p > bp || (isnan(p) && !isnan(bp))) { bp = p; best = e; }
+#pragma unroll
+    for (int e = 1; e < kMaxExperts; ++e) {
+      if (e < E) {
+        const float p = ex[e] / s;
+        if (p > bp || (isnan(p) && !isnan(bp))) {
+          bp = p;
+          best = e;
+        }
+      }
     }
     sel[0] = best;
-    gate[0] = 1.f;  // straight-through gate: gate / gate.detach() == 1
-  } else {
-    float val[kMaxExperts];
-    select_topk(lg, E, k, low_first, sel, val);
-    // softmax over the k values (sorted descending, so val[0] is the max).
-    float m = val[0];
-    for (int r = 1; r < k; ++r) m = fmaxf(m, val[r]);
-    float ex[kMaxExperts];
+    gate[0] = 1.f;  // gate / gate.detach() == 1
+    return;
+  }
+  float val[S];
+  uint32_t taken = 0;
 #pragma unroll
-    for (int r = 0; r < kMaxExperts; ++r) ex[r] = (r < k) ? expf(val[r] - m) : 0.f;
-    const float s = butterfly_sum_rt(ex, next_pow2_le32(k));
-    for (int r = 0; r < k; ++r) gate[r] = ex[r] / s;
-  }
-  for (int r = 0; r < k; ++r) {
-    const int e = sel[r];
-    if (e < 0 || e >= E) {
-      raise_error(err, kErrBadExpert);
-      continue;
+  for (int r = 0; r < S; ++r) {
+    val[r] = 0.f;
+    if (r < k) {
+      int best = -1;
+      float bv = 0.f;
+#pragma unroll
+      for (int e = 0; e < kMaxExperts; ++e) {
+        if (e < E && !((taken >> e) & 1u)) {
+          const float v = lg[e];
+          // NaN compares greater than everything in torch's topk ordering.
+          if (best < 0 || v > bv || (isnan(v) && !isnan(bv))) {
+            best = e;
+            bv = v;
+          }
+        }
+      }
+      if (best >= 0) taken |= 1u << best;
+      sel[r] = best;
+      val[r] = bv;
     }
-    idx_out[tok * k + r] = e;
-    gates_out[tok * k + r] = Traits<T>::from_f(gate[r]);
-    atomicAdd(&hist_s[e], 1);
   }
+  if (!low_first) {
+    // Runs of exactly-equal values come out in ascending index order; an
+    // odd-even pass sort that only swaps equal neighbours reverses each run.
+#pragma unroll
+    for (int pass = 0; pass < S; ++pass) {
+#pragma unroll
+      for (int j = pass & 1; j + 1 < S; j += 2) {
+        if (j + 1 < k && val[j] == val[j + 1] && sel[j] < sel[j + 1]) {
+          const int t = sel[j];
+          sel[j] = sel[j + 1];
+          sel[j + 1] = t;
+        }
+      }
+    }
+  }
+  // softmax over the k values (sorted descending, so val[0] is the max).
+  float m = val[0];
+#pragma unroll
+  for (int r = 1; r < S; ++r)
+    if (r < k) m = fmaxf(m, val[r]);
+  float ex[S];
+#pragma unroll
+  for (int r = 0; r < S; ++r) ex[r] = (r < k) ? expf(val[r] - m) : 0.f;
+  float s;
+  if constexpr (KC > 0) {
+    s = butterfly_sum<S>(ex);
+  } else {
+    s = butterfly_sum_rt(ex, next_pow2_le32(k));
+  }
+#pragma unroll
+  for (int r = 0; r < S; ++r)
+    if (r < k) gate[r] = ex[r] / s;
+}
+
+// One warp's 32 tokens (one per lane; `valid` false past the end): writes the
+// logits (optional), expert indices and gates, and the warp's expert counts
+// into hist_row[0..16) from ballots, without shared-memory atomics.
+template <typename T, int KC>
+__device__ __forceinline__ void route_warp(const float (&lg)[kMaxExperts], bool valid, int E, int k, bool low_first,
+                                           int64_t tok, float* __restrict__ logits_out,
+                                           int32_t* __restrict__ idx_out, T* __restrict__ gates_out, int* hist_row,
+                                           int* err) {
+  constexpr int S = RouteK<KC>::S;
+  if (KC > 0) k = KC;
+  int sel[S];
+  float gate[S];
+  if (valid) {
+    if (logits_out) {
+#pragma unroll
+      for (int e = 0; e < kMaxExperts; ++e)
+        if (e < E) logits_out[tok * E + e] = lg[e];
+    }
+    select_route<KC>(lg, E, k, low_first, sel, gate);
+#pragma unroll
+    for (int r = 0; r < S; ++r) {
+      if (r < k) {
+        const int e = sel[r];
+        if (e < 0 || e >= E) {
+          raise_error(err, kErrBadExpert);
+          sel[r] = -1;
+        } else {
+          idx_out[tok * k + r] = e;
+          gates_out[tok * k + r] = Traits<T>::from_f(gate[r]);
+        }
+      }
+    }
+  } else {
+#pragma unroll
+    for (int r = 0; r < S; ++r) sel[r] = -1;
+  }
+  const int lane = lane_id();
+  int c = 0;
+#pragma unroll
+  for (int r = 0; r < S; ++r) {
+    if (r < k) {  // k is uniform over the warp
+#pragma unroll
+      for (int e = 0; e < kMaxExperts; ++e) {
+        const uint32_t b = __ballot_sync(0xffffffffu, sel[r] == e);
+        if (lane == e) c += __popc(b);
+      }
+    }
+  }
+  if (lane < kMaxExperts) hist_row[lane] = c;
 }
 
 // ---------------------------------------------------------------------------
 // SIMT router (fp32, or caller-supplied logits)
 // ---------------------------------------------------------------------------
-template <typename T>
+template <typename T, int KC>
 __global__ void __launch_bounds__(kDispatchBlock) router_topk_kernel(
     const T* __restrict__ x, const T* __restrict__ w, int64_t n_tokens, int d, int E, int k, int tie_low_first,
     const float* __restrict__ logits_in, float* __restrict__ logits_out, int32_t* __restrict__ idx_out,
@@ -171,11 +250,10 @@ __global__ void __launch_bounds__(kDispatchBlock) router_topk_kernel(
   // then [warps][32 tokens][16] fp32 logits.
   float* w_s = smem_f;
   float* logit_s = smem_f + (compute ? E * d : 0);
-  __shared__ int hist_s[kMaxExperts];
+  __shared__ int hist_w[kRouterWarps][kMaxExperts];
 
   const int warp = warp_id(), lane = lane_id();
   const int64_t blk_tok0 = static_cast<int64_t>(blockIdx.x) * kDispatchBlock;
-  if (threadIdx.x < kMaxExperts) hist_s[threadIdx.x] = 0;
 
   if (compute) {
     // Stage W (vectorised, 16 B per thread per step), converting to fp32.
@@ -284,14 +362,18 @@ __global__ void __launch_bounds__(kDispatchBlock) router_topk_kernel(
 
   // One thread per token: selection, gates, histogram.
   const int64_t tok = warp_tok0 + lane;
-  if (tok < n_tokens) {
-    float lg[kMaxExperts];
+  float lg[kMaxExperts];
 #pragma unroll
-    for (int e = 0; e < kMaxExperts; ++e) lg[e] = (e < E) ? my_logits[lane * kMaxExperts + e] : 0.f;
-    route_token<T>(lg, E, k, tie_low_first != 0, tok, logits_out, idx_out, gates_out, hist_s, err);
-  }
+  for (int e = 0; e < kMaxExperts; ++e) lg[e] = (e < E) ? my_logits[lane * kMaxExperts + e] : 0.f;
+  route_warp<T, KC>(lg, tok < n_tokens, E, k, tie_low_first != 0, tok, logits_out, idx_out, gates_out, hist_w[warp],
+                    err);
   __syncthreads();
-  if (threadIdx.x < E) block_hist[static_cast<int64_t>(blockIdx.x) * E + threadIdx.x] = hist_s[threadIdx.x];
+  if (threadIdx.x < E) {
+    int c = 0;
+#pragma unroll
+    for (int w = 0; w < kRouterWarps; ++w) c += hist_w[w][threadIdx.x];
+    block_hist[static_cast<int64_t>(blockIdx.x) * E + threadIdx.x] = c;
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -303,10 +385,10 @@ constexpr int kRtABytes = 128 * 64 * 2;   // one 128-token x 64-feature tile
 constexpr int kRtWBytes = 16 * 64 * 2;    // one 16-expert x 64-feature tile of the router weight
 
 __host__ __device__ constexpr int rt_smem_bytes(int nkb) {
-  return kRtStages * kRtABytes + nkb * kRtWBytes + 256 + 1024;
+  return kRtStages * kRtABytes + nkb * kRtWBytes + 1024 + 1024;
 }
 
-template <typename T>
+template <typename T, int KC>
 __global__ void __launch_bounds__(kRtThreads, 2) router_tc_kernel(
     const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, int64_t n_tokens, int d,
     int E, int k, int tie_low_first, float* __restrict__ logits_out, int32_t* __restrict__ idx_out,
@@ -325,7 +407,10 @@ __global__ void __launch_bounds__(kRtThreads, 2) router_tc_kernel(
   uint64_t* drain = w_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_s = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int* hist_s = const_cast<int*>(abort_s) + 1;  // [16]
+  // Per-warp expert counts, one set per accumulator buffer: [2][4 warps][16],
+  // then one "an epilogue warp gave up" flag per buffer.
+  int* hist_w = reinterpret_cast<int*>(bars + 16);
+  volatile int* epi_fail = hist_w + 2 * 4 * kMaxExperts;
 
   const int warp = warp_id(), lane = lane_id();
   const int num_tiles = static_cast<int>((n_tokens + 127) / 128);
@@ -342,11 +427,11 @@ __global__ void __launch_bounds__(kRtThreads, 2) router_tc_kernel(
     mbar_init(w_full, 1);
     mbar_init(drain, 1);
     *abort_s = 0;
+    epi_fail[0] = epi_fail[1] = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmX);
     tma_prefetch_desc(&tmW);
   }
-  if (threadIdx.x < kMaxExperts) hist_s[threadIdx.x] = 0;
   if (warp == 1) {
     tmem_alloc(tmem_slot, 32);
     tmem_relinquish();
@@ -434,32 +519,40 @@ __global__ void __launch_bounds__(kRtThreads, 2) router_tc_kernel(
     // ---------------- Epilogue: one thread per token ----------------
     const int quarter = warp & 3;
     int it = 0;
+    // One named barrier per tile: the four warps' counts of tile `it` sit in
+    // hist_w[acc], which is written again only by tile it + 2, after every
+    // warp has passed tile it + 1's barrier (so after the reads below). A
+    // warp that gives up still reaches the barrier and raises epi_fail[acc],
+    // so all four warps leave the loop together and none waits on the
+    // barrier for a warp that has left.
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
       const int acc = it & 1;
-      if (!mbar_wait(&acc_full[acc], (it >> 1) & 1, err, kErrTimeoutAcc) || *abort_s) {
-        *abort_s = 1;
-        break;
-      }
-      tc_fence_after();
-      uint32_t r[16];
-      tmem_ld_32x32b_x16(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * 16, r);
-      tmem_ld_wait();
-      tc_fence_before();
-      mbar_arrive(&acc_empty[acc]);  // the accumulator is in registers: release it
-      const int64_t tok = static_cast<int64_t>(t) * 128 + quarter * 32 + lane;
-      if (tok < n_tokens) {
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[acc], (it >> 1) & 1, err, kErrTimeoutAcc) &&
+                                                  !*abort_s);
+      if (ok) {
+        tc_fence_after();
+        uint32_t r[16];
+        tmem_ld_32x32b_x16(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * 16, r);
+        tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(&acc_empty[acc]);  // the accumulator is in registers: release it
+        const int64_t tok = static_cast<int64_t>(t) * 128 + quarter * 32 + lane;
         float lg[kMaxExperts];
 #pragma unroll
         for (int e = 0; e < kMaxExperts; ++e) lg[e] = round_to<T>(__uint_as_float(r[e]));
-        route_token<T>(lg, E, k, tie_low_first != 0, tok, logits_out, idx_out, gates_out, hist_s, err);
+        route_warp<T, KC>(lg, tok < n_tokens, E, k, tie_low_first != 0, tok, logits_out, idx_out, gates_out,
+                          hist_w + (acc * 4 + quarter) * kMaxExperts, err);
+      } else if (lane == 0) {
+        *abort_s = 1;
+        epi_fail[acc] = 1;
       }
       named_bar_sync(1, 128);
+      if (epi_fail[acc]) break;
       const int et = threadIdx.x - 64;  // epilogue thread index 0..127
       if (et < E) {
-        block_hist[static_cast<int64_t>(t) * E + et] = hist_s[et];
-        hist_s[et] = 0;
+        const int* h = hist_w + acc * 4 * kMaxExperts + et;
+        block_hist[static_cast<int64_t>(t) * E + et] = h[0] + h[kMaxExperts] + h[2 * kMaxExperts] + h[3 * kMaxExperts];
       }
-      named_bar_sync(1, 128);
     }
   }
 
@@ -471,7 +564,7 @@ __global__ void __launch_bounds__(kRtThreads, 2) router_tc_kernel(
   }
 }
 
-template <typename T>
+template <typename T, int KC>
 static cudaError_t launch_router_tc(const void* x, const void* w, int64_t n_tokens, int d, int E, int k,
                                     int tie_low_first, float* logits_out, int32_t* idx, void* gates,
                                     int32_t* block_hist, int* err, int num_sms, cudaStream_t stream) {
@@ -492,26 +585,26 @@ static cudaError_t launch_router_tc(const void* x, const void* w, int64_t n_toke
   }
   const int nkb = (d + 63) / 64;
   const int smem = rt_smem_bytes(nkb);
-  cudaError_t e = cudaFuncSetAttribute(router_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t e = cudaFuncSetAttribute(router_tc_kernel<T, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   const int64_t tiles = (n_tokens + 127) / 128;
   const int grid = static_cast<int>(std::min<int64_t>(tiles, 2 * num_sms));
-  router_tc_kernel<T><<<grid, kRtThreads, smem, stream>>>(tmX, tmW, n_tokens, d, E, k, tie_low_first, logits_out,
-                                                          idx, static_cast<T*>(gates), block_hist, err);
+  router_tc_kernel<T, KC><<<grid, kRtThreads, smem, stream>>>(tmX, tmW, n_tokens, d, E, k, tie_low_first,
+                                                              logits_out, idx, static_cast<T*>(gates), block_hist, err);
   return cudaGetLastError();
 }
 
-template <typename T>
+template <typename T, int KC>
 static cudaError_t launch_router(const void* x, const void* w, int64_t n_tokens, int d, int E, int k,
                                  int tie_low_first, const float* logits_in, float* logits_out, int32_t* idx,
                                  void* gates, int32_t* block_hist, int* err, cudaStream_t stream) {
   const int64_t nblk = (n_tokens + kDispatchBlock - 1) / kDispatchBlock;
   const size_t smem = (logits_in ? 0 : static_cast<size_t>(E) * d * sizeof(float)) +
                       static_cast<size_t>(kRouterWarps) * 32 * kMaxExperts * sizeof(float);
-  cudaError_t e = cudaFuncSetAttribute(router_topk_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  cudaError_t e = cudaFuncSetAttribute(router_topk_kernel<T, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  router_topk_kernel<T><<<static_cast<unsigned>(nblk), kDispatchBlock, smem, stream>>>(
+  router_topk_kernel<T, KC><<<static_cast<unsigned>(nblk), kDispatchBlock, smem, stream>>>(
       static_cast<const T*>(x), static_cast<const T*>(w), n_tokens, d, E, k, tie_low_first, logits_in, logits_out,
       idx, static_cast<T*>(gates), block_hist, err);
   return cudaGetLastError();
@@ -521,6 +614,38 @@ static cudaError_t launch_router(const void* x, const void* w, int64_t n_tokens,
 // 8-stage x ring: d up to 4096 (64 k-blocks of 2 KB) fits in shared memory.
 bool router_tc_supported(int d) { return d > 0 && d % 8 == 0 && rt_smem_bytes((d + 63) / 64) <= 227 * 1024; }
 
+// One kernel per (dtype, top_k <= 4); larger top_k takes it at run time.
+template <typename T, int KC>
+static cudaError_t launch_any(bool tc, const void* x, const void* w, int64_t n_tokens, int d, int E, int k,
+                              int tie_low_first, const float* logits_in, float* logits_out, int32_t* idx, void* gates,
+                              int32_t* block_hist, int* err, int num_sms, cudaStream_t stream) {
+  if constexpr (sizeof(T) == 2) {
+    if (tc)
+      return launch_router_tc<T, KC>(x, w, n_tokens, d, E, k, tie_low_first, logits_out, idx, gates, block_hist, err,
+                                     num_sms, stream);
+  }
+  return launch_router<T, KC>(x, w, n_tokens, d, E, k, tie_low_first, logits_in, logits_out, idx, gates, block_hist,
+                              err, stream);
+}
+
+template <typename T>
+static cudaError_t launch_k(bool tc, const void* x, const void* w, int64_t n_tokens, int d, int E, int k,
+                            int tie_low_first, const float* logits_in, float* logits_out, int32_t* idx, void* gates,
+                            int32_t* block_hist, int* err, int num_sms, cudaStream_t stream) {
+#define AGM_ROUTER_K(KC)                                                                                       \
+  return launch_any<T, KC>(tc, x, w, n_tokens, d, E, k, tie_low_first, logits_in, logits_out, idx, gates, \
+                           block_hist, err, num_sms, stream)
+  static_assert(kFastTopK == 4, "one case per compiled top_k");
+  switch (k) {
+    case 1: AGM_ROUTER_K(1);
+    case 2: AGM_ROUTER_K(2);
+    case 3: AGM_ROUTER_K(3);
+    case 4: AGM_ROUTER_K(4);
+    default: AGM_ROUTER_K(0);
+  }
+#undef AGM_ROUTER_K
+}
+
 cudaError_t router_topk(int dtype, const void* x, const void* w, int64_t n_tokens, int d, int E, int k,
                         int tie_low_first, const float* logits_in, float* logits_out, int32_t* idx, void* gates,
                         int32_t* block_hist, int* err, int num_sms, cudaStream_t stream) {
@@ -528,20 +653,14 @@ cudaError_t router_topk(int dtype, const void* x, const void* w, int64_t n_token
   const bool tc = !logits_in && router_tc_supported(d);
   switch (dtype) {
     case AGM_F32:
-      return launch_router<float>(x, w, n_tokens, d, E, k, tie_low_first, logits_in, logits_out, idx, gates,
-                                  block_hist, err, stream);
+      return launch_k<float>(false, x, w, n_tokens, d, E, k, tie_low_first, logits_in, logits_out, idx, gates,
+                             block_hist, err, num_sms, stream);
     case AGM_BF16:
-      if (tc)
-        return launch_router_tc<__nv_bfloat16>(x, w, n_tokens, d, E, k, tie_low_first, logits_out, idx, gates,
-                                               block_hist, err, num_sms, stream);
-      return launch_router<__nv_bfloat16>(x, w, n_tokens, d, E, k, tie_low_first, logits_in, logits_out, idx, gates,
-                                          block_hist, err, stream);
+      return launch_k<__nv_bfloat16>(tc, x, w, n_tokens, d, E, k, tie_low_first, logits_in, logits_out, idx, gates,
+                                     block_hist, err, num_sms, stream);
     case AGM_F16:
-      if (tc)
-        return launch_router_tc<__half>(x, w, n_tokens, d, E, k, tie_low_first, logits_out, idx, gates, block_hist,
-                                        err, num_sms, stream);
-      return launch_router<__half>(x, w, n_tokens, d, E, k, tie_low_first, logits_in, logits_out, idx, gates,
-                                   block_hist, err, stream);
+      return launch_k<__half>(tc, x, w, n_tokens, d, E, k, tie_low_first, logits_in, logits_out, idx, gates,
+                              block_hist, err, num_sms, stream);
     default:
       return cudaErrorInvalidValue;
   }
