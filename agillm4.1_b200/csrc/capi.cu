@@ -2,7 +2,10 @@
 // launch sequence that replaces MoEFFN.forward (agillm41.py:4389-4431).
 #include <algorithm>
 #include <cstdio>
+#include <map>
+#include <mutex>
 #include <string>
+#include <utility>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -129,6 +132,20 @@ FwdLayout carve(void* ws, int64_t n, int d, int E, int k, int H, int S, int Hs, 
 
 namespace agm {
 void set_last_error(const std::string& msg) { g_err = msg; }
+
+cudaError_t ensure_dynamic_smem(const void* func, int bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  int& have = done[{func, dev}];
+  if (have >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) have = bytes;
+  return e;
+}
 }  // namespace agm
 
 extern "C" {

@@ -425,8 +425,8 @@ static cudaError_t launch_tc(const void* a, int64_t a_rows, const void* w, const
     const uint32_t box[2] = {64, 32};
     if (!encode_tmap(&tmC, args.c, 2, dims, str, box, dt)) return cudaErrorInvalidValue;
   }
-  cudaError_t e = cudaFuncSetAttribute(grouped_gemm_tc_kernel<T, BN, RELU>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+  cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(grouped_gemm_tc_kernel<T, BN, RELU>),
+                                      Cfg::SMEM_BYTES);
   if (e != cudaSuccess) return e;
   const int num_n = (args.n + BN - 1) / BN;
   const int64_t max_total = static_cast<int64_t>(args.max_tiles) * num_n;

@@ -83,6 +83,11 @@ bool encode_tmap(CUtensorMap* m, const void* base, int rank, const uint64_t* dim
 // Set the message returned by agm_last_error() (thread-local).
 void set_last_error(const std::string& msg);
 
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device)
+// and size: later calls that need no more shared memory make no CUDA call, so
+// a forward issued inside a stream capture only enqueues work.
+cudaError_t ensure_dynamic_smem(const void* func, int bytes);
+
 cudaError_t router_topk(int dtype, const void* x, const void* w, int64_t n_tokens, int d, int E, int k,
                         int tie_low_first, const float* logits_in, float* logits_out, int32_t* idx, void* gates,
                         int32_t* block_hist, int* err, int num_sms, cudaStream_t stream);

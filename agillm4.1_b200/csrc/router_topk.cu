@@ -585,7 +585,7 @@ static cudaError_t launch_router_tc(const void* x, const void* w, int64_t n_toke
   }
   const int nkb = (d + 63) / 64;
   const int smem = rt_smem_bytes(nkb);
-  cudaError_t e = cudaFuncSetAttribute(router_tc_kernel<T, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(router_tc_kernel<T, KC>), smem);
   if (e != cudaSuccess) return e;
   const int64_t tiles = (n_tokens + 127) / 128;
   const int grid = static_cast<int>(std::min<int64_t>(tiles, 2 * num_sms));
@@ -601,8 +601,7 @@ static cudaError_t launch_router(const void* x, const void* w, int64_t n_tokens,
   const int64_t nblk = (n_tokens + kDispatchBlock - 1) / kDispatchBlock;
   const size_t smem = (logits_in ? 0 : static_cast<size_t>(E) * d * sizeof(float)) +
                       static_cast<size_t>(kRouterWarps) * 32 * kMaxExperts * sizeof(float);
-  cudaError_t e = cudaFuncSetAttribute(router_topk_kernel<T, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
+  cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(router_topk_kernel<T, KC>), static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   router_topk_kernel<T, KC><<<static_cast<unsigned>(nblk), kDispatchBlock, smem, stream>>>(
       static_cast<const T*>(x), static_cast<const T*>(w), n_tokens, d, E, k, tie_low_first, logits_in, logits_out,

@@ -290,7 +290,8 @@ def run_ours(args, world, rank, local):
         e2e_value = None
     else:
         e2e_value = run_e2e(args, world, dev, sd, x, out, N, stream)
-    report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e_value, x)
+    decode = None if args.skip_decode else run_decode(args, dev, stream)
+    report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e_value, x, decode)
 
 
 def run_ep(args, world, rank, local):
@@ -509,7 +510,106 @@ def run_e2e(args, world, dev, sd, x, out, N, stream):
             "sequential_copy_forward_copy": seq}
 
 
-def report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e, x):
+DECODE_LAYERS, DECODE_BATCH, DECODE_SEED = 28, 64, 2
+
+
+def run_decode(args, dev, stream):
+    """AR decode shape: 28 MoE layers (independent random-init weights,
+    N(0, 0.02^2), seeds 1000 + layer) over 64 sequences x 1 new token; the
+    input of layer l is the output of layer l-1 plus an N(0, 1) perturbation
+    (seed 2). One step = all 28 layers. Timed eagerly and as one CUDA graph
+    replay (the forward has no host synchronisation, so the 28 layers
+    capture into a single graph). Roofline: the step must stream every
+    active expert's weights once (Sum over layers and active experts of
+    W1 + b1 + W2 + b2 bytes); 28 x 229.5 MB > L2, so no flush is needed.
+    """
+    from agillm41_b200 import ops, synthetic
+
+    E, k, B = EXPERTS, TOP_K, DECODE_BATCH
+    layers = []
+    for layer in range(DECODE_LAYERS):
+        sd = synthetic.make_state(D, HIDDEN, E, 1000 + layer, dtype=torch.bfloat16, device=dev)
+        layers.append((sd["router.weight"].contiguous(),
+                       torch.stack([sd[f"experts.{e}.0.weight"] for e in range(E)]).contiguous(),
+                       torch.stack([sd[f"experts.{e}.0.bias"] for e in range(E)]).contiguous(),
+                       torch.stack([sd[f"experts.{e}.2.weight"] for e in range(E)]).contiguous(),
+                       torch.stack([sd[f"experts.{e}.2.bias"] for e in range(E)]).contiguous()))
+        del sd
+    g = torch.Generator(device="cpu").manual_seed(DECODE_SEED)
+    x0 = torch.randn(B, D, generator=g).to(torch.bfloat16).to(dev)
+    noise = [torch.randn(B, D, generator=g).to(torch.bfloat16).to(dev) for _ in range(DECODE_LAYERS)]
+    xs = [torch.empty(B, D, dtype=torch.bfloat16, device=dev) for _ in range(DECODE_LAYERS + 1)]
+    outs = [torch.empty(B, D, dtype=torch.bfloat16, device=dev) for _ in range(DECODE_LAYERS)]
+    counts = [torch.empty(E, dtype=torch.int32, device=dev) for _ in range(DECODE_LAYERS)]
+    ws = torch.empty(ops.workspace_bytes(B, D, E, k, HIDDEN, 0, 1, torch.bfloat16), dtype=torch.uint8, device=dev)
+    lib = ops.load()
+
+    def step():
+        xs[0].copy_(x0)
+        for layer, (wr, w1, b1, w2, b2) in enumerate(layers):
+            # counts are written by the forward (no host read) so the active experts can be summed afterwards
+            rc = lib.agm_moe_forward(
+                ops.ptr(xs[layer]), ops.dtype_code(torch.bfloat16), B, D, E, k, HIDDEN, ops.ptr(wr), ops.ptr(w1),
+                ops.ptr(b1), ops.ptr(w2), ops.ptr(b2), 0, 1, None, None, None, None, ops.ptr(outs[layer]),
+                ops.ptr(ws), ws.numel(), 0, None, None, ops.ptr(counts[layer]), None, None, None,
+                torch.cuda.current_stream(dev).cuda_stream)
+            ops.check(rc, "agm_moe_forward")
+            torch.add(outs[layer], noise[layer], out=xs[layer + 1])
+
+    def timed(fn, steps):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(torch.cuda.current_stream(dev))
+        for _ in range(steps):
+            fn()
+        e1.record(torch.cuda.current_stream(dev))
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    steps = max(10, min(args.steps, 50))
+    eager_ms = timed(step, steps)
+    err = ops._lib.read_device_error(ws[:4].view(torch.int32))
+    if err:
+        raise RuntimeError(f"device error word 0x{err:x} in the decode leg")
+    ref_out = xs[-1].clone()
+    graph_ms = None
+    try:
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            step()                       # one call on the capture stream before capturing
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        graph_ms = timed(graph.replay, steps)
+        if not torch.equal(xs[-1], ref_out):
+            raise RuntimeError("graph replay output differs from the eager decode step")
+        del graph
+    except RuntimeError as exc:
+        if "differs" in str(exc):
+            raise
+        graph_ms = None
+        print(f"decode: CUDA graph capture unavailable: {exc}", file=sys.stderr)
+    active = sum(int((c > 0).sum()) for c in counts)
+    expert_bytes = 2 * (2 * D * HIDDEN + HIDDEN + D)
+    wbytes = active * expert_bytes
+    peaks = load_peaks()
+    best = min(v for v in (eager_ms, graph_ms) if v is not None)
+    gbs = wbytes / (best / 1000.0) / 1e9
+    return {"workload": f"AR decode: {DECODE_LAYERS} MoE layers x {B} tokens, d{D} E{E} H{HIDDEN} top{k} bf16, "
+                        f"seed {DECODE_SEED}",
+            "ms_per_step_eager": round(eager_ms, 4), "ms_per_step_graph": None if graph_ms is None else round(graph_ms, 4),
+            "us_per_layer": round(1000 * best / DECODE_LAYERS, 2), "tokens_per_s": B / (best / 1000.0),
+            "steps": steps, "active_experts": active, "weight_bytes_per_step": wbytes,
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm"], "unit": "GB/s",
+                         "frac": round(gbs / peaks["hbm"], 3), "peak_source": f"{peaks['src']} HBM copy"},
+            "gpu_launches_per_step": KERNELS_PER_STEP * DECODE_LAYERS}
+
+
+def report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e, x, decode=None):
     if rank != 0:
         return
     peaks = load_peaks()
@@ -552,6 +652,8 @@ def report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e, x):
         "cpu_baseline": cpu,
         "clocks": clocks,
     }
+    if decode is not None:
+        line["decode"] = decode
     print(json.dumps(line), flush=True)
 
 
@@ -565,6 +667,7 @@ def main():
                     help="tokens per GPU (default: the 48 x 1536 workload; smaller for profiling)")
     ap.add_argument("--skip-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--skip-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--skip-decode", action="store_true", help="skip the 28-layer decode leg")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)

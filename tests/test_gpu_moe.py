@@ -228,3 +228,38 @@ def test_module_forward_host_matches_device():
         y_host = m.forward_host(x.pin_memory(), chunk_tokens=512)
     assert y_host.shape == x.shape and not y_host.is_cuda
     assert torch.equal(y_host, y_dev)
+
+
+@pytest.mark.parametrize("n,k", [(1000, 2), (64, 2), (300, 1)])
+def test_cuda_graph_capture_replay(n, k):
+    """The forward makes no host synchronisation, so it captures into a CUDA
+    graph; replays on new inputs give exactly the eager forward's result."""
+    d, H, E = 1280, 3200, 14
+    sd = reference_moe.make_state(d, H, E, 23, dtype=torch.bfloat16, device=DEV, bias_std=0.02)
+    w1, b1, w2, b2, _ = packed(sd, E, DEV)
+    wr = sd["router.weight"].contiguous()
+    xs = [reference_moe.make_input(n, d, 23 + i, dtype=torch.bfloat16, device=DEV) for i in range(3)]
+    eager = [ops.moe_forward(x, wr, w1, b1, w2, b2, k).clone() for x in xs]
+    x_static = xs[0].clone()
+    out_static = torch.empty_like(x_static)
+    ws = torch.empty(ops.workspace_bytes(n, d, E, k, H, 0, 1, torch.bfloat16), dtype=torch.uint8, device=DEV)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        ops.moe_forward(x_static, wr, w1, b1, w2, b2, k, out=out_static, workspace=ws)
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        ops.moe_forward(x_static, wr, w1, b1, w2, b2, k, out=out_static, workspace=ws)
+    for x, ref in zip(reversed(xs), reversed(eager)):
+        x_static.copy_(x)
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out_static, ref)
+    assert _lib_error(ws) == 0
+    del graph
+
+
+def _lib_error(ws):
+    from agillm41_b200 import _lib
+    return _lib.read_device_error(ws[:4].view(torch.int32))
