@@ -18,10 +18,14 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "liba
 AGM_F32, AGM_BF16, AGM_F16 = 0, 1, 2
 AGM_OK = 0
 AGM_TILE_M = 128
+AGM_PAIR_ROWS = 256
+AGM_PAIR_MIN_ROWS = 16384
+AGM_GEMM_PAIR = -1
 AGM_DISPATCH_BLOCK = 128
 AGM_MAX_EXPERTS = 16
 AGM_FLAG_TIE_LOW_FIRST = 0x1
 AGM_FLAG_KEEP_ERROR = 0x2
+AGM_FLAG_NO_PAIR = 0x4
 AGM_STAGE_EVENTS = 8
 AGM_EP_STAGE_EVENTS = 9
 

@@ -51,6 +51,7 @@ int num_sms_current() {
 
 int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 
+
 int check_common(int dtype, int d, int n_experts, int top_k) {
   const int eb = elem_bytes(dtype);
   if (!eb) return fail(AGM_ERR_ARG, "dtype must be AGM_F32, AGM_BF16 or AGM_F16");
@@ -160,8 +161,9 @@ int64_t agm_dispatch_blocks(int64_t n_tokens) {
 
 int64_t agm_max_rows(int64_t n_tokens, int top_k, int n_experts) {
   if (n_tokens <= 0) return 0;
-  return round_up(static_cast<int64_t>(top_k) * n_tokens + static_cast<int64_t>(n_experts) * (AGM_TILE_M - 1),
-                  AGM_TILE_M);
+  const int64_t kn = static_cast<int64_t>(top_k) * n_tokens;
+  const int64_t align = kn >= AGM_PAIR_MIN_ROWS ? AGM_PAIR_ROWS : AGM_TILE_M;
+  return round_up(kn + static_cast<int64_t>(n_experts) * (align - 1), align);
 }
 
 int agm_router_topk(const void* x, const void* w_router, int dtype, int64_t n_tokens, int d, int n_experts,
@@ -193,8 +195,8 @@ int agm_dispatch_plan(const int32_t* block_hist, int64_t n_tokens, int n_experts
   const int64_t rows = agm_max_rows(n_tokens, top_k, n_experts);
   if (rows > INT32_MAX) return fail(AGM_ERR_UNSUPPORTED, "too many permuted rows for int32 indices");
   cudaError_t e = agm::dispatch_plan(block_hist, static_cast<int>(agm_dispatch_blocks(n_tokens)), n_experts, rows,
-                                     static_cast<int>(rows / AGM_TILE_M), block_off, counts, seg_start, tile_expert,
-                                     num_tiles, token_of, err, static_cast<cudaStream_t>(stream));
+                                     static_cast<int>(rows / AGM_TILE_M), AGM_TILE_M, block_off, counts, seg_start,
+                                     tile_expert, num_tiles, token_of, err, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? AGM_OK : cuda_fail(e, "dispatch_plan");
 }
 
@@ -226,7 +228,8 @@ int agm_grouped_gemm(const void* a, int64_t a_rows, const void* w, const void* b
   if (!aligned16(a) || !aligned16(w) || !aligned16(c) || (bias && !aligned16(bias)))
     return fail(AGM_ERR_ARG, "a, w, bias and c must be 16-byte aligned");
   if (max_tiles > INT32_MAX / 2) return fail(AGM_ERR_UNSUPPORTED, "too many tiles");
-  if (force_bn != 0 && force_bn != 128 && force_bn != 256) return fail(AGM_ERR_ARG, "force_bn must be 0, 128, 256");
+  if (force_bn != 0 && force_bn != 128 && force_bn != 256 && force_bn != AGM_GEMM_PAIR)
+    return fail(AGM_ERR_ARG, "force_bn must be 0, 128, 256 or AGM_GEMM_PAIR");
   agm::GemmArgs ga;
   ga.c = c;
   ga.ldc = n_out;
@@ -314,6 +317,13 @@ int agm_moe_forward(const void* x, int dtype, int64_t n_tokens, int d, int n_exp
   void* gates = gates_out ? gates_out : L.gates;
   const int sms = num_sms_current();
   const int64_t max_tiles = rows / AGM_TILE_M;
+  // Expert GEMMs on CTA pairs (256 x 256 tiles; expert segments padded to
+  // 256 rows) once there are enough rows that the extra padding is small:
+  // about E x 64 more rows on average, under 6% of k x n from the threshold up.
+  const bool pair = dtype != AGM_F32 && !(flags & AGM_FLAG_NO_PAIR) &&
+                    static_cast<int64_t>(top_k) * n_tokens >= AGM_PAIR_MIN_ROWS;
+  const int seg_align = pair ? AGM_PAIR_ROWS : AGM_TILE_M;
+  const int gemm_mode = pair ? AGM_GEMM_PAIR : 0;
 
   if ((e = mark(0)) != cudaSuccess) return cuda_fail(e, "event record");
   e = agm::router_topk(dtype, x, w_router, n_tokens, d, n_experts, top_k, flags & AGM_FLAG_TIE_LOW_FIRST,
@@ -321,8 +331,8 @@ int agm_moe_forward(const void* x, int dtype, int64_t n_tokens, int d, int n_exp
   if (e != cudaSuccess) return cuda_fail(e, "router_topk");
   if ((e = mark(1)) != cudaSuccess) return cuda_fail(e, "event record");
   e = agm::dispatch_plan(L.block_hist, static_cast<int>(agm_dispatch_blocks(n_tokens)), n_experts, rows,
-                         static_cast<int>(max_tiles), L.block_off, L.counts, L.seg_start, L.tile_expert, L.num_tiles,
-                         L.token_of, L.err, stream);
+                         static_cast<int>(max_tiles), seg_align, L.block_off, L.counts, L.seg_start, L.tile_expert,
+                         L.num_tiles, L.token_of, L.err, stream);
   if (e != cudaSuccess) return cuda_fail(e, "dispatch_plan");
   if ((e = mark(2)) != cudaSuccess) return cuda_fail(e, "event record");
   e = agm::permute_rows(x, eb, n_tokens, d, top_k, n_experts, idx, L.block_off, L.seg_start, L.counts, rows,
@@ -342,7 +352,7 @@ int agm_moe_forward(const void* x, int dtype, int64_t n_tokens, int d, int n_exp
   g1.num_tiles = L.num_tiles;
   g1.max_tiles = static_cast<int>(max_tiles);
   g1.err = L.err;
-  e = agm::grouped_gemm(dtype, L.x_perm, rows, w1, g1, true, sms, stream, 0);
+  e = agm::grouped_gemm(dtype, L.x_perm, rows, w1, g1, true, sms, stream, gemm_mode);
   if (e != cudaSuccess) return cuda_fail(e, "grouped_gemm fc1");
   if ((e = mark(4)) != cudaSuccess) return cuda_fail(e, "event record");
   agm::GemmArgs g2 = g1;
@@ -351,7 +361,7 @@ int agm_moe_forward(const void* x, int dtype, int64_t n_tokens, int d, int n_exp
   g2.bias = b2;
   g2.n = d;
   g2.k = hidden;
-  e = agm::grouped_gemm(dtype, L.h, rows, w2, g2, false, sms, stream, 0);
+  e = agm::grouped_gemm(dtype, L.h, rows, w2, g2, false, sms, stream, gemm_mode);
   if (e != cudaSuccess) return cuda_fail(e, "grouped_gemm fc2");
   if ((e = mark(5)) != cudaSuccess) return cuda_fail(e, "event record");
 

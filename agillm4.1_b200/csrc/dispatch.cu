@@ -7,7 +7,8 @@
 // * dispatch_plan_kernel (one CTA): per expert, an exclusive scan of the
 //   per-block histograms written by the router kernel gives each dispatch
 //   block its base offset inside the expert's segment; per-expert counts;
-//   segment starts padded to the GEMM row tile; the row-tile -> expert table
+//   segment starts padded to the GEMM row tile (128 rows, or 256 when the
+//   expert GEMMs run on CTA pairs); the row-tile -> expert table
 //   and the number of row tiles (read by the persistent GEMM on the device).
 // * permute_kernel (one CTA per dispatch block of 256 tokens, plus one CTA per
 //   expert that zero-fills the segment's padding rows): warp ballots give each
@@ -17,7 +18,7 @@
 //   16-byte vector loads/stores to every destination row of the token.
 //
 // Output layout in HBM: x_perm [max_rows, d] (expert segments back to back,
-// each padded to a multiple of 128 rows), row_of [N, k] (destination row of
+// each padded to a multiple of 128 or 256 rows), row_of [N, k] (destination row of
 // each (token, rank)), token_of [max_rows] (source token of each row, -1 for
 // padding rows).
 #include "common.cuh"
@@ -31,7 +32,7 @@ constexpr int kPlanThreads = 512;
 constexpr int kMaxChunks = 8;  // 16-byte chunks per lane held in registers (rows up to 4 KB)
 
 __global__ void __launch_bounds__(kPlanThreads) dispatch_plan_kernel(
-    const int32_t* __restrict__ block_hist, int n_blocks, int E, int64_t max_rows, int max_tiles,
+    const int32_t* __restrict__ block_hist, int n_blocks, int E, int64_t max_rows, int max_tiles, int seg_align,
     int32_t* __restrict__ block_off, int32_t* __restrict__ counts, int32_t* __restrict__ seg_start,
     int32_t* __restrict__ tile_expert, int32_t* __restrict__ num_tiles, int32_t* __restrict__ token_of, int* err) {
   __shared__ int tot_s[32];
@@ -61,7 +62,7 @@ __global__ void __launch_bounds__(kPlanThreads) dispatch_plan_kernel(
     int acc = 0;
     for (int e = 0; e < E; ++e) {
       seg_s[e] = acc;
-      acc += (tot_s[e] + kTile - 1) / kTile * kTile;
+      acc += (tot_s[e] + seg_align - 1) / seg_align * seg_align;
     }
     seg_s[E] = acc;
     if (acc > max_rows || acc / kTile > max_tiles) raise_error(err, kErrRowOverflow);
@@ -225,10 +226,12 @@ __global__ void __launch_bounds__(kBlk) permute_kernel(
 }
 
 cudaError_t dispatch_plan(const int32_t* block_hist, int n_blocks, int E, int64_t max_rows, int max_tiles,
-                          int32_t* block_off, int32_t* counts, int32_t* seg_start, int32_t* tile_expert,
-                          int32_t* num_tiles, int32_t* token_of, int* err, cudaStream_t stream) {
-  dispatch_plan_kernel<<<1, kPlanThreads, 0, stream>>>(block_hist, n_blocks, E, max_rows, max_tiles, block_off,
-                                                       counts, seg_start, tile_expert, num_tiles, token_of, err);
+                          int seg_align, int32_t* block_off, int32_t* counts, int32_t* seg_start,
+                          int32_t* tile_expert, int32_t* num_tiles, int32_t* token_of, int* err, cudaStream_t stream) {
+  if (seg_align != kTile && seg_align != 2 * kTile) return cudaErrorInvalidValue;
+  dispatch_plan_kernel<<<1, kPlanThreads, 0, stream>>>(block_hist, n_blocks, E, max_rows, max_tiles, seg_align,
+                                                       block_off, counts, seg_start, tile_expert, num_tiles, token_of,
+                                                       err);
   return cudaGetLastError();
 }
 

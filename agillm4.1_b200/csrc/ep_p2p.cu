@@ -412,7 +412,8 @@ AGM_API int agm_ep_dispatch(const void* x, int dtype, int64_t n_tokens, int d, i
                          nullptr, L.idx, L.gates, L.block_hist, L.err, sms, stream);
     if (e != cudaSuccess) return ep_cuda(e, "router_topk");
     e = agm::dispatch_plan(L.block_hist, static_cast<int>(agm_dispatch_blocks(n_tokens)), n_experts, rows,
-                           static_cast<int>(rows / 128), L.block_off, L.counts, L.seg_start, L.tile_expert_local,
+                           static_cast<int>(rows / 128), AGM_TILE_M, L.block_off, L.counts, L.seg_start,
+                           L.tile_expert_local,
                            L.num_tiles_local, L.token_of, L.err, stream);
     if (e != cudaSuccess) return ep_cuda(e, "dispatch_plan");
   }

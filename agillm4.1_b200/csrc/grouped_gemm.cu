@@ -449,6 +449,8 @@ static cudaError_t dispatch_bn(const void* a, int64_t a_rows, const void* w, con
 cudaError_t grouped_gemm(int dtype, const void* a, int64_t a_rows, const void* w, const GemmArgs& args, bool relu,
                          int num_sms, cudaStream_t stream, int force_bn) {
   if (args.max_tiles <= 0 || args.n <= 0) return cudaSuccess;
+  if (force_bn == -1 && dtype != AGM_F32) return grouped_gemm_pair(dtype, a, a_rows, w, args, relu, num_sms, stream);
+  if (force_bn == -1) force_bn = 0;
   if (dtype == AGM_F32) {
     dim3 grid(static_cast<unsigned>(args.max_tiles * (BM / 64)), static_cast<unsigned>((args.n + 63) / 64));
     const float* A = static_cast<const float*>(a);

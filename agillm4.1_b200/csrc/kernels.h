@@ -95,9 +95,11 @@ cudaError_t router_topk(int dtype, const void* x, const void* w, int64_t n_token
 size_t router_smem_bytes(int d, int E);
 // Whether the tensor-core router (bf16/fp16) handles this d.
 bool router_tc_supported(int d);
+// seg_align: expert segments start at multiples of this many rows (128, or
+// 256 for the CTA-pair GEMM).
 cudaError_t dispatch_plan(const int32_t* block_hist, int n_blocks, int E, int64_t max_rows, int max_tiles,
-                          int32_t* block_off, int32_t* counts, int32_t* seg_start, int32_t* tile_expert,
-                          int32_t* num_tiles, int32_t* token_of, int* err, cudaStream_t stream);
+                          int seg_align, int32_t* block_off, int32_t* counts, int32_t* seg_start,
+                          int32_t* tile_expert, int32_t* num_tiles, int32_t* token_of, int* err, cudaStream_t stream);
 cudaError_t permute_rows(const void* x, int elem_bytes, int64_t n_tokens, int d, int k, int E, const int32_t* idx,
                          const int32_t* block_off, const int32_t* seg_start, const int32_t* counts, int64_t max_rows,
                          void* x_perm, int32_t* row_of, int32_t* token_of, int* err, cudaStream_t stream);
@@ -106,8 +108,11 @@ cudaError_t permute_rows_ep(const void* x, int elem_bytes, int64_t n_tokens, int
                             int64_t max_rows, const EpRoute* route, int32_t* row_of, int* err, cudaStream_t stream);
 cudaError_t combine_ep(int dtype, const EpRoute* route, const int32_t* row_of, const void* gates, int64_t n, int d,
                        int k, void* out, int num_sms, cudaStream_t stream);
+// force_bn: 0 = auto, 128 / 256 = one-CTA tile width, -1 = CTA pairs.
 cudaError_t grouped_gemm(int dtype, const void* a, int64_t a_rows, const void* w, const GemmArgs& args, bool relu,
                          int num_sms, cudaStream_t stream, int force_bn);
+cudaError_t grouped_gemm_pair(int dtype, const void* a, int64_t a_rows, const void* w, const GemmArgs& args, bool relu,
+                              int num_sms, cudaStream_t stream);
 cudaError_t combine(int dtype, const void* y, const int32_t* row_of, const void* gates, int64_t n, int d, int k,
                     const void* shared_y, int n_shared, int64_t shared_stride, void* out, int num_sms,
                     cudaStream_t stream);

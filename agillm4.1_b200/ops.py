@@ -177,7 +177,8 @@ def workspace_bytes(n_tokens: int, d: int, n_experts: int, top_k: int, hidden: i
 def moe_forward(x: torch.Tensor, w_router: torch.Tensor, w1: torch.Tensor, b1: torch.Tensor, w2: torch.Tensor,
                 b2: torch.Tensor, top_k: int, *, shared: Optional[tuple] = None, out: Optional[torch.Tensor] = None,
                 want: tuple = (), tie_low_first: bool = False, workspace: Optional[torch.Tensor] = None,
-                check_errors: bool = False, stage_events=None, logits_in: Optional[torch.Tensor] = None):
+                check_errors: bool = False, stage_events=None, logits_in: Optional[torch.Tensor] = None,
+                pair: bool = True):
     """Fused forward: x [N, d] -> out [N, d]. ``want`` may hold 'idx', 'gates', 'counts', 'logits'.
 
     Weights: w_router [E, d]; w1 [E, H, d]; b1 [E, H]; w2 [E, d, H]; b2 [E, d];
@@ -186,6 +187,8 @@ def moe_forward(x: torch.Tensor, w_router: torch.Tensor, w1: torch.Tensor, b1: t
     of computing them in the router kernel.
     ``stage_events``: optional list of AGM_STAGE_EVENTS torch.cuda.Event
     (timing enabled) recorded around each kernel stage on the current stream.
+    ``pair``: let large batches run the expert GEMMs on CTA pairs (False:
+    one-CTA tiles throughout).
     Returns out, or (out, extras dict) when ``want`` is not empty.
     """
     lib = load()
@@ -217,7 +220,7 @@ def moe_forward(x: torch.Tensor, w_router: torch.Tensor, w1: torch.Tensor, b1: t
     rc = lib.agm_moe_forward(
         ptr(x), dtype_code(x.dtype), n, d, E, top_k, H, ptr(w_router), ptr(w1), ptr(b1), ptr(w2), ptr(b2), S,
         max(Hs, 1), ptr(ws1), ptr(sb1), ptr(ws2), ptr(sb2), ptr(out), ptr(workspace), workspace.numel(),
-        _flags(tie_low_first), ptr(extras.get("idx")), ptr(extras.get("gates")), ptr(extras.get("counts")),
+        _flags(tie_low_first) | (0 if pair else _lib.AGM_FLAG_NO_PAIR), ptr(extras.get("idx")), ptr(extras.get("gates")), ptr(extras.get("counts")),
         ptr(extras.get("logits")), ptr(logits_in), None if ev_arr is None else ctypes.addressof(ev_arr),
         stream_handle(dev))
     check(rc, "agm_moe_forward")

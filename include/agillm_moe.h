@@ -46,9 +46,18 @@ enum {
   AGM_ERR_WORKSPACE = -5    /* workspace too small                             */
 };
 
-/* Rows per GEMM tile. Every expert segment of the permuted activations is
- * padded to a multiple of this. */
+/* Rows per GEMM row tile. Every expert segment of the permuted activations is
+ * padded to a multiple of this (of AGM_PAIR_ROWS inside agm_moe_forward when
+ * its expert GEMMs run on CTA pairs). */
 #define AGM_TILE_M 128
+/* Rows of one CTA-pair GEMM tile (two row tiles sharing one weight group). */
+#define AGM_PAIR_ROWS 256
+/* agm_moe_forward runs its expert GEMMs on CTA pairs (and pads expert
+ * segments to AGM_PAIR_ROWS) when top_k * n_tokens reaches this. */
+#define AGM_PAIR_MIN_ROWS 16384
+/* agm_grouped_gemm force_bn value: 256 x 256 tiles on CTA pairs (tcgen05
+ * cta_group::2); row tiles 2i and 2i+1 must share a group. */
+#define AGM_GEMM_PAIR (-1)
 /* Tokens handled by one CTA of the router and permute kernels. */
 #define AGM_DISPATCH_BLOCK 128
 /* Largest supported number of experts (router kernel keeps 16 logits/token). */
@@ -61,13 +70,15 @@ enum {
 #define AGM_FLAG_TIE_LOW_FIRST 0x1 /* order exactly-equal top-k values by ascending expert index
                                       (default: descending, as torch.topk does on CUDA) */
 #define AGM_FLAG_KEEP_ERROR 0x2    /* agm_moe_forward: do not clear the device error word first */
+#define AGM_FLAG_NO_PAIR 0x4       /* agm_moe_forward: one-CTA GEMM tiles even where CTA pairs apply */
 
 AGM_API const char* agm_last_error(void);
 AGM_API int agm_abi_version(void);
 
 /* Number of dispatch blocks for n_tokens tokens: ceil(n / AGM_DISPATCH_BLOCK). */
 AGM_API int64_t agm_dispatch_blocks(int64_t n_tokens);
-/* Upper bound on permuted rows: round_up(k*n + E*(AGM_TILE_M-1), AGM_TILE_M). */
+/* Upper bound on permuted rows: round_up(k*n + E*(P-1), P) with P =
+ * AGM_PAIR_ROWS when k*n >= AGM_PAIR_MIN_ROWS, else AGM_TILE_M. */
 AGM_API int64_t agm_max_rows(int64_t n_tokens, int top_k, int n_experts);
 
 /* Router + top-k. Replaces agillm41.py:4398-4419 (scores = router(x).float();
@@ -107,7 +118,9 @@ AGM_API int agm_permute(const void* x, int dtype, int64_t n_tokens, int d, int n
  *   c [c_rows, n_out]; tile_group (nullable: all tiles use group 0);
  *   num_tiles (nullable device int: valid tiles; else max_tiles are valid).
  *   relu: 1 = ReLU epilogue (FC1), 0 = none (FC2).  force_bn: 0 = auto,
- *   128 or 256 = GEMM tile width (bf16/fp16 only).                        */
+ *   128 or 256 = GEMM tile width, AGM_GEMM_PAIR = 256 x 256 tiles on CTA
+ *   pairs (tile_group[2i] == tile_group[2i+1]; a mismatch sets a device
+ *   error bit) (bf16/fp16 only).                                          */
 AGM_API int agm_grouped_gemm(const void* a, int64_t a_rows, const void* w, const void* bias, int dtype, int groups,
                      int n_out, int k_in, const int32_t* tile_group, const int32_t* num_tiles, int64_t max_tiles,
                      int relu, int force_bn, void* c, int64_t c_rows, int* err, void* stream);

@@ -43,7 +43,9 @@ def test_size_helpers():
     assert lib.agm_dispatch_blocks(1) == 1
     assert lib.agm_dispatch_blocks(B) == 1
     assert lib.agm_dispatch_blocks(B + 1) == 2
-    assert lib.agm_max_rows(73728, 2, 14) == ((2 * 73728 + 14 * 127 + 127) // 128) * 128
+    assert lib.agm_max_rows(73728, 2, 14) == ((2 * 73728 + 14 * 255 + 255) // 256) * 256
+    assert lib.agm_max_rows(64, 2, 14) == ((2 * 64 + 14 * 127 + 127) // 128) * 128
+    assert lib.agm_max_rows(8192, 2, 14) == ((2 * 8192 + 14 * 255 + 255) // 256) * 256
     assert lib.agm_max_rows(0, 2, 14) == 0
     ws = lib.agm_moe_workspace_bytes(73728, 1280, 14, 2, 3200, 0, 1, _lib.AGM_BF16)
     rows = lib.agm_max_rows(73728, 2, 14)

@@ -186,6 +186,49 @@ def test_grouped_gemm_tc(dtype, rows_per_group, N, K, relu, bn):
     torch.testing.assert_close(c.float(), ref.to(dtype).float(), rtol=1e-2, atol=2e-2)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("rows_per_group,N,K,relu", [
+    ([256, 512, 0, 768], 3200, 1280, True),    # FC1 shape, partial last column tile
+    ([256, 512, 0, 768], 1280, 3200, False),   # FC2 shape
+    ([256, 384], 1280, 1280, True),            # odd tile count: the last pair has one tile
+    ([256], 192, 64, False),                   # one column tile narrower than 256
+    ([0, 256, 256], 320, 320, True),
+])
+def test_grouped_gemm_pair(dtype, rows_per_group, N, K, relu):
+    """CTA-pair (cta_group::2, 256 x 256 tiles) grouped GEMM vs an fp32 torch matmul."""
+    G = len(rows_per_group)
+    g = torch.Generator(device="cpu").manual_seed(N + K + 7)
+    rows = sum(rows_per_group)
+    a = torch.randn(rows, K, generator=g).to(dtype).to(DEV)
+    w = (torch.randn(G, N, K, generator=g) * 0.05).to(dtype).to(DEV)
+    bias = (torch.randn(G, N, generator=g) * 0.1).to(dtype).to(DEV)
+    tile_group = torch.tensor(sum([[gi] * (r // 128) for gi, r in enumerate(rows_per_group)], []),
+                              dtype=torch.int32, device=DEV)
+    num_tiles = torch.tensor([tile_group.numel()], dtype=torch.int32, device=DEV)
+    err = _err()
+    c = ops.grouped_gemm(a, w, bias, relu=relu, tile_group=tile_group, num_tiles=num_tiles,
+                         max_tiles=tile_group.numel(), force_bn=_lib.AGM_GEMM_PAIR, err=err)
+    assert read_device_error(err) == 0
+    ref = _ref_grouped(a, w, bias, tile_group, relu)
+    torch.testing.assert_close(c.float(), ref.to(dtype).float(), rtol=1e-2, atol=2e-2)
+    # Same products as the one-CTA kernel: both accumulate in fp32 over K in the same order.
+    c1 = ops.grouped_gemm(a, w, bias, relu=relu, tile_group=tile_group, num_tiles=num_tiles,
+                          max_tiles=tile_group.numel(), force_bn=256, err=err)
+    assert torch.equal(c, c1)
+
+
+def test_grouped_gemm_pair_group_mismatch_flagged():
+    """Row tiles 0 and 1 in different groups cannot share a pair: the kernel
+    sets the device error bit (and still terminates normally)."""
+    a = torch.randn(256, 128, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(2, 256, 128, device=DEV) * 0.05).to(torch.bfloat16)
+    tile_group = torch.tensor([0, 1], dtype=torch.int32, device=DEV)
+    err = _err()
+    ops.grouped_gemm(a, w, None, relu=False, tile_group=tile_group, max_tiles=2, force_bn=_lib.AGM_GEMM_PAIR,
+                     err=err)
+    assert read_device_error(err) & (1 << 7)
+
+
 def test_grouped_gemm_tc_device_tile_count():
     """Tiles beyond the device-side count are not computed (decode-sized case)."""
     dtype = torch.bfloat16

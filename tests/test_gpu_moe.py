@@ -263,3 +263,17 @@ def test_cuda_graph_capture_replay(n, k):
 def _lib_error(ws):
     from agillm41_b200 import _lib
     return _lib.read_device_error(ws[:4].view(torch.int32))
+
+
+def test_pair_gemm_forward_matches_single_cta():
+    """Above the pair threshold the forward pads expert segments to 256 rows and
+    runs the expert GEMMs on CTA pairs; the result equals the one-CTA path."""
+    d, H, E, k, n = 1280, 3200, 14, 2, 12000
+    sd = reference_moe.make_state(d, H, E, 24, dtype=torch.bfloat16, device=DEV, bias_std=0.02)
+    w1, b1, w2, b2, _ = packed(sd, E, DEV)
+    wr = sd["router.weight"].contiguous()
+    x = reference_moe.make_input(n, d, 24, dtype=torch.bfloat16, device=DEV)
+    out_p, ex_p = ops.moe_forward(x, wr, w1, b1, w2, b2, k, want=("idx", "counts"), check_errors=True)
+    out_1, ex_1 = ops.moe_forward(x, wr, w1, b1, w2, b2, k, want=("idx", "counts"), check_errors=True, pair=False)
+    assert torch.equal(ex_p["idx"], ex_1["idx"]) and torch.equal(ex_p["counts"], ex_1["counts"])
+    assert torch.equal(out_p, out_1)
