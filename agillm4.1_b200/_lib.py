@@ -26,6 +26,9 @@ AGM_MAX_EXPERTS = 16
 AGM_FLAG_TIE_LOW_FIRST = 0x1
 AGM_FLAG_KEEP_ERROR = 0x2
 AGM_FLAG_NO_PAIR = 0x4
+AGM_FLAG_NO_SWAP = 0x8
+AGM_FLAG_NO_PDL = 0x10
+AGM_SWAP_ROWS_PER_EXPERT = 32
 AGM_STAGE_EVENTS = 8
 AGM_EP_STAGE_EVENTS = 9
 

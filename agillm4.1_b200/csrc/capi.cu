@@ -2,6 +2,7 @@
 // launch sequence that replaces MoEFFN.forward (agillm41.py:4389-4431).
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <map>
 #include <mutex>
 #include <string>
@@ -133,6 +134,22 @@ FwdLayout carve(void* ws, int64_t n, int d, int E, int k, int H, int S, int Hs, 
 
 namespace agm {
 void set_last_error(const std::string& msg) { g_err = msg; }
+
+namespace {
+thread_local int tl_pdl = -1;  // -1: no forward scope on this thread
+}
+
+bool pdl_enabled() {
+  static const bool env_off = [] {
+    const char* v = std::getenv("AGM_NO_PDL");
+    return v && v[0] == '1';
+  }();
+  if (env_off) return false;
+  return tl_pdl != 0;
+}
+
+PdlScope::PdlScope(bool on) : prev(tl_pdl != 0) { tl_pdl = on ? 1 : 0; }
+PdlScope::~PdlScope() { tl_pdl = prev ? 1 : 0; }
 
 cudaError_t ensure_dynamic_smem(const void* func, int bytes) {
   static std::mutex mu;
@@ -304,6 +321,7 @@ int agm_moe_forward(const void* x, int dtype, int64_t n_tokens, int d, int n_exp
   auto mark = [&](int i) -> cudaError_t {
     return stage_events ? cudaEventRecord(static_cast<cudaEvent_t>(stage_events[i]), stream) : cudaSuccess;
   };
+  agm::PdlScope pdl_scope(!(flags & AGM_FLAG_NO_PDL));
   cudaError_t e = cudaSuccess;
   if (!(flags & AGM_FLAG_KEEP_ERROR)) {
     e = cudaMemsetAsync(L.err, 0, sizeof(int), stream);
@@ -322,8 +340,12 @@ int agm_moe_forward(const void* x, int dtype, int64_t n_tokens, int d, int n_exp
   // about E x 64 more rows on average, under 6% of k x n from the threshold up.
   const bool pair = dtype != AGM_F32 && !(flags & AGM_FLAG_NO_PAIR) &&
                     static_cast<int64_t>(top_k) * n_tokens >= AGM_PAIR_MIN_ROWS;
+  // Decode-sized batches: swapped operands, so the weights stream at full
+  // depth and only the valid rows of each segment enter the MMA.
+  const bool swap = dtype != AGM_F32 && !(flags & AGM_FLAG_NO_SWAP) &&
+                    static_cast<int64_t>(top_k) * n_tokens <= static_cast<int64_t>(AGM_SWAP_ROWS_PER_EXPERT) * n_experts;
   const int seg_align = pair ? AGM_PAIR_ROWS : AGM_TILE_M;
-  const int gemm_mode = pair ? AGM_GEMM_PAIR : 0;
+  const int gemm_mode = pair ? AGM_GEMM_PAIR : (swap ? -2 : 0);
 
   if ((e = mark(0)) != cudaSuccess) return cuda_fail(e, "event record");
   e = agm::router_topk(dtype, x, w_router, n_tokens, d, n_experts, top_k, flags & AGM_FLAG_TIE_LOW_FIRST,
@@ -352,6 +374,12 @@ int agm_moe_forward(const void* x, int dtype, int64_t n_tokens, int d, int n_exp
   g1.num_tiles = L.num_tiles;
   g1.max_tiles = static_cast<int>(max_tiles);
   g1.err = L.err;
+  g1.seg_start = L.seg_start;
+  g1.seg_count = L.counts;
+  // The tile table and counts come from the plan, two or more launches back,
+  // and the weights from before this forward: the GEMMs stream their first
+  // weight tiles while the kernel before them finishes.
+  g1.early_weights = true;
   e = agm::grouped_gemm(dtype, L.x_perm, rows, w1, g1, true, sms, stream, gemm_mode);
   if (e != cudaSuccess) return cuda_fail(e, "grouped_gemm fc1");
   if ((e = mark(4)) != cudaSuccess) return cuda_fail(e, "event record");
@@ -379,6 +407,7 @@ int agm_moe_forward(const void* x, int dtype, int64_t n_tokens, int d, int n_exp
     s1.num_tiles = nullptr;
     s1.max_tiles = static_cast<int>(npad / AGM_TILE_M);
     s1.err = L.err;
+    s1.early_weights = true;
     e = agm::grouped_gemm(dtype, x, n_tokens, static_cast<const uint8_t*>(ws1) + static_cast<size_t>(eb) * s * shared_hidden * d,
                           s1, true, sms, stream, 0);
     if (e != cudaSuccess) return cuda_fail(e, "grouped_gemm shared fc1");

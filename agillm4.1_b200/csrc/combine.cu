@@ -166,6 +166,8 @@ __global__ void __launch_bounds__(256) combine_kernel(Src ysrc, const int32_t* _
   constexpr int CH = 16 / sizeof(T);
   const int nchunk = d / CH;
   const int lane = lane_id();
+  pdl_wait();
+  pdl_trigger();
   const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
   for (int64_t tok = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + warp_id(); tok < n_tokens;
        tok += warps_total) {
@@ -227,12 +229,13 @@ static cudaError_t launch_combine(Src ysrc, const int32_t* row_of, const void* g
   T* o = static_cast<T*>(out);
   const unsigned g = static_cast<unsigned>(blocks);
   if (k <= 2)
-    combine_kernel<T, 2, Src><<<g, 256, 0, stream>>>(ysrc, row_of, gs, n, d, k, sh, n_shared, shared_stride, o);
-  else if (k <= 4)
-    combine_kernel<T, 4, Src><<<g, 256, 0, stream>>>(ysrc, row_of, gs, n, d, k, sh, n_shared, shared_stride, o);
-  else
-    combine_kernel<T, 16, Src><<<g, 256, 0, stream>>>(ysrc, row_of, gs, n, d, k, sh, n_shared, shared_stride, o);
-  return cudaGetLastError();
+    return launch_kernel(combine_kernel<T, 2, Src>, dim3(g), dim3(256), 0, stream, ysrc, row_of, gs, n, d, k, sh,
+                         n_shared, shared_stride, o);
+  if (k <= 4)
+    return launch_kernel(combine_kernel<T, 4, Src>, dim3(g), dim3(256), 0, stream, ysrc, row_of, gs, n, d, k, sh,
+                         n_shared, shared_stride, o);
+  return launch_kernel(combine_kernel<T, 16, Src>, dim3(g), dim3(256), 0, stream, ysrc, row_of, gs, n, d, k, sh,
+                       n_shared, shared_stride, o);
 }
 
 template <typename T>

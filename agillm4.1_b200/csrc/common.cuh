@@ -356,6 +356,20 @@ __device__ __forceinline__ void umma_commit_pair(uint64_t* bar, uint16_t cta_mas
       : "memory");
 }
 
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch. Every kernel of the forward is launched so
+// that it may start while the previous kernel on the stream is finishing. It
+// does only work that depends on nothing the previous kernels write (barrier
+// setup, TMEM allocation, loads of weights), then pdl_wait(): that returns
+// once the previous kernel has completed and its writes are visible, and
+// only then does the kernel read those outputs or write buffers the previous
+// kernels read. pdl_trigger() after the wait lets the next kernel start; the
+// next kernel's prologue may then read outputs of kernels before this one,
+// which have completed. Without the launch attribute both are no-ops.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Named barrier among `count` threads (warps of one role).
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");

@@ -10,8 +10,8 @@
 //   segment starts padded to the GEMM row tile (128 rows, or 256 when the
 //   expert GEMMs run on CTA pairs); the row-tile -> expert table
 //   and the number of row tiles (read by the persistent GEMM on the device).
-// * permute_kernel (one CTA per dispatch block of 256 tokens, plus one CTA per
-//   expert that zero-fills the segment's padding rows): warp ballots give each
+// * permute_kernel (one CTA per dispatch block of 128 tokens, plus 8 CTAs per
+//   expert that zero-fill the segment's padding rows): warp ballots give each
 //   (token, rank) its rank among the block's tokens routed to the same expert,
 //   in ascending token order, so the permutation is deterministic and equals
 //   the reference's ascending `nonzero` order. Rows of x are copied with
@@ -21,6 +21,8 @@
 // each padded to a multiple of 128 or 256 rows), row_of [N, k] (destination row of
 // each (token, rank)), token_of [max_rows] (source token of each row, -1 for
 // padding rows).
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -29,7 +31,11 @@ namespace agm {
 constexpr int kTile = AGM_TILE_M;
 constexpr int kBlk = AGM_DISPATCH_BLOCK;
 constexpr int kPlanThreads = 512;
+constexpr int kPlanUnroll = 8;
 constexpr int kMaxChunks = 8;  // 16-byte chunks per lane held in registers (rows up to 4 KB)
+// CTAs that zero-fill one expert segment's padding rows (up to 255 rows; one
+// CTA per expert made this fill the longest part of a small-batch permute).
+constexpr int kZeroCtas = 8;
 
 __global__ void __launch_bounds__(kPlanThreads) dispatch_plan_kernel(
     const int32_t* __restrict__ block_hist, int n_blocks, int E, int64_t max_rows, int max_tiles, int seg_align,
@@ -38,21 +44,33 @@ __global__ void __launch_bounds__(kPlanThreads) dispatch_plan_kernel(
   __shared__ int tot_s[32];
   __shared__ int seg_s[33];
   const int warp = warp_id(), lane = lane_id();
+  pdl_wait();
+  pdl_trigger();
   const int nwarps = blockDim.x / 32;
-  // 1. Per-expert exclusive scan over blocks (one warp per expert).
+  // 1. Per-expert exclusive scan over blocks (one warp per expert). The
+  //    loads of kPlanUnroll x 32 blocks are issued together before the scan
+  //    so a long histogram costs a few memory round trips, not one per 32.
   for (int e = warp; e < E; e += nwarps) {
     int carry = 0;
-    for (int b0 = 0; b0 < n_blocks; b0 += 32) {
-      const int b = b0 + lane;
-      const int v = (b < n_blocks) ? block_hist[static_cast<int64_t>(b) * E + e] : 0;
-      int incl = v;
+    for (int b0 = 0; b0 < n_blocks; b0 += 32 * kPlanUnroll) {
+      int v[kPlanUnroll];
 #pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const int n = __shfl_up_sync(0xffffffffu, incl, off);
-        if (lane >= off) incl += n;
+      for (int j = 0; j < kPlanUnroll; ++j) {
+        const int b = b0 + 32 * j + lane;
+        v[j] = (b < n_blocks) ? block_hist[static_cast<int64_t>(b) * E + e] : 0;
       }
-      if (b < n_blocks) block_off[static_cast<int64_t>(b) * E + e] = carry + incl - v;
-      carry += __shfl_sync(0xffffffffu, incl, 31);
+#pragma unroll
+      for (int j = 0; j < kPlanUnroll; ++j) {
+        const int b = b0 + 32 * j + lane;
+        int incl = v[j];
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          const int n = __shfl_up_sync(0xffffffffu, incl, off);
+          if (lane >= off) incl += n;
+        }
+        if (b < n_blocks) block_off[static_cast<int64_t>(b) * E + e] = carry + incl - v[j];
+        carry += __shfl_sync(0xffffffffu, incl, 31);
+      }
     }
     if (lane == 0) tot_s[e] = carry;
   }
@@ -97,16 +115,21 @@ struct LocalRows {
 template <int K_MAX, class Dst>
 __global__ void __launch_bounds__(kBlk) permute_kernel(
     const uint4* __restrict__ x, int64_t n_tokens, int nchunk /* 16-byte chunks per row */, int k, int E,
-    int n_blocks, const int32_t* __restrict__ idx, const int32_t* __restrict__ block_off,
+    int n_blocks, int split, const int32_t* __restrict__ idx, const int32_t* __restrict__ block_off,
     const int32_t* __restrict__ seg_start, const int32_t* __restrict__ counts, int64_t max_rows, Dst dst,
     int32_t* __restrict__ row_of, int32_t* __restrict__ token_of, int* err) {
   const int warp = warp_id(), lane = lane_id();
-  if (static_cast<int>(blockIdx.x) >= n_blocks) {
-    // Zero-fill the padding rows of one expert segment.
-    const int e = blockIdx.x - n_blocks;
+  pdl_wait();
+  pdl_trigger();
+  if (static_cast<int>(blockIdx.x) >= n_blocks * split) {
+    // Zero-fill the padding rows of one expert segment: kZeroCtas CTAs per
+    // expert, one row per warp at a time.
+    const int z = blockIdx.x - n_blocks * split;
+    const int e = z / kZeroCtas;
     const int64_t r0 = seg_start[e] + counts[e];
     const int64_t r1 = min(static_cast<int64_t>(seg_start[e + 1]), max_rows);
-    for (int64_t r = r0 + warp; r < r1; r += blockDim.x / 32) {
+    const int nw = blockDim.x / 32;
+    for (int64_t r = r0 + (z % kZeroCtas) * nw + warp; r < r1; r += kZeroCtas * nw) {
       uint4* o = dst.row(r);
       if (o)
         for (int c = lane; c < nchunk; c += 32) o[c] = make_uint4(0, 0, 0, 0);
@@ -114,10 +137,13 @@ __global__ void __launch_bounds__(kBlk) permute_kernel(
     if constexpr (Dst::kSystemFence) __threadfence_system();
     return;
   }
+  // `split` CTAs share one dispatch block (small batches): each computes the
+  // block's destination rows and copies every split-th pair of its tokens.
+  const int blk = blockIdx.x / split, part = blockIdx.x % split;
   __shared__ uint32_t mask_s[kBlk / 32][32];
   __shared__ int cnt_s[kBlk / 32][32];
   __shared__ int off_s[kBlk / 32][32];
-  const int64_t tok = static_cast<int64_t>(blockIdx.x) * kBlk + threadIdx.x;
+  const int64_t tok = static_cast<int64_t>(blk) * kBlk + threadIdx.x;
   const bool valid = tok < n_tokens;
   int my_e[K_MAX];
 #pragma unroll
@@ -150,25 +176,27 @@ __global__ void __launch_bounds__(kBlk) permute_kernel(
     dest[r] = -1;
     const int e = my_e[r];
     if (e >= 0 && e < E) {
-      const int64_t row = static_cast<int64_t>(seg_start[e]) + block_off[static_cast<int64_t>(blockIdx.x) * E + e] +
+      const int64_t row = static_cast<int64_t>(seg_start[e]) + block_off[static_cast<int64_t>(blk) * E + e] +
                           off_s[warp][e] + __popc(mask_s[warp][e] & lt);
       if (row >= 0 && row < max_rows) {
         dest[r] = static_cast<int>(row);
-        row_of[tok * k + r] = static_cast<int32_t>(row);
-        if (token_of) token_of[row] = static_cast<int32_t>(tok);
-      } else {
+        if (part == 0) {
+          row_of[tok * k + r] = static_cast<int32_t>(row);
+          if (token_of) token_of[row] = static_cast<int32_t>(tok);
+        }
+      } else if (part == 0) {
         raise_error(err, kErrRowOverflow);
       }
-    } else if (e >= E) {
+    } else if (e >= E && part == 0) {
       raise_error(err, kErrBadExpert);
     }
   }
   // Copy rows: the warp walks its 32 tokens two at a time; every lane loads
   // all of its 16-byte chunks of both rows before storing them to the k
   // destination rows, so up to 2 x kMaxChunks loads per lane are in flight.
-  const int64_t warp_tok0 = static_cast<int64_t>(blockIdx.x) * kBlk + warp * 32;
+  const int64_t warp_tok0 = static_cast<int64_t>(blk) * kBlk + warp * 32;
   if (nchunk <= 32 * kMaxChunks) {
-    for (int i = 0; i < 32; i += 2) {
+    for (int i = 2 * part; i < 32; i += 2 * split) {
       const int64_t t0 = warp_tok0 + i, t1 = t0 + 1;
       if (t0 >= n_tokens) break;
       const bool has1 = t1 < n_tokens;
@@ -205,7 +233,7 @@ __global__ void __launch_bounds__(kBlk) permute_kernel(
       }
     }
   } else {
-    for (int i = 0; i < 32; ++i) {
+    for (int i = part; i < 32; i += split) {
       const int64_t t = warp_tok0 + i;
       if (t >= n_tokens) break;
       int drow[K_MAX];
@@ -229,10 +257,8 @@ cudaError_t dispatch_plan(const int32_t* block_hist, int n_blocks, int E, int64_
                           int seg_align, int32_t* block_off, int32_t* counts, int32_t* seg_start,
                           int32_t* tile_expert, int32_t* num_tiles, int32_t* token_of, int* err, cudaStream_t stream) {
   if (seg_align != kTile && seg_align != 2 * kTile) return cudaErrorInvalidValue;
-  dispatch_plan_kernel<<<1, kPlanThreads, 0, stream>>>(block_hist, n_blocks, E, max_rows, max_tiles, seg_align,
-                                                       block_off, counts, seg_start, tile_expert, num_tiles, token_of,
-                                                       err);
-  return cudaGetLastError();
+  return launch_kernel(dispatch_plan_kernel, dim3(1), dim3(kPlanThreads), 0, stream, block_hist, n_blocks, E, max_rows,
+                       max_tiles, seg_align, block_off, counts, seg_start, tile_expert, num_tiles, token_of, err);
 }
 
 template <class Dst>
@@ -242,20 +268,20 @@ static cudaError_t launch_permute(const void* x, int elem_bytes, int64_t n_token
                                   int32_t* token_of, int* err, cudaStream_t stream) {
   const int n_blocks = static_cast<int>((n_tokens + kBlk - 1) / kBlk);
   const int nchunk = d * elem_bytes / 16;
-  const unsigned grid = static_cast<unsigned>(n_blocks + E);
+  // Small batches: up to 16 CTAs per dispatch block, so the row copies of a
+  // few hundred tokens are not serialised in one or two warps.
+  const int split = n_blocks >= 64 ? 1 : std::min(16, 64 / n_blocks);
+  const unsigned grid = static_cast<unsigned>(n_blocks * split + E * kZeroCtas);
   if (n_tokens <= 0) return cudaSuccess;
   const uint4* xs = static_cast<const uint4*>(x);
-  if (k <= 2) {
-    permute_kernel<2, Dst><<<grid, kBlk, 0, stream>>>(xs, n_tokens, nchunk, k, E, n_blocks, idx, block_off,
-                                                      seg_start, counts, max_rows, dst, row_of, token_of, err);
-  } else if (k <= 4) {
-    permute_kernel<4, Dst><<<grid, kBlk, 0, stream>>>(xs, n_tokens, nchunk, k, E, n_blocks, idx, block_off,
-                                                      seg_start, counts, max_rows, dst, row_of, token_of, err);
-  } else {
-    permute_kernel<16, Dst><<<grid, kBlk, 0, stream>>>(xs, n_tokens, nchunk, k, E, n_blocks, idx, block_off,
-                                                       seg_start, counts, max_rows, dst, row_of, token_of, err);
-  }
-  return cudaGetLastError();
+  if (k <= 2)
+    return launch_kernel(permute_kernel<2, Dst>, dim3(grid), dim3(kBlk), 0, stream, xs, n_tokens, nchunk, k, E,
+                         n_blocks, split, idx, block_off, seg_start, counts, max_rows, dst, row_of, token_of, err);
+  if (k <= 4)
+    return launch_kernel(permute_kernel<4, Dst>, dim3(grid), dim3(kBlk), 0, stream, xs, n_tokens, nchunk, k, E,
+                         n_blocks, split, idx, block_off, seg_start, counts, max_rows, dst, row_of, token_of, err);
+  return launch_kernel(permute_kernel<16, Dst>, dim3(grid), dim3(kBlk), 0, stream, xs, n_tokens, nchunk, k, E,
+                       n_blocks, split, idx, block_off, seg_start, counts, max_rows, dst, row_of, token_of, err);
 }
 
 cudaError_t permute_rows(const void* x, int elem_bytes, int64_t n_tokens, int d, int k, int E, const int32_t* idx,

@@ -87,6 +87,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   volatile int* abort_s = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id(), lane = lane_id();
+  if (!args.early_weights) {
+    pdl_wait();
+    pdl_trigger();
+  }
   int num_m = args.max_tiles;
   if (args.num_tiles) {
     const int nt = *args.num_tiles;
@@ -132,9 +136,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint32_t armed = 0;             // stages armed at least once
     uint32_t armed_parity = 0;      // parity of the last arming of each stage
     bool ok = true;
+    // With early_weights, the first tile's first `ndef` stages get their
+    // weight tile before the wait for the previous kernel and their A tile
+    // after it.
+    bool waited = !args.early_weights;
+    const int ndef = min(STAGES, num_kb);
+    int deferred = 0, first_m = 0;
     for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
       int m_blk, n_blk;
       tile_coords(t, num_m, num_n, m_blk, n_blk);
+      if (t == static_cast<int>(blockIdx.x)) first_m = m_blk;
       int g = args.tile_group ? args.tile_group[m_blk] : 0;
       if (g < 0 || g >= args.groups) g = 0;  // cannot happen: the plan kernel writes ids < groups
       for (int kb = 0; kb < num_kb; ++kb) {
@@ -145,8 +156,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         if (lane == 0) {
           mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
-          tma_load_2d(sA + stage * Cfg::A_BYTES, &tmA, kb * BK, m_blk * BM, &full[stage]);
           tma_load_3d(sB + stage * Cfg::B_BYTES, &tmB, kb * BK, n_blk * BN, g, &full[stage]);
+          if (waited) tma_load_2d(sA + stage * Cfg::A_BYTES, &tmA, kb * BK, m_blk * BM, &full[stage]);
+        }
+        if (!waited && ++deferred == ndef) {
+          pdl_wait();
+          pdl_trigger();
+          waited = true;
+          if (lane == 0)
+            for (int j = 0; j < deferred; ++j) tma_load_2d(sA + j * Cfg::A_BYTES, &tmA, j * BK, first_m * BM, &full[j]);
         }
         armed |= 1u << stage;
         armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
@@ -157,6 +175,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
     }
+    if (!waited) {  // no tile, or stopped early: still order after the previous kernel
+      pdl_wait();
+      pdl_trigger();
+      if (lane == 0)
+        for (int j = 0; j < deferred; ++j) tma_load_2d(sA + j * Cfg::A_BYTES, &tmA, j * BK, first_m * BM, &full[j]);
+    }
+    __syncwarp();
     // Drain: every armed stage's last load must have landed before exit.
     for (int s = 0; s < STAGES; ++s)
       if (armed & (1u << s)) mbar_wait(&full[s], (armed_parity >> s) & 1, args.err, kErrTimeoutDrain);
@@ -308,6 +333,8 @@ __global__ void __launch_bounds__(256) grouped_gemm_f32_kernel(const float* __re
   constexpr int TM = 64, TN = 64, TK = 16;
   __shared__ float As[TK][TM + 4];
   __shared__ float Bs[TK][TN + 4];
+  pdl_wait();
+  pdl_trigger();
   int num_m = args.max_tiles;
   if (args.num_tiles) num_m = min(*args.num_tiles, args.max_tiles);
   const int tile = blockIdx.x / (BM / TM);
@@ -432,8 +459,8 @@ static cudaError_t launch_tc(const void* a, int64_t a_rows, const void* w, const
   const int64_t max_total = static_cast<int64_t>(args.max_tiles) * num_n;
   const int ctas = args.max_ctas > 0 ? std::min(args.max_ctas, num_sms) : num_sms;
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ctas, max_total)));
-  grouped_gemm_tc_kernel<T, BN, RELU><<<grid, kGemmThreads, Cfg::SMEM_BYTES, stream>>>(tmA, tmB, tmC, args);
-  return cudaGetLastError();
+  return launch_kernel(grouped_gemm_tc_kernel<T, BN, RELU>, dim3(grid), dim3(kGemmThreads), Cfg::SMEM_BYTES, stream,
+                       tmA, tmB, tmC, args);
 }
 
 template <typename T, bool RELU>
@@ -450,16 +477,14 @@ cudaError_t grouped_gemm(int dtype, const void* a, int64_t a_rows, const void* w
                          int num_sms, cudaStream_t stream, int force_bn) {
   if (args.max_tiles <= 0 || args.n <= 0) return cudaSuccess;
   if (force_bn == -1 && dtype != AGM_F32) return grouped_gemm_pair(dtype, a, a_rows, w, args, relu, num_sms, stream);
-  if (force_bn == -1) force_bn = 0;
+  if (force_bn == -2 && dtype != AGM_F32) return grouped_gemm_swap(dtype, a, a_rows, w, args, relu, num_sms, stream);
+  if (force_bn < 0) force_bn = 0;
   if (dtype == AGM_F32) {
     dim3 grid(static_cast<unsigned>(args.max_tiles * (BM / 64)), static_cast<unsigned>((args.n + 63) / 64));
     const float* A = static_cast<const float*>(a);
     const float* W = static_cast<const float*>(w);
-    if (relu)
-      grouped_gemm_f32_kernel<true><<<grid, 256, 0, stream>>>(A, a_rows, W, args);
-    else
-      grouped_gemm_f32_kernel<false><<<grid, 256, 0, stream>>>(A, a_rows, W, args);
-    return cudaGetLastError();
+    return relu ? launch_kernel(grouped_gemm_f32_kernel<true>, grid, dim3(256), 0, stream, A, a_rows, W, args)
+                : launch_kernel(grouped_gemm_f32_kernel<false>, grid, dim3(256), 0, stream, A, a_rows, W, args);
   }
   if (dtype == AGM_BF16) {
     return relu ? dispatch_bn<__nv_bfloat16, true>(a, a_rows, w, args, num_sms, stream, force_bn)

@@ -96,6 +96,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const bool leader = (rank == 0);
   const int cluster = static_cast<int>(cluster_id_x());
   const int nclusters = static_cast<int>(cluster_count_x());
+  if (!args.early_weights) {
+    pdl_wait();
+    pdl_trigger();
+  }
 
   int num_m = args.max_tiles;
   if (args.num_tiles) {
@@ -144,11 +148,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     int stage = 0;
     uint32_t phase = 0, armed = 0, armed_parity = 0;
     bool ok = true;
+    // With early_weights, the first pair tile's first `ndef` stages get their
+    // weight half-tile before the wait for the previous kernel and their A
+    // rows after it.
+    bool waited = !args.early_weights;
+    const int ndef = min(kStages, num_kb);
+    int deferred = 0, first_m = 0;
     for (int t = cluster; t < total && ok; t += nclusters) {
       int p, n_blk;
       pair_coords(t, num_p, num_n, p, n_blk);
       const int m0 = 2 * p;
       const int my_m = (!leader && m0 + 1 < num_m) ? m0 + 1 : m0;
+      if (t == cluster) first_m = my_m;
       int g = args.tile_group ? args.tile_group[m0] : 0;
       if (g < 0 || g >= args.groups) g = 0;
       // Rank r holds weight rows [n0 + r * n_mma / 2, +n_mma / 2) of the tile
@@ -163,8 +174,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (lane == 0) {
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * (kABytes + kBBytes));
           const uint32_t fb = full0 + stage * 8;
-          tma_load_2d_pair(sA + stage * kABytes, &tmA, kb * kBK, my_m * kBM, fb);
           tma_load_3d_pair(sB + stage * kBBytes, &tmB, kb * kBK, b_row, g, fb);
+          if (waited) tma_load_2d_pair(sA + stage * kABytes, &tmA, kb * kBK, my_m * kBM, fb);
+        }
+        if (!waited && ++deferred == ndef) {
+          pdl_wait();
+          pdl_trigger();
+          waited = true;
+          if (lane == 0)
+            for (int j = 0; j < deferred; ++j)
+              tma_load_2d_pair(sA + j * kABytes, &tmA, j * kBK, first_m * kBM, full0 + j * 8);
         }
         armed |= 1u << stage;
         armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
@@ -175,6 +194,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
       }
     }
+    if (!waited) {  // no tile, or stopped early: still order after the previous kernel
+      pdl_wait();
+      pdl_trigger();
+      if (lane == 0)
+        for (int j = 0; j < deferred; ++j)
+          tma_load_2d_pair(sA + j * kABytes, &tmA, j * kBK, first_m * kBM, full0 + j * 8);
+    }
+    __syncwarp();
     // Drain: the pair MMAs that read this CTA's stages have completed (their
     // commit released `empty`), so no copy or read of this shared memory is
     // still in flight when the CTA leaves.
@@ -351,8 +378,8 @@ cudaError_t launch_pair(const void* a, int64_t a_rows, const void* w, const Gemm
   int ctas = args.max_ctas > 0 ? std::min(args.max_ctas, num_sms) : num_sms;
   ctas = static_cast<int>(std::min<int64_t>(ctas, 2 * std::max<int64_t>(1, max_units)));
   ctas = std::max(2, ctas & ~1);
-  grouped_gemm_pair_kernel<T, RELU><<<ctas, kThreads, kSmemBytes, stream>>>(tmA, tmB, tmC, args);
-  return cudaGetLastError();
+  return launch_kernel(grouped_gemm_pair_kernel<T, RELU>, dim3(ctas), dim3(kThreads), kSmemBytes, stream, tmA, tmB,
+                       tmC, args);
 }
 
 }  // namespace

@@ -7,8 +7,39 @@
 #include <stdint.h>
 
 #include <string>
+#include <utility>
 
 namespace agm {
+
+// Whether launches use programmatic dependent launch (see pdl_wait in
+// common.cuh): on unless the environment sets AGM_NO_PDL=1 or the calling
+// thread is inside a forward called with AGM_FLAG_NO_PDL.
+bool pdl_enabled();
+// Scope of one forward call: sets this thread's PDL choice, restores it after.
+struct PdlScope {
+  explicit PdlScope(bool on);
+  ~PdlScope();
+  bool prev;
+};
+
+// Kernel launch on `stream` with the programmatic-serialization attribute
+// (when enabled): the kernel may begin before the previous kernel on the
+// stream completes, and must call pdl_wait() before touching its outputs.
+template <typename... Exp, typename... Act>
+inline cudaError_t launch_kernel(void (*kernel)(Exp...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                                 Act&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Act>(args)...);
+}
 
 // Arguments of the grouped GEMM  c[r, :] = act(a[r, :] @ w[g]^T + bias[g]).
 struct GemmArgs {
@@ -24,6 +55,16 @@ struct GemmArgs {
   int max_tiles;              // host bound (and the count when num_tiles is null)
   int* err;
   int max_ctas = 0;           // cap on persistent CTAs (0 = one per SM), leaves SMs to concurrent kernels
+  // Swapped-operand kernel (small batches) only: expert e's rows are
+  // [seg_start[e], seg_start[e] + seg_count[e]) (device arrays, groups entries).
+  const int32_t* seg_start = nullptr;
+  const int32_t* seg_count = nullptr;
+  // The caller guarantees that the tile table / segment counts and the
+  // weights were written at least two kernels before this launch (true
+  // inside agm_moe_forward): the kernel then reads them and streams its first
+  // weight tiles before waiting for the previous kernel (programmatic
+  // dependent launch). Otherwise it waits before reading anything.
+  bool early_weights = false;
 };
 
 // Expert-parallel routing of one rank's permuted rows (see ep_p2p.cu): a list
@@ -108,10 +149,13 @@ cudaError_t permute_rows_ep(const void* x, int elem_bytes, int64_t n_tokens, int
                             int64_t max_rows, const EpRoute* route, int32_t* row_of, int* err, cudaStream_t stream);
 cudaError_t combine_ep(int dtype, const EpRoute* route, const int32_t* row_of, const void* gates, int64_t n, int d,
                        int k, void* out, int num_sms, cudaStream_t stream);
-// force_bn: 0 = auto, 128 / 256 = one-CTA tile width, -1 = CTA pairs.
+// force_bn: 0 = auto, 128 / 256 = one-CTA tile width, -1 = CTA pairs,
+// -2 = swapped operands over expert segments (args.seg_start / seg_count).
 cudaError_t grouped_gemm(int dtype, const void* a, int64_t a_rows, const void* w, const GemmArgs& args, bool relu,
                          int num_sms, cudaStream_t stream, int force_bn);
 cudaError_t grouped_gemm_pair(int dtype, const void* a, int64_t a_rows, const void* w, const GemmArgs& args, bool relu,
+                              int num_sms, cudaStream_t stream);
+cudaError_t grouped_gemm_swap(int dtype, const void* a, int64_t a_rows, const void* w, const GemmArgs& args, bool relu,
                               int num_sms, cudaStream_t stream);
 cudaError_t combine(int dtype, const void* y, const int32_t* row_of, const void* gates, int64_t n, int d, int k,
                     const void* shared_y, int n_shared, int64_t shared_stride, void* out, int num_sms,

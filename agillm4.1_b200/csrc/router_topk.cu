@@ -246,6 +246,8 @@ __global__ void __launch_bounds__(kDispatchBlock) router_topk_kernel(
   constexpr int CH = 16 / sizeof(T);  // elements per 16-byte chunk
   const int nchunk = d / CH;
   const bool compute = (logits_in == nullptr);
+  pdl_wait();
+  pdl_trigger();
   // Dynamic smem: [E][d] fp32 router weight (only when computing logits),
   // then [warps][32 tokens][16] fp32 logits.
   float* w_s = smem_f;
@@ -379,17 +381,22 @@ __global__ void __launch_bounds__(kDispatchBlock) router_topk_kernel(
 // ---------------------------------------------------------------------------
 // Tensor-core router (bf16 / fp16): TMA-fed tcgen05, thread-per-token epilogue
 // ---------------------------------------------------------------------------
-constexpr int kRtStages = 4;   // two CTAs per SM: 8 x 16 KB of x in flight per SM
+// Stages of the x ring: 4 with two CTAs per SM (8 x 16 KB of x in flight per
+// SM) when CTAs walk several tiles; 10 with one CTA per SM when every CTA has
+// at most one tile (small batches), so most of a tile's k-blocks are in
+// flight at once instead of arriving in 5 serial round trips.
+constexpr int kRtStages = 4;
+constexpr int kRtStagesDeep = 10;
 constexpr int kRtThreads = 192;
 constexpr int kRtABytes = 128 * 64 * 2;   // one 128-token x 64-feature tile
 constexpr int kRtWBytes = 16 * 64 * 2;    // one 16-expert x 64-feature tile of the router weight
 
-__host__ __device__ constexpr int rt_smem_bytes(int nkb) {
-  return kRtStages * kRtABytes + nkb * kRtWBytes + 1024 + 1024;
+__host__ __device__ constexpr int rt_smem_bytes(int nkb, int stages = kRtStages) {
+  return stages * kRtABytes + nkb * kRtWBytes + 1024 + 1024;
 }
 
-template <typename T, int KC>
-__global__ void __launch_bounds__(kRtThreads, 2) router_tc_kernel(
+template <typename T, int KC, int STAGES>
+__global__ void __launch_bounds__(kRtThreads, STAGES == kRtStages ? 2 : 1) router_tc_kernel(
     const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, int64_t n_tokens, int d,
     int E, int k, int tie_low_first, float* __restrict__ logits_out, int32_t* __restrict__ idx_out,
     T* __restrict__ gates_out, int32_t* __restrict__ block_hist, int* err) {
@@ -397,11 +404,11 @@ __global__ void __launch_bounds__(kRtThreads, 2) router_tc_kernel(
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int nkb = (d + 63) / 64;
   uint8_t* sA = smem;
-  uint8_t* sW = smem + kRtStages * kRtABytes;
+  uint8_t* sW = smem + STAGES * kRtABytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sW + nkb * kRtWBytes);
   uint64_t* full = bars;
-  uint64_t* empty = bars + kRtStages;
-  uint64_t* acc_full = empty + kRtStages;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* w_full = acc_empty + 2;
   uint64_t* drain = w_full + 1;
@@ -409,14 +416,14 @@ __global__ void __launch_bounds__(kRtThreads, 2) router_tc_kernel(
   volatile int* abort_s = reinterpret_cast<volatile int*>(tmem_slot + 1);
   // Per-warp expert counts, one set per accumulator buffer: [2][4 warps][16],
   // then one "an epilogue warp gave up" flag per buffer.
-  int* hist_w = reinterpret_cast<int*>(bars + 16);
+  int* hist_w = reinterpret_cast<int*>(bars + 32);  // past up to 26 barriers and the two words after them
   volatile int* epi_fail = hist_w + 2 * 4 * kMaxExperts;
 
   const int warp = warp_id(), lane = lane_id();
   const int num_tiles = static_cast<int>((n_tokens + 127) / 128);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kRtStages; ++s) {
+    for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -440,6 +447,10 @@ __global__ void __launch_bounds__(kRtThreads, 2) router_tc_kernel(
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Setup above overlaps the previous kernel; x, the router weight and the
+  // outputs are touched only after it has completed.
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -464,13 +475,13 @@ __global__ void __launch_bounds__(kRtThreads, 2) router_tc_kernel(
         armed |= 1u << stage;
         armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
         __syncwarp();
-        if (++stage == kRtStages) {
+        if (++stage == STAGES) {
           stage = 0;
           phase ^= 1;
         }
       }
     }
-    for (int s = 0; s < kRtStages; ++s)
+    for (int s = 0; s < STAGES; ++s)
       if (armed & (1u << s)) mbar_wait(&full[s], (armed_parity >> s) & 1, err, kErrTimeoutDrain);
     mbar_wait(w_full, 0, err, kErrTimeoutDrain);
   } else if (warp == 1) {
@@ -506,7 +517,7 @@ __global__ void __launch_bounds__(kRtThreads, 2) router_tc_kernel(
           if (kb == nkb - 1) umma_commit(&acc_full[acc]);
         }
         __syncwarp();
-        if (++stage == kRtStages) {
+        if (++stage == STAGES) {
           stage = 0;
           phase ^= 1;
         }
@@ -584,14 +595,22 @@ static cudaError_t launch_router_tc(const void* x, const void* w, int64_t n_toke
     if (!encode_tmap(&tmW, w, 2, dims, str, box, dt)) return cudaErrorInvalidValue;
   }
   const int nkb = (d + 63) / 64;
-  const int smem = rt_smem_bytes(nkb);
-  cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(router_tc_kernel<T, KC>), smem);
-  if (e != cudaSuccess) return e;
   const int64_t tiles = (n_tokens + 127) / 128;
+  if (tiles <= num_sms && rt_smem_bytes(nkb, kRtStagesDeep) <= 227 * 1024) {
+    const int smem = rt_smem_bytes(nkb, kRtStagesDeep);
+    cudaError_t e =
+        ensure_dynamic_smem(reinterpret_cast<const void*>(router_tc_kernel<T, KC, kRtStagesDeep>), smem);
+    if (e != cudaSuccess) return e;
+    return launch_kernel(router_tc_kernel<T, KC, kRtStagesDeep>, dim3(static_cast<unsigned>(tiles)), dim3(kRtThreads),
+                         smem, stream, tmX, tmW, n_tokens, d, E, k, tie_low_first, logits_out, idx,
+                         static_cast<T*>(gates), block_hist, err);
+  }
+  const int smem = rt_smem_bytes(nkb);
+  cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(router_tc_kernel<T, KC, kRtStages>), smem);
+  if (e != cudaSuccess) return e;
   const int grid = static_cast<int>(std::min<int64_t>(tiles, 2 * num_sms));
-  router_tc_kernel<T, KC><<<grid, kRtThreads, smem, stream>>>(tmX, tmW, n_tokens, d, E, k, tie_low_first,
-                                                              logits_out, idx, static_cast<T*>(gates), block_hist, err);
-  return cudaGetLastError();
+  return launch_kernel(router_tc_kernel<T, KC, kRtStages>, dim3(grid), dim3(kRtThreads), smem, stream, tmX, tmW,
+                       n_tokens, d, E, k, tie_low_first, logits_out, idx, static_cast<T*>(gates), block_hist, err);
 }
 
 template <typename T, int KC>
@@ -603,10 +622,9 @@ static cudaError_t launch_router(const void* x, const void* w, int64_t n_tokens,
                       static_cast<size_t>(kRouterWarps) * 32 * kMaxExperts * sizeof(float);
   cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(router_topk_kernel<T, KC>), static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  router_topk_kernel<T, KC><<<static_cast<unsigned>(nblk), kDispatchBlock, smem, stream>>>(
-      static_cast<const T*>(x), static_cast<const T*>(w), n_tokens, d, E, k, tie_low_first, logits_in, logits_out,
-      idx, static_cast<T*>(gates), block_hist, err);
-  return cudaGetLastError();
+  return launch_kernel(router_topk_kernel<T, KC>, dim3(static_cast<unsigned>(nblk)), dim3(kDispatchBlock), smem, stream,
+                       static_cast<const T*>(x), static_cast<const T*>(w), n_tokens, d, E, k, tie_low_first, logits_in,
+                       logits_out, idx, static_cast<T*>(gates), block_hist, err);
 }
 
 // The tensor-core router keeps the whole router weight resident next to its

@@ -55,6 +55,10 @@ enum {
 /* agm_moe_forward runs its expert GEMMs on CTA pairs (and pads expert
  * segments to AGM_PAIR_ROWS) when top_k * n_tokens reaches this. */
 #define AGM_PAIR_MIN_ROWS 16384
+/* agm_moe_forward runs its expert GEMMs with swapped operands (weights as the
+ * 128-row MMA operand, each expert's rows as N = 32) when top_k * n_tokens is
+ * at most this many rows per expert on average (decode batches). */
+#define AGM_SWAP_ROWS_PER_EXPERT 32
 /* agm_grouped_gemm force_bn value: 256 x 256 tiles on CTA pairs (tcgen05
  * cta_group::2); row tiles 2i and 2i+1 must share a group. */
 #define AGM_GEMM_PAIR (-1)
@@ -71,6 +75,9 @@ enum {
                                       (default: descending, as torch.topk does on CUDA) */
 #define AGM_FLAG_KEEP_ERROR 0x2    /* agm_moe_forward: do not clear the device error word first */
 #define AGM_FLAG_NO_PAIR 0x4       /* agm_moe_forward: one-CTA GEMM tiles even where CTA pairs apply */
+#define AGM_FLAG_NO_SWAP 0x8       /* agm_moe_forward: row-tile GEMMs even for small batches */
+#define AGM_FLAG_NO_PDL 0x10       /* agm_moe_forward: launch each kernel after the previous one
+                                      completes (default: programmatic dependent launch) */
 
 AGM_API const char* agm_last_error(void);
 AGM_API int agm_abi_version(void);

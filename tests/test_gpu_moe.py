@@ -277,3 +277,38 @@ def test_pair_gemm_forward_matches_single_cta():
     out_1, ex_1 = ops.moe_forward(x, wr, w1, b1, w2, b2, k, want=("idx", "counts"), check_errors=True, pair=False)
     assert torch.equal(ex_p["idx"], ex_1["idx"]) and torch.equal(ex_p["counts"], ex_1["counts"])
     assert torch.equal(out_p, out_1)
+
+
+@pytest.mark.parametrize("n,k,E", [(64, 2, 14), (200, 2, 14), (37, 1, 4), (96, 3, 16)])
+def test_swap_gemm_forward_matches_row_tiles(n, k, E):
+    """Decode-sized batches run the expert GEMMs with swapped operands (weights
+    as the MMA's M side, each expert's rows as N); the result equals the
+    row-tile path. (200, 2, 14) puts more than 32 rows on some experts, so
+    their segments span several 32-row blocks; (37, 1, 4) leaves experts empty."""
+    d, H = 1280, 3200
+    sd = reference_moe.make_state(d, H, E, 25 + n, dtype=torch.bfloat16, device=DEV, bias_std=0.02)
+    w1, b1, w2, b2, _ = packed(sd, E, DEV)
+    wr = sd["router.weight"].contiguous()
+    x = reference_moe.make_input(n, d, 25 + n, dtype=torch.bfloat16, device=DEV)
+    out_s, ex_s = ops.moe_forward(x, wr, w1, b1, w2, b2, k, want=("idx", "counts"), check_errors=True)
+    out_t, ex_t = ops.moe_forward(x, wr, w1, b1, w2, b2, k, want=("idx", "counts"), check_errors=True, swap=False)
+    assert torch.equal(ex_s["idx"], ex_t["idx"]) and torch.equal(ex_s["counts"], ex_t["counts"])
+    assert torch.equal(out_s, out_t)
+
+
+@pytest.mark.parametrize("n", [64, 3000, 12000])
+def test_programmatic_launch_matches_serialised(n):
+    """Kernels launched to overlap the previous kernel's tail (each waits for
+    it before touching its outputs) give exactly the serialised result, on the
+    swapped-operand (64), one-CTA (3000) and CTA-pair (12000) GEMM paths."""
+    d, H, E, k = 1280, 3200, 14, 2
+    sd = reference_moe.make_state(d, H, E, 26, dtype=torch.bfloat16, device=DEV, bias_std=0.02)
+    w1, b1, w2, b2, _ = packed(sd, E, DEV)
+    wr = sd["router.weight"].contiguous()
+    xs = [reference_moe.make_input(n, d, 26 + i, dtype=torch.bfloat16, device=DEV) for i in range(3)]
+    serial = [ops.moe_forward(x, wr, w1, b1, w2, b2, k, pdl=False, check_errors=True) for x in xs]
+    # back to back on one stream, so every kernel overlaps the one before it
+    outs = [ops.moe_forward(x, wr, w1, b1, w2, b2, k) for x in xs]
+    torch.cuda.synchronize()
+    for a, b in zip(outs, serial):
+        assert torch.equal(a, b)
