@@ -619,6 +619,15 @@ def run_decode(args, dev, stream):
             "gpu_launches_per_step": KERNELS_PER_STEP * DECODE_LAYERS}
 
 
+PAIR_MIN_ROWS = 16384   # AGM_PAIR_MIN_ROWS: agm_moe_forward runs its expert GEMMs on CTA pairs from k*N rows up
+
+
+def gemm_kernel_name(n_tokens):
+    if TOP_K * n_tokens >= PAIR_MIN_ROWS:
+        return "grouped_gemm_pair_kernel (FC1+FC2, tcgen05 cta_group::2, 256x256 tiles)"
+    return "grouped_gemm_tc_kernel (FC1+FC2, tcgen05, one CTA per tile)"
+
+
 def report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e, x, decode=None):
     if rank != 0:
         return
@@ -647,7 +656,7 @@ def report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e, x, deco
         "config": workload_config(world, N),
         "e2e": e2e,
         "gpu_launches": KERNELS_PER_STEP * args.steps,
-        "roofline": {"kernel": "grouped_gemm_tc_kernel (FC1+FC2, tcgen05)", "bound": "tensor",
+        "roofline": {"kernel": gemm_kernel_name(N), "bound": "tensor",
                      "achieved": round(achieved_tf, 1), "peak": peaks["tf_sus"], "unit": "TFLOP/s",
                      "frac": round(achieved_tf / peaks["tf_sus"], 3),
                      "frac_of_burst_peak": round(achieved_tf / peaks["tf"], 3),
