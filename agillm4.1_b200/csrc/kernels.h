@@ -157,6 +157,34 @@ cudaError_t grouped_gemm_pair(int dtype, const void* a, int64_t a_rows, const vo
                               int num_sms, cudaStream_t stream);
 cudaError_t grouped_gemm_swap(int dtype, const void* a, int64_t a_rows, const void* w, const GemmArgs& args, bool relu,
                               int num_sms, cudaStream_t stream);
+// Backward grouped GEMMs (grouped_gemm_bwd.cu).
+//   dgrad: c[r, n] = sum_k dc[r, k] * w[g(r), k, n]  (w [groups, k, n]; g from
+//          the tile table, row tiles of 128), masked by aux[r, n] > 0 when
+//          relu_mask (ReLU backward on the saved activation aux [rows, ld_aux]).
+//   wgrad: c[g, m, n] = sum_{r in segment g} dc[r, m] * act[r, n], the
+//          segment rows [seg_start[g], seg_start[g+1]) (whole 128-row tiles,
+//          zero padding rows); c is fp32 (out_f32, the value rounded to the
+//          compute dtype first) or the compute dtype.
+struct BwdGemmArgs {
+  void* c = nullptr;
+  int64_t ldc = 0;
+  int64_t c_rows = 0;          // dgrad: rows of c that exist
+  int m = 0;                   // wgrad: rows of each group's c
+  int n = 0;
+  int k = 0;                   // dgrad: inner dimension
+  int groups = 1;
+  const int32_t* tile_group = nullptr;  // dgrad
+  const int32_t* num_tiles = nullptr;   // dgrad
+  int max_tiles = 0;                    // dgrad
+  const int32_t* seg_start = nullptr;   // wgrad: [groups + 1]
+  const void* aux = nullptr;            // dgrad relu_mask: [rows, ld_aux]
+  int64_t ld_aux = 0;
+  int* err = nullptr;
+};
+cudaError_t grouped_gemm_dgrad(int dtype, const void* dc, int64_t rows, const void* w, const BwdGemmArgs& args,
+                               bool relu_mask, int num_sms, cudaStream_t stream);
+cudaError_t grouped_gemm_wgrad(int dtype, bool out_f32, const void* dc, const void* act, int64_t rows,
+                               const BwdGemmArgs& args, int num_sms, cudaStream_t stream);
 cudaError_t combine(int dtype, const void* y, const int32_t* row_of, const void* gates, int64_t n, int d, int k,
                     const void* shared_y, int n_shared, int64_t shared_stride, void* out, int num_sms,
                     cudaStream_t stream);

@@ -1,0 +1,958 @@
+// Training path of the MoE block: a forward that keeps what the backward
+// needs, and the backward, as replacements for PyTorch autograd through
+// MoEFFN.forward (agillm41.py:4389-4431).
+//
+// Two precision modes, the two the reference trains in:
+//
+// * same dtype (x, weights, out all fp32, bf16 or fp16): every op rounds to
+//   that dtype, as the reference does without autocast;
+// * autocast (x, out and the master weights fp32; compute in bf16 or fp16,
+//   torch.autocast as enabled by the reference's `amp()` helper,
+//   agillm41.py:3054-3066): the router and expert Linear layers run on
+//   16-bit casts of their inputs and weights, the router logits are `.float()`
+//   of the 16-bit GEMM output, the gates stay fp32 (`softmax(vals).to(x.dtype)`
+//   with x fp32) and the combine accumulates fp32 products of the 16-bit
+//   expert outputs into an fp32 `zeros_like(flat)`. In the backward the
+//   16-bit weight gradients are rounded to 16 bits and returned as fp32 (the
+//   cast's backward), and input gradients are summed in fp32.
+//
+// Forward (agm_moe_forward_train): [cast x to 16 bits] -> router (keeps the
+// fp32 logits) -> plan -> permute -> FC1 -> FC2 (y in its own buffer, so the
+// permuted input survives for the weight gradient) -> combine_train.
+//
+// Backward (agm_moe_backward), given dout = dL/dout:
+//   combine_bwd:  dy[row(t,r)] = dout[t] * g[t,r]; dgate[t,r] = <dout[t], y[row]>;
+//                 softmax-over-k (or top-1 straight-through) backward to the
+//                 router logits dl [N, 16] (zero-fills dy's padding rows)
+//   wgrad FC2:    dW2[e] = dy_e^T h_e         db2[e] = sum of dy_e's rows
+//   dgrad FC2:    dh = (dy @ W2[e]) * (h > 0)
+//   wgrad FC1:    dW1[e] = dh_e^T x_perm_e    db1[e] = sum of dh_e's rows
+//   dgrad FC1:    dx_perm = dh @ W1[e]
+//   router wgrad: dWr = dl^T x                (x rows read from x_perm)
+//   dx:           dx[t] = ((dx_perm[row(t,k-1)] + ... + dx_perm[row(t,0)]) + dl[t] @ Wr)
+// The order of the dx sum is the order in which autograd accumulates the
+// gradients of `flat`: the index_select nodes of the last rank run first and
+// the router's Linear, created first, runs last.
+#include <algorithm>
+#include <cstdio>
+#include <string>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "route_math.cuh"
+
+namespace agm {
+namespace {
+
+constexpr int kMaxE = AGM_MAX_EXPERTS;  // logits gradient rows are 16 wide
+constexpr int kZeroCtas = 8;            // CTAs zero-filling one expert's padding rows of dy
+constexpr int kColsumCols = 256;        // columns per segment-column-sum CTA (8 per lane)
+constexpr int kRouterCols = 1024;       // columns per router-wgrad CTA (4 per thread)
+
+// 8 consecutive values of T (or fp32) at p -> fp32.
+template <typename T>
+__device__ __forceinline__ void load8f(const T* p, float (&f)[8]) {
+  if constexpr (sizeof(T) == 4) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+    f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  } else {
+    unpack8<T>(__ldg(reinterpret_cast<const uint4*>(p)), f);
+  }
+}
+
+// fp32 -> 8 consecutive values of T (or fp32) at p (round to nearest even).
+template <typename T>
+__device__ __forceinline__ void store8f(T* p, const float (&f)[8]) {
+  if constexpr (sizeof(T) == 4) {
+    reinterpret_cast<float4*>(p)[0] = make_float4(f[0], f[1], f[2], f[3]);
+    reinterpret_cast<float4*>(p)[1] = make_float4(f[4], f[5], f[6], f[7]);
+  } else {
+    *reinterpret_cast<uint4*>(p) =
+        make_uint4(pack2<T>(f[0], f[1]), pack2<T>(f[2], f[3]), pack2<T>(f[4], f[5]), pack2<T>(f[6], f[7]));
+  }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// ---------------------------------------------------------------------------
+// fp32 -> 16-bit cast (autocast's input and weight casts)
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(256) cast_f32_kernel(const float* __restrict__ in, T* __restrict__ out, int64_t n) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t n8 = n / 8;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8; i += stride) {
+    float f[8];
+    load8f<float>(in + i * 8, f);
+    store8f<T>(out + i * 8, f);
+  }
+  for (int64_t i = n8 * 8 + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
+    out[i] = Traits<T>::from_f(in[i]);
+}
+
+// Gates of token t recomputed from the saved fp32 logits with the router's
+// own arithmetic: k >= 2 -> softmax over the chosen logits (fp32, exactly the
+// forward's values); k == 1 -> the straight-through value 1.
+template <int K_MAX>
+__device__ __forceinline__ void token_gates(const float* __restrict__ logits, const int32_t* __restrict__ idx,
+                                            int64_t t, int k, int E, int (&sel)[K_MAX], float (&g)[K_MAX]) {
+  float val[K_MAX];
+#pragma unroll
+  for (int r = 0; r < K_MAX; ++r) {
+    sel[r] = (r < k) ? idx[t * k + r] : 0;
+    if (sel[r] < 0 || sel[r] >= E) sel[r] = 0;  // the router never writes such ids
+    val[r] = (r < k) ? logits[t * E + sel[r]] : 0.f;
+  }
+  if (k == 1) {
+#pragma unroll
+    for (int r = 0; r < K_MAX; ++r) g[r] = (r == 0) ? 1.f : 0.f;
+  } else {
+    topk_gates<0, K_MAX>(val, k, g);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Combine for training (the saved fp32 logits give the gates):
+//   G == T (same dtype): out = ((0 + r(y0*r(g0))) + r(y1*r(g1))) ..., r() = round to T;
+//   G == float (autocast): out = (0 + y0*g0) + y1*g1 in fp32.
+//   k == 1: out = y (the straight-through gate is exactly 1).
+// ---------------------------------------------------------------------------
+template <typename T, typename G, int K_MAX>
+__global__ void __launch_bounds__(256) combine_train_kernel(const T* __restrict__ y, const int32_t* __restrict__ row_of,
+                                                            const float* __restrict__ logits,
+                                                            const int32_t* __restrict__ idx, int64_t n, int d, int k,
+                                                            int E, G* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+  const int lane = lane_id();
+  const int nc8 = d / 8;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + warp_id(); t < n; t += warps) {
+    int sel[K_MAX];
+    float g[K_MAX];
+    token_gates<K_MAX>(logits, idx, t, k, E, sel, g);
+    int64_t row[K_MAX];
+#pragma unroll
+    for (int r = 0; r < K_MAX; ++r) {
+      row[r] = (r < k) ? row_of[t * k + r] : 0;
+      if (sizeof(G) != 4) g[r] = round_to<T>(g[r]);  // weights.to(x.dtype)
+    }
+    for (int c = lane; c < nc8; c += 32) {
+      float acc[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+#pragma unroll
+      for (int r = 0; r < K_MAX; ++r) {
+        if (r < k) {
+          float v[8];
+          load8f<T>(y + row[r] * d + c * 8, v);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            if (k == 1) {
+              acc[i] = v[i];
+            } else if (sizeof(G) == 4) {
+              acc[i] = __fadd_rn(acc[i], __fmul_rn(v[i], g[r]));
+            } else {
+              acc[i] = round_to<T>(__fadd_rn(acc[i], round_to<T>(__fmul_rn(v[i], g[r]))));
+            }
+          }
+        }
+      }
+      store8f<G>(out + t * d + c * 8, acc);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Combine backward + routing backward.
+// One warp per token. For each rank r (row p = row_of[t, r]):
+//   dy[p]   = r_T(dout[t] * g'[r])          g' = r_T(g) (same dtype) or g (fp32)
+//   dg[r]   = sum_c dout[t,c] * y[p,c]      (products rounded to T in same-dtype
+//                                            mode, then the sum rounded to T)
+// then the gradient of the router logits (agillm41.py:4401-4419):
+//   k >= 2: dv = g * (dg - sum_j g_j dg_j)  (softmax over the k chosen), scattered
+//           to the chosen experts;
+//   k == 1: gate = r_T(p_c); dgate = dg / gate; dl_e = p_e * (dprob_e - p_c dgate)
+//           with dprob = dgate at the chosen expert (straight-through gate);
+// rounded to the logits' source dtype T (the `.float()` cast's backward).
+// CTAs past the token CTAs zero-fill dy's padding rows.
+// ---------------------------------------------------------------------------
+template <typename T, typename G, int K_MAX>
+__global__ void __launch_bounds__(256) combine_bwd_kernel(
+    const G* __restrict__ dout, const T* __restrict__ y, const int32_t* __restrict__ row_of,
+    const float* __restrict__ logits, const int32_t* __restrict__ idx, int64_t n, int d, int k, int E,
+    int tok_ctas, const int32_t* __restrict__ seg_start, const int32_t* __restrict__ counts, int64_t max_rows,
+    T* __restrict__ dy, T* __restrict__ dl) {
+  pdl_wait();
+  pdl_trigger();
+  const int lane = lane_id();
+  const int nc8 = d / 8;
+  if (static_cast<int>(blockIdx.x) >= tok_ctas) {
+    const int z = blockIdx.x - tok_ctas;
+    const int e = z / kZeroCtas;
+    const int64_t r0 = static_cast<int64_t>(seg_start[e]) + counts[e];
+    const int64_t r1 = min(static_cast<int64_t>(seg_start[e + 1]), max_rows);
+    const int nw = blockDim.x / 32;
+    const int nchunk = d * static_cast<int>(sizeof(T)) / 16;
+    for (int64_t r = r0 + (z % kZeroCtas) * nw + warp_id(); r < r1; r += kZeroCtas * nw) {
+      uint4* o = reinterpret_cast<uint4*>(dy + r * d);
+      for (int c = lane; c < nchunk; c += 32) o[c] = make_uint4(0, 0, 0, 0);
+    }
+    return;
+  }
+  const int64_t warps = static_cast<int64_t>(tok_ctas) * (blockDim.x / 32);
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + warp_id(); t < n; t += warps) {
+    int sel[K_MAX];
+    float g[K_MAX];
+    token_gates<K_MAX>(logits, idx, t, k, E, sel, g);
+    int64_t row[K_MAX];
+    float gm[K_MAX], dg[K_MAX];
+#pragma unroll
+    for (int r = 0; r < K_MAX; ++r) {
+      row[r] = (r < k) ? row_of[t * k + r] : 0;
+      gm[r] = (sizeof(G) == 4) ? g[r] : round_to<T>(g[r]);
+      dg[r] = 0.f;
+    }
+    for (int c = lane; c < nc8; c += 32) {
+      float go[8];
+      load8f<G>(dout + t * d + c * 8, go);
+#pragma unroll
+      for (int r = 0; r < K_MAX; ++r) {
+        if (r < k) {
+          float v[8], o[8];
+          load8f<T>(y + row[r] * d + c * 8, v);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            o[i] = __fmul_rn(go[i], gm[r]);  // rounded to T by the store
+            const float prod = __fmul_rn(go[i], v[i]);
+            dg[r] += (sizeof(G) == 4) ? prod : round_to<T>(prod);
+          }
+          store8f<T>(dy + row[r] * d + c * 8, o);
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < K_MAX; ++r) {
+      dg[r] = warp_sum(dg[r]);
+      if (sizeof(G) != 4) dg[r] = round_to<T>(dg[r]);
+    }
+    // Gradient of the logits: lane e owns expert e.
+    float dle = 0.f;
+    if (k == 1) {
+      float lg[kMaxE], ex[kMaxE];
+#pragma unroll
+      for (int e = 0; e < kMaxE; ++e) lg[e] = (e < E) ? logits[t * E + e] : 0.f;
+      const float s = softmax_terms(lg, E, ex);
+      const int c = sel[0];
+      float pc = 0.f, pe = 0.f;
+#pragma unroll
+      for (int e = 0; e < kMaxE; ++e) {
+        const float p = ex[e] / s;
+        if (e == c) pc = p;
+        if (e == lane) pe = p;
+      }
+      const float gate_pre = (sizeof(G) == 4) ? pc : round_to<T>(pc);   // probs[..].to(x.dtype)
+      const float gate = fmaxf(gate_pre, 1e-6f);                        // clamp_min(1e-6)
+      float dgate = __fdiv_rn(dg[0], gate);                             // d(gate / gate.detach())
+      if (sizeof(G) != 4) dgate = round_to<T>(dgate);
+      if (!(gate_pre >= 1e-6f)) dgate = 0.f;                            // clamp_min backward
+      const float s2 = __fmul_rn(pc, dgate);                            // sum_e p_e dprob_e
+      const float dprob = (lane == c) ? dgate : 0.f;
+      dle = __fmul_rn(pe, __fsub_rn(dprob, s2));
+    } else {
+      float prod[K_MAX];
+#pragma unroll
+      for (int r = 0; r < K_MAX; ++r) prod[r] = (r < k) ? __fmul_rn(g[r], dg[r]) : 0.f;
+      const float s = butterfly_sum_rt(prod, next_pow2_le32(k));
+#pragma unroll
+      for (int r = 0; r < K_MAX; ++r)
+        if (r < k && sel[r] == lane) dle = __fmul_rn(g[r], __fsub_rn(dg[r], s));
+    }
+    if (lane < kMaxE) dl[t * kMaxE + lane] = Traits<T>::from_f(lane < E ? dle : 0.f);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Per-expert column sums (bias gradients), deterministic:
+//   partial[s, g, c] = sum over rows of split s of segment g of m[row, c]
+//   out[g, c] = r_T(sum_s partial[s, g, c])   (stored as OutT)
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(256) seg_colsum_kernel(const T* __restrict__ m, int ncols,
+                                                         const int32_t* __restrict__ seg_start, int groups, int splits,
+                                                         float* __restrict__ partial) {
+  __shared__ float red[8][kColsumCols];
+  pdl_wait();
+  pdl_trigger();
+  const int g = blockIdx.y, s = blockIdx.z;
+  const int lane = lane_id(), w = warp_id();
+  const int c0 = blockIdx.x * kColsumCols + lane * 8;
+  const int64_t s0 = seg_start[g], s1 = seg_start[g + 1];
+  const int64_t per = (s1 - s0 + splits - 1) / splits;
+  const int64_t lo = s0 + s * per, hi = min(s1, lo + per);
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  if (c0 < ncols) {
+    for (int64_t r = lo + w; r < hi; r += 8) {
+      float v[8];
+      if (c0 + 8 <= ncols) {
+        load8f<T>(m + r * ncols + c0, v);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = (c0 + i < ncols) ? Traits<T>::to_f(m[r * ncols + c0 + i]) : 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] += v[i];
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) red[w][lane * 8 + i] = acc[i];
+  __syncthreads();
+  const int c = threadIdx.x;
+  const int col = blockIdx.x * kColsumCols + c;
+  if (col < ncols) {
+    float v = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v += red[i][c];
+    partial[(static_cast<int64_t>(s) * groups + g) * ncols + col] = v;
+  }
+}
+
+// out[i] = r_T(sum_p partial[p * part_stride + i]) for i < count, p in order.
+template <typename T, typename OutT>
+__global__ void __launch_bounds__(256) reduce_partials_kernel(const float* __restrict__ partial, int parts,
+                                                              int64_t part_stride, int64_t count,
+                                                              OutT* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float v = 0.f;
+    for (int p = 0; p < parts; ++p) v += partial[p * part_stride + i];
+    const float r = round_to<T>(v);
+    if constexpr (sizeof(OutT) == 4)
+      out[i] = r;
+    else
+      out[i] = Traits<OutT>::from_f(r);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Router weight gradient partials: partial[chunk, e, c] = sum over the
+// chunk's tokens of dl[t, e] * x[t, c], x[t] read from x_perm[row_of[t, 0]]
+// (the permuted copy of token t's router input).
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(256) router_wgrad_kernel(const T* __restrict__ dl, const T* __restrict__ xperm,
+                                                           const int32_t* __restrict__ row_of, int k, int64_t n,
+                                                           int d, int64_t tok_per_chunk,
+                                                           float* __restrict__ partial) {
+  pdl_wait();
+  pdl_trigger();
+  const int chunk = blockIdx.x;
+  const int c0 = blockIdx.y * kRouterCols + threadIdx.x * 4;
+  const int64_t t0 = chunk * tok_per_chunk, t1 = min(n, t0 + tok_per_chunk);
+  float acc[kMaxE][4];
+#pragma unroll
+  for (int e = 0; e < kMaxE; ++e)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[e][i] = 0.f;
+  if (c0 < d) {
+    for (int64_t t = t0; t < t1; ++t) {
+      float g[kMaxE];
+      load8f<T>(dl + t * kMaxE, *reinterpret_cast<float(*)[8]>(&g[0]));
+      load8f<T>(dl + t * kMaxE + 8, *reinterpret_cast<float(*)[8]>(&g[8]));
+      const T* xr = xperm + static_cast<int64_t>(row_of[t * k]) * d + c0;
+      float x[4];
+      if constexpr (sizeof(T) == 4) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(xr));
+        x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+      } else {
+        const uint2 u = __ldg(reinterpret_cast<const uint2*>(xr));
+        const uint4 u4 = make_uint4(u.x, u.y, 0, 0);
+        float f[8];
+        unpack8<T>(u4, f);
+        x[0] = f[0]; x[1] = f[1]; x[2] = f[2]; x[3] = f[3];
+      }
+#pragma unroll
+      for (int e = 0; e < kMaxE; ++e)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[e][i] = fmaf(g[e], x[i], acc[e][i]);
+    }
+#pragma unroll
+    for (int e = 0; e < kMaxE; ++e)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) partial[(static_cast<int64_t>(chunk) * kMaxE + e) * d + c0 + i] = acc[e][i];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Input gradient: dx[t] = ((dx_perm[row(t,k-1)] + ... + dx_perm[row(t,0)]) + r_T(dl[t] @ Wr)),
+// each add rounded to G (T in same-dtype mode, fp32 in autocast). Wr [E, d]
+// (compute dtype) is staged in shared memory.
+// ---------------------------------------------------------------------------
+template <typename T, typename G, int K_MAX>
+__global__ void __launch_bounds__(256) dx_kernel(const T* __restrict__ dxp, const int32_t* __restrict__ row_of,
+                                                 const T* __restrict__ dl, const T* __restrict__ wr, int64_t n,
+                                                 int d, int k, int E, G* __restrict__ dx) {
+  extern __shared__ uint8_t smem_raw[];
+  T* w_s = reinterpret_cast<T*>(smem_raw);
+  pdl_wait();
+  pdl_trigger();
+  {
+    const int nchunk = E * d * static_cast<int>(sizeof(T)) / 16;
+    const uint4* src = reinterpret_cast<const uint4*>(wr);
+    uint4* dst = reinterpret_cast<uint4*>(w_s);
+    for (int i = threadIdx.x; i < nchunk; i += blockDim.x) dst[i] = __ldg(src + i);
+  }
+  __syncthreads();
+  const int lane = lane_id();
+  const int nc8 = d / 8;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + warp_id(); t < n; t += warps) {
+    float g[kMaxE];
+    load8f<T>(dl + t * kMaxE, *reinterpret_cast<float(*)[8]>(&g[0]));
+    load8f<T>(dl + t * kMaxE + 8, *reinterpret_cast<float(*)[8]>(&g[8]));
+    int64_t row[K_MAX];
+#pragma unroll
+    for (int r = 0; r < K_MAX; ++r) row[r] = (r < k) ? row_of[t * k + r] : 0;
+    for (int c = lane; c < nc8; c += 32) {
+      float rt[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) rt[i] = 0.f;
+      for (int e = 0; e < E; ++e) {
+        float w[8];
+        if constexpr (sizeof(T) == 4) {
+          const float4* p = reinterpret_cast<const float4*>(w_s + static_cast<int64_t>(e) * d + c * 8);
+          const float4 a = p[0], b = p[1];
+          w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w; w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+        } else {
+          unpack8<T>(*reinterpret_cast<const uint4*>(w_s + static_cast<int64_t>(e) * d + c * 8), w);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) rt[i] = fmaf(g[e], w[i], rt[i]);
+      }
+      float acc[8];
+      load8f<T>(dxp + row[k - 1] * d + c * 8, acc);
+      for (int r = k - 2; r >= 0; --r) {
+        float v[8];
+        load8f<T>(dxp + row[r] * d + c * 8, v);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          acc[i] = (sizeof(G) == 4) ? __fadd_rn(acc[i], v[i]) : round_to<T>(__fadd_rn(acc[i], v[i]));
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float rv = round_to<T>(rt[i]);
+        acc[i] = (sizeof(G) == 4) ? __fadd_rn(acc[i], rv) : round_to<T>(__fadd_rn(acc[i], rv));
+      }
+      store8f<G>(dx + t * d + c * 8, acc);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host helpers
+// ---------------------------------------------------------------------------
+int fail(int code, const std::string& msg) {
+  set_last_error(msg);
+  return code;
+}
+int cuda_fail(cudaError_t e, const char* where) {
+  set_last_error(std::string(where) + ": " + cudaGetErrorString(e));
+  return AGM_ERR_CUDA;
+}
+int esize(int dtype) { return dtype == AGM_F32 ? 4 : (dtype == AGM_BF16 || dtype == AGM_F16) ? 2 : 0; }
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+int64_t rup(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+  return n;
+}
+
+struct Carve {
+  uint8_t* base;
+  size_t off = 0;
+  explicit Carve(void* b) : base(static_cast<uint8_t*>(b)) {}
+  template <typename P>
+  P* take(size_t bytes) {
+    off = (off + 255) & ~size_t(255);
+    P* p = reinterpret_cast<P*>(base ? base + off : nullptr);
+    off += bytes;
+    return p;
+  }
+};
+
+// What the training forward keeps for the backward (plus its own temporaries).
+struct Saved {
+  int* err;
+  float* logits;     // [n, E] fp32 (rounded like the reference's router output)
+  int32_t* idx;      // [n, k]
+  void* gates;       // [n, k] compute dtype (router output, unused afterwards)
+  int32_t* block_hist;
+  int32_t* block_off;
+  int32_t* counts;   // [E]
+  int32_t* seg_start;  // [E + 1]
+  int32_t* num_tiles;
+  int32_t* tile_expert;
+  int32_t* row_of;   // [n, k]
+  int32_t* token_of; // [rows]
+  void* xb;          // [n, d] compute dtype (autocast: the cast input)
+  void* x_perm;      // [rows, d]
+  void* h;           // [rows, H]
+  void* y;           // [rows, d]
+  size_t bytes;
+};
+
+Saved carve_saved(void* ws, int64_t n, int d, int E, int k, int H, int eb, bool amp) {
+  Carve c(ws);
+  Saved S;
+  const int64_t nb = agm_dispatch_blocks(n);
+  const int64_t rows = agm_max_rows(n, k, E);
+  S.err = c.take<int>(sizeof(int));
+  S.logits = c.take<float>(sizeof(float) * n * E);
+  S.idx = c.take<int32_t>(sizeof(int32_t) * n * k);
+  S.gates = c.take<void>(static_cast<size_t>(eb) * n * k);
+  S.block_hist = c.take<int32_t>(sizeof(int32_t) * nb * E);
+  S.block_off = c.take<int32_t>(sizeof(int32_t) * nb * E);
+  S.counts = c.take<int32_t>(sizeof(int32_t) * E);
+  S.seg_start = c.take<int32_t>(sizeof(int32_t) * (E + 1));
+  S.num_tiles = c.take<int32_t>(sizeof(int32_t));
+  S.tile_expert = c.take<int32_t>(sizeof(int32_t) * std::max<int64_t>(rows / AGM_TILE_M, 1));
+  S.row_of = c.take<int32_t>(sizeof(int32_t) * n * k);
+  S.token_of = c.take<int32_t>(sizeof(int32_t) * std::max<int64_t>(rows, 1));
+  S.xb = amp ? c.take<void>(static_cast<size_t>(eb) * n * d) : nullptr;
+  S.x_perm = c.take<void>(static_cast<size_t>(eb) * rows * d);
+  S.h = c.take<void>(static_cast<size_t>(eb) * rows * H);
+  S.y = c.take<void>(static_cast<size_t>(eb) * rows * d);
+  S.bytes = (c.off + 255) & ~size_t(255);
+  return S;
+}
+
+int colsum_splits(int ncols, int E) {
+  const int cb = (ncols + kColsumCols - 1) / kColsumCols;
+  return std::max(1, std::min(64, (4 * 148 + cb * E - 1) / (cb * E)));
+}
+int router_chunks(int64_t n, int d) {
+  const int cb = (d + kRouterCols - 1) / kRouterCols;
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(n, 2 * 148 / cb)));
+}
+
+struct BwdWs {
+  int* err;
+  void* dy;     // [rows, d]; later dx_perm
+  void* dh;     // [rows, H]
+  void* dl;     // [n, 16]
+  float* colsum;  // [splits, E, max(d, H)]
+  float* rpart;   // [chunks, 16, d]
+  size_t bytes;
+};
+
+BwdWs carve_bwd(void* ws, int64_t n, int d, int E, int k, int H, int eb) {
+  Carve c(ws);
+  BwdWs B;
+  const int64_t rows = agm_max_rows(n, k, E);
+  const int64_t cs = std::max<int64_t>(static_cast<int64_t>(colsum_splits(d, E)) * d,
+                                       static_cast<int64_t>(colsum_splits(H, E)) * H) * E;
+  B.err = c.take<int>(sizeof(int));
+  B.dy = c.take<void>(static_cast<size_t>(eb) * rows * d);
+  B.dh = c.take<void>(static_cast<size_t>(eb) * rows * H);
+  B.dl = c.take<void>(static_cast<size_t>(eb) * n * kMaxE);
+  B.colsum = c.take<float>(sizeof(float) * cs);
+  B.rpart = c.take<float>(sizeof(float) * router_chunks(n, d) * kMaxE * d);
+  B.bytes = (c.off + 255) & ~size_t(255);
+  return B;
+}
+
+template <typename T>
+cudaError_t launch_cast(const float* in, void* out, int64_t n, cudaStream_t s) {
+  const int64_t blocks = std::min<int64_t>((n / 8 + 255) / 256 + 1, 148 * 8);
+  return launch_kernel(cast_f32_kernel<T>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, in,
+                       static_cast<T*>(out), n);
+}
+
+cudaError_t cast_any(int dtype, const float* in, void* out, int64_t n, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  if (dtype == AGM_BF16) return launch_cast<__nv_bfloat16>(in, out, n, s);
+  if (dtype == AGM_F16) return launch_cast<__half>(in, out, n, s);
+  return cudaErrorInvalidValue;
+}
+
+template <typename T, typename G>
+cudaError_t launch_combine_train(const Saved& S, int64_t n, int d, int k, int E, void* out, cudaStream_t s) {
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>((n + 7) / 8, 148 * 8));
+  const T* y = static_cast<const T*>(S.y);
+  G* o = static_cast<G*>(out);
+  if (k <= 2)
+    return launch_kernel(combine_train_kernel<T, G, 2>, dim3(grid), dim3(256), 0, s, y, S.row_of, S.logits, S.idx, n,
+                         d, k, E, o);
+  if (k <= 4)
+    return launch_kernel(combine_train_kernel<T, G, 4>, dim3(grid), dim3(256), 0, s, y, S.row_of, S.logits, S.idx, n,
+                         d, k, E, o);
+  return launch_kernel(combine_train_kernel<T, G, 16>, dim3(grid), dim3(256), 0, s, y, S.row_of, S.logits, S.idx, n,
+                       d, k, E, o);
+}
+
+template <typename T, typename G>
+cudaError_t launch_combine_bwd(const void* dout, const Saved& S, const BwdWs& B, int64_t n, int d, int k, int E,
+                               int64_t rows, cudaStream_t s) {
+  const int tok_ctas = static_cast<int>(std::min<int64_t>((n + 7) / 8, 148 * 8));
+  const unsigned grid = static_cast<unsigned>(tok_ctas + E * kZeroCtas);
+  const G* go = static_cast<const G*>(dout);
+  const T* y = static_cast<const T*>(S.y);
+  T* dy = static_cast<T*>(B.dy);
+  T* dl = static_cast<T*>(B.dl);
+  if (k <= 2)
+    return launch_kernel(combine_bwd_kernel<T, G, 2>, dim3(grid), dim3(256), 0, s, go, y, S.row_of, S.logits, S.idx,
+                         n, d, k, E, tok_ctas, S.seg_start, S.counts, rows, dy, dl);
+  if (k <= 4)
+    return launch_kernel(combine_bwd_kernel<T, G, 4>, dim3(grid), dim3(256), 0, s, go, y, S.row_of, S.logits, S.idx,
+                         n, d, k, E, tok_ctas, S.seg_start, S.counts, rows, dy, dl);
+  return launch_kernel(combine_bwd_kernel<T, G, 16>, dim3(grid), dim3(256), 0, s, go, y, S.row_of, S.logits, S.idx,
+                       n, d, k, E, tok_ctas, S.seg_start, S.counts, rows, dy, dl);
+}
+
+template <typename T, typename OutT>
+cudaError_t launch_colsum(const void* m, int ncols, const int32_t* seg_start, int E, float* partial, void* out,
+                          cudaStream_t s) {
+  const int splits = colsum_splits(ncols, E);
+  dim3 grid(static_cast<unsigned>((ncols + kColsumCols - 1) / kColsumCols), static_cast<unsigned>(E),
+            static_cast<unsigned>(splits));
+  cudaError_t e = launch_kernel(seg_colsum_kernel<T>, grid, dim3(256), 0, s, static_cast<const T*>(m), ncols,
+                                seg_start, E, splits, partial);
+  if (e != cudaSuccess) return e;
+  const int64_t count = static_cast<int64_t>(E) * ncols;
+  const unsigned g2 = static_cast<unsigned>(std::min<int64_t>((count + 255) / 256, 148 * 4));
+  return launch_kernel(reduce_partials_kernel<T, OutT>, dim3(g2), dim3(256), 0, s,
+                       static_cast<const float*>(partial), splits, count, count, static_cast<OutT*>(out));
+}
+
+template <typename T, typename OutT>
+cudaError_t launch_router_wgrad(const BwdWs& B, const Saved& S, int64_t n, int d, int k, int E, void* dwr,
+                                cudaStream_t s) {
+  const int chunks = router_chunks(n, d);
+  const int64_t per = (n + chunks - 1) / chunks;
+  dim3 grid(static_cast<unsigned>(chunks), static_cast<unsigned>((d + kRouterCols - 1) / kRouterCols));
+  cudaError_t e = launch_kernel(router_wgrad_kernel<T>, grid, dim3(256), 0, s, static_cast<const T*>(B.dl),
+                                static_cast<const T*>(S.x_perm), S.row_of, k, n, d, per, B.rpart);
+  if (e != cudaSuccess) return e;
+  // Chunk c's partial is [16, d] at c * 16 * d; its first E rows, E * d
+  // contiguous values, are the router weight's.
+  const int64_t count = static_cast<int64_t>(E) * d;
+  const unsigned g2 = static_cast<unsigned>(std::min<int64_t>((count + 255) / 256, 148 * 4));
+  return launch_kernel(reduce_partials_kernel<T, OutT>, dim3(g2), dim3(256), 0, s,
+                       static_cast<const float*>(B.rpart), chunks, static_cast<int64_t>(kMaxE) * d, count,
+                       static_cast<OutT*>(dwr));
+}
+
+template <typename T, typename G>
+cudaError_t launch_dx(const BwdWs& B, const Saved& S, const void* wr, int64_t n, int d, int k, int E, void* dx,
+                      cudaStream_t s) {
+  const int smem = E * d * static_cast<int>(sizeof(T));
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>((n + 7) / 8, 148 * 2));
+  const T* dxp = static_cast<const T*>(B.dy);
+  const T* dl = static_cast<const T*>(B.dl);
+  const T* w = static_cast<const T*>(wr);
+  G* o = static_cast<G*>(dx);
+  cudaError_t e;
+  if (k <= 2) {
+    if ((e = ensure_dynamic_smem(reinterpret_cast<const void*>(dx_kernel<T, G, 2>), smem)) != cudaSuccess) return e;
+    return launch_kernel(dx_kernel<T, G, 2>, dim3(grid), dim3(256), smem, s, dxp, S.row_of, dl, w, n, d, k, E, o);
+  }
+  if (k <= 4) {
+    if ((e = ensure_dynamic_smem(reinterpret_cast<const void*>(dx_kernel<T, G, 4>), smem)) != cudaSuccess) return e;
+    return launch_kernel(dx_kernel<T, G, 4>, dim3(grid), dim3(256), smem, s, dxp, S.row_of, dl, w, n, d, k, E, o);
+  }
+  if ((e = ensure_dynamic_smem(reinterpret_cast<const void*>(dx_kernel<T, G, 16>), smem)) != cudaSuccess) return e;
+  return launch_kernel(dx_kernel<T, G, 16>, dim3(grid), dim3(256), smem, s, dxp, S.row_of, dl, w, n, d, k, E, o);
+}
+
+}  // namespace
+}  // namespace agm
+
+// ---------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------
+namespace {
+
+int check_train_args(int x_dtype, int dtype, int64_t n, int d, int E, int k, int H) {
+  if (!agm::esize(dtype) || !agm::esize(x_dtype)) return agm::fail(AGM_ERR_ARG, "bad dtype code");
+  if (x_dtype != dtype && !(x_dtype == AGM_F32 && dtype != AGM_F32))
+    return agm::fail(AGM_ERR_ARG, "x_dtype must equal dtype, or be AGM_F32 with a 16-bit dtype (autocast)");
+  const int eb = agm::esize(dtype);
+  if (n < 0) return agm::fail(AGM_ERR_ARG, "n_tokens < 0");
+  if (E < 1 || E > AGM_MAX_EXPERTS) return agm::fail(AGM_ERR_UNSUPPORTED, "number of experts must be in [1, 16]");
+  if (k < 1 || k > E) return agm::fail(AGM_ERR_ARG, "top_k must be in [1, n_experts]");
+  if (d <= 0 || d % 8 || H <= 0 || H % 8)
+    return agm::fail(AGM_ERR_UNSUPPORTED, "d and hidden must be positive multiples of 8");
+  if ((static_cast<int64_t>(d) * eb) % 16 || (static_cast<int64_t>(H) * eb) % 16)
+    return agm::fail(AGM_ERR_UNSUPPORTED, "d and hidden must be multiples of 16 bytes of the dtype");
+  if (agm_max_rows(n, k, E) > INT32_MAX) return agm::fail(AGM_ERR_UNSUPPORTED, "too many permuted rows");
+  if (dtype != AGM_F32 && !agm::router_tc_supported(d))
+    return agm::fail(AGM_ERR_UNSUPPORTED, "the tensor-core router does not support this d");
+  if (dtype == AGM_F32 && agm::router_smem_bytes(d, E) > 227 * 1024)
+    return agm::fail(AGM_ERR_UNSUPPORTED, "router weight does not fit in shared memory for this d");
+  if (static_cast<int64_t>(E) * d * eb > 227 * 1024)
+    return agm::fail(AGM_ERR_UNSUPPORTED, "router weight does not fit in shared memory for the input gradient");
+  return AGM_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t agm_moe_train_saved_bytes(int64_t n_tokens, int d, int n_experts, int top_k, int hidden, int x_dtype,
+                                 int dtype) {
+  const int eb = agm::esize(dtype);
+  if (!eb || n_tokens < 0 || d <= 0 || n_experts < 1 || top_k < 1 || hidden <= 0) return 0;
+  return agm::carve_saved(nullptr, n_tokens, d, n_experts, top_k, hidden, eb, x_dtype != dtype).bytes;
+}
+
+size_t agm_moe_backward_workspace_bytes(int64_t n_tokens, int d, int n_experts, int top_k, int hidden, int dtype) {
+  const int eb = agm::esize(dtype);
+  if (!eb || n_tokens < 0 || d <= 0 || n_experts < 1 || top_k < 1 || hidden <= 0) return 0;
+  return agm::carve_bwd(nullptr, n_tokens, d, n_experts, top_k, hidden, eb).bytes;
+}
+
+int agm_cast_f32(const float* in, void* out, int dtype, int64_t n, void* stream) {
+  if (dtype != AGM_BF16 && dtype != AGM_F16) return agm::fail(AGM_ERR_ARG, "dtype must be AGM_BF16 or AGM_F16");
+  if (n < 0) return agm::fail(AGM_ERR_ARG, "n < 0");
+  if (n == 0) return AGM_OK;
+  if (!in || !out || !agm::al16(in) || !agm::al16(out))
+    return agm::fail(AGM_ERR_ARG, "in and out must be non-null and 16-byte aligned");
+  cudaError_t e = agm::cast_any(dtype, in, out, n, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? AGM_OK : agm::cuda_fail(e, "cast");
+}
+
+int agm_moe_forward_train(const void* x, int x_dtype, int dtype, int64_t n_tokens, int d, int n_experts, int top_k,
+                          int hidden, const void* w_router, const void* w1, const void* b1, const void* w2,
+                          const void* b2, void* out, void* saved, size_t saved_bytes, int32_t* counts_out, int flags,
+                          void* stream_) {
+  int rc = check_train_args(x_dtype, dtype, n_tokens, d, n_experts, top_k, hidden);
+  if (rc) return rc;
+  if (!x || !w_router || !w1 || !b1 || !w2 || !b2 || !out || !saved) return agm::fail(AGM_ERR_ARG, "null pointer");
+  const void* ptrs[] = {x, w_router, w1, b1, w2, b2, out, saved};
+  for (const void* p : ptrs)
+    if (!agm::al16(p)) return agm::fail(AGM_ERR_ARG, "all tensors must be 16-byte aligned");
+  const int eb = agm::esize(dtype);
+  const bool amp = x_dtype != dtype;
+  agm::Saved S = agm::carve_saved(saved, n_tokens, d, n_experts, top_k, hidden, eb, amp);
+  if (S.bytes > saved_bytes) return agm::fail(AGM_ERR_WORKSPACE, "saved-state buffer too small");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  agm::PdlScope pdl_scope(!(flags & AGM_FLAG_NO_PDL));
+  cudaError_t e = cudaMemsetAsync(S.err, 0, sizeof(int), stream);
+  if (e != cudaSuccess) return agm::cuda_fail(e, "memset");
+  if (n_tokens == 0) {
+    e = counts_out ? cudaMemsetAsync(counts_out, 0, sizeof(int32_t) * n_experts, stream) : cudaSuccess;
+    return e == cudaSuccess ? AGM_OK : agm::cuda_fail(e, "memset");
+  }
+  const int64_t rows = agm_max_rows(n_tokens, top_k, n_experts);
+  const int sms = agm::sm_count();
+  const void* xin = x;
+  if (amp) {
+    e = agm::cast_any(dtype, static_cast<const float*>(x), S.xb, n_tokens * d, stream);
+    if (e != cudaSuccess) return agm::cuda_fail(e, "cast x");
+    xin = S.xb;
+  }
+  e = agm::router_topk(dtype, xin, w_router, n_tokens, d, n_experts, top_k, flags & AGM_FLAG_TIE_LOW_FIRST, nullptr,
+                       S.logits, S.idx, S.gates, S.block_hist, S.err, sms, stream);
+  if (e != cudaSuccess) return agm::cuda_fail(e, "router_topk");
+  const bool pair = dtype != AGM_F32 && !(flags & AGM_FLAG_NO_PAIR) &&
+                    static_cast<int64_t>(top_k) * n_tokens >= AGM_PAIR_MIN_ROWS;
+  const int max_tiles = static_cast<int>(rows / AGM_TILE_M);
+  e = agm::dispatch_plan(S.block_hist, static_cast<int>(agm_dispatch_blocks(n_tokens)), n_experts, rows, max_tiles,
+                         pair ? AGM_PAIR_ROWS : AGM_TILE_M, S.block_off, S.counts, S.seg_start, S.tile_expert,
+                         S.num_tiles, S.token_of, S.err, stream);
+  if (e != cudaSuccess) return agm::cuda_fail(e, "dispatch_plan");
+  if (counts_out) {
+    e = cudaMemcpyAsync(counts_out, S.counts, sizeof(int32_t) * n_experts, cudaMemcpyDeviceToDevice, stream);
+    if (e != cudaSuccess) return agm::cuda_fail(e, "counts copy");
+  }
+  e = agm::permute_rows(xin, eb, n_tokens, d, top_k, n_experts, S.idx, S.block_off, S.seg_start, S.counts, rows,
+                        S.x_perm, S.row_of, S.token_of, S.err, stream);
+  if (e != cudaSuccess) return agm::cuda_fail(e, "permute");
+  agm::GemmArgs g1;
+  g1.c = S.h;
+  g1.ldc = hidden;
+  g1.c_rows = rows;
+  g1.bias = b1;
+  g1.n = hidden;
+  g1.k = d;
+  g1.groups = n_experts;
+  g1.tile_group = S.tile_expert;
+  g1.num_tiles = S.num_tiles;
+  g1.max_tiles = max_tiles;
+  g1.err = S.err;
+  // Row-tile GEMMs only (no swapped operands): the backward reads whole
+  // 128-row tiles of h, so its padding rows must hold finite values.
+  e = agm::grouped_gemm(dtype, S.x_perm, rows, w1, g1, true, sms, stream, pair ? AGM_GEMM_PAIR : 0);
+  if (e != cudaSuccess) return agm::cuda_fail(e, "grouped_gemm fc1");
+  agm::GemmArgs g2 = g1;
+  g2.c = S.y;
+  g2.ldc = d;
+  g2.bias = b2;
+  g2.n = d;
+  g2.k = hidden;
+  e = agm::grouped_gemm(dtype, S.h, rows, w2, g2, false, sms, stream, pair ? AGM_GEMM_PAIR : 0);
+  if (e != cudaSuccess) return agm::cuda_fail(e, "grouped_gemm fc2");
+  switch (dtype) {
+    case AGM_F32: e = agm::launch_combine_train<float, float>(S, n_tokens, d, top_k, n_experts, out, stream); break;
+    case AGM_BF16:
+      e = amp ? agm::launch_combine_train<__nv_bfloat16, float>(S, n_tokens, d, top_k, n_experts, out, stream)
+              : agm::launch_combine_train<__nv_bfloat16, __nv_bfloat16>(S, n_tokens, d, top_k, n_experts, out, stream);
+      break;
+    default:
+      e = amp ? agm::launch_combine_train<__half, float>(S, n_tokens, d, top_k, n_experts, out, stream)
+              : agm::launch_combine_train<__half, __half>(S, n_tokens, d, top_k, n_experts, out, stream);
+  }
+  return e == cudaSuccess ? AGM_OK : agm::cuda_fail(e, "combine_train");
+}
+
+int agm_moe_backward(const void* dout, int x_dtype, int dtype, int64_t n_tokens, int d, int n_experts, int top_k,
+                     int hidden, const void* w_router, const void* w1, const void* w2, const void* saved,
+                     size_t saved_bytes, void* dx, void* dw_router, void* dw1, void* db1, void* dw2, void* db2,
+                     void* workspace, size_t workspace_bytes, int flags, void* stream_) {
+  int rc = check_train_args(x_dtype, dtype, n_tokens, d, n_experts, top_k, hidden);
+  if (rc) return rc;
+  if (!dout || !w_router || !w1 || !w2 || !saved || !dx || !dw_router || !dw1 || !db1 || !dw2 || !db2 || !workspace)
+    return agm::fail(AGM_ERR_ARG, "null pointer");
+  const void* ptrs[] = {dout, w_router, w1, w2, saved, dx, dw_router, dw1, db1, dw2, db2, workspace};
+  for (const void* p : ptrs)
+    if (!agm::al16(p)) return agm::fail(AGM_ERR_ARG, "all tensors must be 16-byte aligned");
+  const int eb = agm::esize(dtype);
+  const bool amp = x_dtype != dtype;
+  agm::Saved S = agm::carve_saved(const_cast<void*>(saved), n_tokens, d, n_experts, top_k, hidden, eb, amp);
+  if (S.bytes > saved_bytes) return agm::fail(AGM_ERR_WORKSPACE, "saved-state buffer too small");
+  agm::BwdWs B = agm::carve_bwd(workspace, n_tokens, d, n_experts, top_k, hidden, eb);
+  if (B.bytes > workspace_bytes) return agm::fail(AGM_ERR_WORKSPACE, "workspace too small");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  agm::PdlScope pdl_scope(!(flags & AGM_FLAG_NO_PDL));
+  cudaError_t e = cudaMemsetAsync(B.err, 0, sizeof(int), stream);
+  if (e != cudaSuccess) return agm::cuda_fail(e, "memset");
+  const int xe = agm::esize(x_dtype);
+  if (n_tokens == 0) {
+    // No tokens: every gradient is zero.
+    const size_t sizes[] = {static_cast<size_t>(xe) * n_experts * d, static_cast<size_t>(xe) * n_experts * hidden * d,
+                            static_cast<size_t>(xe) * n_experts * hidden, static_cast<size_t>(xe) * n_experts * d * hidden,
+                            static_cast<size_t>(xe) * n_experts * d};
+    void* outs[] = {dw_router, dw1, db1, dw2, db2};
+    for (int i = 0; i < 5 && e == cudaSuccess; ++i) e = cudaMemsetAsync(outs[i], 0, sizes[i], stream);
+    return e == cudaSuccess ? AGM_OK : agm::cuda_fail(e, "memset");
+  }
+  const int64_t rows = agm_max_rows(n_tokens, top_k, n_experts);
+  const int sms = agm::sm_count();
+  const int max_tiles = static_cast<int>(rows / AGM_TILE_M);
+
+  // 1. combine + routing backward -> dy, dl
+  switch (dtype) {
+    case AGM_F32: e = agm::launch_combine_bwd<float, float>(dout, S, B, n_tokens, d, top_k, n_experts, rows, stream); break;
+    case AGM_BF16:
+      e = amp ? agm::launch_combine_bwd<__nv_bfloat16, float>(dout, S, B, n_tokens, d, top_k, n_experts, rows, stream)
+              : agm::launch_combine_bwd<__nv_bfloat16, __nv_bfloat16>(dout, S, B, n_tokens, d, top_k, n_experts, rows,
+                                                                      stream);
+      break;
+    default:
+      e = amp ? agm::launch_combine_bwd<__half, float>(dout, S, B, n_tokens, d, top_k, n_experts, rows, stream)
+              : agm::launch_combine_bwd<__half, __half>(dout, S, B, n_tokens, d, top_k, n_experts, rows, stream);
+  }
+  if (e != cudaSuccess) return agm::cuda_fail(e, "combine_bwd");
+
+  // 2. FC2 weight and bias gradients: dW2[e] [d, H] = dy_e^T h_e, db2 = colsum(dy)
+  agm::BwdGemmArgs w2a;
+  w2a.c = dw2;
+  w2a.m = d;
+  w2a.n = hidden;
+  w2a.groups = n_experts;
+  w2a.seg_start = S.seg_start;
+  w2a.err = B.err;
+  e = agm::grouped_gemm_wgrad(dtype, amp, B.dy, S.h, rows, w2a, sms, stream);
+  if (e != cudaSuccess) return agm::cuda_fail(e, "wgrad fc2");
+  // 3. FC2 input gradient through the ReLU: dh = (dy @ W2[e]) * (h > 0)
+  agm::BwdGemmArgs d2;
+  d2.c = B.dh;
+  d2.ldc = hidden;
+  d2.c_rows = rows;
+  d2.n = hidden;
+  d2.k = d;
+  d2.groups = n_experts;
+  d2.tile_group = S.tile_expert;
+  d2.num_tiles = S.num_tiles;
+  d2.max_tiles = max_tiles;
+  d2.aux = S.h;
+  d2.ld_aux = hidden;
+  d2.err = B.err;
+  e = agm::grouped_gemm_dgrad(dtype, B.dy, rows, w2, d2, true, sms, stream);
+  if (e != cudaSuccess) return agm::cuda_fail(e, "dgrad fc2");
+  // 4. bias gradients (dy is still intact: dgrad wrote dh)
+  auto colsum = [&](const void* m, int ncols, void* out) -> cudaError_t {
+    switch (dtype) {
+      case AGM_F32: return agm::launch_colsum<float, float>(m, ncols, S.seg_start, n_experts, B.colsum, out, stream);
+      case AGM_BF16:
+        return amp ? agm::launch_colsum<__nv_bfloat16, float>(m, ncols, S.seg_start, n_experts, B.colsum, out, stream)
+                   : agm::launch_colsum<__nv_bfloat16, __nv_bfloat16>(m, ncols, S.seg_start, n_experts, B.colsum, out,
+                                                                      stream);
+      default:
+        return amp ? agm::launch_colsum<__half, float>(m, ncols, S.seg_start, n_experts, B.colsum, out, stream)
+                   : agm::launch_colsum<__half, __half>(m, ncols, S.seg_start, n_experts, B.colsum, out, stream);
+    }
+  };
+  e = colsum(B.dy, d, db2);
+  if (e != cudaSuccess) return agm::cuda_fail(e, "db2");
+  e = colsum(B.dh, hidden, db1);
+  if (e != cudaSuccess) return agm::cuda_fail(e, "db1");
+  // 5. FC1 weight gradient: dW1[e] [H, d] = dh_e^T x_perm_e
+  agm::BwdGemmArgs w1a = w2a;
+  w1a.c = dw1;
+  w1a.m = hidden;
+  w1a.n = d;
+  e = agm::grouped_gemm_wgrad(dtype, amp, B.dh, S.x_perm, rows, w1a, sms, stream);
+  if (e != cudaSuccess) return agm::cuda_fail(e, "wgrad fc1");
+  // 6. FC1 input gradient: dx_perm = dh @ W1[e], into dy's buffer
+  agm::BwdGemmArgs d1 = d2;
+  d1.c = B.dy;
+  d1.ldc = d;
+  d1.n = d;
+  d1.k = hidden;
+  d1.aux = nullptr;
+  e = agm::grouped_gemm_dgrad(dtype, B.dh, rows, w1, d1, false, sms, stream);
+  if (e != cudaSuccess) return agm::cuda_fail(e, "dgrad fc1");
+  // 7. router weight gradient: dWr = dl^T x
+  switch (dtype) {
+    case AGM_F32: e = agm::launch_router_wgrad<float, float>(B, S, n_tokens, d, top_k, n_experts, dw_router, stream); break;
+    case AGM_BF16:
+      e = amp ? agm::launch_router_wgrad<__nv_bfloat16, float>(B, S, n_tokens, d, top_k, n_experts, dw_router, stream)
+              : agm::launch_router_wgrad<__nv_bfloat16, __nv_bfloat16>(B, S, n_tokens, d, top_k, n_experts, dw_router,
+                                                                       stream);
+      break;
+    default:
+      e = amp ? agm::launch_router_wgrad<__half, float>(B, S, n_tokens, d, top_k, n_experts, dw_router, stream)
+              : agm::launch_router_wgrad<__half, __half>(B, S, n_tokens, d, top_k, n_experts, dw_router, stream);
+  }
+  if (e != cudaSuccess) return agm::cuda_fail(e, "router wgrad");
+  // 8. input gradient
+  switch (dtype) {
+    case AGM_F32: e = agm::launch_dx<float, float>(B, S, w_router, n_tokens, d, top_k, n_experts, dx, stream); break;
+    case AGM_BF16:
+      e = amp ? agm::launch_dx<__nv_bfloat16, float>(B, S, w_router, n_tokens, d, top_k, n_experts, dx, stream)
+              : agm::launch_dx<__nv_bfloat16, __nv_bfloat16>(B, S, w_router, n_tokens, d, top_k, n_experts, dx, stream);
+      break;
+    default:
+      e = amp ? agm::launch_dx<__half, float>(B, S, w_router, n_tokens, d, top_k, n_experts, dx, stream)
+              : agm::launch_dx<__half, __half>(B, S, w_router, n_tokens, d, top_k, n_experts, dx, stream);
+  }
+  return e == cudaSuccess ? AGM_OK : agm::cuda_fail(e, "dx");
+}
+
+}  // extern "C"

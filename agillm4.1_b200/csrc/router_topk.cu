@@ -25,6 +25,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "route_math.cuh"
 
 namespace agm {
 
@@ -33,39 +34,6 @@ constexpr int kRouterWarps = kDispatchBlock / 32;
 constexpr int kMaxExperts = AGM_MAX_EXPERTS;       // 16
 constexpr int kTokGroup = 4;
 
-// Sum of e[0..W) in the order of a butterfly (xor) reduction over W lanes,
-// which is how torch's warp softmax reduces a row of W <= 32 elements.
-template <int W>
-__device__ __forceinline__ float butterfly_sum(const float* e) {
-  float v[W];
-#pragma unroll
-  for (int i = 0; i < W; ++i) v[i] = e[i];
-#pragma unroll
-  for (int off = W / 2; off > 0; off /= 2) {
-#pragma unroll
-    for (int i = 0; i < off; ++i) v[i] = v[i] + v[i + off];
-  }
-  return v[0];
-}
-
-__device__ __forceinline__ int next_pow2_le32(int n) {
-  int w = 1;
-  while (w < n) w <<= 1;
-  return w;
-}
-
-// Sum with the butterfly order for a runtime width w (power of two, <= 16).
-__device__ __forceinline__ float butterfly_sum_rt(const float* e, int w) {
-  switch (w) {
-    case 1: return e[0];
-    case 2: return butterfly_sum<2>(e);
-    case 4: return butterfly_sum<4>(e);
-    case 8: return butterfly_sum<8>(e);
-    default: return butterfly_sum<16>(e);
-  }
-}
-
-constexpr int pow2_ceil(int n) { return n <= 1 ? 1 : 2 * pow2_ceil((n + 1) / 2); }
 
 // Per-token selection state: top_k = KC in 1..4 is a compile-time constant
 // (arrays of pow2_ceil(KC)); KC = 0 takes top_k at run time (arrays of 16).
@@ -101,14 +69,8 @@ __device__ __forceinline__ void select_route(const float (&lg)[kMaxExperts], int
     gate[r] = 0.f;
   }
   if (k == 1) {
-    float m = lg[0];
-#pragma unroll
-    for (int e = 1; e < kMaxExperts; ++e)
-      if (e < E) m = fmaxf(m, lg[e]);
     float ex[kMaxExperts];
-#pragma unroll
-    for (int e = 0; e < kMaxExperts; ++e) ex[e] = (e < E) ? expf(lg[e] - m) : 0.f;
-    const float s = butterfly_sum_rt(ex, next_pow2_le32(E));
+    const float s = softmax_terms(lg, E, ex);
     int best = 0;
     float bp = ex[0] / s;
 #pragma unroll
@@ -165,22 +127,7 @@ __device__ __forceinline__ void select_route(const float (&lg)[kMaxExperts], int
     }
   }
   // softmax over the k values (sorted descending, so val[0] is the max).
-  float m = val[0];
-#pragma unroll
-  for (int r = 1; r < S; ++r)
-    if (r < k) m = fmaxf(m, val[r]);
-  float ex[S];
-#pragma unroll
-  for (int r = 0; r < S; ++r) ex[r] = (r < k) ? expf(val[r] - m) : 0.f;
-  float s;
-  if constexpr (KC > 0) {
-    s = butterfly_sum<S>(ex);
-  } else {
-    s = butterfly_sum_rt(ex, next_pow2_le32(k));
-  }
-#pragma unroll
-  for (int r = 0; r < S; ++r)
-    if (r < k) gate[r] = ex[r] / s;
+  topk_gates<KC, S>(val, k, gate);
 }
 
 // One warp's 32 tokens (one per lane; `valid` false past the end): writes the

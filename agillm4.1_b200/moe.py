@@ -17,7 +17,16 @@
 The forward calls the fused C-ABI entry point ``agm_moe_forward`` (router ->
 dispatch plan -> permute -> grouped FC1/FC2 -> combine) on the current CUDA
 stream with no host synchronisation. It refuses CPU tensors (there is no CPU
-fallback) and autograd (training keeps the reference class).
+fallback).
+
+Training: when autograd needs gradients, the forward runs
+``agm_moe_forward_train`` inside an autograd node whose backward is
+``agm_moe_backward`` (router, gates, expert FFNs and combine on the B200
+kernels), in the two precision modes the reference trains in: one dtype
+throughout, or torch.autocast (bf16/fp16) over fp32 master weights with an
+fp32 input, as ``Block`` feeds it from its LayerNorm (agillm41.py:4539-4547)
+under the reference's ``amp()`` (agillm41.py:3054-3066). Shared experts are
+inference-only.
 
 ``install(agillm41)`` rebinds the reference module's ``MoEFFN`` to a subclass
 of the reference class that uses this forward, so ``Block`` (4533-4537), the
@@ -35,6 +44,63 @@ from . import ops
 from ._lib import MoEKernelError
 
 
+def _autocast_dtype(device: torch.device) -> Optional[torch.dtype]:
+    """The 16-bit dtype torch.autocast runs CUDA ops in here, or None."""
+    if device.type != "cuda" or not torch.is_autocast_enabled(device.type):
+        return None
+    dt = torch.get_autocast_dtype(device.type)
+    return dt if dt in (torch.bfloat16, torch.float16) else None
+
+
+class _MoETrainNode(torch.autograd.Function):
+    """Autograd node of the MoE block: ``agm_moe_forward_train`` forward,
+    ``agm_moe_backward`` backward. Replaces the graph autograd records through
+    agillm41.py:4398-4428 (router Linear, top-k/softmax or top-1
+    straight-through gates, index_select, expert Linear/ReLU/Linear, the gate
+    product and index_add_).
+
+    Inputs: x [N, d], the router weight, a state dict (compute-dtype weights,
+    top_k, error checking) and the expert parameters in the order
+    experts.{e}.0.weight, .0.bias, .2.weight, .2.bias for e = 0..E-1; their
+    gradients come back as views of the packed [E, ...] gradient tensors.
+    Everything the backward reads is saved with save_for_backward, so
+    activation checkpointing (agillm41.py:1202, 4662) can drop and recompute it.
+
+    An expert that received no row is never called by the reference, so its
+    parameters get no gradient at all (None), which optimisers treat
+    differently from a zero gradient (no weight decay, no moment update). With
+    state["empty_grad"] == "none" (the default) the backward reads the
+    per-expert row counts (one small device-to-host copy) and returns None for
+    such experts; "zero" skips the copy and returns zero gradients.
+    """
+
+    @staticmethod
+    def forward(ctx, x, w_router, state, *params):
+        wr_c, w1, b1, w2, b2 = state["weights"]
+        out, saved, counts = ops.moe_forward_train(x, wr_c, w1, b1, w2, b2, state["top_k"],
+                                                   check_errors=state["check"], want_counts=True)
+        ctx.save_for_backward(saved, wr_c, w1, w2, counts)
+        ctx.top_k = state["top_k"]
+        ctx.check = state["check"]
+        ctx.none_for_empty = state.get("empty_grad", "none") == "none"
+        ctx.n_params = len(params)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        saved, wr_c, w1, w2, counts = ctx.saved_tensors
+        dx, dwr, dw1, db1, dw2, db2 = ops.moe_backward(dout.contiguous(), saved, wr_c, w1, w2, ctx.top_k,
+                                                       check_errors=ctx.check)
+        used = counts.cpu().tolist() if ctx.none_for_empty else None
+        grads = []
+        for e in range(ctx.n_params // 4):
+            if used is not None and used[e] == 0:
+                grads += [None, None, None, None]
+            else:
+                grads += [dw1[e], db1[e], dw2[e], db2[e]]
+        return (dx if ctx.needs_input_grad[0] else None, dwr if ctx.needs_input_grad[1] else None, None, *grads)
+
+
 class _B200Forward:
     """Forward of the MoE block on the B200 kernels (mixed into the module classes)."""
 
@@ -50,6 +116,11 @@ class _B200Forward:
     #                      routing bit-identical to the reference, whose
     #                      library GEMM may round its split-K partial sums.
     router_logits = "kernel"
+    # Gradient of an expert that received no row in a training forward:
+    #   "none" - None, as in the reference, which never calls such an expert
+    #            (costs one small device-to-host copy per backward);
+    #   "zero" - zero tensors, without that copy.
+    empty_expert_grad = "none"
 
     def _packed_weights(self, device: torch.device, dtype: torch.dtype):
         """Expert weights as contiguous [E, ...] device tensors, with the
@@ -93,6 +164,28 @@ class _B200Forward:
         self._b200_pack = (key, packed)
         return packed
 
+    def _expert_params(self):
+        return [p for ex in self.experts for p in (ex[0].weight, ex[0].bias, ex[2].weight, ex[2].bias)]
+
+    def _compute_weights(self, device: torch.device, master_dtype: torch.dtype, compute_dtype: torch.dtype):
+        """(router, w1, b1, w2, b2) in the compute dtype. Same dtype: the
+        packed parameters themselves. Autocast: their 16-bit casts, made once
+        per change of the parameters (the version counters of the parameters
+        key the cache, so an optimiser step or load_state_dict recasts)."""
+        w1, b1, w2, b2, _ = self._packed_weights(device, master_dtype)
+        wr = self.router.weight
+        if compute_dtype == master_dtype:
+            return wr.detach().contiguous(), w1, b1, w2, b2
+        params = [wr] + self._expert_params()
+        key = (device, compute_dtype) + tuple((p.data_ptr(), p._version) for p in params)
+        cache = getattr(self, "_b200_cast", None)
+        if cache is not None and cache[0] == key:
+            return cache[1]
+        with torch.no_grad():
+            cast = tuple(ops.cast_f32(t.detach(), compute_dtype) for t in (wr, w1, b1, w2, b2))
+        self._b200_cast = (key, cast)
+        return cast
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:  # agillm41.py:4389-4431
         orig_shape = x.shape
         flat = x.reshape(-1, orig_shape[-1])
@@ -101,14 +194,33 @@ class _B200Forward:
             self.last_router_input = flat.detach()
         if not flat.is_cuda:
             raise MoEKernelError("MoEFFN (B200) runs on CUDA tensors only; there is no CPU path")
-        if torch.is_grad_enabled() and (flat.requires_grad or any(p.requires_grad for p in self.parameters())):
-            raise MoEKernelError("MoEFFN (B200) implements the inference forward only; run it under "
-                                 "torch.no_grad()/inference_mode or keep the reference module for training")
         if self.expert_stream:
             raise MoEKernelError("expert_stream (CPU-resident experts) is not supported by the B200 forward")
         wr = self.router.weight
-        if flat.dtype != wr.dtype:
+        amp = _autocast_dtype(flat.device)
+        amp_mode = amp is not None and wr.dtype == torch.float32
+        if amp_mode and flat.dtype != torch.float32:
+            raise MoEKernelError(f"under autocast the MoE input must be fp32 (the LayerNorm output), not {flat.dtype}")
+        if not amp_mode and flat.dtype != wr.dtype:
             raise MoEKernelError(f"input dtype {flat.dtype} differs from the weight dtype {wr.dtype}")
+        params = self._expert_params()
+        grad = torch.is_grad_enabled() and (flat.requires_grad or wr.requires_grad
+                                            or any(p.requires_grad for p in params))
+        if grad or amp_mode:
+            if getattr(self, "shared", None) is not None:
+                raise MoEKernelError("shared experts are supported in the inference forward only (no autograd, "
+                                     "no autocast over fp32 weights)")
+            if self.router_logits != "kernel":
+                raise MoEKernelError("training and autocast route with the router kernel's logits only")
+            weights = self._compute_weights(flat.device, wr.dtype, amp if amp_mode else wr.dtype)
+            flat = flat.contiguous()
+            if grad:
+                state = {"weights": weights, "top_k": self.top_k, "check": self.check_device_errors,
+                         "empty_grad": self.empty_expert_grad}
+                out = _MoETrainNode.apply(flat, wr, state, *params)
+            else:
+                out, _ = ops.moe_forward_train(flat, *weights, self.top_k, check_errors=self.check_device_errors)
+            return out.reshape(orig_shape)
         w1, b1, w2, b2, sh = self._packed_weights(flat.device, flat.dtype)
         flat = flat.contiguous()
         logits_in = None

@@ -296,3 +296,88 @@ def moe_forward_host(x_host: torch.Tensor, w_router: torch.Tensor, w1: torch.Ten
         if code:
             raise _lib.MoEKernelError(f"device error word 0x{code:x} after agm_moe_forward_host")
     return out_host
+
+
+# ---------------------------------------------------------------------------
+# Training: forward that keeps its intermediates, and the backward
+# ---------------------------------------------------------------------------
+def cast_f32(x: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """fp32 CUDA tensor -> contiguous copy in bf16/fp16 (round to nearest even)."""
+    if x.dtype != torch.float32:
+        raise _lib.MoEKernelError(f"cast_f32 takes an fp32 tensor, not {x.dtype}")
+    x = x.contiguous()
+    out = torch.empty(x.shape, dtype=dtype, device=x.device)
+    rc = load().agm_cast_f32(ptr(x), ptr(out), dtype_code(dtype), x.numel(), stream_handle(x.device))
+    check(rc, "agm_cast_f32")
+    return out
+
+
+def train_saved_bytes(n_tokens: int, d: int, n_experts: int, top_k: int, hidden: int, x_dtype: torch.dtype,
+                      dtype: torch.dtype) -> int:
+    return int(load().agm_moe_train_saved_bytes(n_tokens, d, n_experts, top_k, hidden, dtype_code(x_dtype),
+                                                dtype_code(dtype)))
+
+
+def moe_forward_train(x: torch.Tensor, w_router: torch.Tensor, w1: torch.Tensor, b1: torch.Tensor,
+                      w2: torch.Tensor, b2: torch.Tensor, top_k: int, *, tie_low_first: bool = False,
+                      pair: bool = True, pdl: bool = True, check_errors: bool = False, want_counts: bool = False):
+    """Training forward: x [N, d] -> (out [N, d] in x's dtype, saved uint8 buffer).
+
+    The weights are in the compute dtype: x's dtype, or bf16/fp16 with x fp32
+    (autocast: the weights are the 16-bit casts of fp32 master weights).
+    ``saved`` holds what :func:`moe_backward` needs; its first int is the
+    device error word. With ``want_counts`` the result also carries the rows
+    routed to each expert (int32 [E]): (out, saved, counts)."""
+    lib = load()
+    n, d = x.shape
+    E = w_router.shape[0]
+    H = w1.shape[1]
+    dev = x.device
+    dtype = w1.dtype
+    nbytes = train_saved_bytes(n, d, E, top_k, H, x.dtype, dtype)
+    saved = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
+    out = torch.empty(n, d, dtype=x.dtype, device=dev)
+    counts = torch.empty(E, dtype=torch.int32, device=dev) if want_counts else None
+    flags = _flags(tie_low_first) | (0 if pair else _lib.AGM_FLAG_NO_PAIR) | (0 if pdl else _lib.AGM_FLAG_NO_PDL)
+    rc = lib.agm_moe_forward_train(ptr(x), dtype_code(x.dtype), dtype_code(dtype), n, d, E, top_k, H, ptr(w_router),
+                                   ptr(w1), ptr(b1), ptr(w2), ptr(b2), ptr(out), ptr(saved), saved.numel(),
+                                   ptr(counts), flags, stream_handle(dev))
+    check(rc, "agm_moe_forward_train")
+    if check_errors:
+        code = _lib.read_device_error(saved[:4].view(torch.int32))
+        if code:
+            raise _lib.MoEKernelError(f"device error word 0x{code:x} after agm_moe_forward_train")
+    return (out, saved, counts) if want_counts else (out, saved)
+
+
+def moe_backward(dout: torch.Tensor, saved: torch.Tensor, w_router: torch.Tensor, w1: torch.Tensor,
+                 w2: torch.Tensor, top_k: int, *, pdl: bool = True, check_errors: bool = False):
+    """Backward of :func:`moe_forward_train`: dout [N, d] (x's dtype) ->
+    (dx, dw_router [E, d], dw1 [E, H, d], db1 [E, H], dw2 [E, d, H], db2 [E, d]),
+    all in x's dtype (fp32 under autocast)."""
+    lib = load()
+    n, d = dout.shape
+    E = w_router.shape[0]
+    H = w1.shape[1]
+    dev = dout.device
+    dtype = w1.dtype
+    gdt = dout.dtype
+    dout = dout.contiguous()
+    dx = torch.empty(n, d, dtype=gdt, device=dev)
+    dwr = torch.empty(E, d, dtype=gdt, device=dev)
+    dw1 = torch.empty(E, H, d, dtype=gdt, device=dev)
+    db1 = torch.empty(E, H, dtype=gdt, device=dev)
+    dw2 = torch.empty(E, d, H, dtype=gdt, device=dev)
+    db2 = torch.empty(E, d, dtype=gdt, device=dev)
+    nbytes = int(lib.agm_moe_backward_workspace_bytes(n, d, E, top_k, H, dtype_code(dtype)))
+    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
+    rc = lib.agm_moe_backward(ptr(dout), dtype_code(gdt), dtype_code(dtype), n, d, E, top_k, H, ptr(w_router),
+                              ptr(w1), ptr(w2), ptr(saved), saved.numel(), ptr(dx), ptr(dwr), ptr(dw1), ptr(db1),
+                              ptr(dw2), ptr(db2), ptr(ws), ws.numel(), 0 if pdl else _lib.AGM_FLAG_NO_PDL,
+                              stream_handle(dev))
+    check(rc, "agm_moe_backward")
+    if check_errors:
+        code = _lib.read_device_error(ws[:4].view(torch.int32))
+        if code:
+            raise _lib.MoEKernelError(f"device error word 0x{code:x} after agm_moe_backward")
+    return dx, dwr, dw1, db1, dw2, db2

@@ -40,6 +40,25 @@ CASES = [
 ]
 
 
+# Gradient golden cases (training backward through the reference MoEFFN):
+# the same tuple layout as CASES (no shared experts, no stored weights).
+GRAD_CASES = [
+    ("grad_top2_fp32_n24", 64, 64, 4, 2, 24, 41, torch.float32, 0, 0, 0.1, None, False),
+    ("grad_top2_bf16_n24", 64, 64, 4, 2, 24, 42, torch.bfloat16, 0, 0, 0.1, None, False),
+    ("grad_top1_fp32_n20", 64, 64, 4, 1, 20, 43, torch.float32, 0, 0, 0.1, None, False),
+    ("grad_top1_bf16_n20", 64, 64, 4, 1, 20, 44, torch.bfloat16, 0, 0, 0.1, None, False),
+    ("grad_top3_fp32_n16", 64, 96, 5, 3, 16, 45, torch.float32, 0, 0, 0.1, None, False),
+    ("grad_empty_fp32_n16", 64, 64, 6, 2, 16, 46, torch.float32, 0, 0, 0.1, "empty", False),
+]
+
+
+def grad_output(case):
+    """Seeded upstream gradient dL/dout [N, d] (fp32) of a gradient case."""
+    (name, d, H, E, k, N, seed, dtype, shared, shared_H, bias_std, special, store_w) = case
+    g = torch.Generator().manual_seed(seed + 1000)
+    return torch.randn(N, d, generator=g, dtype=torch.float32)
+
+
 def special_state(sd, special, experts):
     """Apply a case's special construction to an fp32 state dict in place."""
     if special == "ties":
@@ -53,16 +72,17 @@ def special_state(sd, special, experts):
     elif special == "empty":
         # With an all-positive input, all-negative router rows never win.
         w = sd["router.weight"]
-        w[5] = -w[5].abs() - 0.05
-        w[9] = -w[9].abs() - 0.05
+        empty = (5, 9) if experts == 14 else (1, experts - 2)
+        for e in empty:
+            w[e] = -w[e].abs() - 0.05
         for e in range(experts):
-            if e not in (5, 9):
+            if e not in empty:
                 w[e] = w[e].abs() + 0.01
     return sd
 
 
 def case_by_name(name: str):
-    for c in CASES:
+    for c in CASES + GRAD_CASES:
         if c[0] == name:
             return c
     raise KeyError(name)

@@ -51,9 +51,33 @@ def num_shared_in(sd: Mapping[str, torch.Tensor]) -> int:
     return n
 
 
+class _ValueOf(torch.autograd.Function):
+    """Forward: `value` (a constant); backward: the gradient goes to `t`
+    unchanged. Used by ``logits_override`` so that routing follows given
+    logits while autograd still runs through the reference's router Linear."""
+
+    @staticmethod
+    def forward(ctx, t, value):
+        return value.to(device=t.device, dtype=t.dtype).clone()
+
+    @staticmethod
+    def backward(ctx, g):
+        return g, None
+
+
 def moe_forward(x: torch.Tensor, sd: Mapping[str, torch.Tensor], top_k: int,
-                aux: Optional[Dict[str, torch.Tensor]] = None) -> torch.Tensor:
-    """Reference MoE forward (agillm41.py:4389-4431), eval mode.
+                aux: Optional[Dict[str, torch.Tensor]] = None,
+                logits_override: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Reference MoE forward (agillm41.py:4389-4431).
+
+    Autograd runs through it as through the reference (the same torch ops),
+    so with ``requires_grad`` inputs or weights ``.backward()`` gives the
+    reference's gradients, under torch.autocast too.
+
+    ``logits_override`` (optional fp32 [N, E], test plumbing): route with these
+    logit values instead of the router GEMM's; gradients still flow through the
+    router Linear. Kernels whose router logits differ from the library GEMM's
+    by a rounding step can so be compared on identical routing.
 
     ``aux`` (optional dict) receives ``logits`` (fp32 [N,E]), ``idx`` (int64
     [N,k]), ``gates`` ([N,k], activation dtype), ``counts`` (int64 [E]) and
@@ -69,6 +93,8 @@ def moe_forward(x: torch.Tensor, sd: Mapping[str, torch.Tensor], top_k: int,
     wr = sd["router.weight"]
     router_in = flat.to(wr.dtype) if flat.dtype != wr.dtype else flat  # 4398
     scores = F.linear(router_in, wr).float()                         # 4399
+    if logits_override is not None:
+        scores = _ValueOf.apply(scores, logits_override)
     n_shared = num_shared_in(sd)
 
     scale = torch.zeros(flat.shape, dtype=torch.float32, device=flat.device) if aux is not None else None

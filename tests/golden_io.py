@@ -67,3 +67,39 @@ class Golden:
 
     def inputs_match(self):
         return sha(self.x) == str(self.z["x_sha256"]) and state_sha(self.sd) == str(self.z["state_sha256"])
+
+
+def grad_names():
+    return sorted(n for n in names() if n.startswith("grad_"))
+
+
+class GoldenGrad(Golden):
+    """A gradient case: the reference's backward (tests/golden/make_golden_grads.py)."""
+
+    def __init__(self, name):
+        super().__init__(name)
+        from oracle.golden_cases import grad_output
+
+        z = self.z
+        self.dout = grad_output(self.case).to(self.dtype)
+        self.dx = from_np(z["dx"], self.dtype)
+        self.d_router = from_np(z["d_router"], self.dtype)
+        self.d_w1 = from_np(z["d_w1"], self.dtype)
+        self.d_b1 = from_np(z["d_b1"], self.dtype)
+        self.d_w2 = from_np(z["d_w2"], self.dtype)
+        self.d_b2 = from_np(z["d_b2"], self.dtype)
+        self.expert_has_grad = [bool(v) for v in z["expert_has_grad"]]
+
+    def inputs_match(self):
+        return super().inputs_match() and sha(self.dout) == str(self.z["dout_sha256"])
+
+    def grads(self):
+        """Reference gradients keyed like the state dict (zeros for experts
+        without a gradient)."""
+        g = {"router.weight": self.d_router}
+        for e in range(self.E):
+            g[f"experts.{e}.0.weight"] = self.d_w1[e]
+            g[f"experts.{e}.0.bias"] = self.d_b1[e]
+            g[f"experts.{e}.2.weight"] = self.d_w2[e]
+            g[f"experts.{e}.2.bias"] = self.d_b2[e]
+        return g

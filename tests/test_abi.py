@@ -95,3 +95,36 @@ def test_forward_rejects_small_workspace():
 def test_package_exports():
     assert agillm41_b200.MoEFFN is not None
     assert os.path.exists(agillm41_b200.LIB_PATH)
+
+
+def test_training_entry_points_validate_without_a_device():
+    lib = _lib.load()
+    fake = ctypes.c_void_p(4096)
+    n, d, E, k, H = 1024, 64, 14, 2, 128
+    need = lib.agm_moe_train_saved_bytes(n, d, E, k, H, _lib.AGM_BF16, _lib.AGM_BF16)
+    rows = lib.agm_max_rows(n, k, E)
+    assert need >= rows * (2 * d + H) * 2            # x_perm, y and h are kept
+    amp = lib.agm_moe_train_saved_bytes(n, d, E, k, H, _lib.AGM_F32, _lib.AGM_BF16)
+    assert amp >= need + n * d * 2                   # plus the 16-bit cast of x
+    assert lib.agm_moe_backward_workspace_bytes(n, d, E, k, H, _lib.AGM_BF16) >= rows * (d + H) * 2
+    # saved buffer too small
+    rc = lib.agm_moe_forward_train(fake, _lib.AGM_BF16, _lib.AGM_BF16, n, d, E, k, H, fake, fake, fake, fake, fake,
+                                   fake, fake, 1024, None, 0, None)
+    assert rc == -5 and "saved" in lib.agm_last_error().decode()
+    # fp16 input with bf16 weights is neither mode
+    rc = lib.agm_moe_forward_train(fake, _lib.AGM_F16, _lib.AGM_BF16, n, d, E, k, H, fake, fake, fake, fake, fake,
+                                   fake, fake, need, None, 0, None)
+    assert rc == -1 and "x_dtype" in lib.agm_last_error().decode()
+    # backward: workspace too small
+    rc = lib.agm_moe_backward(fake, _lib.AGM_BF16, _lib.AGM_BF16, n, d, E, k, H, fake, fake, fake, fake, need, fake,
+                              fake, fake, fake, fake, fake, fake, 1024, 0, None)
+    assert rc == -5 and "workspace" in lib.agm_last_error().decode()
+    assert lib.agm_cast_f32(fake, fake, _lib.AGM_F32, 16, None) == -1
+
+
+def test_training_forward_refuses_cpu_tensors():
+    import torch
+
+    m = agillm41_b200.MoEFFN(64, mlp_mult=2, experts=4, top_k=2).train()
+    with pytest.raises(agillm41_b200.MoEKernelError):
+        m(torch.randn(8, 64, requires_grad=True)).sum().backward()
