@@ -298,7 +298,65 @@ def run_ours(args, world, rank, local):
     else:
         e2e_value = run_e2e(args, world, dev, sd, x, out, N, stream)
     decode = None if args.skip_decode else run_decode(args, dev, stream)
-    report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e_value, x, decode)
+    train = None if args.skip_train else run_train(args, dev, stream)
+    report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e_value, x, decode, train)
+
+
+def run_train(args, dev, stream):
+    """Training step of the MoE block as the reference trains it with --amp
+    (torch.autocast bf16 over fp32 master weights, agillm41.py:3054-3066 and
+    6793): the 16-bit casts of the fp32 weights (an optimiser step changes
+    them every step), the forward that keeps its intermediates and the
+    backward to dx, the router weight and every expert weight and bias, on
+    the same B x L token workload (fp32 x and upstream gradient, seeded).
+    GEMM work per step: the two forward projections plus four backward ones
+    (dgrad and wgrad of FC1 and FC2), 3 x 32.768 MFLOP per token.
+    """
+    from agillm41_b200 import ops, synthetic
+
+    N = args.tokens
+    sd = synthetic.make_state(D, HIDDEN, EXPERTS, SEED, dtype=torch.float32, device=dev)
+    master = (sd["router.weight"].contiguous(),
+              torch.stack([sd[f"experts.{e}.0.weight"] for e in range(EXPERTS)]).contiguous(),
+              torch.stack([sd[f"experts.{e}.0.bias"] for e in range(EXPERTS)]).contiguous(),
+              torch.stack([sd[f"experts.{e}.2.weight"] for e in range(EXPERTS)]).contiguous(),
+              torch.stack([sd[f"experts.{e}.2.bias"] for e in range(EXPERTS)]).contiguous())
+    del sd
+    x = synthetic.make_input(N, D, SEED, dtype=torch.float32, device=dev)
+    g = torch.Generator(device="cpu").manual_seed(SEED + 7)
+    dout = torch.randn(N, D, generator=g).to(dev)
+
+    def step(check=False):
+        wc = [ops.cast_f32(t, torch.bfloat16) for t in master]
+        out, saved = ops.moe_forward_train(x, *wc, TOP_K, check_errors=check)
+        return ops.moe_backward(dout, saved, wc[0], wc[1], wc[3], TOP_K, check_errors=check)
+
+    for i in range(max(3, args.warmup)):
+        step(check=(i == 0))
+    torch.cuda.synchronize()
+    steps = max(3, min(args.steps, 30))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    peaks = load_peaks()
+    flop = 3 * FLOP_PER_TOKEN * N
+    tf = flop / (ms / 1000.0) / 1e12
+    return {"workload": f"MoE block training step (forward + backward), B{BATCH} L{SEQ} ({N} tokens) d{D} E{EXPERTS} "
+                        f"H{HIDDEN} top{TOP_K}, autocast bf16 over fp32 master weights, seed {SEED}",
+            "ms_per_step": round(ms, 4), "tokens_per_s": N / (ms / 1000.0), "steps": steps,
+            "gemm_flop_per_step": flop,
+            "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peaks["tf_sus"], "unit": "TFLOP/s",
+                         "frac": round(tf / peaks["tf_sus"], 3),
+                         "note": "all six expert GEMMs' FLOPs over the whole step time (casts, router, permute, "
+                                 "combine and their backward included), so a lower bound on the GEMMs' own rate"},
+            # 5 weight casts; forward: x cast, router, plan, permute, FC1, FC2, combine;
+            # backward: combine/routing, FC2 wgrad + dgrad, 2 x (column sums + reduce),
+            # FC1 wgrad + dgrad, router wgrad + reduce, dx
+            "gpu_launches_per_step": 24}
 
 
 def run_ep(args, world, rank, local):
@@ -628,7 +686,7 @@ def gemm_kernel_name(n_tokens):
     return "grouped_gemm_tc_kernel (FC1+FC2, tcgen05, one CTA per tile)"
 
 
-def report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e, x, decode=None):
+def report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e, x, decode=None, train=None):
     if rank != 0:
         return
     peaks = load_peaks()
@@ -673,6 +731,8 @@ def report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e, x, deco
     }
     if decode is not None:
         line["decode"] = decode
+    if train is not None:
+        line["train"] = train
     print(json.dumps(line), flush=True)
 
 
@@ -687,6 +747,7 @@ def main():
     ap.add_argument("--skip-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--skip-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--skip-decode", action="store_true", help="skip the 28-layer decode leg")
+    ap.add_argument("--skip-train", action="store_true", help="skip the training-step (forward + backward) leg")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
