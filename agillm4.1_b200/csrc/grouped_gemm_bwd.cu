@@ -84,6 +84,55 @@ __device__ __forceinline__ void dgrad_coords(int t, int num_m, int num_n, int& m
   n_blk = r / gm;
 }
 
+// Column sums of a warp's 32 x 64 chunk (lane = row): five exchange steps
+// halve the columns each lane holds (62 shuffles); lane L ends with the sums
+// of columns 2L and 2L + 1, added in a fixed tree order.
+__device__ __forceinline__ void warp_colsum64(const float (&v)[64], int lane, float& s0, float& s1) {
+  float a32[32], a16[16], a8[8], a4[4], a2[2];
+  {
+    const bool hi = lane & 16;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float send = hi ? v[i] : v[i + 32];
+      a32[i] = (hi ? v[i + 32] : v[i]) + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+  }
+  {
+    const bool hi = lane & 8;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float send = hi ? a32[i] : a32[i + 16];
+      a16[i] = (hi ? a32[i + 16] : a32[i]) + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+  }
+  {
+    const bool hi = lane & 4;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float send = hi ? a16[i] : a16[i + 8];
+      a8[i] = (hi ? a16[i + 8] : a16[i]) + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+  }
+  {
+    const bool hi = lane & 2;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float send = hi ? a8[i] : a8[i + 4];
+      a4[i] = (hi ? a8[i + 4] : a8[i]) + __shfl_xor_sync(0xffffffffu, send, 2);
+    }
+  }
+  {
+    const bool hi = lane & 1;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float send = hi ? a4[i] : a4[i + 2];
+      a2[i] = (hi ? a4[i + 2] : a4[i]) + __shfl_xor_sync(0xffffffffu, send, 1);
+    }
+  }
+  s0 = a2[0];
+  s1 = a2[1];
+}
+
 // Work of one output tile.
 struct TileJob {
   int g;       // expert
@@ -119,7 +168,9 @@ __device__ __forceinline__ TileJob tile_job(int t, const BwdGemmArgs& a, int num
 
 // MODE 0 (dgrad): A = dC [rows, K] K-major (2-D map), B = W [G, K, N]
 //                 MN-major (3-D map, N innermost), C = [rows, N].
-//                 RELU_MASK: C = round(acc) where aux[r, n] > 0, else 0.
+//                 RELU_MASK: C = round(acc) where the forward's ReLU bit
+//                 (aux_bits) is set, else 0. col_part (nullable): per-quarter
+//                 column sums of C (the next layer's bias gradient).
 // MODE 1 (wgrad): A = dC [rows, M] MN-major, B = act [rows, N] MN-major
 //                 (2-D maps, K = permuted rows), C = [G, M, N] (3-D map).
 template <typename T, typename OutT, int BN, int MODE, bool RELU_MASK>
@@ -300,21 +351,38 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int half = ew >> 2;
     uint8_t* stg = sStg + ew * kStgBytes;
     const uint32_t stg_row = lane * 128;
+    constexpr int kChunks = BN / 128;  // 64-column chunks per warp per tile
     int it = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
       const TileJob j = tile_job<MODE, BN>(t, args, num_m, num_n);
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
+      const int n0 = j.n_blk * BN;
+      const int n_valid = min(BN, args.n - n0);
+      const int row0 = j.m_blk * BM + quarter * 32;
+      // ReLU mask words of this warp's chunks, fetched while the MMAs run.
+      uint32_t mbits[kChunks][2];
+#pragma unroll
+      for (int c = 0; c < kChunks; ++c) {
+        mbits[c][0] = mbits[c][1] = 0u;
+        const int col = (half + 2 * c) * 64;
+        if (RELU_MASK && col < n_valid) {
+          const int64_t w0 = (n0 + col) >> 5;
+          const uint32_t* b = args.aux_bits + row0 + lane;
+          mbits[c][0] = __ldg(b + w0 * args.ld_aux_bits);
+          if (col + 32 < n_valid) mbits[c][1] = __ldg(b + (w0 + 1) * args.ld_aux_bits);
+        }
+      }
       if (!mbar_wait(&acc_full[acc], acc_phase, args.err, kErrTimeoutAcc) || *abort_s) {
         *abort_s = 1;
         break;
       }
       tc_fence_after();
-      const int n0 = j.n_blk * BN;
-      const int n_valid = min(BN, args.n - n0);
-      const int row0 = j.m_blk * BM + quarter * 32;
       const bool zero = (j.num_kb == 0);
-      for (int c64 = half; c64 * 64 < n_valid; c64 += 2) {
+#pragma unroll
+      for (int c = 0; c < kChunks; ++c) {
+        const int c64 = half + 2 * c;
+        if (c64 * 64 >= n_valid) break;
         const int col = c64 * 64;
         uint32_t r[64];
         if (!zero) {
@@ -330,18 +398,21 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 64; ++i) v[i] = round_to<T>(__uint_as_float(r[i]));
         if (RELU_MASK) {
-          // ReLU backward on the saved activation: keep where h > 0.
-          const T* hrow = static_cast<const T*>(args.aux) + static_cast<int64_t>(row0 + lane) * args.ld_aux + n0 + col;
+          // ReLU backward: keep where the forward's activation was > 0.
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            if (col + q * 8 < n_valid) {
-              float hv[8];
-              unpack8<T>(__ldg(reinterpret_cast<const uint4*>(hrow) + q), hv);
-#pragma unroll
-              for (int i = 0; i < 8; ++i)
-                if (!(hv[i] > 0.f)) v[q * 8 + i] = 0.f;
-            }
+          for (int i = 0; i < 32; ++i) {
+            if (!((mbits[c][0] >> i) & 1u)) v[i] = 0.f;
+            if (!((mbits[c][1] >> i) & 1u)) v[32 + i] = 0.f;
           }
+        }
+        if (MODE == 0 && args.col_part) {
+          // Bias gradient of the layer this gradient feeds: column sums of
+          // the rounded values, one fp32 partial per 32-row quarter.
+          float s0, s1;
+          warp_colsum64(v, lane, s0, s1);
+          if (col + 2 * lane < n_valid)
+            *reinterpret_cast<float2*>(args.col_part + (static_cast<int64_t>(j.m_blk) * 4 + quarter) * args.n + n0 +
+                                       col + 2 * lane) = make_float2(s0, s1);
         }
 #pragma unroll
         for (int sub = 0; sub < 64 / OUT_COLS; ++sub) {

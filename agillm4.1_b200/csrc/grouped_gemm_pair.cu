@@ -263,6 +263,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t stg_row = lane * 128;
     const uint32_t acc_empty0 = cluster_map(smem_u32(acc_empty), 0);
     const T* bias = static_cast<const T*>(args.bias);
+    const bool want_bits = RELU && args.relu_bits != nullptr;  // training: keep the ReLU mask
     int it = 0;
     for (int t = cluster; t < total; t += nclusters, ++it) {
       int p, n_blk;
@@ -293,6 +294,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tmem_ld_wait();
         if (lane == 0) bulk_wait_group_read0();
         __syncwarp();
+        uint64_t bits = 0;
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
           float bv[8];
@@ -308,10 +310,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           for (int j = 0; j < 8; ++j) {
             v[j] = __uint_as_float(r[q * 8 + j]) + bv[j];
             if (RELU) v[j] = fmaxf(v[j], 0.f);
+            if (RELU && want_bits && round_to<T>(v[j]) > 0.f) bits |= 1ull << (q * 8 + j);
           }
           const uint4 o = make_uint4(pack2<T>(v[0], v[1]), pack2<T>(v[2], v[3]), pack2<T>(v[4], v[5]),
                                      pack2<T>(v[6], v[7]));
           *reinterpret_cast<uint4*>(stg + stg_row + ((q ^ (lane & 7)) << 4)) = o;
+        }
+        if (RELU && want_bits) {
+          // lanes are consecutive rows: each word row is one coalesced store
+          const int64_t row = my_m * kBM + quarter * 32 + lane;
+          const int w0 = (n0 + col) >> 5;
+          args.relu_bits[static_cast<int64_t>(w0) * args.ld_bits + row] = static_cast<uint32_t>(bits);
+          if (col + 32 < n_valid)
+            args.relu_bits[static_cast<int64_t>(w0 + 1) * args.ld_bits + row] = static_cast<uint32_t>(bits >> 32);
         }
         fence_proxy_async_smem();
         __syncwarp();

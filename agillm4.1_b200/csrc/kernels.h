@@ -65,6 +65,11 @@ struct GemmArgs {
   // weight tiles before waiting for the previous kernel (programmatic
   // dependent launch). Otherwise it waits before reading anything.
   bool early_weights = false;
+  // ReLU epilogue only, nullable: bit j of relu_bits[w * ld_bits + r] is set
+  // when the stored c[r, 32 w + j] > 0 (training keeps this [ceil(n/32), rows]
+  // mask for the ReLU backward instead of re-reading c).
+  uint32_t* relu_bits = nullptr;
+  int64_t ld_bits = 0;
 };
 
 // Expert-parallel routing of one rank's permuted rows (see ep_p2p.cu): a list
@@ -177,8 +182,13 @@ struct BwdGemmArgs {
   const int32_t* num_tiles = nullptr;   // dgrad
   int max_tiles = 0;                    // dgrad
   const int32_t* seg_start = nullptr;   // wgrad: [groups + 1]
-  const void* aux = nullptr;            // dgrad relu_mask: [rows, ld_aux]
+  const void* aux = nullptr;            // dgrad relu_mask, fp32: the activation [rows, ld_aux]
   int64_t ld_aux = 0;
+  const uint32_t* aux_bits = nullptr;   // dgrad relu_mask, 16-bit: GemmArgs::relu_bits of the forward
+  int64_t ld_aux_bits = 0;
+  // dgrad, nullable: fp32 column sums of c per 32-row quarter of each row
+  // tile, [max_tiles * 4, n] (the bias gradient of the layer c feeds).
+  float* col_part = nullptr;
   int* err = nullptr;
 };
 cudaError_t grouped_gemm_dgrad(int dtype, const void* dc, int64_t rows, const void* w, const BwdGemmArgs& args,

@@ -47,7 +47,6 @@ namespace {
 constexpr int kMaxE = AGM_MAX_EXPERTS;  // logits gradient rows are 16 wide
 constexpr int kZeroCtas = 8;            // CTAs zero-filling one expert's padding rows of dy
 constexpr int kColsumCols = 256;        // columns per segment-column-sum CTA (8 per lane)
-constexpr int kRouterCols = 1024;       // columns per router-wgrad CTA (4 per thread)
 
 // 8 consecutive values of T (or fp32) at p -> fp32.
 template <typename T>
@@ -349,63 +348,157 @@ __global__ void __launch_bounds__(256) reduce_partials_kernel(const float* __res
 // ---------------------------------------------------------------------------
 // Router weight gradient partials: partial[chunk, e, c] = sum over the
 // chunk's tokens of dl[t, e] * x[t, c], x[t] read from x_perm[row_of[t, 0]]
-// (the permuted copy of token t's router input).
+// (the permuted copy of token t's router input). A thread owns 4 columns for
+// all 16 logit rows (64 fp32 accumulators); the chunk's logit gradients and
+// row indices are staged in shared memory first, and the x values of 4 tokens
+// are loaded together ahead of their multiply-adds.
 // ---------------------------------------------------------------------------
+constexpr int kRwMaxChunk = 256;  // tokens per router-wgrad CTA at most
+
 template <typename T>
-__global__ void __launch_bounds__(256) router_wgrad_kernel(const T* __restrict__ dl, const T* __restrict__ xperm,
-                                                           const int32_t* __restrict__ row_of, int k, int64_t n,
-                                                           int d, int64_t tok_per_chunk,
-                                                           float* __restrict__ partial) {
+__global__ void __launch_bounds__(512) router_wgrad_kernel(const T* __restrict__ dl, const T* __restrict__ xperm,
+                                                            const int32_t* __restrict__ row_of, int k, int64_t n,
+                                                            int d, int tok_per_chunk, float* __restrict__ partial) {
+  __shared__ float4 dl_s[kRwMaxChunk][kMaxE / 4];
+  __shared__ int64_t row_s[kRwMaxChunk];
   pdl_wait();
   pdl_trigger();
   const int chunk = blockIdx.x;
-  const int c0 = blockIdx.y * kRouterCols + threadIdx.x * 4;
-  const int64_t t0 = chunk * tok_per_chunk, t1 = min(n, t0 + tok_per_chunk);
+  const int64_t t0 = static_cast<int64_t>(chunk) * tok_per_chunk;
+  const int cnt = static_cast<int>(min(static_cast<int64_t>(tok_per_chunk), n - t0));
+  float* dl_f = reinterpret_cast<float*>(&dl_s[0][0]);
+  for (int i = threadIdx.x; i < cnt * kMaxE; i += blockDim.x) dl_f[i] = Traits<T>::to_f(dl[t0 * kMaxE + i]);
+  for (int i = threadIdx.x; i < cnt; i += blockDim.x) row_s[i] = static_cast<int64_t>(row_of[(t0 + i) * k]) * d;
+  __syncthreads();
+  const int c0 = (blockIdx.y * blockDim.x + threadIdx.x) * 4;
+  if (c0 >= d) return;
   float acc[kMaxE][4];
 #pragma unroll
   for (int e = 0; e < kMaxE; ++e)
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[e][i] = 0.f;
-  if (c0 < d) {
-    for (int64_t t = t0; t < t1; ++t) {
-      float g[kMaxE];
-      load8f<T>(dl + t * kMaxE, *reinterpret_cast<float(*)[8]>(&g[0]));
-      load8f<T>(dl + t * kMaxE + 8, *reinterpret_cast<float(*)[8]>(&g[8]));
-      const T* xr = xperm + static_cast<int64_t>(row_of[t * k]) * d + c0;
-      float x[4];
-      if constexpr (sizeof(T) == 4) {
-        const float4 v = __ldg(reinterpret_cast<const float4*>(xr));
-        x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+  for (int j0 = 0; j0 < cnt; j0 += 4) {
+    float x[4][4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (j0 + u < cnt) {
+        const T* xr = xperm + row_s[j0 + u] + c0;
+        if constexpr (sizeof(T) == 4) {
+          const float4 v = __ldg(reinterpret_cast<const float4*>(xr));
+          x[u][0] = v.x; x[u][1] = v.y; x[u][2] = v.z; x[u][3] = v.w;
+        } else {
+          const uint2 w = __ldg(reinterpret_cast<const uint2*>(xr));
+          float f[8];
+          unpack8<T>(make_uint4(w.x, w.y, 0, 0), f);
+          x[u][0] = f[0]; x[u][1] = f[1]; x[u][2] = f[2]; x[u][3] = f[3];
+        }
       } else {
-        const uint2 u = __ldg(reinterpret_cast<const uint2*>(xr));
-        const uint4 u4 = make_uint4(u.x, u.y, 0, 0);
-        float f[8];
-        unpack8<T>(u4, f);
-        x[0] = f[0]; x[1] = f[1]; x[2] = f[2]; x[3] = f[3];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) x[u][i] = 0.f;
       }
-#pragma unroll
-      for (int e = 0; e < kMaxE; ++e)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) acc[e][i] = fmaf(g[e], x[i], acc[e][i]);
     }
 #pragma unroll
-    for (int e = 0; e < kMaxE; ++e)
+    for (int u = 0; u < 4; ++u) {
+      if (j0 + u < cnt) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) partial[(static_cast<int64_t>(chunk) * kMaxE + e) * d + c0 + i] = acc[e][i];
+        for (int e4 = 0; e4 < kMaxE / 4; ++e4) {
+          const float4 g = dl_s[j0 + u][e4];  // one shared-memory read serves four logit rows
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            acc[4 * e4 + 0][i] = fmaf(g.x, x[u][i], acc[4 * e4 + 0][i]);
+            acc[4 * e4 + 1][i] = fmaf(g.y, x[u][i], acc[4 * e4 + 1][i]);
+            acc[4 * e4 + 2][i] = fmaf(g.z, x[u][i], acc[4 * e4 + 2][i]);
+            acc[4 * e4 + 3][i] = fmaf(g.w, x[u][i], acc[4 * e4 + 3][i]);
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < kMaxE; ++e)
+    *reinterpret_cast<float4*>(partial + (static_cast<int64_t>(chunk) * kMaxE + e) * d + c0) =
+        make_float4(acc[e][0], acc[e][1], acc[e][2], acc[e][3]);
+}
+
+// Bias gradient from the dgrad kernel's per-quarter column sums:
+// out[e, c] = r_T(sum over the 128-row tiles of expert e's segment and their
+// four quarters of part[(tile * 4 + q) * n + c]), in tile order.
+// CTA = (expert, 32 columns); its 8 warps each sum every 8th quarter-row of
+// the expert's partials for the 32 columns (coalesced), then warp 0 adds the
+// 8 warp sums in order.
+template <typename T, typename OutT>
+__global__ void __launch_bounds__(256) tile_parts_reduce_kernel(const float* __restrict__ part,
+                                                                const int32_t* __restrict__ seg_start, int E, int n,
+                                                                OutT* __restrict__ out) {
+  __shared__ float red[8][32];
+  pdl_wait();
+  pdl_trigger();
+  const int e = blockIdx.y;
+  const int c = blockIdx.x * 32 + lane_id();
+  const int w = warp_id();
+  const int64_t q0 = static_cast<int64_t>(seg_start[e] / AGM_TILE_M) * 4;
+  const int64_t q1 = static_cast<int64_t>(seg_start[e + 1] / AGM_TILE_M) * 4;
+  float v = 0.f;
+  if (c < n)
+    for (int64_t q = q0 + w; q < q1; q += 8) v += part[q * n + c];
+  red[w][lane_id()] = v;
+  __syncthreads();
+  if (w == 0 && c < n) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += red[i][lane_id()];
+    const float r = round_to<T>(s);
+    if constexpr (sizeof(OutT) == 4)
+      out[static_cast<int64_t>(e) * n + c] = r;
+    else
+      out[static_cast<int64_t>(e) * n + c] = Traits<OutT>::from_f(r);
   }
 }
 
 // ---------------------------------------------------------------------------
 // Input gradient: dx[t] = ((dx_perm[row(t,k-1)] + ... + dx_perm[row(t,0)]) + r_T(dl[t] @ Wr)),
 // each add rounded to G (T in same-dtype mode, fp32 in autocast). Wr [E, d]
-// (compute dtype) is staged in shared memory.
+// (compute dtype) is staged in shared memory. A warp handles two tokens per
+// iteration: their gathered rows are loaded first, and every Wr value read
+// from shared memory serves both tokens' router terms.
 // ---------------------------------------------------------------------------
+// dx chunk of one token: the ranks' rows summed from the last rank down, then
+// the router term, each add rounded to G.
 template <typename T, typename G, int K_MAX>
-__global__ void __launch_bounds__(256) dx_kernel(const T* __restrict__ dxp, const int32_t* __restrict__ row_of,
+__device__ __forceinline__ void dx_finish(const float (&a)[K_MAX][8], const float (&rt)[8], int k, G* dst) {
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  bool first = true;
+#pragma unroll
+  for (int r = K_MAX - 1; r >= 0; --r) {
+    if (r < k) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (first)
+          acc[i] = a[r][i];
+        else
+          acc[i] = (sizeof(G) == 4) ? __fadd_rn(acc[i], a[r][i]) : round_to<T>(__fadd_rn(acc[i], a[r][i]));
+      }
+      first = false;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float rv = round_to<T>(rt[i]);
+    acc[i] = (sizeof(G) == 4) ? __fadd_rn(acc[i], rv) : round_to<T>(__fadd_rn(acc[i], rv));
+  }
+  store8f<G>(dst, acc);
+}
+
+template <typename T, typename G, int K_MAX>
+__global__ void __launch_bounds__(256, 3) dx_kernel(const T* __restrict__ dxp, const int32_t* __restrict__ row_of,
                                                  const T* __restrict__ dl, const T* __restrict__ wr, int64_t n,
                                                  int d, int k, int E, G* __restrict__ dx) {
   extern __shared__ uint8_t smem_raw[];
-  T* w_s = reinterpret_cast<T*>(smem_raw);
+  // [8 warps][2 tokens][16] logit gradients, then Wr [E, d]
+  float* g_s = reinterpret_cast<float*>(smem_raw) + warp_id() * 2 * kMaxE;
+  T* w_s = reinterpret_cast<T*>(smem_raw + 8 * 2 * kMaxE * sizeof(float));
   pdl_wait();
   pdl_trigger();
   {
@@ -418,44 +511,49 @@ __global__ void __launch_bounds__(256) dx_kernel(const T* __restrict__ dxp, cons
   const int lane = lane_id();
   const int nc8 = d / 8;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
-  for (int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + warp_id(); t < n; t += warps) {
-    float g[kMaxE];
-    load8f<T>(dl + t * kMaxE, *reinterpret_cast<float(*)[8]>(&g[0]));
-    load8f<T>(dl + t * kMaxE + 8, *reinterpret_cast<float(*)[8]>(&g[8]));
-    int64_t row[K_MAX];
+  for (int64_t t = 2 * (static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + warp_id()); t < n; t += 2 * warps) {
+    const bool two = t + 1 < n;
+    // lane j holds the logit gradient (t + j / 16, e = j % 16)
+    __syncwarp();
+    g_s[lane] = (lane < kMaxE || two) ? Traits<T>::to_f(dl[t * kMaxE + lane]) : 0.f;
+    __syncwarp();
+    int64_t row0[K_MAX], row1[K_MAX];
 #pragma unroll
-    for (int r = 0; r < K_MAX; ++r) row[r] = (r < k) ? row_of[t * k + r] : 0;
+    for (int r = 0; r < K_MAX; ++r) {
+      row0[r] = (r < k) ? row_of[t * k + r] : 0;
+      row1[r] = (r < k && two) ? row_of[(t + 1) * k + r] : row0[r];
+    }
     for (int c = lane; c < nc8; c += 32) {
-      float rt[8];
+      // gathered expert-path rows first (their loads overlap the router term)
+      float a0[K_MAX][8], a1[K_MAX][8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) rt[i] = 0.f;
+      for (int r = 0; r < K_MAX; ++r) {
+        if (r < k) {
+          load8f<T>(dxp + row0[r] * d + c * 8, a0[r]);
+          load8f<T>(dxp + row1[r] * d + c * 8, a1[r]);
+        }
+      }
+      float rt0[8], rt1[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) rt0[i] = rt1[i] = 0.f;
       for (int e = 0; e < E; ++e) {
         float w[8];
         if constexpr (sizeof(T) == 4) {
           const float4* p = reinterpret_cast<const float4*>(w_s + static_cast<int64_t>(e) * d + c * 8);
-          const float4 a = p[0], b = p[1];
-          w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w; w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+          const float4 u = p[0], v = p[1];
+          w[0] = u.x; w[1] = u.y; w[2] = u.z; w[3] = u.w; w[4] = v.x; w[5] = v.y; w[6] = v.z; w[7] = v.w;
         } else {
           unpack8<T>(*reinterpret_cast<const uint4*>(w_s + static_cast<int64_t>(e) * d + c * 8), w);
         }
+        const float ge0 = g_s[e], ge1 = g_s[kMaxE + e];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) rt[i] = fmaf(g[e], w[i], rt[i]);
+        for (int i = 0; i < 8; ++i) {
+          rt0[i] = fmaf(ge0, w[i], rt0[i]);
+          rt1[i] = fmaf(ge1, w[i], rt1[i]);
+        }
       }
-      float acc[8];
-      load8f<T>(dxp + row[k - 1] * d + c * 8, acc);
-      for (int r = k - 2; r >= 0; --r) {
-        float v[8];
-        load8f<T>(dxp + row[r] * d + c * 8, v);
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          acc[i] = (sizeof(G) == 4) ? __fadd_rn(acc[i], v[i]) : round_to<T>(__fadd_rn(acc[i], v[i]));
-      }
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float rv = round_to<T>(rt[i]);
-        acc[i] = (sizeof(G) == 4) ? __fadd_rn(acc[i], rv) : round_to<T>(__fadd_rn(acc[i], rv));
-      }
-      store8f<G>(dx + t * d + c * 8, acc);
+      dx_finish<T, G, K_MAX>(a0, rt0, k, dx + t * d + c * 8);
+      if (two) dx_finish<T, G, K_MAX>(a1, rt1, k, dx + (t + 1) * d + c * 8);
     }
   }
 }
@@ -513,6 +611,7 @@ struct Saved {
   void* x_perm;      // [rows, d]
   void* h;           // [rows, H]
   void* y;           // [rows, d]
+  uint32_t* relu_bits;  // [ceil(H / 32), rows]: h > 0 (16-bit compute dtypes)
   size_t bytes;
 };
 
@@ -537,6 +636,7 @@ Saved carve_saved(void* ws, int64_t n, int d, int E, int k, int H, int eb, bool 
   S.x_perm = c.take<void>(static_cast<size_t>(eb) * rows * d);
   S.h = c.take<void>(static_cast<size_t>(eb) * rows * H);
   S.y = c.take<void>(static_cast<size_t>(eb) * rows * d);
+  S.relu_bits = eb == 2 ? c.take<uint32_t>(sizeof(uint32_t) * ((H + 31) / 32) * std::max<int64_t>(rows, 1)) : nullptr;
   S.bytes = (c.off + 255) & ~size_t(255);
   return S;
 }
@@ -545,9 +645,14 @@ int colsum_splits(int ncols, int E) {
   const int cb = (ncols + kColsumCols - 1) / kColsumCols;
   return std::max(1, std::min(64, (4 * 148 + cb * E - 1) / (cb * E)));
 }
+// Tokens per router-wgrad CTA: about three CTAs per SM, at most kRwMaxChunk.
+int router_tok_per_chunk(int64_t n) {
+  return static_cast<int>(std::max<int64_t>(16, std::min<int64_t>(kRwMaxChunk, (n + 3 * 148 - 1) / (3 * 148))));
+}
 int router_chunks(int64_t n, int d) {
-  const int cb = (d + kRouterCols - 1) / kRouterCols;
-  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(n, 2 * 148 / cb)));
+  (void)d;
+  const int tpc = router_tok_per_chunk(n);
+  return static_cast<int>(std::max<int64_t>(1, (n + tpc - 1) / tpc));
 }
 
 struct BwdWs {
@@ -557,6 +662,7 @@ struct BwdWs {
   void* dl;     // [n, 16]
   float* colsum;  // [splits, E, max(d, H)]
   float* rpart;   // [chunks, 16, d]
+  float* dh_part; // [max_tiles * 4, H]: dgrad FC2's column sums of dh (16-bit dtypes)
   size_t bytes;
 };
 
@@ -572,6 +678,7 @@ BwdWs carve_bwd(void* ws, int64_t n, int d, int E, int k, int H, int eb) {
   B.dl = c.take<void>(static_cast<size_t>(eb) * n * kMaxE);
   B.colsum = c.take<float>(sizeof(float) * cs);
   B.rpart = c.take<float>(sizeof(float) * router_chunks(n, d) * kMaxE * d);
+  B.dh_part = eb == 2 ? c.take<float>(sizeof(float) * (rows / AGM_TILE_M) * 4 * H) : nullptr;
   B.bytes = (c.off + 255) & ~size_t(255);
   return B;
 }
@@ -640,13 +747,22 @@ cudaError_t launch_colsum(const void* m, int ncols, const int32_t* seg_start, in
 }
 
 template <typename T, typename OutT>
+cudaError_t launch_tile_parts(const float* part, const int32_t* seg_start, int E, int ncols, void* out,
+                              cudaStream_t s) {
+  dim3 grid(static_cast<unsigned>((ncols + 31) / 32), static_cast<unsigned>(E));
+  return launch_kernel(tile_parts_reduce_kernel<T, OutT>, grid, dim3(256), 0, s, part, seg_start, E, ncols,
+                       static_cast<OutT*>(out));
+}
+
+template <typename T, typename OutT>
 cudaError_t launch_router_wgrad(const BwdWs& B, const Saved& S, int64_t n, int d, int k, int E, void* dwr,
                                 cudaStream_t s) {
   const int chunks = router_chunks(n, d);
-  const int64_t per = (n + chunks - 1) / chunks;
-  dim3 grid(static_cast<unsigned>(chunks), static_cast<unsigned>((d + kRouterCols - 1) / kRouterCols));
-  cudaError_t e = launch_kernel(router_wgrad_kernel<T>, grid, dim3(256), 0, s, static_cast<const T*>(B.dl),
-                                static_cast<const T*>(S.x_perm), S.row_of, k, n, d, per, B.rpart);
+  const int tpc = router_tok_per_chunk(n);
+  const int threads = std::min(512, (d / 4 + 31) / 32 * 32);
+  dim3 grid(static_cast<unsigned>(chunks), static_cast<unsigned>((d / 4 + threads - 1) / threads));
+  cudaError_t e = launch_kernel(router_wgrad_kernel<T>, grid, dim3(threads), 0, s, static_cast<const T*>(B.dl),
+                                static_cast<const T*>(S.x_perm), S.row_of, k, n, d, tpc, B.rpart);
   if (e != cudaSuccess) return e;
   // Chunk c's partial is [16, d] at c * 16 * d; its first E rows, E * d
   // contiguous values, are the router weight's.
@@ -660,8 +776,10 @@ cudaError_t launch_router_wgrad(const BwdWs& B, const Saved& S, int64_t n, int d
 template <typename T, typename G>
 cudaError_t launch_dx(const BwdWs& B, const Saved& S, const void* wr, int64_t n, int d, int k, int E, void* dx,
                       cudaStream_t s) {
-  const int smem = E * d * static_cast<int>(sizeof(T));
-  const unsigned grid = static_cast<unsigned>(std::min<int64_t>((n + 7) / 8, 148 * 2));
+  const int smem = E * d * static_cast<int>(sizeof(T)) + 8 * 2 * kMaxE * static_cast<int>(sizeof(float));
+  // As many CTAs as fit beside each other (Wr staged in each one's shared memory).
+  const int per_sm = std::max(1, std::min(8, (227 * 1024) / std::max(smem + 1024, 1)));
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>((n + 15) / 16, 148 * per_sm));
   const T* dxp = static_cast<const T*>(B.dy);
   const T* dl = static_cast<const T*>(B.dl);
   const T* w = static_cast<const T*>(wr);
@@ -795,11 +913,14 @@ int agm_moe_forward_train(const void* x, int x_dtype, int dtype, int64_t n_token
   g1.num_tiles = S.num_tiles;
   g1.max_tiles = max_tiles;
   g1.err = S.err;
+  g1.relu_bits = S.relu_bits;  // the ReLU backward reads these bits instead of h
+  g1.ld_bits = rows;
   // Row-tile GEMMs only (no swapped operands): the backward reads whole
   // 128-row tiles of h, so its padding rows must hold finite values.
   e = agm::grouped_gemm(dtype, S.x_perm, rows, w1, g1, true, sms, stream, pair ? AGM_GEMM_PAIR : 0);
   if (e != cudaSuccess) return agm::cuda_fail(e, "grouped_gemm fc1");
   agm::GemmArgs g2 = g1;
+  g2.relu_bits = nullptr;
   g2.c = S.y;
   g2.ldc = d;
   g2.bias = b2;
@@ -890,8 +1011,14 @@ int agm_moe_backward(const void* dout, int x_dtype, int dtype, int64_t n_tokens,
   d2.tile_group = S.tile_expert;
   d2.num_tiles = S.num_tiles;
   d2.max_tiles = max_tiles;
-  d2.aux = S.h;
-  d2.ld_aux = hidden;
+  if (dtype == AGM_F32) {
+    d2.aux = S.h;  // SIMT path: the ReLU mask from h, db1 from a column-sum pass
+    d2.ld_aux = hidden;
+  } else {
+    d2.aux_bits = S.relu_bits;
+    d2.ld_aux_bits = rows;
+    d2.col_part = B.dh_part;  // db1 partials from the epilogue
+  }
   d2.err = B.err;
   e = agm::grouped_gemm_dgrad(dtype, B.dy, rows, w2, d2, true, sms, stream);
   if (e != cudaSuccess) return agm::cuda_fail(e, "dgrad fc2");
@@ -910,7 +1037,17 @@ int agm_moe_backward(const void* dout, int x_dtype, int dtype, int64_t n_tokens,
   };
   e = colsum(B.dy, d, db2);
   if (e != cudaSuccess) return agm::cuda_fail(e, "db2");
-  e = colsum(B.dh, hidden, db1);
+  switch (dtype) {
+    case AGM_F32: e = colsum(B.dh, hidden, db1); break;
+    case AGM_BF16:
+      e = amp ? agm::launch_tile_parts<__nv_bfloat16, float>(B.dh_part, S.seg_start, n_experts, hidden, db1, stream)
+              : agm::launch_tile_parts<__nv_bfloat16, __nv_bfloat16>(B.dh_part, S.seg_start, n_experts, hidden, db1,
+                                                                     stream);
+      break;
+    default:
+      e = amp ? agm::launch_tile_parts<__half, float>(B.dh_part, S.seg_start, n_experts, hidden, db1, stream)
+              : agm::launch_tile_parts<__half, __half>(B.dh_part, S.seg_start, n_experts, hidden, db1, stream);
+  }
   if (e != cudaSuccess) return agm::cuda_fail(e, "db1");
   // 5. FC1 weight gradient: dW1[e] [H, d] = dh_e^T x_perm_e
   agm::BwdGemmArgs w1a = w2a;
@@ -926,6 +1063,8 @@ int agm_moe_backward(const void* dout, int x_dtype, int dtype, int64_t n_tokens,
   d1.n = d;
   d1.k = hidden;
   d1.aux = nullptr;
+  d1.aux_bits = nullptr;
+  d1.col_part = nullptr;
   e = agm::grouped_gemm_dgrad(dtype, B.dh, rows, w1, d1, false, sms, stream);
   if (e != cudaSuccess) return agm::cuda_fail(e, "dgrad fc1");
   // 7. router weight gradient: dWr = dl^T x
