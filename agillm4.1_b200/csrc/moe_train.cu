@@ -123,12 +123,15 @@ __device__ __forceinline__ void token_gates(const float* __restrict__ logits, co
 //   G == T (same dtype): out = ((0 + r(y0*r(g0))) + r(y1*r(g1))) ..., r() = round to T;
 //   G == float (autocast): out = (0 + y0*g0) + y1*g1 in fp32.
 //   k == 1: out = y (the straight-through gate is exactly 1).
+// Shared experts (agillm41.py:4381-4387, 4429-4430): s = s_0 + s_1 + ... in
+// T, then out = out + s (rounded to G).
 // ---------------------------------------------------------------------------
 template <typename T, typename G, int K_MAX>
 __global__ void __launch_bounds__(256) combine_train_kernel(const T* __restrict__ y, const int32_t* __restrict__ row_of,
                                                             const float* __restrict__ logits,
                                                             const int32_t* __restrict__ idx, int64_t n, int d, int k,
-                                                            int E, G* __restrict__ out) {
+                                                            int E, const T* __restrict__ shared_y, int n_shared,
+                                                            int64_t shared_stride, G* __restrict__ out) {
   pdl_wait();
   pdl_trigger();
   const int lane = lane_id();
@@ -165,6 +168,19 @@ __global__ void __launch_bounds__(256) combine_train_kernel(const T* __restrict_
           }
         }
       }
+      if (n_shared > 0) {
+        float sh[8];
+        load8f<T>(shared_y + t * d + c * 8, sh);
+        for (int si = 1; si < n_shared; ++si) {
+          float v[8];
+          load8f<T>(shared_y + si * shared_stride + t * d + c * 8, v);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) sh[i] = round_to<T>(__fadd_rn(sh[i], v[i]));
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          acc[i] = (sizeof(G) == 4) ? __fadd_rn(acc[i], sh[i]) : round_to<T>(__fadd_rn(acc[i], sh[i]));
+      }
       store8f<G>(out + t * d + c * 8, acc);
     }
   }
@@ -189,13 +205,23 @@ __global__ void __launch_bounds__(256) combine_bwd_kernel(
     const G* __restrict__ dout, const T* __restrict__ y, const int32_t* __restrict__ row_of,
     const float* __restrict__ logits, const int32_t* __restrict__ idx, int64_t n, int d, int k, int E,
     int tok_ctas, const int32_t* __restrict__ seg_start, const int32_t* __restrict__ counts, int64_t max_rows,
-    T* __restrict__ dy, T* __restrict__ dl) {
+    T* __restrict__ dy, T* __restrict__ dl, T* __restrict__ ds, int64_t npad, int32_t* __restrict__ dense_seg) {
   pdl_wait();
   pdl_trigger();
   const int lane = lane_id();
   const int nc8 = d / 8;
   if (static_cast<int>(blockIdx.x) >= tok_ctas) {
     const int z = blockIdx.x - tok_ctas;
+    if (z == 0 && ds) {
+      // shared experts: their rows past n are zero, and they form one segment
+      if (threadIdx.x == 0) {
+        dense_seg[0] = 0;
+        dense_seg[1] = static_cast<int32_t>(npad);
+      }
+      const int nchunk = d * static_cast<int>(sizeof(T)) / 16;
+      for (int64_t i = threadIdx.x; i < (npad - n) * nchunk; i += blockDim.x)
+        reinterpret_cast<uint4*>(ds + n * d)[i] = make_uint4(0, 0, 0, 0);
+    }
     const int e = z / kZeroCtas;
     const int64_t r0 = static_cast<int64_t>(seg_start[e]) + counts[e];
     const int64_t r1 = min(static_cast<int64_t>(seg_start[e + 1]), max_rows);
@@ -223,6 +249,7 @@ __global__ void __launch_bounds__(256) combine_bwd_kernel(
     for (int c = lane; c < nc8; c += 32) {
       float go[8];
       load8f<G>(dout + t * d + c * 8, go);
+      if (ds) store8f<T>(ds + t * d + c * 8, go);  // gradient of the shared sum: dout in T
 #pragma unroll
       for (int r = 0; r < K_MAX; ++r) {
         if (r < k) {
@@ -465,11 +492,25 @@ __global__ void __launch_bounds__(256) tile_parts_reduce_kernel(const float* __r
 // dx chunk of one token: the ranks' rows summed from the last rank down, then
 // the router term, each add rounded to G.
 template <typename T, typename G, int K_MAX>
-__device__ __forceinline__ void dx_finish(const float (&a)[K_MAX][8], const float (&rt)[8], int k, G* dst) {
+__device__ __forceinline__ void dx_finish(const float (&a)[K_MAX][8], const float (&rt)[8], int k, G* dst,
+                                          const T* __restrict__ dxs, int n_shared, int64_t shared_stride) {
   float acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.f;
   bool first = true;
+  // shared experts' input gradients arrive first, the last shared expert's first
+  for (int si = n_shared - 1; si >= 0; --si) {
+    float v[8];
+    load8f<T>(dxs + si * shared_stride, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (first)
+        acc[i] = v[i];
+      else
+        acc[i] = (sizeof(G) == 4) ? __fadd_rn(acc[i], v[i]) : round_to<T>(__fadd_rn(acc[i], v[i]));
+    }
+    first = false;
+  }
 #pragma unroll
   for (int r = K_MAX - 1; r >= 0; --r) {
     if (r < k) {
@@ -494,7 +535,8 @@ __device__ __forceinline__ void dx_finish(const float (&a)[K_MAX][8], const floa
 template <typename T, typename G, int K_MAX>
 __global__ void __launch_bounds__(256, 3) dx_kernel(const T* __restrict__ dxp, const int32_t* __restrict__ row_of,
                                                  const T* __restrict__ dl, const T* __restrict__ wr, int64_t n,
-                                                 int d, int k, int E, G* __restrict__ dx) {
+                                                 int d, int k, int E, const T* __restrict__ dxs, int n_shared,
+                                                 int64_t shared_stride, G* __restrict__ dx) {
   extern __shared__ uint8_t smem_raw[];
   // [8 warps][2 tokens][16] logit gradients, then Wr [E, d]
   float* g_s = reinterpret_cast<float*>(smem_raw) + warp_id() * 2 * kMaxE;
@@ -552,8 +594,10 @@ __global__ void __launch_bounds__(256, 3) dx_kernel(const T* __restrict__ dxp, c
           rt1[i] = fmaf(ge1, w[i], rt1[i]);
         }
       }
-      dx_finish<T, G, K_MAX>(a0, rt0, k, dx + t * d + c * 8);
-      if (two) dx_finish<T, G, K_MAX>(a1, rt1, k, dx + (t + 1) * d + c * 8);
+      dx_finish<T, G, K_MAX>(a0, rt0, k, dx + t * d + c * 8, dxs + t * d + c * 8, n_shared, shared_stride);
+      if (two)
+        dx_finish<T, G, K_MAX>(a1, rt1, k, dx + (t + 1) * d + c * 8, dxs + (t + 1) * d + c * 8, n_shared,
+                               shared_stride);
     }
   }
 }
@@ -607,19 +651,26 @@ struct Saved {
   int32_t* tile_expert;
   int32_t* row_of;   // [n, k]
   int32_t* token_of; // [rows]
-  void* xb;          // [n, d] compute dtype (autocast: the cast input)
+  void* xb;          // [npad, d] compute dtype, zero rows past n (autocast: the cast input; with
+                     // shared experts: their FC1 input, kept for their weight gradient)
   void* x_perm;      // [rows, d]
   void* h;           // [rows, H]
   void* y;           // [rows, d]
   uint32_t* relu_bits;  // [ceil(H / 32), rows]: h > 0 (16-bit compute dtypes)
+  void* h_sh;        // [S, npad, Hs] shared experts' FC1 activations
+  void* y_sh;        // [S, npad, d] shared experts' outputs
+  uint32_t* bits_sh; // [S, ceil(Hs / 32), npad] (16-bit compute dtypes)
   size_t bytes;
 };
 
-Saved carve_saved(void* ws, int64_t n, int d, int E, int k, int H, int eb, bool amp) {
+int64_t npad_of(int64_t n) { return rup(std::max<int64_t>(n, 1), AGM_TILE_M); }
+
+Saved carve_saved(void* ws, int64_t n, int d, int E, int k, int H, int eb, bool amp, int S_, int Hs) {
   Carve c(ws);
   Saved S;
   const int64_t nb = agm_dispatch_blocks(n);
   const int64_t rows = agm_max_rows(n, k, E);
+  const int64_t npad = npad_of(n);
   S.err = c.take<int>(sizeof(int));
   S.logits = c.take<float>(sizeof(float) * n * E);
   S.idx = c.take<int32_t>(sizeof(int32_t) * n * k);
@@ -632,11 +683,14 @@ Saved carve_saved(void* ws, int64_t n, int d, int E, int k, int H, int eb, bool 
   S.tile_expert = c.take<int32_t>(sizeof(int32_t) * std::max<int64_t>(rows / AGM_TILE_M, 1));
   S.row_of = c.take<int32_t>(sizeof(int32_t) * n * k);
   S.token_of = c.take<int32_t>(sizeof(int32_t) * std::max<int64_t>(rows, 1));
-  S.xb = amp ? c.take<void>(static_cast<size_t>(eb) * n * d) : nullptr;
+  S.xb = (amp || S_ > 0) ? c.take<void>(static_cast<size_t>(eb) * npad * d) : nullptr;
   S.x_perm = c.take<void>(static_cast<size_t>(eb) * rows * d);
   S.h = c.take<void>(static_cast<size_t>(eb) * rows * H);
   S.y = c.take<void>(static_cast<size_t>(eb) * rows * d);
   S.relu_bits = eb == 2 ? c.take<uint32_t>(sizeof(uint32_t) * ((H + 31) / 32) * std::max<int64_t>(rows, 1)) : nullptr;
+  S.h_sh = S_ > 0 ? c.take<void>(static_cast<size_t>(eb) * S_ * npad * Hs) : nullptr;
+  S.y_sh = S_ > 0 ? c.take<void>(static_cast<size_t>(eb) * S_ * npad * d) : nullptr;
+  S.bits_sh = (S_ > 0 && eb == 2) ? c.take<uint32_t>(sizeof(uint32_t) * S_ * ((Hs + 31) / 32) * npad) : nullptr;
   S.bytes = (c.off + 255) & ~size_t(255);
   return S;
 }
@@ -660,18 +714,27 @@ struct BwdWs {
   void* dy;     // [rows, d]; later dx_perm
   void* dh;     // [rows, H]
   void* dl;     // [n, 16]
-  float* colsum;  // [splits, E, max(d, H)]
+  float* colsum;  // [splits, groups, ncols] for the largest use
   float* rpart;   // [chunks, 16, d]
   float* dh_part; // [max_tiles * 4, H]: dgrad FC2's column sums of dh (16-bit dtypes)
+  void* ds;       // [npad, d] gradient of the shared experts' sum (zero rows past n)
+  void* dh_sh;    // [npad, Hs] one shared expert's dh at a time
+  void* dx_sh;    // [S, npad, d] shared experts' input gradients
+  float* dhs_part;  // [npad / 128 * 4, Hs]
+  int32_t* dense_seg;  // [2] = {0, npad}: the shared experts' one segment
   size_t bytes;
 };
 
-BwdWs carve_bwd(void* ws, int64_t n, int d, int E, int k, int H, int eb) {
+BwdWs carve_bwd(void* ws, int64_t n, int d, int E, int k, int H, int eb, int S_, int Hs) {
   Carve c(ws);
   BwdWs B;
   const int64_t rows = agm_max_rows(n, k, E);
-  const int64_t cs = std::max<int64_t>(static_cast<int64_t>(colsum_splits(d, E)) * d,
-                                       static_cast<int64_t>(colsum_splits(H, E)) * H) * E;
+  const int64_t npad = npad_of(n);
+  int64_t cs = std::max<int64_t>(static_cast<int64_t>(colsum_splits(d, E)) * d * E,
+                                 static_cast<int64_t>(colsum_splits(H, E)) * H * E);
+  if (S_ > 0)
+    cs = std::max<int64_t>(cs, std::max<int64_t>(static_cast<int64_t>(colsum_splits(d, 1)) * d,
+                                                 static_cast<int64_t>(colsum_splits(Hs, 1)) * Hs));
   B.err = c.take<int>(sizeof(int));
   B.dy = c.take<void>(static_cast<size_t>(eb) * rows * d);
   B.dh = c.take<void>(static_cast<size_t>(eb) * rows * H);
@@ -679,6 +742,11 @@ BwdWs carve_bwd(void* ws, int64_t n, int d, int E, int k, int H, int eb) {
   B.colsum = c.take<float>(sizeof(float) * cs);
   B.rpart = c.take<float>(sizeof(float) * router_chunks(n, d) * kMaxE * d);
   B.dh_part = eb == 2 ? c.take<float>(sizeof(float) * (rows / AGM_TILE_M) * 4 * H) : nullptr;
+  B.ds = S_ > 0 ? c.take<void>(static_cast<size_t>(eb) * npad * d) : nullptr;
+  B.dh_sh = S_ > 0 ? c.take<void>(static_cast<size_t>(eb) * npad * Hs) : nullptr;
+  B.dx_sh = S_ > 0 ? c.take<void>(static_cast<size_t>(eb) * S_ * npad * d) : nullptr;
+  B.dhs_part = (S_ > 0 && eb == 2) ? c.take<float>(sizeof(float) * (npad / AGM_TILE_M) * 4 * Hs) : nullptr;
+  B.dense_seg = S_ > 0 ? c.take<int32_t>(sizeof(int32_t) * 2) : nullptr;
   B.bytes = (c.off + 255) & ~size_t(255);
   return B;
 }
@@ -698,18 +766,21 @@ cudaError_t cast_any(int dtype, const float* in, void* out, int64_t n, cudaStrea
 }
 
 template <typename T, typename G>
-cudaError_t launch_combine_train(const Saved& S, int64_t n, int d, int k, int E, void* out, cudaStream_t s) {
+cudaError_t launch_combine_train(const Saved& S, int64_t n, int d, int k, int E, int n_shared, void* out,
+                                 cudaStream_t s) {
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>((n + 7) / 8, 148 * 8));
   const T* y = static_cast<const T*>(S.y);
+  const T* sh = static_cast<const T*>(S.y_sh);
+  const int64_t stride = npad_of(n) * d;
   G* o = static_cast<G*>(out);
   if (k <= 2)
     return launch_kernel(combine_train_kernel<T, G, 2>, dim3(grid), dim3(256), 0, s, y, S.row_of, S.logits, S.idx, n,
-                         d, k, E, o);
+                         d, k, E, sh, n_shared, stride, o);
   if (k <= 4)
     return launch_kernel(combine_train_kernel<T, G, 4>, dim3(grid), dim3(256), 0, s, y, S.row_of, S.logits, S.idx, n,
-                         d, k, E, o);
+                         d, k, E, sh, n_shared, stride, o);
   return launch_kernel(combine_train_kernel<T, G, 16>, dim3(grid), dim3(256), 0, s, y, S.row_of, S.logits, S.idx, n,
-                       d, k, E, o);
+                       d, k, E, sh, n_shared, stride, o);
 }
 
 template <typename T, typename G>
@@ -721,14 +792,16 @@ cudaError_t launch_combine_bwd(const void* dout, const Saved& S, const BwdWs& B,
   const T* y = static_cast<const T*>(S.y);
   T* dy = static_cast<T*>(B.dy);
   T* dl = static_cast<T*>(B.dl);
+  T* ds = static_cast<T*>(B.ds);
+  const int64_t npad = npad_of(n);
   if (k <= 2)
     return launch_kernel(combine_bwd_kernel<T, G, 2>, dim3(grid), dim3(256), 0, s, go, y, S.row_of, S.logits, S.idx,
-                         n, d, k, E, tok_ctas, S.seg_start, S.counts, rows, dy, dl);
+                         n, d, k, E, tok_ctas, S.seg_start, S.counts, rows, dy, dl, ds, npad, B.dense_seg);
   if (k <= 4)
     return launch_kernel(combine_bwd_kernel<T, G, 4>, dim3(grid), dim3(256), 0, s, go, y, S.row_of, S.logits, S.idx,
-                         n, d, k, E, tok_ctas, S.seg_start, S.counts, rows, dy, dl);
+                         n, d, k, E, tok_ctas, S.seg_start, S.counts, rows, dy, dl, ds, npad, B.dense_seg);
   return launch_kernel(combine_bwd_kernel<T, G, 16>, dim3(grid), dim3(256), 0, s, go, y, S.row_of, S.logits, S.idx,
-                       n, d, k, E, tok_ctas, S.seg_start, S.counts, rows, dy, dl);
+                       n, d, k, E, tok_ctas, S.seg_start, S.counts, rows, dy, dl, ds, npad, B.dense_seg);
 }
 
 template <typename T, typename OutT>
@@ -774,8 +847,10 @@ cudaError_t launch_router_wgrad(const BwdWs& B, const Saved& S, int64_t n, int d
 }
 
 template <typename T, typename G>
-cudaError_t launch_dx(const BwdWs& B, const Saved& S, const void* wr, int64_t n, int d, int k, int E, void* dx,
-                      cudaStream_t s) {
+cudaError_t launch_dx(const BwdWs& B, const Saved& S, const void* wr, int64_t n, int d, int k, int E, int n_shared,
+                      void* dx, cudaStream_t s) {
+  const T* dxs = static_cast<const T*>(B.dx_sh);
+  const int64_t sstride = npad_of(n) * d;
   const int smem = E * d * static_cast<int>(sizeof(T)) + 8 * 2 * kMaxE * static_cast<int>(sizeof(float));
   // As many CTAs as fit beside each other (Wr staged in each one's shared memory).
   const int per_sm = std::max(1, std::min(8, (227 * 1024) / std::max(smem + 1024, 1)));
@@ -787,14 +862,17 @@ cudaError_t launch_dx(const BwdWs& B, const Saved& S, const void* wr, int64_t n,
   cudaError_t e;
   if (k <= 2) {
     if ((e = ensure_dynamic_smem(reinterpret_cast<const void*>(dx_kernel<T, G, 2>), smem)) != cudaSuccess) return e;
-    return launch_kernel(dx_kernel<T, G, 2>, dim3(grid), dim3(256), smem, s, dxp, S.row_of, dl, w, n, d, k, E, o);
+    return launch_kernel(dx_kernel<T, G, 2>, dim3(grid), dim3(256), smem, s, dxp, S.row_of, dl, w, n, d, k, E, dxs, n_shared,
+                         sstride, o);
   }
   if (k <= 4) {
     if ((e = ensure_dynamic_smem(reinterpret_cast<const void*>(dx_kernel<T, G, 4>), smem)) != cudaSuccess) return e;
-    return launch_kernel(dx_kernel<T, G, 4>, dim3(grid), dim3(256), smem, s, dxp, S.row_of, dl, w, n, d, k, E, o);
+    return launch_kernel(dx_kernel<T, G, 4>, dim3(grid), dim3(256), smem, s, dxp, S.row_of, dl, w, n, d, k, E, dxs, n_shared,
+                         sstride, o);
   }
   if ((e = ensure_dynamic_smem(reinterpret_cast<const void*>(dx_kernel<T, G, 16>), smem)) != cudaSuccess) return e;
-  return launch_kernel(dx_kernel<T, G, 16>, dim3(grid), dim3(256), smem, s, dxp, S.row_of, dl, w, n, d, k, E, o);
+  return launch_kernel(dx_kernel<T, G, 16>, dim3(grid), dim3(256), smem, s, dxp, S.row_of, dl, w, n, d, k, E, dxs, n_shared,
+                         sstride, o);
 }
 
 }  // namespace
@@ -805,7 +883,7 @@ cudaError_t launch_dx(const BwdWs& B, const Saved& S, const void* wr, int64_t n,
 // ---------------------------------------------------------------------------
 namespace {
 
-int check_train_args(int x_dtype, int dtype, int64_t n, int d, int E, int k, int H) {
+int check_train_args(int x_dtype, int dtype, int64_t n, int d, int E, int k, int H, int S, int Hs) {
   if (!agm::esize(dtype) || !agm::esize(x_dtype)) return agm::fail(AGM_ERR_ARG, "bad dtype code");
   if (x_dtype != dtype && !(x_dtype == AGM_F32 && dtype != AGM_F32))
     return agm::fail(AGM_ERR_ARG, "x_dtype must equal dtype, or be AGM_F32 with a 16-bit dtype (autocast)");
@@ -813,35 +891,61 @@ int check_train_args(int x_dtype, int dtype, int64_t n, int d, int E, int k, int
   if (n < 0) return agm::fail(AGM_ERR_ARG, "n_tokens < 0");
   if (E < 1 || E > AGM_MAX_EXPERTS) return agm::fail(AGM_ERR_UNSUPPORTED, "number of experts must be in [1, 16]");
   if (k < 1 || k > E) return agm::fail(AGM_ERR_ARG, "top_k must be in [1, n_experts]");
-  if (d <= 0 || d % 8 || H <= 0 || H % 8)
-    return agm::fail(AGM_ERR_UNSUPPORTED, "d and hidden must be positive multiples of 8");
-  if ((static_cast<int64_t>(d) * eb) % 16 || (static_cast<int64_t>(H) * eb) % 16)
+  if (S < 0) return agm::fail(AGM_ERR_ARG, "n_shared < 0");
+  if (d <= 0 || d % 8 || H <= 0 || H % 8 || (S > 0 && (Hs <= 0 || Hs % 8)))
+    return agm::fail(AGM_ERR_UNSUPPORTED, "d, hidden and shared_hidden must be positive multiples of 8");
+  if ((static_cast<int64_t>(d) * eb) % 16 || (static_cast<int64_t>(H) * eb) % 16 ||
+      (S > 0 && (static_cast<int64_t>(Hs) * eb) % 16))
     return agm::fail(AGM_ERR_UNSUPPORTED, "d and hidden must be multiples of 16 bytes of the dtype");
   if (agm_max_rows(n, k, E) > INT32_MAX) return agm::fail(AGM_ERR_UNSUPPORTED, "too many permuted rows");
   if (dtype != AGM_F32 && !agm::router_tc_supported(d))
     return agm::fail(AGM_ERR_UNSUPPORTED, "the tensor-core router does not support this d");
   if (dtype == AGM_F32 && agm::router_smem_bytes(d, E) > 227 * 1024)
     return agm::fail(AGM_ERR_UNSUPPORTED, "router weight does not fit in shared memory for this d");
-  if (static_cast<int64_t>(E) * d * eb > 227 * 1024)
+  if (static_cast<int64_t>(E) * d * eb > 200 * 1024)
     return agm::fail(AGM_ERR_UNSUPPORTED, "router weight does not fit in shared memory for the input gradient");
   return AGM_OK;
 }
+
+// One shared expert's FC1 / FC2 over all npad token rows (a single group).
+agm::GemmArgs dense_args(void* c, int64_t npad, int n_out, int k_in, const void* bias, int* err) {
+  agm::GemmArgs g;
+  g.c = c;
+  g.ldc = n_out;
+  g.c_rows = npad;
+  g.bias = bias;
+  g.n = n_out;
+  g.k = k_in;
+  g.groups = 1;
+  g.tile_group = nullptr;
+  g.num_tiles = nullptr;
+  g.max_tiles = static_cast<int>(npad / AGM_TILE_M);
+  g.err = err;
+  return g;
+}
+
+const uint8_t* at(const void* p, size_t bytes) { return static_cast<const uint8_t*>(p) + bytes; }
+uint8_t* at(void* p, size_t bytes) { return static_cast<uint8_t*>(p) + bytes; }
 
 }  // namespace
 
 extern "C" {
 
-size_t agm_moe_train_saved_bytes(int64_t n_tokens, int d, int n_experts, int top_k, int hidden, int x_dtype,
-                                 int dtype) {
+size_t agm_moe_train_saved_bytes(int64_t n_tokens, int d, int n_experts, int top_k, int hidden, int n_shared,
+                                 int shared_hidden, int x_dtype, int dtype) {
   const int eb = agm::esize(dtype);
-  if (!eb || n_tokens < 0 || d <= 0 || n_experts < 1 || top_k < 1 || hidden <= 0) return 0;
-  return agm::carve_saved(nullptr, n_tokens, d, n_experts, top_k, hidden, eb, x_dtype != dtype).bytes;
+  if (!eb || n_tokens < 0 || d <= 0 || n_experts < 1 || top_k < 1 || hidden <= 0 || n_shared < 0) return 0;
+  return agm::carve_saved(nullptr, n_tokens, d, n_experts, top_k, hidden, eb, x_dtype != dtype, n_shared,
+                          std::max(1, shared_hidden))
+      .bytes;
 }
 
-size_t agm_moe_backward_workspace_bytes(int64_t n_tokens, int d, int n_experts, int top_k, int hidden, int dtype) {
+size_t agm_moe_backward_workspace_bytes(int64_t n_tokens, int d, int n_experts, int top_k, int hidden, int n_shared,
+                                        int shared_hidden, int dtype) {
   const int eb = agm::esize(dtype);
-  if (!eb || n_tokens < 0 || d <= 0 || n_experts < 1 || top_k < 1 || hidden <= 0) return 0;
-  return agm::carve_bwd(nullptr, n_tokens, d, n_experts, top_k, hidden, eb).bytes;
+  if (!eb || n_tokens < 0 || d <= 0 || n_experts < 1 || top_k < 1 || hidden <= 0 || n_shared < 0) return 0;
+  return agm::carve_bwd(nullptr, n_tokens, d, n_experts, top_k, hidden, eb, n_shared, std::max(1, shared_hidden))
+      .bytes;
 }
 
 int agm_cast_f32(const float* in, void* out, int dtype, int64_t n, void* stream) {
@@ -856,17 +960,22 @@ int agm_cast_f32(const float* in, void* out, int dtype, int64_t n, void* stream)
 
 int agm_moe_forward_train(const void* x, int x_dtype, int dtype, int64_t n_tokens, int d, int n_experts, int top_k,
                           int hidden, const void* w_router, const void* w1, const void* b1, const void* w2,
-                          const void* b2, void* out, void* saved, size_t saved_bytes, int32_t* counts_out, int flags,
-                          void* stream_) {
-  int rc = check_train_args(x_dtype, dtype, n_tokens, d, n_experts, top_k, hidden);
+                          const void* b2, int n_shared, int shared_hidden, const void* ws1, const void* sb1,
+                          const void* ws2, const void* sb2, void* out, void* saved, size_t saved_bytes,
+                          int32_t* counts_out, int flags, void* stream_) {
+  int rc = check_train_args(x_dtype, dtype, n_tokens, d, n_experts, top_k, hidden, n_shared, shared_hidden);
   if (rc) return rc;
   if (!x || !w_router || !w1 || !b1 || !w2 || !b2 || !out || !saved) return agm::fail(AGM_ERR_ARG, "null pointer");
+  if (n_shared > 0 && (!ws1 || !sb1 || !ws2 || !sb2)) return agm::fail(AGM_ERR_ARG, "null shared-expert pointer");
   const void* ptrs[] = {x, w_router, w1, b1, w2, b2, out, saved};
   for (const void* p : ptrs)
     if (!agm::al16(p)) return agm::fail(AGM_ERR_ARG, "all tensors must be 16-byte aligned");
+  if (n_shared > 0 && (!agm::al16(ws1) || !agm::al16(sb1) || !agm::al16(ws2) || !agm::al16(sb2)))
+    return agm::fail(AGM_ERR_ARG, "all tensors must be 16-byte aligned");
   const int eb = agm::esize(dtype);
   const bool amp = x_dtype != dtype;
-  agm::Saved S = agm::carve_saved(saved, n_tokens, d, n_experts, top_k, hidden, eb, amp);
+  const int Hs = std::max(1, shared_hidden);
+  agm::Saved S = agm::carve_saved(saved, n_tokens, d, n_experts, top_k, hidden, eb, amp, n_shared, Hs);
   if (S.bytes > saved_bytes) return agm::fail(AGM_ERR_WORKSPACE, "saved-state buffer too small");
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   agm::PdlScope pdl_scope(!(flags & AGM_FLAG_NO_PDL));
@@ -877,11 +986,20 @@ int agm_moe_forward_train(const void* x, int x_dtype, int dtype, int64_t n_token
     return e == cudaSuccess ? AGM_OK : agm::cuda_fail(e, "memset");
   }
   const int64_t rows = agm_max_rows(n_tokens, top_k, n_experts);
+  const int64_t npad = agm::npad_of(n_tokens);
   const int sms = agm::sm_count();
   const void* xin = x;
-  if (amp) {
-    e = agm::cast_any(dtype, static_cast<const float*>(x), S.xb, n_tokens * d, stream);
-    if (e != cudaSuccess) return agm::cuda_fail(e, "cast x");
+  if (S.xb) {
+    // [npad, d]: the compute-dtype input with zero rows past n (the shared
+    // experts' weight gradient reads whole 128-row tiles of it).
+    if (amp)
+      e = agm::cast_any(dtype, static_cast<const float*>(x), S.xb, n_tokens * d, stream);
+    else
+      e = cudaMemcpyAsync(S.xb, x, static_cast<size_t>(eb) * n_tokens * d, cudaMemcpyDeviceToDevice, stream);
+    if (e == cudaSuccess && npad > n_tokens)
+      e = cudaMemsetAsync(at(S.xb, static_cast<size_t>(eb) * n_tokens * d), 0,
+                          static_cast<size_t>(eb) * (npad - n_tokens) * d, stream);
+    if (e != cudaSuccess) return agm::cuda_fail(e, "input copy");
     xin = S.xb;
   }
   e = agm::router_topk(dtype, xin, w_router, n_tokens, d, n_experts, top_k, flags & AGM_FLAG_TIE_LOW_FIRST, nullptr,
@@ -928,35 +1046,65 @@ int agm_moe_forward_train(const void* x, int x_dtype, int dtype, int64_t n_token
   g2.k = hidden;
   e = agm::grouped_gemm(dtype, S.h, rows, w2, g2, false, sms, stream, pair ? AGM_GEMM_PAIR : 0);
   if (e != cudaSuccess) return agm::cuda_fail(e, "grouped_gemm fc2");
+  for (int s = 0; s < n_shared; ++s) {
+    void* hs = at(S.h_sh, static_cast<size_t>(eb) * s * npad * Hs);
+    agm::GemmArgs s1 = dense_args(hs, npad, Hs, d, at(sb1, static_cast<size_t>(eb) * s * Hs), S.err);
+    if (S.bits_sh) {
+      s1.relu_bits = S.bits_sh + static_cast<int64_t>(s) * ((Hs + 31) / 32) * npad;
+      s1.ld_bits = npad;
+    }
+    e = agm::grouped_gemm(dtype, xin, n_tokens, at(ws1, static_cast<size_t>(eb) * s * Hs * d), s1, true, sms,
+                          stream, 0);
+    if (e != cudaSuccess) return agm::cuda_fail(e, "grouped_gemm shared fc1");
+    agm::GemmArgs s2 = dense_args(at(S.y_sh, static_cast<size_t>(eb) * s * npad * d), npad, d, Hs,
+                                  at(sb2, static_cast<size_t>(eb) * s * d), S.err);
+    e = agm::grouped_gemm(dtype, hs, npad, at(ws2, static_cast<size_t>(eb) * s * d * Hs), s2, false, sms, stream,
+                          0);
+    if (e != cudaSuccess) return agm::cuda_fail(e, "grouped_gemm shared fc2");
+  }
   switch (dtype) {
-    case AGM_F32: e = agm::launch_combine_train<float, float>(S, n_tokens, d, top_k, n_experts, out, stream); break;
+    case AGM_F32:
+      e = agm::launch_combine_train<float, float>(S, n_tokens, d, top_k, n_experts, n_shared, out, stream);
+      break;
     case AGM_BF16:
-      e = amp ? agm::launch_combine_train<__nv_bfloat16, float>(S, n_tokens, d, top_k, n_experts, out, stream)
-              : agm::launch_combine_train<__nv_bfloat16, __nv_bfloat16>(S, n_tokens, d, top_k, n_experts, out, stream);
+      e = amp ? agm::launch_combine_train<__nv_bfloat16, float>(S, n_tokens, d, top_k, n_experts, n_shared, out,
+                                                                 stream)
+              : agm::launch_combine_train<__nv_bfloat16, __nv_bfloat16>(S, n_tokens, d, top_k, n_experts, n_shared,
+                                                                         out, stream);
       break;
     default:
-      e = amp ? agm::launch_combine_train<__half, float>(S, n_tokens, d, top_k, n_experts, out, stream)
-              : agm::launch_combine_train<__half, __half>(S, n_tokens, d, top_k, n_experts, out, stream);
+      e = amp ? agm::launch_combine_train<__half, float>(S, n_tokens, d, top_k, n_experts, n_shared, out, stream)
+              : agm::launch_combine_train<__half, __half>(S, n_tokens, d, top_k, n_experts, n_shared, out, stream);
   }
   return e == cudaSuccess ? AGM_OK : agm::cuda_fail(e, "combine_train");
 }
 
 int agm_moe_backward(const void* dout, int x_dtype, int dtype, int64_t n_tokens, int d, int n_experts, int top_k,
-                     int hidden, const void* w_router, const void* w1, const void* w2, const void* saved,
-                     size_t saved_bytes, void* dx, void* dw_router, void* dw1, void* db1, void* dw2, void* db2,
-                     void* workspace, size_t workspace_bytes, int flags, void* stream_) {
-  int rc = check_train_args(x_dtype, dtype, n_tokens, d, n_experts, top_k, hidden);
+                     int hidden, const void* w_router, const void* w1, const void* w2, int n_shared,
+                     int shared_hidden, const void* ws1, const void* ws2, const void* saved, size_t saved_bytes,
+                     void* dx, void* dw_router, void* dw1, void* db1, void* dw2, void* db2, void* dws1, void* dsb1,
+                     void* dws2, void* dsb2, void* workspace, size_t workspace_bytes, int flags, void* stream_) {
+  int rc = check_train_args(x_dtype, dtype, n_tokens, d, n_experts, top_k, hidden, n_shared, shared_hidden);
   if (rc) return rc;
   if (!dout || !w_router || !w1 || !w2 || !saved || !dx || !dw_router || !dw1 || !db1 || !dw2 || !db2 || !workspace)
     return agm::fail(AGM_ERR_ARG, "null pointer");
+  if (n_shared > 0 && (!ws1 || !ws2 || !dws1 || !dsb1 || !dws2 || !dsb2))
+    return agm::fail(AGM_ERR_ARG, "null shared-expert pointer");
   const void* ptrs[] = {dout, w_router, w1, w2, saved, dx, dw_router, dw1, db1, dw2, db2, workspace};
   for (const void* p : ptrs)
     if (!agm::al16(p)) return agm::fail(AGM_ERR_ARG, "all tensors must be 16-byte aligned");
+  if (n_shared > 0) {
+    const void* sp[] = {ws1, ws2, dws1, dsb1, dws2, dsb2};
+    for (const void* p : sp)
+      if (!agm::al16(p)) return agm::fail(AGM_ERR_ARG, "all tensors must be 16-byte aligned");
+  }
   const int eb = agm::esize(dtype);
   const bool amp = x_dtype != dtype;
-  agm::Saved S = agm::carve_saved(const_cast<void*>(saved), n_tokens, d, n_experts, top_k, hidden, eb, amp);
+  const int Hs = std::max(1, shared_hidden);
+  agm::Saved S = agm::carve_saved(const_cast<void*>(saved), n_tokens, d, n_experts, top_k, hidden, eb, amp, n_shared,
+                                  Hs);
   if (S.bytes > saved_bytes) return agm::fail(AGM_ERR_WORKSPACE, "saved-state buffer too small");
-  agm::BwdWs B = agm::carve_bwd(workspace, n_tokens, d, n_experts, top_k, hidden, eb);
+  agm::BwdWs B = agm::carve_bwd(workspace, n_tokens, d, n_experts, top_k, hidden, eb, n_shared, Hs);
   if (B.bytes > workspace_bytes) return agm::fail(AGM_ERR_WORKSPACE, "workspace too small");
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   agm::PdlScope pdl_scope(!(flags & AGM_FLAG_NO_PDL));
@@ -967,16 +1115,44 @@ int agm_moe_backward(const void* dout, int x_dtype, int dtype, int64_t n_tokens,
     // No tokens: every gradient is zero.
     const size_t sizes[] = {static_cast<size_t>(xe) * n_experts * d, static_cast<size_t>(xe) * n_experts * hidden * d,
                             static_cast<size_t>(xe) * n_experts * hidden, static_cast<size_t>(xe) * n_experts * d * hidden,
-                            static_cast<size_t>(xe) * n_experts * d};
-    void* outs[] = {dw_router, dw1, db1, dw2, db2};
-    for (int i = 0; i < 5 && e == cudaSuccess; ++i) e = cudaMemsetAsync(outs[i], 0, sizes[i], stream);
+                            static_cast<size_t>(xe) * n_experts * d, static_cast<size_t>(xe) * n_shared * Hs * d,
+                            static_cast<size_t>(xe) * n_shared * Hs, static_cast<size_t>(xe) * n_shared * d * Hs,
+                            static_cast<size_t>(xe) * n_shared * d};
+    void* outs[] = {dw_router, dw1, db1, dw2, db2, dws1, dsb1, dws2, dsb2};
+    for (int i = 0; i < 9 && e == cudaSuccess; ++i)
+      if (outs[i] && sizes[i]) e = cudaMemsetAsync(outs[i], 0, sizes[i], stream);
     return e == cudaSuccess ? AGM_OK : agm::cuda_fail(e, "memset");
   }
   const int64_t rows = agm_max_rows(n_tokens, top_k, n_experts);
+  const int64_t npad = agm::npad_of(n_tokens);
   const int sms = agm::sm_count();
   const int max_tiles = static_cast<int>(rows / AGM_TILE_M);
 
-  // 1. combine + routing backward -> dy, dl
+  // Per-segment column sums (fp32 SIMT path, and db2) into out.
+  auto colsum = [&](const void* m, int ncols, const int32_t* seg, int groups, void* out) -> cudaError_t {
+    switch (dtype) {
+      case AGM_F32: return agm::launch_colsum<float, float>(m, ncols, seg, groups, B.colsum, out, stream);
+      case AGM_BF16:
+        return amp ? agm::launch_colsum<__nv_bfloat16, float>(m, ncols, seg, groups, B.colsum, out, stream)
+                   : agm::launch_colsum<__nv_bfloat16, __nv_bfloat16>(m, ncols, seg, groups, B.colsum, out, stream);
+      default:
+        return amp ? agm::launch_colsum<__half, float>(m, ncols, seg, groups, B.colsum, out, stream)
+                   : agm::launch_colsum<__half, __half>(m, ncols, seg, groups, B.colsum, out, stream);
+    }
+  };
+  // Bias gradient from the dgrad epilogue's per-quarter partials.
+  auto tile_parts = [&](const float* part, const int32_t* seg, int groups, int ncols, void* out) -> cudaError_t {
+    switch (dtype) {
+      case AGM_BF16:
+        return amp ? agm::launch_tile_parts<__nv_bfloat16, float>(part, seg, groups, ncols, out, stream)
+                   : agm::launch_tile_parts<__nv_bfloat16, __nv_bfloat16>(part, seg, groups, ncols, out, stream);
+      default:
+        return amp ? agm::launch_tile_parts<__half, float>(part, seg, groups, ncols, out, stream)
+                   : agm::launch_tile_parts<__half, __half>(part, seg, groups, ncols, out, stream);
+    }
+  };
+
+  // 1. combine + routing backward -> dy, dl (and the shared sum's gradient ds)
   switch (dtype) {
     case AGM_F32: e = agm::launch_combine_bwd<float, float>(dout, S, B, n_tokens, d, top_k, n_experts, rows, stream); break;
     case AGM_BF16:
@@ -1023,31 +1199,10 @@ int agm_moe_backward(const void* dout, int x_dtype, int dtype, int64_t n_tokens,
   e = agm::grouped_gemm_dgrad(dtype, B.dy, rows, w2, d2, true, sms, stream);
   if (e != cudaSuccess) return agm::cuda_fail(e, "dgrad fc2");
   // 4. bias gradients (dy is still intact: dgrad wrote dh)
-  auto colsum = [&](const void* m, int ncols, void* out) -> cudaError_t {
-    switch (dtype) {
-      case AGM_F32: return agm::launch_colsum<float, float>(m, ncols, S.seg_start, n_experts, B.colsum, out, stream);
-      case AGM_BF16:
-        return amp ? agm::launch_colsum<__nv_bfloat16, float>(m, ncols, S.seg_start, n_experts, B.colsum, out, stream)
-                   : agm::launch_colsum<__nv_bfloat16, __nv_bfloat16>(m, ncols, S.seg_start, n_experts, B.colsum, out,
-                                                                      stream);
-      default:
-        return amp ? agm::launch_colsum<__half, float>(m, ncols, S.seg_start, n_experts, B.colsum, out, stream)
-                   : agm::launch_colsum<__half, __half>(m, ncols, S.seg_start, n_experts, B.colsum, out, stream);
-    }
-  };
-  e = colsum(B.dy, d, db2);
+  e = colsum(B.dy, d, S.seg_start, n_experts, db2);
   if (e != cudaSuccess) return agm::cuda_fail(e, "db2");
-  switch (dtype) {
-    case AGM_F32: e = colsum(B.dh, hidden, db1); break;
-    case AGM_BF16:
-      e = amp ? agm::launch_tile_parts<__nv_bfloat16, float>(B.dh_part, S.seg_start, n_experts, hidden, db1, stream)
-              : agm::launch_tile_parts<__nv_bfloat16, __nv_bfloat16>(B.dh_part, S.seg_start, n_experts, hidden, db1,
-                                                                     stream);
-      break;
-    default:
-      e = amp ? agm::launch_tile_parts<__half, float>(B.dh_part, S.seg_start, n_experts, hidden, db1, stream)
-              : agm::launch_tile_parts<__half, __half>(B.dh_part, S.seg_start, n_experts, hidden, db1, stream);
-  }
+  e = dtype == AGM_F32 ? colsum(B.dh, hidden, S.seg_start, n_experts, db1)
+                       : tile_parts(B.dh_part, S.seg_start, n_experts, hidden, db1);
   if (e != cudaSuccess) return agm::cuda_fail(e, "db1");
   // 5. FC1 weight gradient: dW1[e] [H, d] = dh_e^T x_perm_e
   agm::BwdGemmArgs w1a = w2a;
@@ -1067,7 +1222,71 @@ int agm_moe_backward(const void* dout, int x_dtype, int dtype, int64_t n_tokens,
   d1.col_part = nullptr;
   e = agm::grouped_gemm_dgrad(dtype, B.dh, rows, w1, d1, false, sms, stream);
   if (e != cudaSuccess) return agm::cuda_fail(e, "dgrad fc1");
-  // 7. router weight gradient: dWr = dl^T x
+
+  // 7. shared experts: one dense segment of npad rows each, gradient ds
+  //    (agillm41.py:4381-4387: s = shared[0](x) + shared[1](x) + ..., out += s)
+  const int xs = agm::esize(x_dtype);
+  if (n_shared > 0) {
+    e = colsum(B.ds, d, B.dense_seg, 1, dsb2);  // the same for every shared expert
+    for (int s = 1; s < n_shared && e == cudaSuccess; ++s)
+      e = cudaMemcpyAsync(at(dsb2, static_cast<size_t>(xs) * s * d), dsb2, static_cast<size_t>(xs) * d,
+                          cudaMemcpyDeviceToDevice, stream);
+    if (e != cudaSuccess) return agm::cuda_fail(e, "shared db2");
+  }
+  for (int s = 0; s < n_shared; ++s) {
+    const void* hs = at(S.h_sh, static_cast<size_t>(eb) * s * npad * Hs);
+    agm::BwdGemmArgs sw2;
+    sw2.c = at(dws2, static_cast<size_t>(xs) * s * d * Hs);
+    sw2.m = d;
+    sw2.n = Hs;
+    sw2.groups = 1;
+    sw2.seg_start = B.dense_seg;
+    sw2.err = B.err;
+    e = agm::grouped_gemm_wgrad(dtype, amp, B.ds, hs, npad, sw2, sms, stream);
+    if (e != cudaSuccess) return agm::cuda_fail(e, "shared wgrad fc2");
+    agm::BwdGemmArgs sd2;
+    sd2.c = B.dh_sh;
+    sd2.ldc = Hs;
+    sd2.c_rows = npad;
+    sd2.n = Hs;
+    sd2.k = d;
+    sd2.groups = 1;
+    sd2.max_tiles = static_cast<int>(npad / AGM_TILE_M);
+    if (dtype == AGM_F32) {
+      sd2.aux = hs;
+      sd2.ld_aux = Hs;
+    } else {
+      sd2.aux_bits = S.bits_sh + static_cast<int64_t>(s) * ((Hs + 31) / 32) * npad;
+      sd2.ld_aux_bits = npad;
+      sd2.col_part = B.dhs_part;
+    }
+    sd2.err = B.err;
+    e = agm::grouped_gemm_dgrad(dtype, B.ds, npad, at(ws2, static_cast<size_t>(eb) * s * d * Hs), sd2, true, sms,
+                                stream);
+    if (e != cudaSuccess) return agm::cuda_fail(e, "shared dgrad fc2");
+    void* db1s = at(dsb1, static_cast<size_t>(xs) * s * Hs);
+    e = dtype == AGM_F32 ? colsum(B.dh_sh, Hs, B.dense_seg, 1, db1s) : tile_parts(B.dhs_part, B.dense_seg, 1, Hs, db1s);
+    if (e != cudaSuccess) return agm::cuda_fail(e, "shared db1");
+    agm::BwdGemmArgs sw1 = sw2;
+    sw1.c = at(dws1, static_cast<size_t>(xs) * s * Hs * d);
+    sw1.m = Hs;
+    sw1.n = d;
+    e = agm::grouped_gemm_wgrad(dtype, amp, B.dh_sh, S.xb, npad, sw1, sms, stream);
+    if (e != cudaSuccess) return agm::cuda_fail(e, "shared wgrad fc1");
+    agm::BwdGemmArgs sd1 = sd2;
+    sd1.c = at(B.dx_sh, static_cast<size_t>(eb) * s * npad * d);
+    sd1.ldc = d;
+    sd1.n = d;
+    sd1.k = Hs;
+    sd1.aux = nullptr;
+    sd1.aux_bits = nullptr;
+    sd1.col_part = nullptr;
+    e = agm::grouped_gemm_dgrad(dtype, B.dh_sh, npad, at(ws1, static_cast<size_t>(eb) * s * Hs * d), sd1, false,
+                                sms, stream);
+    if (e != cudaSuccess) return agm::cuda_fail(e, "shared dgrad fc1");
+  }
+
+  // 8. router weight gradient: dWr = dl^T x
   switch (dtype) {
     case AGM_F32: e = agm::launch_router_wgrad<float, float>(B, S, n_tokens, d, top_k, n_experts, dw_router, stream); break;
     case AGM_BF16:
@@ -1080,16 +1299,20 @@ int agm_moe_backward(const void* dout, int x_dtype, int dtype, int64_t n_tokens,
               : agm::launch_router_wgrad<__half, __half>(B, S, n_tokens, d, top_k, n_experts, dw_router, stream);
   }
   if (e != cudaSuccess) return agm::cuda_fail(e, "router wgrad");
-  // 8. input gradient
+  // 9. input gradient
   switch (dtype) {
-    case AGM_F32: e = agm::launch_dx<float, float>(B, S, w_router, n_tokens, d, top_k, n_experts, dx, stream); break;
+    case AGM_F32:
+      e = agm::launch_dx<float, float>(B, S, w_router, n_tokens, d, top_k, n_experts, n_shared, dx, stream);
+      break;
     case AGM_BF16:
-      e = amp ? agm::launch_dx<__nv_bfloat16, float>(B, S, w_router, n_tokens, d, top_k, n_experts, dx, stream)
-              : agm::launch_dx<__nv_bfloat16, __nv_bfloat16>(B, S, w_router, n_tokens, d, top_k, n_experts, dx, stream);
+      e = amp ? agm::launch_dx<__nv_bfloat16, float>(B, S, w_router, n_tokens, d, top_k, n_experts, n_shared, dx,
+                                                     stream)
+              : agm::launch_dx<__nv_bfloat16, __nv_bfloat16>(B, S, w_router, n_tokens, d, top_k, n_experts, n_shared,
+                                                             dx, stream);
       break;
     default:
-      e = amp ? agm::launch_dx<__half, float>(B, S, w_router, n_tokens, d, top_k, n_experts, dx, stream)
-              : agm::launch_dx<__half, __half>(B, S, w_router, n_tokens, d, top_k, n_experts, dx, stream);
+      e = amp ? agm::launch_dx<__half, float>(B, S, w_router, n_tokens, d, top_k, n_experts, n_shared, dx, stream)
+              : agm::launch_dx<__half, __half>(B, S, w_router, n_tokens, d, top_k, n_experts, n_shared, dx, stream);
   }
   return e == cudaSuccess ? AGM_OK : agm::cuda_fail(e, "dx");
 }

@@ -25,8 +25,8 @@ Training: when autograd needs gradients, the forward runs
 kernels), in the two precision modes the reference trains in: one dtype
 throughout, or torch.autocast (bf16/fp16) over fp32 master weights with an
 fp32 input, as ``Block`` feeds it from its LayerNorm (agillm41.py:4539-4547)
-under the reference's ``amp()`` (agillm41.py:3054-3066). Shared experts are
-inference-only.
+under the reference's ``amp()`` (agillm41.py:3054-3066), shared experts
+included.
 
 ``install(agillm41)`` rebinds the reference module's ``MoEFFN`` to a subclass
 of the reference class that uses this forward, so ``Block`` (4533-4537), the
@@ -60,9 +60,10 @@ class _MoETrainNode(torch.autograd.Function):
     product and index_add_).
 
     Inputs: x [N, d], the router weight, a state dict (compute-dtype weights,
-    top_k, error checking) and the expert parameters in the order
-    experts.{e}.0.weight, .0.bias, .2.weight, .2.bias for e = 0..E-1; their
-    gradients come back as views of the packed [E, ...] gradient tensors.
+    top_k, error checking) and the parameters in the order
+    experts.{e}.0.weight, .0.bias, .2.weight, .2.bias for e = 0..E-1, then
+    shared.{s}.0.weight, ... for the shared experts; their gradients come
+    back as views of the packed [E, ...] / [S, ...] gradient tensors.
     Everything the backward reads is saved with save_for_backward, so
     activation checkpointing (agillm41.py:1202, 4662) can drop and recompute it.
 
@@ -77,27 +78,40 @@ class _MoETrainNode(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w_router, state, *params):
         wr_c, w1, b1, w2, b2 = state["weights"]
-        out, saved, counts = ops.moe_forward_train(x, wr_c, w1, b1, w2, b2, state["top_k"],
+        sh = state.get("shared")
+        out, saved, counts = ops.moe_forward_train(x, wr_c, w1, b1, w2, b2, state["top_k"], shared=sh,
                                                    check_errors=state["check"], want_counts=True)
-        ctx.save_for_backward(saved, wr_c, w1, w2, counts)
+        if sh is not None:
+            ctx.save_for_backward(saved, wr_c, w1, w2, counts, sh[0], sh[2])
+        else:
+            ctx.save_for_backward(saved, wr_c, w1, w2, counts)
         ctx.top_k = state["top_k"]
         ctx.check = state["check"]
         ctx.none_for_empty = state.get("empty_grad", "none") == "none"
-        ctx.n_params = len(params)
+        ctx.n_experts = w1.shape[0]
         return out
 
     @staticmethod
     def backward(ctx, dout):
-        saved, wr_c, w1, w2, counts = ctx.saved_tensors
-        dx, dwr, dw1, db1, dw2, db2 = ops.moe_backward(dout.contiguous(), saved, wr_c, w1, w2, ctx.top_k,
-                                                       check_errors=ctx.check)
+        saved, wr_c, w1, w2, counts, *sw = ctx.saved_tensors
+        shared = None
+        if sw:
+            # only the weights' shapes and pointers matter for the biases here
+            shared = (sw[0], None, sw[1], None)
+        res = ops.moe_backward(dout.contiguous(), saved, wr_c, w1, w2, ctx.top_k, shared=shared,
+                               check_errors=ctx.check)
+        dx, dwr, dw1, db1, dw2, db2 = res[:6]
         used = counts.cpu().tolist() if ctx.none_for_empty else None
         grads = []
-        for e in range(ctx.n_params // 4):
+        for e in range(ctx.n_experts):
             if used is not None and used[e] == 0:
                 grads += [None, None, None, None]
             else:
                 grads += [dw1[e], db1[e], dw2[e], db2[e]]
+        if sw:
+            dws1, dsb1, dws2, dsb2 = res[6]
+            for s in range(dws1.shape[0]):
+                grads += [dws1[s], dsb1[s], dws2[s], dsb2[s]]
         return (dx if ctx.needs_input_grad[0] else None, dwr if ctx.needs_input_grad[1] else None, None, *grads)
 
 
@@ -165,17 +179,20 @@ class _B200Forward:
         return packed
 
     def _expert_params(self):
-        return [p for ex in self.experts for p in (ex[0].weight, ex[0].bias, ex[2].weight, ex[2].bias)]
+        experts = [p for ex in self.experts for p in (ex[0].weight, ex[0].bias, ex[2].weight, ex[2].bias)]
+        shared = list(self.shared) if getattr(self, "shared", None) is not None else []
+        return experts + [p for ex in shared for p in (ex[0].weight, ex[0].bias, ex[2].weight, ex[2].bias)]
 
     def _compute_weights(self, device: torch.device, master_dtype: torch.dtype, compute_dtype: torch.dtype):
-        """(router, w1, b1, w2, b2) in the compute dtype. Same dtype: the
-        packed parameters themselves. Autocast: their 16-bit casts, made once
-        per change of the parameters (the version counters of the parameters
-        key the cache, so an optimiser step or load_state_dict recasts)."""
-        w1, b1, w2, b2, _ = self._packed_weights(device, master_dtype)
+        """((router, w1, b1, w2, b2), shared (ws1, sb1, ws2, sb2) or None) in
+        the compute dtype. Same dtype: the packed parameters themselves.
+        Autocast: their 16-bit casts, made once per change of the parameters
+        (the version counters of the parameters key the cache, so an
+        optimiser step or load_state_dict recasts)."""
+        w1, b1, w2, b2, sh = self._packed_weights(device, master_dtype)
         wr = self.router.weight
         if compute_dtype == master_dtype:
-            return wr.detach().contiguous(), w1, b1, w2, b2
+            return (wr.detach().contiguous(), w1, b1, w2, b2), sh
         params = [wr] + self._expert_params()
         key = (device, compute_dtype) + tuple((p.data_ptr(), p._version) for p in params)
         cache = getattr(self, "_b200_cast", None)
@@ -183,8 +200,9 @@ class _B200Forward:
             return cache[1]
         with torch.no_grad():
             cast = tuple(ops.cast_f32(t.detach(), compute_dtype) for t in (wr, w1, b1, w2, b2))
-        self._b200_cast = (key, cast)
-        return cast
+            csh = None if sh is None else tuple(ops.cast_f32(t, compute_dtype) for t in sh)
+        self._b200_cast = (key, (cast, csh))
+        return cast, csh
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:  # agillm41.py:4389-4431
         orig_shape = x.shape
@@ -207,19 +225,17 @@ class _B200Forward:
         grad = torch.is_grad_enabled() and (flat.requires_grad or wr.requires_grad
                                             or any(p.requires_grad for p in params))
         if grad or amp_mode:
-            if getattr(self, "shared", None) is not None:
-                raise MoEKernelError("shared experts are supported in the inference forward only (no autograd, "
-                                     "no autocast over fp32 weights)")
             if self.router_logits != "kernel":
                 raise MoEKernelError("training and autocast route with the router kernel's logits only")
-            weights = self._compute_weights(flat.device, wr.dtype, amp if amp_mode else wr.dtype)
+            weights, shared = self._compute_weights(flat.device, wr.dtype, amp if amp_mode else wr.dtype)
             flat = flat.contiguous()
             if grad:
-                state = {"weights": weights, "top_k": self.top_k, "check": self.check_device_errors,
-                         "empty_grad": self.empty_expert_grad}
+                state = {"weights": weights, "shared": shared, "top_k": self.top_k,
+                         "check": self.check_device_errors, "empty_grad": self.empty_expert_grad}
                 out = _MoETrainNode.apply(flat, wr, state, *params)
             else:
-                out, _ = ops.moe_forward_train(flat, *weights, self.top_k, check_errors=self.check_device_errors)
+                out, _ = ops.moe_forward_train(flat, *weights, self.top_k, shared=shared,
+                                               check_errors=self.check_device_errors)
             return out.reshape(orig_shape)
         w1, b1, w2, b2, sh = self._packed_weights(flat.device, flat.dtype)
         flat = flat.contiguous()

@@ -313,18 +313,27 @@ def cast_f32(x: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
 
 
 def train_saved_bytes(n_tokens: int, d: int, n_experts: int, top_k: int, hidden: int, x_dtype: torch.dtype,
-                      dtype: torch.dtype) -> int:
-    return int(load().agm_moe_train_saved_bytes(n_tokens, d, n_experts, top_k, hidden, dtype_code(x_dtype),
-                                                dtype_code(dtype)))
+                      dtype: torch.dtype, n_shared: int = 0, shared_hidden: int = 1) -> int:
+    return int(load().agm_moe_train_saved_bytes(n_tokens, d, n_experts, top_k, hidden, n_shared,
+                                                max(shared_hidden, 1), dtype_code(x_dtype), dtype_code(dtype)))
+
+
+def _shared_parts(shared):
+    if shared is None:
+        return None, None, None, None, 0, 1
+    ws1, sb1, ws2, sb2 = shared
+    return ws1, sb1, ws2, sb2, ws1.shape[0], ws1.shape[1]
 
 
 def moe_forward_train(x: torch.Tensor, w_router: torch.Tensor, w1: torch.Tensor, b1: torch.Tensor,
-                      w2: torch.Tensor, b2: torch.Tensor, top_k: int, *, tie_low_first: bool = False,
-                      pair: bool = True, pdl: bool = True, check_errors: bool = False, want_counts: bool = False):
+                      w2: torch.Tensor, b2: torch.Tensor, top_k: int, *, shared: Optional[tuple] = None,
+                      tie_low_first: bool = False, pair: bool = True, pdl: bool = True, check_errors: bool = False,
+                      want_counts: bool = False):
     """Training forward: x [N, d] -> (out [N, d] in x's dtype, saved uint8 buffer).
 
     The weights are in the compute dtype: x's dtype, or bf16/fp16 with x fp32
     (autocast: the weights are the 16-bit casts of fp32 master weights).
+    ``shared`` = (ws1 [S,Hs,d], sb1 [S,Hs], ws2 [S,d,Hs], sb2 [S,d]) or None.
     ``saved`` holds what :func:`moe_backward` needs; its first int is the
     device error word. With ``want_counts`` the result also carries the rows
     routed to each expert (int32 [E]): (out, saved, counts)."""
@@ -334,14 +343,15 @@ def moe_forward_train(x: torch.Tensor, w_router: torch.Tensor, w1: torch.Tensor,
     H = w1.shape[1]
     dev = x.device
     dtype = w1.dtype
-    nbytes = train_saved_bytes(n, d, E, top_k, H, x.dtype, dtype)
+    ws1, sb1, ws2, sb2, S, Hs = _shared_parts(shared)
+    nbytes = train_saved_bytes(n, d, E, top_k, H, x.dtype, dtype, S, Hs)
     saved = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
     out = torch.empty(n, d, dtype=x.dtype, device=dev)
     counts = torch.empty(E, dtype=torch.int32, device=dev) if want_counts else None
     flags = _flags(tie_low_first) | (0 if pair else _lib.AGM_FLAG_NO_PAIR) | (0 if pdl else _lib.AGM_FLAG_NO_PDL)
     rc = lib.agm_moe_forward_train(ptr(x), dtype_code(x.dtype), dtype_code(dtype), n, d, E, top_k, H, ptr(w_router),
-                                   ptr(w1), ptr(b1), ptr(w2), ptr(b2), ptr(out), ptr(saved), saved.numel(),
-                                   ptr(counts), flags, stream_handle(dev))
+                                   ptr(w1), ptr(b1), ptr(w2), ptr(b2), S, Hs, ptr(ws1), ptr(sb1), ptr(ws2), ptr(sb2),
+                                   ptr(out), ptr(saved), saved.numel(), ptr(counts), flags, stream_handle(dev))
     check(rc, "agm_moe_forward_train")
     if check_errors:
         code = _lib.read_device_error(saved[:4].view(torch.int32))
@@ -351,10 +361,12 @@ def moe_forward_train(x: torch.Tensor, w_router: torch.Tensor, w1: torch.Tensor,
 
 
 def moe_backward(dout: torch.Tensor, saved: torch.Tensor, w_router: torch.Tensor, w1: torch.Tensor,
-                 w2: torch.Tensor, top_k: int, *, pdl: bool = True, check_errors: bool = False):
+                 w2: torch.Tensor, top_k: int, *, shared: Optional[tuple] = None, pdl: bool = True,
+                 check_errors: bool = False):
     """Backward of :func:`moe_forward_train`: dout [N, d] (x's dtype) ->
-    (dx, dw_router [E, d], dw1 [E, H, d], db1 [E, H], dw2 [E, d, H], db2 [E, d]),
-    all in x's dtype (fp32 under autocast)."""
+    (dx, dw_router [E, d], dw1 [E, H, d], db1 [E, H], dw2 [E, d, H], db2 [E, d])
+    plus, with ``shared`` (the forward's (ws1, sb1, ws2, sb2)), a fourth-level
+    tuple (dws1, dsb1, dws2, dsb2); all in x's dtype (fp32 under autocast)."""
     lib = load()
     n, d = dout.shape
     E = w_router.shape[0]
@@ -362,6 +374,7 @@ def moe_backward(dout: torch.Tensor, saved: torch.Tensor, w_router: torch.Tensor
     dev = dout.device
     dtype = w1.dtype
     gdt = dout.dtype
+    ws1, _, ws2, _, S, Hs = _shared_parts(shared)
     dout = dout.contiguous()
     dx = torch.empty(n, d, dtype=gdt, device=dev)
     dwr = torch.empty(E, d, dtype=gdt, device=dev)
@@ -369,15 +382,22 @@ def moe_backward(dout: torch.Tensor, saved: torch.Tensor, w_router: torch.Tensor
     db1 = torch.empty(E, H, dtype=gdt, device=dev)
     dw2 = torch.empty(E, d, H, dtype=gdt, device=dev)
     db2 = torch.empty(E, d, dtype=gdt, device=dev)
-    nbytes = int(lib.agm_moe_backward_workspace_bytes(n, d, E, top_k, H, dtype_code(dtype)))
+    sg = None
+    if S:
+        sg = (torch.empty(S, Hs, d, dtype=gdt, device=dev), torch.empty(S, Hs, dtype=gdt, device=dev),
+              torch.empty(S, d, Hs, dtype=gdt, device=dev), torch.empty(S, d, dtype=gdt, device=dev))
+    nbytes = int(lib.agm_moe_backward_workspace_bytes(n, d, E, top_k, H, S, Hs, dtype_code(dtype)))
     ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
     rc = lib.agm_moe_backward(ptr(dout), dtype_code(gdt), dtype_code(dtype), n, d, E, top_k, H, ptr(w_router),
-                              ptr(w1), ptr(w2), ptr(saved), saved.numel(), ptr(dx), ptr(dwr), ptr(dw1), ptr(db1),
-                              ptr(dw2), ptr(db2), ptr(ws), ws.numel(), 0 if pdl else _lib.AGM_FLAG_NO_PDL,
-                              stream_handle(dev))
+                              ptr(w1), ptr(w2), S, Hs, ptr(ws1), ptr(ws2), ptr(saved), saved.numel(), ptr(dx),
+                              ptr(dwr), ptr(dw1), ptr(db1), ptr(dw2), ptr(db2),
+                              *(ptr(t) for t in (sg or (None, None, None, None))), ptr(ws), ws.numel(),
+                              0 if pdl else _lib.AGM_FLAG_NO_PDL, stream_handle(dev))
     check(rc, "agm_moe_backward")
     if check_errors:
         code = _lib.read_device_error(ws[:4].view(torch.int32))
         if code:
             raise _lib.MoEKernelError(f"device error word 0x{code:x} after agm_moe_backward")
+    if S:
+        return dx, dwr, dw1, db1, dw2, db2, sg
     return dx, dwr, dw1, db1, dw2, db2

@@ -289,21 +289,23 @@ AGM_API int agm_ep_forward(const void* x, int dtype, int64_t n_tokens, int d, in
  *     dout, dx and every weight/bias gradient are fp32; the weights passed are
  *     their 16-bit casts (agm_cast_f32); the gradients are the 16-bit values
  *     autograd computes for those casts, returned as fp32.
- * Shared experts are not part of these entry points. */
+ * Shared experts (n_shared >= 0, hidden shared_hidden; agillm41.py:4381-4387,
+ * 4429-4430) have the layouts of agm_moe_forward: ws1 [S, Hs, d], sb1 [S, Hs],
+ * ws2 [S, d, Hs], sb2 [S, d]; their gradients have the same shapes. */
 
 /* Bytes of the state agm_moe_forward_train keeps for agm_moe_backward. */
-AGM_API size_t agm_moe_train_saved_bytes(int64_t n_tokens, int d, int n_experts, int top_k, int hidden, int x_dtype,
-                                         int dtype);
+AGM_API size_t agm_moe_train_saved_bytes(int64_t n_tokens, int d, int n_experts, int top_k, int hidden, int n_shared,
+                                         int shared_hidden, int x_dtype, int dtype);
 /* Bytes of agm_moe_backward's scratch workspace. */
 AGM_API size_t agm_moe_backward_workspace_bytes(int64_t n_tokens, int d, int n_experts, int top_k, int hidden,
-                                                int dtype);
+                                                int n_shared, int shared_hidden, int dtype);
 /* fp32 -> bf16/fp16 cast of n values (autocast's casts of the input and of
  * the weights, agillm41.py:4399 and 4332-4336 under torch.autocast). */
 AGM_API int agm_cast_f32(const float* in, void* out, int dtype, int64_t n, void* stream);
 /* MoEFFN.forward in training mode (agillm41.py:4389-4431): the same result
  * as agm_moe_forward (x_dtype == dtype) or as the reference under autocast
  * (x_dtype == AGM_F32), keeping the router logits, routing, plan, permuted
- * input, FC1 activation and expert outputs in `saved`
+ * input, FC1 activations (and their ReLU masks) and expert outputs in `saved`
  * (agm_moe_train_saved_bytes) for agm_moe_backward. counts_out (nullable)
  * int32 [E]: rows routed to each expert (an expert with none gets no
  * gradient at all in the reference, which never calls it). The device error
@@ -311,20 +313,24 @@ AGM_API int agm_cast_f32(const float* in, void* out, int dtype, int64_t n, void*
  * flags: AGM_FLAG_TIE_LOW_FIRST, AGM_FLAG_NO_PAIR, AGM_FLAG_NO_PDL. */
 AGM_API int agm_moe_forward_train(const void* x, int x_dtype, int dtype, int64_t n_tokens, int d, int n_experts,
                                   int top_k, int hidden, const void* w_router, const void* w1, const void* b1,
-                                  const void* w2, const void* b2, void* out, void* saved, size_t saved_bytes,
-                                  int32_t* counts_out, int flags, void* stream);
+                                  const void* w2, const void* b2, int n_shared, int shared_hidden, const void* ws1,
+                                  const void* sb1, const void* ws2, const void* sb2, void* out, void* saved,
+                                  size_t saved_bytes, int32_t* counts_out, int flags, void* stream);
 /* Backward of agm_moe_forward_train. Replaces autograd through
- * agillm41.py:4398-4428 (router Linear, top-k/softmax gates or the top-1
+ * agillm41.py:4398-4430 (router Linear, top-k/softmax gates or the top-1
  * straight-through gate, index_select, expert Linear/ReLU/Linear, `* weight`,
- * index_add_): dout [n, d] (x_dtype) -> dx [n, d] (x_dtype),
- * dw_router [E, d], dw1 [E, H, d], db1 [E, H], dw2 [E, d, H], db2 [E, d]
- * (x_dtype; these are written, not accumulated). w_router/w1/w2 are the
- * compute-dtype weights the forward used; `saved` is unchanged. The device
- * error word is the first int of `workspace`. */
+ * index_add_, shared experts): dout [n, d] (x_dtype) -> dx [n, d] (x_dtype),
+ * dw_router [E, d], dw1 [E, H, d], db1 [E, H], dw2 [E, d, H], db2 [E, d] and
+ * the shared experts' dws1, dsb1, dws2, dsb2 (x_dtype; written, not
+ * accumulated). w_router/w1/w2/ws1/ws2 are the compute-dtype weights the
+ * forward used; `saved` is unchanged. The device error word is the first int
+ * of `workspace`. */
 AGM_API int agm_moe_backward(const void* dout, int x_dtype, int dtype, int64_t n_tokens, int d, int n_experts,
-                             int top_k, int hidden, const void* w_router, const void* w1, const void* w2,
-                             const void* saved, size_t saved_bytes, void* dx, void* dw_router, void* dw1, void* db1,
-                             void* dw2, void* db2, void* workspace, size_t workspace_bytes, int flags, void* stream);
+                             int top_k, int hidden, const void* w_router, const void* w1, const void* w2, int n_shared,
+                             int shared_hidden, const void* ws1, const void* ws2, const void* saved,
+                             size_t saved_bytes, void* dx, void* dw_router, void* dw1, void* db1, void* dw2, void* db2,
+                             void* dws1, void* dsb1, void* dws2, void* dsb2, void* workspace, size_t workspace_bytes,
+                             int flags, void* stream);
 
 /* Synchronise `stream`, read the device error word at `err` (e.g. the first
  * int of a forward workspace) into *code and reset it to 0. Returns AGM_OK if

@@ -49,6 +49,8 @@ GRAD_CASES = [
     ("grad_top1_bf16_n20", 64, 64, 4, 1, 20, 44, torch.bfloat16, 0, 0, 0.1, None, False),
     ("grad_top3_fp32_n16", 64, 96, 5, 3, 16, 45, torch.float32, 0, 0, 0.1, None, False),
     ("grad_empty_fp32_n16", 64, 64, 6, 2, 16, 46, torch.float32, 0, 0, 0.1, "empty", False),
+    ("grad_shared_top1_fp32_n20", 64, 64, 2, 1, 20, 47, torch.float32, 1, 128, 0.1, None, False),
+    ("grad_shared2_top2_bf16_n24", 64, 64, 4, 2, 24, 48, torch.bfloat16, 2, 64, 0.1, None, False),
 ]
 
 

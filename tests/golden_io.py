@@ -89,6 +89,12 @@ class GoldenGrad(Golden):
         self.d_w2 = from_np(z["d_w2"], self.dtype)
         self.d_b2 = from_np(z["d_b2"], self.dtype)
         self.expert_has_grad = [bool(v) for v in z["expert_has_grad"]]
+        self.shared_grads = {}
+        if self.shared:
+            for i, a, p in ((0, "w1", "weight"), (0, "b1", "bias"), (2, "w2", "weight"), (2, "b2", "bias")):
+                stack = from_np(z[f"d_s{i}{a}"], self.dtype)
+                for s in range(self.shared):
+                    self.shared_grads[f"shared.{s}.{i}.{p}"] = stack[s]
 
     def inputs_match(self):
         return super().inputs_match() and sha(self.dout) == str(self.z["dout_sha256"])
@@ -102,4 +108,5 @@ class GoldenGrad(Golden):
             g[f"experts.{e}.0.bias"] = self.d_b1[e]
             g[f"experts.{e}.2.weight"] = self.d_w2[e]
             g[f"experts.{e}.2.bias"] = self.d_b2[e]
+        g.update(self.shared_grads)
         return g

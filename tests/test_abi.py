@@ -101,23 +101,32 @@ def test_training_entry_points_validate_without_a_device():
     lib = _lib.load()
     fake = ctypes.c_void_p(4096)
     n, d, E, k, H = 1024, 64, 14, 2, 128
-    need = lib.agm_moe_train_saved_bytes(n, d, E, k, H, _lib.AGM_BF16, _lib.AGM_BF16)
+    need = lib.agm_moe_train_saved_bytes(n, d, E, k, H, 0, 1, _lib.AGM_BF16, _lib.AGM_BF16)
     rows = lib.agm_max_rows(n, k, E)
     assert need >= rows * (2 * d + H) * 2            # x_perm, y and h are kept
-    amp = lib.agm_moe_train_saved_bytes(n, d, E, k, H, _lib.AGM_F32, _lib.AGM_BF16)
+    amp = lib.agm_moe_train_saved_bytes(n, d, E, k, H, 0, 1, _lib.AGM_F32, _lib.AGM_BF16)
     assert amp >= need + n * d * 2                   # plus the 16-bit cast of x
-    assert lib.agm_moe_backward_workspace_bytes(n, d, E, k, H, _lib.AGM_BF16) >= rows * (d + H) * 2
+    shared = lib.agm_moe_train_saved_bytes(n, d, E, k, H, 1, 2 * d, _lib.AGM_BF16, _lib.AGM_BF16)
+    assert shared >= need + n * (d + 2 * d + d) * 2  # x copy, shared FC1 activation and output
+    assert lib.agm_moe_backward_workspace_bytes(n, d, E, k, H, 0, 1, _lib.AGM_BF16) >= rows * (d + H) * 2
+    fwd = [fake, _lib.AGM_BF16, _lib.AGM_BF16, n, d, E, k, H, fake, fake, fake, fake, fake, 0, 1, None, None, None,
+           None, fake, fake]
     # saved buffer too small
-    rc = lib.agm_moe_forward_train(fake, _lib.AGM_BF16, _lib.AGM_BF16, n, d, E, k, H, fake, fake, fake, fake, fake,
-                                   fake, fake, 1024, None, 0, None)
-    assert rc == -5 and "saved" in lib.agm_last_error().decode()
+    assert lib.agm_moe_forward_train(*fwd, 1024, None, 0, None) == -5
+    assert "saved" in lib.agm_last_error().decode()
     # fp16 input with bf16 weights is neither mode
-    rc = lib.agm_moe_forward_train(fake, _lib.AGM_F16, _lib.AGM_BF16, n, d, E, k, H, fake, fake, fake, fake, fake,
-                                   fake, fake, need, None, 0, None)
-    assert rc == -1 and "x_dtype" in lib.agm_last_error().decode()
+    bad = list(fwd)
+    bad[1] = _lib.AGM_F16
+    assert lib.agm_moe_forward_train(*bad, need, None, 0, None) == -1
+    assert "x_dtype" in lib.agm_last_error().decode()
+    # shared experts without their weights
+    sh = list(fwd)
+    sh[13], sh[14] = 1, 2 * d
+    assert lib.agm_moe_forward_train(*sh, shared, None, 0, None) == -1
     # backward: workspace too small
-    rc = lib.agm_moe_backward(fake, _lib.AGM_BF16, _lib.AGM_BF16, n, d, E, k, H, fake, fake, fake, fake, need, fake,
-                              fake, fake, fake, fake, fake, fake, 1024, 0, None)
+    rc = lib.agm_moe_backward(fake, _lib.AGM_BF16, _lib.AGM_BF16, n, d, E, k, H, fake, fake, fake, 0, 1, None, None,
+                              fake, need, fake, fake, fake, fake, fake, fake, None, None, None, None, fake, 1024, 0,
+                              None)
     assert rc == -5 and "workspace" in lib.agm_last_error().decode()
     assert lib.agm_cast_f32(fake, fake, _lib.AGM_F32, 16, None) == -1
 

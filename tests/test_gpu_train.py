@@ -56,9 +56,14 @@ def assert_grad_close(ours, ref, dtype, name):
 
 
 def make_module(sd, d, H, E, k, dtype):
-    m = agillm41_b200.MoEFFN(d, mlp_mult=max(1, H // d), experts=E, top_k=k)
+    S = reference_moe.num_shared_in(sd)
+    Hs = sd["shared.0.0.weight"].shape[0] if S else 0
+    m = agillm41_b200.MoEFFN(d, mlp_mult=max(1, H // d), experts=E, top_k=k, shared_experts=S,
+                             shared_mlp_mult=max(1, Hs // d) if S else 0)
     if H != m.mlp_mult * d:
         m.experts = nn.ModuleList([nn.Sequential(nn.Linear(d, H), nn.ReLU(), nn.Linear(H, d)) for _ in range(E)])
+    if S and m.shared[0][0].weight.shape[0] != Hs:
+        m.shared = nn.ModuleList([nn.Sequential(nn.Linear(d, Hs), nn.ReLU(), nn.Linear(Hs, d)) for _ in range(S)])
     m.load_state_dict({kk: v.float() for kk, v in sd.items()})
     m = m.to(device=DEV, dtype=dtype).train()
     m.check_device_errors = True
@@ -115,8 +120,9 @@ def compare(ours, ref, dtype, counts=None):
         assert_grad_close(o, r, dtype, key)
 
 
-def case(d, H, E, k, n, seed, bias_std=0.02):
-    sd = synthetic.make_state(d, H, E, seed, dtype=torch.float32, bias_std=bias_std)
+def case(d, H, E, k, n, seed, bias_std=0.02, shared=0, shared_hidden=None):
+    sd = synthetic.make_state(d, H, E, seed, dtype=torch.float32, bias_std=bias_std, shared=shared,
+                              shared_hidden=shared_hidden)
     x = synthetic.make_input(n, d, seed)
     g = torch.Generator().manual_seed(seed + 7)
     dout = torch.randn(n, d, generator=g)
@@ -272,11 +278,22 @@ def test_inference_under_autocast_matches_reference():
     assert_grad_close(y, yr, torch.bfloat16, "out")
 
 
-def test_cpu_input_and_shared_experts_are_refused():
-    m = agillm41_b200.MoEFFN(64, mlp_mult=2, experts=4, top_k=2, shared_experts=1).to(DEV).train()
-    x = torch.randn(8, 64, device=DEV, requires_grad=True)
-    with pytest.raises(agillm41_b200.MoEKernelError):
-        m(x)
+def test_shared_expert_production_shape_autocast():
+    """The production MoE of AGILLM4.1: 2 experts, top-1, one shared expert of
+    hidden 2d (agillm41.py:8590-8591), under autocast over fp32 weights."""
+    sd, x, dout = case(256, 1024, 2, 1, 512, 141, shared=1, shared_hidden=512)
+    ours, ref, counts = run_pair(sd, x, dout, 1, torch.float32, amp=torch.bfloat16)
+    compare(ours, ref, torch.bfloat16, counts)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_two_shared_experts_top2(dtype):
+    sd, x, dout = case(256, 512, 6, 2, 400, 151, shared=2, shared_hidden=256)
+    ours, ref, counts = run_pair(sd, x, dout, 2, dtype)
+    compare(ours, ref, dtype, counts)
+
+
+def test_cpu_input_is_refused():
     m2 = agillm41_b200.MoEFFN(64, mlp_mult=2, experts=4, top_k=2).train()
     with pytest.raises(agillm41_b200.MoEKernelError):
         m2(torch.randn(8, 64, requires_grad=True))
