@@ -298,29 +298,42 @@ def run_ours(args, world, rank, local):
     else:
         e2e_value = run_e2e(args, world, dev, sd, x, out, N, stream)
     decode = None if args.skip_decode else run_decode(args, dev, stream)
-    train = None if args.skip_train else run_train(args, dev, stream)
+    train = None
+    if not args.skip_train:
+        train = run_train(args, dev, stream)
+        # The reference's production MoE (agillm41.py:8590-8594: --moe_experts 2 --moe_top_k 1
+        # --moe_mlp_mult 4 --moe_shared_experts 1 --moe_shared_mlp_mult 2 --amp, batch 22 x 1536)
+        train["production"] = run_train(args, dev, stream, experts=2, hidden=4 * D, top_k=1, shared=1,
+                                        shared_hidden=2 * D, batch=22, seq=1536,
+                                        label="production MoE block training step")
     report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e_value, x, decode, train)
 
 
-def run_train(args, dev, stream):
+def run_train(args, dev, stream, *, experts=EXPERTS, hidden=HIDDEN, top_k=TOP_K, shared=0, shared_hidden=0,
+              batch=BATCH, seq=SEQ, label="MoE block training step"):
     """Training step of the MoE block as the reference trains it with --amp
     (torch.autocast bf16 over fp32 master weights, agillm41.py:3054-3066 and
     6793): the 16-bit casts of the fp32 weights (an optimiser step changes
     them every step), the forward that keeps its intermediates and the
-    backward to dx, the router weight and every expert weight and bias, on
-    the same B x L token workload (fp32 x and upstream gradient, seeded).
-    GEMM work per step: the two forward projections plus four backward ones
-    (dgrad and wgrad of FC1 and FC2), 3 x 32.768 MFLOP per token.
+    backward to dx, the router weight and every expert (and shared-expert)
+    weight and bias, on a B x L token workload (fp32 x and upstream gradient,
+    seeded). GEMM work per step: the forward projections plus their dgrad and
+    wgrad, 3 x 4 x d x (k H + S Hs) FLOP per token.
     """
     from agillm41_b200 import ops, synthetic
 
-    N = args.tokens
-    sd = synthetic.make_state(D, HIDDEN, EXPERTS, SEED, dtype=torch.float32, device=dev)
+    N = batch * seq if args.tokens == BATCH * SEQ else args.tokens
+    sd = synthetic.make_state(D, hidden, experts, SEED, dtype=torch.float32, device=dev, shared=shared,
+                              shared_hidden=shared_hidden or None)
     master = (sd["router.weight"].contiguous(),
-              torch.stack([sd[f"experts.{e}.0.weight"] for e in range(EXPERTS)]).contiguous(),
-              torch.stack([sd[f"experts.{e}.0.bias"] for e in range(EXPERTS)]).contiguous(),
-              torch.stack([sd[f"experts.{e}.2.weight"] for e in range(EXPERTS)]).contiguous(),
-              torch.stack([sd[f"experts.{e}.2.bias"] for e in range(EXPERTS)]).contiguous())
+              torch.stack([sd[f"experts.{e}.0.weight"] for e in range(experts)]).contiguous(),
+              torch.stack([sd[f"experts.{e}.0.bias"] for e in range(experts)]).contiguous(),
+              torch.stack([sd[f"experts.{e}.2.weight"] for e in range(experts)]).contiguous(),
+              torch.stack([sd[f"experts.{e}.2.bias"] for e in range(experts)]).contiguous())
+    smaster = None
+    if shared:
+        smaster = tuple(torch.stack([sd[f"shared.{s}.{i}.{p}"] for s in range(shared)]).contiguous()
+                        for i, p in ((0, "weight"), (0, "bias"), (2, "weight"), (2, "bias")))
     del sd
     x = synthetic.make_input(N, D, SEED, dtype=torch.float32, device=dev)
     g = torch.Generator(device="cpu").manual_seed(SEED + 7)
@@ -328,8 +341,9 @@ def run_train(args, dev, stream):
 
     def step(check=False):
         wc = [ops.cast_f32(t, torch.bfloat16) for t in master]
-        out, saved = ops.moe_forward_train(x, *wc, TOP_K, check_errors=check)
-        return ops.moe_backward(dout, saved, wc[0], wc[1], wc[3], TOP_K, check_errors=check)
+        sc = None if smaster is None else tuple(ops.cast_f32(t, torch.bfloat16) for t in smaster)
+        out, saved = ops.moe_forward_train(x, *wc, top_k, shared=sc, check_errors=check)
+        return ops.moe_backward(dout, saved, wc[0], wc[1], wc[3], top_k, shared=sc, check_errors=check)
 
     for i in range(max(3, args.warmup)):
         step(check=(i == 0))
@@ -343,20 +357,22 @@ def run_train(args, dev, stream):
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
     peaks = load_peaks()
-    flop = 3 * FLOP_PER_TOKEN * N
+    flop = 3 * 4 * D * (top_k * hidden + shared * shared_hidden) * N
     tf = flop / (ms / 1000.0) / 1e12
-    return {"workload": f"MoE block training step (forward + backward), B{BATCH} L{SEQ} ({N} tokens) d{D} E{EXPERTS} "
-                        f"H{HIDDEN} top{TOP_K}, autocast bf16 over fp32 master weights, seed {SEED}",
+    shared_txt = f" + {shared} shared H{shared_hidden}" if shared else ""
+    # launches: 5 (+4) weight casts; forward: x cast, router, plan, permute, FC1, FC2, 2 per shared
+    # expert, combine; backward: combine/routing, FC2 wgrad + dgrad, 2 x (column sums + reduce), FC1
+    # wgrad + dgrad, router wgrad + reduce, dx, and per shared expert 4 GEMMs + bias reduce (+ db2 once)
+    launches = 24 + (4 + 2 + 2 + 5 * shared if shared else 0)
+    return {"workload": f"{label} (forward + backward), B{batch} L{seq} ({N} tokens) d{D} E{experts} "
+                        f"H{hidden} top{top_k}{shared_txt}, autocast bf16 over fp32 master weights, seed {SEED}",
             "ms_per_step": round(ms, 4), "tokens_per_s": N / (ms / 1000.0), "steps": steps,
             "gemm_flop_per_step": flop,
             "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peaks["tf_sus"], "unit": "TFLOP/s",
                          "frac": round(tf / peaks["tf_sus"], 3),
-                         "note": "all six expert GEMMs' FLOPs over the whole step time (casts, router, permute, "
+                         "note": "all expert GEMMs' FLOPs over the whole step time (casts, router, permute, "
                                  "combine and their backward included), so a lower bound on the GEMMs' own rate"},
-            # 5 weight casts; forward: x cast, router, plan, permute, FC1, FC2, combine;
-            # backward: combine/routing, FC2 wgrad + dgrad, 2 x (column sums + reduce),
-            # FC1 wgrad + dgrad, router wgrad + reduce, dx
-            "gpu_launches_per_step": 24}
+            "gpu_launches_per_step": launches}
 
 
 def run_ep(args, world, rank, local):
