@@ -28,6 +28,7 @@ AGM_FLAG_KEEP_ERROR = 0x2
 AGM_FLAG_NO_PAIR = 0x4
 AGM_FLAG_NO_SWAP = 0x8
 AGM_FLAG_NO_PDL = 0x10
+AGM_FLAG_BWD_PAIR = 0x20
 AGM_SWAP_ROWS_PER_EXPERT = 32
 AGM_STAGE_EVENTS = 8
 AGM_EP_STAGE_EVENTS = 9

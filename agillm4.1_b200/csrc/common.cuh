@@ -398,6 +398,68 @@ __device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// Shared-memory descriptor of an MN-major operand tile (128-byte swizzle):
+// leading byte offset = distance between 64-element MN chunks, stride byte
+// offset = distance between 8-row K groups (1024 B).
+__device__ __forceinline__ uint64_t smem_desc_mn_sw128(uint32_t smem_addr, uint32_t chunk_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(chunk_bytes >> 4) << 16;
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(2u) << 61;
+  return d;
+}
+
+// Column sums of a warp's 32 x 64 chunk (lane = row): five exchange steps
+// halve the columns each lane holds (62 shuffles); lane L ends with the sums
+// of columns 2L and 2L + 1, added in a fixed tree order.
+__device__ __forceinline__ void warp_colsum64(const float (&v)[64], int lane, float& s0, float& s1) {
+  float a32[32], a16[16], a8[8], a4[4], a2[2];
+  {
+    const bool hi = lane & 16;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float send = hi ? v[i] : v[i + 32];
+      a32[i] = (hi ? v[i + 32] : v[i]) + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+  }
+  {
+    const bool hi = lane & 8;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float send = hi ? a32[i] : a32[i + 16];
+      a16[i] = (hi ? a32[i + 16] : a32[i]) + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+  }
+  {
+    const bool hi = lane & 4;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float send = hi ? a16[i] : a16[i + 8];
+      a8[i] = (hi ? a16[i + 8] : a16[i]) + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+  }
+  {
+    const bool hi = lane & 2;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float send = hi ? a8[i] : a8[i + 4];
+      a4[i] = (hi ? a8[i + 4] : a8[i]) + __shfl_xor_sync(0xffffffffu, send, 2);
+    }
+  }
+  {
+    const bool hi = lane & 1;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float send = hi ? a4[i] : a4[i + 2];
+      a2[i] = (hi ? a4[i + 2] : a4[i]) + __shfl_xor_sync(0xffffffffu, send, 1);
+    }
+  }
+  s0 = a2[0];
+  s1 = a2[1];
+}
+
 // Instruction descriptor, kind::f16: fp32 accumulator (bits 4-5 = 1), A and
 // B format (bits 7-9, 10-12: 0 = f16, 1 = bf16), both K-major (bits 15, 16 =
 // 0), N >> 3 at bits 17-22, M >> 4 at bits 24-28.

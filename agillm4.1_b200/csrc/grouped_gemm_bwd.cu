@@ -61,19 +61,6 @@ struct BwdCfg {
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STG_BYTES + 256 + 1024;
 };
 
-// Shared-memory descriptor of an MN-major operand tile (128-byte swizzle):
-// leading byte offset = distance between 64-element MN chunks, stride byte
-// offset = distance between 8-row K groups (1024 B).
-__device__ __forceinline__ uint64_t smem_desc_mn_sw128(uint32_t smem_addr, uint32_t chunk_bytes) {
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
-  d |= static_cast<uint64_t>(chunk_bytes >> 4) << 16;
-  d |= static_cast<uint64_t>(1024u >> 4) << 32;
-  d |= static_cast<uint64_t>(1u) << 46;
-  d |= static_cast<uint64_t>(2u) << 61;
-  return d;
-}
-
 __device__ __forceinline__ void dgrad_coords(int t, int num_m, int num_n, int& m_blk, int& n_blk) {
   const int span = kGroupM * num_n;
   const int g = t / span;
@@ -82,55 +69,6 @@ __device__ __forceinline__ void dgrad_coords(int t, int num_m, int num_n, int& m
   const int r = t - g * span;
   m_blk = first_m + r % gm;
   n_blk = r / gm;
-}
-
-// Column sums of a warp's 32 x 64 chunk (lane = row): five exchange steps
-// halve the columns each lane holds (62 shuffles); lane L ends with the sums
-// of columns 2L and 2L + 1, added in a fixed tree order.
-__device__ __forceinline__ void warp_colsum64(const float (&v)[64], int lane, float& s0, float& s1) {
-  float a32[32], a16[16], a8[8], a4[4], a2[2];
-  {
-    const bool hi = lane & 16;
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const float send = hi ? v[i] : v[i + 32];
-      a32[i] = (hi ? v[i + 32] : v[i]) + __shfl_xor_sync(0xffffffffu, send, 16);
-    }
-  }
-  {
-    const bool hi = lane & 8;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float send = hi ? a32[i] : a32[i + 16];
-      a16[i] = (hi ? a32[i + 16] : a32[i]) + __shfl_xor_sync(0xffffffffu, send, 8);
-    }
-  }
-  {
-    const bool hi = lane & 4;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float send = hi ? a16[i] : a16[i + 8];
-      a8[i] = (hi ? a16[i + 8] : a16[i]) + __shfl_xor_sync(0xffffffffu, send, 4);
-    }
-  }
-  {
-    const bool hi = lane & 2;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float send = hi ? a8[i] : a8[i + 4];
-      a4[i] = (hi ? a8[i + 4] : a8[i]) + __shfl_xor_sync(0xffffffffu, send, 2);
-    }
-  }
-  {
-    const bool hi = lane & 1;
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const float send = hi ? a4[i] : a4[i + 2];
-      a2[i] = (hi ? a4[i + 2] : a4[i]) + __shfl_xor_sync(0xffffffffu, send, 1);
-    }
-  }
-  s0 = a2[0];
-  s1 = a2[1];
 }
 
 // Work of one output tile.

@@ -195,6 +195,12 @@ cudaError_t grouped_gemm_dgrad(int dtype, const void* dc, int64_t rows, const vo
                                bool relu_mask, int num_sms, cudaStream_t stream);
 cudaError_t grouped_gemm_wgrad(int dtype, bool out_f32, const void* dc, const void* act, int64_t rows,
                                const BwdGemmArgs& args, int num_sms, cudaStream_t stream);
+// The same on CTA pairs (grouped_gemm_bwd_pair.cu, 16-bit dtypes): 256 x 256
+// tiles; dgrad needs row tiles 2i and 2i+1 in one group (256-row segments).
+cudaError_t grouped_gemm_dgrad_pair(int dtype, const void* dc, int64_t rows, const void* w, const BwdGemmArgs& args,
+                                    bool relu_mask, int num_sms, cudaStream_t stream);
+cudaError_t grouped_gemm_wgrad_pair(int dtype, bool out_f32, const void* dc, const void* act, int64_t rows,
+                                    const BwdGemmArgs& args, int num_sms, cudaStream_t stream);
 cudaError_t combine(int dtype, const void* y, const int32_t* row_of, const void* gates, int64_t n, int d, int k,
                     const void* shared_y, int n_shared, int64_t shared_stride, void* out, int num_sms,
                     cudaStream_t stream);

@@ -924,6 +924,26 @@ agm::GemmArgs dense_args(void* c, int64_t npad, int n_out, int k_in, const void*
   return g;
 }
 
+// Backward GEMMs: CTA pairs for 16-bit dtypes when there are enough 256 x 256
+// units for the 74 clusters (dgrad also needs 256-row segments), one CTA per
+// tile otherwise.
+cudaError_t wgrad_any(int dtype, bool amp, const void* dc, const void* act, int64_t rows,
+                      const agm::BwdGemmArgs& a, int sms, int pair_mode, cudaStream_t s) {
+  // pair_mode: 0 = one CTA per tile (AGM_FLAG_NO_PAIR), 1 = pairs when they
+  // fill the GPU, 2 = pairs always (AGM_FLAG_BWD_PAIR)
+  const int64_t units = static_cast<int64_t>(a.groups) * (((a.m + 127) / 128 + 1) / 2) * ((a.n + 255) / 256);
+  if (dtype != AGM_F32 && pair_mode > 0 && (pair_mode == 2 || units >= sms / 2))
+    return agm::grouped_gemm_wgrad_pair(dtype, amp, dc, act, rows, a, sms, s);
+  return agm::grouped_gemm_wgrad(dtype, amp, dc, act, rows, a, sms, s);
+}
+cudaError_t dgrad_any(int dtype, bool pair_rows, const void* dc, int64_t rows, const void* w,
+                      const agm::BwdGemmArgs& a, bool relu_mask, int sms, int pair_mode, cudaStream_t s) {
+  const int64_t units = ((static_cast<int64_t>(a.max_tiles) + 1) / 2) * ((a.n + 255) / 256);
+  if (dtype != AGM_F32 && pair_rows && pair_mode > 0 && (pair_mode == 2 || units >= sms / 2))
+    return agm::grouped_gemm_dgrad_pair(dtype, dc, rows, w, a, relu_mask, sms, s);
+  return agm::grouped_gemm_dgrad(dtype, dc, rows, w, a, relu_mask, sms, s);
+}
+
 const uint8_t* at(const void* p, size_t bytes) { return static_cast<const uint8_t*>(p) + bytes; }
 uint8_t* at(void* p, size_t bytes) { return static_cast<uint8_t*>(p) + bytes; }
 
@@ -1127,6 +1147,11 @@ int agm_moe_backward(const void* dout, int x_dtype, int dtype, int64_t n_tokens,
   const int64_t npad = agm::npad_of(n_tokens);
   const int sms = agm::sm_count();
   const int max_tiles = static_cast<int>(rows / AGM_TILE_M);
+  // The forward padded expert segments to 256 rows exactly when this holds
+  // (the caller passes the forward's AGM_FLAG_NO_PAIR here too).
+  const bool pair_rows = dtype != AGM_F32 && !(flags & AGM_FLAG_NO_PAIR) &&
+                         static_cast<int64_t>(top_k) * n_tokens >= AGM_PAIR_MIN_ROWS;
+  const int pair_mode = (flags & AGM_FLAG_NO_PAIR) ? 0 : (flags & AGM_FLAG_BWD_PAIR) ? 2 : 1;
 
   // Per-segment column sums (fp32 SIMT path, and db2) into out.
   auto colsum = [&](const void* m, int ncols, const int32_t* seg, int groups, void* out) -> cudaError_t {
@@ -1174,7 +1199,7 @@ int agm_moe_backward(const void* dout, int x_dtype, int dtype, int64_t n_tokens,
   w2a.groups = n_experts;
   w2a.seg_start = S.seg_start;
   w2a.err = B.err;
-  e = agm::grouped_gemm_wgrad(dtype, amp, B.dy, S.h, rows, w2a, sms, stream);
+  e = wgrad_any(dtype, amp, B.dy, S.h, rows, w2a, sms, pair_mode, stream);
   if (e != cudaSuccess) return agm::cuda_fail(e, "wgrad fc2");
   // 3. FC2 input gradient through the ReLU: dh = (dy @ W2[e]) * (h > 0)
   agm::BwdGemmArgs d2;
@@ -1196,7 +1221,7 @@ int agm_moe_backward(const void* dout, int x_dtype, int dtype, int64_t n_tokens,
     d2.col_part = B.dh_part;  // db1 partials from the epilogue
   }
   d2.err = B.err;
-  e = agm::grouped_gemm_dgrad(dtype, B.dy, rows, w2, d2, true, sms, stream);
+  e = dgrad_any(dtype, pair_rows, B.dy, rows, w2, d2, true, sms, pair_mode, stream);
   if (e != cudaSuccess) return agm::cuda_fail(e, "dgrad fc2");
   // 4. bias gradients (dy is still intact: dgrad wrote dh)
   e = colsum(B.dy, d, S.seg_start, n_experts, db2);
@@ -1209,7 +1234,7 @@ int agm_moe_backward(const void* dout, int x_dtype, int dtype, int64_t n_tokens,
   w1a.c = dw1;
   w1a.m = hidden;
   w1a.n = d;
-  e = agm::grouped_gemm_wgrad(dtype, amp, B.dh, S.x_perm, rows, w1a, sms, stream);
+  e = wgrad_any(dtype, amp, B.dh, S.x_perm, rows, w1a, sms, pair_mode, stream);
   if (e != cudaSuccess) return agm::cuda_fail(e, "wgrad fc1");
   // 6. FC1 input gradient: dx_perm = dh @ W1[e], into dy's buffer
   agm::BwdGemmArgs d1 = d2;
@@ -1220,7 +1245,7 @@ int agm_moe_backward(const void* dout, int x_dtype, int dtype, int64_t n_tokens,
   d1.aux = nullptr;
   d1.aux_bits = nullptr;
   d1.col_part = nullptr;
-  e = agm::grouped_gemm_dgrad(dtype, B.dh, rows, w1, d1, false, sms, stream);
+  e = dgrad_any(dtype, pair_rows, B.dh, rows, w1, d1, false, sms, pair_mode, stream);
   if (e != cudaSuccess) return agm::cuda_fail(e, "dgrad fc1");
 
   // 7. shared experts: one dense segment of npad rows each, gradient ds
@@ -1242,7 +1267,7 @@ int agm_moe_backward(const void* dout, int x_dtype, int dtype, int64_t n_tokens,
     sw2.groups = 1;
     sw2.seg_start = B.dense_seg;
     sw2.err = B.err;
-    e = agm::grouped_gemm_wgrad(dtype, amp, B.ds, hs, npad, sw2, sms, stream);
+    e = wgrad_any(dtype, amp, B.ds, hs, npad, sw2, sms, pair_mode, stream);
     if (e != cudaSuccess) return agm::cuda_fail(e, "shared wgrad fc2");
     agm::BwdGemmArgs sd2;
     sd2.c = B.dh_sh;
@@ -1261,8 +1286,8 @@ int agm_moe_backward(const void* dout, int x_dtype, int dtype, int64_t n_tokens,
       sd2.col_part = B.dhs_part;
     }
     sd2.err = B.err;
-    e = agm::grouped_gemm_dgrad(dtype, B.ds, npad, at(ws2, static_cast<size_t>(eb) * s * d * Hs), sd2, true, sms,
-                                stream);
+    e = dgrad_any(dtype, true, B.ds, npad, at(ws2, static_cast<size_t>(eb) * s * d * Hs), sd2, true, sms, pair_mode,
+                  stream);
     if (e != cudaSuccess) return agm::cuda_fail(e, "shared dgrad fc2");
     void* db1s = at(dsb1, static_cast<size_t>(xs) * s * Hs);
     e = dtype == AGM_F32 ? colsum(B.dh_sh, Hs, B.dense_seg, 1, db1s) : tile_parts(B.dhs_part, B.dense_seg, 1, Hs, db1s);
@@ -1271,7 +1296,7 @@ int agm_moe_backward(const void* dout, int x_dtype, int dtype, int64_t n_tokens,
     sw1.c = at(dws1, static_cast<size_t>(xs) * s * Hs * d);
     sw1.m = Hs;
     sw1.n = d;
-    e = agm::grouped_gemm_wgrad(dtype, amp, B.dh_sh, S.xb, npad, sw1, sms, stream);
+    e = wgrad_any(dtype, amp, B.dh_sh, S.xb, npad, sw1, sms, pair_mode, stream);
     if (e != cudaSuccess) return agm::cuda_fail(e, "shared wgrad fc1");
     agm::BwdGemmArgs sd1 = sd2;
     sd1.c = at(B.dx_sh, static_cast<size_t>(eb) * s * npad * d);
@@ -1281,8 +1306,8 @@ int agm_moe_backward(const void* dout, int x_dtype, int dtype, int64_t n_tokens,
     sd1.aux = nullptr;
     sd1.aux_bits = nullptr;
     sd1.col_part = nullptr;
-    e = agm::grouped_gemm_dgrad(dtype, B.dh_sh, npad, at(ws1, static_cast<size_t>(eb) * s * Hs * d), sd1, false,
-                                sms, stream);
+    e = dgrad_any(dtype, true, B.dh_sh, npad, at(ws1, static_cast<size_t>(eb) * s * Hs * d), sd1, false, sms,
+                  pair_mode, stream);
     if (e != cudaSuccess) return agm::cuda_fail(e, "shared dgrad fc1");
   }
 

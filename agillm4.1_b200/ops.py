@@ -361,12 +361,14 @@ def moe_forward_train(x: torch.Tensor, w_router: torch.Tensor, w1: torch.Tensor,
 
 
 def moe_backward(dout: torch.Tensor, saved: torch.Tensor, w_router: torch.Tensor, w1: torch.Tensor,
-                 w2: torch.Tensor, top_k: int, *, shared: Optional[tuple] = None, pdl: bool = True,
-                 check_errors: bool = False):
+                 w2: torch.Tensor, top_k: int, *, shared: Optional[tuple] = None, pair: bool = True,
+                 pair_always: bool = False, pdl: bool = True, check_errors: bool = False):
     """Backward of :func:`moe_forward_train`: dout [N, d] (x's dtype) ->
     (dx, dw_router [E, d], dw1 [E, H, d], db1 [E, H], dw2 [E, d, H], db2 [E, d])
-    plus, with ``shared`` (the forward's (ws1, sb1, ws2, sb2)), a fourth-level
-    tuple (dws1, dsb1, dws2, dsb2); all in x's dtype (fp32 under autocast)."""
+    plus, with ``shared`` (the forward's (ws1, sb1, ws2, sb2)), a seventh item
+    (dws1, dsb1, dws2, dsb2); all in x's dtype (fp32 under autocast).
+    ``pair`` must be the value the forward was called with; ``pair_always``
+    runs the GEMMs on CTA pairs wherever they apply, whatever the size."""
     lib = load()
     n, d = dout.shape
     E = w_router.shape[0]
@@ -392,7 +394,8 @@ def moe_backward(dout: torch.Tensor, saved: torch.Tensor, w_router: torch.Tensor
                               ptr(w1), ptr(w2), S, Hs, ptr(ws1), ptr(ws2), ptr(saved), saved.numel(), ptr(dx),
                               ptr(dwr), ptr(dw1), ptr(db1), ptr(dw2), ptr(db2),
                               *(ptr(t) for t in (sg or (None, None, None, None))), ptr(ws), ws.numel(),
-                              0 if pdl else _lib.AGM_FLAG_NO_PDL, stream_handle(dev))
+                              (0 if pdl else _lib.AGM_FLAG_NO_PDL) | (0 if pair else _lib.AGM_FLAG_NO_PAIR)
+                              | (_lib.AGM_FLAG_BWD_PAIR if pair_always else 0), stream_handle(dev))
     check(rc, "agm_moe_backward")
     if check_errors:
         code = _lib.read_device_error(ws[:4].view(torch.int32))

@@ -78,6 +78,8 @@ enum {
 #define AGM_FLAG_NO_SWAP 0x8       /* agm_moe_forward: row-tile GEMMs even for small batches */
 #define AGM_FLAG_NO_PDL 0x10       /* agm_moe_forward: launch each kernel after the previous one
                                       completes (default: programmatic dependent launch) */
+#define AGM_FLAG_BWD_PAIR 0x20     /* agm_moe_backward: CTA-pair GEMMs wherever they apply, also for
+                                      problems too small to fill the GPU with pair tiles */
 
 AGM_API const char* agm_last_error(void);
 AGM_API int agm_abi_version(void);

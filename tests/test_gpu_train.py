@@ -214,6 +214,44 @@ def test_fp32_gradients_match_reference_golden(name):
         assert_grad_close(p.grad.cpu(), ref[key], torch.float32, key)
 
 
+def _ops_grads(sd, x, dout, k, amp, fwd_pair, bwd_pair, bwd_always):
+    E = sd["router.weight"].shape[0]
+    compute = torch.bfloat16
+    sdc = {kk: v.to(DEV, compute) for kk, v in sd.items()}
+    w1, b1, w2, b2, shared = packed(sdc, E, DEV)
+    wr = sdc["router.weight"].contiguous()
+    xin = x.to(DEV, torch.float32 if amp else compute).contiguous()
+    gout = dout.to(DEV, xin.dtype).contiguous()
+    out, saved = ops.moe_forward_train(xin, wr, w1, b1, w2, b2, k, shared=shared, pair=fwd_pair, check_errors=True)
+    res = ops.moe_backward(gout, saved, wr, w1, w2, k, shared=shared, pair=bwd_pair, pair_always=bwd_always,
+                           check_errors=True)
+    flat = [out] + list(res[:6]) + (list(res[6]) if shared is not None else [])
+    return flat
+
+
+@pytest.mark.parametrize("shape", ["full_width_8192", "ragged_shared"])
+@pytest.mark.parametrize("amp", [False, True])
+def test_cta_pair_backward_matches_one_cta(shape, amp):
+    """The CTA-pair backward GEMMs (256 x 256 tiles on two SMs) give the same
+    bits as the one-CTA kernels: odd row-tile counts, a ragged last column
+    tile, experts without rows and a shared expert included."""
+    if shape == "full_width_8192":
+        sd, x, dout = case(1280, 3200, 14, 2, 8192, 161)
+        k = 2
+    else:
+        d, H, E, k, n = 256, 320, 6, 2, 300
+        sd = synthetic.make_state(d, H, E, 162, dtype=torch.float32, bias_std=0.05, shared=1, shared_hidden=192)
+        w = sd["router.weight"]
+        for e in range(E):
+            w[e] = -w[e].abs() - 0.05 if e in (1, 4) else w[e].abs() + 0.01
+        x = synthetic.make_input(n, d, 162).abs() + 0.01
+        dout = torch.randn(n, d, generator=torch.Generator().manual_seed(163))
+    one_cta = _ops_grads(sd, x, dout, k, amp, fwd_pair=False, bwd_pair=False, bwd_always=False)
+    pairs = _ops_grads(sd, x, dout, k, amp, fwd_pair=True, bwd_pair=True, bwd_always=True)
+    for i, (a, b) in enumerate(zip(one_cta, pairs)):
+        assert torch.equal(a, b), f"output {i} differs"
+
+
 def test_backward_is_deterministic():
     sd, x, dout = case(256, 512, 14, 2, 700, 101)
     grads = []
