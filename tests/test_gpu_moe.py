@@ -199,7 +199,7 @@ def test_module_production_shape_top1_shared():
                       torch.bfloat16)
 
 
-@pytest.mark.parametrize("n,chunk", [(5000, 1024), (4096, 4096), (3000, 8192), (777, 100)])
+@pytest.mark.parametrize("n,chunk", [(5000, 1024), (4096, 4096), (3000, 8192), (777, 100), (40000, 8192)])
 def test_host_pipeline_bit_identical(n, chunk):
     """agm_moe_forward_host (host buffers, chunked, copies overlapped with the
     forward) gives exactly the device forward's result."""
