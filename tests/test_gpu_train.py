@@ -335,3 +335,24 @@ def test_cpu_input_is_refused():
     m2 = agillm41_b200.MoEFFN(64, mlp_mult=2, experts=4, top_k=2).train()
     with pytest.raises(agillm41_b200.MoEKernelError):
         m2(torch.randn(8, 64, requires_grad=True))
+
+
+def test_top5_generic_width():
+    """top_k above 4 takes the kernels' generic (16-wide) variant."""
+    sd, x, dout = case(128, 256, 8, 5, 160, 171, bias_std=0.1)
+    ours, ref, counts = run_pair(sd, x, dout, 5, torch.bfloat16)
+    compare(ours, ref, torch.bfloat16, counts)
+
+
+def test_autocast_fp16():
+    sd, x, dout = case(256, 512, 14, 2, 512, 181)
+    ours, ref, counts = run_pair(sd, x, dout, 2, torch.float32, amp=torch.float16)
+    compare(ours, ref, torch.float16, counts)
+
+
+def test_full_size_bench_workload_autocast():
+    """The bench's 73,728-token workload (B=48 x L=1536, d=1280, H=3200,
+    14 experts, top-2) under autocast: CTA-pair GEMMs forward and backward."""
+    sd, x, dout = case(1280, 3200, 14, 2, 73728, 191)
+    ours, ref, counts = run_pair(sd, x, dout, 2, torch.float32, amp=torch.bfloat16)
+    compare(ours, ref, torch.bfloat16, counts)
