@@ -17,7 +17,8 @@
 The forward calls the fused C-ABI entry point ``agm_moe_forward`` (router ->
 dispatch plan -> permute -> grouped FC1/FC2 -> combine) on the current CUDA
 stream with no host synchronisation. It refuses CPU tensors (there is no CPU
-fallback).
+fallback). With ``set_expert_stream(True)`` the routed experts stay on the host
+and only the active ones are copied in for each call.
 
 Training: when autograd needs gradients, the forward runs
 ``agm_moe_forward_train`` inside an autograd node whose backward is
@@ -204,6 +205,93 @@ class _B200Forward:
         self._b200_cast = (key, (cast, csh))
         return cast, csh
 
+    # ---- expert streaming (agillm41.py:4367-4379, 7656-7668) ----
+    def _host_expert_pack(self, dtype: torch.dtype):
+        """The routed experts' weights (on the host, as the reference's block
+        streaming leaves them) packed into page-locked [E, ...] tensors, made
+        again whenever a parameter changes (pointer or version)."""
+        experts = list(self.experts)
+        params = [p for ex in experts for p in (ex[0].weight, ex[0].bias, ex[2].weight, ex[2].bias)]
+        key = (dtype,) + tuple((p.data_ptr(), p._version, p.device) for p in params)
+        cache = getattr(self, "_b200_host_pack", None)
+        if cache is not None and cache[0] == key:
+            return cache[1]
+        with torch.no_grad():
+            pack = []
+            for i, attr in ((0, "weight"), (0, "bias"), (2, "weight"), (2, "bias")):
+                t = torch.stack([getattr(ex[i], attr).detach().to("cpu", dtype) for ex in experts])
+                pack.append(t.contiguous().pin_memory())
+        self._b200_host_pack = (key, tuple(pack))
+        return tuple(pack)
+
+    def _forward_expert_stream(self, flat: torch.Tensor) -> torch.Tensor:
+        """MoEFFN.forward with the routed experts resident on the host
+        (`set_expert_stream(True)`, agillm41.py:4362-4379): route on the GPU,
+        read the per-expert row counts, copy only the active experts' weights
+        to the GPU (page-locked, on a side stream while the rows are permuted)
+        and run the same kernels. Each active expert is copied once, where the
+        reference copies it once per (rank, expert) call. The output equals the
+        device-resident forward's bit for bit; `expert_stream_stats` counts
+        loads and tokens as the reference does (one load per (rank, expert)
+        call with rows, its rows as tokens)."""
+        if torch.is_grad_enabled() and (flat.requires_grad or any(p.requires_grad for p in self.parameters())):
+            raise MoEKernelError("expert_stream (host-resident experts) runs the inference forward only; call it "
+                                 "under torch.no_grad()")
+        wr = self.router.weight
+        if not wr.is_cuda or wr.device != flat.device:
+            raise MoEKernelError("expert_stream: the router weight must be on the input's GPU")
+        if flat.dtype != wr.dtype:
+            raise MoEKernelError(f"input dtype {flat.dtype} differs from the router weight dtype {wr.dtype}")
+        dev, dt = flat.device, flat.dtype
+        flat = flat.contiguous()
+        n, d = flat.shape
+        E, k = self.num_experts, self.top_k
+        w1h, b1h, w2h, b2h = self._host_expert_pack(dt)
+        H = w1h.shape[1]
+        with torch.no_grad():
+            wrc = wr.detach().contiguous()
+            idx, gates, hist, _ = ops.router_topk(flat, wrc, k)
+            plan = ops.dispatch_plan(hist, n, k)
+            per_rank = torch.stack([torch.bincount(idx[:, r].long(), minlength=E) for r in range(k)])
+            per_rank = per_rank.cpu()                    # the one host synchronisation
+            active = [e for e in range(E) if int(per_rank[:, e].sum()) > 0]
+            st = self.expert_stream_stats
+            st["loads"] = int(st.get("loads", 0)) + int((per_rank > 0).sum())
+            st["tokens"] = int(st.get("tokens", 0)) + int(per_rank.sum())
+            cur = torch.cuda.current_stream(dev)
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(cur)
+            w1 = torch.empty(E, H, d, dtype=dt, device=dev)
+            b1 = torch.empty(E, H, dtype=dt, device=dev)
+            w2 = torch.empty(E, d, H, dtype=dt, device=dev)
+            b2 = torch.empty(E, d, dtype=dt, device=dev)
+            with torch.cuda.stream(side):
+                for e in active:
+                    for dst, src in ((w1, w1h), (b1, b1h), (w2, w2h), (b2, b2h)):
+                        dst[e].copy_(src[e], non_blocking=True)
+            x_perm, row_of = ops.permute(flat, idx, plan, E)
+            cur.wait_stream(side)
+            for t in (w1, b1, w2, b2):
+                t.record_stream(side)
+            max_tiles = plan["tile_expert"].numel()
+            h = ops.grouped_gemm(x_perm, w1, b1, relu=True, tile_group=plan["tile_expert"],
+                                 num_tiles=plan["num_tiles"], max_tiles=max_tiles)
+            y = ops.grouped_gemm(h, w2, b2, relu=False, tile_group=plan["tile_expert"], num_tiles=plan["num_tiles"],
+                                 max_tiles=max_tiles)
+            shared_y = None
+            if getattr(self, "shared", None) is not None:
+                outs = [ops.grouped_gemm(ops.grouped_gemm(flat, ex[0].weight.detach().contiguous(),
+                                                          ex[0].bias.detach().contiguous(), relu=True),
+                                         ex[2].weight.detach().contiguous(), ex[2].bias.detach().contiguous(),
+                                         relu=False)
+                        for ex in self.shared]
+                shared_y = torch.stack(outs)
+            out = ops.combine(y, row_of, gates, shared_y)
+            del w1, b1, w2, b2, h, y, x_perm
+        if self.expert_stream_empty_cache:
+            torch.cuda.empty_cache()
+        return out
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:  # agillm41.py:4389-4431
         orig_shape = x.shape
         flat = x.reshape(-1, orig_shape[-1])
@@ -213,7 +301,7 @@ class _B200Forward:
         if not flat.is_cuda:
             raise MoEKernelError("MoEFFN (B200) runs on CUDA tensors only; there is no CPU path")
         if self.expert_stream:
-            raise MoEKernelError("expert_stream (CPU-resident experts) is not supported by the B200 forward")
+            return self._forward_expert_stream(flat).reshape(orig_shape)
         wr = self.router.weight
         amp = _autocast_dtype(flat.device)
         amp_mode = amp is not None and wr.dtype == torch.float32

@@ -312,3 +312,34 @@ def test_programmatic_launch_matches_serialised(n):
     torch.cuda.synchronize()
     for a, b in zip(outs, serial):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("k,E,S", [(2, 14, 0), (1, 2, 1)])
+def test_expert_stream_matches_resident(k, E, S):
+    """set_expert_stream(True) with the routed experts on the host, as the
+    reference's block streaming leaves them (agillm41.py:7656-7668): the
+    output equals the device-resident forward bit for bit, and the load and
+    token counters follow the reference (one load per (rank, expert) call
+    with rows)."""
+    d, H, n = 256, 512, 300
+    m = agillm41_b200.MoEFFN(d, mlp_mult=2, experts=E, top_k=k, shared_experts=S, shared_mlp_mult=2 if S else 0)
+    m.load_state_dict(reference_moe.make_state(d, H, E, 27, bias_std=0.02, shared=S, shared_hidden=2 * d if S else None))
+    m = m.to(device=DEV, dtype=torch.bfloat16).eval()
+    x = reference_moe.make_input(n, d, 27, dtype=torch.bfloat16, device=DEV).reshape(3, 100, d)
+    with torch.no_grad():
+        ref = m(x)
+        idx, _, _, _ = ops.router_topk(x.reshape(n, d), m.router.weight.detach().contiguous(), k)
+    for ex in m.experts:
+        ex.to("cpu")
+    m.set_expert_stream(True)
+    m.expert_stream_stats = {"loads": 0, "tokens": 0}
+    with torch.no_grad():
+        out = m(x)
+        out2 = m(x)
+    assert torch.equal(out, ref) and torch.equal(out2, ref)
+    loads = sum(int((torch.bincount(idx[:, r].long(), minlength=E) > 0).sum()) for r in range(k))
+    assert m.expert_stream_stats == {"loads": 2 * loads, "tokens": 2 * k * n}
+    assert all(p.device.type == "cpu" for ex in m.experts for p in ex.parameters())
+    with pytest.raises(agillm41_b200.MoEKernelError):
+        m.train()
+        m(x.requires_grad_(True))
