@@ -74,7 +74,9 @@ SIGNATURES = {
     "agm_moe_backward_workspace_bytes": (_SZ, [_I64, _I, _I, _I, _I, _I, _I, _I]),
     "agm_cast_f32": (_I, [_P, _P, _I, _I64, _P]),
     "agm_moe_forward_train": (_I, [_P, _I, _I, _I64, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _P,
-                                   _P, _P, _SZ, _P, _I, _P]),
+                                   _P, _P, _P, _SZ, _P, _I, _P]),
+    "agm_moe_forward_residual": (_I, [_P, _P, _I, _I64, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _P,
+                                      _P, _P, _SZ, _I, _P]),
     "agm_moe_backward": (_I, [_P, _I, _I, _I64, _I, _I, _I, _I, _P, _P, _P, _I, _I, _P, _P, _P, _SZ,
                               _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _I, _P]),
 }

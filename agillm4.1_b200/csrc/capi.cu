@@ -276,7 +276,8 @@ int agm_combine(const void* y_perm, const int32_t* row_of, const void* gates, in
   if (!aligned16(y_perm) || !aligned16(out) || (shared_y && !aligned16(shared_y)))
     return fail(AGM_ERR_ARG, "y_perm, shared_y and out must be 16-byte aligned");
   cudaError_t e = agm::combine(dtype, y_perm, row_of, gates, n_tokens, d, top_k, shared_y, n_shared,
-                               shared_stride_rows * d, out, num_sms_current(), static_cast<cudaStream_t>(stream));
+                               shared_stride_rows * d, nullptr, out, num_sms_current(),
+                               static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? AGM_OK : cuda_fail(e, "combine");
 }
 
@@ -288,12 +289,18 @@ size_t agm_moe_workspace_bytes(int64_t n_tokens, int d, int n_experts, int top_k
       .bytes;
 }
 
-int agm_moe_forward(const void* x, int dtype, int64_t n_tokens, int d, int n_experts, int top_k, int hidden,
-                    const void* w_router, const void* w1, const void* b1, const void* w2, const void* b2, int n_shared,
-                    int shared_hidden, const void* ws1, const void* sb1, const void* ws2, const void* sb2, void* out,
-                    void* workspace, size_t workspace_bytes, int flags, int32_t* idx_out, void* gates_out,
-                    int32_t* counts_out, float* logits_out, const float* logits_in, void* const* stage_events,
-                    void* stream_) {
+}  // extern "C"
+
+namespace {
+
+// agm_moe_forward with an optional residual added in the combine.
+int moe_forward_impl(const void* x, int dtype, int64_t n_tokens, int d, int n_experts, int top_k, int hidden,
+                     const void* w_router, const void* w1, const void* b1, const void* w2, const void* b2,
+                     int n_shared, int shared_hidden, const void* ws1, const void* sb1, const void* ws2,
+                     const void* sb2, const void* residual, void* out, void* workspace, size_t workspace_bytes,
+                     int flags, int32_t* idx_out, void* gates_out, int32_t* counts_out, float* logits_out,
+                     const float* logits_in, void* const* stage_events, void* stream_) {
+  if (residual && !aligned16(residual)) return fail(AGM_ERR_ARG, "residual must be 16-byte aligned");
   int rc = check_common(dtype, d, n_experts, top_k);
   if (rc) return rc;
   const int eb = elem_bytes(dtype);
@@ -423,8 +430,8 @@ int agm_moe_forward(const void* x, int dtype, int64_t n_tokens, int d, int n_exp
   }
   if ((e = mark(6)) != cudaSuccess) return cuda_fail(e, "event record");
 
-  e = agm::combine(dtype, L.x_perm, L.row_of, gates, n_tokens, d, top_k, L.y_sh, n_shared, npad * d, out, sms,
-                   stream);
+  e = agm::combine(dtype, L.x_perm, L.row_of, gates, n_tokens, d, top_k, L.y_sh, n_shared, npad * d, residual, out,
+                   sms, stream);
   if (e != cudaSuccess) return cuda_fail(e, "combine");
   if ((e = mark(7)) != cudaSuccess) return cuda_fail(e, "event record");
   if (counts_out) {
@@ -432,6 +439,32 @@ int agm_moe_forward(const void* x, int dtype, int64_t n_tokens, int d, int n_exp
     if (e != cudaSuccess) return cuda_fail(e, "counts copy");
   }
   return AGM_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int agm_moe_forward(const void* x, int dtype, int64_t n_tokens, int d, int n_experts, int top_k, int hidden,
+                    const void* w_router, const void* w1, const void* b1, const void* w2, const void* b2, int n_shared,
+                    int shared_hidden, const void* ws1, const void* sb1, const void* ws2, const void* sb2, void* out,
+                    void* workspace, size_t workspace_bytes, int flags, int32_t* idx_out, void* gates_out,
+                    int32_t* counts_out, float* logits_out, const float* logits_in, void* const* stage_events,
+                    void* stream) {
+  return moe_forward_impl(x, dtype, n_tokens, d, n_experts, top_k, hidden, w_router, w1, b1, w2, b2, n_shared,
+                          shared_hidden, ws1, sb1, ws2, sb2, nullptr, out, workspace, workspace_bytes, flags, idx_out,
+                          gates_out, counts_out, logits_out, logits_in, stage_events, stream);
+}
+
+int agm_moe_forward_residual(const void* x, const void* residual, int dtype, int64_t n_tokens, int d, int n_experts,
+                             int top_k, int hidden, const void* w_router, const void* w1, const void* b1,
+                             const void* w2, const void* b2, int n_shared, int shared_hidden, const void* ws1,
+                             const void* sb1, const void* ws2, const void* sb2, void* out, void* workspace,
+                             size_t workspace_bytes, int flags, void* stream) {
+  if (!residual) return fail(AGM_ERR_ARG, "null residual");
+  return moe_forward_impl(x, dtype, n_tokens, d, n_experts, top_k, hidden, w_router, w1, b1, w2, b2, n_shared,
+                          shared_hidden, ws1, sb1, ws2, sb2, residual, out, workspace, workspace_bytes, flags, nullptr,
+                          nullptr, nullptr, nullptr, nullptr, nullptr, stream);
 }
 
 int agm_read_device_error(int* err, int* code, void* stream) {

@@ -69,7 +69,8 @@ template <> struct Pair<__half> {
 template <typename T, int K_MAX>
 __device__ __forceinline__ uint4 combine_chunk16(const uint4 (&v)[K_MAX], const float (&g)[K_MAX], int k,
                                                  const T* __restrict__ shared_y, int n_shared,
-                                                 int64_t shared_stride, int64_t tok, int d, int c) {
+                                                 int64_t shared_stride, const T* __restrict__ residual, int64_t tok,
+                                                 int d, int c) {
   using P = Pair<T>;
   using V = typename P::V;
   V acc[4] = {P::zero(), P::zero(), P::zero(), P::zero()};
@@ -93,6 +94,12 @@ __device__ __forceinline__ uint4 combine_chunk16(const uint4 (&v)[K_MAX], const 
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[j] = P::add(acc[j], s[j]);
   }
+  if (residual) {  // Block: x + ff(ln2(x)), agillm41.py:4547
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(residual + tok * d) + c);
+    const V* f = reinterpret_cast<const V*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[j] = P::add(f[j], acc[j]);
+  }
   uint4 o;
   o.x = *reinterpret_cast<uint32_t*>(&acc[0]);
   o.y = *reinterpret_cast<uint32_t*>(&acc[1]);
@@ -104,9 +111,10 @@ __device__ __forceinline__ uint4 combine_chunk16(const uint4 (&v)[K_MAX], const 
 template <typename T, int K_MAX>
 __device__ __forceinline__ uint4 combine_chunk(const uint4 (&v)[K_MAX], const float (&g)[K_MAX], int k,
                                                const T* __restrict__ shared_y, int n_shared,
-                                               int64_t shared_stride, int64_t tok, int d, int c) {
+                                               int64_t shared_stride, const T* __restrict__ residual, int64_t tok,
+                                               int d, int c) {
   if constexpr (sizeof(T) == 2) {
-    return combine_chunk16<T, K_MAX>(v, g, k, shared_y, n_shared, shared_stride, tok, d, c);
+    return combine_chunk16<T, K_MAX>(v, g, k, shared_y, n_shared, shared_stride, residual, tok, d, c);
   }
   constexpr int CH = 16 / sizeof(T);
   float acc[8];
@@ -132,6 +140,12 @@ __device__ __forceinline__ uint4 combine_chunk(const uint4 (&v)[K_MAX], const fl
     }
 #pragma unroll
     for (int j = 0; j < CH; ++j) acc[j] = round_to<T>(__fadd_rn(acc[j], s[j]));
+  }
+  if (residual) {
+    float f[8];
+    load8<T>(__ldg(reinterpret_cast<const uint4*>(residual + tok * d) + c), f);
+#pragma unroll
+    for (int j = 0; j < CH; ++j) acc[j] = round_to<T>(__fadd_rn(f[j], acc[j]));
   }
   return store8<T>(acc);
 }
@@ -162,7 +176,8 @@ template <typename T, int K_MAX, class Src>
 __global__ void __launch_bounds__(256) combine_kernel(Src ysrc, const int32_t* __restrict__ row_of,
                                                       const T* __restrict__ gates, int64_t n_tokens, int d, int k,
                                                       const T* __restrict__ shared_y, int n_shared,
-                                                      int64_t shared_stride, T* __restrict__ out) {
+                                                      int64_t shared_stride, const T* __restrict__ residual,
+                                                      T* __restrict__ out) {
   constexpr int CH = 16 / sizeof(T);
   const int nchunk = d / CH;
   const int lane = lane_id();
@@ -202,7 +217,7 @@ __global__ void __launch_bounds__(256) combine_kernel(Src ysrc, const int32_t* _
       for (int j = 0; j < kMaxChunks; ++j) {
         const int c = lane + 32 * j;
         if (c < nchunk)
-          dst[c] = combine_chunk<T, K_MAX>(v[j], g, k, shared_y, n_shared, shared_stride, tok, d, c);
+          dst[c] = combine_chunk<T, K_MAX>(v[j], g, k, shared_y, n_shared, shared_stride, residual, tok, d, c);
       }
       }
     }
@@ -212,7 +227,7 @@ __global__ void __launch_bounds__(256) combine_kernel(Src ysrc, const int32_t* _
 #pragma unroll
         for (int r = 0; r < K_MAX; ++r)
           if (r < k) v[r] = src[r] ? Src::load(src[r] + c) : make_uint4(0, 0, 0, 0);
-        dst[c] = combine_chunk<T, K_MAX>(v, g, k, shared_y, n_shared, shared_stride, tok, d, c);
+        dst[c] = combine_chunk<T, K_MAX>(v, g, k, shared_y, n_shared, shared_stride, residual, tok, d, c);
       }
     }
   }
@@ -220,44 +235,47 @@ __global__ void __launch_bounds__(256) combine_kernel(Src ysrc, const int32_t* _
 
 template <typename T, class Src>
 static cudaError_t launch_combine(Src ysrc, const int32_t* row_of, const void* gates, int64_t n, int d, int k,
-                                  const void* shared_y, int n_shared, int64_t shared_stride, void* out, int num_sms,
-                                  cudaStream_t stream) {
+                                  const void* shared_y, int n_shared, int64_t shared_stride, const void* residual,
+                                  void* out, int num_sms, cudaStream_t stream) {
   const int64_t blocks = std::min<int64_t>((n + 7) / 8, static_cast<int64_t>(num_sms) * 8);
   if (blocks <= 0) return cudaSuccess;
   const T* gs = static_cast<const T*>(gates);
   const T* sh = static_cast<const T*>(shared_y);
+  const T* res = static_cast<const T*>(residual);
   T* o = static_cast<T*>(out);
   const unsigned g = static_cast<unsigned>(blocks);
   if (k <= 2)
     return launch_kernel(combine_kernel<T, 2, Src>, dim3(g), dim3(256), 0, stream, ysrc, row_of, gs, n, d, k, sh,
-                         n_shared, shared_stride, o);
+                         n_shared, shared_stride, res, o);
   if (k <= 4)
     return launch_kernel(combine_kernel<T, 4, Src>, dim3(g), dim3(256), 0, stream, ysrc, row_of, gs, n, d, k, sh,
-                         n_shared, shared_stride, o);
+                         n_shared, shared_stride, res, o);
   return launch_kernel(combine_kernel<T, 16, Src>, dim3(g), dim3(256), 0, stream, ysrc, row_of, gs, n, d, k, sh,
-                       n_shared, shared_stride, o);
+                       n_shared, shared_stride, res, o);
 }
 
 template <typename T>
 static cudaError_t combine_local(const void* y, const int32_t* row_of, const void* gates, int64_t n, int d, int k,
-                                 const void* shared_y, int n_shared, int64_t shared_stride, void* out, int num_sms,
-                                 cudaStream_t stream) {
+                                 const void* shared_y, int n_shared, int64_t shared_stride, const void* residual,
+                                 void* out, int num_sms, cudaStream_t stream) {
   LocalY src{static_cast<const uint4*>(y), static_cast<int>(d * sizeof(T) / 16)};
-  return launch_combine<T>(src, row_of, gates, n, d, k, shared_y, n_shared, shared_stride, out, num_sms, stream);
+  return launch_combine<T>(src, row_of, gates, n, d, k, shared_y, n_shared, shared_stride, residual, out, num_sms,
+                           stream);
 }
 
 cudaError_t combine(int dtype, const void* y, const int32_t* row_of, const void* gates, int64_t n, int d, int k,
-                    const void* shared_y, int n_shared, int64_t shared_stride, void* out, int num_sms,
-                    cudaStream_t stream) {
+                    const void* shared_y, int n_shared, int64_t shared_stride, const void* residual, void* out,
+                    int num_sms, cudaStream_t stream) {
   switch (dtype) {
     case AGM_F32:
-      return combine_local<float>(y, row_of, gates, n, d, k, shared_y, n_shared, shared_stride, out, num_sms, stream);
+      return combine_local<float>(y, row_of, gates, n, d, k, shared_y, n_shared, shared_stride, residual, out,
+                                  num_sms, stream);
     case AGM_BF16:
-      return combine_local<__nv_bfloat16>(y, row_of, gates, n, d, k, shared_y, n_shared, shared_stride, out, num_sms,
-                                          stream);
+      return combine_local<__nv_bfloat16>(y, row_of, gates, n, d, k, shared_y, n_shared, shared_stride, residual,
+                                          out, num_sms, stream);
     case AGM_F16:
-      return combine_local<__half>(y, row_of, gates, n, d, k, shared_y, n_shared, shared_stride, out, num_sms,
-                                   stream);
+      return combine_local<__half>(y, row_of, gates, n, d, k, shared_y, n_shared, shared_stride, residual, out,
+                                   num_sms, stream);
     default:
       return cudaErrorInvalidValue;
   }
@@ -267,14 +285,14 @@ cudaError_t combine_ep(int dtype, const EpRoute* route, const int32_t* row_of, c
                        int k, void* out, int num_sms, cudaStream_t stream) {
   switch (dtype) {
     case AGM_F32:
-      return launch_combine<float>(EpY{route, d * 4 / 16}, row_of, gates, n, d, k, nullptr, 0, 0, out, num_sms,
-                                   stream);
+      return launch_combine<float>(EpY{route, d * 4 / 16}, row_of, gates, n, d, k, nullptr, 0, 0, nullptr, out,
+                                   num_sms, stream);
     case AGM_BF16:
-      return launch_combine<__nv_bfloat16>(EpY{route, d * 2 / 16}, row_of, gates, n, d, k, nullptr, 0, 0, out,
-                                           num_sms, stream);
+      return launch_combine<__nv_bfloat16>(EpY{route, d * 2 / 16}, row_of, gates, n, d, k, nullptr, 0, 0, nullptr,
+                                           out, num_sms, stream);
     case AGM_F16:
-      return launch_combine<__half>(EpY{route, d * 2 / 16}, row_of, gates, n, d, k, nullptr, 0, 0, out, num_sms,
-                                    stream);
+      return launch_combine<__half>(EpY{route, d * 2 / 16}, row_of, gates, n, d, k, nullptr, 0, 0, nullptr, out,
+                                    num_sms, stream);
     default:
       return cudaErrorInvalidValue;
   }

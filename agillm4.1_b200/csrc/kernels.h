@@ -201,8 +201,9 @@ cudaError_t grouped_gemm_dgrad_pair(int dtype, const void* dc, int64_t rows, con
                                     bool relu_mask, int num_sms, cudaStream_t stream);
 cudaError_t grouped_gemm_wgrad_pair(int dtype, bool out_f32, const void* dc, const void* act, int64_t rows,
                                     const BwdGemmArgs& args, int num_sms, cudaStream_t stream);
+// residual (nullable, [n, d]): added last, out = residual + (routed + shared).
 cudaError_t combine(int dtype, const void* y, const int32_t* row_of, const void* gates, int64_t n, int d, int k,
-                    const void* shared_y, int n_shared, int64_t shared_stride, void* out, int num_sms,
-                    cudaStream_t stream);
+                    const void* shared_y, int n_shared, int64_t shared_stride, const void* residual, void* out,
+                    int num_sms, cudaStream_t stream);
 
 }  // namespace agm

@@ -131,7 +131,8 @@ __global__ void __launch_bounds__(256) combine_train_kernel(const T* __restrict_
                                                             const float* __restrict__ logits,
                                                             const int32_t* __restrict__ idx, int64_t n, int d, int k,
                                                             int E, const T* __restrict__ shared_y, int n_shared,
-                                                            int64_t shared_stride, G* __restrict__ out) {
+                                                            int64_t shared_stride, const G* __restrict__ residual,
+                                                            G* __restrict__ out) {
   pdl_wait();
   pdl_trigger();
   const int lane = lane_id();
@@ -180,6 +181,13 @@ __global__ void __launch_bounds__(256) combine_train_kernel(const T* __restrict_
 #pragma unroll
         for (int i = 0; i < 8; ++i)
           acc[i] = (sizeof(G) == 4) ? __fadd_rn(acc[i], sh[i]) : round_to<T>(__fadd_rn(acc[i], sh[i]));
+      }
+      if (residual) {  // Block: x + ff(ln2(x)), agillm41.py:4547
+        float rv[8];
+        load8f<G>(residual + t * d + c * 8, rv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          acc[i] = (sizeof(G) == 4) ? __fadd_rn(rv[i], acc[i]) : round_to<T>(__fadd_rn(rv[i], acc[i]));
       }
       store8f<G>(out + t * d + c * 8, acc);
     }
@@ -766,8 +774,9 @@ cudaError_t cast_any(int dtype, const float* in, void* out, int64_t n, cudaStrea
 }
 
 template <typename T, typename G>
-cudaError_t launch_combine_train(const Saved& S, int64_t n, int d, int k, int E, int n_shared, void* out,
-                                 cudaStream_t s) {
+cudaError_t launch_combine_train(const Saved& S, int64_t n, int d, int k, int E, int n_shared, const void* residual,
+                                 void* out, cudaStream_t s) {
+  const G* res = static_cast<const G*>(residual);
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>((n + 7) / 8, 148 * 8));
   const T* y = static_cast<const T*>(S.y);
   const T* sh = static_cast<const T*>(S.y_sh);
@@ -775,12 +784,12 @@ cudaError_t launch_combine_train(const Saved& S, int64_t n, int d, int k, int E,
   G* o = static_cast<G*>(out);
   if (k <= 2)
     return launch_kernel(combine_train_kernel<T, G, 2>, dim3(grid), dim3(256), 0, s, y, S.row_of, S.logits, S.idx, n,
-                         d, k, E, sh, n_shared, stride, o);
+                         d, k, E, sh, n_shared, stride, res, o);
   if (k <= 4)
     return launch_kernel(combine_train_kernel<T, G, 4>, dim3(grid), dim3(256), 0, s, y, S.row_of, S.logits, S.idx, n,
-                         d, k, E, sh, n_shared, stride, o);
+                         d, k, E, sh, n_shared, stride, res, o);
   return launch_kernel(combine_train_kernel<T, G, 16>, dim3(grid), dim3(256), 0, s, y, S.row_of, S.logits, S.idx, n,
-                       d, k, E, sh, n_shared, stride, o);
+                       d, k, E, sh, n_shared, stride, res, o);
 }
 
 template <typename T, typename G>
@@ -981,8 +990,8 @@ int agm_cast_f32(const float* in, void* out, int dtype, int64_t n, void* stream)
 int agm_moe_forward_train(const void* x, int x_dtype, int dtype, int64_t n_tokens, int d, int n_experts, int top_k,
                           int hidden, const void* w_router, const void* w1, const void* b1, const void* w2,
                           const void* b2, int n_shared, int shared_hidden, const void* ws1, const void* sb1,
-                          const void* ws2, const void* sb2, void* out, void* saved, size_t saved_bytes,
-                          int32_t* counts_out, int flags, void* stream_) {
+                          const void* ws2, const void* sb2, const void* residual, void* out, void* saved,
+                          size_t saved_bytes, int32_t* counts_out, int flags, void* stream_) {
   int rc = check_train_args(x_dtype, dtype, n_tokens, d, n_experts, top_k, hidden, n_shared, shared_hidden);
   if (rc) return rc;
   if (!x || !w_router || !w1 || !b1 || !w2 || !b2 || !out || !saved) return agm::fail(AGM_ERR_ARG, "null pointer");
@@ -992,6 +1001,7 @@ int agm_moe_forward_train(const void* x, int x_dtype, int dtype, int64_t n_token
     if (!agm::al16(p)) return agm::fail(AGM_ERR_ARG, "all tensors must be 16-byte aligned");
   if (n_shared > 0 && (!agm::al16(ws1) || !agm::al16(sb1) || !agm::al16(ws2) || !agm::al16(sb2)))
     return agm::fail(AGM_ERR_ARG, "all tensors must be 16-byte aligned");
+  if (residual && !agm::al16(residual)) return agm::fail(AGM_ERR_ARG, "residual must be 16-byte aligned");
   const int eb = agm::esize(dtype);
   const bool amp = x_dtype != dtype;
   const int Hs = std::max(1, shared_hidden);
@@ -1084,17 +1094,20 @@ int agm_moe_forward_train(const void* x, int x_dtype, int dtype, int64_t n_token
   }
   switch (dtype) {
     case AGM_F32:
-      e = agm::launch_combine_train<float, float>(S, n_tokens, d, top_k, n_experts, n_shared, out, stream);
+      e = agm::launch_combine_train<float, float>(S, n_tokens, d, top_k, n_experts, n_shared, residual, out,
+                                                  stream);
       break;
     case AGM_BF16:
-      e = amp ? agm::launch_combine_train<__nv_bfloat16, float>(S, n_tokens, d, top_k, n_experts, n_shared, out,
-                                                                 stream)
+      e = amp ? agm::launch_combine_train<__nv_bfloat16, float>(S, n_tokens, d, top_k, n_experts, n_shared, residual,
+                                                                 out, stream)
               : agm::launch_combine_train<__nv_bfloat16, __nv_bfloat16>(S, n_tokens, d, top_k, n_experts, n_shared,
-                                                                         out, stream);
+                                                                         residual, out, stream);
       break;
     default:
-      e = amp ? agm::launch_combine_train<__half, float>(S, n_tokens, d, top_k, n_experts, n_shared, out, stream)
-              : agm::launch_combine_train<__half, __half>(S, n_tokens, d, top_k, n_experts, n_shared, out, stream);
+      e = amp ? agm::launch_combine_train<__half, float>(S, n_tokens, d, top_k, n_experts, n_shared, residual, out,
+                                                         stream)
+              : agm::launch_combine_train<__half, __half>(S, n_tokens, d, top_k, n_experts, n_shared, residual, out,
+                                                          stream);
   }
   return e == cudaSuccess ? AGM_OK : agm::cuda_fail(e, "combine_train");
 }

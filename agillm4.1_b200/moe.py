@@ -60,7 +60,8 @@ class _MoETrainNode(torch.autograd.Function):
     straight-through gates, index_select, expert Linear/ReLU/Linear, the gate
     product and index_add_).
 
-    Inputs: x [N, d], the router weight, a state dict (compute-dtype weights,
+    Inputs: x [N, d], the residual added last (or None), the router weight, a
+    state dict (compute-dtype weights,
     top_k, error checking) and the parameters in the order
     experts.{e}.0.weight, .0.bias, .2.weight, .2.bias for e = 0..E-1, then
     shared.{s}.0.weight, ... for the shared experts; their gradients come
@@ -77,11 +78,11 @@ class _MoETrainNode(torch.autograd.Function):
     """
 
     @staticmethod
-    def forward(ctx, x, w_router, state, *params):
+    def forward(ctx, x, residual, w_router, state, *params):
         wr_c, w1, b1, w2, b2 = state["weights"]
         sh = state.get("shared")
         out, saved, counts = ops.moe_forward_train(x, wr_c, w1, b1, w2, b2, state["top_k"], shared=sh,
-                                                   check_errors=state["check"], want_counts=True)
+                                                   residual=residual, check_errors=state["check"], want_counts=True)
         if sh is not None:
             ctx.save_for_backward(saved, wr_c, w1, w2, counts, sh[0], sh[2])
         else:
@@ -113,7 +114,9 @@ class _MoETrainNode(torch.autograd.Function):
             dws1, dsb1, dws2, dsb2 = res[6]
             for s in range(dws1.shape[0]):
                 grads += [dws1[s], dsb1[s], dws2[s], dsb2[s]]
-        return (dx if ctx.needs_input_grad[0] else None, dwr if ctx.needs_input_grad[1] else None, None, *grads)
+        # the residual enters the output unchanged: its gradient is dout
+        dres = dout if ctx.needs_input_grad[1] else None
+        return (dx if ctx.needs_input_grad[0] else None, dres, dwr if ctx.needs_input_grad[2] else None, None, *grads)
 
 
 class _B200Forward:
@@ -293,15 +296,31 @@ class _B200Forward:
         return out
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:  # agillm41.py:4389-4431
+        return self._forward_impl(x, None)
+
+    def forward_residual(self, x: torch.Tensor, residual: torch.Tensor) -> torch.Tensor:
+        """``residual + self(x)`` with the add done by the combine kernel: the
+        tail of Block.forward (`x + self.ff(self.ln2(x))`, agillm41.py:4547),
+        x being the LayerNorm output and residual the block input. Same
+        value and gradients as the two separate ops."""
+        if residual.shape != x.shape:
+            raise MoEKernelError(f"residual shape {tuple(residual.shape)} differs from {tuple(x.shape)}")
+        return self._forward_impl(x, residual)
+
+    def _forward_impl(self, x: torch.Tensor, residual: Optional[torch.Tensor]) -> torch.Tensor:
         orig_shape = x.shape
         flat = x.reshape(-1, orig_shape[-1])
+        res = None if residual is None else residual.reshape(-1, orig_shape[-1])
         if self.training:
             # agillm41.py:4392-4397: stash the detached input for _collect_moe_aux.
             self.last_router_input = flat.detach()
         if not flat.is_cuda:
             raise MoEKernelError("MoEFFN (B200) runs on CUDA tensors only; there is no CPU path")
+        if res is not None and (not res.is_cuda or res.device != flat.device):
+            raise MoEKernelError("the residual must be on the input's GPU")
         if self.expert_stream:
-            return self._forward_expert_stream(flat).reshape(orig_shape)
+            out = self._forward_expert_stream(flat)
+            return (out if res is None else res + out).reshape(orig_shape)
         wr = self.router.weight
         amp = _autocast_dtype(flat.device)
         amp_mode = amp is not None and wr.dtype == torch.float32
@@ -317,12 +336,15 @@ class _B200Forward:
                 raise MoEKernelError("training and autocast route with the router kernel's logits only")
             weights, shared = self._compute_weights(flat.device, wr.dtype, amp if amp_mode else wr.dtype)
             flat = flat.contiguous()
-            if grad:
+            if res is not None and res.dtype != flat.dtype:
+                raise MoEKernelError(f"residual dtype {res.dtype} differs from the input dtype {flat.dtype}")
+            if grad or (res is not None and res.requires_grad and torch.is_grad_enabled()):
                 state = {"weights": weights, "shared": shared, "top_k": self.top_k,
                          "check": self.check_device_errors, "empty_grad": self.empty_expert_grad}
-                out = _MoETrainNode.apply(flat, wr, state, *params)
+                out = _MoETrainNode.apply(flat, None if res is None else res.contiguous(), wr, state, *params)
             else:
                 out, _ = ops.moe_forward_train(flat, *weights, self.top_k, shared=shared,
+                                               residual=None if res is None else res.contiguous(),
                                                check_errors=self.check_device_errors)
             return out.reshape(orig_shape)
         w1, b1, w2, b2, sh = self._packed_weights(flat.device, flat.dtype)
@@ -332,8 +354,16 @@ class _B200Forward:
             logits_in = self.router(flat).float()
         elif self.router_logits != "kernel":
             raise MoEKernelError(f"router_logits must be 'kernel' or 'reference_gemm', not {self.router_logits!r}")
+        if res is not None and res.dtype != flat.dtype:
+            raise MoEKernelError(f"residual dtype {res.dtype} differs from the input dtype {flat.dtype}")
+        if res is not None and logits_in is None:
+            out = ops.moe_forward_residual(flat, res.contiguous(), wr.detach().contiguous(), w1, b1, w2, b2,
+                                           self.top_k, shared=sh, check_errors=self.check_device_errors)
+            return out.reshape(orig_shape)
         out = ops.moe_forward(flat, wr.detach().contiguous(), w1, b1, w2, b2, self.top_k, shared=sh,
                               check_errors=self.check_device_errors, logits_in=logits_in)
+        if res is not None:
+            out = res + out
         return out.reshape(orig_shape)
 
 
@@ -427,7 +457,23 @@ class MoEFFN(_B200Forward, nn.Module):
                                              unexpected_keys, error_msgs)
 
 
-def install(agillm41_module, name: str = "MoEFFN"):
+def _fused_block_forward(self, x, mask, kv=None, use_cache=False, total_seq_len=None):
+    """Block.forward (agillm41.py:4539-4547) with the MoE FFN's residual add
+    done by its combine kernel (`x + ff(ln2(x))` as one call); any other ff
+    runs the reference's own forward."""
+    ff = self.ff
+    if not isinstance(ff, _B200Forward):
+        return self._reference_block_forward(x, mask, kv=kv, use_cache=use_cache, total_seq_len=total_seq_len)
+    if use_cache:
+        y, new_kv = self.mha(self.ln1(x), mask, rel_bias_tokens=total_seq_len, kv_cache=kv, use_cache=True)
+        r = x + y  # the reference's `x + y + ff(ln2(x + y))`
+        return ff.forward_residual(self.ln2(r), r), new_kv
+    n = x.size(1)
+    x = x + self.mha(self.ln1(x), mask, rel_bias_tokens=n)
+    return ff.forward_residual(self.ln2(x), x)
+
+
+def install(agillm41_module, name: str = "MoEFFN", fuse_residual: bool = False):
     """Rebind ``agillm41_module.MoEFFN`` to a subclass of the reference class
     whose forward runs on the B200 kernels. Returns the new class.
 
@@ -435,17 +481,29 @@ def install(agillm41_module, name: str = "MoEFFN"):
     streaming toggles, aux-loss stash) is inherited from the reference class.
     Modules built after the call (``Block``, ``Encoder``, the inference and
     pipeline-stage runtimes) use it.
+
+    ``fuse_residual``: also rebind ``Block`` to a subclass whose forward adds
+    the residual inside the MoE block's combine kernel (same values and
+    gradients, one elementwise pass less per layer).
     """
     ref_cls = getattr(agillm41_module, name)
     if getattr(ref_cls, "_is_b200", False):
-        return ref_cls
-    cls = type(name, (_B200Forward, ref_cls), {"_is_b200": True, "_reference_class": ref_cls,
-                                               "__module__": ref_cls.__module__})
-    setattr(agillm41_module, name, cls)
+        cls = ref_cls
+    else:
+        cls = type(name, (_B200Forward, ref_cls), {"_is_b200": True, "_reference_class": ref_cls,
+                                                   "__module__": ref_cls.__module__})
+        setattr(agillm41_module, name, cls)
+    block = getattr(agillm41_module, "Block", None)
+    if fuse_residual and block is not None and not getattr(block, "_is_b200", False):
+        fused = type("Block", (block,), {"_is_b200": True, "_reference_class": block,
+                                         "_reference_block_forward": block.forward,
+                                         "forward": _fused_block_forward, "__module__": block.__module__})
+        setattr(agillm41_module, "Block", fused)
     return cls
 
 
 def uninstall(agillm41_module, name: str = "MoEFFN") -> None:
-    cls = getattr(agillm41_module, name)
-    if getattr(cls, "_is_b200", False):
-        setattr(agillm41_module, name, cls._reference_class)
+    for attr in (name, "Block"):
+        cls = getattr(agillm41_module, attr, None)
+        if getattr(cls, "_is_b200", False):
+            setattr(agillm41_module, attr, cls._reference_class)

@@ -174,6 +174,35 @@ def workspace_bytes(n_tokens: int, d: int, n_experts: int, top_k: int, hidden: i
                                               dtype_code(dtype)))
 
 
+def moe_forward_residual(x: torch.Tensor, residual: torch.Tensor, w_router: torch.Tensor, w1: torch.Tensor,
+                         b1: torch.Tensor, w2: torch.Tensor, b2: torch.Tensor, top_k: int, *,
+                         shared: Optional[tuple] = None, check_errors: bool = False) -> torch.Tensor:
+    """residual + MoE(x) in one launch sequence (Block's `x + ff(ln2(x))`,
+    agillm41.py:4547): x [N, d] is the LayerNorm output, residual [N, d] the
+    block input; the combine adds the residual last."""
+    lib = load()
+    n, d = x.shape
+    E = w_router.shape[0]
+    H = w1.shape[1]
+    dev = x.device
+    if residual.shape != x.shape or residual.dtype != x.dtype:
+        raise _lib.MoEKernelError("residual must have x's shape and dtype")
+    ws1, sb1, ws2, sb2, S, Hs = _shared_parts(shared)
+    out = torch.empty_like(x)
+    nbytes = workspace_bytes(n, d, E, top_k, H, S, Hs, x.dtype)
+    workspace = Workspace.get(dev, nbytes)
+    rc = lib.agm_moe_forward_residual(ptr(x), ptr(residual.contiguous()), dtype_code(x.dtype), n, d, E, top_k, H,
+                                      ptr(w_router), ptr(w1), ptr(b1), ptr(w2), ptr(b2), S, Hs, ptr(ws1), ptr(sb1),
+                                      ptr(ws2), ptr(sb2), ptr(out), ptr(workspace), workspace.numel(), 0,
+                                      stream_handle(dev))
+    check(rc, "agm_moe_forward_residual")
+    if check_errors:
+        code = _lib.read_device_error(workspace[:4].view(torch.int32))
+        if code:
+            raise _lib.MoEKernelError(f"device error word 0x{code:x} after agm_moe_forward_residual")
+    return out
+
+
 def moe_forward(x: torch.Tensor, w_router: torch.Tensor, w1: torch.Tensor, b1: torch.Tensor, w2: torch.Tensor,
                 b2: torch.Tensor, top_k: int, *, shared: Optional[tuple] = None, out: Optional[torch.Tensor] = None,
                 want: tuple = (), tie_low_first: bool = False, workspace: Optional[torch.Tensor] = None,
@@ -327,8 +356,8 @@ def _shared_parts(shared):
 
 def moe_forward_train(x: torch.Tensor, w_router: torch.Tensor, w1: torch.Tensor, b1: torch.Tensor,
                       w2: torch.Tensor, b2: torch.Tensor, top_k: int, *, shared: Optional[tuple] = None,
-                      tie_low_first: bool = False, pair: bool = True, pdl: bool = True, check_errors: bool = False,
-                      want_counts: bool = False):
+                      residual: Optional[torch.Tensor] = None, tie_low_first: bool = False, pair: bool = True,
+                      pdl: bool = True, check_errors: bool = False, want_counts: bool = False):
     """Training forward: x [N, d] -> (out [N, d] in x's dtype, saved uint8 buffer).
 
     The weights are in the compute dtype: x's dtype, or bf16/fp16 with x fp32
@@ -351,7 +380,8 @@ def moe_forward_train(x: torch.Tensor, w_router: torch.Tensor, w1: torch.Tensor,
     flags = _flags(tie_low_first) | (0 if pair else _lib.AGM_FLAG_NO_PAIR) | (0 if pdl else _lib.AGM_FLAG_NO_PDL)
     rc = lib.agm_moe_forward_train(ptr(x), dtype_code(x.dtype), dtype_code(dtype), n, d, E, top_k, H, ptr(w_router),
                                    ptr(w1), ptr(b1), ptr(w2), ptr(b2), S, Hs, ptr(ws1), ptr(sb1), ptr(ws2), ptr(sb2),
-                                   ptr(out), ptr(saved), saved.numel(), ptr(counts), flags, stream_handle(dev))
+                                   ptr(None if residual is None else residual.contiguous()), ptr(out), ptr(saved),
+                                   saved.numel(), ptr(counts), flags, stream_handle(dev))
     check(rc, "agm_moe_forward_train")
     if check_errors:
         code = _lib.read_device_error(saved[:4].view(torch.int32))

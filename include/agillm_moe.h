@@ -168,6 +168,17 @@ AGM_API int agm_moe_forward(const void* x, int dtype, int64_t n_tokens, int d, i
                     int32_t* counts_out, float* logits_out, const float* logits_in, void* const* stage_events,
                     void* stream);
 
+/* agm_moe_forward plus the residual add that follows it in Block.forward
+ * (agillm41.py:4547, `x + self.ff(self.ln2(x))`; 4543 with a KV cache): the
+ * combine adds residual [n, d] (dtype) last, out = residual + MoEFFN(x), with
+ * the reference's rounding (the sum rounded once). x is the LayerNorm output,
+ * residual the block input; out may alias neither. Flags as agm_moe_forward. */
+AGM_API int agm_moe_forward_residual(const void* x, const void* residual, int dtype, int64_t n_tokens, int d,
+                                     int n_experts, int top_k, int hidden, const void* w_router, const void* w1,
+                                     const void* b1, const void* w2, const void* b2, int n_shared, int shared_hidden,
+                                     const void* ws1, const void* sb1, const void* ws2, const void* sb2, void* out,
+                                     void* workspace, size_t workspace_bytes, int flags, void* stream);
+
 /* Size of the scratch area compiled into the library for
  * agm_moe_forward_noalloc (32 MiB; e.g. up to about 950 tokens at d=1280,
  * H=3200, 14 experts, top-2, bf16). */
@@ -310,14 +321,16 @@ AGM_API int agm_cast_f32(const float* in, void* out, int dtype, int64_t n, void*
  * input, FC1 activations (and their ReLU masks) and expert outputs in `saved`
  * (agm_moe_train_saved_bytes) for agm_moe_backward. counts_out (nullable)
  * int32 [E]: rows routed to each expert (an expert with none gets no
- * gradient at all in the reference, which never calls it). The device error
+ * gradient at all in the reference, which never calls it). residual
+ * (nullable, [n, d], x_dtype): added last as in agm_moe_forward_residual
+ * (its gradient is dout itself; agm_moe_backward is unchanged). The device error
  * word is the first int of `saved`. Weight layouts as agm_moe_forward.
  * flags: AGM_FLAG_TIE_LOW_FIRST, AGM_FLAG_NO_PAIR, AGM_FLAG_NO_PDL. */
 AGM_API int agm_moe_forward_train(const void* x, int x_dtype, int dtype, int64_t n_tokens, int d, int n_experts,
                                   int top_k, int hidden, const void* w_router, const void* w1, const void* b1,
                                   const void* w2, const void* b2, int n_shared, int shared_hidden, const void* ws1,
-                                  const void* sb1, const void* ws2, const void* sb2, void* out, void* saved,
-                                  size_t saved_bytes, int32_t* counts_out, int flags, void* stream);
+                                  const void* sb1, const void* ws2, const void* sb2, const void* residual, void* out,
+                                  void* saved, size_t saved_bytes, int32_t* counts_out, int flags, void* stream);
 /* Backward of agm_moe_forward_train. Replaces autograd through
  * agillm41.py:4398-4430 (router Linear, top-k/softmax gates or the top-1
  * straight-through gate, index_select, expert Linear/ReLU/Linear, `* weight`,

@@ -110,7 +110,7 @@ def test_training_entry_points_validate_without_a_device():
     assert shared >= need + n * (d + 2 * d + d) * 2  # x copy, shared FC1 activation and output
     assert lib.agm_moe_backward_workspace_bytes(n, d, E, k, H, 0, 1, _lib.AGM_BF16) >= rows * (d + H) * 2
     fwd = [fake, _lib.AGM_BF16, _lib.AGM_BF16, n, d, E, k, H, fake, fake, fake, fake, fake, 0, 1, None, None, None,
-           None, fake, fake]
+           None, None, fake, fake]
     # saved buffer too small
     assert lib.agm_moe_forward_train(*fwd, 1024, None, 0, None) == -5
     assert "saved" in lib.agm_last_error().decode()
@@ -123,6 +123,12 @@ def test_training_entry_points_validate_without_a_device():
     sh = list(fwd)
     sh[13], sh[14] = 1, 2 * d
     assert lib.agm_moe_forward_train(*sh, shared, None, 0, None) == -1
+    # misaligned residual
+    mis = list(fwd)
+    mis[19] = ctypes.c_void_p(4096 + 8)
+    assert lib.agm_moe_forward_train(*mis, need, None, 0, None) == -1
+    assert lib.agm_moe_forward_residual(fake, None, _lib.AGM_BF16, n, d, E, k, H, fake, fake, fake, fake, fake, 0, 1,
+                                        None, None, None, None, fake, fake, 1 << 30, 0, None) == -1
     # backward: workspace too small
     rc = lib.agm_moe_backward(fake, _lib.AGM_BF16, _lib.AGM_BF16, n, d, E, k, H, fake, fake, fake, 0, 1, None, None,
                               fake, need, fake, fake, fake, fake, fake, fake, None, None, None, None, fake, 1024, 0,

@@ -343,3 +343,21 @@ def test_expert_stream_matches_resident(k, E, S):
     with pytest.raises(agillm41_b200.MoEKernelError):
         m.train()
         m(x.requires_grad_(True))
+
+
+@pytest.mark.parametrize("S", [0, 1])
+def test_forward_residual_equals_separate_add(S):
+    """forward_residual(h, x) (the residual added by the combine kernel, as
+    Block's `x + ff(ln2(x))`) equals x + forward(h) bit for bit."""
+    d, H, E, k, n = 1280, 3200, 14, 2, 3000
+    m = agillm41_b200.MoEFFN(d, mlp_mult=4, experts=E, top_k=k, shared_experts=S, shared_mlp_mult=2 if S else 0)
+    m.experts = torch.nn.ModuleList([torch.nn.Sequential(torch.nn.Linear(d, H), torch.nn.ReLU(),
+                                                         torch.nn.Linear(H, d)) for _ in range(E)])
+    m.load_state_dict(reference_moe.make_state(d, H, E, 28, bias_std=0.02, shared=S, shared_hidden=2 * d if S else None))
+    m = m.to(device=DEV, dtype=torch.bfloat16).eval()
+    h = reference_moe.make_input(n, d, 28, dtype=torch.bfloat16, device=DEV)
+    x = reference_moe.make_input(n, d, 29, dtype=torch.bfloat16, device=DEV)
+    with torch.no_grad():
+        assert torch.equal(m.forward_residual(h, x), x + m(h))
+        m.router_logits = "reference_gemm"
+        assert torch.equal(m.forward_residual(h, x), x + m(h))

@@ -356,3 +356,23 @@ def test_full_size_bench_workload_autocast():
     sd, x, dout = case(1280, 3200, 14, 2, 73728, 191)
     ours, ref, counts = run_pair(sd, x, dout, 2, torch.float32, amp=torch.bfloat16)
     compare(ours, ref, torch.bfloat16, counts)
+
+
+@pytest.mark.parametrize("amp", [None, torch.bfloat16])
+def test_forward_residual_training_equals_separate_add(amp):
+    """The fused residual (Block's `x + ff(ln2(x))`) gives the same output and
+    gradients, bit for bit, as the MoE block followed by a separate add."""
+    sd, x, dout = case(256, 512, 14, 2, 512, 201, shared=1, shared_hidden=256)
+    master = torch.float32 if amp else torch.bfloat16
+    res_in = synthetic.make_input(512, 256, 202)
+    outs = []
+    for fused in (False, True):
+        m = make_module(sd, 256, 512, 14, 2, master)
+        h = x.to(DEV, master).clone().requires_grad_(True)
+        r = res_in.to(DEV, master).clone().requires_grad_(True)
+        with torch.autocast("cuda", dtype=amp or torch.bfloat16, enabled=amp is not None):
+            y = m.forward_residual(h, r) if fused else r + m(h)
+        y.backward(dout.to(DEV, master))
+        outs.append([y.detach(), h.grad, r.grad] + [p.grad for p in m.parameters()])
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)

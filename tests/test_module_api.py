@@ -106,6 +106,29 @@ def test_install_into_reference(ref):
     assert not getattr(ref.MoEFFN, "_is_b200", False)
 
 
+def test_fused_residual_block(ref):
+    """install(fuse_residual=True) rebinds Block to a subclass whose MoE
+    residual add runs in the combine kernel; other FFNs keep the reference's
+    own forward (checked numerically here on CPU with a dense FFN)."""
+    orig_block = ref.Block
+    agillm41_b200.install(ref, fuse_residual=True)
+    try:
+        assert ref.Block is not orig_block and issubclass(ref.Block, orig_block)
+        torch.manual_seed(0)
+        dense = ref.Block(64, 4, 16, moe_ffn=False).eval()
+        plain = orig_block(64, 4, 16, moe_ffn=False).eval()
+        plain.load_state_dict(dense.state_dict())
+        x = torch.randn(2, 5, 64)
+        with torch.no_grad():
+            assert torch.equal(dense(x, None), plain(x, None))
+        moe = ref.Block(64, 4, 16, moe_ffn=True, moe_experts=14, moe_top_k=2, moe_mlp_mult=2).eval()
+        with torch.no_grad(), pytest.raises(MoEKernelError):
+            moe(x, None)                         # CPU tensors: no fallback
+    finally:
+        agillm41_b200.uninstall(ref)
+    assert ref.Block is orig_block and not getattr(ref.MoEFFN, "_is_b200", False)
+
+
 def test_cpu_input_raises():
     m = MoEFFN(64, experts=14, top_k=2).eval()
     with torch.no_grad(), pytest.raises(MoEKernelError, match="CUDA"):
