@@ -401,6 +401,10 @@ int moe_forward_impl(const void* x, int dtype, int64_t n_tokens, int d, int n_ex
   if ((e = mark(5)) != cudaSuccess) return cuda_fail(e, "event record");
 
   const int64_t npad = round_up(n_tokens, AGM_TILE_M);
+  // Shared experts: one dense group over all tokens, so any two row tiles
+  // share their weights and the CTA-pair GEMM applies without padding.
+  const int shared_mode = (dtype != AGM_F32 && !(flags & AGM_FLAG_NO_PAIR) && n_tokens >= AGM_PAIR_MIN_ROWS)
+                              ? AGM_GEMM_PAIR : 0;
   for (int s = 0; s < n_shared; ++s) {
     agm::GemmArgs s1;
     s1.c = L.h_sh;
@@ -416,7 +420,7 @@ int moe_forward_impl(const void* x, int dtype, int64_t n_tokens, int d, int n_ex
     s1.err = L.err;
     s1.early_weights = true;
     e = agm::grouped_gemm(dtype, x, n_tokens, static_cast<const uint8_t*>(ws1) + static_cast<size_t>(eb) * s * shared_hidden * d,
-                          s1, true, sms, stream, 0);
+                          s1, true, sms, stream, shared_mode);
     if (e != cudaSuccess) return cuda_fail(e, "grouped_gemm shared fc1");
     agm::GemmArgs s2 = s1;
     s2.c = static_cast<uint8_t*>(L.y_sh) + static_cast<size_t>(eb) * s * npad * d;
@@ -425,7 +429,7 @@ int moe_forward_impl(const void* x, int dtype, int64_t n_tokens, int d, int n_ex
     s2.n = d;
     s2.k = shared_hidden;
     e = agm::grouped_gemm(dtype, L.h_sh, npad, static_cast<const uint8_t*>(ws2) + static_cast<size_t>(eb) * s * d * shared_hidden,
-                          s2, false, sms, stream, 0);
+                          s2, false, sms, stream, shared_mode);
     if (e != cudaSuccess) return cuda_fail(e, "grouped_gemm shared fc2");
   }
   if ((e = mark(6)) != cudaSuccess) return cuda_fail(e, "event record");

@@ -1076,6 +1076,9 @@ int agm_moe_forward_train(const void* x, int x_dtype, int dtype, int64_t n_token
   g2.k = hidden;
   e = agm::grouped_gemm(dtype, S.h, rows, w2, g2, false, sms, stream, pair ? AGM_GEMM_PAIR : 0);
   if (e != cudaSuccess) return agm::cuda_fail(e, "grouped_gemm fc2");
+  // Shared experts: one dense group, so the CTA-pair GEMM applies for large batches.
+  const int shared_mode = (dtype != AGM_F32 && !(flags & AGM_FLAG_NO_PAIR) && n_tokens >= AGM_PAIR_MIN_ROWS)
+                              ? AGM_GEMM_PAIR : 0;
   for (int s = 0; s < n_shared; ++s) {
     void* hs = at(S.h_sh, static_cast<size_t>(eb) * s * npad * Hs);
     agm::GemmArgs s1 = dense_args(hs, npad, Hs, d, at(sb1, static_cast<size_t>(eb) * s * Hs), S.err);
@@ -1084,12 +1087,12 @@ int agm_moe_forward_train(const void* x, int x_dtype, int dtype, int64_t n_token
       s1.ld_bits = npad;
     }
     e = agm::grouped_gemm(dtype, xin, n_tokens, at(ws1, static_cast<size_t>(eb) * s * Hs * d), s1, true, sms,
-                          stream, 0);
+                          stream, shared_mode);
     if (e != cudaSuccess) return agm::cuda_fail(e, "grouped_gemm shared fc1");
     agm::GemmArgs s2 = dense_args(at(S.y_sh, static_cast<size_t>(eb) * s * npad * d), npad, d, Hs,
                                   at(sb2, static_cast<size_t>(eb) * s * d), S.err);
     e = agm::grouped_gemm(dtype, hs, npad, at(ws2, static_cast<size_t>(eb) * s * d * Hs), s2, false, sms, stream,
-                          0);
+                          shared_mode);
     if (e != cudaSuccess) return agm::cuda_fail(e, "grouped_gemm shared fc2");
   }
   switch (dtype) {

@@ -306,7 +306,51 @@ def run_ours(args, world, rank, local):
         train["production"] = run_train(args, dev, stream, experts=2, hidden=4 * D, top_k=1, shared=1,
                                         shared_hidden=2 * D, batch=22, seq=1536,
                                         label="production MoE block training step")
+        train["production"]["forward"] = run_forward_production(args, dev, stream)
     report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e_value, x, decode, train)
+
+
+def run_forward_production(args, dev, stream):
+    """Inference forward of the reference's production MoE (2 experts, top-1,
+    H = 4d, one shared expert of 2d, agillm41.py:8590-8594) in bf16 over
+    22 x 1536 tokens: tokens/s and the expert GEMMs' rate over the whole
+    forward (router, permute and combine included)."""
+    from agillm41_b200 import ops, synthetic
+
+    E, H, k, Hs, N = 2, 4 * D, 1, 2 * D, 22 * 1536
+    sd = synthetic.make_state(D, H, E, SEED, dtype=torch.bfloat16, device=dev, shared=1, shared_hidden=Hs)
+    w = [torch.stack([sd[f"experts.{e}.{i}.{p}"] for e in range(E)]).contiguous()
+         for i, p in ((0, "weight"), (0, "bias"), (2, "weight"), (2, "bias"))]
+    sh = tuple(sd[f"shared.0.{i}.{p}"].unsqueeze(0).contiguous()
+               for i, p in ((0, "weight"), (0, "bias"), (2, "weight"), (2, "bias")))
+    wr = sd["router.weight"].contiguous()
+    x = synthetic.make_input(N, D, SEED, dtype=torch.bfloat16, device=dev)
+    out = torch.empty_like(x)
+
+    def step():
+        ops.moe_forward(x, wr, *w, k, shared=sh, out=out)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    steps = max(10, min(args.steps, 100))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    peaks = load_peaks()
+    flop = 4 * D * (k * H + Hs) * N
+    tf = flop / (ms / 1000.0) / 1e12
+    return {"workload": f"production MoE block forward, B22 L1536 ({N} tokens) d{D} E{E} H{H} top{k} + 1 shared "
+                        f"H{Hs}, bf16, seed {SEED}",
+            "ms_per_step": round(ms, 4), "tokens_per_s": N / (ms / 1000.0), "steps": steps,
+            "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peaks["tf_sus"], "unit": "TFLOP/s",
+                         "frac": round(tf / peaks["tf_sus"], 3),
+                         "note": "expert and shared GEMM FLOPs over the whole forward"},
+            "gpu_launches_per_step": 8}
 
 
 def run_train(args, dev, stream, *, experts=EXPERTS, hidden=HIDDEN, top_k=TOP_K, shared=0, shared_hidden=0,

@@ -23,7 +23,7 @@ import torch
 import torch.nn.functional as F
 
 import agillm41_b200
-from agillm41_b200 import ops
+from agillm41_b200 import ops, synthetic
 from gpu_helpers import assert_close_rows, explained_index_mismatches, gate_slack, packed
 from golden_io import Golden, names
 from oracle import reference_moe
@@ -277,6 +277,26 @@ def test_pair_gemm_forward_matches_single_cta():
     out_1, ex_1 = ops.moe_forward(x, wr, w1, b1, w2, b2, k, want=("idx", "counts"), check_errors=True, pair=False)
     assert torch.equal(ex_p["idx"], ex_1["idx"]) and torch.equal(ex_p["counts"], ex_1["counts"])
     assert torch.equal(out_p, out_1)
+
+
+def test_pair_gemm_shared_expert_matches_single_cta():
+    """The production MoE (2 experts, top-1, one shared expert of 2d) above the
+    pair threshold: the shared expert's dense GEMMs run on CTA pairs over 129
+    row tiles (the last pair holds one) and match the one-CTA path bit for bit."""
+    d, E, k, n = 1280, 2, 1, 16500
+    sd = synthetic.make_state(d, 4 * d, E, 26, dtype=torch.bfloat16, device=DEV, bias_std=0.02, shared=1,
+                              shared_hidden=2 * d)
+    w1, b1, w2, b2, _ = packed(sd, E, DEV)
+    sh = tuple(sd[f"shared.0.{i}.{p}"].unsqueeze(0).contiguous()
+               for i, p in ((0, "weight"), (0, "bias"), (2, "weight"), (2, "bias")))
+    wr = sd["router.weight"].contiguous()
+    x = synthetic.make_input(n, d, 26, dtype=torch.bfloat16, device=DEV)
+    out_p = ops.moe_forward(x, wr, w1, b1, w2, b2, k, shared=sh, check_errors=True)
+    out_1 = ops.moe_forward(x, wr, w1, b1, w2, b2, k, shared=sh, check_errors=True, pair=False)
+    assert torch.equal(out_p, out_1)
+    res = torch.randn(n, d, generator=torch.Generator().manual_seed(27)).to(DEV, torch.bfloat16)
+    out_r = ops.moe_forward_residual(x, res, wr, w1, b1, w2, b2, k, shared=sh, check_errors=True)
+    assert torch.equal(out_r, out_p + res)
 
 
 @pytest.mark.parametrize("n,k,E", [(64, 2, 14), (200, 2, 14), (37, 1, 4), (96, 3, 16)])

@@ -229,7 +229,7 @@ def _ops_grads(sd, x, dout, k, amp, fwd_pair, bwd_pair, bwd_always):
     return flat
 
 
-@pytest.mark.parametrize("shape", ["full_width_8192", "ragged_shared"])
+@pytest.mark.parametrize("shape", ["full_width_8192", "ragged_shared", "production_16500"])
 @pytest.mark.parametrize("amp", [False, True])
 def test_cta_pair_backward_matches_one_cta(shape, amp):
     """The CTA-pair backward GEMMs (256 x 256 tiles on two SMs) give the same
@@ -238,6 +238,11 @@ def test_cta_pair_backward_matches_one_cta(shape, amp):
     if shape == "full_width_8192":
         sd, x, dout = case(1280, 3200, 14, 2, 8192, 161)
         k = 2
+    elif shape == "production_16500":
+        # Above the pair threshold the shared expert's dense GEMMs run on CTA
+        # pairs too: 129 row tiles, so the last pair holds one tile.
+        sd, x, dout = case(1280, 5120, 2, 1, 16500, 164, shared=1, shared_hidden=2560)
+        k = 1
     else:
         d, H, E, k, n = 256, 320, 6, 2, 300
         sd = synthetic.make_state(d, H, E, 162, dtype=torch.float32, bias_std=0.05, shared=1, shared_hidden=192)
