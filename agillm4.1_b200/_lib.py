@@ -79,6 +79,10 @@ SIGNATURES = {
                                       _P, _P, _SZ, _I, _P]),
     "agm_moe_backward": (_I, [_P, _I, _I, _I64, _I, _I, _I, _I, _P, _P, _P, _I, _I, _P, _P, _P, _SZ,
                               _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _I, _P]),
+    "agm_moe_aux_saved_bytes": (_SZ, [_I64, _I, _I]),
+    "agm_moe_aux_backward_workspace_bytes": (_SZ, [_I64, _I, _I]),
+    "agm_moe_aux_forward": (_I, [_P, _I, _I64, _I, _I, _P, ctypes.c_double, ctypes.c_double, _P, _P, _SZ, _I, _P]),
+    "agm_moe_aux_backward": (_I, [_P, _P, _I, _I64, _I, _I, _P, _SZ, _P, _P, _SZ, _I, _P]),
 }
 
 

@@ -383,7 +383,8 @@ __global__ void __launch_bounds__(256) reduce_partials_kernel(const float* __res
 // ---------------------------------------------------------------------------
 // Router weight gradient partials: partial[chunk, e, c] = sum over the
 // chunk's tokens of dl[t, e] * x[t, c], x[t] read from x_perm[row_of[t, 0]]
-// (the permuted copy of token t's router input). A thread owns 4 columns for
+// (the permuted copy of token t's router input), or from x_perm[t] when
+// row_of is null. A thread owns 4 columns for
 // all 16 logit rows (64 fp32 accumulators); the chunk's logit gradients and
 // row indices are staged in shared memory first, and the x values of 4 tokens
 // are loaded together ahead of their multiply-adds.
@@ -403,7 +404,8 @@ __global__ void __launch_bounds__(512) router_wgrad_kernel(const T* __restrict__
   const int cnt = static_cast<int>(min(static_cast<int64_t>(tok_per_chunk), n - t0));
   float* dl_f = reinterpret_cast<float*>(&dl_s[0][0]);
   for (int i = threadIdx.x; i < cnt * kMaxE; i += blockDim.x) dl_f[i] = Traits<T>::to_f(dl[t0 * kMaxE + i]);
-  for (int i = threadIdx.x; i < cnt; i += blockDim.x) row_s[i] = static_cast<int64_t>(row_of[(t0 + i) * k]) * d;
+  for (int i = threadIdx.x; i < cnt; i += blockDim.x)
+    row_s[i] = (row_of ? static_cast<int64_t>(row_of[(t0 + i) * k]) : t0 + i) * d;
   __syncthreads();
   const int c0 = (blockIdx.y * blockDim.x + threadIdx.x) * 4;
   if (c0 >= d) return;
@@ -884,6 +886,248 @@ cudaError_t launch_dx(const BwdWs& B, const Saved& S, const void* wr, int64_t n,
                          sstride, o);
 }
 
+// ---------------------------------------------------------------------------
+// Auxiliary router losses (_collect_moe_aux, agillm41.py:4463-4492): the
+// load-balance loss aux_coef * E * sum_e(load_e * importance_e) and the
+// router-z loss z_coef * mean_t(logsumexp(scores_t)^2), over the router logits
+// recomputed from the stashed FFN input (kept as fp32 values [N, E] in the
+// saved state, each rounded to the router's dtype as F.linear rounds it).
+//   importance_e = mean_t softmax(scores_t)_e
+//   load_e       = #{t : argmax_e softmax(scores_t) = e} / max(1, N)   (no gradient)
+// aux_stats: one CTA per token chunk, fixed-order partial sums; aux_finalize
+// (one warp) adds the partials in chunk order and writes the loss and the
+// backward's per-expert factors.
+// ---------------------------------------------------------------------------
+constexpr int kAuxThreads = 256;
+constexpr int kAuxParts = kMaxE + 1;  // importance sums [16], then the sum of lse^2
+
+int aux_tok_per_chunk(int64_t n) {
+  // Chunking depends on n only, so the loss is the same on every GPU.
+  const int64_t per = (n + 295) / 296;
+  return static_cast<int>(std::max<int64_t>(kAuxThreads, (per + kAuxThreads - 1) / kAuxThreads * kAuxThreads));
+}
+int aux_chunks(int64_t n) { return n == 0 ? 0 : static_cast<int>((n + aux_tok_per_chunk(n) - 1) / aux_tok_per_chunk(n)); }
+
+// Softmax of one token's logits (exp(l - max) / sum, the first maximum's index
+// as argmax) and its logsumexp.
+__device__ __forceinline__ void aux_softmax(const float* __restrict__ lrow, int E, float (&p)[kMaxE], float& lse,
+                                            int& top) {
+  float m = -INFINITY;
+#pragma unroll
+  for (int e = 0; e < kMaxE; ++e) {
+    p[e] = e < E ? lrow[e] : -INFINITY;
+    m = fmaxf(m, p[e]);
+  }
+  float sum = 0.f;
+#pragma unroll
+  for (int e = 0; e < kMaxE; ++e) {
+    p[e] = e < E ? expf(p[e] - m) : 0.f;
+    sum += p[e];
+  }
+  lse = m + logf(sum);
+  top = 0;
+  float best = -1.f;
+#pragma unroll
+  for (int e = 0; e < kMaxE; ++e) {
+    p[e] = p[e] / sum;
+    if (e < E && p[e] > best) {
+      best = p[e];
+      top = e;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kAuxThreads) aux_stats_kernel(const float* __restrict__ logits, int64_t n, int E,
+                                                                int tok_per_chunk, float* __restrict__ part,
+                                                                int32_t* __restrict__ cnt_part) {
+  __shared__ float red[kAuxThreads / 32][kAuxParts];
+  __shared__ int cnt_s[kMaxE];
+  pdl_wait();
+  pdl_trigger();
+  if (threadIdx.x < kMaxE) cnt_s[threadIdx.x] = 0;
+  __syncthreads();
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * tok_per_chunk;
+  const int64_t t1 = min(n, t0 + tok_per_chunk);
+  float acc[kAuxParts];
+#pragma unroll
+  for (int i = 0; i < kAuxParts; ++i) acc[i] = 0.f;
+  for (int64_t t = t0 + threadIdx.x; t < t1; t += kAuxThreads) {
+    float p[kMaxE], lse;
+    int top;
+    aux_softmax(logits + t * E, E, p, lse, top);
+#pragma unroll
+    for (int e = 0; e < kMaxE; ++e) acc[e] += p[e];
+    acc[kMaxE] += lse * lse;
+    atomicAdd(&cnt_s[top], 1);  // integer counts: exact in any order
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int i = 0; i < kAuxParts; ++i) {
+    const float v = warp_sum(acc[i]);
+    if (lane == 0) red[warp][i] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x < kAuxParts) {
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < kAuxThreads / 32; ++w) v += red[w][threadIdx.x];
+    part[static_cast<int64_t>(blockIdx.x) * kAuxParts + threadIdx.x] = v;
+  }
+  if (threadIdx.x < kMaxE) cnt_part[static_cast<int64_t>(blockIdx.x) * kMaxE + threadIdx.x] = cnt_s[threadIdx.x];
+}
+
+// factors[e] = c_lb * load_e / N (the load-balance term's gradient with
+// respect to probs[t, e]), factors[16] = 2 * z_coef / N (the z term's, times
+// lse_t). Missing terms (coefficient <= 0) get zero factors.
+__global__ void aux_finalize_kernel(const float* __restrict__ part, const int32_t* __restrict__ cnt_part, int chunks,
+                                    int64_t n, int E, float c_lb, float z_coef, int use_lb, int use_z,
+                                    float* __restrict__ loss, float* __restrict__ factors) {
+  __shared__ float terms[kMaxE];
+  __shared__ float zsum;
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x;  // one warp
+  float s = 0.f;
+  int c = 0;
+  if (lane < kAuxParts)
+    for (int i = 0; i < chunks; ++i) s += part[static_cast<int64_t>(i) * kAuxParts + lane];
+  if (lane < kMaxE)
+    for (int i = 0; i < chunks; ++i) c += cnt_part[static_cast<int64_t>(i) * kMaxE + lane];
+  const float nf = static_cast<float>(n);
+  if (lane < kMaxE) {
+    const float importance = s / nf;  // mean over tokens (NaN for no tokens, as torch's mean)
+    const float load = static_cast<float>(c) / static_cast<float>(n > 0 ? n : 1);
+    terms[lane] = lane < E ? load * importance : 0.f;
+    factors[lane] = (use_lb && lane < E) ? c_lb * load / nf : 0.f;
+  }
+  if (lane == kMaxE) zsum = s;
+  __syncwarp();
+  if (lane == 0) {
+    float dot = 0.f;
+    for (int e = 0; e < E; ++e) dot += terms[e];  // the sum over experts in expert order
+    const float lb = c_lb * dot;
+    const float zl = z_coef * (zsum / nf);
+    *loss = use_lb ? (use_z ? lb + zl : lb) : (use_z ? zl : 0.f);
+    factors[kMaxE] = use_z ? 2.f * z_coef / nf : 0.f;
+  }
+}
+
+// Logit gradients of the auxiliary loss for one token, written as T to
+// dl[t, 0..15] (zero past E): with G the loss's upstream gradient,
+//   d/dl_e = p_e * (G * f_e - sum_j p_j * G * f_j) + G * f_z * lse * p_e.
+template <typename T>
+__global__ void __launch_bounds__(kAuxThreads) aux_dlogit_kernel(const float* __restrict__ logits, int64_t n, int E,
+                                                                 const float* __restrict__ dloss,
+                                                                 const float* __restrict__ factors,
+                                                                 T* __restrict__ dl) {
+  pdl_wait();
+  pdl_trigger();
+  const float G = *dloss;
+  float f[kMaxE];
+#pragma unroll
+  for (int e = 0; e < kMaxE; ++e) f[e] = G * factors[e];
+  const float fz = G * factors[kMaxE];
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * kAuxThreads + threadIdx.x; t < n;
+       t += static_cast<int64_t>(gridDim.x) * kAuxThreads) {
+    float p[kMaxE], lse;
+    int top;
+    aux_softmax(logits + t * E, E, p, lse, top);
+    float dot = 0.f;
+#pragma unroll
+    for (int e = 0; e < kMaxE; ++e) dot += p[e] * f[e];
+    const float z = fz * lse;
+    float g[kMaxE];
+#pragma unroll
+    for (int e = 0; e < kMaxE; ++e) g[e] = e < E ? p[e] * (f[e] - dot) + z * p[e] : 0.f;
+    float lo[8], hi[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      lo[i] = g[i];
+      hi[i] = g[8 + i];
+    }
+    store8f<T>(dl + t * kMaxE, lo);
+    store8f<T>(dl + t * kMaxE + 8, hi);
+  }
+}
+
+// What the auxiliary-loss forward keeps for its backward (plus temporaries).
+struct AuxSaved {
+  int* err;
+  float* factors;   // [17]: per-expert load-balance factors, then the z factor
+  float* logits;    // [n, E] router logits (values of the router's dtype)
+  int32_t* idx;     // [n] top-1 expert (the router kernel's output, unused)
+  void* gates;      // [n]
+  int32_t* block_hist;
+  float* part;      // [chunks, 17]
+  int32_t* cnt_part;  // [chunks, 16]
+  size_t bytes;
+};
+
+AuxSaved carve_aux(void* ws, int64_t n, int E, int eb) {
+  Carve c(ws);
+  AuxSaved A;
+  const int chunks = aux_chunks(n);
+  A.err = c.take<int>(sizeof(int));
+  A.factors = c.take<float>(sizeof(float) * (kMaxE + 1));
+  A.logits = c.take<float>(sizeof(float) * n * E);
+  A.idx = c.take<int32_t>(sizeof(int32_t) * n);
+  A.gates = c.take<void>(static_cast<size_t>(eb) * n);
+  A.block_hist = c.take<int32_t>(sizeof(int32_t) * agm_dispatch_blocks(n) * E);
+  A.part = c.take<float>(sizeof(float) * chunks * kAuxParts);
+  A.cnt_part = c.take<int32_t>(sizeof(int32_t) * chunks * kMaxE);
+  A.bytes = c.off;
+  return A;
+}
+
+struct AuxBwd {
+  void* dl;      // [n, 16] logit gradients in the router's dtype
+  float* rpart;  // [router chunks, 16, d] weight-gradient partials
+  size_t bytes;
+};
+
+AuxBwd carve_aux_bwd(void* ws, int64_t n, int d, int eb) {
+  Carve c(ws);
+  AuxBwd B;
+  B.dl = c.take<void>(static_cast<size_t>(eb) * n * kMaxE);
+  B.rpart = c.take<float>(sizeof(float) * router_chunks(n, d) * kMaxE * d);
+  B.bytes = c.off;
+  return B;
+}
+
+cudaError_t launch_aux_forward(const AuxSaved& A, int64_t n, int E, float c_lb, float z_coef, int use_lb, int use_z,
+                               float* loss, cudaStream_t s) {
+  const int chunks = aux_chunks(n);
+  cudaError_t e = cudaSuccess;
+  if (chunks > 0)
+    e = launch_kernel(aux_stats_kernel, dim3(static_cast<unsigned>(chunks)), dim3(kAuxThreads), 0, s,
+                      static_cast<const float*>(A.logits), n, E, aux_tok_per_chunk(n), A.part, A.cnt_part);
+  if (e != cudaSuccess) return e;
+  return launch_kernel(aux_finalize_kernel, dim3(1), dim3(32), 0, s, static_cast<const float*>(A.part),
+                       static_cast<const int32_t*>(A.cnt_part), chunks, n, E, c_lb, z_coef, use_lb, use_z, loss,
+                       A.factors);
+}
+
+template <typename T>
+cudaError_t launch_aux_backward(const AuxSaved& A, const AuxBwd& B, const float* dloss, const void* x, int64_t n,
+                                int d, int E, void* dw, cudaStream_t s) {
+  const unsigned g = static_cast<unsigned>(std::min<int64_t>((n + kAuxThreads - 1) / kAuxThreads, 148 * 8));
+  cudaError_t e = launch_kernel(aux_dlogit_kernel<T>, dim3(g), dim3(kAuxThreads), 0, s,
+                                static_cast<const float*>(A.logits), n, E, dloss,
+                                static_cast<const float*>(A.factors), static_cast<T*>(B.dl));
+  if (e != cudaSuccess) return e;
+  const int chunks = router_chunks(n, d);
+  const int tpc = router_tok_per_chunk(n);
+  const int threads = std::min(512, (d / 4 + 31) / 32 * 32);
+  dim3 grid(static_cast<unsigned>(chunks), static_cast<unsigned>((d / 4 + threads - 1) / threads));
+  e = launch_kernel(router_wgrad_kernel<T>, grid, dim3(threads), 0, s, static_cast<const T*>(B.dl),
+                    static_cast<const T*>(x), static_cast<const int32_t*>(nullptr), 1, n, d, tpc, B.rpart);
+  if (e != cudaSuccess) return e;
+  const int64_t count = static_cast<int64_t>(E) * d;
+  const unsigned g2 = static_cast<unsigned>(std::min<int64_t>((count + 255) / 256, 148 * 4));
+  return launch_kernel(reduce_partials_kernel<T, T>, dim3(g2), dim3(256), 0, s, static_cast<const float*>(B.rpart),
+                       chunks, static_cast<int64_t>(kMaxE) * d, count, static_cast<T*>(dw));
+}
+
 }  // namespace
 }  // namespace agm
 
@@ -1356,6 +1600,88 @@ int agm_moe_backward(const void* dout, int x_dtype, int dtype, int64_t n_tokens,
               : agm::launch_dx<__half, __half>(B, S, w_router, n_tokens, d, top_k, n_experts, n_shared, dx, stream);
   }
   return e == cudaSuccess ? AGM_OK : agm::cuda_fail(e, "dx");
+}
+
+// ---------------------------------------------------------------------------
+// Auxiliary router losses (agillm41.py:4463-4492).
+// ---------------------------------------------------------------------------
+static int check_aux_args(int dtype, int64_t n, int d, int E) {
+  if (!agm::esize(dtype)) return agm::fail(AGM_ERR_ARG, "dtype must be AGM_F32, AGM_BF16 or AGM_F16");
+  if (n < 0 || n > (int64_t(1) << 31) - 1) return agm::fail(AGM_ERR_ARG, "n_tokens out of range");
+  if (d <= 0 || d % 8) return agm::fail(AGM_ERR_ARG, "d must be a positive multiple of 8");
+  if (E < 1 || E > AGM_MAX_EXPERTS) return agm::fail(AGM_ERR_UNSUPPORTED, "n_experts must be in [1, 16]");
+  return AGM_OK;
+}
+
+size_t agm_moe_aux_saved_bytes(int64_t n_tokens, int n_experts, int dtype) {
+  const int eb = agm::esize(dtype);
+  if (!eb || n_tokens < 0 || n_experts < 1) return 0;
+  return agm::carve_aux(nullptr, n_tokens, n_experts, eb).bytes;
+}
+
+size_t agm_moe_aux_backward_workspace_bytes(int64_t n_tokens, int d, int dtype) {
+  const int eb = agm::esize(dtype);
+  if (!eb || n_tokens < 0 || d <= 0) return 0;
+  return agm::carve_aux_bwd(nullptr, n_tokens, d, eb).bytes;
+}
+
+int agm_moe_aux_forward(const void* x, int dtype, int64_t n_tokens, int d, int n_experts, const void* w_router,
+                        double aux_coef, double z_coef, float* loss_out, void* saved, size_t saved_bytes, int flags,
+                        void* stream_) {
+  int rc = check_aux_args(dtype, n_tokens, d, n_experts);
+  if (rc) return rc;
+  if ((n_tokens > 0 && !x) || !w_router || !loss_out || !saved) return agm::fail(AGM_ERR_ARG, "null pointer");
+  if (!agm::al16(x) || !agm::al16(w_router) || !agm::al16(saved))
+    return agm::fail(AGM_ERR_ARG, "x, w_router and saved must be 16-byte aligned");
+  const int eb = agm::esize(dtype);
+  agm::AuxSaved A = agm::carve_aux(saved, n_tokens, n_experts, eb);
+  if (A.bytes > saved_bytes) return agm::fail(AGM_ERR_WORKSPACE, "saved-state buffer too small");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  agm::PdlScope pdl_scope(!(flags & AGM_FLAG_NO_PDL));
+  cudaError_t e = cudaMemsetAsync(A.err, 0, sizeof(int), stream);
+  if (e != cudaSuccess) return agm::cuda_fail(e, "memset");
+  if (n_tokens > 0) {
+    e = agm::router_topk(dtype, x, w_router, n_tokens, d, n_experts, 1, 1, nullptr, A.logits, A.idx, A.gates,
+                         A.block_hist, A.err, agm::sm_count(), stream);
+    if (e != cudaSuccess) return agm::cuda_fail(e, "router");
+  }
+  // The reference multiplies by the Python product aux_coef * num_experts.
+  const float c_lb = static_cast<float>(aux_coef * n_experts);
+  e = agm::launch_aux_forward(A, n_tokens, n_experts, c_lb, static_cast<float>(z_coef), aux_coef > 0, z_coef > 0,
+                              loss_out, stream);
+  return e == cudaSuccess ? AGM_OK : agm::cuda_fail(e, "aux loss");
+}
+
+int agm_moe_aux_backward(const float* dloss, const void* x, int dtype, int64_t n_tokens, int d, int n_experts,
+                         const void* saved, size_t saved_bytes, void* dw_router, void* workspace,
+                         size_t workspace_bytes, int flags, void* stream_) {
+  int rc = check_aux_args(dtype, n_tokens, d, n_experts);
+  if (rc) return rc;
+  if (!dloss || !saved || !dw_router || (n_tokens > 0 && (!x || !workspace)))
+    return agm::fail(AGM_ERR_ARG, "null pointer");
+  if (!agm::al16(x) || !agm::al16(saved) || !agm::al16(dw_router) || !agm::al16(workspace))
+    return agm::fail(AGM_ERR_ARG, "x, saved, dw_router and workspace must be 16-byte aligned");
+  const int eb = agm::esize(dtype);
+  agm::AuxSaved A = agm::carve_aux(const_cast<void*>(saved), n_tokens, n_experts, eb);
+  if (A.bytes > saved_bytes) return agm::fail(AGM_ERR_WORKSPACE, "saved-state buffer too small");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  cudaError_t e;
+  if (n_tokens == 0) {
+    // No tokens: the router weight's gradient is an empty sum.
+    e = cudaMemsetAsync(dw_router, 0, static_cast<size_t>(eb) * n_experts * d, stream);
+    return e == cudaSuccess ? AGM_OK : agm::cuda_fail(e, "memset");
+  }
+  agm::AuxBwd B = agm::carve_aux_bwd(workspace, n_tokens, d, eb);
+  if (B.bytes > workspace_bytes) return agm::fail(AGM_ERR_WORKSPACE, "workspace too small");
+  agm::PdlScope pdl_scope(!(flags & AGM_FLAG_NO_PDL));
+  switch (dtype) {
+    case AGM_F32: e = agm::launch_aux_backward<float>(A, B, dloss, x, n_tokens, d, n_experts, dw_router, stream); break;
+    case AGM_BF16:
+      e = agm::launch_aux_backward<__nv_bfloat16>(A, B, dloss, x, n_tokens, d, n_experts, dw_router, stream);
+      break;
+    default: e = agm::launch_aux_backward<__half>(A, B, dloss, x, n_tokens, d, n_experts, dw_router, stream);
+  }
+  return e == cudaSuccess ? AGM_OK : agm::cuda_fail(e, "aux loss backward");
 }
 
 }  // extern "C"

@@ -119,6 +119,69 @@ class _MoETrainNode(torch.autograd.Function):
         return (dx if ctx.needs_input_grad[0] else None, dres, dwr if ctx.needs_input_grad[2] else None, None, *grads)
 
 
+class _MoEAuxNode(torch.autograd.Function):
+    """Auxiliary router losses of one MoE module (agillm41.py:4477-4491) on the
+    B200 kernels: ``agm_moe_aux_forward`` recomputes the router logits from the
+    stashed input and reduces the load-balance and router-z terms to one fp32
+    scalar; ``agm_moe_aux_backward`` gives the router weight's gradient (the
+    stashed input is detached in the reference, so it gets none).
+
+    ``cdt`` is the autocast dtype when the call runs under torch.autocast (the
+    router Linear then computes in 16 bits on casts of the fp32 input and
+    weight, and the weight's gradient comes back through the cast), else None.
+    """
+
+    @staticmethod
+    def forward(ctx, w_router, x, aux_coef, z_coef, cdt, check):
+        wc, xc = w_router, x
+        if cdt is not None and w_router.dtype != cdt:
+            wc = ops.cast_f32(w_router, cdt) if w_router.dtype == torch.float32 else w_router.to(cdt)
+        if xc.dtype != wc.dtype:
+            xc = ops.cast_f32(xc, wc.dtype) if xc.dtype == torch.float32 else xc.to(wc.dtype)
+        loss, saved = ops.moe_aux_forward(xc.contiguous(), wc.contiguous(), aux_coef, z_coef, check_errors=check)
+        ctx.save_for_backward(saved, xc, wc)
+        ctx.w_dtype = w_router.dtype
+        return loss
+
+    @staticmethod
+    def backward(ctx, gl):
+        saved, xc, wc = ctx.saved_tensors
+        dw = ops.moe_aux_backward(gl, xc, wc, saved)
+        if dw.dtype != ctx.w_dtype:
+            dw = dw.to(ctx.w_dtype)  # the autocast cast's backward
+        return dw, None, None, None, None, None
+
+
+def collect_moe_aux(model, aux_coef=0.0, z_coef=0.0):
+    """``_collect_moe_aux`` (agillm41.py:4463-4492) with each module's losses
+    computed by the fused auxiliary-loss kernels: sum and clear the
+    load-balance / router-z losses of every B200 MoE module in ``model``.
+
+    Same contract as the reference: the router is recomputed on the detached
+    input each module stashed during its training forward (so it works with
+    gradient checkpointing and only ``router.weight`` gets a gradient), every
+    stash is cleared, and the result is a scalar fp32 tensor to add to the
+    loss before ``backward()``, or 0.0 when both coefficients are <= 0 or
+    nothing was stashed. The module losses are added in module order.
+    """
+    total = None
+    for m in model.modules():
+        if isinstance(m, _B200Forward):
+            inp = m.last_router_input
+            m.last_router_input = None
+            if inp is None or (aux_coef <= 0 and z_coef <= 0):
+                continue
+            w = m.router.weight
+            router_in = inp.to(w.dtype) if inp.dtype != w.dtype else inp  # agillm41.py:4481
+            if router_in.device.type != "cuda":
+                raise MoEKernelError("collect_moe_aux: the stashed router input is not a CUDA tensor")
+            flat = router_in.reshape(-1, router_in.shape[-1])
+            loss = _MoEAuxNode.apply(w, flat, float(aux_coef), float(z_coef), _autocast_dtype(flat.device),
+                                     bool(m.check_device_errors))
+            total = loss if total is None else total + loss
+    return total if total is not None else 0.0
+
+
 class _B200Forward:
     """Forward of the MoE block on the B200 kernels (mixed into the module classes)."""
 
@@ -473,7 +536,7 @@ def _fused_block_forward(self, x, mask, kv=None, use_cache=False, total_seq_len=
     return ff.forward_residual(self.ln2(x), x)
 
 
-def install(agillm41_module, name: str = "MoEFFN", fuse_residual: bool = False):
+def install(agillm41_module, name: str = "MoEFFN", fuse_residual: bool = False, fuse_aux: bool = True):
     """Rebind ``agillm41_module.MoEFFN`` to a subclass of the reference class
     whose forward runs on the B200 kernels. Returns the new class.
 
@@ -485,6 +548,10 @@ def install(agillm41_module, name: str = "MoEFFN", fuse_residual: bool = False):
     ``fuse_residual``: also rebind ``Block`` to a subclass whose forward adds
     the residual inside the MoE block's combine kernel (same values and
     gradients, one elementwise pass less per layer).
+
+    ``fuse_aux``: also rebind ``_collect_moe_aux`` (called by the training
+    steps, agillm41.py:1378, 6798) to :func:`collect_moe_aux`, which computes
+    the auxiliary router losses of the B200 modules with the fused kernels.
     """
     ref_cls = getattr(agillm41_module, name)
     if getattr(ref_cls, "_is_b200", False):
@@ -499,6 +566,14 @@ def install(agillm41_module, name: str = "MoEFFN", fuse_residual: bool = False):
                                          "_reference_block_forward": block.forward,
                                          "forward": _fused_block_forward, "__module__": block.__module__})
         setattr(agillm41_module, "Block", fused)
+    aux = getattr(agillm41_module, "_collect_moe_aux", None)
+    if fuse_aux and aux is not None and not getattr(aux, "_is_b200", False):
+        def _collect(model, aux_coef=0.0, z_coef=0.0):
+            return collect_moe_aux(model, aux_coef, z_coef)
+        _collect._is_b200 = True
+        _collect._reference_function = aux
+        _collect.__doc__ = collect_moe_aux.__doc__
+        setattr(agillm41_module, "_collect_moe_aux", _collect)
     return cls
 
 
@@ -507,3 +582,6 @@ def uninstall(agillm41_module, name: str = "MoEFFN") -> None:
         cls = getattr(agillm41_module, attr, None)
         if getattr(cls, "_is_b200", False):
             setattr(agillm41_module, attr, cls._reference_class)
+    aux = getattr(agillm41_module, "_collect_moe_aux", None)
+    if getattr(aux, "_is_b200", False):
+        setattr(agillm41_module, "_collect_moe_aux", aux._reference_function)

@@ -434,3 +434,45 @@ def moe_backward(dout: torch.Tensor, saved: torch.Tensor, w_router: torch.Tensor
     if S:
         return dx, dwr, dw1, db1, dw2, db2, sg
     return dx, dwr, dw1, db1, dw2, db2
+
+
+def moe_aux_forward(x: torch.Tensor, w_router: torch.Tensor, aux_coef: float, z_coef: float, *,
+                    check_errors: bool = False):
+    """Load-balance + router-z loss of one MoE module (agillm41.py:4477-4491):
+    x [N, d] in the router weight's dtype -> (loss, a 0-d fp32 CUDA tensor;
+    saved uint8 buffer for :func:`moe_aux_backward`)."""
+    lib = load()
+    n, d = x.shape
+    E = w_router.shape[0]
+    dev = x.device
+    dt = dtype_code(w_router.dtype)
+    x = x.contiguous()
+    saved = torch.empty(max(int(lib.agm_moe_aux_saved_bytes(n, E, dt)), 256), dtype=torch.uint8, device=dev)
+    loss = torch.empty((), dtype=torch.float32, device=dev)
+    rc = lib.agm_moe_aux_forward(ptr(x), dt, n, d, E, ptr(w_router.contiguous()), float(aux_coef), float(z_coef),
+                                 ptr(loss), ptr(saved), saved.numel(), 0, stream_handle(dev))
+    check(rc, "agm_moe_aux_forward")
+    if check_errors:
+        code = _lib.read_device_error(saved[:4].view(torch.int32))
+        if code:
+            raise _lib.MoEKernelError(f"device error word 0x{code:x} after agm_moe_aux_forward")
+    return loss, saved
+
+
+def moe_aux_backward(dloss: torch.Tensor, x: torch.Tensor, w_router: torch.Tensor, saved: torch.Tensor
+                     ) -> torch.Tensor:
+    """Router weight gradient [E, d] (the weight's dtype) of the loss of
+    :func:`moe_aux_forward`, given its upstream gradient ``dloss`` (0-d)."""
+    lib = load()
+    n, d = x.shape
+    E = w_router.shape[0]
+    dev = x.device
+    dt = dtype_code(w_router.dtype)
+    g = dloss.to(device=dev, dtype=torch.float32).reshape(1).contiguous()
+    dw = torch.empty(E, d, dtype=w_router.dtype, device=dev)
+    ws = torch.empty(max(int(lib.agm_moe_aux_backward_workspace_bytes(n, d, dt)), 256), dtype=torch.uint8,
+                     device=dev)
+    rc = lib.agm_moe_aux_backward(ptr(g), ptr(x.contiguous()), dt, n, d, E, ptr(saved), saved.numel(), ptr(dw),
+                                  ptr(ws), ws.numel(), 0, stream_handle(dev))
+    check(rc, "agm_moe_aux_backward")
+    return dw

@@ -307,6 +307,7 @@ def run_ours(args, world, rank, local):
                                         shared_hidden=2 * D, batch=22, seq=1536,
                                         label="production MoE block training step")
         train["production"]["forward"] = run_forward_production(args, dev, stream)
+        train["aux_loss"] = run_aux(args, dev, stream)
     report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e_value, x, decode, train)
 
 
@@ -417,6 +418,48 @@ def run_train(args, dev, stream, *, experts=EXPERTS, hidden=HIDDEN, top_k=TOP_K,
                          "note": "all expert GEMMs' FLOPs over the whole step time (casts, router, permute, "
                                  "combine and their backward included), so a lower bound on the GEMMs' own rate"},
             "gpu_launches_per_step": launches}
+
+
+def run_aux(args, dev, stream):
+    """Auxiliary router losses (_collect_moe_aux, agillm41.py:4463-4492) as the
+    autocast trainer calls them after its forward: the fp32 stashed router
+    input of B x L tokens and the fp32 router weight, load-balance 0.01 and
+    router-z 0.001 (the production run's coefficients, agillm41.py:8591); one
+    step = agm_moe_aux_forward + agm_moe_aux_backward. Each reads the input
+    once: 2 x N x d x 4 bytes of algorithmic traffic (plus the [N, E] logits,
+    written once and read twice)."""
+    from agillm41_b200 import ops, synthetic
+
+    N = BATCH * SEQ if args.tokens == BATCH * SEQ else args.tokens
+    w = synthetic.make_state(D, D, EXPERTS, SEED, dtype=torch.float32, device=dev)["router.weight"].contiguous()
+    x = synthetic.make_input(N, D, SEED, dtype=torch.float32, device=dev)
+    g = torch.ones((), device=dev)
+
+    def step():
+        loss, saved = ops.moe_aux_forward(x, w, 0.01, 0.001)
+        return loss, ops.moe_aux_backward(g, x, w, saved)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    steps = max(10, min(args.steps, 100))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    peaks = load_peaks()
+    nbytes = 2 * N * D * 4 + 3 * N * EXPERTS * 4
+    gbs = nbytes / (ms / 1000.0) / 1e9
+    return {"workload": f"MoE auxiliary losses forward + backward, {N} tokens d{D} E{EXPERTS}, fp32 stash and "
+                        f"router weight, aux 0.01 z 0.001, seed {SEED}",
+            "ms_per_step": round(ms, 4), "steps": steps,
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm"], "unit": "GB/s",
+                         "frac": round(gbs / peaks["hbm"], 3),
+                         "note": "the input read once by each pass plus the logits, over both passes' time"},
+            "gpu_launches_per_step": 6}
 
 
 def run_ep(args, world, rank, local):

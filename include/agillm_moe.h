@@ -347,6 +347,29 @@ AGM_API int agm_moe_backward(const void* dout, int x_dtype, int dtype, int64_t n
                              void* dws1, void* dsb1, void* dws2, void* dsb2, void* workspace, size_t workspace_bytes,
                              int flags, void* stream);
 
+/* ---- Auxiliary router losses --------------------------------------------
+ * Replaces the per-module body of _collect_moe_aux (agillm41.py:4463-4492):
+ * recompute the router logits from the stashed FFN input x [n_tokens, d]
+ * (dtype = the router weight's dtype, as `inp.to(router.weight.dtype)`), then
+ *   loss = aux_coef * E * sum_e(load_e * importance_e)      if aux_coef > 0
+ *        + z_coef * mean_t(logsumexp(logits_t)^2)           if z_coef > 0
+ * with importance = mean over tokens of softmax(logits), load_e = the
+ * fraction of tokens whose softmax argmax is e (no gradient). loss_out is one
+ * device float; 0 when both coefficients are <= 0, NaN for no tokens (as
+ * torch's mean of nothing). Sums run in a fixed order: the loss is
+ * deterministic. The backward reads the upstream gradient of the loss from
+ * device memory (dloss, one float) and writes the router weight's gradient
+ * dw_router [E, d] in dtype (the input x is not differentiated: the reference
+ * detaches it). */
+AGM_API size_t agm_moe_aux_saved_bytes(int64_t n_tokens, int n_experts, int dtype);
+AGM_API size_t agm_moe_aux_backward_workspace_bytes(int64_t n_tokens, int d, int dtype);
+AGM_API int agm_moe_aux_forward(const void* x, int dtype, int64_t n_tokens, int d, int n_experts,
+                                const void* w_router, double aux_coef, double z_coef, float* loss_out, void* saved,
+                                size_t saved_bytes, int flags, void* stream);
+AGM_API int agm_moe_aux_backward(const float* dloss, const void* x, int dtype, int64_t n_tokens, int d,
+                                 int n_experts, const void* saved, size_t saved_bytes, void* dw_router,
+                                 void* workspace, size_t workspace_bytes, int flags, void* stream);
+
 /* Synchronise `stream`, read the device error word at `err` (e.g. the first
  * int of a forward workspace) into *code and reset it to 0. Returns AGM_OK if
  * the word was 0, AGM_ERR_DEVICE otherwise.                                */

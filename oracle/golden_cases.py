@@ -54,6 +54,33 @@ GRAD_CASES = [
 ]
 
 
+# Auxiliary-loss golden cases (_collect_moe_aux, agillm41.py:4463-4492):
+# (name, d, experts, n_tokens, seed, dtype, aux_coef, z_coef, modules,
+#  upstream gradient, special). "zero_rows" zeroes every 7th input row, so
+# those tokens' probabilities tie and argmax takes the first expert.
+AUX_CASES = [
+    ("aux_lb_z_fp32_e14_n300", 64, 14, 300, 61, torch.float32, 0.01, 0.001, 1, 1.0, None),
+    ("aux_lb_z_bf16_e2_n257", 64, 2, 257, 62, torch.bfloat16, 0.01, 0.001, 1, 1.0, None),
+    ("aux_lb_only_fp32_e8_n128", 64, 8, 128, 63, torch.float32, 0.05, 0.0, 1, 1.0, None),
+    ("aux_z_only_fp32_e16_n96", 64, 16, 96, 64, torch.float32, 0.0, 0.01, 1, 1.0, None),
+    ("aux_two_modules_fp32_e4_n200", 64, 4, 200, 65, torch.float32, 0.01, 0.001, 2, 1024.0, None),
+    ("aux_ties_fp32_e6_n140", 64, 6, 140, 66, torch.float32, 0.02, 0.002, 1, 1.0, "zero_rows"),
+]
+
+
+def aux_case_inputs(case):
+    """Return [(fp32 stashed input [N, d], fp32 router weight [E, d])] per module."""
+    (name, d, E, N, seed, dtype, aux_coef, z_coef, modules, gscale, special) = case
+    out = []
+    for i in range(modules):
+        w = orc.make_state(d, d, E, seed + 100 * i, dtype=torch.float32)["router.weight"]
+        x = orc.make_input(N, d, seed + 100 * i)
+        if special == "zero_rows":
+            x[::7] = 0
+        out.append((x, w))
+    return out
+
+
 def grad_output(case):
     """Seeded upstream gradient dL/dout [N, d] (fp32) of a gradient case."""
     (name, d, H, E, k, N, seed, dtype, shared, shared_H, bias_std, special, store_w) = case
@@ -84,7 +111,7 @@ def special_state(sd, special, experts):
 
 
 def case_by_name(name: str):
-    for c in CASES + GRAD_CASES:
+    for c in CASES + GRAD_CASES + AUX_CASES:
         if c[0] == name:
             return c
     raise KeyError(name)

@@ -14,6 +14,7 @@ Follows ``MoEFFN`` in the reference's ``agillm41.py``:
       ``* weight`` / ``index_add_`` into ``zeros_like(flat)``  4420-4428
     - shared experts: ``s = shared[0](flat); s = s + shared[i](flat)``,
       ``out = out + s``                                     4381-4387, 4429-4430
+* ``_collect_moe_aux`` (load-balance and router-z losses)  agillm41.py:4463-4492
 
 The restatement uses exactly the same torch calls in the same order as the
 reference, so on the same device and dtype it reproduces the reference bit for
@@ -146,6 +147,44 @@ def moe_forward(x: torch.Tensor, sd: Mapping[str, torch.Tensor], top_k: int,
         aux["counts"] = torch.bincount(idx.reshape(-1), minlength=E)
         aux["term_scale"] = scale.reshape(orig_shape)
     return out.reshape(orig_shape)
+
+
+def collect_moe_aux(router_inputs, router_weights, aux_coef: float = 0.0, z_coef: float = 0.0,
+                    scores_override=None):
+    """Restatement of ``_collect_moe_aux`` (agillm41.py:4463-4492) over the
+    (stashed router input, router weight) pairs of the MoE modules in module
+    order: the load-balance loss ``aux_coef * E * sum(load * importance)`` and
+    the router-z loss ``z_coef * mean(logsumexp(scores) ** 2)`` with the same
+    torch calls in the same order (the router is the bias-free Linear of
+    agillm41.py:4332), so autograd through it gives the reference's gradients.
+    An input of None (nothing stashed) is skipped. Returns a scalar tensor or
+    0.0.
+
+    ``scores_override`` (test-only, one entry per module or None): the given
+    fp32 logit values replace the router's in the forward while the gradient
+    still flows through the reference's router Linear, so that a kernel
+    whose logits round differently can be compared on identical argmax."""
+    total = None
+    overrides = scores_override if scores_override is not None else [None] * len(router_inputs)
+    for inp, w, ov in zip(router_inputs, router_weights, overrides):
+        if inp is None or (aux_coef <= 0 and z_coef <= 0):                 # 4478
+            continue
+        router_in = inp.to(w.dtype) if inp.dtype != w.dtype else inp        # 4481
+        scores = F.linear(router_in, w).float()                             # 4482
+        if ov is not None:
+            scores = _ValueOf.apply(scores, ov)
+        probs = scores.softmax(dim=-1)                                      # 4483
+        importance = probs.mean(dim=0)                                      # 4484
+        top1 = probs.argmax(dim=-1)                                         # 4485
+        n_exp = w.shape[0]
+        load = torch.bincount(top1, minlength=n_exp).to(importance.dtype) / max(1, top1.numel())  # 4486
+        if aux_coef > 0:
+            lb = aux_coef * n_exp * (load.detach() * importance).sum()     # 4487-4489
+            total = lb if total is None else total + lb
+        if z_coef > 0:
+            zl = z_coef * (torch.logsumexp(scores, dim=-1) ** 2).mean()     # 4490-4491
+            total = zl if total is None else total + zl
+    return total if total is not None else 0.0
 
 
 # Seeded synthetic weights and inputs (the workload definitions) live in the

@@ -12,8 +12,18 @@ GOLDEN_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 DTYPES = {"float32": torch.float32, "bfloat16": torch.bfloat16, "float16": torch.float16}
 
 
-def names():
+def _all_names():
     return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz")))
+
+
+def names():
+    """Forward (and gradient) cases of the MoE block."""
+    return [n for n in _all_names() if not n.startswith("aux_")]
+
+
+def aux_names():
+    """Auxiliary-loss cases (tests/golden/make_golden_aux.py)."""
+    return [n for n in _all_names() if n.startswith("aux_")]
 
 
 def _to_np(t):
@@ -110,3 +120,33 @@ class GoldenGrad(Golden):
             g[f"experts.{e}.2.bias"] = self.d_b2[e]
         g.update(self.shared_grads)
         return g
+
+
+class GoldenAux:
+    """An auxiliary-loss case: per module the stashed router input and router
+    weight (as stored, and as regenerated from the seeds), the reference's
+    loss and its router weight gradients for the stored upstream gradient."""
+
+    def __init__(self, name):
+        from oracle.golden_cases import aux_case_inputs
+
+        self.name = name
+        z = self.z = np.load(os.path.join(GOLDEN_DIR, name + ".npz"))
+        self.case = case_by_name(name)
+        self.dtype = DTYPES[str(z["dtype"])]
+        self.E = int(z["experts"])
+        self.d = int(z["d"])
+        self.N = int(z["n_tokens"])
+        self.aux_coef = float(z["aux_coef"])
+        self.z_coef = float(z["z_coef"])
+        self.upstream = float(z["upstream"])
+        self.modules = int(z["modules"])
+        self.xs = [from_np(z[f"x{i}"], self.dtype) for i in range(self.modules)]
+        self.ws = [from_np(z[f"w{i}"], self.dtype) for i in range(self.modules)]
+        self.d_router = [from_np(z[f"d_router{i}"], self.dtype) for i in range(self.modules)]
+        self.loss = torch.tensor(float(z["loss"]), dtype=torch.float32)
+        self.regenerated = [(x.to(self.dtype), w.to(self.dtype)) for x, w in aux_case_inputs(self.case)]
+
+    def inputs_match(self):
+        return all(torch.equal(x, xr) and torch.equal(w, wr)
+                   for x, w, (xr, wr) in zip(self.xs, self.ws, self.regenerated))

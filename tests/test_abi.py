@@ -137,6 +137,33 @@ def test_training_entry_points_validate_without_a_device():
     assert lib.agm_cast_f32(fake, fake, _lib.AGM_F32, 16, None) == -1
 
 
+def test_aux_entry_points_validate_without_a_device():
+    lib = _lib.load()
+    fake = ctypes.c_void_p(4096)
+    n, d, E = 1000, 64, 14
+    need = lib.agm_moe_aux_saved_bytes(n, E, _lib.AGM_F32)
+    assert need >= n * E * 4                          # the fp32 logits are kept
+    assert lib.agm_moe_aux_saved_bytes(-1, E, _lib.AGM_F32) == 0
+    assert lib.agm_moe_aux_backward_workspace_bytes(n, d, _lib.AGM_BF16) >= n * 16 * 2
+    fwd = [fake, _lib.AGM_F32, n, d, E, fake, 0.01, 0.001, fake, fake]
+    assert lib.agm_moe_aux_forward(*fwd, 1024, 0, None) == -5
+    assert "saved" in lib.agm_last_error().decode()
+    bad = list(fwd)
+    bad[4] = 17
+    assert lib.agm_moe_aux_forward(*bad, need, 0, None) == -2
+    bad = list(fwd)
+    bad[3] = 12
+    assert lib.agm_moe_aux_forward(*bad, need, 0, None) == -1
+    bad = list(fwd)
+    bad[8] = None
+    assert lib.agm_moe_aux_forward(*bad, need, 0, None) == -1
+    bad = list(fwd)
+    bad[0] = ctypes.c_void_p(4096 + 4)
+    assert lib.agm_moe_aux_forward(*bad, need, 0, None) == -1
+    rc = lib.agm_moe_aux_backward(fake, fake, _lib.AGM_F32, n, d, E, fake, need, fake, fake, 1024, 0, None)
+    assert rc == -5 and "workspace" in lib.agm_last_error().decode()
+
+
 def test_training_forward_refuses_cpu_tensors():
     import torch
 

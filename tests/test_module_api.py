@@ -106,6 +106,34 @@ def test_install_into_reference(ref):
     assert not getattr(ref.MoEFFN, "_is_b200", False)
 
 
+def test_install_rebinds_collect_moe_aux(ref):
+    """install() rebinds _collect_moe_aux to the fused version (the training
+    steps call it through the module global, agillm41.py:1378, 6798); its
+    host-side contract is the reference's: stashes are cleared, 0.0 when
+    nothing is stashed or both coefficients are <= 0, CPU tensors refused."""
+    orig = ref._collect_moe_aux
+    agillm41_b200.install(ref)
+    try:
+        assert ref._collect_moe_aux is not orig and ref._collect_moe_aux._is_b200
+        model = torch.nn.ModuleList([ref.MoEFFN(64, experts=4, top_k=1), ref.MoEFFN(64, experts=4, top_k=1)])
+        assert ref._collect_moe_aux(model, 0.01, 0.001) == 0.0
+        model[0].last_router_input = torch.randn(8, 64)
+        assert ref._collect_moe_aux(model, 0.0, 0.0) == 0.0
+        assert model[0].last_router_input is None
+        model[1].last_router_input = torch.randn(8, 64)
+        with pytest.raises(MoEKernelError):
+            ref._collect_moe_aux(model, 0.01, 0.0)   # CPU tensor: no fallback
+        assert model[1].last_router_input is None
+    finally:
+        agillm41_b200.uninstall(ref)
+    assert ref._collect_moe_aux is orig
+    agillm41_b200.install(ref, fuse_aux=False)
+    try:
+        assert ref._collect_moe_aux is orig
+    finally:
+        agillm41_b200.uninstall(ref)
+
+
 def test_fused_residual_block(ref):
     """install(fuse_residual=True) rebinds Block to a subclass whose MoE
     residual add runs in the combine kernel; other FFNs keep the reference's
