@@ -457,6 +457,46 @@ __global__ void __launch_bounds__(512) router_wgrad_kernel(const T* __restrict__
         make_float4(acc[e][0], acc[e][1], acc[e][2], acc[e][3]);
 }
 
+// The same sum for many partials (the router weight gradient's per-chunk
+// partials): a CTA owns 32 consecutive outputs; warp w adds the partials
+// p = w, w + 8, w + 16, ... in order (coalesced 128-byte rows, four loads in
+// flight), then warp 0 adds the 8 warp sums in warp order. The order depends
+// on `parts` only: deterministic.
+template <typename T, typename OutT>
+__global__ void __launch_bounds__(256) reduce_partials_wide_kernel(const float* __restrict__ partial, int parts,
+                                                                   int64_t part_stride, int64_t count,
+                                                                   OutT* __restrict__ out) {
+  __shared__ float red[8][32];
+  pdl_wait();
+  pdl_trigger();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * 32 + lane;
+  float v = 0.f;
+  if (i < count) {
+    int p = warp;
+    for (; p + 24 < parts; p += 32) {
+      const float a = partial[p * part_stride + i];
+      const float b = partial[(p + 8) * part_stride + i];
+      const float c = partial[(p + 16) * part_stride + i];
+      const float d = partial[(p + 24) * part_stride + i];
+      v = (((v + a) + b) + c) + d;
+    }
+    for (; p < parts; p += 8) v += partial[p * part_stride + i];
+  }
+  red[warp][lane] = v;
+  __syncthreads();
+  if (warp == 0 && i < count) {
+    float t = red[0][lane];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) t += red[w][lane];
+    const float r = round_to<T>(t);
+    if constexpr (sizeof(OutT) == 4)
+      out[i] = r;
+    else
+      out[i] = Traits<OutT>::from_f(r);
+  }
+}
+
 // Bias gradient from the dgrad kernel's per-quarter column sums:
 // out[e, c] = r_T(sum over the 128-row tiles of expert e's segment and their
 // four quarters of part[(tile * 4 + q) * n + c]), in tile order.
@@ -851,10 +891,9 @@ cudaError_t launch_router_wgrad(const BwdWs& B, const Saved& S, int64_t n, int d
   // Chunk c's partial is [16, d] at c * 16 * d; its first E rows, E * d
   // contiguous values, are the router weight's.
   const int64_t count = static_cast<int64_t>(E) * d;
-  const unsigned g2 = static_cast<unsigned>(std::min<int64_t>((count + 255) / 256, 148 * 4));
-  return launch_kernel(reduce_partials_kernel<T, OutT>, dim3(g2), dim3(256), 0, s,
-                       static_cast<const float*>(B.rpart), chunks, static_cast<int64_t>(kMaxE) * d, count,
-                       static_cast<OutT*>(dwr));
+  return launch_kernel(reduce_partials_wide_kernel<T, OutT>, dim3(static_cast<unsigned>((count + 31) / 32)),
+                       dim3(256), 0, s, static_cast<const float*>(B.rpart), chunks,
+                       static_cast<int64_t>(kMaxE) * d, count, static_cast<OutT*>(dwr));
 }
 
 template <typename T, typename G>
@@ -979,20 +1018,37 @@ __global__ void __launch_bounds__(kAuxThreads) aux_stats_kernel(const float* __r
 // factors[e] = c_lb * load_e / N (the load-balance term's gradient with
 // respect to probs[t, e]), factors[16] = 2 * z_coef / N (the z term's, times
 // lse_t). Missing terms (coefficient <= 0) get zero factors.
-__global__ void aux_finalize_kernel(const float* __restrict__ part, const int32_t* __restrict__ cnt_part, int chunks,
-                                    int64_t n, int E, float c_lb, float z_coef, int use_lb, int use_z,
-                                    float* __restrict__ loss, float* __restrict__ factors) {
+__global__ void __launch_bounds__(512) aux_finalize_kernel(const float* __restrict__ part,
+                                                            const int32_t* __restrict__ cnt_part, int chunks,
+                                                            int64_t n, int E, float c_lb, float z_coef, int use_lb,
+                                                            int use_z, float* __restrict__ loss,
+                                                            float* __restrict__ factors) {
+  // Warp w adds chunks w, w + 16, ... (lane < 17: the float partials, lane
+  // 17..32 reads nothing); then warp 0 adds the 16 warp sums in warp order.
+  __shared__ float red_s[16][32];
+  __shared__ int red_c[16][32];
   __shared__ float terms[kMaxE];
   __shared__ float zsum;
   pdl_wait();
   pdl_trigger();
-  const int lane = threadIdx.x;  // one warp
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float s = 0.f;
   int c = 0;
-  if (lane < kAuxParts)
-    for (int i = 0; i < chunks; ++i) s += part[static_cast<int64_t>(i) * kAuxParts + lane];
-  if (lane < kMaxE)
-    for (int i = 0; i < chunks; ++i) c += cnt_part[static_cast<int64_t>(i) * kMaxE + lane];
+  for (int i = warp; i < chunks; i += 16) {
+    if (lane < kAuxParts) s += part[static_cast<int64_t>(i) * kAuxParts + lane];
+    if (lane < kMaxE) c += cnt_part[static_cast<int64_t>(i) * kMaxE + lane];
+  }
+  red_s[warp][lane] = s;
+  red_c[warp][lane] = c;
+  __syncthreads();
+  if (warp != 0) return;
+  s = 0.f;
+  c = 0;
+#pragma unroll
+  for (int w = 0; w < 16; ++w) {
+    s += red_s[w][lane];
+    c += red_c[w][lane];
+  }
   const float nf = static_cast<float>(n);
   if (lane < kMaxE) {
     const float importance = s / nf;  // mean over tokens (NaN for no tokens, as torch's mean)
@@ -1102,7 +1158,7 @@ cudaError_t launch_aux_forward(const AuxSaved& A, int64_t n, int E, float c_lb, 
     e = launch_kernel(aux_stats_kernel, dim3(static_cast<unsigned>(chunks)), dim3(kAuxThreads), 0, s,
                       static_cast<const float*>(A.logits), n, E, aux_tok_per_chunk(n), A.part, A.cnt_part);
   if (e != cudaSuccess) return e;
-  return launch_kernel(aux_finalize_kernel, dim3(1), dim3(32), 0, s, static_cast<const float*>(A.part),
+  return launch_kernel(aux_finalize_kernel, dim3(1), dim3(512), 0, s, static_cast<const float*>(A.part),
                        static_cast<const int32_t*>(A.cnt_part), chunks, n, E, c_lb, z_coef, use_lb, use_z, loss,
                        A.factors);
 }
@@ -1123,9 +1179,9 @@ cudaError_t launch_aux_backward(const AuxSaved& A, const AuxBwd& B, const float*
                     static_cast<const T*>(x), static_cast<const int32_t*>(nullptr), 1, n, d, tpc, B.rpart);
   if (e != cudaSuccess) return e;
   const int64_t count = static_cast<int64_t>(E) * d;
-  const unsigned g2 = static_cast<unsigned>(std::min<int64_t>((count + 255) / 256, 148 * 4));
-  return launch_kernel(reduce_partials_kernel<T, T>, dim3(g2), dim3(256), 0, s, static_cast<const float*>(B.rpart),
-                       chunks, static_cast<int64_t>(kMaxE) * d, count, static_cast<T*>(dw));
+  return launch_kernel(reduce_partials_wide_kernel<T, T>, dim3(static_cast<unsigned>((count + 31) / 32)), dim3(256),
+                       0, s, static_cast<const float*>(B.rpart), chunks, static_cast<int64_t>(kMaxE) * d, count,
+                       static_cast<T*>(dw));
 }
 
 }  // namespace
@@ -1610,6 +1666,10 @@ static int check_aux_args(int dtype, int64_t n, int d, int E) {
   if (n < 0 || n > (int64_t(1) << 31) - 1) return agm::fail(AGM_ERR_ARG, "n_tokens out of range");
   if (d <= 0 || d % 8) return agm::fail(AGM_ERR_ARG, "d must be a positive multiple of 8");
   if (E < 1 || E > AGM_MAX_EXPERTS) return agm::fail(AGM_ERR_UNSUPPORTED, "n_experts must be in [1, 16]");
+  if (dtype != AGM_F32 && !agm::router_tc_supported(d))
+    return agm::fail(AGM_ERR_UNSUPPORTED, "the tensor-core router does not support this d");
+  if (dtype == AGM_F32 && agm::router_smem_bytes(d, E) > 227 * 1024)
+    return agm::fail(AGM_ERR_UNSUPPORTED, "router weight does not fit in shared memory for this d");
   return AGM_OK;
 }
 

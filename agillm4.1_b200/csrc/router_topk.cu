@@ -202,7 +202,6 @@ __global__ void __launch_bounds__(kDispatchBlock) router_topk_kernel(
   __shared__ int hist_w[kRouterWarps][kMaxExperts];
 
   const int warp = warp_id(), lane = lane_id();
-  const int64_t blk_tok0 = static_cast<int64_t>(blockIdx.x) * kDispatchBlock;
 
   if (compute) {
     // Stage W (vectorised, 16 B per thread per step), converting to fp32.
@@ -222,8 +221,11 @@ __global__ void __launch_bounds__(kDispatchBlock) router_topk_kernel(
   }
   __syncthreads();
 
+  // Persistent over 128-token blocks: W is staged once per CTA.
   float* my_logits = logit_s + warp * 32 * kMaxExperts;
-  const int64_t warp_tok0 = blk_tok0 + warp * 32;
+  const int64_t nblk = (n_tokens + kDispatchBlock - 1) / kDispatchBlock;
+  for (int64_t blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
+  const int64_t warp_tok0 = blk * kDispatchBlock + warp * 32;
 
   if (compute) {
     for (int g = 0; g < 32; g += kTokGroup) {
@@ -321,7 +323,9 @@ __global__ void __launch_bounds__(kDispatchBlock) router_topk_kernel(
     int c = 0;
 #pragma unroll
     for (int w = 0; w < kRouterWarps; ++w) c += hist_w[w][threadIdx.x];
-    block_hist[static_cast<int64_t>(blockIdx.x) * E + threadIdx.x] = c;
+    block_hist[blk * E + threadIdx.x] = c;
+  }
+  __syncthreads();  // logit_s and hist_w are reused by the next block
   }
 }
 
@@ -563,13 +567,18 @@ static cudaError_t launch_router_tc(const void* x, const void* w, int64_t n_toke
 template <typename T, int KC>
 static cudaError_t launch_router(const void* x, const void* w, int64_t n_tokens, int d, int E, int k,
                                  int tie_low_first, const float* logits_in, float* logits_out, int32_t* idx,
-                                 void* gates, int32_t* block_hist, int* err, cudaStream_t stream) {
+                                 void* gates, int32_t* block_hist, int* err, int num_sms, cudaStream_t stream) {
   const int64_t nblk = (n_tokens + kDispatchBlock - 1) / kDispatchBlock;
   const size_t smem = (logits_in ? 0 : static_cast<size_t>(E) * d * sizeof(float)) +
                       static_cast<size_t>(kRouterWarps) * 32 * kMaxExperts * sizeof(float);
   cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(router_topk_kernel<T, KC>), static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  return launch_kernel(router_topk_kernel<T, KC>, dim3(static_cast<unsigned>(nblk)), dim3(kDispatchBlock), smem, stream,
+  // As many CTAs as are resident at once, each looping over token blocks.
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, router_topk_kernel<T, KC>, kDispatchBlock, smem);
+  if (e != cudaSuccess) return e;
+  const int64_t grid = std::min<int64_t>(nblk, static_cast<int64_t>(std::max(per_sm, 1)) * std::max(num_sms, 1));
+  return launch_kernel(router_topk_kernel<T, KC>, dim3(static_cast<unsigned>(grid)), dim3(kDispatchBlock), smem, stream,
                        static_cast<const T*>(x), static_cast<const T*>(w), n_tokens, d, E, k, tie_low_first, logits_in,
                        logits_out, idx, static_cast<T*>(gates), block_hist, err);
 }
@@ -589,7 +598,7 @@ static cudaError_t launch_any(bool tc, const void* x, const void* w, int64_t n_t
                                      num_sms, stream);
   }
   return launch_router<T, KC>(x, w, n_tokens, d, E, k, tie_low_first, logits_in, logits_out, idx, gates, block_hist,
-                              err, stream);
+                              err, num_sms, stream);
 }
 
 template <typename T>
