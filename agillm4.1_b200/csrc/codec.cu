@@ -1,0 +1,283 @@
+// Tensor-state codec decode on the GPU: the payloads of the reference's
+// tensor codec (agillm41.py:4858-5074, decoded by
+// _agillm43_decode_tensor_state, agillm41.py:5076-5102) turned into weights
+// in device memory, optionally applied to them the way the DBlock side-update
+// consumer applies a decoded state (agillm41.py:6029-6046):
+//
+//   value  = payload                         (pack_kind "lossless" / "fp16")
+//          = float(q) * scale                (pack_kind "int8_symmetric")
+//          = float(q[r, c]) * float(s[r])    (pack_kind "int8_rowwise", the
+//                                             row scales stored as fp16 or fp32)
+//   src    = value rounded to the target's dtype   (`value.to(dtype=target.dtype)`)
+//   target = src                             (copy_,  alpha >= 1)
+//          = lerp(target, src, alpha)        (lerp_,  state update)
+//          = target + alpha * src            (add_,   delta update)
+//
+// The host decompresses the payload (zstd or zlib, a CPU library) and copies
+// the packed bytes to the device: 1 byte per int8 element crosses PCIe instead
+// of the 4 of the reference's fp32 decode. This kernel then reads the packed
+// bytes once and writes (or reads and writes) the target once: HBM-bound byte
+// work, 16 elements per thread per step, grid-stride over the tensor.
+#include <algorithm>
+#include <cstdint>
+#include <string>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace agm {
+namespace {
+
+constexpr int kCodecThreads = 256;
+constexpr int kCodecVec = 16;  // elements per thread per step
+
+// torch's lerp on CUDA (ATen/native/Lerp.h, opmath float): the small-weight
+// form below |w| < 0.5, the end-anchored form above it.
+__device__ __forceinline__ float lerp_f(float self, float end, float w) {
+  return fabsf(w) < 0.5f ? self + w * (end - self) : end - (end - self) * (1.0f - w);
+}
+
+template <typename P>
+__device__ __forceinline__ float packed_value(P v) {
+  if constexpr (sizeof(P) == 1)
+    return static_cast<float>(v);
+  else
+    return Traits<P>::to_f(v);
+}
+
+template <typename S>
+__device__ __forceinline__ float scale_value(const S* s, int64_t row) {
+  return Traits<S>::to_f(s[row]);
+}
+
+// KIND: AGM_CODEC_PLAIN (P = float / bf16 / fp16), AGM_CODEC_INT8,
+// AGM_CODEC_INT8_ROWWISE (P = int8_t, S = the row-scale type).
+template <int KIND, typename P, typename S, typename OutT, int MODE>
+__device__ __forceinline__ void decode_one(const P* __restrict__ payload, int64_t i, int64_t cols, float scale,
+                                           const S* __restrict__ row_scales, OutT* __restrict__ target, float alpha) {
+  float v = packed_value<P>(payload[i]);
+  if constexpr (KIND == AGM_CODEC_INT8) v = __fmul_rn(v, scale);
+  if constexpr (KIND == AGM_CODEC_INT8_ROWWISE) v = __fmul_rn(v, scale_value<S>(row_scales, i / cols));
+  const float src = round_to<OutT>(v);
+  float t;
+  if constexpr (MODE == AGM_APPLY_COPY) {
+    t = src;
+  } else {
+    const float cur = Traits<OutT>::to_f(target[i]);
+    t = MODE == AGM_APPLY_ADD ? cur + alpha * src : lerp_f(cur, src, alpha);
+  }
+  target[i] = Traits<OutT>::from_f(t);
+}
+
+template <int KIND, typename P, typename S, typename OutT, int MODE>
+__global__ void __launch_bounds__(kCodecThreads) codec_decode_kernel(const P* __restrict__ payload, int64_t n,
+                                                                     int64_t cols, float scale,
+                                                                     const S* __restrict__ row_scales,
+                                                                     OutT* __restrict__ target, float alpha,
+                                                                     int vec_ok) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kCodecThreads;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * kCodecThreads + threadIdx.x;
+  if (vec_ok) {
+    // 16 consecutive elements per thread: 16 B of int8 (32 / 64 B of 16-bit /
+    // fp32 payload) in, 32 / 64 B of target out, whole 16-byte vectors.
+    const int64_t nvec = n / kCodecVec;
+    for (int64_t b = tid; b < nvec; b += stride) {
+      const int64_t i0 = b * kCodecVec;
+      float v[kCodecVec];
+      if constexpr (sizeof(P) == 1) {
+        const int4 u = __ldg(reinterpret_cast<const int4*>(payload + i0));
+        const int w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int j = 0; j < kCodecVec; ++j) v[j] = static_cast<float>(static_cast<int8_t>(w[j >> 2] >> (8 * (j & 3))));
+      } else if constexpr (sizeof(P) == 2) {
+        float f[8];
+        unpack8<P>(__ldg(reinterpret_cast<const uint4*>(payload + i0)), f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = f[j];
+        unpack8<P>(__ldg(reinterpret_cast<const uint4*>(payload + i0 + 8)), f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[8 + j] = f[j];
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 f = __ldg(reinterpret_cast<const float4*>(payload + i0) + q);
+          v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
+        }
+      }
+      if constexpr (KIND == AGM_CODEC_INT8) {
+#pragma unroll
+        for (int j = 0; j < kCodecVec; ++j) v[j] = __fmul_rn(v[j], scale);
+      }
+      if constexpr (KIND == AGM_CODEC_INT8_ROWWISE) {
+        // The scale changes wherever a row starts inside the 16-element group.
+        int64_t row = i0 / cols;
+        int64_t next = (row + 1) * cols;
+        float s = scale_value<S>(row_scales, row);
+#pragma unroll
+        for (int j = 0; j < kCodecVec; ++j) {
+          if (i0 + j >= next) {
+            ++row;
+            next += cols;
+            s = scale_value<S>(row_scales, row);
+          }
+          v[j] = __fmul_rn(v[j], s);
+        }
+      }
+      float t[kCodecVec];
+      if constexpr (MODE == AGM_APPLY_COPY) {
+#pragma unroll
+        for (int j = 0; j < kCodecVec; ++j) t[j] = round_to<OutT>(v[j]);
+      } else {
+        float cur[kCodecVec];
+        if constexpr (sizeof(OutT) == 2) {
+          float f[8];
+          unpack8<OutT>(*reinterpret_cast<const uint4*>(target + i0), f);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) cur[j] = f[j];
+          unpack8<OutT>(*reinterpret_cast<const uint4*>(target + i0 + 8), f);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) cur[8 + j] = f[j];
+        } else {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float4 f = reinterpret_cast<const float4*>(target + i0)[q];
+            cur[4 * q] = f.x; cur[4 * q + 1] = f.y; cur[4 * q + 2] = f.z; cur[4 * q + 3] = f.w;
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < kCodecVec; ++j) {
+          const float src = round_to<OutT>(v[j]);
+          t[j] = MODE == AGM_APPLY_ADD ? cur[j] + alpha * src : lerp_f(cur[j], src, alpha);
+        }
+      }
+      if constexpr (sizeof(OutT) == 2) {
+        reinterpret_cast<uint4*>(target + i0)[0] =
+            make_uint4(pack2<OutT>(t[0], t[1]), pack2<OutT>(t[2], t[3]), pack2<OutT>(t[4], t[5]), pack2<OutT>(t[6], t[7]));
+        reinterpret_cast<uint4*>(target + i0)[1] = make_uint4(pack2<OutT>(t[8], t[9]), pack2<OutT>(t[10], t[11]),
+                                                              pack2<OutT>(t[12], t[13]), pack2<OutT>(t[14], t[15]));
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          reinterpret_cast<float4*>(target + i0)[q] = make_float4(t[4 * q], t[4 * q + 1], t[4 * q + 2], t[4 * q + 3]);
+      }
+    }
+    for (int64_t i = nvec * kCodecVec + tid; i < n; i += stride)
+      decode_one<KIND, P, S, OutT, MODE>(payload, i, cols, scale, row_scales, target, alpha);
+  } else {
+    for (int64_t i = tid; i < n; i += stride)
+      decode_one<KIND, P, S, OutT, MODE>(payload, i, cols, scale, row_scales, target, alpha);
+  }
+}
+
+template <int KIND, typename P, typename S, typename OutT, int MODE>
+cudaError_t launch_decode(const void* payload, int64_t n, int64_t cols, float scale, const void* row_scales,
+                          void* target, float alpha, bool vec_ok, int sms, cudaStream_t s) {
+  const int64_t want = (n / (vec_ok ? kCodecVec : 1) + kCodecThreads - 1) / kCodecThreads;
+  const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(sms) * 8)));
+  codec_decode_kernel<KIND, P, S, OutT, MODE><<<grid, kCodecThreads, 0, s>>>(
+      static_cast<const P*>(payload), n, cols, scale, static_cast<const S*>(row_scales), static_cast<OutT*>(target),
+      alpha, vec_ok ? 1 : 0);
+  return cudaGetLastError();
+}
+
+template <int KIND, typename P, typename S, typename OutT>
+cudaError_t by_mode(int mode, const void* payload, int64_t n, int64_t cols, float scale, const void* row_scales,
+                    void* target, float alpha, bool vec_ok, int sms, cudaStream_t s) {
+  switch (mode) {
+    case AGM_APPLY_COPY:
+      return launch_decode<KIND, P, S, OutT, AGM_APPLY_COPY>(payload, n, cols, scale, row_scales, target, alpha, vec_ok,
+                                                             sms, s);
+    case AGM_APPLY_LERP:
+      return launch_decode<KIND, P, S, OutT, AGM_APPLY_LERP>(payload, n, cols, scale, row_scales, target, alpha, vec_ok,
+                                                             sms, s);
+    default:
+      return launch_decode<KIND, P, S, OutT, AGM_APPLY_ADD>(payload, n, cols, scale, row_scales, target, alpha, vec_ok,
+                                                            sms, s);
+  }
+}
+
+template <int KIND, typename P, typename S>
+cudaError_t by_target(int target_dtype, int mode, const void* payload, int64_t n, int64_t cols, float scale,
+                      const void* row_scales, void* target, float alpha, bool vec_ok, int sms, cudaStream_t s) {
+  switch (target_dtype) {
+    case AGM_F32: return by_mode<KIND, P, S, float>(mode, payload, n, cols, scale, row_scales, target, alpha, vec_ok, sms, s);
+    case AGM_BF16:
+      return by_mode<KIND, P, S, __nv_bfloat16>(mode, payload, n, cols, scale, row_scales, target, alpha, vec_ok, sms, s);
+    default: return by_mode<KIND, P, S, __half>(mode, payload, n, cols, scale, row_scales, target, alpha, vec_ok, sms, s);
+  }
+}
+
+int codec_fail(int code, const char* msg) {
+  set_last_error(std::string("agm_codec_decode: ") + msg);
+  return code;
+}
+
+int dtype_bytes(int dtype) { return dtype == AGM_F32 ? 4 : (dtype == AGM_BF16 || dtype == AGM_F16) ? 2 : 0; }
+
+}  // namespace
+}  // namespace agm
+
+extern "C" {
+
+int agm_codec_decode(const void* payload, int kind, int packed_dtype, int64_t n, int64_t cols, float scale,
+                     const void* row_scales, int scales_dtype, void* target, int target_dtype, int mode, float alpha,
+                     void* stream_) {
+  using namespace agm;
+  if (n < 0) return codec_fail(AGM_ERR_ARG, "n < 0");
+  if (kind != AGM_CODEC_PLAIN && kind != AGM_CODEC_INT8 && kind != AGM_CODEC_INT8_ROWWISE)
+    return codec_fail(AGM_ERR_ARG, "unknown pack kind");
+  if (mode != AGM_APPLY_COPY && mode != AGM_APPLY_LERP && mode != AGM_APPLY_ADD)
+    return codec_fail(AGM_ERR_ARG, "unknown apply mode");
+  if (!dtype_bytes(target_dtype)) return codec_fail(AGM_ERR_ARG, "target dtype must be AGM_F32, AGM_BF16 or AGM_F16");
+  if (kind == AGM_CODEC_PLAIN && !dtype_bytes(packed_dtype))
+    return codec_fail(AGM_ERR_UNSUPPORTED, "lossless payloads must be fp32, bf16 or fp16");
+  if (kind == AGM_CODEC_INT8_ROWWISE) {
+    if (cols <= 0 || n % cols) return codec_fail(AGM_ERR_ARG, "cols must divide n for row-wise int8");
+    if (scales_dtype != AGM_F32 && scales_dtype != AGM_F16)
+      return codec_fail(AGM_ERR_ARG, "row scales must be AGM_F32 or AGM_F16");
+    if (n > 0 && !row_scales) return codec_fail(AGM_ERR_ARG, "null row scales");
+  }
+  if (n == 0) return AGM_OK;
+  if (!payload || !target) return codec_fail(AGM_ERR_ARG, "null pointer");
+  // Whole 16-byte vectors need 16-byte aligned payload and target.
+  const uintptr_t pa = reinterpret_cast<uintptr_t>(payload), ta = reinterpret_cast<uintptr_t>(target);
+  const int pb = kind == AGM_CODEC_PLAIN ? dtype_bytes(packed_dtype) : 1;
+  const int tb = dtype_bytes(target_dtype);
+  if (pa % pb || ta % tb) return codec_fail(AGM_ERR_ARG, "payload and target must be aligned to their element size");
+  const bool vec_ok = (pa % 16 == 0) && (ta % 16 == 0);
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaStream_t s = static_cast<cudaStream_t>(stream_);
+  cudaError_t e;
+  if (kind == AGM_CODEC_INT8) {
+    e = by_target<AGM_CODEC_INT8, int8_t, float>(target_dtype, mode, payload, n, 1, scale, nullptr, target, alpha,
+                                                 vec_ok, sms, s);
+  } else if (kind == AGM_CODEC_INT8_ROWWISE) {
+    e = scales_dtype == AGM_F16
+            ? by_target<AGM_CODEC_INT8_ROWWISE, int8_t, __half>(target_dtype, mode, payload, n, cols, 1.f, row_scales,
+                                                                target, alpha, vec_ok, sms, s)
+            : by_target<AGM_CODEC_INT8_ROWWISE, int8_t, float>(target_dtype, mode, payload, n, cols, 1.f, row_scales,
+                                                               target, alpha, vec_ok, sms, s);
+  } else {
+    switch (packed_dtype) {
+      case AGM_F32:
+        e = by_target<AGM_CODEC_PLAIN, float, float>(target_dtype, mode, payload, n, 1, 1.f, nullptr, target, alpha,
+                                                     vec_ok, sms, s);
+        break;
+      case AGM_BF16:
+        e = by_target<AGM_CODEC_PLAIN, __nv_bfloat16, float>(target_dtype, mode, payload, n, 1, 1.f, nullptr, target,
+                                                             alpha, vec_ok, sms, s);
+        break;
+      default:
+        e = by_target<AGM_CODEC_PLAIN, __half, float>(target_dtype, mode, payload, n, 1, 1.f, nullptr, target, alpha,
+                                                      vec_ok, sms, s);
+    }
+  }
+  if (e != cudaSuccess) {
+    set_last_error(std::string("agm_codec_decode: ") + cudaGetErrorString(e));
+    return AGM_ERR_CUDA;
+  }
+  return AGM_OK;
+}
+
+}  // extern "C"

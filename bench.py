@@ -308,7 +308,8 @@ def run_ours(args, world, rank, local):
                                         label="production MoE block training step")
         train["production"]["forward"] = run_forward_production(args, dev, stream)
         train["aux_loss"] = run_aux(args, dev, stream)
-    report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e_value, x, decode, train)
+    codec_leg = None if args.skip_codec else run_codec(args, dev, stream, world == 1 and not args.skip_cpu)
+    report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e_value, x, decode, train, codec_leg)
 
 
 def run_forward_production(args, dev, stream):
@@ -460,6 +461,131 @@ def run_aux(args, dev, stream):
                          "frac": round(gbs / peaks["hbm"], 3),
                          "note": "the input read once by each pass plus the logits, over both passes' time"},
             "gpu_launches_per_step": 6}
+
+
+def _codec_layer_state():
+    """A codec state (the reference's tensor codec, agillm41.py:4858-5074)
+    holding one production MoE layer's expert tensors (2 experts, d = 1280,
+    H = 4d; 26.2 M values): seeded Gaussian weights quantised row-wise to int8
+    with fp16 row scales, biases to int8 with one scale, zlib level 1 behind
+    the "ZLIB" tag (the reference's compressor without zstandard)."""
+    import zlib
+
+    import numpy as np
+
+    rng = np.random.default_rng(SEED)
+    H = 4 * D
+    shapes = {}
+    for e in range(2):
+        shapes[f"experts.{e}.0.weight"] = (H, D)
+        shapes[f"experts.{e}.0.bias"] = (H,)
+        shapes[f"experts.{e}.2.weight"] = (D, H)
+        shapes[f"experts.{e}.2.bias"] = (D,)
+    tensors = {}
+    for key, shape in shapes.items():
+        w = rng.standard_normal(shape, dtype=np.float32) * 0.02
+        item = {"shape": list(shape), "orig_dtype": "float32", "packed_dtype": "int8", "codec": "zstd"}
+        if len(shape) == 2:
+            s = np.maximum(np.abs(w).max(axis=1) / 127.0, 1e-12).astype(np.float16)
+            q = np.clip(np.rint(w / s.astype(np.float32)[:, None]), -127, 127).astype(np.int8)
+            item.update(pack_kind="int8_rowwise", rows=shape[0], cols=shape[1], scales_dtype="float16",
+                        scales_codec="raw", scales_data=torch.from_numpy(s.view(np.uint8).copy()))
+        else:
+            scale = max(float(np.abs(w).max()) / 127.0, 1e-12)
+            q = np.clip(np.rint(w / scale), -127, 127).astype(np.int8)
+            item.update(pack_kind="int8_symmetric", scale=scale)
+        item["data"] = torch.frombuffer(bytearray(b"ZLIB" + zlib.compress(q.tobytes(), 1)), dtype=torch.uint8)
+        tensors[key] = item
+    return {"__agillm43_tensor_state_codec__": "agillm43_tensor_state_v3_rowq8c", "mode": "rowq8-zstd",
+            "plain": {}, "tensors": tensors}, shapes
+
+
+def run_codec(args, dev, stream, cpu_leg):
+    """Tensor-codec decode of one production MoE layer's experts into fp32
+    device parameters (the side-update consumer's copy, agillm41.py:6029-6046):
+
+    * kernel: agm_codec_decode over the int8 payloads already in device memory,
+      algorithmic bytes = 1 B read + 4 B written per value (+ row scales);
+    * e2e: agillm41_b200.codec.apply_tensor_state from the compressed host
+      state (threaded decompression, pinned H2D of the packed bytes, decode);
+    * cpu_baseline: the reference's path (decode_tensor_state on the host's
+      cores, then value.to(device) and copy_), restated by the oracle.
+    """
+    from agillm41_b200 import _lib, codec
+    from agillm41_b200._lib import load, ptr, stream_handle
+
+    state, shapes = _codec_layer_state()
+    targets = {k: torch.empty(v, dtype=torch.float32, device=dev) for k, v in shapes.items()}
+    n_total = sum(v[0] * (v[1] if len(v) > 1 else 1) for v in shapes.values())
+    # kernel leg: payloads resident on the device
+    staged = [codec._Payload(k, it) for k, it in state["tensors"].items()]
+    dev_q = [(p, p.packed.to(dev), None if p.scales is None else p.scales.to(dev)) for p in staged]
+    lib = load()
+    h = stream_handle(dev)
+
+    def kernels():
+        for p, q, sc in dev_q:
+            kind = _lib.AGM_CODEC_INT8_ROWWISE if p.kind_name == "int8_rowwise" else _lib.AGM_CODEC_INT8
+            cols = p.n // p.rows if p.rows else 1
+            rc = lib.agm_codec_decode(ptr(q), kind, 0, p.n, cols, p.scale, ptr(sc), _lib.AGM_F16 if sc is not None
+                                      else 0, ptr(targets[p.key]), _lib.AGM_F32, _lib.AGM_APPLY_COPY, 1.0, h)
+            _lib.check(rc, "agm_codec_decode")
+
+    for _ in range(3):
+        kernels()
+    torch.cuda.synchronize()
+    steps = max(10, min(args.steps, 50))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        kernels()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    k_ms = e0.elapsed_time(e1) / steps
+    scale_bytes = sum(p.scales.numel() for p in staged if p.scales is not None)
+    nbytes = n_total * (1 + 4) + scale_bytes
+    gbs = nbytes / (k_ms / 1000.0) / 1e9
+    peaks = load_peaks()
+    # e2e leg: compressed host state -> applied device parameters
+    for _ in range(2):
+        codec.apply_tensor_state(state, targets)
+    torch.cuda.synchronize()
+    e2e_steps = 5
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        codec.apply_tensor_state(state, targets)
+    torch.cuda.synchronize()
+    e2e_ms = (time.perf_counter() - t0) * 1000.0 / e2e_steps
+    h2d = sum(p.packed.numel() for p in staged) + scale_bytes
+    out = {"workload": f"tensor-codec decode of one production MoE layer's experts (2 experts, d{D}, H{4 * D}: "
+                       f"{n_total} values, row-wise int8 weights, int8 biases) into fp32 device parameters",
+           "kernel_ms": round(k_ms, 4), "values_per_s": n_total / (k_ms / 1000.0), "steps": steps,
+           "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm"], "unit": "GB/s",
+                        "frac": round(gbs / peaks["hbm"], 3),
+                        "note": "1 B of int8 read and 4 B of fp32 written per value, plus the row scales"},
+           "e2e": {"ms": round(e2e_ms, 3), "values_per_s": n_total / (e2e_ms / 1000.0),
+                   "h2d_bytes": int(h2d), "note": "host wall clock from the compressed state to applied "
+                                                  "parameters: threaded zlib, pinned H2D, decode"},
+           "gpu_launches_per_step": len(staged)}
+    if cpu_leg:
+        from oracle import codec_oracle
+
+        for _ in range(1):
+            for k, v in codec_oracle.decode_tensor_state(state).items():
+                codec_oracle.apply_value(targets[k], v)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        reps = 3
+        for _ in range(reps):
+            for k, v in codec_oracle.decode_tensor_state(state).items():
+                codec_oracle.apply_value(targets[k], v)
+            torch.cuda.synchronize()
+        c_ms = (time.perf_counter() - t0) * 1000.0 / reps
+        out["cpu_baseline"] = {"ms": round(c_ms, 3), "values_per_s": n_total / (c_ms / 1000.0),
+                               "cores": torch.get_num_threads(), "kind": "port",
+                               "sample": "the whole layer: the reference's decode on the host (zlib, int8 x scale "
+                                         "in fp32) then value.to(device) and copy_ per tensor"}
+    return out
 
 
 def run_ep(args, world, rank, local):
@@ -789,7 +915,7 @@ def gemm_kernel_name(n_tokens):
     return "grouped_gemm_tc_kernel (FC1+FC2, tcgen05, one CTA per tile)"
 
 
-def report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e, x, decode=None, train=None):
+def report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e, x, decode=None, train=None, codec=None):
     if rank != 0:
         return
     peaks = load_peaks()
@@ -836,6 +962,8 @@ def report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e, x, deco
         line["decode"] = decode
     if train is not None:
         line["train"] = train
+    if codec is not None:
+        line["codec"] = codec
     print(json.dumps(line), flush=True)
 
 
@@ -851,6 +979,7 @@ def main():
     ap.add_argument("--skip-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--skip-decode", action="store_true", help="skip the 28-layer decode leg")
     ap.add_argument("--skip-train", action="store_true", help="skip the training-step (forward + backward) leg")
+    ap.add_argument("--skip-codec", action="store_true", help="skip the tensor-codec decode leg")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)

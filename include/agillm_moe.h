@@ -347,6 +347,31 @@ AGM_API int agm_moe_backward(const void* dout, int x_dtype, int dtype, int64_t n
                              void* dws1, void* dsb1, void* dws2, void* dsb2, void* workspace, size_t workspace_bytes,
                              int flags, void* stream);
 
+/* ---- Tensor-state codec decode ------------------------------------------
+ * Decodes one tensor of the reference's tensor codec
+ * (_agillm43_encode_tensor_state / _agillm43_decode_tensor_state,
+ * agillm41.py:4858-5102) from its packed payload, already decompressed and in
+ * device memory, and writes or applies it to a device tensor of n elements,
+ * as the DBlock side-update consumer applies a decoded state
+ * (agillm41.py:6029-6046):
+ *   kind AGM_CODEC_PLAIN         value = payload (packed_dtype: "lossless" or
+ *                                "fp16" pack kinds)
+ *   kind AGM_CODEC_INT8          value = float(q) * scale ("int8_symmetric")
+ *   kind AGM_CODEC_INT8_ROWWISE  value = float(q[r, c]) * float(row_scales[r])
+ *                                with cols elements per row, row scales in
+ *                                scales_dtype (AGM_F16 or AGM_F32) ("int8_rowwise")
+ * then src = value rounded to target_dtype and
+ *   mode AGM_APPLY_COPY  target = src                  (copy_)
+ *   mode AGM_APPLY_LERP  target = lerp(target, src, alpha)   (lerp_, torch's formula)
+ *   mode AGM_APPLY_ADD   target = target + alpha * src (add_, delta updates)
+ * Payload and target need their element alignment; 16-byte alignment takes
+ * the vectorised path. */
+enum { AGM_CODEC_PLAIN = 0, AGM_CODEC_INT8 = 1, AGM_CODEC_INT8_ROWWISE = 2 };
+enum { AGM_APPLY_COPY = 0, AGM_APPLY_LERP = 1, AGM_APPLY_ADD = 2 };
+AGM_API int agm_codec_decode(const void* payload, int kind, int packed_dtype, int64_t n, int64_t cols, float scale,
+                             const void* row_scales, int scales_dtype, void* target, int target_dtype, int mode,
+                             float alpha, void* stream);
+
 /* ---- Auxiliary router losses --------------------------------------------
  * Replaces the per-module body of _collect_moe_aux (agillm41.py:4463-4492):
  * recompute the router logits from the stashed FFN input x [n_tokens, d]

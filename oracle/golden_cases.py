@@ -127,3 +127,37 @@ def case_inputs(case):
     if special == "empty":
         x32 = x32.abs() + 0.01
     return sd32, x32
+
+
+# Tensor-codec golden cases (agillm41.py:4858-5102): the encoder modes, and
+# the side-update applications (name, alpha, delta) of agillm41.py:6035-6045.
+CODEC_MODES = ["int8-zstd", "rowq8-zstd", "fp16-zstd", "zstd", "adaptive-zstd"]
+CODEC_APPLY = [("copy", 1.0, False), ("lerp03", 0.3, False), ("lerp075", 0.75, False), ("add05", 0.5, True)]
+CODEC_APPLY_KEYS = ["experts.0.0.weight", "experts.1.0.weight", "experts.1.2.bias", "shared.0.0.weight"]
+
+
+def codec_state():
+    """A small seeded MoE-layer state: two experts (expert 1's FC1 weight has
+    an outlier row), the router, and a bf16 shared-expert weight. Weights are
+    drawn at the scale of trained block weights (std 0.02), so the adaptive
+    mode's error budget picks int8 for some tensors and row-wise int8 or fp16
+    for others."""
+    g = torch.Generator().manual_seed(91)
+    d, H, E = 64, 96, 2
+    sd = {}
+    for e in range(E):
+        sd[f"experts.{e}.0.weight"] = torch.randn(H, d, generator=g) * 0.02
+        sd[f"experts.{e}.0.bias"] = torch.randn(H, generator=g) * 0.01
+        sd[f"experts.{e}.2.weight"] = torch.randn(d, H, generator=g) * 0.02
+        sd[f"experts.{e}.2.bias"] = torch.randn(d, generator=g) * 0.01
+    sd["experts.1.0.weight"][7] = torch.linspace(-4.0, 4.0, d)   # one outlier row: row-wise int8
+    sd["experts.1.2.bias"] *= 200.0                               # large 1-D values: fp16
+    sd["router.weight"] = torch.randn(E, d, generator=g) * 0.05
+    sd["shared.0.0.weight"] = (torch.randn(2 * d, d, generator=g) * 0.02).to(torch.bfloat16)
+    return sd
+
+
+def codec_target(key, shape, dtype):
+    """Seeded target tensor that a decoded value is applied to."""
+    g = torch.Generator().manual_seed(92 + sum(map(ord, key)))
+    return (torch.randn(tuple(shape), generator=g) * 0.02).to(dtype)

@@ -18,7 +18,7 @@ def _all_names():
 
 def names():
     """Forward (and gradient) cases of the MoE block."""
-    return [n for n in _all_names() if not n.startswith("aux_")]
+    return [n for n in _all_names() if not n.startswith(("aux_", "codec_"))]
 
 
 def aux_names():
@@ -150,3 +150,44 @@ class GoldenAux:
     def inputs_match(self):
         return all(torch.equal(x, xr) and torch.equal(w, wr)
                    for x, w, (xr, wr) in zip(self.xs, self.ws, self.regenerated))
+
+
+def codec_names():
+    """Tensor-codec cases (tests/golden/make_golden_codec.py)."""
+    return [n for n in _all_names() if n.startswith("codec_")]
+
+
+class GoldenCodec:
+    """A tensor-codec case: the reference's encoded state for one encoder
+    mode (rebuilt from the stored metadata and payload bytes), its decoded
+    values and the targets after each side-update application."""
+
+    def __init__(self, name):
+        import json
+
+        self.name = name
+        z = self.z = np.load(os.path.join(GOLDEN_DIR, name + ".npz"))
+        self.mode = str(z["mode"])
+        self.meta = json.loads(str(z["meta"]))
+        header = json.loads(str(z["header"]))
+        tensors = {}
+        for key, m in self.meta.items():
+            item = dict(m)
+            item["data"] = torch.from_numpy(z[f"data/{key}"].copy())
+            item["scales"] = None
+            item["scales_data"] = (torch.from_numpy(z[f"scales_data/{key}"].copy())
+                                   if f"scales_data/{key}" in z.files else None)
+            tensors[key] = item
+        self.state = dict(header)
+        self.state["tensors"] = tensors
+
+    def decoded(self, key):
+        m = self.meta[key]
+        dt = torch.float32 if m["pack_kind"] in ("int8_symmetric", "int8_rowwise") else DTYPES[m["packed_dtype"]]
+        return from_np(self.z[f"decoded/{key}"], dt)
+
+    def applied(self, name, dtype, key):
+        return from_np(self.z[f"applied/{name}/{str(dtype)[6:]}/{key}"], dtype)
+
+    def applied_keys(self):
+        return sorted({f.split("/", 3)[3] for f in self.z.files if f.startswith("applied/")})

@@ -164,6 +164,30 @@ def test_aux_entry_points_validate_without_a_device():
     assert rc == -5 and "workspace" in lib.agm_last_error().decode()
 
 
+def test_codec_decode_validates_without_a_device():
+    lib = _lib.load()
+    fake = ctypes.c_void_p(4096)
+    args = dict(payload=fake, kind=_lib.AGM_CODEC_INT8, packed=0, n=1000, cols=1, scale=0.5, scales=None,
+                scales_dtype=0, target=fake, target_dtype=_lib.AGM_F32, mode=_lib.AGM_APPLY_COPY, alpha=1.0)
+
+    def call(**kw):
+        a = dict(args, **kw)
+        return lib.agm_codec_decode(a["payload"], a["kind"], a["packed"], a["n"], a["cols"], a["scale"], a["scales"],
+                                    a["scales_dtype"], a["target"], a["target_dtype"], a["mode"], a["alpha"], None)
+
+    assert call(kind=7) == -1
+    assert call(mode=9) == -1
+    assert call(target_dtype=5) == -1
+    assert call(kind=_lib.AGM_CODEC_PLAIN, packed=5) == -2
+    assert call(kind=_lib.AGM_CODEC_INT8_ROWWISE, cols=7, scales=fake, scales_dtype=_lib.AGM_F16) == -1
+    assert call(kind=_lib.AGM_CODEC_INT8_ROWWISE, cols=10, scales=fake, scales_dtype=_lib.AGM_BF16) == -1
+    assert call(kind=_lib.AGM_CODEC_INT8_ROWWISE, cols=10, scales=None, scales_dtype=_lib.AGM_F16) == -1
+    assert call(payload=None) == -1
+    assert call(target=ctypes.c_void_p(4096 + 2)) == -1          # fp32 target off its 4-byte alignment
+    assert call(n=-1) == -1
+    assert call(n=0, payload=None, target=None) == 0              # nothing to do
+
+
 def test_training_forward_refuses_cpu_tensors():
     import torch
 
