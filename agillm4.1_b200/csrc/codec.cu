@@ -69,6 +69,138 @@ __device__ __forceinline__ void decode_one(const P* __restrict__ payload, int64_
   target[i] = Traits<OutT>::from_f(t);
 }
 
+// 16 consecutive elements of type E as raw 16-byte words (sizeof(E) words):
+// loads are issued into these, the conversion to fp32 waits until the math.
+template <typename E>
+struct Raw16 {
+  uint4 w[sizeof(E)];
+};
+
+template <typename E>
+__device__ __forceinline__ void load_raw(const E* __restrict__ p, int64_t i0, Raw16<E>& r, bool nc) {
+#pragma unroll
+  for (int q = 0; q < static_cast<int>(sizeof(E)); ++q)
+    r.w[q] = nc ? __ldg(reinterpret_cast<const uint4*>(p + i0) + q) : reinterpret_cast<const uint4*>(p + i0)[q];
+}
+
+template <typename E>
+__device__ __forceinline__ void to_float(const Raw16<E>& r, float (&v)[kCodecVec]) {
+  if constexpr (sizeof(E) == 1) {
+    const uint32_t w[4] = {r.w[0].x, r.w[0].y, r.w[0].z, r.w[0].w};
+#pragma unroll
+    for (int j = 0; j < kCodecVec; ++j)
+      v[j] = static_cast<float>(static_cast<int8_t>(static_cast<uint8_t>(w[j >> 2] >> (8 * (j & 3)))));
+  } else if constexpr (sizeof(E) == 2) {
+    float f[8];
+    unpack8<E>(r.w[0], f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = f[j];
+    unpack8<E>(r.w[1], f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[8 + j] = f[j];
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      v[4 * q] = __uint_as_float(r.w[q].x); v[4 * q + 1] = __uint_as_float(r.w[q].y);
+      v[4 * q + 2] = __uint_as_float(r.w[q].z); v[4 * q + 3] = __uint_as_float(r.w[q].w);
+    }
+  }
+}
+
+template <typename OutT>
+__device__ __forceinline__ void store_target(OutT* __restrict__ target, int64_t i0, const float (&t)[kCodecVec]) {
+  if constexpr (sizeof(OutT) == 2) {
+    reinterpret_cast<uint4*>(target + i0)[0] =
+        make_uint4(pack2<OutT>(t[0], t[1]), pack2<OutT>(t[2], t[3]), pack2<OutT>(t[4], t[5]), pack2<OutT>(t[6], t[7]));
+    reinterpret_cast<uint4*>(target + i0)[1] = make_uint4(pack2<OutT>(t[8], t[9]), pack2<OutT>(t[10], t[11]),
+                                                          pack2<OutT>(t[12], t[13]), pack2<OutT>(t[14], t[15]));
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      reinterpret_cast<float4*>(target + i0)[q] = make_float4(t[4 * q], t[4 * q + 1], t[4 * q + 2], t[4 * q + 3]);
+  }
+}
+
+// Vectorised path: U groups of 16 consecutive elements per thread per step
+// (U = 4 for int8 payloads: 64 B of loads in flight per thread), all loads
+// (payload, row scale, and for lerp/add the target) issued before any math.
+// ROW_VEC: row-wise scales with cols a multiple of 16, so one scale per group
+// (found by a 32-bit division when n < 2^32).
+template <int KIND, typename P, typename S, typename OutT, int MODE, bool ROW_VEC>
+__device__ __forceinline__ void decode_vectors(const P* __restrict__ payload, int64_t n, int64_t cols, float scale,
+                                               const S* __restrict__ row_scales, OutT* __restrict__ target,
+                                               float alpha, int64_t tid, int64_t stride) {
+  constexpr int U = sizeof(P) == 1 ? 4 : (sizeof(P) == 2 ? 2 : 1);
+  const int64_t nvec = n / kCodecVec;
+  const bool small = n < (int64_t(1) << 32);
+  for (int64_t b0 = tid; b0 < nvec; b0 += stride * U) {
+    Raw16<P> raw[U];
+    Raw16<OutT> cur_raw[MODE == AGM_APPLY_COPY ? 1 : U];
+    float sc[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t b = b0 + u * stride;
+      if (b < nvec) {
+        const int64_t i0 = b * kCodecVec;
+        load_raw<P>(payload, i0, raw[u], true);
+        if constexpr (KIND == AGM_CODEC_INT8_ROWWISE && ROW_VEC) {
+          const int64_t row = small ? static_cast<int64_t>(static_cast<uint32_t>(i0) / static_cast<uint32_t>(cols))
+                                    : i0 / cols;
+          sc[u] = scale_value<S>(row_scales, row);
+        }
+        if constexpr (MODE != AGM_APPLY_COPY) load_raw<OutT>(target, i0, cur_raw[u], false);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t b = b0 + u * stride;
+      if (b >= nvec) continue;
+      const int64_t i0 = b * kCodecVec;
+      float v[kCodecVec];
+      to_float<P>(raw[u], v);
+      if constexpr (KIND == AGM_CODEC_INT8) {
+#pragma unroll
+        for (int j = 0; j < kCodecVec; ++j) v[j] = __fmul_rn(v[j], scale);
+      }
+      if constexpr (KIND == AGM_CODEC_INT8_ROWWISE) {
+        if constexpr (ROW_VEC) {
+#pragma unroll
+          for (int j = 0; j < kCodecVec; ++j) v[j] = __fmul_rn(v[j], sc[u]);
+        } else {
+          // Rows shorter than, or not aligned to, the group: the scale
+          // changes wherever a row starts inside it.
+          int64_t row = i0 / cols;
+          int64_t next = (row + 1) * cols;
+          float s = scale_value<S>(row_scales, row);
+#pragma unroll
+          for (int j = 0; j < kCodecVec; ++j) {
+            if (i0 + j >= next) {
+              ++row;
+              next += cols;
+              s = scale_value<S>(row_scales, row);
+            }
+            v[j] = __fmul_rn(v[j], s);
+          }
+        }
+      }
+      float t[kCodecVec];
+      if constexpr (MODE == AGM_APPLY_COPY) {
+#pragma unroll
+        for (int j = 0; j < kCodecVec; ++j) t[j] = round_to<OutT>(v[j]);
+      } else {
+        float cur[kCodecVec];
+        to_float<OutT>(cur_raw[u], cur);
+#pragma unroll
+        for (int j = 0; j < kCodecVec; ++j) {
+          const float src = round_to<OutT>(v[j]);
+          t[j] = MODE == AGM_APPLY_ADD ? cur[j] + alpha * src : lerp_f(cur[j], src, alpha);
+        }
+      }
+      store_target<OutT>(target, i0, t);
+    }
+  }
+}
+
 template <int KIND, typename P, typename S, typename OutT, int MODE>
 __global__ void __launch_bounds__(kCodecThreads) codec_decode_kernel(const P* __restrict__ payload, int64_t n,
                                                                      int64_t cols, float scale,
@@ -78,90 +210,11 @@ __global__ void __launch_bounds__(kCodecThreads) codec_decode_kernel(const P* __
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kCodecThreads;
   const int64_t tid = static_cast<int64_t>(blockIdx.x) * kCodecThreads + threadIdx.x;
   if (vec_ok) {
-    // 16 consecutive elements per thread: 16 B of int8 (32 / 64 B of 16-bit /
-    // fp32 payload) in, 32 / 64 B of target out, whole 16-byte vectors.
-    const int64_t nvec = n / kCodecVec;
-    for (int64_t b = tid; b < nvec; b += stride) {
-      const int64_t i0 = b * kCodecVec;
-      float v[kCodecVec];
-      if constexpr (sizeof(P) == 1) {
-        const int4 u = __ldg(reinterpret_cast<const int4*>(payload + i0));
-        const int w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int j = 0; j < kCodecVec; ++j) v[j] = static_cast<float>(static_cast<int8_t>(w[j >> 2] >> (8 * (j & 3))));
-      } else if constexpr (sizeof(P) == 2) {
-        float f[8];
-        unpack8<P>(__ldg(reinterpret_cast<const uint4*>(payload + i0)), f);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = f[j];
-        unpack8<P>(__ldg(reinterpret_cast<const uint4*>(payload + i0 + 8)), f);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[8 + j] = f[j];
-      } else {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float4 f = __ldg(reinterpret_cast<const float4*>(payload + i0) + q);
-          v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
-        }
-      }
-      if constexpr (KIND == AGM_CODEC_INT8) {
-#pragma unroll
-        for (int j = 0; j < kCodecVec; ++j) v[j] = __fmul_rn(v[j], scale);
-      }
-      if constexpr (KIND == AGM_CODEC_INT8_ROWWISE) {
-        // The scale changes wherever a row starts inside the 16-element group.
-        int64_t row = i0 / cols;
-        int64_t next = (row + 1) * cols;
-        float s = scale_value<S>(row_scales, row);
-#pragma unroll
-        for (int j = 0; j < kCodecVec; ++j) {
-          if (i0 + j >= next) {
-            ++row;
-            next += cols;
-            s = scale_value<S>(row_scales, row);
-          }
-          v[j] = __fmul_rn(v[j], s);
-        }
-      }
-      float t[kCodecVec];
-      if constexpr (MODE == AGM_APPLY_COPY) {
-#pragma unroll
-        for (int j = 0; j < kCodecVec; ++j) t[j] = round_to<OutT>(v[j]);
-      } else {
-        float cur[kCodecVec];
-        if constexpr (sizeof(OutT) == 2) {
-          float f[8];
-          unpack8<OutT>(*reinterpret_cast<const uint4*>(target + i0), f);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) cur[j] = f[j];
-          unpack8<OutT>(*reinterpret_cast<const uint4*>(target + i0 + 8), f);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) cur[8 + j] = f[j];
-        } else {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float4 f = reinterpret_cast<const float4*>(target + i0)[q];
-            cur[4 * q] = f.x; cur[4 * q + 1] = f.y; cur[4 * q + 2] = f.z; cur[4 * q + 3] = f.w;
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < kCodecVec; ++j) {
-          const float src = round_to<OutT>(v[j]);
-          t[j] = MODE == AGM_APPLY_ADD ? cur[j] + alpha * src : lerp_f(cur[j], src, alpha);
-        }
-      }
-      if constexpr (sizeof(OutT) == 2) {
-        reinterpret_cast<uint4*>(target + i0)[0] =
-            make_uint4(pack2<OutT>(t[0], t[1]), pack2<OutT>(t[2], t[3]), pack2<OutT>(t[4], t[5]), pack2<OutT>(t[6], t[7]));
-        reinterpret_cast<uint4*>(target + i0)[1] = make_uint4(pack2<OutT>(t[8], t[9]), pack2<OutT>(t[10], t[11]),
-                                                              pack2<OutT>(t[12], t[13]), pack2<OutT>(t[14], t[15]));
-      } else {
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          reinterpret_cast<float4*>(target + i0)[q] = make_float4(t[4 * q], t[4 * q + 1], t[4 * q + 2], t[4 * q + 3]);
-      }
-    }
-    for (int64_t i = nvec * kCodecVec + tid; i < n; i += stride)
+    if (KIND == AGM_CODEC_INT8_ROWWISE && cols % kCodecVec == 0)
+      decode_vectors<KIND, P, S, OutT, MODE, true>(payload, n, cols, scale, row_scales, target, alpha, tid, stride);
+    else
+      decode_vectors<KIND, P, S, OutT, MODE, false>(payload, n, cols, scale, row_scales, target, alpha, tid, stride);
+    for (int64_t i = n / kCodecVec * kCodecVec + tid; i < n; i += stride)
       decode_one<KIND, P, S, OutT, MODE>(payload, i, cols, scale, row_scales, target, alpha);
   } else {
     for (int64_t i = tid; i < n; i += stride)
@@ -172,8 +225,14 @@ __global__ void __launch_bounds__(kCodecThreads) codec_decode_kernel(const P* __
 template <int KIND, typename P, typename S, typename OutT, int MODE>
 cudaError_t launch_decode(const void* payload, int64_t n, int64_t cols, float scale, const void* row_scales,
                           void* target, float alpha, bool vec_ok, int sms, cudaStream_t s) {
+  // One wave of resident CTAs at most, each striding over the tensor.
+  int per_sm = 0;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, codec_decode_kernel<KIND, P, S, OutT, MODE>,
+                                                                kCodecThreads, 0);
+  if (e != cudaSuccess) return e;
   const int64_t want = (n / (vec_ok ? kCodecVec : 1) + kCodecThreads - 1) / kCodecThreads;
-  const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(sms) * 8)));
+  const unsigned grid = static_cast<unsigned>(
+      std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(sms) * std::max(per_sm, 1))));
   codec_decode_kernel<KIND, P, S, OutT, MODE><<<grid, kCodecThreads, 0, s>>>(
       static_cast<const P*>(payload), n, cols, scale, static_cast<const S*>(row_scales), static_cast<OutT*>(target),
       alpha, vec_ok ? 1 : 0);

@@ -235,13 +235,30 @@ __global__ void __launch_bounds__(kDispatchBlock) router_topk_kernel(
 #pragma unroll
         for (int e = 0; e < kMaxExperts; ++e) acc[t][e] = 0.f;
 
+      // The next chunk's x vectors are loaded before this chunk's FMAs (two
+      // chunks of loads in flight per lane).
+      uint4 u_next[kTokGroup];
+#pragma unroll
+      for (int t = 0; t < kTokGroup; ++t) {
+        const int64_t tok = warp_tok0 + g + t;
+        u_next[t] = (lane < nchunk && tok < n_tokens) ? __ldg(reinterpret_cast<const uint4*>(x + tok * d) + lane)
+                                                      : make_uint4(0, 0, 0, 0);
+      }
       for (int c = lane; c < nchunk; c += 32) {
         float xf[kTokGroup][8];
+        uint4 u_cur[kTokGroup];
+#pragma unroll
+        for (int t = 0; t < kTokGroup; ++t) u_cur[t] = u_next[t];
+        const int cn = c + 32;
 #pragma unroll
         for (int t = 0; t < kTokGroup; ++t) {
           const int64_t tok = warp_tok0 + g + t;
-          uint4 u = make_uint4(0, 0, 0, 0);
-          if (tok < n_tokens) u = __ldg(reinterpret_cast<const uint4*>(x + tok * d) + c);
+          u_next[t] = (cn < nchunk && tok < n_tokens) ? __ldg(reinterpret_cast<const uint4*>(x + tok * d) + cn)
+                                                       : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int t = 0; t < kTokGroup; ++t) {
+          const uint4 u = u_cur[t];
           if constexpr (sizeof(T) == 4) {
             xf[t][0] = __uint_as_float(u.x); xf[t][1] = __uint_as_float(u.y);
             xf[t][2] = __uint_as_float(u.z); xf[t][3] = __uint_as_float(u.w);
