@@ -47,7 +47,7 @@ def assert_close(ours, ref, dtype, name):
 
 
 def assert_loss_close(ours, ref, dtype, name="loss"):
-    a, b = float(ours), float(ref)
+    a, b = float(ours.detach() if torch.is_tensor(ours) else ours), float(ref.detach() if torch.is_tensor(ref) else ref)
     tol = (1e-5 if dtype == torch.float32 else 1e-3) * abs(b) + 1e-8
     assert abs(a - b) <= tol, f"{name}: {a!r} vs {b!r}"
 
