@@ -307,7 +307,12 @@ def run_ours(args, world, rank, local):
                                         shared_hidden=2 * D, batch=22, seq=1536,
                                         label="production MoE block training step")
         train["production"]["forward"] = run_forward_production(args, dev, stream)
-        train["aux_loss"] = run_aux(args, dev, stream)
+    if not args.skip_aux:
+        aux = run_aux(args, dev, stream)
+        if train is None:
+            train = {"aux_loss": aux}
+        else:
+            train["aux_loss"] = aux
     codec_leg = None if args.skip_codec else run_codec(args, dev, stream, world == 1 and not args.skip_cpu)
     report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e_value, x, decode, train, codec_leg)
 
@@ -992,6 +997,7 @@ def main():
     ap.add_argument("--skip-decode", action="store_true", help="skip the 28-layer decode leg")
     ap.add_argument("--skip-train", action="store_true", help="skip the training-step (forward + backward) leg")
     ap.add_argument("--skip-codec", action="store_true", help="skip the tensor-codec decode leg")
+    ap.add_argument("--skip-aux", action="store_true", help="skip the auxiliary router-loss leg")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
