@@ -31,6 +31,13 @@ AGM_FLAG_NO_PDL = 0x10
 AGM_FLAG_BWD_PAIR = 0x20
 AGM_CODEC_PLAIN, AGM_CODEC_INT8, AGM_CODEC_INT8_ROWWISE = 0, 1, 2
 AGM_APPLY_COPY, AGM_APPLY_LERP, AGM_APPLY_ADD = 0, 1, 2
+
+
+class AgmCodecTensor(ctypes.Structure):
+    """One entry of agm_codec_decode_batch's table (include/agillm_moe.h)."""
+    _fields_ = [("payload", ctypes.c_void_p), ("row_scales", ctypes.c_void_p), ("target", ctypes.c_void_p),
+                ("n", ctypes.c_int64), ("cols", ctypes.c_int64), ("scale", ctypes.c_float), ("kind", ctypes.c_int),
+                ("packed_dtype", ctypes.c_int), ("scales_dtype", ctypes.c_int), ("target_dtype", ctypes.c_int)]
 AGM_SWAP_ROWS_PER_EXPERT = 32
 AGM_STAGE_EVENTS = 8
 AGM_EP_STAGE_EVENTS = 9
@@ -82,6 +89,7 @@ SIGNATURES = {
     "agm_moe_backward": (_I, [_P, _I, _I, _I64, _I, _I, _I, _I, _P, _P, _P, _I, _I, _P, _P, _P, _SZ,
                               _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _I, _P]),
     "agm_codec_decode": (_I, [_P, _I, _I, _I64, _I64, ctypes.c_float, _P, _I, _P, _I, _I, ctypes.c_float, _P]),
+    "agm_codec_decode_batch": (_I, [_P, _I, _I, ctypes.c_float, _P]),
     "agm_moe_aux_saved_bytes": (_SZ, [_I64, _I, _I]),
     "agm_moe_aux_backward_workspace_bytes": (_SZ, [_I64, _I, _I]),
     "agm_moe_aux_forward": (_I, [_P, _I, _I64, _I, _I, _P, ctypes.c_double, ctypes.c_double, _P, _P, _SZ, _I, _P]),

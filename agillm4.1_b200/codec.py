@@ -11,8 +11,9 @@ then copies each fp32 value to the GPU and applies it to the parameter
 
 Here the host only decompresses (threads in parallel; zlib and zstandard
 release the GIL), the packed bytes cross PCIe (1 byte per int8 element
-instead of 4), and ``agm_codec_decode`` dequantises and applies them on the
-GPU in one pass over the parameter:
+instead of 4), and ``agm_codec_decode_batch`` dequantises and applies them on
+the GPU in one pass over each parameter, the tensors of one kind in one
+launch:
 
 * :func:`decode_tensor_state` - drop-in for ``_agillm43_decode_tensor_state``
   that returns device tensors (fp32 for the int8 kinds, the packed dtype
@@ -24,6 +25,7 @@ GPU in one pass over the parameter:
 from __future__ import annotations
 
 import concurrent.futures as cf
+import ctypes
 import os
 import zlib
 from typing import Dict, Mapping, Optional
@@ -114,17 +116,38 @@ class _Payload:
         """The dtype of the reference's decoded value."""
         return torch.float32 if self.kind_name in _KINDS else self.packed_dtype
 
-    def launch(self, target: torch.Tensor, mode: int, alpha: float, stream) -> None:
-        dev = target.device
+    def upload(self, dev):
+        """Asynchronous copies of the packed bytes (and row scales) to ``dev``."""
         q = self.packed.to(dev, non_blocking=True)
         s = self.scales.to(dev, non_blocking=True) if self.scales is not None else None
+        return q, s
+
+    def entry(self, q, s, target: torch.Tensor) -> "_lib.AgmCodecTensor":
+        """This tensor's row of agm_codec_decode_batch's table."""
         kind = _KINDS.get(self.kind_name, _lib.AGM_CODEC_PLAIN)
-        cols = self.n // self.rows if kind == _lib.AGM_CODEC_INT8_ROWWISE else 1
-        rc = load().agm_codec_decode(ptr(q), kind, _lib.dtype_code(self.packed_dtype) if kind == _lib.AGM_CODEC_PLAIN
-                                     else 0, self.n, cols, self.scale, ptr(s),
-                                     _lib.dtype_code(self.scales_dtype) if s is not None else 0, ptr(target),
-                                     _lib.dtype_code(target.dtype), mode, float(alpha), stream)
-        _lib.check(rc, "agm_codec_decode")
+        return _lib.AgmCodecTensor(
+            payload=ptr(q), row_scales=ptr(s), target=ptr(target), n=self.n,
+            cols=self.n // self.rows if kind == _lib.AGM_CODEC_INT8_ROWWISE else 1, scale=self.scale, kind=kind,
+            packed_dtype=_lib.dtype_code(self.packed_dtype) if kind == _lib.AGM_CODEC_PLAIN else 0,
+            scales_dtype=_lib.dtype_code(self.scales_dtype) if s is not None else 0,
+            target_dtype=_lib.dtype_code(target.dtype))
+
+
+def _decode_into(jobs, mode: int, alpha: float) -> None:
+    """Decode every (payload, target) pair of ``jobs`` (an iterable): the
+    packed bytes are copied to the target's device as each payload is staged
+    (while later ones still decompress), then one agm_codec_decode_batch
+    call per device decodes the lot (tensors of one signature share a
+    launch)."""
+    per_dev = {}
+    for p, target in jobs:
+        q, s = p.upload(target.device)
+        per_dev.setdefault(target.device, []).append((p.entry(q, s, target), q, s))
+    for dev, rows in per_dev.items():
+        table = (_lib.AgmCodecTensor * len(rows))(*[r[0] for r in rows])
+        rc = load().agm_codec_decode_batch(ctypes.cast(table, ctypes.c_void_p), len(rows), mode, float(alpha),
+                                           stream_handle(dev))
+        _lib.check(rc, "agm_codec_decode_batch")
 
 
 def _pinned(raw: bytes) -> torch.Tensor:
@@ -154,11 +177,13 @@ def decode_tensor_state(state, device="cuda", *, threads: Optional[int] = None) 
     if dev.type != "cuda":
         raise MoEKernelError("decode_tensor_state decodes on a CUDA device (there is no CPU path)")
     out = dict(state.get("plain") or {})
-    stream = stream_handle(dev)
-    for p in _staged(state, threads):
-        value = torch.empty(p.shape, dtype=p.value_dtype(), device=dev)
-        p.launch(value, _lib.AGM_APPLY_COPY, 1.0, stream)
-        out[p.key] = value
+
+    def jobs():
+        for p in _staged(state, threads):
+            out[p.key] = torch.empty(p.shape, dtype=p.value_dtype(), device=dev)
+            yield p, out[p.key]
+
+    _decode_into(jobs(), _lib.AGM_APPLY_COPY, 1.0)
     return out
 
 
@@ -186,14 +211,18 @@ def apply_tensor_state(state, targets: Mapping[str, torch.Tensor], *, alpha: flo
     for key in state.get("tensors") or {}:
         if not targets[key].is_cuda or not targets[key].is_contiguous():
             raise MoEKernelError(f"{key}: targets must be contiguous CUDA tensors (there is no CPU path)")
-    changed = 0
-    with torch.no_grad():
+    done = []
+
+    def jobs():
         for p in _staged(state, threads):
-            target = targets[p.key]
-            p.launch(target, mode, alpha, stream_handle(target.device))
-            # An in-place update: bump the version counter as torch's own
-            # in-place ops do, so caches keyed on it (the MoE block's packed
-            # weights) see the new values.
-            torch.autograd.graph.increment_version(target)
-            changed += 1
-    return changed
+            done.append(targets[p.key])
+            yield p, targets[p.key]
+
+    with torch.no_grad():
+        _decode_into(jobs(), mode, alpha)
+    for target in done:
+        # An in-place update: bump the version counter as torch's own
+        # in-place ops do, so caches keyed on it (the MoE block's packed
+        # weights) see the new values.
+        torch.autograd.graph.increment_version(target)
+    return len(done)

@@ -21,6 +21,7 @@
 #include <algorithm>
 #include <cstdint>
 #include <string>
+#include <vector>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -222,6 +223,146 @@ __global__ void __launch_bounds__(kCodecThreads) codec_decode_kernel(const P* __
   }
 }
 
+// ---------------------------------------------------------------------------
+// Batched decode: up to kCodecBatch tensors of one signature (pack kind,
+// payload / scale / target types, apply mode) in one launch. The tensors'
+// 16-element groups are numbered one after the other (vec_begin holds the
+// prefix sums); a thread finds its group's tensor by a scan of at most 16
+// entries of the table, which stays in the kernel's parameter space
+// (__grid_constant__). Every tensor is 16-byte aligned and, for row-wise
+// scales, has rows of a multiple of 16 elements; the n % 16 tail elements of
+// each tensor are decoded one per thread after the groups.
+// ---------------------------------------------------------------------------
+constexpr int kCodecBatch = 16;
+
+struct CodecBatch {
+  const void* payload[kCodecBatch];
+  const void* scales[kCodecBatch];
+  void* target[kCodecBatch];
+  int64_t n[kCodecBatch];
+  int64_t cols[kCodecBatch];
+  int64_t vec_begin[kCodecBatch + 1];
+  float scale[kCodecBatch];
+  int count;
+};
+
+template <int KIND, typename P, typename S, typename OutT, int MODE>
+__global__ void __launch_bounds__(kCodecThreads) codec_batch_kernel(const __grid_constant__ CodecBatch b,
+                                                                    float alpha) {
+  constexpr int U = sizeof(P) == 1 ? 4 : (sizeof(P) == 2 ? 2 : 1);
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kCodecThreads;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * kCodecThreads + threadIdx.x;
+  const int64_t total = b.vec_begin[b.count];
+  for (int64_t v0 = tid; v0 < total; v0 += stride * U) {
+    Raw16<P> raw[U];
+    Raw16<OutT> cur_raw[MODE == AGM_APPLY_COPY ? 1 : U];
+    float sc[U];
+    int tt[U];
+    int64_t ii[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t v = v0 + u * stride;
+      tt[u] = -1;
+      if (v < total) {
+        int t = 0;
+        while (t + 1 < b.count && v >= b.vec_begin[t + 1]) ++t;
+        const int64_t i0 = (v - b.vec_begin[t]) * kCodecVec;
+        tt[u] = t;
+        ii[u] = i0;
+        load_raw<P>(static_cast<const P*>(b.payload[t]), i0, raw[u], true);
+        if constexpr (KIND == AGM_CODEC_INT8_ROWWISE) {
+          const int64_t cols = b.cols[t];
+          const int64_t row = b.n[t] < (int64_t(1) << 32)
+                                  ? static_cast<int64_t>(static_cast<uint32_t>(i0) / static_cast<uint32_t>(cols))
+                                  : i0 / cols;
+          sc[u] = scale_value<S>(static_cast<const S*>(b.scales[t]), row);
+        } else {
+          sc[u] = b.scale[t];
+        }
+        if constexpr (MODE != AGM_APPLY_COPY) load_raw<OutT>(static_cast<const OutT*>(b.target[t]), i0, cur_raw[u], false);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (tt[u] < 0) continue;
+      float v[kCodecVec];
+      to_float<P>(raw[u], v);
+      if constexpr (KIND != AGM_CODEC_PLAIN) {
+#pragma unroll
+        for (int j = 0; j < kCodecVec; ++j) v[j] = __fmul_rn(v[j], sc[u]);
+      }
+      float t[kCodecVec];
+      if constexpr (MODE == AGM_APPLY_COPY) {
+#pragma unroll
+        for (int j = 0; j < kCodecVec; ++j) t[j] = round_to<OutT>(v[j]);
+      } else {
+        float cur[kCodecVec];
+        to_float<OutT>(cur_raw[u], cur);
+#pragma unroll
+        for (int j = 0; j < kCodecVec; ++j) {
+          const float src = round_to<OutT>(v[j]);
+          t[j] = MODE == AGM_APPLY_ADD ? cur[j] + alpha * src : lerp_f(cur[j], src, alpha);
+        }
+      }
+      store_target<OutT>(static_cast<OutT*>(b.target[tt[u]]), ii[u], t);
+    }
+  }
+  for (int64_t j = tid; j < static_cast<int64_t>(b.count) * kCodecVec; j += stride) {
+    const int t = static_cast<int>(j / kCodecVec);
+    const int64_t i = b.n[t] / kCodecVec * kCodecVec + j % kCodecVec;
+    if (i < b.n[t])
+      decode_one<KIND, P, S, OutT, MODE>(static_cast<const P*>(b.payload[t]), i, b.cols[t], b.scale[t],
+                                         static_cast<const S*>(b.scales[t]), static_cast<OutT*>(b.target[t]), alpha);
+  }
+}
+
+template <int KIND, typename P, typename S, typename OutT, int MODE>
+cudaError_t launch_batch(const CodecBatch& b, float alpha, int sms, cudaStream_t s) {
+  int per_sm = 0;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, codec_batch_kernel<KIND, P, S, OutT, MODE>,
+                                                                kCodecThreads, 0);
+  if (e != cudaSuccess) return e;
+  const int64_t want = (b.vec_begin[b.count] + kCodecThreads - 1) / kCodecThreads;
+  const unsigned grid = static_cast<unsigned>(
+      std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(sms) * std::max(per_sm, 1))));
+  codec_batch_kernel<KIND, P, S, OutT, MODE><<<grid, kCodecThreads, 0, s>>>(b, alpha);
+  return cudaGetLastError();
+}
+
+template <int KIND, typename P, typename S, typename OutT>
+cudaError_t batch_by_mode(int mode, const CodecBatch& b, float alpha, int sms, cudaStream_t s) {
+  switch (mode) {
+    case AGM_APPLY_COPY: return launch_batch<KIND, P, S, OutT, AGM_APPLY_COPY>(b, alpha, sms, s);
+    case AGM_APPLY_LERP: return launch_batch<KIND, P, S, OutT, AGM_APPLY_LERP>(b, alpha, sms, s);
+    default: return launch_batch<KIND, P, S, OutT, AGM_APPLY_ADD>(b, alpha, sms, s);
+  }
+}
+
+template <int KIND, typename P, typename S>
+cudaError_t batch_by_target(int target_dtype, int mode, const CodecBatch& b, float alpha, int sms, cudaStream_t s) {
+  switch (target_dtype) {
+    case AGM_F32: return batch_by_mode<KIND, P, S, float>(mode, b, alpha, sms, s);
+    case AGM_BF16: return batch_by_mode<KIND, P, S, __nv_bfloat16>(mode, b, alpha, sms, s);
+    default: return batch_by_mode<KIND, P, S, __half>(mode, b, alpha, sms, s);
+  }
+}
+
+// One launch for a table of tensors sharing kind, packed / scale / target
+// dtypes (checked by the caller).
+cudaError_t launch_batch_any(int kind, int packed_dtype, int scales_dtype, int target_dtype, int mode,
+                             const CodecBatch& b, float alpha, int sms, cudaStream_t s) {
+  if (kind == AGM_CODEC_INT8) return batch_by_target<AGM_CODEC_INT8, int8_t, float>(target_dtype, mode, b, alpha, sms, s);
+  if (kind == AGM_CODEC_INT8_ROWWISE)
+    return scales_dtype == AGM_F16
+               ? batch_by_target<AGM_CODEC_INT8_ROWWISE, int8_t, __half>(target_dtype, mode, b, alpha, sms, s)
+               : batch_by_target<AGM_CODEC_INT8_ROWWISE, int8_t, float>(target_dtype, mode, b, alpha, sms, s);
+  switch (packed_dtype) {
+    case AGM_F32: return batch_by_target<AGM_CODEC_PLAIN, float, float>(target_dtype, mode, b, alpha, sms, s);
+    case AGM_BF16: return batch_by_target<AGM_CODEC_PLAIN, __nv_bfloat16, float>(target_dtype, mode, b, alpha, sms, s);
+    default: return batch_by_target<AGM_CODEC_PLAIN, __half, float>(target_dtype, mode, b, alpha, sms, s);
+  }
+}
+
 template <int KIND, typename P, typename S, typename OutT, int MODE>
 cudaError_t launch_decode(const void* payload, int64_t n, int64_t cols, float scale, const void* row_scales,
                           void* target, float alpha, bool vec_ok, int sms, cudaStream_t s) {
@@ -272,6 +413,30 @@ int codec_fail(int code, const char* msg) {
 }
 
 int dtype_bytes(int dtype) { return dtype == AGM_F32 ? 4 : (dtype == AGM_BF16 || dtype == AGM_F16) ? 2 : 0; }
+
+// The argument checks of one tensor (AGM_OK, or the failure's code with the
+// message set).
+int check_tensor(const void* payload, int kind, int packed_dtype, int64_t n, int64_t cols, const void* row_scales,
+                 int scales_dtype, const void* target, int target_dtype) {
+  if (n < 0) return codec_fail(AGM_ERR_ARG, "n < 0");
+  if (kind != AGM_CODEC_PLAIN && kind != AGM_CODEC_INT8 && kind != AGM_CODEC_INT8_ROWWISE)
+    return codec_fail(AGM_ERR_ARG, "unknown pack kind");
+  if (!dtype_bytes(target_dtype)) return codec_fail(AGM_ERR_ARG, "target dtype must be AGM_F32, AGM_BF16 or AGM_F16");
+  if (kind == AGM_CODEC_PLAIN && !dtype_bytes(packed_dtype))
+    return codec_fail(AGM_ERR_UNSUPPORTED, "lossless payloads must be fp32, bf16 or fp16");
+  if (kind == AGM_CODEC_INT8_ROWWISE) {
+    if (cols <= 0 || n % cols) return codec_fail(AGM_ERR_ARG, "cols must divide n for row-wise int8");
+    if (scales_dtype != AGM_F32 && scales_dtype != AGM_F16)
+      return codec_fail(AGM_ERR_ARG, "row scales must be AGM_F32 or AGM_F16");
+    if (n > 0 && !row_scales) return codec_fail(AGM_ERR_ARG, "null row scales");
+  }
+  if (n == 0) return AGM_OK;
+  if (!payload || !target) return codec_fail(AGM_ERR_ARG, "null pointer");
+  const int pb = kind == AGM_CODEC_PLAIN ? dtype_bytes(packed_dtype) : 1;
+  if (reinterpret_cast<uintptr_t>(payload) % pb || reinterpret_cast<uintptr_t>(target) % dtype_bytes(target_dtype))
+    return codec_fail(AGM_ERR_ARG, "payload and target must be aligned to their element size");
+  return AGM_OK;
+}
 
 }  // namespace
 }  // namespace agm
@@ -335,6 +500,68 @@ int agm_codec_decode(const void* payload, int kind, int packed_dtype, int64_t n,
   if (e != cudaSuccess) {
     set_last_error(std::string("agm_codec_decode: ") + cudaGetErrorString(e));
     return AGM_ERR_CUDA;
+  }
+  return AGM_OK;
+}
+
+int agm_codec_decode_batch(const AgmCodecTensor* tensors, int count, int mode, float alpha, void* stream_) {
+  using namespace agm;
+  if (count < 0 || (count > 0 && !tensors)) return codec_fail(AGM_ERR_ARG, "bad tensor table");
+  if (mode != AGM_APPLY_COPY && mode != AGM_APPLY_LERP && mode != AGM_APPLY_ADD)
+    return codec_fail(AGM_ERR_ARG, "unknown apply mode");
+  for (int i = 0; i < count; ++i) {
+    const AgmCodecTensor& t = tensors[i];
+    const int rc = check_tensor(t.payload, t.kind, t.packed_dtype, t.n, t.cols, t.row_scales, t.scales_dtype,
+                                t.target, t.target_dtype);
+    if (rc) return rc;
+  }
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaStream_t s = static_cast<cudaStream_t>(stream_);
+  std::vector<char> done(static_cast<size_t>(count), 0);
+  for (int i = 0; i < count; ++i) {
+    if (done[i]) continue;
+    const AgmCodecTensor& a = tensors[i];
+    done[i] = 1;
+    if (a.n == 0) continue;
+    const bool batchable = reinterpret_cast<uintptr_t>(a.payload) % 16 == 0 &&
+                           reinterpret_cast<uintptr_t>(a.target) % 16 == 0 &&
+                           (a.kind != AGM_CODEC_INT8_ROWWISE || a.cols % kCodecVec == 0);
+    if (!batchable) {
+      const int rc = agm_codec_decode(a.payload, a.kind, a.packed_dtype, a.n, a.cols, a.scale, a.row_scales,
+                                      a.scales_dtype, a.target, a.target_dtype, mode, alpha, stream_);
+      if (rc) return rc;
+      continue;
+    }
+    // Gather the later tensors of the same signature (kind, payload, scale and
+    // target types), up to kCodecBatch per launch.
+    CodecBatch b{};
+    auto add = [&](const AgmCodecTensor& t) {
+      const int k = b.count++;
+      b.payload[k] = t.payload;
+      b.scales[k] = t.row_scales;
+      b.target[k] = t.target;
+      b.n[k] = t.n;
+      b.cols[k] = t.kind == AGM_CODEC_INT8_ROWWISE ? t.cols : 1;
+      b.scale[k] = t.scale;
+      b.vec_begin[k + 1] = b.vec_begin[k] + t.n / kCodecVec;
+    };
+    add(a);
+    for (int j = i + 1; j < count && b.count < kCodecBatch; ++j) {
+      const AgmCodecTensor& t = tensors[j];
+      if (done[j] || t.n == 0 || t.kind != a.kind || t.target_dtype != a.target_dtype) continue;
+      if (a.kind == AGM_CODEC_PLAIN && t.packed_dtype != a.packed_dtype) continue;
+      if (a.kind == AGM_CODEC_INT8_ROWWISE && (t.scales_dtype != a.scales_dtype || t.cols % kCodecVec)) continue;
+      if (reinterpret_cast<uintptr_t>(t.payload) % 16 || reinterpret_cast<uintptr_t>(t.target) % 16) continue;
+      done[j] = 1;
+      add(t);
+    }
+    const cudaError_t e = launch_batch_any(a.kind, a.packed_dtype, a.scales_dtype, a.target_dtype, mode, b, alpha,
+                                           sms, s);
+    if (e != cudaSuccess) {
+      set_last_error(std::string("agm_codec_decode_batch: ") + cudaGetErrorString(e));
+      return AGM_ERR_CUDA;
+    }
   }
   return AGM_OK;
 }

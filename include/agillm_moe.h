@@ -372,6 +372,27 @@ AGM_API int agm_codec_decode(const void* payload, int kind, int packed_dtype, in
                              const void* row_scales, int scales_dtype, void* target, int target_dtype, int mode,
                              float alpha, void* stream);
 
+/* Several tensors in as few launches as possible (the side-update consumer's
+ * loop over a decoded state, agillm41.py:6029-6046, applies every tensor of
+ * the state with the same alpha and mode): tensors that share pack kind and
+ * payload / scale / target dtypes, are 16-byte aligned and (row-wise int8)
+ * have rows of a multiple of 16 elements go up to 16 per launch; any other
+ * tensor takes agm_codec_decode. Each entry's fields mean what the arguments
+ * of agm_codec_decode mean; every entry is checked before anything launches. */
+typedef struct AgmCodecTensor {
+  const void* payload;
+  const void* row_scales;
+  void* target;
+  int64_t n;
+  int64_t cols;
+  float scale;
+  int kind;
+  int packed_dtype;
+  int scales_dtype;
+  int target_dtype;
+} AgmCodecTensor;
+AGM_API int agm_codec_decode_batch(const AgmCodecTensor* tensors, int count, int mode, float alpha, void* stream);
+
 /* ---- Auxiliary router losses --------------------------------------------
  * Replaces the per-module body of _collect_moe_aux (agillm41.py:4463-4492):
  * recompute the router logits from the stashed FFN input x [n_tokens, d]

@@ -188,6 +188,24 @@ def test_codec_decode_validates_without_a_device():
     assert call(n=0, payload=None, target=None) == 0              # nothing to do
 
 
+def test_codec_batch_validates_every_entry_first():
+    lib = _lib.load()
+    fake = 4096
+    good = _lib.AgmCodecTensor(payload=fake, row_scales=None, target=fake, n=64, cols=1, scale=0.5,
+                               kind=_lib.AGM_CODEC_INT8, packed_dtype=0, scales_dtype=0, target_dtype=_lib.AGM_F32)
+    bad = _lib.AgmCodecTensor(payload=fake, row_scales=None, target=fake, n=64, cols=7, scale=1.0,
+                              kind=_lib.AGM_CODEC_INT8_ROWWISE, packed_dtype=0, scales_dtype=_lib.AGM_F16,
+                              target_dtype=_lib.AGM_F32)
+    table = (_lib.AgmCodecTensor * 2)(good, bad)
+    # the second entry is rejected before the first one launches (no device here)
+    assert lib.agm_codec_decode_batch(ctypes.cast(table, ctypes.c_void_p), 2, _lib.AGM_APPLY_COPY, 1.0, None) == -1
+    assert "cols" in lib.agm_last_error().decode()
+    assert lib.agm_codec_decode_batch(ctypes.cast(table, ctypes.c_void_p), 1, 9, 1.0, None) == -1
+    assert lib.agm_codec_decode_batch(None, -1, _lib.AGM_APPLY_COPY, 1.0, None) == -1
+    assert lib.agm_codec_decode_batch(None, 0, _lib.AGM_APPLY_COPY, 1.0, None) == 0
+    assert ctypes.sizeof(_lib.AgmCodecTensor) == 64
+
+
 def test_training_forward_refuses_cpu_tensors():
     import torch
 

@@ -126,3 +126,43 @@ def test_update_reaches_the_moe_forward():
         y1, y2 = m(x), fresh(x)
     assert not torch.equal(y0, y1)
     assert torch.equal(y1, y2)
+
+
+def test_batch_matches_single_tensor_calls():
+    """agm_codec_decode_batch (the path of decode/apply_tensor_state) against
+    one agm_codec_decode call per tensor: 23 tensors of mixed pack kinds and
+    target dtypes, 18 of one kind (two launches), rows of 8 elements (not
+    batchable), an unaligned target view (t5); bit for bit, in lerp mode."""
+    import ctypes
+
+    from agillm41_b200 import _lib
+
+    g = torch.Generator().manual_seed(96)
+    specs = [(f"t{i}", "int8_symmetric", (1000 + i,), torch.float32) for i in range(18)]  # two launches of a kind
+    specs += [("t18", "int8_rowwise", (64, 64), torch.bfloat16), ("t19", "int8_rowwise", (37, 8), torch.float32),
+              ("t20", "fp16", (333,), torch.bfloat16), ("t21", "lossless", (515,), torch.float32),
+              ("t22", "int8_rowwise", (12, 8), torch.bfloat16)]
+    state = {k: torch.randn(shape, generator=g) for k, _, shape, _ in specs}
+    enc = codec_oracle.encode_state(state, {k: kind for k, kind, _, _ in specs})
+    staged = [codec._Payload(k, enc["tensors"][k]) for k, _, _, _ in specs]
+    base = {k: torch.randn(int(torch.tensor(shape).prod()) + 1, generator=g).to(DEV, dt) for k, _, shape, dt in specs}
+    view = {k: (base[k][1:] if k == "t5" else base[k][:-1]).view(shape) for k, _, shape, dt in specs}
+    single = {k: v.clone() for k, v in view.items()}
+    lib = _lib.load()
+    stream = _lib.stream_handle(DEV)
+    keep = []
+    rows = []
+    for p in staged:
+        q, s = p.upload(DEV)
+        keep += [q, s]
+        e = p.entry(q, s, single[p.key])
+        rc = lib.agm_codec_decode(e.payload, e.kind, e.packed_dtype, e.n, e.cols, e.scale, e.row_scales,
+                                  e.scales_dtype, e.target, e.target_dtype, _lib.AGM_APPLY_LERP, 0.4, stream)
+        _lib.check(rc, "agm_codec_decode")
+        rows.append(p.entry(q, s, view[p.key]))
+    table = (_lib.AgmCodecTensor * len(rows))(*rows)
+    _lib.check(lib.agm_codec_decode_batch(ctypes.cast(table, ctypes.c_void_p), len(rows), _lib.AGM_APPLY_LERP, 0.4,
+                                          stream), "agm_codec_decode_batch")
+    torch.cuda.synchronize()
+    for k in view:
+        assert torch.equal(view[k], single[k]), k
