@@ -79,6 +79,7 @@ SIGNATURES = {
     "agm_ep_combine": (_I, [_I, _I64, _I, _I, _I, _I, _I64, _P, _P, _SZ, _P]),
     "agm_moe_forward_noalloc": (_I, [_P, _I, _I64, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _P, _P,
                                      _I, _P]),
+    "agm_moe_noalloc_error_word": (_I, [_P]),
     "agm_moe_train_saved_bytes": (_SZ, [_I64, _I, _I, _I, _I, _I, _I, _I, _I]),
     "agm_moe_backward_workspace_bytes": (_SZ, [_I64, _I, _I, _I, _I, _I, _I, _I]),
     "agm_cast_f32": (_I, [_P, _P, _I, _I64, _P]),

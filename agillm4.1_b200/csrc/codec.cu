@@ -518,6 +518,18 @@ int agm_codec_decode_batch(const AgmCodecTensor* tensors, int count, int mode, f
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   cudaStream_t s = static_cast<cudaStream_t>(stream_);
+  // Tensors are applied in table order, as the reference's loop does: a
+  // tensor joins an earlier tensor's launch only if its target overlaps no
+  // target of that launch and none of an earlier tensor still waiting for a
+  // later launch (a repeated or overlapping target in ADD / LERP mode is a
+  // read-modify-write that must follow the one before it).
+  auto overlap = [&](int a, int b) {
+    const uintptr_t a0 = reinterpret_cast<uintptr_t>(tensors[a].target);
+    const uintptr_t b0 = reinterpret_cast<uintptr_t>(tensors[b].target);
+    const uintptr_t a1 = a0 + static_cast<uintptr_t>(tensors[a].n) * dtype_bytes(tensors[a].target_dtype);
+    const uintptr_t b1 = b0 + static_cast<uintptr_t>(tensors[b].n) * dtype_bytes(tensors[b].target_dtype);
+    return tensors[a].n > 0 && tensors[b].n > 0 && a0 < b1 && b0 < a1;
+  };
   std::vector<char> done(static_cast<size_t>(count), 0);
   for (int i = 0; i < count; ++i) {
     if (done[i]) continue;
@@ -547,13 +559,19 @@ int agm_codec_decode_batch(const AgmCodecTensor* tensors, int count, int mode, f
       b.vec_begin[k + 1] = b.vec_begin[k] + t.n / kCodecVec;
     };
     add(a);
+    std::vector<int> members(1, i);
     for (int j = i + 1; j < count && b.count < kCodecBatch; ++j) {
       const AgmCodecTensor& t = tensors[j];
       if (done[j] || t.n == 0 || t.kind != a.kind || t.target_dtype != a.target_dtype) continue;
       if (a.kind == AGM_CODEC_PLAIN && t.packed_dtype != a.packed_dtype) continue;
       if (a.kind == AGM_CODEC_INT8_ROWWISE && (t.scales_dtype != a.scales_dtype || t.cols % kCodecVec)) continue;
       if (reinterpret_cast<uintptr_t>(t.payload) % 16 || reinterpret_cast<uintptr_t>(t.target) % 16) continue;
+      bool clash = false;
+      for (int m : members) clash = clash || overlap(m, j);
+      for (int k = i + 1; k < j && !clash; ++k) clash = !done[k] && overlap(k, j);
+      if (clash) continue;
       done[j] = 1;
+      members.push_back(j);
       add(t);
     }
     const cudaError_t e = launch_batch_any(a.kind, a.packed_dtype, a.scales_dtype, a.target_dtype, mode, b, alpha,

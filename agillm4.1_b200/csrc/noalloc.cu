@@ -12,9 +12,12 @@
 // exits. Its device address is looked up once per device (cudaGetSymbolAddress,
 // on the first call made while that device is current) and then reused.
 // All calls share the array and it keeps the last call's contents; the only
-// state that must start at zero (the device error word) is cleared by every
-// call. Calls that overlap on the GPU (different streams, or different host
-// threads on one device) race on the array.
+// state that must start at zero (the device error word, the array's first int)
+// is cleared by every call, AGM_FLAG_KEEP_ERROR or not, so the word reports
+// the latest call alone. agm_moe_noalloc_error_word hands its device address
+// to the caller, who reads it with agm_read_device_error. Calls that overlap
+// on the GPU (different streams, or different host threads on one device)
+// race on the array.
 #include <mutex>
 #include <string>
 
@@ -76,7 +79,21 @@ extern "C" AGM_API int agm_moe_forward_noalloc(const void* x, int dtype, int64_t
   const int rc = scratch_address(&scratch);
   if (rc != AGM_OK) return rc;
   // Argument checks (shapes, alignment, dtype) happen in agm_moe_forward.
+  // The shared error word is always cleared first: an error left by an
+  // earlier, unrelated call must not be reported as this call's.
   return agm_moe_forward(x, dtype, n_tokens, d, n_experts, top_k, hidden, w_router, w1, b1, w2, b2, n_shared,
-                         shared_hidden, ws1, sb1, ws2, sb2, out, scratch, AGM_NOALLOC_SCRATCH_BYTES, flags, nullptr,
-                         nullptr, nullptr, nullptr, nullptr, nullptr, stream);
+                         shared_hidden, ws1, sb1, ws2, sb2, out, scratch, AGM_NOALLOC_SCRATCH_BYTES,
+                         flags & ~AGM_FLAG_KEEP_ERROR, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, stream);
+}
+
+extern "C" AGM_API int agm_moe_noalloc_error_word(int** err) {
+  if (!err) {
+    agm::set_last_error("agm_moe_noalloc_error_word: null pointer argument");
+    return AGM_ERR_ARG;
+  }
+  void* scratch = nullptr;
+  const int rc = scratch_address(&scratch);
+  if (rc != AGM_OK) return rc;
+  *err = static_cast<int*>(scratch);
+  return AGM_OK;
 }

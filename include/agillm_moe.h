@@ -180,8 +180,9 @@ AGM_API int agm_moe_forward_residual(const void* x, const void* residual, int dt
                                      void* workspace, size_t workspace_bytes, int flags, void* stream);
 
 /* Size of the scratch area compiled into the library for
- * agm_moe_forward_noalloc (32 MiB; e.g. up to about 950 tokens at d=1280,
- * H=3200, 14 experts, top-2, bf16). */
+ * agm_moe_forward_noalloc (32 MiB; e.g. up to 967 tokens at d=1280, H=3200,
+ * 14 experts, top-2, bf16 without shared experts, or 647 tokens with one
+ * shared expert of hidden 2560). */
 #define AGM_NOALLOC_SCRATCH_BYTES (32u << 20)
 
 /* agm_moe_forward for callers that cannot allocate device memory (no
@@ -194,11 +195,19 @@ AGM_API int agm_moe_forward_residual(const void* x, const void* residual, int dt
  * AGM_ERR_WORKSPACE. The first call on each device looks up the array's device
  * address (with that device current); make that first call before any stream
  * capture. All calls share the array: calls that overlap on the GPU race. The
- * device error word is the array's first int, cleared by every call.       */
+ * device error word is the array's first int, cleared by every call (the
+ * AGM_FLAG_KEEP_ERROR flag is ignored here), so it reports the latest call
+ * alone; agm_moe_noalloc_error_word gives its address.                     */
 AGM_API int agm_moe_forward_noalloc(const void* x, int dtype, int64_t n_tokens, int d, int n_experts, int top_k,
                                     int hidden, const void* w_router, const void* w1, const void* b1, const void* w2,
                                     const void* b2, int n_shared, int shared_hidden, const void* ws1, const void* sb1,
                                     const void* ws2, const void* sb2, void* out, int flags, void* stream);
+
+/* Device address of agm_moe_forward_noalloc's error word on the current
+ * device (the first int of its built-in scratch), for agm_read_device_error.
+ * Like agm_moe_forward_noalloc it allocates nothing; the first call on a
+ * device looks the address up with that device current. */
+AGM_API int agm_moe_noalloc_error_word(int** err);
 
 /* Device workspace for agm_moe_forward_host with chunks of chunk_tokens. */
 AGM_API size_t agm_moe_host_workspace_bytes(int64_t chunk_tokens, int d, int n_experts, int top_k, int hidden,
@@ -378,7 +387,10 @@ AGM_API int agm_codec_decode(const void* payload, int kind, int packed_dtype, in
  * payload / scale / target dtypes, are 16-byte aligned and (row-wise int8)
  * have rows of a multiple of 16 elements go up to 16 per launch; any other
  * tensor takes agm_codec_decode. Each entry's fields mean what the arguments
- * of agm_codec_decode mean; every entry is checked before anything launches. */
+ * of agm_codec_decode mean; every entry is checked before anything launches.
+ * The result is that of applying the entries one after another in table
+ * order: an entry whose target overlaps the target of an earlier entry (the
+ * same tensor twice, say, in ADD or LERP mode) is decoded in a later launch. */
 typedef struct AgmCodecTensor {
   const void* payload;
   const void* row_scales;

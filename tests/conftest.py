@@ -8,7 +8,10 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 GOLDEN_DIR = os.path.join(ROOT, "tests", "golden")
-REFERENCE_PY = "/root/reference/agillm41.py"
+# The reference's agillm41.py: $AGILLM41_REFERENCE, else a checkout named
+# "reference" beside this repository. Tests that import it skip without it.
+REFERENCE_PY = os.environ.get("AGILLM41_REFERENCE") or os.path.join(os.path.dirname(ROOT), "reference",
+                                                                     "agillm41.py")
 
 
 def pytest_configure(config):

@@ -166,3 +166,42 @@ def test_batch_matches_single_tensor_calls():
     torch.cuda.synchronize()
     for k in view:
         assert torch.equal(view[k], single[k]), k
+
+
+def test_batch_overlapping_targets_apply_in_order():
+    """Entries whose targets overlap (the same tensor three times, and a view
+    overlapping half of it) are applied one after another in table order, as
+    the reference's loop over keys does: in ADD mode each update must see the
+    previous one. Compared bit for bit with one agm_codec_decode call per
+    entry, in order."""
+    import ctypes
+
+    from agillm41_b200 import _lib
+
+    g = torch.Generator().manual_seed(97)
+    specs = [(f"u{i}", "int8_symmetric", (2048,)) for i in range(4)]
+    state = {k: torch.randn(shape, generator=g) for k, _, shape in specs}
+    enc = codec_oracle.encode_state(state, {k: kind for k, kind, _ in specs})
+    staged = [codec._Payload(k, enc["tensors"][k]) for k, _, _ in specs]
+    base = torch.randn(4096, generator=g).to(DEV)
+    # u0, u1, u2 -> base[0:2048]; u3 -> base[1024:3072] (overlaps the upper half)
+    tgt = {"u0": (0, 2048), "u1": (0, 2048), "u2": (0, 2048), "u3": (1024, 3072)}
+    lib = _lib.load()
+    stream = _lib.stream_handle(DEV)
+    single, batched = base.clone(), base.clone()
+    keep, rows = [], []
+    for p in staged:
+        q, s = p.upload(DEV)
+        keep += [q, s]
+        lo, hi = tgt[p.key]
+        e = p.entry(q, s, single[lo:hi])
+        _lib.check(lib.agm_codec_decode(e.payload, e.kind, e.packed_dtype, e.n, e.cols, e.scale, e.row_scales,
+                                        e.scales_dtype, e.target, e.target_dtype, _lib.AGM_APPLY_ADD, 0.5, stream),
+                   "agm_codec_decode")
+        rows.append(p.entry(q, s, batched[lo:hi]))
+    table = (_lib.AgmCodecTensor * len(rows))(*rows)
+    _lib.check(lib.agm_codec_decode_batch(ctypes.cast(table, ctypes.c_void_p), len(rows), _lib.AGM_APPLY_ADD, 0.5,
+                                          stream), "agm_codec_decode_batch")
+    torch.cuda.synchronize()
+    assert torch.equal(batched, single)
+    assert not torch.equal(batched, base)

@@ -14,7 +14,7 @@ import torch
 import agillm41_b200
 from agillm41_b200 import MoEFFN, MoEKernelError
 
-REF = "/root/reference/agillm41.py"
+from conftest import REFERENCE_PY as REF
 
 
 @pytest.fixture(scope="module")
