@@ -86,14 +86,24 @@ def test_against_golden(name):
     idx = ex["idx"].cpu().long()
     ties = tie_rows(g.logits, g.top_k)
     same = (idx == g.idx).all(1)
+    E = g.logits.shape[1]
     if g.dtype == torch.float32:
         assert bool(same[~ties].all()), f"index mismatch outside tie rows: {(~same & ~ties).nonzero().flatten()[:8]}"
         torch.testing.assert_close(ex["logits"].cpu(), g.logits, rtol=1e-5, atol=1e-5)
+        # Per-expert counts over the rows without a tie (CPU and CUDA order
+        # exact ties differently; every other row must route identically).
+        ours_c = torch.bincount(idx[~ties].flatten(), minlength=E)
+        ref_c = torch.bincount(g.idx[~ties].flatten(), minlength=E)
+        assert torch.equal(ours_c, ref_c)
         if not ties.any():
             assert torch.equal(ex["counts"].cpu().long(), g.counts)
     else:
-        frac_bad = 1.0 - same.float().mean().item()
-        assert frac_bad <= 0.02 + ties.float().mean().item(), frac_bad
+        # Every index mismatch must be explained: the kernel's logit differs
+        # from the reference's (the CPU library GEMM's bf16 rounding of its
+        # partial sums) or the reference's top k+1 logits hold an exact tie.
+        rows, unexplained = explained_index_mismatches(idx, g.idx, ex["logits"].cpu(), g.logits, g.top_k)
+        assert not unexplained, f"unexplained index mismatches at rows {unexplained[:10]}"
+        assert int(rows.numel()) == int((~same).sum())
     assert_close_rows(out, g.out, same, g.dtype)
 
 
