@@ -81,11 +81,21 @@ def load_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clock/throttle sampling while the timed region runs."""
+    """nvidia-smi clock/throttle sampling (every 20 ms) around a timed region.
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    The sampler is started before the warm-up (nvidia-smi takes ~0.1 s to
+    produce its first sample) and stopped after the last pass over the same
+    workload. ``mark_start()`` / ``mark_stop()`` bracket the timed region on
+    the host clock; ``summary()`` reports the samples whose timestamps fall in
+    that window, and when the window holds fewer than 5 (a short timed
+    region), the samples of the whole loaded period (warm-up, timed region and
+    the per-stage pass, all the same forward) instead, saying which.
+    """
+
+    QUERY = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    PERIOD_MS = 20
 
     def __init__(self, device):
         # nvidia-smi numbers GPUs differently from CUDA under CUDA_VISIBLE_DEVICES: use the UUID.
@@ -95,6 +105,7 @@ class ClockSampler:
             self.gpu = str(device.index if isinstance(device, torch.device) else device)
         self.proc = None
         self.path = None
+        self.t0 = self.t1 = None
 
     def __enter__(self):
         try:
@@ -102,11 +113,18 @@ class ClockSampler:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", str(self.PERIOD_MS)],
                                          stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(0.3)               # let nvidia-smi start sampling before the load begins
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
+
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_stop(self):
+        self.t1 = time.time()
 
     def __exit__(self, *exc):
         if self.proc is not None:
@@ -115,6 +133,16 @@ class ClockSampler:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+
+    @staticmethod
+    def _ts(text):
+        import datetime
+        for fmt in ("%Y/%m/%d %H:%M:%S.%f", "%Y/%m/%d %H:%M:%S"):
+            try:
+                return datetime.datetime.strptime(text.strip(), fmt).timestamp()
+            except ValueError:
+                continue
+        return None
 
     def summary(self):
         if self.proc is None or not self.path or not os.path.exists(self.path):
@@ -128,13 +156,24 @@ class ClockSampler:
         os.unlink(self.path)
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        window = "whole loaded period (warm-up, timed region, per-stage pass)"
+        if self.t0 is not None and self.t1 is not None:
+            # nvidia-smi prints local time; allow one period of slack at each end
+            slack = self.PERIOD_MS / 1000.0
+            inside = []
+            for r in rows:
+                t = self._ts(r[0])
+                if t is not None and self.t0 - slack <= t <= self.t1 + slack:
+                    inside.append(r)
+            if len(inside) >= 5:
+                rows, window = inside, "timed region"
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
         mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
         loaded = [s for s in sm if mx and s > 0.3 * max(mx)] or sm
         return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows),
+                "reasons": reasons, "samples": len(rows), "window": window, "period_ms": self.PERIOD_MS,
                 "power_w_max": max((float(r[3]) for r in rows if r[3].replace(".", "").isdigit()), default=None)}
 
 
@@ -195,7 +234,12 @@ def cpu_model():
 
 
 def run_reference(args, world, rank):
-    """--impl reference: the reference's CPU path (oracle) on the host cores."""
+    """--impl reference: the reference's CPU path (the oracle, i.e. the
+    reference's torch op sequence) on the host cores, on a 2,048-token sample
+    of the workload per step. Also reported (key ``gpu``): the same op
+    sequence in bf16 on this B200 over the whole 73,728-token workload, the
+    reference's own GPU forward (a library GEMM per linear, 28 host syncs per
+    block) for like-for-like context."""
     if rank != 0:
         return
     from oracle import reference_moe
@@ -213,18 +257,50 @@ def run_reference(args, world, rank):
                 times.append(time.perf_counter() - t0)
     total = sum(times)
     value = sample * len(times) / total
+    cfg = workload_config(world)
+    cfg["sample"] = f"{sample} tokens of the B{BATCH} L{SEQ} workload per step (fp32, host cores)"
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / len(times),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded N(0,1) input, N(0,0.02^2) weights)",
-        "config": workload_config(world),
+        "config": cfg,
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": f"{sample} tokens of the workload per step, fp32, torch.set_num_threads({threads}), "
                                    f"CPU {cpu_model()}"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if torch.cuda.is_available() and not args.skip_reference_gpu:
+        line["gpu"] = reference_gpu_rate(args)
     print(json.dumps(line), flush=True)
+
+
+def reference_gpu_rate(args):
+    """The reference's op sequence (oracle/reference_moe.py restates
+    MoEFFN.forward, agillm41.py:4389-4431) in bf16 on one GPU over the whole
+    B48 x L1536 workload, CUDA-event timed; inputs resident in HBM."""
+    from oracle import reference_moe
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    N = BATCH * SEQ
+    sd = reference_moe.make_state(D, HIDDEN, EXPERTS, SEED, dtype=torch.bfloat16, device=dev)
+    x = reference_moe.make_input(N, D, SEED, dtype=torch.bfloat16, device=dev)
+    with torch.no_grad():
+        for _ in range(3):
+            reference_moe.moe_forward(x, sd, TOP_K)
+        torch.cuda.synchronize(dev)
+        steps = 10
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            reference_moe.moe_forward(x, sd, TOP_K)
+        e1.record()
+        torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / steps
+    return {"value": N / (ms / 1000.0), "unit": UNIT, "ms_per_step": round(ms, 3), "steps": steps,
+            "workload": f"B{BATCH} L{SEQ} ({N} tokens) d{D} E{EXPERTS} H{HIDDEN} top{TOP_K} bf16, seed {SEED}",
+            "what": "the reference's torch op sequence (router Linear, topk, softmax, per-(rank, expert) nonzero, "
+                    "index_select, expert Linear-ReLU-Linear, index_add_) on one B200, library kernels"}
 
 
 def workload_config(world, tokens=BATCH * SEQ):
@@ -243,48 +319,46 @@ def run_ours(args, world, rank, local):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     N = args.tokens
-    sd = synthetic.make_state(D, HIDDEN, EXPERTS, SEED + rank * 1000, dtype=torch.bfloat16, device=dev)
+    sd = synthetic.make_state(D, HIDDEN, EXPERTS, SEED, dtype=torch.bfloat16, device=dev)
     x = synthetic.make_input(N, D, SEED + rank * 1000, dtype=torch.bfloat16, device=dev)
-    w1 = torch.stack([sd[f"experts.{e}.0.weight"] for e in range(EXPERTS)]).contiguous()
-    b1 = torch.stack([sd[f"experts.{e}.0.bias"] for e in range(EXPERTS)]).contiguous()
-    w2 = torch.stack([sd[f"experts.{e}.2.weight"] for e in range(EXPERTS)]).contiguous()
-    b2 = torch.stack([sd[f"experts.{e}.2.bias"] for e in range(EXPERTS)]).contiguous()
-    wr = sd["router.weight"].contiguous()
+    w1, b1, w2, b2, wr = pack_weights(sd)
     out = torch.empty_like(x)
     stream = torch.cuda.current_stream(dev)
 
     def step(events=None):
         ops.moe_forward(x, wr, w1, b1, w2, b2, TOP_K, out=out, stage_events=events)
 
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    from agillm41_b200._lib import read_device_error
-    err = read_device_error(ops.Workspace.get(dev, 0)[:4].view(torch.int32))
-    if err:
-        raise RuntimeError(f"device error word 0x{err:x} after warm-up")
-
-    # ---- timed region (device time) ----
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier(world)
-    torch.cuda.synchronize()
     with ClockSampler(dev) as clk:
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        from agillm41_b200._lib import read_device_error
+        err = read_device_error(ops.Workspace.get(dev, 0)[:4].view(torch.int32))
+        if err:
+            raise RuntimeError(f"device error word 0x{err:x} after warm-up")
+
+        # ---- timed region (device time) ----
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier(world)
+        torch.cuda.synchronize()
+        clk.mark_start()
         start.record(stream)
         for i in range(args.steps):
             step()
         stop.record(stream)
         torch.cuda.synchronize()
-    barrier(world)
-    ms_total = start.elapsed_time(stop)
-    ms_total = max_over_ranks(ms_total, world)
-    # ---- per-stage breakdown: a second pass with CUDA events between the
-    # kernels (not part of the headline number; events between kernels keep
-    # the next kernel from starting early) ----
-    n_ev = max(3, min(args.steps, 50))
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(8)] for _ in range(n_ev)]
-    for i in range(n_ev):
-        step(evs[i])
-    torch.cuda.synchronize()
+        clk.mark_stop()
+        barrier(world)
+        ms_total = start.elapsed_time(stop)
+        ms_total = max_over_ranks(ms_total, world)
+        # ---- per-stage breakdown: a second pass with CUDA events between the
+        # kernels (not part of the headline number; events between kernels keep
+        # the next kernel from starting early) ----
+        n_ev = max(3, min(args.steps, 50))
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(8)] for _ in range(n_ev)]
+        for i in range(n_ev):
+            step(evs[i])
+        torch.cuda.synchronize()
     stage_ms = {s: 0.0 for s in STAGES}
     for e in evs:
         for j, s in enumerate(STAGES):
@@ -292,11 +366,13 @@ def run_ours(args, world, rank, local):
     stage_ms = {s: v / n_ev for s, v in stage_ms.items()}
     clocks = clk.summary()
     value = N * world * args.steps / (ms_total / 1000.0)
+    parity = None if args.skip_parity else parity_check(x, wr, w1, b1, w2, b2, out)
 
     if args.skip_e2e:
         e2e_value = None
     else:
         e2e_value = run_e2e(args, world, dev, sd, x, out, N, stream)
+        e2e_value["copy_roofline"] = copy_roofline(dev, x.numel() * 2, e2e_value["value"], N)
     decode = None if args.skip_decode else run_decode(args, dev, stream)
     train = None
     if not args.skip_train:
@@ -314,7 +390,156 @@ def run_ours(args, world, rank, local):
         else:
             train["aux_loss"] = aux
     codec_leg = None if args.skip_codec else run_codec(args, dev, stream, world == 1 and not args.skip_cpu)
-    report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e_value, x, decode, train, codec_leg)
+    skewed = None if args.skip_skewed else run_skewed_single(args, dev, stream)
+    report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e_value, x, decode, train, codec_leg,
+           parity=parity, skewed=skewed)
+
+
+def pack_weights(sd, experts=EXPERTS):
+    """[E, ...] expert weight stacks and the router weight of a state dict."""
+    w1 = torch.stack([sd[f"experts.{e}.0.weight"] for e in range(experts)]).contiguous()
+    b1 = torch.stack([sd[f"experts.{e}.0.bias"] for e in range(experts)]).contiguous()
+    w2 = torch.stack([sd[f"experts.{e}.2.weight"] for e in range(experts)]).contiguous()
+    b2 = torch.stack([sd[f"experts.{e}.2.bias"] for e in range(experts)]).contiguous()
+    return w1, b1, w2, b2, sd["router.weight"].contiguous()
+
+
+def parity_check(x, wr, w1, b1, w2, b2, out, slice_tokens=4096):
+    """Parity of the timed forward's output (run after the timed region).
+
+    Routing: the reference computes its router logits with torch's library
+    GEMM (``F.linear(x, W_r).float()``, agillm41.py:4399) and picks
+    ``topk`` of them (4418). The kernel's routing is compared with that over
+    the whole workload: tokens routed differently, and how many of those are
+    explained (the kernel's logit differs from the library's, whose bf16
+    rounding of split-K partial sums is not the correctly rounded value, or
+    the library's top k+1 logits hold an exact tie).
+    Output: on the first ``slice_tokens`` tokens whose routing matches, the
+    largest error of the timed output against an fp32 evaluation of the
+    block's formula (gate-weighted FC2(ReLU(FC1 x)) over the chosen experts,
+    from the same bf16 weights and gates), and the fraction of elements
+    outside the bf16 parity bound 1e-2 + 2e-2 |ref|.
+    """
+    import torch.nn.functional as F
+    from agillm41_b200 import ops
+
+    with torch.no_grad():
+        lib_logits = F.linear(x, wr).float()
+        ref_idx = torch.topk(lib_logits, TOP_K, dim=-1).indices
+        _, ex = ops.moe_forward(x, wr, w1, b1, w2, b2, TOP_K, want=("idx", "gates", "logits"))
+        idx = ex["idx"].long()
+        diff = (idx != ref_idx).any(dim=1)
+        n_diff = int(diff.sum())
+        logit_differs = (ex["logits"] != lib_logits).any(dim=1)
+        top = torch.topk(lib_logits, TOP_K + 1, dim=-1).values
+        tie = (top[:, 1:] == top[:, :-1]).any(dim=1)
+        explained = int((diff & (logit_differs | tie)).sum())
+        n = min(slice_tokens, x.shape[0])
+        ok = ~diff[:n]
+        xs = x[:n].float()
+        gates = ex["gates"][:n].float()
+        ref = torch.zeros(n, D, dtype=torch.float32, device=x.device)
+        for r in range(TOP_K):
+            for e in range(EXPERTS):
+                rows = (idx[:n, r] == e).nonzero().flatten()
+                if rows.numel() == 0:
+                    continue
+                h = torch.relu(xs[rows] @ w1[e].float().t() + b1[e].float())
+                h = h.to(torch.bfloat16).float()            # the reference rounds the hidden to the dtype
+                y = h @ w2[e].float().t() + b2[e].float()
+                ref.index_add_(0, rows, y * gates[rows, r:r + 1])
+        o = out[:n].float()
+        err = (o - ref).abs()[ok]
+        bound = 1e-2 + 2e-2 * ref.abs()[ok]
+    return {"tokens": int(x.shape[0]), "routed_differently": n_diff, "explained": explained,
+            "unexplained": n_diff - explained,
+            "routing_reference": "torch F.linear(x, W_r).float() then topk (the reference's library GEMM)",
+            "output_slice_tokens": n, "output_rows_compared": int(ok.sum()),
+            "max_abs_err": float(err.max()) if err.numel() else 0.0,
+            "frac_outside_bf16_bound": float((err > bound).float().mean()) if err.numel() else 0.0,
+            "output_reference": "fp32 evaluation of sum_r g_r FC2_e(ReLU(FC1_e x)) from the bf16 weights and "
+                                "the kernel's gates, hidden rounded to bf16"}
+
+
+def copy_roofline(dev, nbytes, e2e_tokens_per_s, n_tokens, reps=10):
+    """Pinned host<->device copy rates on this box, the ceiling of the
+    end-to-end leg: H2D alone, D2H alone, and both at once on two streams
+    (what the host pipeline overlaps), each of ``nbytes`` per step. The e2e
+    fraction is the bidirectional copy time of one step's input and output
+    over the e2e step time."""
+    h_in = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    h_out = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    d_in = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    d_out = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    s1, s2 = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+    def run(h2d, d2h, n):
+        for _ in range(n):
+            if h2d:
+                with torch.cuda.stream(s1):
+                    d_in.copy_(h_in, non_blocking=True)
+            if d2h:
+                with torch.cuda.stream(s2):
+                    h_out.copy_(d_out, non_blocking=True)
+
+    def timed(h2d, d2h):
+        run(h2d, d2h, 2)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        run(h2d, d2h, reps)
+        torch.cuda.synchronize()
+        return (time.perf_counter() - t0) / reps
+
+    t_h2d, t_d2h, t_bi = timed(True, False), timed(False, True), timed(True, True)
+    e2e_step = n_tokens / e2e_tokens_per_s
+    return {"bytes_each_way": nbytes, "h2d_gbs": round(nbytes / t_h2d / 1e9, 2),
+            "d2h_gbs": round(nbytes / t_d2h / 1e9, 2), "bidirectional_gbs_each_way": round(nbytes / t_bi / 1e9, 2),
+            "bidirectional_ms": round(1000 * t_bi, 3), "e2e_ms_per_step": round(1000 * e2e_step, 3),
+            "frac": round(t_bi / e2e_step, 3),
+            "note": "pinned buffers, host wall clock over 10 copies; frac = bidirectional copy time of one step's "
+                    "input and output / e2e step time"}
+
+
+def skewed_workload(dev, rank, n_tokens):
+    """The expert-parallel configuration's per-rank workload: B x L tokens of
+    this rank (input seed 3 + 1000 * rank), weights seed 3 whose router
+    carries the Zipf(1.2) per-expert logit bias (~5:1 max/mean expert load)."""
+    from agillm41_b200 import synthetic
+
+    bias = synthetic.zipf_logit_bias(EXPERTS, EP_SEED, s=ZIPF_S, scale=ZIPF_SCALE)
+    sd = synthetic.make_state(D, HIDDEN, EXPERTS, EP_SEED, dtype=torch.bfloat16, device=dev,
+                              router_logit_bias=bias)
+    x = synthetic.make_input(n_tokens, D, EP_SEED + 1000 * rank, dtype=torch.bfloat16, device=dev,
+                             pin_feature0=True)
+    return x, pack_weights(sd)
+
+
+def run_skewed_single(args, dev, stream):
+    """The skewed (Zipf) routing workload of the expert-parallel runs on one
+    GPU: the same per-rank work as ``skewed`` at N > 1, so that its scaling
+    compares like with like."""
+    from agillm41_b200 import ops
+
+    x, (w1, b1, w2, b2, wr) = skewed_workload(dev, 0, args.tokens)
+    out = torch.empty_like(x)
+    for _ in range(max(3, args.warmup)):
+        ops.moe_forward(x, wr, w1, b1, w2, b2, TOP_K, out=out)
+    torch.cuda.synchronize()
+    steps = max(10, min(args.steps, 100))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        ops.moe_forward(x, wr, w1, b1, w2, b2, TOP_K, out=out)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    _, ex = ops.moe_forward(x, wr, w1, b1, w2, b2, TOP_K, want=("counts",))
+    c = ex["counts"].float()
+    return {"workload": f"MoE block forward, {args.tokens} tokens d{D} E{EXPERTS} H{HIDDEN} top{TOP_K} bf16, "
+                        f"Zipf({ZIPF_S}) router logit bias x{ZIPF_SCALE} (seed {EP_SEED})",
+            "value": args.tokens / (ms / 1000.0), "unit": UNIT, "ms_per_step": round(ms, 4), "steps": steps,
+            "expert_load_max_over_mean": round(float(c.max() / c.mean()), 3),
+            "placement": "single GPU (all experts)"}
 
 
 def run_forward_production(args, dev, stream):
@@ -933,14 +1158,16 @@ def gemm_kernel_name(n_tokens):
     return "grouped_gemm_tc_kernel (FC1+FC2, tcgen05, one CTA per tile)"
 
 
-def report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e, x, decode=None, train=None, codec=None):
+def report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e, x, decode=None, train=None, codec=None,
+           parity=None, skewed=None):
     if rank != 0:
         return
     peaks = load_peaks()
     gemm_ms = (stage_ms["fc1"] + stage_ms["fc2"]) / 2.0          # average launch of the grouped GEMM
     gemm_flop_per_launch = FLOP_PER_TOKEN * N / 2.0
     achieved_tf = gemm_flop_per_launch / (gemm_ms / 1000.0) / 1e12
-    traffic = load_traffic().get("grouped_gemm_fc1_fc2_avg_bytes_per_launch")
+    traffic_rec = load_traffic()
+    traffic = traffic_rec.get("grouped_gemm_fc1_fc2_avg_bytes_per_launch")
 
     def hbm(stage, per_tok):
         gbs = per_tok * N / (stage_ms[stage] / 1000.0) / 1e9
@@ -962,11 +1189,15 @@ def report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e, x, deco
         "e2e": e2e,
         "gpu_launches": KERNELS_PER_STEP * args.steps,
         "roofline": {"kernel": gemm_kernel_name(N), "bound": "tensor",
-                     "achieved": round(achieved_tf, 1), "peak": peaks["tf_sus"], "unit": "TFLOP/s",
-                     "frac": round(achieved_tf / peaks["tf_sus"], 3),
-                     "frac_of_burst_peak": round(achieved_tf / peaks["tf"], 3),
-                     "peak_source": f"{peaks['src']} bf16 sustained (burst {peaks['tf']})",
-                     "traffic": traffic, "flop_per_launch": gemm_flop_per_launch},
+                     "achieved": round(achieved_tf, 1), "peak": peaks["tf"], "unit": "TFLOP/s",
+                     "frac": round(achieved_tf / peaks["tf"], 3),
+                     "frac_of_sustained_peak": round(achieved_tf / peaks["tf_sus"], 3),
+                     "peak_source": f"{peaks['src']} bf16 burst (the GEMM launches are timed inside a "
+                                    f"{ms_total:.0f} ms region, not a seconds-long loop; sustained "
+                                    f"{peaks['tf_sus']})",
+                     "traffic": traffic,
+                     "traffic_source": traffic_rec.get("source", "not measured in this run") if traffic else None,
+                     "flop_per_launch": gemm_flop_per_launch},
         "stages": {
             "router": hbm("router", ROUTER_BYTES), "permute": hbm("permute", PERMUTE_BYTES),
             "combine": hbm("combine", COMBINE_BYTES),
@@ -976,6 +1207,10 @@ def report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e, x, deco
         "cpu_baseline": cpu,
         "clocks": clocks,
     }
+    if parity is not None:
+        line["parity"] = parity
+    if skewed is not None:
+        line["skewed"] = skewed
     if decode is not None:
         line["decode"] = decode
     if train is not None:
@@ -999,6 +1234,10 @@ def main():
     ap.add_argument("--skip-train", action="store_true", help="skip the training-step (forward + backward) leg")
     ap.add_argument("--skip-codec", action="store_true", help="skip the tensor-codec decode leg")
     ap.add_argument("--skip-aux", action="store_true", help="skip the auxiliary router-loss leg")
+    ap.add_argument("--skip-parity", action="store_true", help="skip the routing/output parity check")
+    ap.add_argument("--skip-skewed", action="store_true", help="skip the skewed-routing single-GPU leg")
+    ap.add_argument("--skip-reference-gpu", action="store_true",
+                    help="--impl reference: skip the reference's op sequence timed on the GPU")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
