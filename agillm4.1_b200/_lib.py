@@ -28,6 +28,7 @@ AGM_FLAG_KEEP_ERROR = 0x2
 AGM_FLAG_NO_PAIR = 0x4
 AGM_FLAG_NO_SWAP = 0x8
 AGM_FLAG_NO_PDL = 0x10
+AGM_EP_HOLDERS, AGM_EP_BALANCED, AGM_EP_LOCAL = 0, 1, 2
 AGM_FLAG_BWD_PAIR = 0x20
 AGM_CODEC_PLAIN, AGM_CODEC_INT8, AGM_CODEC_INT8_ROWWISE = 0, 1, 2
 AGM_APPLY_COPY, AGM_APPLY_LERP, AGM_APPLY_ADD = 0, 1, 2
@@ -63,20 +64,22 @@ SIGNATURES = {
     "agm_moe_host_workspace_bytes": (_SZ, [_I64, _I, _I, _I, _I, _I, _I, _I]),
     "agm_moe_forward_host": (_I, [_P, _I, _I64, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _P, _P, _P,
                                   _SZ, _I64, _I, _P]),
-    "agm_ep_comm_bytes": (_SZ, [_I, _I64, _I, _I]),
+    "agm_ep_max_rows": (_I64, [_I64, _I, _I]),
+    "agm_ep_comm_bytes": (_SZ, [_I, _I64, _I64, _I, _I]),
+    "agm_ep_home_offset": (_I64, [_I, _I64, _I, _I]),
     "agm_ep_alloc": (_I, [_SZ, _P]),
     "agm_ep_free": (_I, [_P]),
     "agm_ep_ipc_handle": (_I, [_P, _P]),
     "agm_ep_ipc_open": (_I, [_P, _P]),
     "agm_ep_ipc_close": (_I, [_P]),
     "agm_ep_workspace_bytes": (_SZ, [_I64, _I, _I, _I, _I, _I64, _I]),
-    "agm_ep_forward": (_I, [_P, _I, _I64, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _I64,
+    "agm_ep_forward": (_I, [_P, _I, _I64, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _P, _I, _I, _P, _I64, _I64,
                             ctypes.c_uint64, _P, _P, _SZ, _I, _P, _P]),
-    "agm_ep_dispatch": (_I, [_P, _I, _I64, _I, _I, _I, _I, _P, _I, _I, _I, _I, _I, _P, _I64, ctypes.c_uint64, _P,
+    "agm_ep_dispatch": (_I, [_P, _I, _I64, _I, _I, _I, _I, _P, _I, _P, _I, _I, _P, _I64, _I64, ctypes.c_uint64, _P,
                              _SZ, _I, _P, _P]),
-    "agm_ep_expert": (_I, [_I, _I64, _I, _I, _I, _I, _P, _P, _P, _P, _I, _I, _I, _P, _I64, ctypes.c_uint64, _P, _SZ,
-                           _I, _P, _P]),
-    "agm_ep_combine": (_I, [_I, _I64, _I, _I, _I, _I, _I64, _P, _P, _SZ, _P]),
+    "agm_ep_expert": (_I, [_I, _I64, _I, _I, _I, _I, _P, _P, _P, _P, _I, _I, _I, _P, _I64, _I64, ctypes.c_uint64, _P,
+                           _SZ, _I, _P, _P]),
+    "agm_ep_combine": (_I, [_I, _I64, _I, _I, _I, _I, _I64, _P, _P, _P, _SZ, _P]),
     "agm_moe_forward_noalloc": (_I, [_P, _I, _I64, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _P, _P,
                                      _I, _P]),
     "agm_moe_noalloc_error_word": (_I, [_P]),

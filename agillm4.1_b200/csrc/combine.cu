@@ -158,20 +158,6 @@ struct LocalY {
   __device__ __forceinline__ static uint4 load(const uint4* p) { return __ldg(p); }
 };
 
-// Expert-parallel source: the row lives in the result buffer of the rank that
-// computed it (read over NVLink for peers).
-struct EpY {
-  const EpRoute* route;
-  int nchunk;
-  __device__ __forceinline__ const uint4* row(int64_t p) const {
-    int r = 0;
-    const int64_t drow = ep_dest_row(route, p, &r);
-    return drow < 0 ? nullptr : reinterpret_cast<const uint4*>(route->peer_y[r]) + drow * nchunk;
-  }
-  // Rows written by other GPUs: cache in L2 only (ld.global.cg).
-  __device__ __forceinline__ static uint4 load(const uint4* p) { return __ldcg(p); }
-};
-
 template <typename T, int K_MAX, class Src>
 __global__ void __launch_bounds__(256) combine_kernel(Src ysrc, const int32_t* __restrict__ row_of,
                                                       const T* __restrict__ gates, int64_t n_tokens, int d, int k,
@@ -276,23 +262,6 @@ cudaError_t combine(int dtype, const void* y, const int32_t* row_of, const void*
     case AGM_F16:
       return combine_local<__half>(y, row_of, gates, n, d, k, shared_y, n_shared, shared_stride, residual, out,
                                    num_sms, stream);
-    default:
-      return cudaErrorInvalidValue;
-  }
-}
-
-cudaError_t combine_ep(int dtype, const EpRoute* route, const int32_t* row_of, const void* gates, int64_t n, int d,
-                       int k, void* out, int num_sms, cudaStream_t stream) {
-  switch (dtype) {
-    case AGM_F32:
-      return launch_combine<float>(EpY{route, d * 4 / 16}, row_of, gates, n, d, k, nullptr, 0, 0, nullptr, out,
-                                   num_sms, stream);
-    case AGM_BF16:
-      return launch_combine<__nv_bfloat16>(EpY{route, d * 2 / 16}, row_of, gates, n, d, k, nullptr, 0, 0, nullptr,
-                                           out, num_sms, stream);
-    case AGM_F16:
-      return launch_combine<__half>(EpY{route, d * 2 / 16}, row_of, gates, n, d, k, nullptr, 0, 0, nullptr, out,
-                                    num_sms, stream);
     default:
       return cudaErrorInvalidValue;
   }

@@ -324,11 +324,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if (col + 32 < n_valid)
             args.relu_bits[static_cast<int64_t>(w0 + 1) * args.ld_bits + row] = static_cast<uint32_t>(bits >> 32);
         }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(&tmC, stg, n0 + col, my_m * kBM + quarter * 32);
-          bulk_commit_group();
+        if (args.tile_dst) {
+          // This tile's rows go to their own buffer (expert parallelism: the
+          // token owner's home rows, possibly in a peer GPU's memory): read
+          // the staged chunk back unswizzled, 4 rows of 128 B per store.
+          __syncwarp();
+          uint8_t* dst = reinterpret_cast<uint8_t*>(args.tile_dst[my_m]) +
+                         (static_cast<int64_t>(quarter * 32) * args.ldc + n0 + col) * sizeof(T);
+          const int sub = lane >> 3, q = lane & 7;
+          const bool col_ok = col + q * 8 < n_valid;
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            const int r = it * 4 + sub;
+            const uint4 v = *reinterpret_cast<const uint4*>(stg + r * 128 + ((q ^ (r & 7)) << 4));
+            if (col_ok) *reinterpret_cast<uint4*>(dst + (static_cast<int64_t>(r) * args.ldc + q * 8) * sizeof(T)) = v;
+          }
+          __syncwarp();
+        } else {
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, stg, n0 + col, my_m * kBM + quarter * 32);
+            bulk_commit_group();
+          }
         }
       }
       tc_fence_before();
@@ -345,6 +363,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       asm volatile("fence.proxy.async.global;" ::: "memory");
       __threadfence_system();
     }
+    if (args.tile_dst) __threadfence_system();  // every lane stored rows, some into peers' memory
     __syncwarp();
   }
 

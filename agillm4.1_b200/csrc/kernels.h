@@ -70,15 +70,20 @@ struct GemmArgs {
   // mask for the ReLU backward instead of re-reading c).
   uint32_t* relu_bits = nullptr;
   int64_t ld_bits = 0;
+  // CTA-pair kernel only, nullable: row tile t's 128 output rows go to the
+  // 16-bit row-major buffer at address tile_dst[t] (row stride ldc elements)
+  // instead of c, e.g. the token owner's buffer on a peer GPU (expert
+  // parallelism); stored with 16-byte vector stores.
+  const uint64_t* tile_dst = nullptr;
 };
 
 // Expert-parallel routing of one rank's permuted rows (see ep_p2p.cu): a list
 // of segments of its x_perm tiles; segment s sends tiles [seg_lo, seg_hi) to
 // rank seg_rank, landing at tile seg_base of that rank's receive buffer
-// (at most seg_limit tiles fit). peer_recv/peer_y are the device addresses of
-// every rank's receive and result buffers as mapped into this process.
+// (at most seg_limit tiles fit). peer_recv holds the device addresses of
+// every rank's receive buffer as mapped into this process.
 constexpr int kEpMaxRanks = 16;
-constexpr int kEpMaxSegs = 2 * kEpMaxRanks;
+constexpr int kEpMaxSegs = 64;
 struct EpRoute {
   int world;
   int rank;
@@ -89,11 +94,11 @@ struct EpRoute {
   int64_t seg_base[kEpMaxSegs];
   int64_t seg_limit[kEpMaxSegs];
   uint64_t peer_recv[kEpMaxRanks];
-  uint64_t peer_y[kEpMaxRanks];
 };
 
-// Address of permuted row p on the rank that computes it: base[] is peer_recv
-// or peer_y. nullptr if the row is not sent (or would overflow).
+// Row index of permuted row p in the receive buffer of the rank that
+// computes it (that rank in *dest_rank); -1 if the row is not sent (or would
+// overflow).
 __device__ __forceinline__ int64_t ep_dest_row(const EpRoute* route, int64_t p, int* dest_rank) {
   const int64_t t = p >> 7;
   const int n = route->n_seg;
@@ -152,8 +157,6 @@ cudaError_t permute_rows(const void* x, int elem_bytes, int64_t n_tokens, int d,
 cudaError_t permute_rows_ep(const void* x, int elem_bytes, int64_t n_tokens, int d, int k, int E, const int32_t* idx,
                             const int32_t* block_off, const int32_t* seg_start, const int32_t* counts,
                             int64_t max_rows, const EpRoute* route, int32_t* row_of, int* err, cudaStream_t stream);
-cudaError_t combine_ep(int dtype, const EpRoute* route, const int32_t* row_of, const void* gates, int64_t n, int d,
-                       int k, void* out, int num_sms, cudaStream_t stream);
 // force_bn: 0 = auto, 128 / 256 = one-CTA tile width, -1 = CTA pairs,
 // -2 = swapped operands over expert segments (args.seg_start / seg_count).
 cudaError_t grouped_gemm(int dtype, const void* a, int64_t a_rows, const void* w, const GemmArgs& args, bool relu,

@@ -29,6 +29,11 @@ Placement:
   and computes its own tiles up to an equal share of the total; only the
   excess moves (to the ranks below their share), so the exchange carries just
   the imbalance between the ranks' token counts.
+* ``"replicated"`` (peer-memory forward only): the static ownership plus
+  replicas of the hottest experts, at most ``budget`` extra experts per rank
+  (:func:`choose_replicas`, from a profile of per-expert counts); each call
+  splits a replicated expert's rows among its holders by water-filling their
+  loads (:func:`plan_cuts`).
 
 Rows are independent in the MoE block, so the output of every token is
 bit-identical to the single-GPU forward of the same token.
@@ -54,6 +59,192 @@ def static_owner_ranges(n_experts: int, world: int) -> List[range]:
         out.append(range(e, e + n))
         e += n
     return out
+
+
+UNIT = 256   # peer-memory path: work unit of 256 rows (a CTA-pair GEMM row tile pair)
+
+
+def holder_masks(n_experts: int, world: int, placement: str, replicas=None) -> List[int]:
+    """Bitmask of the ranks holding each expert's weights (bit r = rank r).
+
+    "static": the contiguous ownership ranges; "replicated": the same plus
+    ``replicas[r]`` (expert ids rank r also holds); "balanced"/"local": all.
+    """
+    if placement in ("balanced", "local"):
+        return [(1 << world) - 1] * n_experts
+    masks = [0] * n_experts
+    for r, rng in enumerate(static_owner_ranges(n_experts, world)):
+        for e in rng:
+            masks[e] |= 1 << r
+    if placement == "replicated":
+        for r, extra in enumerate(replicas or []):
+            for e in extra:
+                masks[int(e)] |= 1 << r
+    elif placement != "static":
+        raise ValueError(f"unknown placement {placement!r}")
+    return masks
+
+
+def held_experts(masks: Sequence[int], rank: int) -> List[int]:
+    """Experts whose weights rank ``rank`` holds, ascending (its weight stack order)."""
+    return [e for e, m in enumerate(masks) if (m >> rank) & 1]
+
+
+def _waterfill_alloc(U: np.ndarray, masks: Sequence[int], world: int) -> np.ndarray:
+    """alloc[e, r]: units of expert e computed by rank r under holder masks
+    (the device plan's rule, ep_p2p.cu ep_plan_kernel): single-holder experts
+    whole, then the replicated ones, largest first (ties: lower index), each
+    water-filled over its holders from the lowest load (ties: lower rank)."""
+    E = len(masks)
+    alloc = np.zeros((E, world), dtype=np.int64)
+    load = np.zeros(world, dtype=np.int64)
+    rep = []
+    for e in range(E):
+        h = [r for r in range(world) if (masks[e] >> r) & 1]
+        if len(h) == 1:
+            alloc[e, h[0]] = U[e]
+            load[h[0]] += U[e]
+        else:
+            rep.append(e)
+    rep.sort(key=lambda e: (-int(U[e]), e))
+    for e in rep:
+        hs = sorted((r for r in range(world) if (masks[e] >> r) & 1), key=lambda r: (int(load[r]), r))
+        remaining, cnt, level = int(U[e]), 1, int(load[hs[0]])
+        while cnt < len(hs) and remaining >= (int(load[hs[cnt]]) - level) * cnt:
+            remaining -= (int(load[hs[cnt]]) - level) * cnt
+            level = int(load[hs[cnt]])
+            cnt += 1
+        q, rem = divmod(remaining, cnt)
+        for t in range(cnt):
+            target = level + q + (1 if t < rem else 0)
+            alloc[e, hs[t]] = target - load[hs[t]]
+            load[hs[t]] = target
+    return alloc
+
+
+def plan_cuts(counts_all: np.ndarray, placement: str, masks: Optional[Sequence[int]] = None,
+              unit: int = UNIT) -> np.ndarray:
+    """Host mirror of the peer-memory device plan (ep_p2p.cu ep_plan_kernel).
+
+    Returns cut [P, E, P, 2]: source i's rows of expert e in its x_perm units
+    [lo, hi) (units of ``unit`` rows, counted from the start of its x_perm,
+    every (source, expert) segment padded to whole units) computed by rank r.
+    """
+    counts_all = np.asarray(counts_all, dtype=np.int64)
+    P, E = counts_all.shape
+    units = (counts_all + unit - 1) // unit
+    T = units.sum(axis=1)
+    U = units.sum(axis=0)
+    total = int(T.sum())
+    xoff = np.zeros((P, E), dtype=np.int64)
+    xoff[:, 1:] = np.cumsum(units, axis=1)[:, :-1]
+    gofs = np.zeros((P, E), dtype=np.int64)
+    gofs[1:, :] = np.cumsum(units, axis=0)[:-1, :]
+    cut = np.zeros((P, E, P, 2), dtype=np.int64)
+    if placement == "local":
+        pieces = np.zeros((P, P, 2), dtype=np.int64)
+        quota = np.array([total // P + (1 if r < total % P else 0) for r in range(P)], dtype=np.int64)
+        keep = np.minimum(T, quota)
+        deficit = quota - keep
+        for r in range(P):
+            pieces[r, r] = (0, keep[r])
+        r = 0
+        for i in range(P):
+            pos = int(keep[i])
+            while pos < T[i]:
+                while r < P and deficit[r] == 0:
+                    r += 1
+                n = int(min(T[i] - pos, deficit[r]))
+                pieces[i, r] = (pos, pos + n)
+                pos += n
+                deficit[r] -= n
+        for i in range(P):
+            for e in range(E):
+                for r in range(P):
+                    a = max(pieces[i, r, 0], xoff[i, e])
+                    b = min(pieces[i, r, 1], xoff[i, e] + units[i, e])
+                    cut[i, e, r] = (a, max(a, b))
+        return cut
+    chunk = np.zeros((E, P, 2), dtype=np.int64)
+    if placement == "balanced":
+        e_start = 0
+        for e in range(E):
+            for r in range(P):
+                lo, hi = (r * total) // P, ((r + 1) * total) // P
+                a, b = max(lo, e_start), min(hi, e_start + U[e])
+                chunk[e, r] = (a - e_start, b - e_start) if b > a else (0, 0)
+            e_start += U[e]
+    else:
+        if masks is None:
+            masks = holder_masks(E, P, placement)
+        alloc = _waterfill_alloc(U, masks, P)
+        for e in range(E):
+            c = 0
+            for r in range(P):
+                chunk[e, r] = (c, c + alloc[e, r])
+                c += alloc[e, r]
+    for i in range(P):
+        for e in range(E):
+            u, x0, g0 = units[i, e], xoff[i, e], gofs[i, e]
+            for r in range(P):
+                a = x0 + max(chunk[e, r, 0], g0) - g0
+                b = x0 + min(chunk[e, r, 1], g0 + u) - g0
+                cut[i, e, r] = (a, max(a, b))
+    return cut
+
+
+def rank_loads(counts_all: np.ndarray, placement: str, masks: Optional[Sequence[int]] = None,
+               unit: int = UNIT) -> np.ndarray:
+    """Units each rank computes under a placement (sum of its pieces)."""
+    cut = plan_cuts(counts_all, placement, masks, unit)
+    return (cut[..., 1] - cut[..., 0]).sum(axis=(0, 1))
+
+
+def choose_replicas(counts_all: np.ndarray, budget: int = 2, target: float = 1.02,
+                    unit: int = UNIT) -> List[List[int]]:
+    """Replicas of hot experts on top of the static ownership, at most
+    ``budget`` extra experts per rank, chosen from a profile of per-expert row
+    counts (e.g. the all-gathered counts of a calibration forward).
+
+    Greedy: while the busiest rank's planned load (:func:`rank_loads`, the
+    same water-filling the device runs) exceeds ``target`` x the mean, give
+    the expert it computes most of a replica on the least-loaded rank with
+    budget left that does not hold it yet; a move is kept only if it lowers
+    (the busiest load, the number of ranks at it), so ties among several
+    busiest ranks are worked off one by one. Returns ``replicas[r]`` = expert
+    ids rank r adds.
+    """
+    counts_all = np.asarray(counts_all, dtype=np.int64)
+    P, E = counts_all.shape
+    replicas: List[List[int]] = [[] for _ in range(P)]
+    if P == 1:
+        return replicas
+    while True:
+        masks = holder_masks(E, P, "replicated", replicas)
+        loads = rank_loads(counts_all, "holders", masks, unit)
+        mean = loads.sum() / P
+        if mean == 0 or loads.max() <= target * mean:
+            return replicas
+        cut = plan_cuts(counts_all, "holders", masks, unit)
+        per_e = (cut[..., 1] - cut[..., 0]).sum(axis=0)        # [E, P] units of e computed by r
+        busiest = int(np.argmax(loads))
+        improved = False
+        for e in sorted(range(E), key=lambda e: -int(per_e[e, busiest])):
+            if per_e[e, busiest] == 0:
+                break
+            cands = [r for r in range(P) if len(replicas[r]) < budget and not (masks[e] >> r) & 1]
+            for dest in sorted(cands, key=lambda r: (int(loads[r]), r)):
+                trial = [list(x) for x in replicas]
+                trial[dest].append(e)
+                tl = rank_loads(counts_all, "holders", holder_masks(E, P, "replicated", trial), unit)
+                if (tl.max(), int((tl == tl.max()).sum())) < (loads.max(), int((loads == loads.max()).sum())):
+                    replicas = trial
+                    improved = True
+                    break
+            if improved:
+                break
+        if not improved:
+            return replicas
 
 
 @dataclass
@@ -197,13 +388,15 @@ class ExpertParallelMoE:
         self.last_plan: Optional[DispatchPlan] = None
 
     @staticmethod
-    def shard_weights(w1, b1, w2, b2, rank: int, world: int, placement: str):
-        """The expert weights a rank keeps for a placement."""
+    def shard_weights(w1, b1, w2, b2, rank: int, world: int, placement: str, replicas=None):
+        """The expert weights a rank keeps for a placement (held experts in
+        ascending order; "replicated" adds ``replicas[rank]`` to the static
+        ownership)."""
         if placement in ("balanced", "local"):
             return w1, b1, w2, b2
-        r = static_owner_ranges(w1.shape[0], world)[rank]
-        return (w1[r.start:r.stop].contiguous(), b1[r.start:r.stop].contiguous(),
-                w2[r.start:r.stop].contiguous(), b2[r.start:r.stop].contiguous())
+        keep = held_experts(holder_masks(w1.shape[0], world, placement, replicas), rank)
+        idx = torch.tensor(keep, dtype=torch.long, device=w1.device)
+        return tuple(t.index_select(0, idx).contiguous() for t in (w1, b1, w2, b2))
 
     def forward(self, x: torch.Tensor, events: Optional[Sequence] = None) -> torch.Tensor:
         """``events``: optional 7 CUDA events recorded on the current stream at
@@ -251,13 +444,15 @@ class _CommSlot:
     """One communication buffer (mapped on every rank) plus its workspace and
     epoch sequence: the resources of one token chunk in flight."""
 
-    def __init__(self, lib, _lib, group, world, rank, n_experts, cap_rows, d, hidden, top_k, max_tokens, dtype,
-                 device):
+    def __init__(self, lib, _lib, group, world, rank, n_experts, cap_rows, home_rows, d, hidden, top_k, max_tokens,
+                 dtype, device):
         import ctypes
 
         self.lib, self._lib, self.group = lib, _lib, group
         code = _lib.dtype_code(dtype)
-        nbytes = int(lib.agm_ep_comm_bytes(n_experts, cap_rows, d, code))
+        nbytes = int(lib.agm_ep_comm_bytes(n_experts, cap_rows, home_rows, d, code))
+        if nbytes == 0:
+            raise ValueError("expert-parallel communication buffer: unsupported dtype or sizes")
         ptr = ctypes.c_void_p()
         _lib.check(lib.agm_ep_alloc(nbytes, ctypes.byref(ptr)), "agm_ep_alloc")
         self.own = ptr.value
@@ -276,6 +471,7 @@ class _CommSlot:
             self.opened.append(pp.value)
             ptrs.append(pp.value)
         self.peer_comm = (ctypes.c_uint64 * world)(*ptrs)
+        self.home = self.own + int(lib.agm_ep_home_offset(n_experts, cap_rows, d, code))
         self.ws = torch.empty(int(lib.agm_ep_workspace_bytes(max_tokens, d, n_experts, top_k, hidden, cap_rows,
                                                               code)), dtype=torch.uint8, device=device)
         self.epoch = 1
@@ -294,26 +490,34 @@ class _CommSlot:
 class P2PExpertParallelMoE:
     """Expert-parallel forward with the all-to-all fused into the kernels.
 
-    Every rank allocates a communication buffer (receive rows, result rows,
+    Every rank allocates a communication buffer (receive rows, home rows,
     signal flags, counts inbox) and maps every peer's buffer through CUDA IPC.
     ``forward`` runs with no host sync: the permute kernel writes each row
     straight into the receive buffer of the rank that computes it (NVLink
-    stores), flag barriers in peer memory order the phases, and the combine
-    kernel reads the expert outputs straight from the ranks that computed them
-    (NVLink loads). See the C ABI ``agm_ep_forward``.
+    stores), flag barriers in peer memory order the phases, the FC2 epilogue
+    writes every output row straight into the home buffer of the rank that
+    owns the token (NVLink stores, overlapped with the GEMM), and the combine
+    reads this rank's own home buffer. See the C ABI ``agm_ep_forward``.
+
+    ``weights``: (w_router [E, d], w1, b1, w2, b2) where the expert stacks
+    hold this rank's experts in ascending order (:meth:`ExpertParallelMoE.
+    shard_weights` with the same placement and ``replicas``). Placements:
+    "static" (contiguous ownership 7/7, 4/4/3/3, 2x6+1x2 for 14 experts),
+    "replicated" (static plus ``replicas[r]``, see :func:`choose_replicas`),
+    "balanced" and "local" (every rank holds every expert).
 
     ``chunks > 1`` splits this rank's tokens into chunks and overlaps them on
     two streams: chunk j's expert GEMMs (capped at ``num_SMs - reserve_sms``
     CTAs) run while chunk j+1 is dispatched and chunk j-1 combined on the
     caller's stream; two communication slots alternate between chunks.
-    Results are bit-identical for any chunking (tokens are independent).
-    All ranks must call ``forward`` the same number of times with the same
-    ``chunks`` (every call is a collective).
+    Results are bit-identical for any chunking and placement (tokens are
+    independent). All ranks must call ``forward`` the same number of times
+    with the same ``chunks`` (every call is a collective).
     """
 
     def __init__(self, weights: Sequence[torch.Tensor], top_k: int, n_experts: int, max_tokens: int, group=None,
                  placement: str = "balanced", cap_rows: Optional[int] = None, chunks: int = 1,
-                 reserve_sms: int = 20):
+                 reserve_sms: int = 20, replicas=None):
         from . import _lib, ops
 
         self._lib = _lib
@@ -325,12 +529,13 @@ class P2PExpertParallelMoE:
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.placement = placement
-        self.pl_code = {"static": 0, "balanced": 1, "local": 2}[placement]
-        if placement == "static":
-            r = static_owner_ranges(self.E, self.world)[self.rank]
-            self.first_local, self.n_local = r.start, len(r)
-        else:
-            self.first_local, self.n_local = 0, self.E
+        self.replicas = [list(map(int, r)) for r in (replicas or [[] for _ in range(self.world)])]
+        self.masks = holder_masks(self.E, self.world, placement, self.replicas)
+        self.pl_code = {"static": _lib.AGM_EP_HOLDERS, "replicated": _lib.AGM_EP_HOLDERS,
+                        "balanced": _lib.AGM_EP_BALANCED, "local": _lib.AGM_EP_LOCAL}[placement]
+        import ctypes
+        self.holders = (ctypes.c_uint32 * self.E)(*self.masks)
+        self.n_local = len(held_experts(self.masks, self.rank))
         if self.w1.shape[0] != self.n_local:
             raise ValueError(f"rank holds {self.w1.shape[0]} experts, placement {placement} needs {self.n_local}")
         self.device = self.w1.device
@@ -340,15 +545,17 @@ class P2PExpertParallelMoE:
         self.max_tokens = int(max_tokens)
         self.chunks = max(1, int(chunks))
         self.chunk_tokens = (self.max_tokens + self.chunks - 1) // self.chunks
-        rows = ops.max_rows(self.chunk_tokens, self.top_k, self.E)
+        rows = int(self.lib.agm_ep_max_rows(self.chunk_tokens, self.top_k, self.E))
+        self.home_rows = max(UNIT, rows)
         if cap_rows is None:
-            cap_rows = self.world * rows if placement == "static" else 2 * rows
-        self.cap_rows = (int(cap_rows) + TILE - 1) // TILE * TILE
+            cap_rows = self.world * self.home_rows if placement in ("static", "replicated") else 2 * self.home_rows
+        self.cap_rows = (int(cap_rows) + UNIT - 1) // UNIT * UNIT
         n_slots = 1 if self.chunks == 1 else 2
-        self.slots = [_CommSlot(self.lib, _lib, group, self.world, self.rank, self.E, self.cap_rows, self.d, self.H,
-                                self.top_k, self.chunk_tokens, self.dtype, self.device) for _ in range(n_slots)]
+        self.slots = [_CommSlot(self.lib, _lib, group, self.world, self.rank, self.E, self.cap_rows, self.home_rows,
+                                self.d, self.H, self.top_k, self.chunk_tokens, self.dtype, self.device)
+                      for _ in range(n_slots)]
         sms = torch.cuda.get_device_properties(self.device).multi_processor_count
-        self.gemm_ctas = 0 if self.chunks == 1 else max(1, sms - int(reserve_sms))
+        self.gemm_ctas = 0 if self.chunks == 1 else max(2, (sms - int(reserve_sms)) & ~1)
         self.compute_stream = torch.cuda.Stream(self.device) if self.chunks > 1 else None
         dist.barrier(group=group)
 
@@ -359,9 +566,9 @@ class P2PExpertParallelMoE:
         ev = self._event_array(events)
         rc = self.lib.agm_ep_dispatch(
             _lib.ptr(x), _lib.dtype_code(x.dtype), x.shape[0], self.d, self.E, self.top_k, self.H,
-            _lib.ptr(self.w_router), self.n_local, self.first_local, self.pl_code, self.world, self.rank,
-            ctypes.addressof(slot.peer_comm), self.cap_rows, slot.epoch, _lib.ptr(slot.ws), slot.ws.numel(), 0,
-            None if ev is None else ctypes.addressof(ev), _lib.stream_handle(x.device))
+            _lib.ptr(self.w_router), self.pl_code, ctypes.addressof(self.holders), self.world, self.rank,
+            ctypes.addressof(slot.peer_comm), self.cap_rows, self.home_rows, slot.epoch, _lib.ptr(slot.ws),
+            slot.ws.numel(), 0, None if ev is None else ctypes.addressof(ev), _lib.stream_handle(x.device))
         _lib.check(rc, "agm_ep_dispatch")
 
     def _expert(self, slot, n, events=None):
@@ -371,15 +578,15 @@ class P2PExpertParallelMoE:
         rc = self.lib.agm_ep_expert(
             _lib.dtype_code(self.dtype), n, self.d, self.E, self.top_k, self.H, _lib.ptr(self.w1),
             _lib.ptr(self.b1), _lib.ptr(self.w2), _lib.ptr(self.b2), self.n_local, self.world, self.rank,
-            ctypes.addressof(slot.peer_comm), self.cap_rows, slot.epoch, _lib.ptr(slot.ws), slot.ws.numel(),
-            self.gemm_ctas, None if ev is None else ctypes.addressof(ev),
+            ctypes.addressof(slot.peer_comm), self.cap_rows, self.home_rows, slot.epoch, _lib.ptr(slot.ws),
+            slot.ws.numel(), self.gemm_ctas, None if ev is None else ctypes.addressof(ev),
             torch.cuda.current_stream(self.device).cuda_stream)
         _lib.check(rc, "agm_ep_expert")
 
     def _combine(self, slot, n, out):
         _lib = self._lib
         rc = self.lib.agm_ep_combine(_lib.dtype_code(self.dtype), n, self.d, self.E, self.top_k, self.H,
-                                     self.cap_rows, _lib.ptr(out), _lib.ptr(slot.ws), slot.ws.numel(),
+                                     self.cap_rows, slot.home, _lib.ptr(out), _lib.ptr(slot.ws), slot.ws.numel(),
                                      torch.cuda.current_stream(self.device).cuda_stream)
         _lib.check(rc, "agm_ep_combine")
         slot.epoch += 3

@@ -9,9 +9,11 @@ weights N(0, 0.02^2), x ~ N(0, 1), seed 1. Inputs (x: 189 MB, expert
 weights: 229 MB) are larger than the 126 MB L2, so no flush is needed between
 steps.
 
-With N > 1 (one process per GPU under torchrun) every rank runs the same
-workload on its own tokens (weak scaling, replicas); tokens/s is the sum over
-ranks and the time is the max over ranks.
+With N > 1 (one process per GPU under torchrun) every rank holds the same
+B x L workload of its own tokens (weak scaling) and the block runs expert
+parallel: the static expert ownership plus at most 2 hot-expert replicas per
+rank, rows moved over NVLink peer memory inside the kernels; tokens/s is the
+sum over ranks and the time is the max over ranks.
 
 The JSON line carries the whole-job tokens/s (device-timed, inputs resident
 in HBM), the end-to-end tokens/s through the public module API with host
@@ -56,10 +58,9 @@ TILE_ROWS = 128
 # per-expert bias log(p_e) * ZIPF_SCALE with p Zipf(1.2) over a seeded
 # permutation of the experts (seed 3), which gives a ~5:1 max/mean expert load.
 EP_SEED, ZIPF_S, ZIPF_SCALE = 3, 1.2, 0.63
-EP_CHUNKS = 4          # token chunks overlapped on two streams in the peer-memory forward
 EP_STAGES = ["route", "counts_plan", "dispatch_a2a", "expert_ffn", "return_a2a", "combine"]
-P2P_STAGES = ["route", "counts_exchange_plan", "dispatch_to_peers", "barrier", "fc1", "fc2", "barrier2",
-              "combine_from_peers"]
+P2P_STAGES = ["route", "counts_exchange_plan", "dispatch_to_peers", "barrier", "fc1", "fc2_to_owners", "barrier2",
+              "combine"]
 
 
 def load_peaks():
@@ -831,107 +832,152 @@ def run_codec(args, dev, stream, cpu_leg):
     return out
 
 
+def _ep_variant(args, world, rank, dev, stream, x, weights, ref, counts_all, kind, placement, replicas=None,
+                chunks=1):
+    """Time one expert-parallel variant on this rank's tokens x; the max over
+    ranks of the device time of exactly args.steps forwards."""
+    import torch.distributed as dist
+
+    from agillm41_b200 import ep
+
+    w1, b1, w2, b2, wr = weights
+    N = x.shape[0]
+    mine = ep.ExpertParallelMoE.shard_weights(w1, b1, w2, b2, rank, world, placement, replicas=replicas)
+    if kind == "p2p":
+        moe = ep.P2PExpertParallelMoE((wr,) + tuple(mine), TOP_K, EXPERTS, max_tokens=N, placement=placement,
+                                      chunks=chunks, replicas=replicas)
+    else:
+        moe = ep.ExpertParallelMoE((wr,) + tuple(mine), TOP_K, EXPERTS, placement=placement)
+    for _ in range(args.warmup):
+        out = moe.forward(x)
+    torch.cuda.synchronize()
+    same = bool(torch.equal(out, ref))
+    names = P2P_STAGES if kind == "p2p" else EP_STAGES
+    evs = None if chunks > 1 else [[torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
+                                   for _ in range(args.steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(dev) as clk:
+        barrier(world)
+        clk.mark_start()
+        start.record(stream)
+        for i in range(args.steps):
+            moe.forward(x)
+        stop.record(stream)
+        torch.cuda.synchronize()
+        clk.mark_stop()
+        barrier(world)
+        # per-phase pass (events between the phases; not the headline number)
+        if evs is not None:
+            for i in range(args.steps):
+                moe.forward(x, events=evs[i])
+            torch.cuda.synchronize()
+    ms = max_over_ranks(start.elapsed_time(stop), world)
+    st = None
+    if evs is not None:
+        st = {s_: 0.0 for s_ in names}
+        for e in evs:
+            for j, s_ in enumerate(names):
+                st[s_] += e[j].elapsed_time(e[j + 1])
+        st = {s_: round(max_over_ranks(v / args.steps, world), 4) for s_, v in st.items()}
+    if kind == "p2p":
+        same = same and moe.device_error() == 0
+        moe.close()
+    if kind == "p2p":
+        masks = ep.holder_masks(EXPERTS, world, placement, replicas)
+        units = ep.rank_loads(counts_all, placement, masks)
+        works = [int(2 * u) for u in units]                     # 128-row tiles (units of 256 rows)
+    else:
+        works = [ep.plan_dispatch(counts_all, r, placement).recv_tile_expert.size for r in range(world)]
+    ok = torch.tensor([1.0 if same else 0.0], device=dev)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    mean = sum(works) / world
+    res = dict(value=N * world * args.steps / (ms / 1000.0), ms_per_step=ms / args.steps, stages_ms=st,
+               tiles_per_rank=works, max_over_mean_tiles=round(max(works) / mean, 3) if mean else None,
+               placement_bound_efficiency=round(mean / max(works), 3) if max(works) else None,
+               bit_identical_to_single_gpu=bool(ok.item() > 0), clocks=clk.summary())
+    if replicas is not None:
+        res["replicas"] = replicas
+    return res
+
+
+def _gathered_counts(x, weights, world):
+    import torch.distributed as dist
+
+    from agillm41_b200 import ops
+
+    w1, b1, w2, b2, wr = weights
+    counts = ops.moe_forward(x, wr, w1, b1, w2, b2, TOP_K, want=("counts",))[1]["counts"].to(torch.int32)
+    counts_all = torch.empty(world * EXPERTS, dtype=torch.int32, device=x.device)
+    dist.all_gather_into_tensor(counts_all, counts.contiguous())
+    return counts_all.cpu().numpy().reshape(world, EXPERTS)
+
+
+EP_DECLARED = "replicated"     # the placement of the N > 1 headline
+EP_BUDGET = 2                  # replicas per rank on top of the static ownership
+
+
 def run_ep(args, world, rank, local):
     """Expert-parallel forward over `world` GPUs (one process each).
 
-    Skewed workload: every rank holds B x L tokens of its own (input seed
-    3 + 1000*rank); all ranks share the weights (seed 3) whose router carries
-    the Zipf logit bias. Rows move inside the permute/combine kernels over
-    NVLink peer memory ("p2p"). Headline: the fastest bit-exact p2p variant;
-    reported per variant: "local" (all experts on every rank, each rank keeps
-    its own tiles up to an equal share, only the excess moves), "balanced"
-    (global tile sequence cut evenly: hot experts' tiles spread over all
-    ranks, most rows cross NVLink), "static" (ownership 7/7, 4/4/3/3,
-    2x6+1x2), "balanced_overlap" (4 token chunks overlapped on two streams),
-    and the NCCL all-to-all variants.
+    Headline (``value``): the same per-rank workload as the one-GPU line (B x
+    L = 73,728 tokens of this rank, weights seed 1, input seed 1 + 1000 x
+    rank), so value(N) / (N x value(1)) compares like with like, on ONE
+    declared placement: "replicated" = the static ownership the configuration
+    names (14 experts over 2/4/8 ranks: 7/7, 4/4/3/3, 2x6+1x2) plus replicas
+    of the experts that make a rank busiest, at most 2 extra experts per rank,
+    chosen at set-up from the all-gathered counts of one calibration forward
+    (ep.choose_replicas); each forward splits a replicated expert's rows among
+    its holders on the device. Rows move inside the permute kernel and the
+    FC2 epilogue over NVLink peer memory.
+    Extra keys: ``placements`` (the same workload under static, balanced and
+    local placements) and ``skewed`` (the expert-parallel configuration's
+    Zipf(1.2)-skewed routing, weights seed 3, input seed 3 + 1000 x rank:
+    replicated, static, local and the NCCL all-to-all static path), each with
+    per-phase times, tiles per rank and the placement-implied efficiency bound.
     """
-    import torch.distributed as dist
-
-    import agillm41_b200
     from agillm41_b200 import ep, ops, synthetic
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     N = args.tokens
-    bias = synthetic.zipf_logit_bias(EXPERTS, EP_SEED, s=ZIPF_S, scale=ZIPF_SCALE)
-    sd = synthetic.make_state(D, HIDDEN, EXPERTS, EP_SEED, dtype=torch.bfloat16, device=dev,
-                              router_logit_bias=bias)
-    x = synthetic.make_input(N, D, EP_SEED + 1000 * rank, dtype=torch.bfloat16, device=dev, pin_feature0=True)
-    w1 = torch.stack([sd[f"experts.{e}.0.weight"] for e in range(EXPERTS)]).contiguous()
-    b1 = torch.stack([sd[f"experts.{e}.0.bias"] for e in range(EXPERTS)]).contiguous()
-    w2 = torch.stack([sd[f"experts.{e}.2.weight"] for e in range(EXPERTS)]).contiguous()
-    b2 = torch.stack([sd[f"experts.{e}.2.bias"] for e in range(EXPERTS)]).contiguous()
-    wr = sd["router.weight"].contiguous()
     stream = torch.cuda.current_stream(dev)
-    ref = ops.moe_forward(x, wr, w1, b1, w2, b2, TOP_K)    # single-GPU forward of this rank's tokens
-
-    results = {}
-    # Tiles each rank computes (from the same global plan every variant uses).
-    counts = torch.bincount(ops.moe_forward(x, wr, w1, b1, w2, b2, TOP_K, want=("idx",))[1]["idx"].flatten().long(),
-                            minlength=EXPERTS).to(torch.int32)
-    counts_all = torch.empty(world * EXPERTS, dtype=torch.int32, device=dev)
-    dist.all_gather_into_tensor(counts_all, counts)
-    counts_all = counts_all.cpu().numpy().reshape(world, EXPERTS)
-    for variant in ("p2p_local", "p2p_balanced", "p2p_static", "p2p_balanced_overlap", "nccl_balanced",
-                    "nccl_static"):
-        kind, placement = variant.split("_")[:2]
-        overlap = variant.endswith("_overlap")
-        mine = ep.ExpertParallelMoE.shard_weights(w1, b1, w2, b2, rank, world, placement)
-        if kind == "p2p":
-            moe = ep.P2PExpertParallelMoE((wr,) + tuple(mine), TOP_K, EXPERTS, max_tokens=N, placement=placement,
-                                          chunks=EP_CHUNKS if overlap else 1)
-            fwd = moe.forward
-        else:
-            moe = ep.ExpertParallelMoE((wr,) + tuple(mine), TOP_K, EXPERTS, placement=placement)
-            fwd = moe.forward
-        for _ in range(args.warmup):
-            out = fwd(x)
-        torch.cuda.synchronize()
-        same = bool(torch.equal(out, ref))
-        n_ev = 7 if kind == "nccl" else 9
-        names = EP_STAGES if kind == "nccl" else P2P_STAGES
-        evs = None if overlap else [[torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
-                                    for _ in range(args.steps)]
-        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        barrier(world)
-        torch.cuda.synchronize()
-        with ClockSampler(dev) as clk:
-            start.record(stream)
-            for i in range(args.steps):
-                if evs is None:
-                    fwd(x)
-                else:
-                    moe.forward(x, events=evs[i])
-            stop.record(stream)
-            torch.cuda.synchronize()
-        barrier(world)
-        ms = max_over_ranks(start.elapsed_time(stop), world)
-        st = None
-        if evs is not None:
-            st = {s_: 0.0 for s_ in names}
-            for e in evs:
-                for j, s_ in enumerate(names):
-                    st[s_] += e[j].elapsed_time(e[j + 1])
-            st = {s_: round(max_over_ranks(v / args.steps, world), 4) for s_, v in st.items()}
-        if kind == "p2p":
-            err = moe.device_error()
-            same = same and err == 0
-            moe.close()
-        if placement == "local":
-            pieces = ep.plan_pieces(counts_all, "local")
-            works = [int((pieces[:, r, 1] - pieces[:, r, 0]).sum()) for r in range(world)]
-        else:
-            works = [ep.plan_dispatch(counts_all, r, placement).recv_tile_expert.size for r in range(world)]
-        ok = torch.tensor([1.0 if same else 0.0], device=dev)
-        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
-        results[variant] = dict(value=N * world * args.steps / (ms / 1000.0), ms_per_step=ms / args.steps,
-                                stages_ms=st, tiles_per_rank=works,
-                                max_over_mean_tiles=round(max(works) / (sum(works) / world), 3),
-                                bit_identical_to_single_gpu=bool(ok.item() > 0), clocks=clk.summary())
+    sd = synthetic.make_state(D, HIDDEN, EXPERTS, SEED, dtype=torch.bfloat16, device=dev)
+    x = synthetic.make_input(N, D, SEED + rank * 1000, dtype=torch.bfloat16, device=dev)
+    weights = pack_weights(sd)
+    w1, b1, w2, b2, wr = weights
+    ref = ops.moe_forward(x, wr, w1, b1, w2, b2, TOP_K)          # single-GPU forward of this rank's tokens
+    counts_all = _gathered_counts(x, weights, world)
+    replicas = ep.choose_replicas(counts_all, budget=EP_BUDGET)
+    head = _ep_variant(args, world, rank, dev, stream, x, weights, ref, counts_all, "p2p", EP_DECLARED, replicas)
+    others = {}
+    if not args.skip_ep_variants:
+        for placement in ("static", "balanced", "local"):
+            others[f"p2p_{placement}"] = _ep_variant(args, world, rank, dev, stream, x, weights, ref, counts_all,
+                                                     "p2p", placement)
+    skewed = {}
+    if not args.skip_skewed:
+        xs, wsk = skewed_workload(dev, rank, N)
+        ref_s = ops.moe_forward(xs, wsk[4], *wsk[:4], TOP_K)
+        counts_s = _gathered_counts(xs, wsk, world)
+        reps_s = ep.choose_replicas(counts_s, budget=EP_BUDGET)
+        skewed["p2p_replicated"] = _ep_variant(args, world, rank, dev, stream, xs, wsk, ref_s, counts_s, "p2p",
+                                               "replicated", reps_s)
+        if not args.skip_ep_variants:
+            for kind, placement in (("p2p", "static"), ("p2p", "local"), ("nccl", "static")):
+                skewed[f"{kind}_{placement}"] = _ep_variant(args, world, rank, dev, stream, xs, wsk, ref_s,
+                                                            counts_s, kind, placement)
+        c = counts_s.sum(axis=0).astype(float)
+        skewed["expert_load_max_over_mean"] = round(float(c.max() / c.mean()), 3)
+        skewed["workload"] = (f"expert-parallel MoE block forward, {N} tokens/rank d{D} E{EXPERTS} H{HIDDEN} "
+                              f"top{TOP_K} bf16, Zipf({ZIPF_S}) logit bias x{ZIPF_SCALE} (seed {EP_SEED})")
+        del xs, wsk, ref_s
 
     # End to end through the public API with host buffers (copy in, forward, copy out).
-    moe = ep.P2PExpertParallelMoE((wr, w1, b1, w2, b2), TOP_K, EXPERTS, max_tokens=N, placement="balanced",
-                                  chunks=EP_CHUNKS)
+    mine = ep.ExpertParallelMoE.shard_weights(w1, b1, w2, b2, rank, world, EP_DECLARED, replicas=replicas)
+    moe = ep.P2PExpertParallelMoE((wr,) + tuple(mine), TOP_K, EXPERTS, max_tokens=N, placement=EP_DECLARED,
+                                  replicas=replicas)
     x_host = x.cpu().pin_memory()
     y_host = torch.empty_like(x_host).pin_memory()
     x_dev = torch.empty_like(x)
@@ -954,15 +1000,12 @@ def run_ep(args, world, rank, local):
     torch.cuda.synchronize()
     barrier(world)
     e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    e2e_same = bool(torch.equal(y_host.to(dev), ref))
     moe.close()
     if rank != 0:
         return
     peaks = load_peaks()
-    ok_p2p = [k_ for k_ in ("p2p_local", "p2p_balanced_overlap", "p2p_balanced")
-              if results[k_]["bit_identical_to_single_gpu"]]
-    head_name = max(ok_p2p or ["p2p_balanced"], key=lambda k_: results[k_]["value"])
-    head = results[head_name]
-    stages = results["p2p_balanced"]["stages_ms"]
+    stages = head["stages_ms"]
     ffn_ms = stages["fc1"] + stages["fc2"]
     # Grouped GEMM roofline: FLOPs of the busiest rank's FC1+FC2 launches / their event-timed duration.
     flop = 2 * 2 * TILE_ROWS * max(head["tiles_per_rank"]) * D * HIDDEN
@@ -971,22 +1014,26 @@ def run_ep(args, world, rank, local):
         "metric": METRIC, "value": head["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded N(0,1) input, N(0,0.02^2) random-init expert weights, Zipf(1.2) router bias)",
-        "config": {"workload": f"expert-parallel MoE block forward, {N} tokens/rank d{D} E{EXPERTS} H{HIDDEN} "
-                               f"top{TOP_K} bf16, Zipf(1.2) logit bias x{ZIPF_SCALE} (seed {EP_SEED})",
+        "data": "synthetic (seeded N(0,1) input, N(0,0.02^2) random-init expert weights)",
+        "config": {"workload": f"MoE block forward B{BATCH} L{SEQ} d{D} E{EXPERTS} H{HIDDEN} top{TOP_K} bf16 "
+                               f"seed{SEED} per rank (the one-GPU workload on every rank)",
                    "global_batch": BATCH * world, "seq_len": SEQ, "tokens_per_gpu": N,
-                   "parallelism": f"expert parallel x{world}: rows moved by the permute/combine kernels over "
-                                  f"NVLink peer memory, balanced placement ({head_name})",
+                   "parallelism": f"expert parallel x{world}, placement '{EP_DECLARED}': static ownership "
+                                  f"{[len(r) for r in ep.static_owner_ranges(EXPERTS, world)]} + at most "
+                                  f"{EP_BUDGET} hot-expert replicas per rank {replicas}; rows moved by the permute "
+                                  f"kernel and the FC2 epilogue over NVLink peer memory",
                    "l2": "inputs larger than L2; no flush"},
         "e2e": {"value": N * world * args.steps / (e2e_ms / 1000.0), "unit": UNIT,
                 "h2d_bytes_per_step": x_host.numel() * 2, "d2h_bytes_per_step": y_host.numel() * 2,
-                "api": "P2PExpertParallelMoE.forward with host copies"},
-        "gpu_launches": KERNELS_PER_STEP * args.steps,
-        "roofline": {"kernel": "grouped_gemm_tc_kernel (FC1+FC2, busiest rank)", "bound": "tensor",
-                     "achieved": round(achieved, 1), "peak": peaks["tf_sus"], "unit": "TFLOP/s",
-                     "frac": round(achieved / peaks["tf_sus"], 3),
-                     "peak_source": f"{peaks['src']} bf16 sustained", "traffic": None},
-        "placements": results,
+                "api": "P2PExpertParallelMoE.forward with host copies", "output_matches": e2e_same},
+        "gpu_launches": 10 * args.steps,   # router, plan, counts exchange, EP plan, permute, barrier, FC1, FC2, barrier, combine
+        "roofline": {"kernel": "grouped_gemm_pair_kernel (FC1+FC2, busiest rank)", "bound": "tensor",
+                     "achieved": round(achieved, 1), "peak": peaks["tf"], "unit": "TFLOP/s",
+                     "frac": round(achieved / peaks["tf"], 3),
+                     "peak_source": f"{peaks['src']} bf16 burst", "traffic": None},
+        "placement": head,
+        "placements": others,
+        "skewed": skewed,
         "cpu_baseline": None,
         "clocks": head["clocks"],
     }
@@ -1235,7 +1282,9 @@ def main():
     ap.add_argument("--skip-codec", action="store_true", help="skip the tensor-codec decode leg")
     ap.add_argument("--skip-aux", action="store_true", help="skip the auxiliary router-loss leg")
     ap.add_argument("--skip-parity", action="store_true", help="skip the routing/output parity check")
-    ap.add_argument("--skip-skewed", action="store_true", help="skip the skewed-routing single-GPU leg")
+    ap.add_argument("--skip-skewed", action="store_true", help="skip the skewed-routing legs")
+    ap.add_argument("--skip-ep-variants", action="store_true",
+                    help="N > 1: time only the declared expert-parallel placement")
     ap.add_argument("--skip-reference-gpu", action="store_true",
                     help="--impl reference: skip the reference's op sequence timed on the GPU")
     args = ap.parse_args()

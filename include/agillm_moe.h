@@ -232,16 +232,32 @@ AGM_API int agm_moe_forward_host(const void* x_host, int dtype, int64_t n_tokens
 
 /* ---- Expert parallelism across the GPUs of one node (NVLink peer memory) ----
  * The reference runs MoEFFN.forward (agillm41.py:4389-4431) on one device; the
- * entry points below spread its expert FFN work over P ranks (one process per
- * GPU) and move rows inside the kernels instead of through a collective.
- * Each rank allocates one communication buffer (agm_ep_alloc, IPC-shareable),
- * shares its handle (agm_ep_ipc_handle) with the other ranks, which map it
- * (agm_ep_ipc_open); every rank then calls agm_ep_forward with the same
- * sequence of epochs (1, 4, 7, ...: each call uses epoch, epoch+1, epoch+2). */
+ * entry points below spread its expert FFN work (the loop over experts,
+ * agillm41.py:4421-4428) over P ranks (one process per GPU) and move rows
+ * inside the kernels instead of through a collective. Each rank allocates one
+ * communication buffer (agm_ep_alloc, IPC-shareable), shares its handle
+ * (agm_ep_ipc_handle) with the other ranks, which map it (agm_ep_ipc_open);
+ * every rank then calls agm_ep_forward with the same sequence of epochs
+ * (1, 4, 7, ...: each call uses epoch, epoch+1, epoch+2). 16-bit dtypes
+ * (AGM_BF16, AGM_F16) only: the expert GEMMs run on CTA pairs, and every
+ * (rank, expert) segment is padded to AGM_PAIR_ROWS rows.                   */
 
+/* Placements (where each expert's weights live and who computes its rows). */
+#define AGM_EP_HOLDERS 0   /* expert e on the ranks of bitmask holders[e]: the static
+                              contiguous ownership, optionally plus replicas of hot experts */
+#define AGM_EP_BALANCED 1  /* every rank holds every expert; equal shares of the global work */
+#define AGM_EP_LOCAL 2     /* every rank holds every expert; each keeps its own rows up to
+                              an equal share, only the excess moves */
+
+/* Rows of one rank's permuted buffer for n_tokens (segments padded to 256). */
+AGM_API int64_t agm_ep_max_rows(int64_t n_tokens, int top_k, int n_experts);
 /* Bytes of one rank's communication buffer: signals, counts inbox, receive
- * rows and result rows for up to cap_rows rows of d features. */
-AGM_API size_t agm_ep_comm_bytes(int n_experts, int64_t cap_rows, int d, int dtype);
+ * rows (cap_rows: rows this rank may compute) and home rows (home_rows =
+ * agm_ep_max_rows of the most tokens a rank routes per call: the FFN outputs
+ * of its own rows, written by the computing ranks). Both multiples of 256. */
+AGM_API size_t agm_ep_comm_bytes(int n_experts, int64_t cap_rows, int64_t home_rows, int d, int dtype);
+/* Byte offset of the home rows in a communication buffer (for agm_ep_combine). */
+AGM_API int64_t agm_ep_home_offset(int n_experts, int64_t cap_rows, int d, int dtype);
 /* cudaMalloc a communication buffer (signals and inbox zeroed). */
 AGM_API int agm_ep_alloc(size_t bytes, void** ptr);
 AGM_API int agm_ep_free(void* ptr);
@@ -254,19 +270,20 @@ AGM_API int agm_ep_ipc_close(void* peer_ptr);
 AGM_API size_t agm_ep_workspace_bytes(int64_t n_tokens, int d, int n_experts, int top_k, int hidden, int64_t cap_rows,
                                       int dtype);
 /* Expert-parallel MoEFFN.forward of this rank's tokens x [n, d] -> out [n, d].
- * w_router [E, d] (all experts); w1/b1/w2/b2 hold n_local_experts experts
- * starting at first_local_expert. placement 0 = static contiguous ownership
- * (first E mod P ranks own one more expert), 1 = balanced (every rank holds
- * all experts; the global tile sequence is split evenly, hot experts span
- * ranks), 2 = local (every rank holds all experts and computes its own tiles
- * up to an equal share of the total; only the excess moves to ranks below
- * their share). peer_comm: HOST array of `world` device addresses of every rank's
+ * w_router [E, d] (all experts). expert_holders: HOST array of E bitmasks,
+ * bit r set when rank r holds expert e (every rank passes the same array);
+ * w1/b1/w2/b2 hold this rank's experts in ascending expert order. placement
+ * AGM_EP_HOLDERS: an expert with one holder is computed there; an expert with
+ * several is split among them each call, largest first, by water-filling the
+ * holders' loads. AGM_EP_BALANCED / AGM_EP_LOCAL need every bit set.
+ * peer_comm: HOST array of `world` device addresses of every rank's
  * communication buffer as mapped here (own buffer at [rank]). The counts
  * exchange and three barriers are flag writes in peer memory, bounded waits
  * (a time-out sets the device error word, the first int of the workspace).
  * stage_events (nullable): AGM_EP_STAGE_EVENTS cudaEvent_t handles recorded
  * before the router and after: local plan, counts exchange + global plan,
- * dispatch (permute into peers), barrier, FC1, FC2, barrier, combine.
+ * dispatch (permute into peers), barrier, FC1, FC2 (which writes every output
+ * row into its owner's home buffer), barrier, combine.
  * No host synchronisation; outputs are bit-identical to agm_moe_forward on
  * the same tokens.                                                           */
 #define AGM_EP_STAGE_EVENTS 9
@@ -279,25 +296,30 @@ AGM_API size_t agm_ep_workspace_bytes(int64_t n_tokens, int d, int n_experts, in
  * combine) with the caller ordering them across streams (events).
  * agm_ep_dispatch: router, local plan, counts exchange, device plan, rows into
  *   the computing ranks' receive buffers, barrier (stage_events: 5 events).
- * agm_ep_expert: FC1/FC2 on the received tiles, barrier; gemm_ctas > 0 caps
- *   the GEMM's persistent CTAs (stage_events: 3 events).
- * agm_ep_combine: gate-weighted combine from the computing ranks' results.   */
+ * agm_ep_expert: FC1/FC2 on the received tiles (n_local_experts weights),
+ *   results into the owners' home buffers, barrier; gemm_ctas > 0 caps the
+ *   GEMM's persistent CTAs (stage_events: 3 events).
+ * agm_ep_combine: gate-weighted combine from `home` (this rank's buffer +
+ *   agm_ep_home_offset).                                                      */
 AGM_API int agm_ep_dispatch(const void* x, int dtype, int64_t n_tokens, int d, int n_experts, int top_k, int hidden,
-                            const void* w_router, int n_local_experts, int first_local_expert, int placement,
-                            int world, int rank, const uint64_t* peer_comm, int64_t cap_rows, uint64_t epoch,
+                            const void* w_router, int placement, const uint32_t* expert_holders, int world, int rank,
+                            const uint64_t* peer_comm, int64_t cap_rows, int64_t home_rows, uint64_t epoch,
                             void* workspace, size_t workspace_bytes, int flags, void* const* stage_events,
                             void* stream);
 AGM_API int agm_ep_expert(int dtype, int64_t n_tokens, int d, int n_experts, int top_k, int hidden, const void* w1,
                           const void* b1, const void* w2, const void* b2, int n_local_experts, int world, int rank,
-                          const uint64_t* peer_comm, int64_t cap_rows, uint64_t epoch, void* workspace,
-                          size_t workspace_bytes, int gemm_ctas, void* const* stage_events, void* stream);
+                          const uint64_t* peer_comm, int64_t cap_rows, int64_t home_rows, uint64_t epoch,
+                          void* workspace, size_t workspace_bytes, int gemm_ctas, void* const* stage_events,
+                          void* stream);
 AGM_API int agm_ep_combine(int dtype, int64_t n_tokens, int d, int n_experts, int top_k, int hidden,
-                           int64_t cap_rows, void* out, void* workspace, size_t workspace_bytes, void* stream);
+                           int64_t cap_rows, const void* home, void* out, void* workspace, size_t workspace_bytes,
+                           void* stream);
 AGM_API int agm_ep_forward(const void* x, int dtype, int64_t n_tokens, int d, int n_experts, int top_k, int hidden,
                            const void* w_router, const void* w1, const void* b1, const void* w2, const void* b2,
-                           int n_local_experts, int first_local_expert, int placement, int world, int rank,
-                           const uint64_t* peer_comm, int64_t cap_rows, uint64_t epoch, void* out, void* workspace,
-                           size_t workspace_bytes, int flags, void* const* stage_events, void* stream);
+                           int placement, const uint32_t* expert_holders, int world, int rank,
+                           const uint64_t* peer_comm, int64_t cap_rows, int64_t home_rows, uint64_t epoch, void* out,
+                           void* workspace, size_t workspace_bytes, int flags, void* const* stage_events,
+                           void* stream);
 
 /* ---- Training: forward that keeps its intermediates, and the backward ----
  * Together these replace PyTorch autograd through MoEFFN.forward

@@ -115,3 +115,99 @@ def test_local_plan_pieces():
         assert moved <= np.maximum(tiles - share, 0).sum()
         same = ep.plan_pieces(np.tile(counts[1], (P, 1)), "local")
         assert all(same[i, r, 1] == same[i, r, 0] for i in range(P) for r in range(P) if r != i)
+
+
+def _check_cuts(counts, cut, unit=ep.UNIT):
+    """Pieces of every source tile its expert segments exactly, in order."""
+    P, E = counts.shape
+    units = (counts + unit - 1) // unit
+    for i in range(P):
+        start = 0
+        for e in range(E):
+            spans = sorted((int(lo), int(hi)) for lo, hi in cut[i, e] if hi > lo)
+            if units[i, e] == 0:
+                assert not spans
+                continue
+            assert spans[0][0] == start and spans[-1][1] == start + units[i, e]
+            assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+            start += units[i, e]
+
+
+@pytest.mark.parametrize("P", [1, 2, 4, 8])
+def test_peer_plan_cuts_cover_every_unit(P):
+    """The host mirror of the device plan (ep_plan_kernel): for every
+    placement the pieces partition each (source, expert) segment, experts go
+    only to ranks that hold them, and balanced/local loads are even."""
+    rng = np.random.default_rng(10 + P)
+    E = 14
+    counts = rng.integers(0, 20000, size=(P, E))
+    counts[:, 5] *= 5
+    counts[0, 2] = 0
+    for placement in ("static", "balanced", "local"):
+        masks = ep.holder_masks(E, P, placement)
+        cut = ep.plan_cuts(counts, placement, masks)
+        _check_cuts(counts, cut)
+        per_e = (cut[..., 1] - cut[..., 0]).sum(axis=0)          # [E, P]
+        for e in range(E):
+            for r in range(P):
+                if per_e[e, r]:
+                    assert (masks[e] >> r) & 1
+        load = per_e.sum(axis=0)
+        if placement != "static":
+            assert load.max() - load.min() <= 1
+    # replicated: random replica sets within a budget of 2
+    reps = [sorted(rng.choice(E, size=min(2, E), replace=False).tolist()) for _ in range(P)]
+    masks = ep.holder_masks(E, P, "replicated", reps)
+    cut = ep.plan_cuts(counts, "replicated", masks)
+    _check_cuts(counts, cut)
+    per_e = (cut[..., 1] - cut[..., 0]).sum(axis=0)
+    assert all((masks[e] >> r) & 1 for e in range(E) for r in range(P) if per_e[e, r])
+    # water-filling never loads a rank more than static ownership does
+    assert per_e.sum(axis=0).max() <= ep.rank_loads(counts, "static").max()
+
+
+def _zipf_profile(P, n_tok=73728, seed=3):
+    """Per-rank expert counts of the skewed expert-parallel workload's
+    routing: the Zipf(1.2) logit bias on top of N(0, 1) x against the seeded
+    router (computed in fp32 on a token sample, scaled to n_tok)."""
+    E, d = 14, 1280
+    bias = reference_moe.zipf_logit_bias(E, seed, s=1.2, scale=0.63)
+    sd = reference_moe.make_state(d, 64, E, seed, router_logit_bias=bias)
+    counts = np.zeros((P, E), dtype=np.int64)
+    for r in range(P):
+        x = reference_moe.make_input(2048, d, seed + 1000 * r, pin_feature0=True)
+        idx = torch.topk(x @ sd["router.weight"].t(), 2, dim=-1).indices
+        counts[r] = np.bincount(idx.flatten().numpy(), minlength=E) * (n_tok // 2048)
+    return counts
+
+
+@pytest.mark.parametrize("P", [2, 4, 8])
+def test_choose_replicas_balances_skew(P):
+    """Hot-expert replication on top of static ownership (at most 2 extra
+    experts per rank) brings the skewed workload's busiest rank to within 15%
+    of the mean, where static ownership alone is far above it."""
+    counts = _zipf_profile(P)
+    static = ep.rank_loads(counts, "static")
+    reps = ep.choose_replicas(counts, budget=2)
+    assert all(len(r) <= 2 for r in reps)
+    masks = ep.holder_masks(14, P, "replicated", reps)
+    for r in range(P):
+        assert not set(reps[r]) & set(ep.static_owner_ranges(14, P)[r])
+    load = ep.rank_loads(counts, "replicated", masks)
+    mean = load.sum() / P
+    assert load.sum() == static.sum()
+    assert load.max() <= 1.15 * mean, (load.max() / mean, static.max() / mean, reps)
+    if P == 8:
+        assert static.max() / mean > 2.0
+
+
+def test_choose_replicas_uniform_profile():
+    """Uniform routing: 14 experts over 8 ranks (2x6 + 1x2) leaves the
+    two-expert ranks 14% above the mean; replicas level it."""
+    P, E = 8, 14
+    counts = np.full((P, E), 73728 * 2 // E, dtype=np.int64)
+    static = ep.rank_loads(counts, "static")
+    reps = ep.choose_replicas(counts, budget=2)
+    load = ep.rank_loads(counts, "replicated", ep.holder_masks(E, P, "replicated", reps))
+    assert static.max() / (static.sum() / P) > 1.1
+    assert load.max() / (load.sum() / P) <= 1.03

@@ -1,6 +1,8 @@
-"""Expert-parallel forward on 2 GPUs (NCCL): every rank's output equals the
-single-GPU forward of its own tokens, bit for bit, for both placements and
-skewed routing. Skipped on a host with fewer than two GPUs."""
+"""Expert-parallel forward on 2 GPUs: every rank's output equals the
+single-GPU forward of its own tokens, bit for bit, for every placement
+(static, replicated hot experts, balanced, local; NCCL all-to-all and
+peer-memory paths) under skewed routing. Skipped on a host with fewer than
+two GPUs."""
 import os
 import socket
 
@@ -50,11 +52,17 @@ def _worker(rank, world, port, q):
             out2 = moe.forward(x)
             torch.cuda.synchronize()
             res[placement] = (bool(torch.equal(out, ref)), bool(torch.equal(out, out2)))
-        for placement, chunks in (("static", 1), ("balanced", 1), ("local", 1), ("balanced", 2), ("static", 3),
-                                  ("local", 2)):
-            mine = ep.ExpertParallelMoE.shard_weights(*w, rank, world, placement)
+        # replicas of the hot experts from the all-gathered counts of this batch
+        counts = ops.moe_forward(x, wr, *w, k, want=("counts",))[1]["counts"].to(torch.int32)
+        counts_all = torch.empty(world * E, dtype=torch.int32, device=dev)
+        dist.all_gather_into_tensor(counts_all, counts)
+        replicas = ep.choose_replicas(counts_all.cpu().numpy().reshape(world, E), budget=2)
+        for placement, chunks in (("static", 1), ("balanced", 1), ("local", 1), ("replicated", 1), ("balanced", 2),
+                                  ("static", 3), ("local", 2), ("replicated", 2)):
+            reps = replicas if placement == "replicated" else None
+            mine = ep.ExpertParallelMoE.shard_weights(*w, rank, world, placement, replicas=reps)
             moe = ep.P2PExpertParallelMoE((wr,) + tuple(mine), k, E, max_tokens=4000, placement=placement,
-                                          chunks=chunks)
+                                          chunks=chunks, replicas=reps)
             outs = [moe.forward(x).clone() for _ in range(3)]
             torch.cuda.synchronize()
             err = moe.device_error()
@@ -104,9 +112,9 @@ def test_p2p_path_single_rank():
         w = [torch.stack([sd[f"experts.{e}.{i}.{p}"] for e in range(E)]).contiguous()
              for i, p in ((0, "weight"), (0, "bias"), (2, "weight"), (2, "bias"))]
         wr = sd["router.weight"].contiguous()
-        for placement, chunks in (("static", 1), ("balanced", 1), ("local", 1), ("balanced", 3)):
+        for placement, chunks in (("static", 1), ("balanced", 1), ("local", 1), ("replicated", 1), ("balanced", 3)):
             moe = ep.P2PExpertParallelMoE((wr,) + tuple(w), k, E, max_tokens=5000, placement=placement,
-                                          chunks=chunks)
+                                          chunks=chunks, replicas=[[]] if placement == "replicated" else None)
             for n in (4096, 1, 777, 5000):
                 x = synthetic.make_input(n, d, n, dtype=torch.bfloat16, device=dev)
                 out = moe.forward(x)
