@@ -124,7 +124,7 @@ FwdLayout carve(void* ws, int64_t n, int d, int E, int k, int H, int S, int Hs, 
   L.token_of = c.take<int32_t>(sizeof(int32_t) * rows);
   L.x_perm = c.take<void>(static_cast<size_t>(eb) * rows * d);
   L.h = c.take<void>(static_cast<size_t>(eb) * rows * H);
-  L.h_sh = S > 0 ? c.take<void>(static_cast<size_t>(eb) * npad * Hs) : nullptr;
+  L.h_sh = S > 0 ? c.take<void>(static_cast<size_t>(eb) * S * npad * Hs) : nullptr;  // [S, npad, Hs]
   L.y_sh = S > 0 ? c.take<void>(static_cast<size_t>(eb) * S * npad * d) : nullptr;
   L.bytes = (c.off + 255) & ~size_t(255);
   return L;
@@ -387,6 +387,30 @@ int moe_forward_impl(const void* x, int dtype, int64_t n_tokens, int d, int n_ex
   // and the weights from before this forward: the GEMMs stream their first
   // weight tiles while the kernel before them finishes.
   g1.early_weights = true;
+  const int64_t npad = round_up(n_tokens, AGM_TILE_M);
+  // Shared experts: one dense group over all tokens, so any two row tiles
+  // share their weights and the CTA-pair GEMM applies without padding.
+  const int shared_mode = (dtype != AGM_F32 && !(flags & AGM_FLAG_NO_PAIR) && n_tokens >= AGM_PAIR_MIN_ROWS)
+                              ? AGM_GEMM_PAIR : 0;
+  // Both on CTA pairs: the shared experts ride in the routed launches as a
+  // second, dense problem (one FC1 and one FC2 launch for the whole block;
+  // every tile computed exactly as by its own launch).
+  const bool fold = n_shared > 0 && pair && shared_mode == AGM_GEMM_PAIR && !(flags & AGM_FLAG_NO_FOLD);
+  if (fold) {
+    g1.groups2 = n_shared;
+    g1.a2 = x;
+    g1.a2_rows = n_tokens;
+    g1.w2 = ws1;
+    g1.bias2 = sb1;
+    g1.c2 = L.h_sh;
+    g1.c2_rows = n_shared * npad;
+    g1.ldc2 = shared_hidden;
+    g1.n2 = shared_hidden;
+    g1.k2 = d;
+    g1.tiles2 = static_cast<int>(npad / AGM_TILE_M);
+    g1.a2_group_rows = 0;
+    g1.c2_group_rows = npad;
+  }
   e = agm::grouped_gemm(dtype, L.x_perm, rows, w1, g1, true, sms, stream, gemm_mode);
   if (e != cudaSuccess) return cuda_fail(e, "grouped_gemm fc1");
   if ((e = mark(4)) != cudaSuccess) return cuda_fail(e, "event record");
@@ -396,16 +420,24 @@ int moe_forward_impl(const void* x, int dtype, int64_t n_tokens, int d, int n_ex
   g2.bias = b2;
   g2.n = d;
   g2.k = hidden;
+  if (fold) {
+    g2.a2 = L.h_sh;
+    g2.a2_rows = n_shared * npad;
+    g2.w2 = ws2;
+    g2.bias2 = sb2;
+    g2.c2 = L.y_sh;
+    g2.c2_rows = n_shared * npad;
+    g2.ldc2 = d;
+    g2.n2 = d;
+    g2.k2 = shared_hidden;
+    g2.a2_group_rows = npad;
+    g2.c2_group_rows = npad;
+  }
   e = agm::grouped_gemm(dtype, L.h, rows, w2, g2, false, sms, stream, gemm_mode);
   if (e != cudaSuccess) return cuda_fail(e, "grouped_gemm fc2");
   if ((e = mark(5)) != cudaSuccess) return cuda_fail(e, "event record");
 
-  const int64_t npad = round_up(n_tokens, AGM_TILE_M);
-  // Shared experts: one dense group over all tokens, so any two row tiles
-  // share their weights and the CTA-pair GEMM applies without padding.
-  const int shared_mode = (dtype != AGM_F32 && !(flags & AGM_FLAG_NO_PAIR) && n_tokens >= AGM_PAIR_MIN_ROWS)
-                              ? AGM_GEMM_PAIR : 0;
-  for (int s = 0; s < n_shared; ++s) {
+  for (int s = 0; s < (fold ? 0 : n_shared); ++s) {
     agm::GemmArgs s1;
     s1.c = L.h_sh;
     s1.ldc = shared_hidden;

@@ -20,6 +20,12 @@
 // no second tile: the peer CTA then repeats the first tile's rows and stores
 // nothing.
 //
+// A second, dense problem may share the launch (GemmArgs::groups2 > 0: the
+// shared experts of a MoE block, every token through each of them): its
+// units follow the first problem's, with their own tensor maps, N, K, bias
+// and per-group row offsets, so the block's routed and shared projections
+// take one launch each and the shared units fill the routed tail.
+//
 // Roles (320 threads per CTA, both CTAs):
 //   warp 0   TMA producer: waits for a free stage (its own `empty` barrier,
 //            released by the pair MMA's commit), loads its A rows and B half
@@ -73,10 +79,63 @@ __device__ __forceinline__ void pair_coords(int t, int num_p, int num_n, int& p,
   n_blk = r / gp;
 }
 
+// One work unit: a pair of row tiles x one 256-column tile, of the first
+// (grouped, tile-table) problem or of the optional second (dense) problem.
+struct PairUnit {
+  int prob;     // 0 or 1
+  int m0;       // first row tile of the pair (problem 0: tile-table index; problem 1: tile within its group)
+  int n_blk;    // column tile
+  int g;        // weight group
+  int row0;     // A / C row of tile m0 (problem 1: includes the group's offsets via a_off / c_off)
+  int a_off;    // problem 1: the group's A row offset
+  int c_off;    // problem 1: the group's C row offset
+  bool has2;    // tile m0 + 1 exists
+  int n;        // columns of the problem
+  int k;        // inner dimension of the problem
+};
+
+__device__ __forceinline__ PairUnit pair_unit(int t, int total0, int num_p, int num_m, int num_n, int num_p2,
+                                              int num_n2, const GemmArgs& args) {
+  PairUnit u;
+  if (t < total0) {
+    int p, n_blk;
+    pair_coords(t, num_p, num_n, p, n_blk);
+    u.prob = 0;
+    u.m0 = 2 * p;
+    u.n_blk = n_blk;
+    int g = args.tile_group ? args.tile_group[u.m0] : 0;
+    u.g = (g < 0 || g >= args.groups) ? 0 : g;
+    u.row0 = u.m0 * kBM;
+    u.a_off = u.c_off = 0;
+    u.has2 = u.m0 + 1 < num_m;
+    u.n = args.n;
+    u.k = args.k;
+  } else {
+    const int t2 = t - total0;
+    const int per_group = num_p2 * num_n2;
+    const int g = t2 / per_group;
+    int p, n_blk;
+    pair_coords(t2 - g * per_group, num_p2, num_n2, p, n_blk);
+    u.prob = 1;
+    u.m0 = 2 * p;
+    u.n_blk = n_blk;
+    u.g = g;
+    u.row0 = u.m0 * kBM;
+    u.a_off = static_cast<int>(g * args.a2_group_rows);
+    u.c_off = static_cast<int>(g * args.c2_group_rows);
+    u.has2 = u.m0 + 1 < args.tiles2;
+    u.n = args.n2;
+    u.k = args.k2;
+  }
+  return u;
+}
+
 template <typename T, bool RELU>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                             const __grid_constant__ CUtensorMap tmC, GemmArgs args) {
+                             const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmA2,
+                             const __grid_constant__ CUtensorMap tmB2, const __grid_constant__ CUtensorMap tmC2,
+                             GemmArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -112,8 +171,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   }
   const int num_p = (num_m + 1) / 2;
   const int num_n = (args.n + kPairN - 1) / kPairN;
-  const int total = num_p * num_n;
-  const int num_kb = (args.k + kBK - 1) / kBK;
+  const int total0 = num_p * num_n;
+  const int num_p2 = args.groups2 > 0 ? (args.tiles2 + 1) / 2 : 0;
+  const int num_n2 = args.groups2 > 0 ? (args.n2 + kPairN - 1) / kPairN : 0;
+  const int total = total0 + args.groups2 * num_p2 * num_n2;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -130,6 +191,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     tma_prefetch_desc(&tmC);
+    if (args.groups2 > 0) {
+      tma_prefetch_desc(&tmA2);
+      tma_prefetch_desc(&tmB2);
+      tma_prefetch_desc(&tmC2);
+    }
   }
   __syncthreads();
   cluster_sync();  // both CTAs' barriers exist before any cross-CTA arrive or copy
@@ -148,23 +214,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     int stage = 0;
     uint32_t phase = 0, armed = 0, armed_parity = 0;
     bool ok = true;
-    // With early_weights, the first pair tile's first `ndef` stages get their
+    // With early_weights, the first unit's first `ndef` stages get their
     // weight half-tile before the wait for the previous kernel and their A
     // rows after it.
     bool waited = !args.early_weights;
-    const int ndef = min(kStages, num_kb);
-    int deferred = 0, first_m = 0;
+    int deferred = 0, ndef = 0, first_row = 0;
+    const CUtensorMap* first_a = &tmA;
     for (int t = cluster; t < total && ok; t += nclusters) {
-      int p, n_blk;
-      pair_coords(t, num_p, num_n, p, n_blk);
-      const int m0 = 2 * p;
-      const int my_m = (!leader && m0 + 1 < num_m) ? m0 + 1 : m0;
-      if (t == cluster) first_m = my_m;
-      int g = args.tile_group ? args.tile_group[m0] : 0;
-      if (g < 0 || g >= args.groups) g = 0;
+      const PairUnit u = pair_unit(t, total0, num_p, num_m, num_n, num_p2, num_n2, args);
+      const CUtensorMap* mA = u.prob ? &tmA2 : &tmA;
+      const CUtensorMap* mB = u.prob ? &tmB2 : &tmB;
+      // Rank 1 loads the pair's second row tile (or repeats the first when there is none).
+      const int a_row = u.a_off + (u.m0 + ((!leader && u.has2) ? 1 : 0)) * kBM;
+      const int num_kb = (u.k + kBK - 1) / kBK;
+      if (t == cluster) {
+        first_row = a_row;
+        first_a = mA;
+        ndef = min(kStages, num_kb);
+      }
       // Rank r holds weight rows [n0 + r * n_mma / 2, +n_mma / 2) of the tile
       // (its 128-row box may run past them; the MMA reads only n_mma / 2).
-      const int b_row = n_blk * kPairN + static_cast<int>(rank) * (pair_n_mma(args.n - n_blk * kPairN) / 2);
+      const int b_row = u.n_blk * kPairN + static_cast<int>(rank) * (pair_n_mma(u.n - u.n_blk * kPairN) / 2);
       for (int kb = 0; kb < num_kb; ++kb) {
         if (!mbar_wait(&empty[stage], phase ^ 1, args.err, kErrTimeoutEmpty) || *abort_s) {
           *abort_s = 1;
@@ -174,8 +244,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (lane == 0) {
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * (kABytes + kBBytes));
           const uint32_t fb = full0 + stage * 8;
-          tma_load_3d_pair(sB + stage * kBBytes, &tmB, kb * kBK, b_row, g, fb);
-          if (waited) tma_load_2d_pair(sA + stage * kABytes, &tmA, kb * kBK, my_m * kBM, fb);
+          tma_load_3d_pair(sB + stage * kBBytes, mB, kb * kBK, b_row, u.g, fb);
+          if (waited) tma_load_2d_pair(sA + stage * kABytes, mA, kb * kBK, a_row, fb);
         }
         if (!waited && ++deferred == ndef) {
           pdl_wait();
@@ -183,7 +253,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           waited = true;
           if (lane == 0)
             for (int j = 0; j < deferred; ++j)
-              tma_load_2d_pair(sA + j * kABytes, &tmA, j * kBK, first_m * kBM, full0 + j * 8);
+              tma_load_2d_pair(sA + j * kABytes, first_a, j * kBK, first_row, full0 + j * 8);
         }
         armed |= 1u << stage;
         armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
@@ -194,12 +264,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
       }
     }
-    if (!waited) {  // no tile, or stopped early: still order after the previous kernel
+    if (!waited) {  // no unit, or stopped early: still order after the previous kernel
       pdl_wait();
       pdl_trigger();
       if (lane == 0)
         for (int j = 0; j < deferred; ++j)
-          tma_load_2d_pair(sA + j * kABytes, &tmA, j * kBK, first_m * kBM, full0 + j * 8);
+          tma_load_2d_pair(sA + j * kABytes, first_a, j * kBK, first_row, full0 + j * 8);
     }
     __syncwarp();
     // Drain: the pair MMAs that read this CTA's stages have completed (their
@@ -216,10 +286,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int t = cluster; t < total && ok; t += nclusters, ++it) {
-        int p, n_blk;
-        pair_coords(t, num_p, num_n, p, n_blk);
-        const uint32_t idesc =
-            idesc_f16(Traits<T>::code == AGM_BF16, 2 * kBM, pair_n_mma(args.n - n_blk * kPairN));
+        const PairUnit u = pair_unit(t, total0, num_p, num_m, num_n, num_p2, num_n2, args);
+        const int num_kb = (u.k + kBK - 1) / kBK;
+        const uint32_t idesc = idesc_f16(Traits<T>::code == AGM_BF16, 2 * kBM, pair_n_mma(u.n - u.n_blk * kPairN));
         const int acc = it & 1;
         if (!mbar_wait(&acc_empty[acc], ((it >> 1) & 1) ^ 1, args.err, kErrTimeoutAcc) || *abort_s) {
           *abort_s = 1;
@@ -262,19 +331,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     uint8_t* stg = sStg + ew * kStgBytes;
     const uint32_t stg_row = lane * 128;
     const uint32_t acc_empty0 = cluster_map(smem_u32(acc_empty), 0);
-    const T* bias = static_cast<const T*>(args.bias);
-    const bool want_bits = RELU && args.relu_bits != nullptr;  // training: keep the ReLU mask
     int it = 0;
     for (int t = cluster; t < total; t += nclusters, ++it) {
-      int p, n_blk;
-      pair_coords(t, num_p, num_n, p, n_blk);
-      const int m0 = 2 * p;
-      const bool has2 = m0 + 1 < num_m;
-      const int my_m = leader ? m0 : m0 + 1;
-      const bool store = leader || has2;
-      int g = args.tile_group ? args.tile_group[m0] : 0;
-      if (g < 0 || g >= args.groups) g = 0;
-      if (leader && ew == 0 && lane == 0 && has2 && args.tile_group && args.tile_group[m0 + 1] != args.tile_group[m0])
+      const PairUnit u = pair_unit(t, total0, num_p, num_m, num_n, num_p2, num_n2, args);
+      const int my_m = leader ? u.m0 : u.m0 + 1;
+      const bool store = leader || u.has2;
+      const T* bias = static_cast<const T*>(u.prob ? args.bias2 : args.bias);
+      const CUtensorMap* mC = u.prob ? &tmC2 : &tmC;
+      // training (first problem only): keep the ReLU mask
+      const bool want_bits = RELU && u.prob == 0 && args.relu_bits != nullptr;
+      const bool to_tiles = u.prob == 0 && args.tile_dst != nullptr;
+      if (u.prob == 0 && leader && ew == 0 && lane == 0 && u.has2 && args.tile_group &&
+          args.tile_group[u.m0 + 1] != args.tile_group[u.m0])
         raise_error(args.err, kErrPairGroup);
       const int acc = it & 1;
       if (!mbar_wait(&acc_full[acc], (it >> 1) & 1, args.err, kErrTimeoutAcc) || *abort_s) {
@@ -282,9 +350,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      const int n0 = n_blk * kPairN;
-      const int n_valid = min(kPairN, args.n - n0);
-      const T* brow = bias ? bias + static_cast<int64_t>(g) * args.n + n0 : nullptr;
+      const int n0 = u.n_blk * kPairN;
+      const int n_valid = min(kPairN, u.n - n0);
+      const T* brow = bias ? bias + static_cast<int64_t>(u.g) * u.n + n0 : nullptr;
+      const int c_row = u.c_off + my_m * kBM + quarter * 32;
       for (int c64 = half; store && c64 * 64 < n_valid; c64 += 2) {
         const int col = c64 * 64;
         uint32_t r[64];
@@ -324,7 +393,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if (col + 32 < n_valid)
             args.relu_bits[static_cast<int64_t>(w0 + 1) * args.ld_bits + row] = static_cast<uint32_t>(bits >> 32);
         }
-        if (args.tile_dst) {
+        if (to_tiles) {
           // This tile's rows go to their own buffer (expert parallelism: the
           // token owner's home rows, possibly in a peer GPU's memory): read
           // the staged chunk back unswizzled, 4 rows of 128 B per store.
@@ -334,17 +403,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const int sub = lane >> 3, q = lane & 7;
           const bool col_ok = col + q * 8 < n_valid;
 #pragma unroll
-          for (int it = 0; it < 8; ++it) {
-            const int r = it * 4 + sub;
-            const uint4 v = *reinterpret_cast<const uint4*>(stg + r * 128 + ((q ^ (r & 7)) << 4));
-            if (col_ok) *reinterpret_cast<uint4*>(dst + (static_cast<int64_t>(r) * args.ldc + q * 8) * sizeof(T)) = v;
+          for (int itr = 0; itr < 8; ++itr) {
+            const int rr = itr * 4 + sub;
+            const uint4 v = *reinterpret_cast<const uint4*>(stg + rr * 128 + ((q ^ (rr & 7)) << 4));
+            if (col_ok) *reinterpret_cast<uint4*>(dst + (static_cast<int64_t>(rr) * args.ldc + q * 8) * sizeof(T)) = v;
           }
           __syncwarp();
         } else {
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&tmC, stg, n0 + col, my_m * kBM + quarter * 32);
+            tma_store_2d(mC, stg, n0 + col, c_row);
             bulk_commit_group();
           }
         }
@@ -376,40 +445,61 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   }
 }
 
+template <typename T>
+bool encode_pair_maps(const void* a, int64_t a_rows, const void* w, void* c, int64_t c_rows, int64_t ldc, int n,
+                      int k, int groups, CUtensorMap* tmA, CUtensorMap* tmB, CUtensorMap* tmC) {
+  const CUtensorMapDataType dt = (Traits<T>::code == AGM_BF16) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                                : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(a_rows)};
+    const uint64_t str[1] = {static_cast<uint64_t>(k) * 2};
+    const uint32_t box[2] = {kBK, kBM};
+    if (!encode_tmap(tmA, a, 2, dims, str, box, dt)) return false;
+  }
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(k), static_cast<uint64_t>(n), static_cast<uint64_t>(groups)};
+    const uint64_t str[2] = {static_cast<uint64_t>(k) * 2, static_cast<uint64_t>(k) * n * 2};
+    const uint32_t box[3] = {kBK, kHalfN, 1};
+    if (!encode_tmap(tmB, w, 3, dims, str, box, dt)) return false;
+  }
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(n), static_cast<uint64_t>(c_rows)};
+    const uint64_t str[1] = {static_cast<uint64_t>(ldc) * 2};
+    const uint32_t box[2] = {64, 32};
+    if (!encode_tmap(tmC, c, 2, dims, str, box, dt)) return false;
+  }
+  return true;
+}
+
 template <typename T, bool RELU>
 cudaError_t launch_pair(const void* a, int64_t a_rows, const void* w, const GemmArgs& args, int num_sms,
                         cudaStream_t stream) {
-  const CUtensorMapDataType dt = (Traits<T>::code == AGM_BF16) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                                                : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  CUtensorMap tmA, tmB, tmC;
-  {
-    const uint64_t dims[2] = {static_cast<uint64_t>(args.k), static_cast<uint64_t>(a_rows)};
-    const uint64_t str[1] = {static_cast<uint64_t>(args.k) * 2};
-    const uint32_t box[2] = {kBK, kBM};
-    if (!encode_tmap(&tmA, a, 2, dims, str, box, dt)) return cudaErrorInvalidValue;
-  }
-  {
-    const uint64_t dims[3] = {static_cast<uint64_t>(args.k), static_cast<uint64_t>(args.n),
-                              static_cast<uint64_t>(args.groups)};
-    const uint64_t str[2] = {static_cast<uint64_t>(args.k) * 2, static_cast<uint64_t>(args.k) * args.n * 2};
-    const uint32_t box[3] = {kBK, kHalfN, 1};
-    if (!encode_tmap(&tmB, w, 3, dims, str, box, dt)) return cudaErrorInvalidValue;
-  }
-  {
-    const uint64_t dims[2] = {static_cast<uint64_t>(args.n), static_cast<uint64_t>(args.c_rows)};
-    const uint64_t str[1] = {static_cast<uint64_t>(args.ldc) * 2};
-    const uint32_t box[2] = {64, 32};
-    if (!encode_tmap(&tmC, args.c, 2, dims, str, box, dt)) return cudaErrorInvalidValue;
+  CUtensorMap tmA, tmB, tmC, tmA2, tmB2, tmC2;
+  if (!encode_pair_maps<T>(a, a_rows, w, args.c, args.c_rows, args.ldc, args.n, args.k, args.groups, &tmA, &tmB,
+                           &tmC))
+    return cudaErrorInvalidValue;
+  if (args.groups2 > 0) {
+    if (args.tiles2 <= 0 || !args.a2 || !args.w2 || !args.c2 || args.n2 <= 0 || args.k2 <= 0)
+      return cudaErrorInvalidValue;
+    if (!encode_pair_maps<T>(args.a2, args.a2_rows, args.w2, args.c2, args.c2_rows, args.ldc2, args.n2, args.k2,
+                             args.groups2, &tmA2, &tmB2, &tmC2))
+      return cudaErrorInvalidValue;
+  } else {
+    tmA2 = tmA;
+    tmB2 = tmB;
+    tmC2 = tmC;
   }
   cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(grouped_gemm_pair_kernel<T, RELU>), kSmemBytes);
   if (e != cudaSuccess) return e;
   const int num_n = (args.n + kPairN - 1) / kPairN;
-  const int64_t max_units = static_cast<int64_t>((args.max_tiles + 1) / 2) * num_n;
+  int64_t max_units = static_cast<int64_t>((args.max_tiles + 1) / 2) * num_n;
+  if (args.groups2 > 0)
+    max_units += static_cast<int64_t>(args.groups2) * ((args.tiles2 + 1) / 2) * ((args.n2 + kPairN - 1) / kPairN);
   int ctas = args.max_ctas > 0 ? std::min(args.max_ctas, num_sms) : num_sms;
   ctas = static_cast<int>(std::min<int64_t>(ctas, 2 * std::max<int64_t>(1, max_units)));
   ctas = std::max(2, ctas & ~1);
   return launch_kernel(grouped_gemm_pair_kernel<T, RELU>, dim3(ctas), dim3(kThreads), kSmemBytes, stream, tmA, tmB,
-                       tmC, args);
+                       tmC, tmA2, tmB2, tmC2, args);
 }
 
 }  // namespace

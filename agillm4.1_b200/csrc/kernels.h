@@ -75,6 +75,25 @@ struct GemmArgs {
   // instead of c, e.g. the token owner's buffer on a peer GPU (expert
   // parallelism); stored with 16-byte vector stores.
   const uint64_t* tile_dst = nullptr;
+  // CTA-pair kernel only: a second, dense problem computed in the same launch
+  // after this one's tiles (the shared experts of a MoE block): groups2
+  // groups of tiles2 row tiles each; group g reads A rows from
+  // g * a2_group_rows (a2: a2_rows x k2), weight [g] of w2 ([groups2, n2, k2]),
+  // bias2 [groups2, n2], and writes C rows from g * c2_group_rows of c2
+  // (c2_rows x n2, row stride ldc2). groups2 = 0: no second problem.
+  int groups2 = 0;
+  const void* a2 = nullptr;
+  int64_t a2_rows = 0;
+  const void* w2 = nullptr;
+  const void* bias2 = nullptr;
+  void* c2 = nullptr;
+  int64_t c2_rows = 0;
+  int64_t ldc2 = 0;
+  int n2 = 0;
+  int k2 = 0;
+  int tiles2 = 0;
+  int64_t a2_group_rows = 0;
+  int64_t c2_group_rows = 0;
 };
 
 // Expert-parallel routing of one rank's permuted rows (see ep_p2p.cu): a list

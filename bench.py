@@ -583,7 +583,8 @@ def run_forward_production(args, dev, stream):
             "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peaks["tf_sus"], "unit": "TFLOP/s",
                          "frac": round(tf / peaks["tf_sus"], 3),
                          "note": "expert and shared GEMM FLOPs over the whole forward"},
-            "gpu_launches_per_step": 8}
+            "gpu_launches_per_step": 6,   # router, plan, permute, FC1 (+ shared FC1), FC2 (+ shared FC2), combine
+            "shared_folded": True}
 
 
 def run_train(args, dev, stream, *, experts=EXPERTS, hidden=HIDDEN, top_k=TOP_K, shared=0, shared_hidden=0,

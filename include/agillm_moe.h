@@ -80,6 +80,8 @@ enum {
                                       completes (default: programmatic dependent launch) */
 #define AGM_FLAG_BWD_PAIR 0x20     /* agm_moe_backward: CTA-pair GEMMs wherever they apply, also for
                                       problems too small to fill the GPU with pair tiles */
+#define AGM_FLAG_NO_FOLD 0x40     /* agm_moe_forward: shared experts in their own GEMM launches
+                                      (default: inside the routed FC1 / FC2 launches on CTA pairs) */
 
 AGM_API const char* agm_last_error(void);
 AGM_API int agm_abi_version(void);

@@ -309,6 +309,32 @@ def test_pair_gemm_shared_expert_matches_single_cta():
     assert torch.equal(out_r, out_p + res)
 
 
+@pytest.mark.parametrize("E,k,H,S,n", [(2, 1, 5120, 1, 33792), (2, 1, 5120, 1, 16500), (14, 2, 3200, 2, 16400),
+                                       (8, 3, 2048, 1, 20000)])
+def test_shared_experts_folded_into_routed_launches(E, k, H, S, n):
+    """Above the pair threshold the shared experts' dense GEMMs ride in the
+    routed FC1/FC2 launches as a second problem (agillm41.py:4381-4387,
+    4429-4430). The production shape (2 experts, top-1, H = 4d, one shared
+    expert of 2d, 22 x 1536 tokens, agillm41.py:8590-8594), an odd number of
+    shared row tiles (16,500 tokens: 129), two shared experts with top-2, and
+    top-3: bit-identical to the shared experts in their own launches and to
+    the one-CTA path; the fused residual add on top of the folded forward."""
+    d = 1280
+    sd = synthetic.make_state(d, H, E, 40 + S, dtype=torch.bfloat16, device=DEV, bias_std=0.02, shared=S,
+                              shared_hidden=2 * d)
+    w1, b1, w2, b2, sh = packed(sd, E, DEV)
+    wr = sd["router.weight"].contiguous()
+    x = synthetic.make_input(n, d, 41 + S, dtype=torch.bfloat16, device=DEV)
+    out_f = ops.moe_forward(x, wr, w1, b1, w2, b2, k, shared=sh, check_errors=True)
+    out_s = ops.moe_forward(x, wr, w1, b1, w2, b2, k, shared=sh, check_errors=True, fold=False)
+    assert torch.equal(out_f, out_s)
+    out_1 = ops.moe_forward(x, wr, w1, b1, w2, b2, k, shared=sh, check_errors=True, pair=False)
+    assert torch.equal(out_f, out_1)
+    res = torch.randn(n, d, generator=torch.Generator().manual_seed(43)).to(DEV, torch.bfloat16)
+    out_r = ops.moe_forward_residual(x, res, wr, w1, b1, w2, b2, k, shared=sh, check_errors=True)
+    assert torch.equal(out_r, out_f + res)
+
+
 @pytest.mark.parametrize("n,k,E", [(64, 2, 14), (200, 2, 14), (37, 1, 4), (96, 3, 16)])
 def test_swap_gemm_forward_matches_row_tiles(n, k, E):
     """Decode-sized batches run the expert GEMMs with swapped operands (weights
