@@ -1007,7 +1007,7 @@ def run_ep(args, world, rank, local):
         return
     peaks = load_peaks()
     stages = head["stages_ms"]
-    ffn_ms = stages["fc1"] + stages["fc2"]
+    ffn_ms = stages["fc1"] + stages["fc2_to_owners"]
     # Grouped GEMM roofline: FLOPs of the busiest rank's FC1+FC2 launches / their event-timed duration.
     flop = 2 * 2 * TILE_ROWS * max(head["tiles_per_rank"]) * D * HIDDEN
     achieved = flop / (ffn_ms / 1000.0) / 1e12
