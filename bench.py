@@ -392,8 +392,56 @@ def run_ours(args, world, rank, local):
             train["aux_loss"] = aux
     codec_leg = None if args.skip_codec else run_codec(args, dev, stream, world == 1 and not args.skip_cpu)
     skewed = None if args.skip_skewed else run_skewed_single(args, dev, stream)
+    block_ffn = None if args.skip_block else run_block_ffn(args, dev, stream, x, (w1, b1, w2, b2, wr))
     report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e_value, x, decode, train, codec_leg,
-           parity=parity, skewed=skewed)
+           parity=parity, skewed=skewed, block_ffn=block_ffn)
+
+
+def run_block_ffn(args, dev, stream, x, weights):
+    """The FFN half of the reference Block at this workload (agillm41.py:4547,
+    `x + self.ff(self.ln2(x))`): torch's LayerNorm (ln2, d = 1280, seeded
+    affine parameters) then agm_moe_forward_residual (the MoE block with the
+    residual add fused into its combine). Reports the LayerNorm's share of
+    that half, i.e. what a LayerNorm fused into the router and permute could
+    save at most (its read of x and write of the normalised rows)."""
+    import torch.nn.functional as F
+
+    from agillm41_b200 import ops
+
+    w1, b1, w2, b2, wr = weights
+    g = torch.Generator(device="cpu").manual_seed(SEED + 11)
+    ln_w = (1.0 + 0.1 * torch.randn(D, generator=g)).to(dev, torch.bfloat16)
+    ln_b = (0.1 * torch.randn(D, generator=g)).to(dev, torch.bfloat16)
+
+    def ln():
+        return F.layer_norm(x, (D,), ln_w, ln_b, 1e-5)
+
+    def block():
+        return ops.moe_forward_residual(ln(), x, wr, w1, b1, w2, b2, TOP_K)
+
+    def timed(fn, steps):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    steps = max(10, min(args.steps, 50))
+    ln_ms = timed(ln, steps)
+    block_ms = timed(block, steps)
+    peaks = load_peaks()
+    nbytes = 2 * x.numel() * 2
+    return {"workload": f"x + MoEFFN(LayerNorm(x)), B{BATCH} L{SEQ} d{D} bf16 (torch LayerNorm, fused residual)",
+            "ms_per_step": round(block_ms, 4), "layernorm_ms": round(ln_ms, 4),
+            "layernorm_share": round(ln_ms / block_ms, 4),
+            "layernorm_hbm_frac": round(nbytes / (ln_ms / 1000.0) / 1e9 / peaks["hbm"], 3),
+            "note": "the LayerNorm reads x and writes the normalised rows (2 x 189 MB); fused into the router "
+                    "and permute (which read x anyway) those bytes would not move"}
 
 
 def pack_weights(sd, experts=EXPERTS):
@@ -1207,7 +1255,7 @@ def gemm_kernel_name(n_tokens):
 
 
 def report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e, x, decode=None, train=None, codec=None,
-           parity=None, skewed=None):
+           parity=None, skewed=None, block_ffn=None):
     if rank != 0:
         return
     peaks = load_peaks()
@@ -1259,6 +1307,8 @@ def report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e, x, deco
         line["parity"] = parity
     if skewed is not None:
         line["skewed"] = skewed
+    if block_ffn is not None:
+        line["block_ffn"] = block_ffn
     if decode is not None:
         line["decode"] = decode
     if train is not None:
@@ -1284,6 +1334,7 @@ def main():
     ap.add_argument("--skip-aux", action="store_true", help="skip the auxiliary router-loss leg")
     ap.add_argument("--skip-parity", action="store_true", help="skip the routing/output parity check")
     ap.add_argument("--skip-skewed", action="store_true", help="skip the skewed-routing legs")
+    ap.add_argument("--skip-block", action="store_true", help="skip the Block FFN-half (LayerNorm share) leg")
     ap.add_argument("--skip-ep-variants", action="store_true",
                     help="N > 1: time only the declared expert-parallel placement")
     ap.add_argument("--skip-reference-gpu", action="store_true",
