@@ -1183,14 +1183,26 @@ def run_decode(args, dev, stream):
         ws[:4].zero_()                   # one clear of the error word per decode step
         xs[0].copy_(x0)
         for layer, (wr, w1, b1, w2, b2) in enumerate(layers):
-            # counts are written by the forward (no host read) so the active experts can be summed afterwards
+            # x_{l+1} = noise_l + MoE(x_l): the perturbation is added inside the combine kernel
+            # (agm_moe_forward_residual; the same bits as a separate add)
+            rc = lib.agm_moe_forward_residual(
+                ops.ptr(xs[layer]), ops.ptr(noise[layer]), ops.dtype_code(torch.bfloat16), B, D, E, k, HIDDEN,
+                ops.ptr(wr), ops.ptr(w1), ops.ptr(b1), ops.ptr(w2), ops.ptr(b2), 0, 1, None, None, None, None,
+                ops.ptr(xs[layer + 1]), ops.ptr(ws), ws.numel(), keep, torch.cuda.current_stream(dev).cuda_stream)
+            ops.check(rc, "agm_moe_forward_residual")
+
+    def counts_pass():
+        # one untimed pass that also writes the per-expert counts (the active experts per layer)
+        for layer, (wr, w1, b1, w2, b2) in enumerate(layers):
             rc = lib.agm_moe_forward(
                 ops.ptr(xs[layer]), ops.dtype_code(torch.bfloat16), B, D, E, k, HIDDEN, ops.ptr(wr), ops.ptr(w1),
                 ops.ptr(b1), ops.ptr(w2), ops.ptr(b2), 0, 1, None, None, None, None, ops.ptr(outs[layer]),
                 ops.ptr(ws), ws.numel(), keep, None, None, ops.ptr(counts[layer]), None, None, None,
                 torch.cuda.current_stream(dev).cuda_stream)
             ops.check(rc, "agm_moe_forward")
-            torch.add(outs[layer], noise[layer], out=xs[layer + 1])
+            torch.add(outs[layer], noise[layer], out=chk)
+            if not torch.equal(chk, xs[layer + 1]):
+                raise RuntimeError("fused residual add differs from the separate add in the decode chain")
 
     def timed(fn, steps):
         for _ in range(max(3, args.warmup)):
@@ -1210,6 +1222,9 @@ def run_decode(args, dev, stream):
     if err:
         raise RuntimeError(f"device error word 0x{err:x} in the decode leg")
     ref_out = xs[-1].clone()
+    chk = torch.empty(B, D, dtype=torch.bfloat16, device=dev)
+    counts_pass()
+    torch.cuda.synchronize()
     graph_ms = None
     try:
         side = torch.cuda.Stream(dev)
@@ -1242,7 +1257,8 @@ def run_decode(args, dev, stream):
             "steps": steps, "active_experts": active, "weight_bytes_per_step": wbytes,
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm"], "unit": "GB/s",
                          "frac": round(gbs / peaks["hbm"], 3), "peak_source": f"{peaks['src']} HBM copy"},
-            "gpu_launches_per_step": KERNELS_PER_STEP * DECODE_LAYERS}
+            "gpu_launches_per_step": KERNELS_PER_STEP * DECODE_LAYERS + 2,
+            "residual": "perturbation added inside each layer's combine kernel (agm_moe_forward_residual)"}
 
 
 PAIR_MIN_ROWS = 16384   # AGM_PAIR_MIN_ROWS: agm_moe_forward runs its expert GEMMs on CTA pairs from k*N rows up
