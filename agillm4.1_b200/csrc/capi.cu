@@ -352,7 +352,7 @@ int moe_forward_impl(const void* x, int dtype, int64_t n_tokens, int d, int n_ex
   const bool swap = dtype != AGM_F32 && !(flags & AGM_FLAG_NO_SWAP) &&
                     static_cast<int64_t>(top_k) * n_tokens <= static_cast<int64_t>(AGM_SWAP_ROWS_PER_EXPERT) * n_experts;
   const int seg_align = pair ? AGM_PAIR_ROWS : AGM_TILE_M;
-  int gemm_mode = pair ? AGM_GEMM_PAIR : (swap ? -2 : 0);
+  const int gemm_mode = pair ? AGM_GEMM_PAIR : (swap ? -2 : 0);
 
   if ((e = mark(0)) != cudaSuccess) return cuda_fail(e, "event record");
   e = agm::router_topk(dtype, x, w_router, n_tokens, d, n_experts, top_k, flags & AGM_FLAG_TIE_LOW_FIRST,
@@ -396,8 +396,6 @@ int moe_forward_impl(const void* x, int dtype, int64_t n_tokens, int d, int n_ex
   // second, dense problem (one FC1 and one FC2 launch for the whole block;
   // every tile computed exactly as by its own launch).
   const bool fold = n_shared > 0 && pair && shared_mode == AGM_GEMM_PAIR && !(flags & AGM_FLAG_NO_FOLD);
-  // 256 x 512 pair tiles for the routed GEMMs (not with the shared experts folded in).
-  if (pair && !fold && (flags & AGM_FLAG_WIDE) && hidden % 8 == 0 && d % 8 == 0) gemm_mode = -3;
   if (fold) {
     g1.groups2 = n_shared;
     g1.a2 = x;

@@ -488,7 +488,6 @@ cudaError_t grouped_gemm(int dtype, const void* a, int64_t a_rows, const void* w
                          int num_sms, cudaStream_t stream, int force_bn) {
   if (args.max_tiles <= 0 || args.n <= 0) return cudaSuccess;
   if (force_bn == -1 && dtype != AGM_F32) return grouped_gemm_pair(dtype, a, a_rows, w, args, relu, num_sms, stream);
-  if (force_bn == -3 && dtype != AGM_F32) return grouped_gemm_wide(dtype, a, a_rows, w, args, relu, num_sms, stream);
   if (force_bn == -2 && dtype != AGM_F32) return grouped_gemm_swap(dtype, a, a_rows, w, args, relu, num_sms, stream);
   if (force_bn < 0) force_bn = 0;
   if (dtype == AGM_F32) {

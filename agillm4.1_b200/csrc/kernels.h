@@ -177,16 +177,10 @@ cudaError_t permute_rows_ep(const void* x, int elem_bytes, int64_t n_tokens, int
                             const int32_t* block_off, const int32_t* seg_start, const int32_t* counts,
                             int64_t max_rows, const EpRoute* route, int32_t* row_of, int* err, cudaStream_t stream);
 // force_bn: 0 = auto, 128 / 256 = one-CTA tile width, -1 = CTA pairs,
-// -2 = swapped operands over expert segments (args.seg_start / seg_count),
-// -3 = CTA pairs with 256 x 512 tiles.
+// -2 = swapped operands over expert segments (args.seg_start / seg_count).
 cudaError_t grouped_gemm(int dtype, const void* a, int64_t a_rows, const void* w, const GemmArgs& args, bool relu,
                          int num_sms, cudaStream_t stream, int force_bn);
 cudaError_t grouped_gemm_pair(int dtype, const void* a, int64_t a_rows, const void* w, const GemmArgs& args, bool relu,
-                              int num_sms, cudaStream_t stream);
-// 256 x 512 tiles on CTA pairs (grouped_gemm_wide.cu): the pair kernel's
-// arithmetic with each A k-block reused for two 256-column accumulators;
-// no relu_bits, tile_dst or second problem.
-cudaError_t grouped_gemm_wide(int dtype, const void* a, int64_t a_rows, const void* w, const GemmArgs& args, bool relu,
                               int num_sms, cudaStream_t stream);
 cudaError_t grouped_gemm_swap(int dtype, const void* a, int64_t a_rows, const void* w, const GemmArgs& args, bool relu,
                               int num_sms, cudaStream_t stream);

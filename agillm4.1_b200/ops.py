@@ -207,7 +207,7 @@ def moe_forward(x: torch.Tensor, w_router: torch.Tensor, w1: torch.Tensor, b1: t
                 b2: torch.Tensor, top_k: int, *, shared: Optional[tuple] = None, out: Optional[torch.Tensor] = None,
                 want: tuple = (), tie_low_first: bool = False, workspace: Optional[torch.Tensor] = None,
                 check_errors: bool = False, stage_events=None, logits_in: Optional[torch.Tensor] = None,
-                pair: bool = True, swap: bool = True, pdl: bool = True, fold: bool = True, wide: bool = False):
+                pair: bool = True, swap: bool = True, pdl: bool = True, fold: bool = True):
     """Fused forward: x [N, d] -> out [N, d]. ``want`` may hold 'idx', 'gates', 'counts', 'logits'.
 
     Weights: w_router [E, d]; w1 [E, H, d]; b1 [E, H]; w2 [E, d, H]; b2 [E, d];
@@ -223,7 +223,6 @@ def moe_forward(x: torch.Tensor, w_router: torch.Tensor, w1: torch.Tensor, b1: t
     waits for the previous kernel to complete before it launches). ``fold``:
     on CTA pairs, run the shared experts inside the routed FC1/FC2 launches
     (False: their own launches; the result is the same bit for bit).
-    ``wide``: run the routed CTA-pair GEMMs with 256 x 512 tiles (same bits).
     Returns out, or (out, extras dict) when ``want`` is not empty.
     """
     lib = load()
@@ -256,8 +255,7 @@ def moe_forward(x: torch.Tensor, w_router: torch.Tensor, w1: torch.Tensor, b1: t
         ptr(x), dtype_code(x.dtype), n, d, E, top_k, H, ptr(w_router), ptr(w1), ptr(b1), ptr(w2), ptr(b2), S,
         max(Hs, 1), ptr(ws1), ptr(sb1), ptr(ws2), ptr(sb2), ptr(out), ptr(workspace), workspace.numel(),
         _flags(tie_low_first) | (0 if pair else _lib.AGM_FLAG_NO_PAIR) | (0 if swap else _lib.AGM_FLAG_NO_SWAP)
-        | (0 if pdl else _lib.AGM_FLAG_NO_PDL) | (0 if fold else _lib.AGM_FLAG_NO_FOLD)
-        | (_lib.AGM_FLAG_WIDE if wide else 0),
+        | (0 if pdl else _lib.AGM_FLAG_NO_PDL) | (0 if fold else _lib.AGM_FLAG_NO_FOLD),
         ptr(extras.get("idx")), ptr(extras.get("gates")), ptr(extras.get("counts")),
         ptr(extras.get("logits")), ptr(logits_in), None if ev_arr is None else ctypes.addressof(ev_arr),
         stream_handle(dev))

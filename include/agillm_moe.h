@@ -82,8 +82,6 @@ enum {
                                       problems too small to fill the GPU with pair tiles */
 #define AGM_FLAG_NO_FOLD 0x40     /* agm_moe_forward: shared experts in their own GEMM launches
                                       (default: inside the routed FC1 / FC2 launches on CTA pairs) */
-#define AGM_FLAG_WIDE 0x80        /* agm_moe_forward: CTA-pair expert GEMMs with 256 x 512 tiles (each
-                                      A k-block feeds two accumulators; same bits as 256 x 256) */
 
 AGM_API const char* agm_last_error(void);
 AGM_API int agm_abi_version(void);

@@ -335,26 +335,6 @@ def test_shared_experts_folded_into_routed_launches(E, k, H, S, n):
     assert torch.equal(out_r, out_f + res)
 
 
-@pytest.mark.parametrize("d,H,E,k,n,dtype", [(1280, 3200, 14, 2, 20000, torch.bfloat16),
-                                               (1280, 5120, 2, 1, 33792, torch.bfloat16),
-                                               (1280, 3200, 14, 2, 9000, torch.float16),
-                                               (256, 768, 8, 3, 12000, torch.bfloat16)])
-def test_wide_pair_tiles_match_pair_tiles(d, H, E, k, n, dtype):
-    """The 256 x 512 CTA-pair GEMM (AGM_FLAG_WIDE) against the 256 x 256 one:
-    every output element sums the same k-blocks in the same order, so the
-    forward is identical bit for bit; FC1's 3200 columns end in a 128-column
-    tile and FC2's 1280 in a half-used one, 768 in a 256-column one."""
-    sd = synthetic.make_state(d, H, E, 60 + k, dtype=dtype, device=DEV, bias_std=0.02)
-    w1, b1, w2, b2, _ = packed(sd, E, DEV)
-    wr = sd["router.weight"].contiguous()
-    x = synthetic.make_input(n, d, 61 + k, dtype=dtype, device=DEV)
-    out_p = ops.moe_forward(x, wr, w1, b1, w2, b2, k, check_errors=True)
-    out_w = ops.moe_forward(x, wr, w1, b1, w2, b2, k, check_errors=True, wide=True)
-    assert torch.equal(out_w, out_p)
-    out_w2 = ops.moe_forward(x, wr, w1, b1, w2, b2, k, check_errors=True, wide=True)
-    assert torch.equal(out_w2, out_w)
-
-
 @pytest.mark.parametrize("n,k,E", [(64, 2, 14), (200, 2, 14), (37, 1, 4), (96, 3, 16)])
 def test_swap_gemm_forward_matches_row_tiles(n, k, E):
     """Decode-sized batches run the expert GEMMs with swapped operands (weights
