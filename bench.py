@@ -882,7 +882,7 @@ def run_codec(args, dev, stream, cpu_leg):
 
 
 def _ep_variant(args, world, rank, dev, stream, x, weights, ref, counts_all, kind, placement, replicas=None,
-                chunks=1):
+                chunks=1, reserve_sms=20):
     """Time one expert-parallel variant on this rank's tokens x; the max over
     ranks of the device time of exactly args.steps forwards."""
     import torch.distributed as dist
@@ -894,7 +894,7 @@ def _ep_variant(args, world, rank, dev, stream, x, weights, ref, counts_all, kin
     mine = ep.ExpertParallelMoE.shard_weights(w1, b1, w2, b2, rank, world, placement, replicas=replicas)
     if kind == "p2p":
         moe = ep.P2PExpertParallelMoE((wr,) + tuple(mine), TOP_K, EXPERTS, max_tokens=N, placement=placement,
-                                      chunks=chunks, replicas=replicas)
+                                      chunks=chunks, replicas=replicas, reserve_sms=reserve_sms)
     else:
         moe = ep.ExpertParallelMoE((wr,) + tuple(mine), TOP_K, EXPERTS, placement=placement)
     for _ in range(args.warmup):
@@ -1005,6 +1005,12 @@ def run_ep(args, world, rank, local):
         for placement in ("static", "balanced", "local"):
             others[f"p2p_{placement}"] = _ep_variant(args, world, rank, dev, stream, x, weights, ref, counts_all,
                                                      "p2p", placement)
+        # the declared placement with token chunks overlapped on two streams (dispatch of chunk j+1
+        # while chunk j's GEMMs run on all but `reserve` SMs)
+        for chunks, reserve in ((2, 8), (4, 8), (2, 20)):
+            others[f"p2p_{EP_DECLARED}_chunks{chunks}_reserve{reserve}"] = _ep_variant(
+                args, world, rank, dev, stream, x, weights, ref, counts_all, "p2p", EP_DECLARED, replicas,
+                chunks=chunks, reserve_sms=reserve)
     skewed = {}
     if not args.skip_skewed:
         xs, wsk = skewed_workload(dev, rank, N)
