@@ -114,6 +114,17 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 #define AGM_WAIT_LIMIT_NS 4000000000ull
 #endif
 
+// System-scope release store / acquire load of a flag (flags that other GPUs
+// write or read over NVLink).
+__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -9,15 +9,18 @@
 //   -> device plan (every rank computes the same one from the counts)
 //   -> permute: every (token, rank) row is written straight into the
 //      receive buffer of the rank that computes it (NVLink stores)
-//   -> [flag barrier] -> grouped FC1/FC2 (CTA pairs) on the received tiles;
+//   -> [signal to every rank] -> grouped FC1/FC2 (CTA pairs) on the received
+//      tiles, own rows first; FC1 waits for a source's signal only before its
+//      first tile from that source, so it starts while peers' rows arrive;
 //      FC2's epilogue writes each output row straight into the home buffer
 //      of the rank that owns the token, at the row's x_perm position
 //      (NVLink stores, overlapped with the GEMM) -> [flag barrier]
 //   -> combine: each token's k expert rows, read from this rank's own home
 //      buffer (the single-GPU combine kernel).
 //
-// No host synchronisation and no library collective: the counts exchange and
-// the three barriers are flag writes/reads in peer memory with bounded waits.
+// No host synchronisation and no library collective: the counts exchange, the
+// delivery signals and the barrier after FC2 are flag writes/reads in peer
+// memory with bounded waits.
 //
 // Every rank owns one "comm" buffer allocated with cudaMalloc (IPC-shareable),
 // laid out identically on all ranks:
@@ -68,14 +71,6 @@ struct EpPlacement {
   uint32_t holders[AGM_MAX_EXPERTS];  // bit r: rank r holds expert e's weights
 };
 
-__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
-  uint64_t v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
 
 struct PeerComm {
   uint64_t base[kEpMaxRanks];  // every rank's comm buffer as mapped in this process
@@ -121,6 +116,18 @@ __global__ void ep_barrier_kernel(PeerComm pc, int world, int rank, uint64_t epo
   ep_barrier_warp(pc, world, rank, epoch, err);
 }
 
+// The release half of a barrier: after the permute has written this rank's
+// rows into the computing ranks' receive buffers, tell every rank so
+// (signal[rank] = epoch on each). The waits happen where the rows are
+// consumed: the expert GEMM's producer waits, per source, before loading the
+// first tile that source sent (GemmArgs::tile_src).
+__global__ void ep_signal_kernel(PeerComm pc, int world, int rank, uint64_t epoch) {
+  const int lane = lane_id();
+  __threadfence_system();
+  __syncwarp();
+  if (lane < world) st_release_sys(reinterpret_cast<uint64_t*>(pc.base[lane]) + rank, epoch);
+}
+
 // One CTA: the global plan from the counts inbox (identical on every rank),
 // this rank's send segments and its receive-side tile tables.
 //
@@ -141,12 +148,14 @@ __global__ void ep_barrier_kernel(PeerComm pc, int world, int rank, uint64_t epo
 //   local (every rank holds every expert): rank r's quota is an equal share
 //     of all units; each source keeps its first min(own, quota) units and
 //     sends the rest, in order, to the ranks below quota (lowest rank first).
-// A destination lays its pieces out by (source, expert). For every received
-// tile the tables give the local weight index of its expert and the address,
-// in the source rank's home buffer, where the tile's FFN output goes.
+// A destination lays its pieces out by (source, expert), its own source
+// first. For every received tile the tables give the local weight index of
+// its expert, the source rank, and the address, in the source rank's home
+// buffer, where the tile's FFN output goes.
 __global__ void __launch_bounds__(256) ep_plan_kernel(PeerComm pc, int world, int rank, int E, EpPlacement pl,
                                                       int64_t cap_rows, int64_t home_rows, int d, int eb,
                                                       EpRoute* route, int32_t* __restrict__ recv_tile_expert,
+                                                      int32_t* __restrict__ recv_tile_src,
                                                       uint64_t* __restrict__ recv_tile_dst,
                                                       int32_t* __restrict__ recv_num_tiles, int* err) {
   __shared__ int units[kEpMaxRanks][AGM_MAX_EXPERTS];
@@ -308,15 +317,20 @@ __global__ void __launch_bounds__(256) ep_plan_kernel(PeerComm pc, int world, in
   }
   __syncthreads();
   // Destination offsets: one thread per destination rank.
+  // A destination lays its pieces out source by source starting with its
+  // own rows (sources r, r+1, ... mod P), so its GEMM can begin on rows that
+  // never crossed NVLink while the peers' rows are still arriving.
   if (tid < world) {
     const int r = tid;
     int acc = 0;
-    for (int i = 0; i < world; ++i)
+    for (int j = 0; j < world; ++j) {
+      const int i = (r + j) % world;
       for (int e = 0; e < E; ++e) {
         if (i == rank) base_send[e][r] = acc;
         if (r == rank) base_recv[i][e] = acc;
         acc += cut_hi[i][e][r] - cut_lo[i][e][r];
       }
+    }
     if (r == rank) total_recv = acc;
   }
   __syncthreads();
@@ -372,6 +386,7 @@ __global__ void __launch_bounds__(256) ep_plan_kernel(PeerComm pc, int world, in
         continue;
       }
       recv_tile_expert[slot] = le;
+      recv_tile_src[slot] = i;
       recv_tile_dst[slot] = home + static_cast<uint64_t>(src_tile * 128 * row_bytes);
     }
   }
@@ -407,6 +422,7 @@ struct EpLayout {
   int32_t* row_of;
   agm::EpRoute* route;
   int32_t* recv_tile_expert;
+  int32_t* recv_tile_src;
   uint64_t* recv_tile_dst;
   int32_t* recv_num_tiles;
   void* h;
@@ -439,6 +455,7 @@ EpLayout ep_carve(void* ws, int64_t n, int d, int E, int k, int H, int64_t cap_r
   L.row_of = static_cast<int32_t*>(take(sizeof(int32_t) * n * k));
   L.route = static_cast<agm::EpRoute*>(take(sizeof(agm::EpRoute)));
   L.recv_tile_expert = static_cast<int32_t*>(take(sizeof(int32_t) * (cap_tiles + 1)));
+  L.recv_tile_src = static_cast<int32_t*>(take(sizeof(int32_t) * (cap_tiles + 1)));
   L.recv_tile_dst = static_cast<uint64_t*>(take(sizeof(uint64_t) * (cap_tiles + 1)));
   L.recv_num_tiles = static_cast<int32_t*>(take(sizeof(int32_t)));
   L.h = take(static_cast<size_t>(eb) * cap_rows * H);
@@ -526,8 +543,8 @@ AGM_API size_t agm_ep_workspace_bytes(int64_t n_tokens, int d, int n_experts, in
 }
 
 // Phase 1 (comm stream): route and permute this rank's tokens into the
-// receive buffers of the ranks that compute them; ends with the barrier after
-// which every rank's received rows are complete.
+// receive buffers of the ranks that compute them; ends by signalling every
+// rank that this rank's rows are delivered.
 AGM_API int agm_ep_dispatch(const void* x, int dtype, int64_t n_tokens, int d, int n_experts, int top_k, int hidden,
                             const void* w_router, int placement, const uint32_t* expert_holders, int world, int rank,
                             const uint64_t* peer_comm, int64_t cap_rows, int64_t home_rows, uint64_t epoch,
@@ -585,7 +602,8 @@ AGM_API int agm_ep_dispatch(const void* x, int dtype, int64_t n_tokens, int d, i
   agm::ep_counts_exchange_kernel<<<1, 256, 0, stream>>>(pc, world, rank, n_experts, L.counts, epoch, L.err);
   if ((e = cudaGetLastError()) != cudaSuccess) return ep_cuda(e, "counts exchange");
   agm::ep_plan_kernel<<<1, 256, 0, stream>>>(pc, world, rank, n_experts, pl, cap_rows, home_rows, d, eb, L.route,
-                                             L.recv_tile_expert, L.recv_tile_dst, L.recv_num_tiles, L.err);
+                                             L.recv_tile_expert, L.recv_tile_src, L.recv_tile_dst,
+                                             L.recv_num_tiles, L.err);
   if ((e = cudaGetLastError()) != cudaSuccess) return ep_cuda(e, "ep plan");
   if ((e = mark(2)) != cudaSuccess) return ep_cuda(e, "event");
   if (n_tokens > 0) {
@@ -594,13 +612,15 @@ AGM_API int agm_ep_dispatch(const void* x, int dtype, int64_t n_tokens, int d, i
     if (e != cudaSuccess) return ep_cuda(e, "dispatch");
   }
   if ((e = mark(3)) != cudaSuccess) return ep_cuda(e, "event");
-  agm::ep_barrier_kernel<<<1, 32, 0, stream>>>(pc, world, rank, epoch + 1, L.err);
-  if ((e = cudaGetLastError()) != cudaSuccess) return ep_cuda(e, "barrier");
+  agm::ep_signal_kernel<<<1, 32, 0, stream>>>(pc, world, rank, epoch + 1);
+  if ((e = cudaGetLastError()) != cudaSuccess) return ep_cuda(e, "signal");
   if ((e = mark(4)) != cudaSuccess) return ep_cuda(e, "event");
   return AGM_OK;
 }
 
-// Phase 2 (compute stream): FC1 over the received tiles into h, FC2 from h
+// Phase 2 (compute stream): FC1 over the received tiles into h (its producer
+// waits, per source, for that source's signal before loading its first
+// tile; own rows come first), FC2 from h
 // straight into the home buffers of the ranks whose tokens they are (NVLink
 // stores for peers), then the barrier after which every rank's results are
 // complete. gemm_ctas > 0 caps the GEMM's persistent CTAs (leaving SMs to
@@ -643,6 +663,10 @@ AGM_API int agm_ep_expert(int dtype, int64_t n_tokens, int d, int n_experts, int
   g1.max_tiles = static_cast<int>(cap_rows / 128);
   g1.err = L.err;
   g1.max_ctas = gemm_ctas;
+  // Rows of source i are complete once i signalled epoch + 1 here.
+  g1.tile_src = L.recv_tile_src;
+  g1.src_signal = reinterpret_cast<const uint64_t*>(peer_comm[rank]);
+  g1.src_epoch = epoch + 1;
   e = agm::grouped_gemm(dtype, recv, cap_rows, w1, g1, true, sms, stream, AGM_GEMM_PAIR);
   if (e != cudaSuccess) return ep_cuda(e, "grouped_gemm fc1");
   if ((e = mark(0)) != cudaSuccess) return ep_cuda(e, "event");
@@ -653,6 +677,7 @@ AGM_API int agm_ep_expert(int dtype, int64_t n_tokens, int d, int n_experts, int
   g2.n = d;
   g2.k = hidden;
   g2.tile_dst = L.recv_tile_dst;
+  g2.tile_src = nullptr;  // h is this rank's own
   e = agm::grouped_gemm(dtype, L.h, cap_rows, w2, g2, false, sms, stream, AGM_GEMM_PAIR);
   if (e != cudaSuccess) return ep_cuda(e, "grouped_gemm fc2");
   if ((e = mark(1)) != cudaSuccess) return ep_cuda(e, "event");

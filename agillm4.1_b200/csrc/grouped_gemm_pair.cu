@@ -220,8 +220,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     bool waited = !args.early_weights;
     int deferred = 0, ndef = 0, first_row = 0;
     const CUtensorMap* first_a = &tmA;
+    uint32_t src_ready = 0;  // sources whose rows are known to have arrived (tile_src)
     for (int t = cluster; t < total && ok; t += nclusters) {
       const PairUnit u = pair_unit(t, total0, num_p, num_m, num_n, num_p2, num_n2, args);
+      if (u.prob == 0 && args.tile_src) {
+        // Expert parallelism: wait (bounded) for the source's "rows
+        // delivered" release before the first load of one of its tiles; the
+        // proxy fence orders the TMA reads after that acquire.
+        const int src = args.tile_src[u.m0];
+        if (src >= 0 && src < 32 && !((src_ready >> src) & 1u)) {
+          if (lane == 0 && ld_acquire_sys(args.src_signal + src) < args.src_epoch) {
+            const uint64_t t0 = globaltimer_ns();
+            while (ld_acquire_sys(args.src_signal + src) < args.src_epoch) {
+              if (globaltimer_ns() - t0 > AGM_WAIT_LIMIT_NS) {
+                raise_error(args.err, kErrTimeoutFull);
+                *abort_s = 1;
+                break;
+              }
+              __nanosleep(128);
+            }
+          }
+          if (lane == 0) asm volatile("fence.proxy.async.global;" ::: "memory");
+          __syncwarp();
+          if (*abort_s) {
+            ok = false;
+            break;
+          }
+          src_ready |= 1u << src;
+        }
+      }
       const CUtensorMap* mA = u.prob ? &tmA2 : &tmA;
       const CUtensorMap* mB = u.prob ? &tmB2 : &tmB;
       // Rank 1 loads the pair's second row tile (or repeats the first when there is none).

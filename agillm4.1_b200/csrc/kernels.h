@@ -75,6 +75,13 @@ struct GemmArgs {
   // instead of c, e.g. the token owner's buffer on a peer GPU (expert
   // parallelism); stored with 16-byte vector stores.
   const uint64_t* tile_dst = nullptr;
+  // CTA-pair kernel only, nullable: row tile t came from source rank
+  // tile_src[t] (expert parallelism); before loading the first tile of a
+  // source the producer waits (bounded) until src_signal[source] >= src_epoch,
+  // the source's release of "rows delivered".
+  const int32_t* tile_src = nullptr;
+  const uint64_t* src_signal = nullptr;
+  uint64_t src_epoch = 0;
   // CTA-pair kernel only: a second, dense problem computed in the same launch
   // after this one's tiles (the shared experts of a MoE block): groups2
   // groups of tiles2 row tiles each; group g reads A rows from

@@ -59,7 +59,7 @@ TILE_ROWS = 128
 # permutation of the experts (seed 3), which gives a ~5:1 max/mean expert load.
 EP_SEED, ZIPF_S, ZIPF_SCALE = 3, 1.2, 0.63
 EP_STAGES = ["route", "counts_plan", "dispatch_a2a", "expert_ffn", "return_a2a", "combine"]
-P2P_STAGES = ["route", "counts_exchange_plan", "dispatch_to_peers", "barrier", "fc1", "fc2_to_owners", "barrier2",
+P2P_STAGES = ["route", "counts_exchange_plan", "dispatch_to_peers", "signal", "fc1", "fc2_to_owners", "barrier2",
               "combine"]
 
 

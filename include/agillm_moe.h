@@ -280,12 +280,15 @@ AGM_API size_t agm_ep_workspace_bytes(int64_t n_tokens, int d, int n_experts, in
  * holders' loads. AGM_EP_BALANCED / AGM_EP_LOCAL need every bit set.
  * peer_comm: HOST array of `world` device addresses of every rank's
  * communication buffer as mapped here (own buffer at [rank]). The counts
- * exchange and three barriers are flag writes in peer memory, bounded waits
- * (a time-out sets the device error word, the first int of the workspace).
+ * exchange, the delivery signals and the barrier after FC2 are flag writes
+ * in peer memory, bounded waits (a time-out sets the device error word, the
+ * first int of the workspace). A rank's receive buffer holds its own rows
+ * first; FC1 waits for a source's delivery signal only before that source's
+ * first tile, so it starts while the peers' rows still arrive.
  * stage_events (nullable): AGM_EP_STAGE_EVENTS cudaEvent_t handles recorded
  * before the router and after: local plan, counts exchange + global plan,
- * dispatch (permute into peers), barrier, FC1, FC2 (which writes every output
- * row into its owner's home buffer), barrier, combine.
+ * dispatch (permute into peers), delivery signal, FC1, FC2 (which writes
+ * every output row into its owner's home buffer), barrier, combine.
  * No host synchronisation; outputs are bit-identical to agm_moe_forward on
  * the same tokens.                                                           */
 #define AGM_EP_STAGE_EVENTS 9
@@ -297,7 +300,8 @@ AGM_API size_t agm_ep_workspace_bytes(int64_t n_tokens, int d, int n_experts, in
  * and epoch sequence; a chunk's phases must run in order (dispatch, expert,
  * combine) with the caller ordering them across streams (events).
  * agm_ep_dispatch: router, local plan, counts exchange, device plan, rows into
- *   the computing ranks' receive buffers, barrier (stage_events: 5 events).
+ *   the computing ranks' receive buffers, delivery signal to every rank
+ *   (stage_events: 5 events).
  * agm_ep_expert: FC1/FC2 on the received tiles (n_local_experts weights),
  *   results into the owners' home buffers, barrier; gemm_ctas > 0 caps the
  *   GEMM's persistent CTAs (stage_events: 3 events).
