@@ -1005,12 +1005,7 @@ def run_ep(args, world, rank, local):
         for placement in ("static", "balanced", "local"):
             others[f"p2p_{placement}"] = _ep_variant(args, world, rank, dev, stream, x, weights, ref, counts_all,
                                                      "p2p", placement)
-        # the declared placement with token chunks overlapped on two streams (dispatch of chunk j+1
-        # while chunk j's GEMMs run on all but `reserve` SMs)
-        for chunks, reserve in ((2, 8), (4, 8), (2, 20)):
-            others[f"p2p_{EP_DECLARED}_chunks{chunks}_reserve{reserve}"] = _ep_variant(
-                args, world, rank, dev, stream, x, weights, ref, counts_all, "p2p", EP_DECLARED, replicas,
-                chunks=chunks, reserve_sms=reserve)
+
     skewed = {}
     if not args.skip_skewed:
         xs, wsk = skewed_workload(dev, rank, N)
