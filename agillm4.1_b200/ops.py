@@ -283,7 +283,7 @@ class HostWorkspace:
         return buf
 
 
-DEFAULT_CHUNK_TOKENS = 8192
+DEFAULT_CHUNK_TOKENS = 6144
 
 
 def moe_forward_host(x_host: torch.Tensor, w_router: torch.Tensor, w1: torch.Tensor, b1: torch.Tensor,
