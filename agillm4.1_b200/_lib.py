@@ -84,6 +84,10 @@ SIGNATURES = {
     "agm_moe_forward_noalloc": (_I, [_P, _I, _I64, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _P, _P,
                                      _I, _P]),
     "agm_moe_noalloc_error_word": (_I, [_P]),
+    "agm_layernorm": (_I, [_P, _P, _P, ctypes.c_float, _I, _I64, _I, _P, _P]),
+    "agm_moe_block_workspace_bytes": (_SZ, [_I64, _I, _I, _I, _I, _I, _I, _I]),
+    "agm_moe_block_forward": (_I, [_P, _P, _P, ctypes.c_float, _I, _I64, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I,
+                                   _P, _P, _P, _P, _P, _P, _SZ, _I, _P]),
     "agm_moe_train_saved_bytes": (_SZ, [_I64, _I, _I, _I, _I, _I, _I, _I, _I]),
     "agm_moe_backward_workspace_bytes": (_SZ, [_I64, _I, _I, _I, _I, _I, _I, _I]),
     "agm_cast_f32": (_I, [_P, _P, _I, _I64, _P]),

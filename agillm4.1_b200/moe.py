@@ -370,6 +370,37 @@ class _B200Forward:
             raise MoEKernelError(f"residual shape {tuple(residual.shape)} differs from {tuple(x.shape)}")
         return self._forward_impl(x, residual)
 
+    def forward_block(self, x: torch.Tensor, ln: nn.Module) -> torch.Tensor:
+        """``x + self(ln(x))``: the whole FFN half of Block.forward
+        (agillm41.py:4547, `x + self.ff(self.ln2(x))`; with a KV cache pass
+        x + y, 4543), x being the block input and ``ln`` its ``ln2``. In
+        inference (no gradient, device-resident experts, kernel routing, one
+        dtype throughout) the LayerNorm runs on this library's HBM-bound kernel
+        and the residual is added in the combine (agm_moe_forward_residual);
+        otherwise it is ``self.forward_residual(ln(x), x)`` with torch's
+        LayerNorm. The LayerNorm's statistics are reduced in another order than
+        torch's, so the result is within the bf16 parity tolerance of the
+        reference, not bit-identical to it."""
+        wr = self.router.weight
+        flat = x.reshape(-1, x.shape[-1])
+        fusable = (
+            isinstance(ln, nn.LayerNorm) and ln.elementwise_affine and tuple(ln.normalized_shape) == (x.shape[-1],)
+            and ln.weight is not None and ln.bias is not None
+            and not (torch.is_grad_enabled() and (x.requires_grad or any(p.requires_grad for p in self.parameters())
+                                                  or ln.weight.requires_grad))
+            and not self.training and not self.expert_stream and self.router_logits == "kernel"
+            and flat.is_cuda and wr.is_cuda and flat.dtype == wr.dtype == ln.weight.dtype == ln.bias.dtype
+            and _autocast_dtype(flat.device) is None
+            and x.shape[-1] <= (1536 if flat.dtype == torch.float32 else 2048)
+        )
+        if not fusable:
+            return self.forward_residual(ln(x), x)
+        w1, b1, w2, b2, sh = self._packed_weights(flat.device, flat.dtype)
+        out = ops.moe_block_forward(flat.contiguous(), ln.weight.detach().contiguous(), ln.bias.detach().contiguous(),
+                                    float(ln.eps), wr.detach().contiguous(), w1, b1, w2, b2, self.top_k, shared=sh,
+                                    check_errors=self.check_device_errors)
+        return out.reshape(x.shape)
+
     def _forward_impl(self, x: torch.Tensor, residual: Optional[torch.Tensor]) -> torch.Tensor:
         orig_shape = x.shape
         flat = x.reshape(-1, orig_shape[-1])
@@ -522,21 +553,29 @@ class MoEFFN(_B200Forward, nn.Module):
 
 def _fused_block_forward(self, x, mask, kv=None, use_cache=False, total_seq_len=None):
     """Block.forward (agillm41.py:4539-4547) with the MoE FFN's residual add
-    done by its combine kernel (`x + ff(ln2(x))` as one call); any other ff
-    runs the reference's own forward."""
+    done by its combine kernel (`x + ff(ln2(x))` as one call) and, when the
+    Block was installed with ``fuse_layernorm``, ln2 on this library's
+    LayerNorm kernel in inference; any other ff runs the reference's own
+    forward."""
     ff = self.ff
     if not isinstance(ff, _B200Forward):
         return self._reference_block_forward(x, mask, kv=kv, use_cache=use_cache, total_seq_len=total_seq_len)
+
+    def ffn_half(r):
+        if getattr(self, "_fuse_layernorm", False):
+            return ff.forward_block(r, self.ln2)
+        return ff.forward_residual(self.ln2(r), r)
+
     if use_cache:
         y, new_kv = self.mha(self.ln1(x), mask, rel_bias_tokens=total_seq_len, kv_cache=kv, use_cache=True)
-        r = x + y  # the reference's `x + y + ff(ln2(x + y))`
-        return ff.forward_residual(self.ln2(r), r), new_kv
+        return ffn_half(x + y), new_kv  # the reference's `x + y + ff(ln2(x + y))`
     n = x.size(1)
     x = x + self.mha(self.ln1(x), mask, rel_bias_tokens=n)
-    return ff.forward_residual(self.ln2(x), x)
+    return ffn_half(x)
 
 
-def install(agillm41_module, name: str = "MoEFFN", fuse_residual: bool = False, fuse_aux: bool = True):
+def install(agillm41_module, name: str = "MoEFFN", fuse_residual: bool = False, fuse_aux: bool = True,
+            fuse_layernorm: bool = False):
     """Rebind ``agillm41_module.MoEFFN`` to a subclass of the reference class
     whose forward runs on the B200 kernels. Returns the new class.
 
@@ -548,6 +587,10 @@ def install(agillm41_module, name: str = "MoEFFN", fuse_residual: bool = False, 
     ``fuse_residual``: also rebind ``Block`` to a subclass whose forward adds
     the residual inside the MoE block's combine kernel (same values and
     gradients, one elementwise pass less per layer).
+
+    ``fuse_layernorm`` (implies ``fuse_residual``): that Block's inference
+    forward also runs ln2 on this library's LayerNorm kernel
+    (:meth:`forward_block`); training keeps torch's LayerNorm.
 
     ``fuse_aux``: also rebind ``_collect_moe_aux`` (called by the training
     steps, agillm41.py:1378, 6798) to :func:`collect_moe_aux`, which computes
@@ -561,9 +604,10 @@ def install(agillm41_module, name: str = "MoEFFN", fuse_residual: bool = False, 
                                                    "__module__": ref_cls.__module__})
         setattr(agillm41_module, name, cls)
     block = getattr(agillm41_module, "Block", None)
-    if fuse_residual and block is not None and not getattr(block, "_is_b200", False):
+    if (fuse_residual or fuse_layernorm) and block is not None and not getattr(block, "_is_b200", False):
         fused = type("Block", (block,), {"_is_b200": True, "_reference_class": block,
                                          "_reference_block_forward": block.forward,
+                                         "_fuse_layernorm": bool(fuse_layernorm),
                                          "forward": _fused_block_forward, "__module__": block.__module__})
         setattr(agillm41_module, "Block", fused)
     aux = getattr(agillm41_module, "_collect_moe_aux", None)

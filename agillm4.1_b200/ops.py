@@ -203,6 +203,49 @@ def moe_forward_residual(x: torch.Tensor, residual: torch.Tensor, w_router: torc
     return out
 
 
+def layernorm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float = 1e-5,
+              out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """LayerNorm over the last dimension of x [N, d] (agm_layernorm)."""
+    lib = load()
+    n, d = x.shape
+    out = torch.empty_like(x) if out is None else out
+    rc = lib.agm_layernorm(ptr(x), ptr(weight), ptr(bias), float(eps), dtype_code(x.dtype), n, d, ptr(out),
+                           stream_handle(x.device))
+    check(rc, "agm_layernorm")
+    return out
+
+
+def moe_block_forward(x: torch.Tensor, ln_weight: torch.Tensor, ln_bias: torch.Tensor, ln_eps: float,
+                      w_router: torch.Tensor, w1: torch.Tensor, b1: torch.Tensor, w2: torch.Tensor, b2: torch.Tensor,
+                      top_k: int, *, shared: Optional[tuple] = None, check_errors: bool = False) -> torch.Tensor:
+    """x + MoEFFN(LayerNorm(x)): the FFN half of Block.forward (agillm41.py:4547) in one call."""
+    lib = load()
+    n, d = x.shape
+    E = w_router.shape[0]
+    H = w1.shape[1]
+    if shared is not None:
+        ws1, sb1, ws2, sb2 = shared
+        S, Hs = ws1.shape[0], ws1.shape[1]
+    else:
+        ws1 = sb1 = ws2 = sb2 = None
+        S, Hs = 0, 1
+    nbytes = int(lib.agm_moe_block_workspace_bytes(n, d, E, top_k, H, S, Hs, dtype_code(x.dtype)))
+    if nbytes == 0:
+        raise _lib.MoEKernelError("agm_moe_block_workspace_bytes: unsupported shape or dtype")
+    ws = Workspace.get(x.device, nbytes)
+    out = torch.empty_like(x)
+    rc = lib.agm_moe_block_forward(ptr(x), ptr(ln_weight), ptr(ln_bias), float(ln_eps), dtype_code(x.dtype), n, d, E,
+                                   top_k, H, ptr(w_router), ptr(w1), ptr(b1), ptr(w2), ptr(b2), S, Hs, ptr(ws1),
+                                   ptr(sb1), ptr(ws2), ptr(sb2), ptr(out), ptr(ws), ws.numel(), 0,
+                                   stream_handle(x.device))
+    check(rc, "agm_moe_block_forward")
+    if check_errors:
+        code = _lib.read_device_error(ws[:4].view(torch.int32))
+        if code:
+            raise _lib.MoEKernelError(f"device error word 0x{code:x} after agm_moe_block_forward")
+    return out
+
+
 def moe_forward(x: torch.Tensor, w_router: torch.Tensor, w1: torch.Tensor, b1: torch.Tensor, w2: torch.Tensor,
                 b2: torch.Tensor, top_k: int, *, shared: Optional[tuple] = None, out: Optional[torch.Tensor] = None,
                 want: tuple = (), tie_low_first: bool = False, workspace: Optional[torch.Tensor] = None,

@@ -181,6 +181,32 @@ AGM_API int agm_moe_forward_residual(const void* x, const void* residual, int dt
                                      const void* ws1, const void* sb1, const void* ws2, const void* sb2, void* out,
                                      void* workspace, size_t workspace_bytes, int flags, void* stream);
 
+/* LayerNorm over the last dimension with an affine weight and bias, as the
+ * Block's nn.LayerNorm(d) computes it (agillm41.py:4518; applied as ln2 at
+ * 4543 and 4547): x [n, d] -> out [n, d] in dtype. Statistics in fp32 (mean,
+ * then the mean squared deviation from it, rstd = rsqrt(var + eps)); y =
+ * (x - mean) * rstd * weight + bias rounded once to dtype. torch reduces in
+ * another order, so a value can differ from torch's by one unit in the last
+ * place of dtype. d * sizeof(dtype) a multiple of 16 bytes; d <= 2048 for
+ * 16-bit dtypes, <= 1536 for fp32. One warp per row, HBM-bound.            */
+AGM_API int agm_layernorm(const void* x, const void* weight, const void* bias, float eps, int dtype, int64_t n_rows,
+                          int d, void* out, void* stream);
+
+/* The FFN half of Block.forward (agillm41.py:4547, `x + self.ff(self.ln2(x))`;
+ * with a KV cache 4543, pass x + y): out = x + MoEFFN(LayerNorm(x)) with the
+ * LayerNorm of agm_layernorm written into the workspace and the residual
+ * added in the combine (agm_moe_forward_residual). workspace >=
+ * agm_moe_block_workspace_bytes(...); its first int is the device error
+ * word. out may not alias x.                                                 */
+AGM_API size_t agm_moe_block_workspace_bytes(int64_t n_tokens, int d, int n_experts, int top_k, int hidden,
+                                             int n_shared, int shared_hidden, int dtype);
+AGM_API int agm_moe_block_forward(const void* x, const void* ln_weight, const void* ln_bias, float ln_eps, int dtype,
+                                  int64_t n_tokens, int d, int n_experts, int top_k, int hidden,
+                                  const void* w_router, const void* w1, const void* b1, const void* w2, const void* b2,
+                                  int n_shared, int shared_hidden, const void* ws1, const void* sb1, const void* ws2,
+                                  const void* sb2, void* out, void* workspace, size_t workspace_bytes, int flags,
+                                  void* stream);
+
 /* Size of the scratch area compiled into the library for
  * agm_moe_forward_noalloc (32 MiB; e.g. up to 967 tokens at d=1280, H=3200,
  * 14 experts, top-2, bf16 without shared experts, or 647 tokens with one

@@ -157,6 +157,31 @@ def test_fused_residual_block(ref):
     assert ref.Block is orig_block and not getattr(ref.MoEFFN, "_is_b200", False)
 
 
+def test_fused_layernorm_block(ref):
+    """install(fuse_layernorm=True) rebinds Block to the fused subclass with
+    ln2 on the library's LayerNorm in inference; a dense FFN keeps the
+    reference's forward, and a MoE block on CPU still refuses (no CPU path)."""
+    orig_block = ref.Block
+    agillm41_b200.install(ref, fuse_layernorm=True)
+    try:
+        assert issubclass(ref.Block, orig_block) and ref.Block._fuse_layernorm
+        torch.manual_seed(0)
+        dense = ref.Block(64, 4, 16, moe_ffn=False).eval()
+        plain = orig_block(64, 4, 16, moe_ffn=False).eval()
+        plain.load_state_dict(dense.state_dict())
+        x = torch.randn(2, 5, 64)
+        with torch.no_grad():
+            assert torch.equal(dense(x, None), plain(x, None))
+        moe = ref.Block(64, 4, 16, moe_ffn=True, moe_experts=14, moe_top_k=2, moe_mlp_mult=2).eval()
+        assert set(moe.state_dict()) == set(orig_block(64, 4, 16, moe_ffn=True, moe_experts=14, moe_top_k=2,
+                                                       moe_mlp_mult=2).state_dict())
+        with torch.no_grad(), pytest.raises(MoEKernelError):
+            moe(x, None)
+    finally:
+        agillm41_b200.uninstall(ref)
+    assert ref.Block is orig_block
+
+
 def test_cpu_input_raises():
     m = MoEFFN(64, experts=14, top_k=2).eval()
     with torch.no_grad(), pytest.raises(MoEKernelError, match="CUDA"):
