@@ -31,6 +31,7 @@ AGM_FLAG_NO_PDL = 0x10
 AGM_EP_HOLDERS, AGM_EP_BALANCED, AGM_EP_LOCAL = 0, 1, 2
 AGM_FLAG_BWD_PAIR = 0x20
 AGM_FLAG_NO_FOLD = 0x40
+AGM_FLAG_DECODE_TILES = 0x80
 AGM_CODEC_PLAIN, AGM_CODEC_INT8, AGM_CODEC_INT8_ROWWISE = 0, 1, 2
 AGM_APPLY_COPY, AGM_APPLY_LERP, AGM_APPLY_ADD = 0, 1, 2
 
@@ -85,6 +86,7 @@ SIGNATURES = {
                                      _I, _P]),
     "agm_moe_noalloc_error_word": (_I, [_P]),
     "agm_layernorm": (_I, [_P, _P, _P, ctypes.c_float, _I, _I64, _I, _P, _P]),
+    "agm_decode_tile_layout": (_I, [_P, _P, _I, _I64, _I, _I, _P]),
     "agm_moe_block_workspace_bytes": (_SZ, [_I64, _I, _I, _I, _I, _I, _I, _I]),
     "agm_moe_block_forward": (_I, [_P, _P, _P, ctypes.c_float, _I, _I64, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I,
                                    _P, _P, _P, _P, _P, _P, _SZ, _I, _P]),

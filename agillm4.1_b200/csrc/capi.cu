@@ -351,6 +351,10 @@ int moe_forward_impl(const void* x, int dtype, int64_t n_tokens, int d, int n_ex
   // depth and only the valid rows of each segment enter the MMA.
   const bool swap = dtype != AGM_F32 && !(flags & AGM_FLAG_NO_SWAP) &&
                     static_cast<int64_t>(top_k) * n_tokens <= static_cast<int64_t>(AGM_SWAP_ROWS_PER_EXPERT) * n_experts;
+  const bool tiled = (flags & AGM_FLAG_DECODE_TILES) != 0;
+  if (tiled && (!swap || hidden % 128 || d % 128))
+    return fail(AGM_ERR_UNSUPPORTED, "decode tile layout: decode-sized batches (top_k * n_tokens <= 32 * n_experts), "
+                                     "16-bit dtypes, d and hidden multiples of 128");
   const int seg_align = pair ? AGM_PAIR_ROWS : AGM_TILE_M;
   const int gemm_mode = pair ? AGM_GEMM_PAIR : (swap ? -2 : 0);
 
@@ -387,6 +391,7 @@ int moe_forward_impl(const void* x, int dtype, int64_t n_tokens, int d, int n_ex
   // and the weights from before this forward: the GEMMs stream their first
   // weight tiles while the kernel before them finishes.
   g1.early_weights = true;
+  g1.w_tiled = tiled;
   const int64_t npad = round_up(n_tokens, AGM_TILE_M);
   // Shared experts: one dense group over all tokens, so any two row tiles
   // share their weights and the CTA-pair GEMM applies without padding.
@@ -501,6 +506,17 @@ int agm_moe_forward_residual(const void* x, const void* residual, int dtype, int
   return moe_forward_impl(x, dtype, n_tokens, d, n_experts, top_k, hidden, w_router, w1, b1, w2, b2, n_shared,
                           shared_hidden, ws1, sb1, ws2, sb2, residual, out, workspace, workspace_bytes, flags, nullptr,
                           nullptr, nullptr, nullptr, nullptr, nullptr, stream);
+}
+
+int agm_decode_tile_layout(const void* w, void* out, int dtype, int64_t groups, int n, int k, void* stream) {
+  if (dtype != AGM_BF16 && dtype != AGM_F16)
+    return fail(AGM_ERR_UNSUPPORTED, "agm_decode_tile_layout: 16-bit weights only");
+  if (groups <= 0 || n <= 0 || k <= 0 || n % 128 || k % 64)
+    return fail(AGM_ERR_ARG, "agm_decode_tile_layout: n must be a multiple of 128 and k of 64");
+  if (!w || !out || !aligned16(w) || !aligned16(out) || w == out)
+    return fail(AGM_ERR_ARG, "agm_decode_tile_layout: 16-byte aligned, distinct source and destination");
+  cudaError_t e = agm::decode_tile_layout(w, out, groups, n, k, num_sms_current(), static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? AGM_OK : cuda_fail(e, "agm_decode_tile_layout");
 }
 
 int agm_read_device_error(int* err, int* code, void* stream) {

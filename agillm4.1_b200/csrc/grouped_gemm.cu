@@ -422,9 +422,9 @@ static EncodeTiledFn get_encode_fn() {
 bool encode_tmap(CUtensorMap* m, const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
                         const uint32_t* box, CUtensorMapDataType dt) {
   EncodeTiledFn fn = get_encode_fn();
-  if (!fn) return false;
-  cuuint64_t gdim[3], gstr[2];
-  cuuint32_t bx[3], es[3];
+  if (!fn || rank < 1 || rank > 5) return false;
+  cuuint64_t gdim[5], gstr[4];
+  cuuint32_t bx[5], es[5];
   for (int i = 0; i < rank; ++i) {
     gdim[i] = dims[i];
     bx[i] = box[i];

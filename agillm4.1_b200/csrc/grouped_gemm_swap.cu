@@ -149,7 +149,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (lane == 0) {
           mbar_arrive_expect_tx(&full[stage], kWBytes + kABytes);
-          tma_load_3d(sW + stage * kWBytes, &tmW, kb * kBK, fb * kFM, e, &full[stage]);
+          if (args.w_tiled)
+            tma_load_5d(sW + stage * kWBytes, &tmW, 0, 0, kb, fb, e, &full[stage]);
+          else
+            tma_load_3d(sW + stage * kWBytes, &tmW, kb * kBK, fb * kFM, e, &full[stage]);
           if (waited) tma_load_2d(sA + stage * kABytes, &tmA, kb * kBK, row0, &full[stage]);
         }
         if (!waited && ++deferred == ndef) {
@@ -278,7 +281,16 @@ cudaError_t launch_swap(const void* a, int64_t a_rows, const void* w, const Gemm
     const uint32_t box[2] = {kBK, kRows};
     if (!encode_tmap(&tmA, a, 2, dims, str, box, dt)) return cudaErrorInvalidValue;
   }
-  {
+  if (args.w_tiled) {
+    // [groups][n / 128][k / 64][128 rows][64 elements]: a box is one contiguous 16 KB tile
+    if (args.n % kFM || args.k % kBK) return cudaErrorInvalidValue;
+    const uint64_t nkb = static_cast<uint64_t>(args.k / kBK), nfb = static_cast<uint64_t>(args.n / kFM);
+    const uint64_t dims[5] = {kBK, kFM, nkb, nfb, static_cast<uint64_t>(args.groups)};
+    const uint64_t tile = static_cast<uint64_t>(kFM) * kBK * 2;
+    const uint64_t str[4] = {kBK * 2, tile, tile * nkb, tile * nkb * nfb};
+    const uint32_t box[5] = {kBK, kFM, 1, 1, 1};
+    if (!encode_tmap(&tmW, w, 5, dims, str, box, dt)) return cudaErrorInvalidValue;
+  } else {
     const uint64_t dims[3] = {static_cast<uint64_t>(args.k), static_cast<uint64_t>(args.n),
                               static_cast<uint64_t>(args.groups)};
     const uint64_t str[2] = {static_cast<uint64_t>(args.k) * 2, static_cast<uint64_t>(args.k) * args.n * 2};
@@ -297,6 +309,38 @@ cudaError_t launch_swap(const void* a, int64_t a_rows, const void* w, const Gemm
 }
 
 }  // namespace
+
+namespace {
+
+// dst [groups][n / 128][k / 64][128][64] <- src [groups][n][k], 16 bytes per thread step.
+__global__ void decode_tile_layout_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, int64_t groups,
+                                          int n, int k) {
+  const int64_t total = groups * static_cast<int64_t>(n) * k / 8;
+  const int nkb = k / kBK, nfb = n / kFM;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < total;
+       v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t e = v * 8;                       // destination element
+    const int c = static_cast<int>(e % kBK);
+    const int r = static_cast<int>((e / kBK) % kFM);
+    const int64_t t = e / (kBK * kFM);             // tile index ((g * nfb + fb) * nkb + kb)
+    const int kb = static_cast<int>(t % nkb);
+    const int64_t gf = t / nkb;
+    const int fb = static_cast<int>(gf % nfb);
+    const int64_t g = gf / nfb;
+    const int64_t src_e = (g * n + static_cast<int64_t>(fb) * kFM + r) * k + static_cast<int64_t>(kb) * kBK + c;
+    dst[v] = __ldcs(src + src_e / 8);
+  }
+}
+
+}  // namespace
+
+cudaError_t decode_tile_layout(const void* src, void* dst, int64_t groups, int n, int k, int num_sms,
+                               cudaStream_t stream) {
+  if (n % kFM || k % kBK || groups <= 0) return cudaErrorInvalidValue;
+  decode_tile_layout_kernel<<<4 * num_sms, 256, 0, stream>>>(static_cast<const uint4*>(src), static_cast<uint4*>(dst),
+                                                             groups, n, k);
+  return cudaGetLastError();
+}
 
 cudaError_t grouped_gemm_swap(int dtype, const void* a, int64_t a_rows, const void* w, const GemmArgs& args, bool relu,
                               int num_sms, cudaStream_t stream) {

@@ -59,6 +59,10 @@ struct GemmArgs {
   // [seg_start[e], seg_start[e] + seg_count[e]) (device arrays, groups entries).
   const int32_t* seg_start = nullptr;
   const int32_t* seg_count = nullptr;
+  // Swapped-operand kernel only: the weight is in the decode tile layout
+  // [groups][n / 128][k / 64][128][64] (each 128 x 64 tile one contiguous
+  // 16 KB block) instead of [groups][n][k]; n % 128 == 0, k % 64 == 0.
+  bool w_tiled = false;
   // The caller guarantees that the tile table / segment counts and the
   // weights were written at least two kernels before this launch (true
   // inside agm_moe_forward): the kernel then reads them and streams its first
@@ -153,7 +157,7 @@ struct EpRows {
 };
 
 // Tiled TMA descriptor (128-byte swizzle, zero OOB fill) for a row-major
-// tensor of rank 2 or 3; dims and box innermost first, strides in bytes.
+// tensor of rank 1 to 5; dims and box innermost first, strides in bytes.
 bool encode_tmap(CUtensorMap* m, const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
                  const uint32_t* box, CUtensorMapDataType dt);
 
@@ -189,6 +193,9 @@ cudaError_t grouped_gemm(int dtype, const void* a, int64_t a_rows, const void* w
                          int num_sms, cudaStream_t stream, int force_bn);
 cudaError_t grouped_gemm_pair(int dtype, const void* a, int64_t a_rows, const void* w, const GemmArgs& args, bool relu,
                               int num_sms, cudaStream_t stream);
+// 16-bit weight [groups][n][k] -> the decode tile layout [groups][n/128][k/64][128][64].
+cudaError_t decode_tile_layout(const void* src, void* dst, int64_t groups, int n, int k, int num_sms,
+                               cudaStream_t stream);
 cudaError_t grouped_gemm_swap(int dtype, const void* a, int64_t a_rows, const void* w, const GemmArgs& args, bool relu,
                               int num_sms, cudaStream_t stream);
 // Backward grouped GEMMs (grouped_gemm_bwd.cu).

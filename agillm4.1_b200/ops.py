@@ -203,6 +203,18 @@ def moe_forward_residual(x: torch.Tensor, residual: torch.Tensor, w_router: torc
     return out
 
 
+def decode_tile_layout(w: torch.Tensor) -> torch.Tensor:
+    """[E, n, k] 16-bit weight stack -> the decode tile layout [E, n/128, k/64, 128, 64]
+    (agm_decode_tile_layout), for moe_forward(..., decode_tiles=True)."""
+    lib = load()
+    E, n, k = w.shape
+    out = torch.empty(E, n // 128, k // 64, 128, 64, dtype=w.dtype, device=w.device)
+    rc = lib.agm_decode_tile_layout(ptr(w.contiguous()), ptr(out), dtype_code(w.dtype), E, n, k,
+                                    stream_handle(w.device))
+    check(rc, "agm_decode_tile_layout")
+    return out
+
+
 def layernorm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float = 1e-5,
               out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """LayerNorm over the last dimension of x [N, d] (agm_layernorm)."""
@@ -250,7 +262,8 @@ def moe_forward(x: torch.Tensor, w_router: torch.Tensor, w1: torch.Tensor, b1: t
                 b2: torch.Tensor, top_k: int, *, shared: Optional[tuple] = None, out: Optional[torch.Tensor] = None,
                 want: tuple = (), tie_low_first: bool = False, workspace: Optional[torch.Tensor] = None,
                 check_errors: bool = False, stage_events=None, logits_in: Optional[torch.Tensor] = None,
-                pair: bool = True, swap: bool = True, pdl: bool = True, fold: bool = True):
+                pair: bool = True, swap: bool = True, pdl: bool = True, fold: bool = True,
+                decode_tiles: bool = False):
     """Fused forward: x [N, d] -> out [N, d]. ``want`` may hold 'idx', 'gates', 'counts', 'logits'.
 
     Weights: w_router [E, d]; w1 [E, H, d]; b1 [E, H]; w2 [E, d, H]; b2 [E, d];
@@ -266,6 +279,8 @@ def moe_forward(x: torch.Tensor, w_router: torch.Tensor, w1: torch.Tensor, b1: t
     waits for the previous kernel to complete before it launches). ``fold``:
     on CTA pairs, run the shared experts inside the routed FC1/FC2 launches
     (False: their own launches; the result is the same bit for bit).
+    ``decode_tiles``: w1 and w2 are in the decode tile layout
+    (:func:`decode_tile_layout`); decode-sized batches only.
     Returns out, or (out, extras dict) when ``want`` is not empty.
     """
     lib = load()
@@ -298,7 +313,8 @@ def moe_forward(x: torch.Tensor, w_router: torch.Tensor, w1: torch.Tensor, b1: t
         ptr(x), dtype_code(x.dtype), n, d, E, top_k, H, ptr(w_router), ptr(w1), ptr(b1), ptr(w2), ptr(b2), S,
         max(Hs, 1), ptr(ws1), ptr(sb1), ptr(ws2), ptr(sb2), ptr(out), ptr(workspace), workspace.numel(),
         _flags(tie_low_first) | (0 if pair else _lib.AGM_FLAG_NO_PAIR) | (0 if swap else _lib.AGM_FLAG_NO_SWAP)
-        | (0 if pdl else _lib.AGM_FLAG_NO_PDL) | (0 if fold else _lib.AGM_FLAG_NO_FOLD),
+        | (0 if pdl else _lib.AGM_FLAG_NO_PDL) | (0 if fold else _lib.AGM_FLAG_NO_FOLD)
+        | (_lib.AGM_FLAG_DECODE_TILES if decode_tiles else 0),
         ptr(extras.get("idx")), ptr(extras.get("gates")), ptr(extras.get("counts")),
         ptr(extras.get("logits")), ptr(logits_in), None if ev_arr is None else ctypes.addressof(ev_arr),
         stream_handle(dev))

@@ -1189,17 +1189,23 @@ def run_decode(args, dev, stream):
     lib = ops.load()
 
     keep = ops._lib.AGM_FLAG_KEEP_ERROR
+    # the same weights in the decode tile layout (each 128 x 64 tile one contiguous 16 KB block)
+    tiled = [(ops.decode_tile_layout(w1), ops.decode_tile_layout(w2)) for (_, w1, _, w2, _) in layers]
+    use_tiles = [False]
 
     def step():
         ws[:4].zero_()                   # one clear of the error word per decode step
         xs[0].copy_(x0)
+        flags = keep | (ops._lib.AGM_FLAG_DECODE_TILES if use_tiles[0] else 0)
         for layer, (wr, w1, b1, w2, b2) in enumerate(layers):
+            if use_tiles[0]:
+                w1, w2 = tiled[layer]
             # x_{l+1} = noise_l + MoE(x_l): the perturbation is added inside the combine kernel
             # (agm_moe_forward_residual; the same bits as a separate add)
             rc = lib.agm_moe_forward_residual(
                 ops.ptr(xs[layer]), ops.ptr(noise[layer]), ops.dtype_code(torch.bfloat16), B, D, E, k, HIDDEN,
                 ops.ptr(wr), ops.ptr(w1), ops.ptr(b1), ops.ptr(w2), ops.ptr(b2), 0, 1, None, None, None, None,
-                ops.ptr(xs[layer + 1]), ops.ptr(ws), ws.numel(), keep, torch.cuda.current_stream(dev).cuda_stream)
+                ops.ptr(xs[layer + 1]), ops.ptr(ws), ws.numel(), flags, torch.cuda.current_stream(dev).cuda_stream)
             ops.check(rc, "agm_moe_forward_residual")
 
     def counts_pass():
@@ -1236,7 +1242,7 @@ def run_decode(args, dev, stream):
     chk = torch.empty(B, D, dtype=torch.bfloat16, device=dev)
     counts_pass()
     torch.cuda.synchronize()
-    graph_ms = None
+    graph_ms = graph_tiles_ms = None
     try:
         side = torch.cuda.Stream(dev)
         side.wait_stream(torch.cuda.current_stream(dev))
@@ -1250,20 +1256,36 @@ def run_decode(args, dev, stream):
         if not torch.equal(xs[-1], ref_out):
             raise RuntimeError("graph replay output differs from the eager decode step")
         del graph
+        # the decode tile layout, captured the same way
+        use_tiles[0] = True
+        with torch.cuda.stream(side):
+            step()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph_t = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph_t):
+            step()
+        graph_tiles_ms = timed(graph_t.replay, steps)
+        if not torch.equal(xs[-1], ref_out):
+            raise RuntimeError("decode tile layout output differs from the nn.Linear layout")
+        del graph_t
+        use_tiles[0] = False
     except RuntimeError as exc:
         if "differs" in str(exc):
             raise
-        graph_ms = None
+        graph_ms = graph_tiles_ms = None
         print(f"decode: CUDA graph capture unavailable: {exc}", file=sys.stderr)
     active = sum(int((c > 0).sum()) for c in counts)
     expert_bytes = 2 * (2 * D * HIDDEN + HIDDEN + D)
     wbytes = active * expert_bytes
     peaks = load_peaks()
-    best = min(v for v in (eager_ms, graph_ms) if v is not None)
+    best = min(v for v in (eager_ms, graph_ms, graph_tiles_ms) if v is not None)
+    layout = "decode tiles" if best == graph_tiles_ms else "nn.Linear"
     gbs = wbytes / (best / 1000.0) / 1e9
     return {"workload": f"AR decode: {DECODE_LAYERS} MoE layers x {B} tokens, d{D} E{E} H{HIDDEN} top{k} bf16, "
                         f"seed {DECODE_SEED}",
             "ms_per_step_eager": round(eager_ms, 4), "ms_per_step_graph": None if graph_ms is None else round(graph_ms, 4),
+            "ms_per_step_graph_decode_tiles": None if graph_tiles_ms is None else round(graph_tiles_ms, 4),
+            "weight_layout_of_best": layout,
             "us_per_layer": round(1000 * best / DECODE_LAYERS, 2), "tokens_per_s": B / (best / 1000.0),
             "steps": steps, "active_experts": active, "weight_bytes_per_step": wbytes,
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm"], "unit": "GB/s",

@@ -82,6 +82,11 @@ enum {
                                       problems too small to fill the GPU with pair tiles */
 #define AGM_FLAG_NO_FOLD 0x40     /* agm_moe_forward: shared experts in their own GEMM launches
                                       (default: inside the routed FC1 / FC2 launches on CTA pairs) */
+#define AGM_FLAG_DECODE_TILES 0x80 /* agm_moe_forward: w1 and w2 are in the decode tile layout
+                                      [E][n/128][k/64][128][64] (agm_decode_tile_layout), each
+                                      128 x 64 weight tile one contiguous 16 KB block; only for
+                                      decode-sized batches (top_k * n_tokens <= 32 * n_experts,
+                                      16-bit dtypes, d and hidden multiples of 128) */
 
 AGM_API const char* agm_last_error(void);
 AGM_API int agm_abi_version(void);
@@ -481,6 +486,13 @@ AGM_API int agm_moe_aux_forward(const void* x, int dtype, int64_t n_tokens, int 
 AGM_API int agm_moe_aux_backward(const float* dloss, const void* x, int dtype, int64_t n_tokens, int d,
                                  int n_experts, const void* saved, size_t saved_bytes, void* dw_router,
                                  void* workspace, size_t workspace_bytes, int flags, void* stream);
+
+/* Decode tile layout of an expert weight stack for AGM_FLAG_DECODE_TILES:
+ * w [groups][n][k] (nn.Linear layout, 16-bit) -> out [groups][n/128][k/64]
+ * [128][64], every 128 x 64 tile one contiguous 16 KB block, so the
+ * decode-regime GEMM streams each weight tile from HBM as one run instead of
+ * 128 pieces of 128 bytes. n % 128 == 0, k % 64 == 0; out has w's size. */
+AGM_API int agm_decode_tile_layout(const void* w, void* out, int dtype, int64_t groups, int n, int k, void* stream);
 
 /* Synchronise `stream`, read the device error word at `err` (e.g. the first
  * int of a forward workspace) into *code and reset it to 0. Returns AGM_OK if

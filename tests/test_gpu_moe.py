@@ -335,6 +335,37 @@ def test_shared_experts_folded_into_routed_launches(E, k, H, S, n):
     assert torch.equal(out_r, out_f + res)
 
 
+@pytest.mark.parametrize("n,k,E,S", [(64, 2, 14, 0), (200, 2, 14, 0), (37, 1, 4, 0), (64, 1, 2, 1)])
+def test_decode_tile_layout_forward(n, k, E, S):
+    """Decode-regime forward with w1/w2 in the decode tile layout
+    (AGM_FLAG_DECODE_TILES): each 128 x 64 weight tile is one contiguous 16 KB
+    block, loaded by a 5-D TMA box into the same shared-memory image, so the
+    result equals the nn.Linear-layout forward bit for bit (shared experts,
+    when present, keep their own layout)."""
+    d, H = 1280, 3200 if E != 2 else 5120
+    sd = synthetic.make_state(d, H, E, 95 + n, dtype=torch.bfloat16, device=DEV, bias_std=0.02, shared=S,
+                              shared_hidden=2 * d if S else None)
+    w1, b1, w2, b2, sh = packed(sd, E, DEV)
+    wr = sd["router.weight"].contiguous()
+    t1, t2 = ops.decode_tile_layout(w1), ops.decode_tile_layout(w2)
+    assert torch.equal(t1, w1.view(E, H // 128, 128, d // 64, 64).permute(0, 1, 3, 2, 4))
+    assert torch.equal(t2, w2.view(E, d // 128, 128, H // 64, 64).permute(0, 1, 3, 2, 4))
+    x = synthetic.make_input(n, d, 96 + n, dtype=torch.bfloat16, device=DEV)
+    ref = ops.moe_forward(x, wr, w1, b1, w2, b2, k, shared=sh, check_errors=True)
+    out = ops.moe_forward(x, wr, t1, b1, t2, b2, k, shared=sh, check_errors=True, decode_tiles=True)
+    assert torch.equal(out, ref)
+
+
+def test_decode_tile_layout_refused_outside_decode():
+    d, H, E, k, n = 1280, 3200, 14, 2, 4096
+    sd = synthetic.make_state(d, H, E, 97, dtype=torch.bfloat16, device=DEV)
+    w1, b1, w2, b2, _ = packed(sd, E, DEV)
+    x = synthetic.make_input(n, d, 98, dtype=torch.bfloat16, device=DEV)
+    with pytest.raises(agillm41_b200.MoEKernelError):
+        ops.moe_forward(x, sd["router.weight"].contiguous(), ops.decode_tile_layout(w1), b1,
+                        ops.decode_tile_layout(w2), b2, k, decode_tiles=True)
+
+
 @pytest.mark.parametrize("n,k,E", [(64, 2, 14), (200, 2, 14), (37, 1, 4), (96, 3, 16)])
 def test_swap_gemm_forward_matches_row_tiles(n, k, E):
     """Decode-sized batches run the expert GEMMs with swapped operands (weights
