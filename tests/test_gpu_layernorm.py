@@ -1,10 +1,11 @@
 """LayerNorm at the Block boundary (agm_layernorm) and the Block's FFN half
 in one call (agm_moe_block_forward: x + MoEFFN(LayerNorm(x)), agillm41.py:4547).
 
-The LayerNorm is compared with torch's F.layer_norm on the same GPU: fp32
-within 1e-5 (relative + absolute); 16-bit outputs within one unit in the last
-place of the dtype, and at most 1e-3 of the elements differing at all (the
-statistics are reduced in another order than torch's). The FFN half equals
+The LayerNorm is compared with the float64 LayerNorm of the same 16-bit
+inputs: every output within one unit in the last place of the dtype and at
+most 1e-3 of them not the correctly rounded value; with torch's F.layer_norm
+on the same GPU, at most 1e-2 of the elements differ (fp32: within 1e-5,
+relative + absolute). The FFN half equals
 the separate LayerNorm + agm_moe_forward_residual bit for bit, and against
 the reference formula with torch's LayerNorm it is within the bf16 parity
 tolerance on every row whose routing matches; rows routed differently must
@@ -49,9 +50,17 @@ def test_layernorm_matches_torch(dtype, d, n):
     if dtype == torch.float32:
         torch.testing.assert_close(ours, ref, rtol=1e-5, atol=1e-5)
         return
-    diff = (ours.float() - ref.float()).abs()
-    assert bool((diff <= _ulp(ref, dtype) * 1.001).all()), float(diff.max())
-    assert float((diff > 0).float().mean()) <= 1e-3
+    # the LayerNorm of the same 16-bit values in float64, rounded once to the dtype
+    xd = x.double()
+    mean = xd.mean(dim=-1, keepdim=True)
+    var = ((xd - mean) ** 2).mean(dim=-1, keepdim=True)
+    exact64 = (xd - mean) / torch.sqrt(var + 1e-5) * w.double() + b.double()
+    exact = exact64.to(dtype)
+    d_ours = (ours.double() - exact64).abs()
+    assert bool((d_ours <= _ulp(exact64, dtype).double() * 1.001).all()), float(d_ours.max())
+    assert float((ours != exact).float().mean()) <= 1e-3          # correctly rounded almost everywhere
+    # agreement with torch's kernel (which reduces in another order)
+    assert float((ours != ref).float().mean()) <= 1e-2
 
 
 def test_layernorm_rejects_unsupported_width():
