@@ -2,8 +2,9 @@
 in one call (agm_moe_block_forward: x + MoEFFN(LayerNorm(x)), agillm41.py:4547).
 
 The LayerNorm is compared with the float64 LayerNorm of the same 16-bit
-inputs: every output within one unit in the last place of the dtype and at
-most 1e-3 of them not the correctly rounded value; with torch's F.layer_norm
+inputs: every output within one unit in the last place of the dtype (plus
+fp32 rounding of the terms where the normalised value and the bias nearly
+cancel) and at most 1e-3 of them not the correctly rounded value; with torch's F.layer_norm
 on the same GPU, at most 1e-2 of the elements differ (fp32: within 1e-5,
 relative + absolute). The FFN half equals
 the separate LayerNorm + agm_moe_forward_residual bit for bit, and against
@@ -54,10 +55,14 @@ def test_layernorm_matches_torch(dtype, d, n):
     xd = x.double()
     mean = xd.mean(dim=-1, keepdim=True)
     var = ((xd - mean) ** 2).mean(dim=-1, keepdim=True)
-    exact64 = (xd - mean) / torch.sqrt(var + 1e-5) * w.double() + b.double()
+    scaled = (xd - mean) / torch.sqrt(var + 1e-5) * w.double()
+    exact64 = scaled + b.double()
     exact = exact64.to(dtype)
     d_ours = (ours.double() - exact64).abs()
-    assert bool((d_ours <= _ulp(exact64, dtype).double() * 1.001).all()), float(d_ours.max())
+    # one unit in the last place of the result, plus fp32 rounding of the terms where
+    # the normalised value and the bias nearly cancel
+    bound = _ulp(exact64, dtype).double() * 1.001 + 1e-6 * (scaled.abs() + b.double().abs())
+    assert bool((d_ours <= bound).all()), float((d_ours - bound).max())
     assert float((ours != exact).float().mean()) <= 1e-3          # correctly rounded almost everywhere
     # agreement with torch's kernel (which reduces in another order)
     assert float((ours != ref).float().mean()) <= 1e-2
