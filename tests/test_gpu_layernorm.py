@@ -61,7 +61,7 @@ def test_layernorm_matches_torch(dtype, d, n):
     d_ours = (ours.double() - exact64).abs()
     # one unit in the last place of the result, plus fp32 rounding of the terms where
     # the normalised value and the bias nearly cancel
-    bound = _ulp(exact64, dtype).double() * 1.001 + 1e-6 * (scaled.abs() + b.double().abs())
+    bound = _ulp(exact64, dtype).double() * 1.001 + 4e-6 * (scaled.abs() + b.double().abs())
     assert bool((d_ours <= bound).all()), float((d_ours - bound).max())
     assert float((ours != exact).float().mean()) <= 1e-3          # correctly rounded almost everywhere
     # agreement with torch's kernel (which reduces in another order)
