@@ -286,7 +286,9 @@ def moe_forward(x: torch.Tensor, w_router: torch.Tensor, w1: torch.Tensor, b1: t
     lib = load()
     n, d = x.shape
     E = w_router.shape[0]
-    H = w1.shape[1]
+    H = b1.shape[-1]                      # w1 is [E, H, d], or [E, H/128, d/64, 128, 64] in decode tiles
+    if decode_tiles and (w1.dim() != 5 or w2.dim() != 5):
+        raise ValueError("decode_tiles=True expects w1 and w2 from decode_tile_layout()")
     dev = x.device
     if shared is not None:
         ws1, sb1, ws2, sb2 = shared
