@@ -8,13 +8,17 @@
 // LayerNorm into the workspace, then agm_moe_forward with the residual added
 // in its combine.
 //
-// Kernel: one warp per row, persistent over rows. A lane holds the row's
-// elements 8 * (lane + 32 j) .. + 7 (j < VPL, 16-byte vectors) in registers,
-// and the same columns of the affine weight and bias (packed) for every row
-// it visits. Statistics in fp32: mean = sum(x) / d, then the variance as the
-// mean of squared deviations from it (two passes over the registers, no
-// cancellation), rstd = rsqrt(var + eps). Output y = (x - mean) * rstd *
-// weight + bias, rounded once to the input dtype. torch's kernel uses a
+// Kernel: one warp per row, persistent CTAs walking the rows. A lane holds
+// the row's 16-byte vectors lane + 32 j (j < VPL) packed in registers, in
+// one of two buffers used in turn, so each warp keeps two rows in flight.
+// The affine weight and bias sit in shared memory as fp32 float4 planes,
+// staged once per CTA, so their reads are conflict-free 16-byte loads (with
+// scalar loads at the lanes' 32-byte stride, an 8-way bank conflict made the
+// kernel latency-bound at half of HBM bandwidth). Statistics in fp32:
+// mean = sum(x) / d, then the variance as the mean of squared deviations
+// from it (two passes over the registers, no cancellation),
+// rstd = rsqrt(var + eps). Output y = (x - mean) * rstd * weight + bias,
+// rounded once to the input dtype. torch's kernel uses a
 // Welford reduction in a different order, so its mean and rstd can differ
 // in the last fp32 bit and a normalised value by one unit in the last place
 // of the output dtype.
@@ -68,72 +72,125 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// Row x of one warp, packed: lane holds the 16-byte vectors lane + 32 j.
+template <typename T, int VPL>
+__device__ __forceinline__ void ln_load_row(const T* __restrict__ x, int64_t row, int d, int lane, uint4 (&r)[VPL]) {
+  const uint4* xr = reinterpret_cast<const uint4*>(x + row * d);
+  const int nvec = d / LnVec<T>::kElems;
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const int v = lane + 32 * j;
+    r[j] = v < nvec ? __ldcs(xr + v) : make_uint4(0, 0, 0, 0);
+  }
+}
+
+// Statistics and output of one row held packed in registers. The affine
+// parameters are float4 planes in shared memory: plane h holds elements
+// 4h .. 4h+3 of every 16-byte vector, so vector v's weights are
+// w_s[h * nvec + v] (h < EV / 4) and a warp's 16-byte reads of one plane are
+// contiguous (no bank conflicts).
+template <typename T, int VPL>
+__device__ __forceinline__ void ln_row(const uint4 (&r)[VPL], const float4* __restrict__ w_s,
+                                       const float4* __restrict__ b_s, float eps, float inv_d, int d, int lane,
+                                       uint4* __restrict__ orow) {
+  constexpr int EV = LnVec<T>::kElems;
+  const int nvec = d / EV;
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    if (lane + 32 * j < nvec) {
+      float f[EV];
+      ln_unpack<T>(r[j], f);
+#pragma unroll
+      for (int e = 0; e < EV; ++e) s += f[e];
+    }
+  }
+  const float mean = warp_sum(s) * inv_d;
+  float q = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    if (lane + 32 * j < nvec) {
+      float f[EV];
+      ln_unpack<T>(r[j], f);
+#pragma unroll
+      for (int e = 0; e < EV; ++e) {
+        const float dv = f[e] - mean;
+        q += dv * dv;
+      }
+    }
+  }
+  const float rstd = rsqrtf(warp_sum(q) * inv_d + eps);
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const int v = lane + 32 * j;
+    if (v < nvec) {
+      float f[EV], y[EV], wv[EV], bv[EV];
+      ln_unpack<T>(r[j], f);
+#pragma unroll
+      for (int h = 0; h < EV / 4; ++h) {
+        const float4 w4 = w_s[h * nvec + v];
+        const float4 b4 = b_s[h * nvec + v];
+        wv[4 * h] = w4.x, wv[4 * h + 1] = w4.y, wv[4 * h + 2] = w4.z, wv[4 * h + 3] = w4.w;
+        bv[4 * h] = b4.x, bv[4 * h + 1] = b4.y, bv[4 * h + 2] = b4.z, bv[4 * h + 3] = b4.w;
+      }
+#pragma unroll
+      for (int e = 0; e < EV; ++e) y[e] = (f[e] - mean) * rstd * wv[e] + bv[e];
+      orow[v] = ln_pack<T>(y);
+    }
+  }
+}
+
 template <typename T, int VPL>
 __global__ void __launch_bounds__(32 * kLnWarps) layernorm_kernel(const T* __restrict__ x, const T* __restrict__ w,
                                                                    const T* __restrict__ b, float eps, int64_t n,
                                                                    int d, T* __restrict__ out) {
-  constexpr int EV = LnVec<T>::kElems;  // elements per 16-byte vector
+  constexpr int EV = LnVec<T>::kElems;
+  extern __shared__ float4 ln_smem[];
+  const int nvec = d / EV;
+  float4* w_s = ln_smem;         // [EV / 4][nvec] the affine weight in fp32, in float4 planes
+  float4* b_s = ln_smem + d / 4; // the bias, same layout
   const int lane = lane_id();
-  const int nvec = d / EV;              // vectors per row
   pdl_wait();
   pdl_trigger();
-  uint4 wp[VPL], bp[VPL];  // this lane's columns of the affine parameters, packed
-#pragma unroll
-  for (int j = 0; j < VPL; ++j) {
-    const int v = lane + 32 * j;
-    wp[j] = v < nvec ? __ldg(reinterpret_cast<const uint4*>(w) + v) : make_uint4(0, 0, 0, 0);
-    bp[j] = v < nvec ? __ldg(reinterpret_cast<const uint4*>(b) + v) : make_uint4(0, 0, 0, 0);
+  for (int i = threadIdx.x; i < d; i += blockDim.x) {
+    const int v = i / EV, h = (i % EV) / 4, c = i % 4;
+    reinterpret_cast<float*>(w_s + h * nvec + v)[c] = Traits<T>::to_f(w[i]);
+    reinterpret_cast<float*>(b_s + h * nvec + v)[c] = Traits<T>::to_f(b[i]);
   }
+  __syncthreads();
   const float inv_d = 1.0f / static_cast<float>(d);
-  const int64_t warps = static_cast<int64_t>(gridDim.x) * kLnWarps;
-  for (int64_t row = static_cast<int64_t>(blockIdx.x) * kLnWarps + warp_id(); row < n; row += warps) {
-    const uint4* xr = reinterpret_cast<const uint4*>(x + row * d);
-    float xv[VPL][EV];
-    float s = 0.f;
-#pragma unroll
-    for (int j = 0; j < VPL; ++j) {
-      const int v = lane + 32 * j;
-      if (v < nvec) {
-        ln_unpack<T>(__ldcs(xr + v), xv[j]);
-#pragma unroll
-        for (int e = 0; e < EV; ++e) s += xv[j][e];
-      }
-    }
-    const float mean = warp_sum(s) * inv_d;
-    float q = 0.f;
-#pragma unroll
-    for (int j = 0; j < VPL; ++j) {
-      if (lane + 32 * j < nvec) {
-#pragma unroll
-        for (int e = 0; e < EV; ++e) {
-          const float dv = xv[j][e] - mean;
-          q += dv * dv;
-        }
-      }
-    }
-    const float rstd = rsqrtf(warp_sum(q) * inv_d + eps);
-    uint4* orow = reinterpret_cast<uint4*>(out + row * d);
-#pragma unroll
-    for (int j = 0; j < VPL; ++j) {
-      const int v = lane + 32 * j;
-      if (v < nvec) {
-        float y[EV], wv[EV], bv[EV];
-        ln_unpack<T>(wp[j], wv);
-        ln_unpack<T>(bp[j], bv);
-#pragma unroll
-        for (int e = 0; e < EV; ++e) y[e] = (xv[j][e] - mean) * rstd * wv[e] + bv[e];
-        orow[v] = ln_pack<T>(y);
-      }
-    }
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kLnWarps;
+  int64_t row = static_cast<int64_t>(blockIdx.x) * kLnWarps + warp_id();
+  // Two rows in flight per warp, in two register buffers used in turn: a
+  // buffer is refilled (the row two strides on) as soon as its row is
+  // written, so while the warp waits for one row the other is outstanding
+  // too. (A copy from a prefetch buffer would wait for that buffer's loads
+  // with nothing else outstanding.)
+  uint4 ra[VPL], rb[VPL];
+  if (row < n) ln_load_row<T, VPL>(x, row, d, lane, ra);
+  if (row + stride < n) ln_load_row<T, VPL>(x, row + stride, d, lane, rb);
+  for (; row < n; row += 2 * stride) {
+    ln_row<T, VPL>(ra, w_s, b_s, eps, inv_d, d, lane, reinterpret_cast<uint4*>(out + row * d));
+    if (row + 2 * stride < n) ln_load_row<T, VPL>(x, row + 2 * stride, d, lane, ra);
+    if (row + stride >= n) break;
+    ln_row<T, VPL>(rb, w_s, b_s, eps, inv_d, d, lane, reinterpret_cast<uint4*>(out + (row + stride) * d));
+    if (row + 3 * stride < n) ln_load_row<T, VPL>(x, row + 3 * stride, d, lane, rb);
   }
 }
 
 template <typename T, int VPL>
 cudaError_t launch_ln_vpl(const void* x, const void* w, const void* b, float eps, int64_t n, int d, void* out,
                           int num_sms, cudaStream_t stream) {
+  const size_t smem = 2 * static_cast<size_t>(d) * sizeof(float);
+  int per_sm = 0;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, layernorm_kernel<T, VPL>, 32 * kLnWarps,
+                                                                smem);
+  if (e != cudaSuccess) return e;
+  // persistent: every resident CTA walks rows; no more CTAs than rows need
   const int64_t blocks_needed = (n + kLnWarps - 1) / kLnWarps;
-  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(blocks_needed, 8LL * num_sms)));
-  return launch_kernel(layernorm_kernel<T, VPL>, dim3(grid), dim3(32 * kLnWarps), 0, stream,
+  const int grid = static_cast<int>(
+      std::max<int64_t>(1, std::min<int64_t>(blocks_needed, static_cast<int64_t>(std::max(per_sm, 1)) * num_sms)));
+  return launch_kernel(layernorm_kernel<T, VPL>, dim3(grid), dim3(32 * kLnWarps), smem, stream,
                        static_cast<const T*>(x), static_cast<const T*>(w), static_cast<const T*>(b), eps, n, d,
                        static_cast<T*>(out));
 }
