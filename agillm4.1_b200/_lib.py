@@ -32,6 +32,7 @@ AGM_EP_HOLDERS, AGM_EP_BALANCED, AGM_EP_LOCAL = 0, 1, 2
 AGM_FLAG_BWD_PAIR = 0x20
 AGM_FLAG_NO_FOLD = 0x40
 AGM_FLAG_DECODE_TILES = 0x80
+AGM_FLAG_NO_FRONT = 0x100
 AGM_CODEC_PLAIN, AGM_CODEC_INT8, AGM_CODEC_INT8_ROWWISE = 0, 1, 2
 AGM_APPLY_COPY, AGM_APPLY_LERP, AGM_APPLY_ADD = 0, 1, 2
 

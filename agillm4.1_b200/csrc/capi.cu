@@ -16,6 +16,7 @@ namespace {
 
 thread_local std::string g_err;
 
+
 int fail(int code, const std::string& msg) {
   g_err = msg;
   return code;
@@ -359,20 +360,37 @@ int moe_forward_impl(const void* x, int dtype, int64_t n_tokens, int d, int n_ex
   const int gemm_mode = pair ? AGM_GEMM_PAIR : (swap ? -2 : 0);
 
   if ((e = mark(0)) != cudaSuccess) return cuda_fail(e, "event record");
-  e = agm::router_topk(dtype, x, w_router, n_tokens, d, n_experts, top_k, flags & AGM_FLAG_TIE_LOW_FIRST,
-                       logits_in, logits_out, idx, gates, L.block_hist, L.err, sms, stream);
-  if (e != cudaSuccess) return cuda_fail(e, "router_topk");
-  if ((e = mark(1)) != cudaSuccess) return cuda_fail(e, "event record");
-  e = agm::dispatch_plan(L.block_hist, static_cast<int>(agm_dispatch_blocks(n_tokens)), n_experts, rows,
-                         static_cast<int>(max_tiles), seg_align, L.block_off, L.counts, L.seg_start, L.tile_expert,
-                         L.num_tiles, L.token_of, L.err, stream);
-  if (e != cudaSuccess) return cuda_fail(e, "dispatch_plan");
-  if ((e = mark(2)) != cudaSuccess) return cuda_fail(e, "event record");
-  e = agm::permute_rows(x, eb, n_tokens, d, top_k, n_experts, idx, L.block_off, L.seg_start, L.counts, rows,
-                        L.x_perm, L.row_of, L.token_of, L.err, stream);
-  if (e != cudaSuccess) return cuda_fail(e, "permute");
-  if ((e = mark(3)) != cudaSuccess) return cuda_fail(e, "event record");
-
+  // The swapped-operand GEMMs read no padding row of x_perm into a written
+  // output: its zero-fill (E x up to 127 rows) is skipped.
+  const bool zero_pad = gemm_mode != -2;
+  // At most one dispatch block (decode): router, plan and permute in one
+  // cluster launch, with the same outputs.
+  const bool front = !(flags & AGM_FLAG_NO_FRONT) && !logits_in &&
+                     agm::decode_front_supported(dtype, n_tokens, d, n_experts, top_k);
+  if (front) {
+    agm::FrontOut fo{L.block_hist, L.block_off,  L.counts, L.seg_start,          L.tile_expert,
+                     L.num_tiles,  L.token_of,   L.row_of, L.x_perm,             rows,
+                     static_cast<int>(max_tiles), seg_align, zero_pad ? 1 : 0};
+    e = agm::decode_front(dtype, x, w_router, n_tokens, d, n_experts, top_k, flags & AGM_FLAG_TIE_LOW_FIRST,
+                          logits_out, idx, gates, fo, L.err, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "decode_front");
+    for (int i = 1; i <= 3 && e == cudaSuccess; ++i) e = mark(i);
+    if (e != cudaSuccess) return cuda_fail(e, "event record");
+  } else {
+    e = agm::router_topk(dtype, x, w_router, n_tokens, d, n_experts, top_k, flags & AGM_FLAG_TIE_LOW_FIRST,
+                         logits_in, logits_out, idx, gates, L.block_hist, L.err, sms, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "router_topk");
+    if ((e = mark(1)) != cudaSuccess) return cuda_fail(e, "event record");
+    e = agm::dispatch_plan(L.block_hist, static_cast<int>(agm_dispatch_blocks(n_tokens)), n_experts, rows,
+                           static_cast<int>(max_tiles), seg_align, L.block_off, L.counts, L.seg_start, L.tile_expert,
+                           L.num_tiles, L.token_of, L.err, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "dispatch_plan");
+    if ((e = mark(2)) != cudaSuccess) return cuda_fail(e, "event record");
+    e = agm::permute_rows(x, eb, n_tokens, d, top_k, n_experts, idx, L.block_off, L.seg_start, L.counts, rows,
+                          L.x_perm, L.row_of, L.token_of, L.err, stream, zero_pad);
+    if (e != cudaSuccess) return cuda_fail(e, "permute");
+    if ((e = mark(3)) != cudaSuccess) return cuda_fail(e, "event record");
+  }
   agm::GemmArgs g1;
   g1.c = L.h;
   g1.ldc = hidden;
@@ -389,8 +407,10 @@ int moe_forward_impl(const void* x, int dtype, int64_t n_tokens, int d, int n_ex
   g1.seg_count = L.counts;
   // The tile table and counts come from the plan, two or more launches back,
   // and the weights from before this forward: the GEMMs stream their first
-  // weight tiles while the kernel before them finishes.
-  g1.early_weights = true;
+  // weight tiles while the kernel before them finishes. Behind the decode
+  // front the tables come from the kernel just before, so the GEMMs wait for
+  // it before reading anything.
+  g1.early_weights = !front;
   g1.w_tiled = tiled;
   const int64_t npad = round_up(n_tokens, AGM_TILE_M);
   // Shared experts: one dense group over all tokens, so any two row tiles
@@ -420,6 +440,7 @@ int moe_forward_impl(const void* x, int dtype, int64_t n_tokens, int d, int n_ex
   if (e != cudaSuccess) return cuda_fail(e, "grouped_gemm fc1");
   if ((e = mark(4)) != cudaSuccess) return cuda_fail(e, "event record");
   agm::GemmArgs g2 = g1;
+  g2.early_weights = true;  // the tables are two launches back here in both cases
   g2.c = L.x_perm;  // y reuses the x_perm buffer
   g2.ldc = d;
   g2.bias = b2;

@@ -11,7 +11,8 @@
 //   expert GEMMs run on CTA pairs); the row-tile -> expert table
 //   and the number of row tiles (read by the persistent GEMM on the device).
 // * permute_kernel (one CTA per dispatch block of 128 tokens, plus 8 CTAs per
-//   expert that zero-fill the segment's padding rows): warp ballots give each
+//   expert that zero-fill the segment's padding rows, except for the
+//   swapped-operand GEMMs, which never use them): warp ballots give each
 //   (token, rank) its rank among the block's tokens routed to the same expert,
 //   in ascending token order, so the permutation is deterministic and equals
 //   the reference's ascending `nonzero` order. Rows of x are copied with
@@ -265,13 +266,13 @@ template <class Dst>
 static cudaError_t launch_permute(const void* x, int elem_bytes, int64_t n_tokens, int d, int k, int E,
                                   const int32_t* idx, const int32_t* block_off, const int32_t* seg_start,
                                   const int32_t* counts, int64_t max_rows, Dst dst, int32_t* row_of,
-                                  int32_t* token_of, int* err, cudaStream_t stream) {
+                                  int32_t* token_of, int* err, cudaStream_t stream, bool zero_pad = true) {
   const int n_blocks = static_cast<int>((n_tokens + kBlk - 1) / kBlk);
   const int nchunk = d * elem_bytes / 16;
   // Small batches: up to 16 CTAs per dispatch block, so the row copies of a
   // few hundred tokens are not serialised in one or two warps.
   const int split = n_blocks >= 64 ? 1 : std::min(16, 64 / n_blocks);
-  const unsigned grid = static_cast<unsigned>(n_blocks * split + E * kZeroCtas);
+  const unsigned grid = static_cast<unsigned>(n_blocks * split + (zero_pad ? E * kZeroCtas : 0));
   if (n_tokens <= 0) return cudaSuccess;
   const uint4* xs = static_cast<const uint4*>(x);
   if (k <= 2)
@@ -286,10 +287,11 @@ static cudaError_t launch_permute(const void* x, int elem_bytes, int64_t n_token
 
 cudaError_t permute_rows(const void* x, int elem_bytes, int64_t n_tokens, int d, int k, int E, const int32_t* idx,
                          const int32_t* block_off, const int32_t* seg_start, const int32_t* counts, int64_t max_rows,
-                         void* x_perm, int32_t* row_of, int32_t* token_of, int* err, cudaStream_t stream) {
+                         void* x_perm, int32_t* row_of, int32_t* token_of, int* err, cudaStream_t stream,
+                         bool zero_pad) {
   LocalRows dst{static_cast<uint4*>(x_perm), d * elem_bytes / 16};
   return launch_permute(x, elem_bytes, n_tokens, d, k, E, idx, block_off, seg_start, counts, max_rows, dst, row_of,
-                        token_of, err, stream);
+                        token_of, err, stream, zero_pad);
 }
 
 cudaError_t permute_rows_ep(const void* x, int elem_bytes, int64_t n_tokens, int d, int k, int E, const int32_t* idx,

@@ -91,13 +91,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_s = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id(), lane = lane_id();
+  __shared__ Units u;
+  const int num_fb = (args.n + kFM - 1) / kFM;
+  const int num_kb = (args.k + kBK - 1) / kBK;
   if (!args.early_weights) {
     pdl_wait();
     pdl_trigger();
   }
-  __shared__ Units u;
-  const int num_fb = (args.n + kFM - 1) / kFM;
-  const int num_kb = (args.k + kBK - 1) / kBK;
 
   if (threadIdx.x == 0) {
     load_units(args, u);

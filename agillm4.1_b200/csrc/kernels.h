@@ -41,6 +41,27 @@ inline cudaError_t launch_kernel(void (*kernel)(Exp...), dim3 grid, dim3 block, 
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Act>(args)...);
 }
 
+// launch_kernel with a cluster of `cluster` CTAs along x (grid a multiple of it).
+template <typename... Exp, typename... Act>
+inline cudaError_t launch_cluster_kernel(void (*kernel)(Exp...), dim3 grid, dim3 block, int cluster, size_t smem,
+                                         cudaStream_t stream, Act&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = cluster;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Act>(args)...);
+}
+
 // Arguments of the grouped GEMM  c[r, :] = act(a[r, :] @ w[g]^T + bias[g]).
 struct GemmArgs {
   void* c;
@@ -172,6 +193,29 @@ cudaError_t ensure_dynamic_smem(const void* func, int bytes);
 cudaError_t router_topk(int dtype, const void* x, const void* w, int64_t n_tokens, int d, int E, int k,
                         int tie_low_first, const float* logits_in, float* logits_out, int32_t* idx, void* gates,
                         int32_t* block_hist, int* err, int num_sms, cudaStream_t stream);
+// Decode front (router_topk.cu): router, dispatch plan and permute of at most
+// one 128-token dispatch block in one launch (a cluster of 8 CTAs), with the
+// outputs of router_topk + dispatch_plan + permute_rows; the logits are fp32
+// dot products (CUDA cores) rounded once to the dtype.
+struct FrontOut {
+  int32_t* block_hist;
+  int32_t* block_off;
+  int32_t* counts;
+  int32_t* seg_start;
+  int32_t* tile_expert;
+  int32_t* num_tiles;
+  int32_t* token_of;
+  int32_t* row_of;
+  void* x_perm;
+  int64_t max_rows;
+  int max_tiles;
+  int seg_align;
+  int zero_pad;
+};
+bool decode_front_supported(int dtype, int64_t n_tokens, int d, int E, int k);
+cudaError_t decode_front(int dtype, const void* x, const void* w, int64_t n_tokens, int d, int E, int k,
+                         int tie_low_first, float* logits_out, int32_t* idx, void* gates, const FrontOut& o, int* err,
+                         cudaStream_t stream);
 // Shared memory of the SIMT router (fp32, or caller-supplied logits).
 size_t router_smem_bytes(int d, int E);
 // Whether the tensor-core router (bf16/fp16) handles this d.
@@ -181,9 +225,13 @@ bool router_tc_supported(int d);
 cudaError_t dispatch_plan(const int32_t* block_hist, int n_blocks, int E, int64_t max_rows, int max_tiles,
                           int seg_align, int32_t* block_off, int32_t* counts, int32_t* seg_start,
                           int32_t* tile_expert, int32_t* num_tiles, int32_t* token_of, int* err, cudaStream_t stream);
+// zero_pad: zero-fill each segment's padding rows of x_perm (false only where
+// nothing reads them: the swapped-operand GEMMs, whose output columns of a
+// padding row are computed from that row alone and never written).
 cudaError_t permute_rows(const void* x, int elem_bytes, int64_t n_tokens, int d, int k, int E, const int32_t* idx,
                          const int32_t* block_off, const int32_t* seg_start, const int32_t* counts, int64_t max_rows,
-                         void* x_perm, int32_t* row_of, int32_t* token_of, int* err, cudaStream_t stream);
+                         void* x_perm, int32_t* row_of, int32_t* token_of, int* err, cudaStream_t stream,
+                         bool zero_pad = true);
 cudaError_t permute_rows_ep(const void* x, int elem_bytes, int64_t n_tokens, int d, int k, int E, const int32_t* idx,
                             const int32_t* block_off, const int32_t* seg_start, const int32_t* counts,
                             int64_t max_rows, const EpRoute* route, int32_t* row_of, int* err, cudaStream_t stream);

@@ -656,6 +656,363 @@ cudaError_t router_topk(int dtype, const void* x, const void* w, int64_t n_token
   }
 }
 
+// ---------------------------------------------------------------------------
+// Decode front: router + dispatch plan + permute of one dispatch block
+// ---------------------------------------------------------------------------
+// At decode batch sizes (<= 128 tokens, one dispatch block) the three kernels
+// above cost about 19 us per layer in a CUDA graph, mostly latency: the
+// tensor-core router is one CTA whose 20 x tiles pass through one SM, then
+// two more launches follow. Here one cluster of 8 CTAs does all three: CTA r
+// takes tokens [16 r, 16 r + 16), two per warp, with its token rows and the
+// router weight (fp32) staged in shared memory; the logits are fp32 FMAs over
+// the lane's 16-byte chunks lane + 32 j then
+// a transpose-reduce across lanes (the SIMT router's order), rounded once to
+// the dtype; warp 0 selects top-k for the CTA's 16
+// tokens (select_route, as in the other routers) and ballots per-expert
+// token masks. After a cluster barrier every CTA reads the 8 CTAs' per-expert
+// counts through distributed shared memory: the totals give the block
+// histogram, counts and padded segment starts (as dispatch_plan_kernel
+// computes them for one block), the counts of lower-ranked CTAs give each
+// token's rank within its expert (ascending token order, as permute_kernel),
+// and each warp copies its two tokens' rows to their destination rows. Code is kept loop-based (not unrolled over chunks): a
+// launch runs it once, and cold instruction-cache misses were its largest
+// stall. A last cluster barrier keeps every CTA's shared memory
+// alive until the others have read it.
+constexpr int kFrontCtas = 8;
+constexpr int kFrontWarps = 8;
+constexpr int kFrontTokCta = kDispatchBlock / kFrontCtas;  // 16
+constexpr int kFrontTokWarp = kFrontTokCta / kFrontWarps;  // 2
+constexpr int kFrontChunks = 8;  // d <= 32 x 8 chunks = 2048: 16 rows x 2d + E x 4d bytes of shared memory
+
+template <typename T, int KC>
+__global__ void __launch_bounds__(32 * kFrontWarps) decode_front_kernel(
+    const T* __restrict__ x, const T* __restrict__ w, int n_tokens, int d, int E, int k, int tie_low_first,
+    float* __restrict__ logits_out, int32_t* __restrict__ idx_out, T* __restrict__ gates_out, FrontOut o, int* err) {
+  constexpr int S = RouteK<KC>::S;
+  if (KC > 0) k = KC;
+  __shared__ float logit_s[kFrontTokCta][kMaxExperts];
+  __shared__ int cnt_s[kMaxExperts];          // this CTA's tokens per expert (read by the whole cluster)
+  __shared__ uint32_t mask_s[kMaxExperts];    // bit t: local token t picked expert e
+  __shared__ uint32_t pm_s[kFrontWarps][kMaxExperts];  // the same, per warp (bits 0-1: its two tokens)
+  __shared__ int tot_s[kMaxExperts], pre_s[kMaxExperts], seg_s[kMaxExperts + 1];
+  const int warp = warp_id(), lane = lane_id();
+  const int rank = static_cast<int>(cluster_ctarank());
+  const int nchunk = d / 8;  // 16-byte chunks per row (16-bit dtypes)
+  pdl_wait();
+  pdl_trigger();
+
+  // 1. Logits of this warp's two tokens. The CTA stages its 16 token rows
+  // (packed, as loaded) and the router weight (fp32, in two float4 planes:
+  // plane h holds elements 4h..4h+3 of every 16-byte chunk,
+  // w_s[h][e * nchunk + c]) in shared memory, every load in flight at once;
+  // the FMA loop then reads both with conflict-free 16-byte loads. Loops over
+  // chunks are not unrolled: the kernel runs once per launch, so its code has
+  // to stay small enough not to wait on instruction-cache misses.
+  extern __shared__ float4 front_smem[];
+  const int wchunks = E * nchunk;
+  float4* w_s = front_smem;                                          // [2][E * nchunk]
+  uint4* x_s = reinterpret_cast<uint4*>(front_smem + 2 * wchunks);   // [16][nchunk]
+  {
+    const uint4* w4 = reinterpret_cast<const uint4*>(w);
+    const uint4* x4 = reinterpret_cast<const uint4*>(x) + static_cast<int64_t>(rank) * kFrontTokCta * nchunk;
+    const int valid_rows = max(0, min(kFrontTokCta, n_tokens - rank * kFrontTokCta));
+    const int xchunks = valid_rows * nchunk;
+    constexpr int kBatch = 4;
+#pragma unroll 1
+    for (int i0 = threadIdx.x; i0 < xchunks; i0 += kBatch * blockDim.x) {
+      uint4 u[kBatch];
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) {
+        const int i = i0 + b * blockDim.x;
+        u[b] = i < xchunks ? __ldg(x4 + i) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) {
+        const int i = i0 + b * blockDim.x;
+        if (i < xchunks) x_s[i] = u[b];
+      }
+    }
+#pragma unroll 1
+    for (int i0 = threadIdx.x; i0 < wchunks; i0 += kBatch * blockDim.x) {
+      uint4 u[kBatch];
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) {
+        const int i = i0 + b * blockDim.x;
+        u[b] = i < wchunks ? __ldg(w4 + i) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) {
+        const int i = i0 + b * blockDim.x;
+        if (i < wchunks) {
+          float f[8];
+          unpack8<T>(u[b], f);
+          w_s[i] = make_float4(f[0], f[1], f[2], f[3]);
+          w_s[wchunks + i] = make_float4(f[4], f[5], f[6], f[7]);
+        }
+      }
+    }
+  }
+  __syncthreads();
+  const int ltok0 = warp * kFrontTokWarp;  // local token index
+  const bool live[kFrontTokWarp] = {rank * kFrontTokCta + ltok0 < n_tokens, rank * kFrontTokCta + ltok0 + 1 < n_tokens};
+  float acc[kFrontTokWarp][kMaxExperts];
+#pragma unroll
+  for (int t = 0; t < kFrontTokWarp; ++t)
+#pragma unroll
+    for (int e = 0; e < kMaxExperts; ++e) acc[t][e] = 0.f;
+#pragma unroll 1
+  for (int c = lane; c < nchunk; c += 32) {
+    float xf[kFrontTokWarp][8];
+#pragma unroll
+    for (int t = 0; t < kFrontTokWarp; ++t)
+      unpack8<T>(live[t] ? x_s[(ltok0 + t) * nchunk + c] : make_uint4(0, 0, 0, 0), xf[t]);
+#pragma unroll
+    for (int e = 0; e < kMaxExperts; ++e) {
+      if (e < E) {
+        const float4 lo = w_s[e * nchunk + c], hi = w_s[wchunks + e * nchunk + c];
+        const float wf[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+#pragma unroll
+        for (int t = 0; t < kFrontTokWarp; ++t)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[t][e] = fmaf(xf[t][i], wf[i], acc[t][e]);
+      }
+    }
+  }
+  // Transpose-reduce (as the SIMT router): after the xor-16/8/4/2 steps lane l
+  // holds a partial sum of expert 8*b4 + 4*b3 + 2*b2 + b1 (b = bits of l).
+#pragma unroll
+  for (int t = 0; t < kFrontTokWarp; ++t) {
+    float v8[8], v4[4], v2[2];
+    const bool u16 = lane & 16, u8 = lane & 8, u4 = lane & 4, u2 = lane & 2;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float send = u16 ? acc[t][i] : acc[t][i + 8];
+      const float keep = u16 ? acc[t][i + 8] : acc[t][i];
+      v8[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float send = u8 ? v8[i] : v8[i + 4];
+      const float keep = u8 ? v8[i + 4] : v8[i];
+      v4[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float send = u4 ? v4[i] : v4[i + 2];
+      const float keep = u4 ? v4[i + 2] : v4[i];
+      v2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+    float v1;
+    {
+      const float send = u2 ? v2[0] : v2[1];
+      const float keep = u2 ? v2[1] : v2[0];
+      v1 = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+    }
+    const float sum = v1 + __shfl_xor_sync(0xffffffffu, v1, 1);
+    const int e = ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
+    if ((lane & 1) == 0) logit_s[ltok0 + t][e] = round_to<T>(sum);
+  }
+  __syncwarp();
+
+  // 2. Selection: lanes 0 and 1 of each warp take its two tokens.
+  int sel[S];
+#pragma unroll
+  for (int r = 0; r < S; ++r) sel[r] = -1;
+  const int my_ltok = ltok0 + (lane & 1);
+  const int64_t my_tok = static_cast<int64_t>(rank) * kFrontTokCta + my_ltok;
+  const bool my_valid = lane < kFrontTokWarp && my_tok < n_tokens;
+  if (my_valid) {
+    float lg[kMaxExperts];
+#pragma unroll
+    for (int e = 0; e < kMaxExperts; ++e) lg[e] = (e < E) ? logit_s[my_ltok][e] : 0.f;
+    if (logits_out) {
+#pragma unroll
+      for (int e = 0; e < kMaxExperts; ++e)
+        if (e < E) logits_out[my_tok * E + e] = lg[e];
+    }
+    float gate[S];
+    select_route<KC>(lg, E, k, tie_low_first != 0, sel, gate);
+#pragma unroll
+    for (int r = 0; r < S; ++r) {
+      if (r < k) {
+        const int e = sel[r];
+        if (e < 0 || e >= E) {
+          raise_error(err, kErrBadExpert);
+          sel[r] = -1;
+        } else {
+          idx_out[my_tok * k + r] = e;
+          gates_out[my_tok * k + r] = Traits<T>::from_f(gate[r]);
+        }
+      }
+    }
+  }
+#pragma unroll 1
+  for (int e = 0; e < E; ++e) {
+    bool hit = false;
+#pragma unroll
+    for (int r = 0; r < S; ++r) hit |= (r < k && sel[r] == e);
+    const uint32_t m = __ballot_sync(0xffffffffu, hit) & 3u;
+    if (lane == 0) pm_s[warp][e] = m;
+  }
+  __syncthreads();
+  if (threadIdx.x < E) {
+    uint32_t m = 0;
+#pragma unroll
+    for (int q = 0; q < kFrontWarps; ++q) m |= pm_s[q][threadIdx.x] << (kFrontTokWarp * q);
+    mask_s[threadIdx.x] = m;
+    cnt_s[threadIdx.x] = __popc(m);
+  }
+  cluster_sync();  // every CTA's cnt_s is written
+
+  // 3. Plan of the block: totals over the cluster, this CTA's offsets, padded segment starts.
+  if (warp == 0) {
+    int tot = 0, pre = 0;
+    if (lane < E) {
+      const uint32_t a = smem_u32(&cnt_s[lane]);
+      for (int q = 0; q < kFrontCtas; ++q) {
+        const int v = ld_shared_cluster_s32(cluster_map(a, q));
+        tot += v;
+        if (q < rank) pre += v;
+      }
+    }
+    const int padded = lane < E ? (tot + o.seg_align - 1) / o.seg_align * o.seg_align : 0;
+    int incl = padded;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += v;
+    }
+    if (lane < E) {
+      tot_s[lane] = tot;
+      pre_s[lane] = pre;
+      seg_s[lane] = incl - padded;
+    }
+    const int total = __shfl_sync(0xffffffffu, incl, 31);
+    if (lane == 0) {
+      seg_s[E] = total;
+      if (rank == 0 && (total > o.max_rows || total / AGM_TILE_M > o.max_tiles)) raise_error(err, kErrRowOverflow);
+    }
+  }
+  __syncthreads();
+  const int total_rows = static_cast<int>(min(static_cast<int64_t>(seg_s[E]), o.max_rows));
+  const int ntiles = total_rows / AGM_TILE_M;
+  if (rank == 0) {
+    if (threadIdx.x < E) {
+      o.block_hist[threadIdx.x] = tot_s[threadIdx.x];
+      o.block_off[threadIdx.x] = 0;
+      o.counts[threadIdx.x] = tot_s[threadIdx.x];
+    }
+    if (threadIdx.x <= E) o.seg_start[threadIdx.x] = seg_s[threadIdx.x];
+    if (threadIdx.x == 0) *o.num_tiles = ntiles;
+    for (int m = threadIdx.x; m < ntiles; m += blockDim.x) {
+      const int row = m * AGM_TILE_M;
+      int e = 0;
+      while (e + 1 < E && seg_s[e + 1] <= row) ++e;
+      o.tile_expert[m] = e;
+    }
+  }
+  // Padding rows of x_perm are zeroed when the GEMMs read them (row tiles),
+  // spread over the cluster's threads. token_of keeps the source token of
+  // every valid row; its padding entries are not written (nothing reads them).
+  if (o.zero_pad) {
+    const int gt = rank * blockDim.x + threadIdx.x, gn = kFrontCtas * blockDim.x;
+    uint4* xp = static_cast<uint4*>(o.x_perm);
+#pragma unroll 1
+    for (int e = 0; e < E; ++e) {
+      const int p0 = seg_s[e] + tot_s[e], p1 = min(seg_s[e + 1], total_rows);
+      const int64_t q1 = static_cast<int64_t>(max(p1 - p0, 0)) * nchunk;
+      for (int64_t q = gt; q < q1; q += gn)
+        xp[(p0 + q / nchunk) * static_cast<int64_t>(nchunk) + q % nchunk] = make_uint4(0, 0, 0, 0);
+    }
+  }
+
+  // 4. Destination rows of lanes 0-1's tokens, then 5. the warp copies both tokens' rows.
+  int dest[S];
+#pragma unroll
+  for (int r = 0; r < S; ++r) dest[r] = -1;
+  if (my_valid) {
+    const uint32_t lt_mask = (1u << my_ltok) - 1u;
+#pragma unroll
+    for (int r = 0; r < S; ++r) {
+      const int e = sel[r];
+      if (r < k && e >= 0 && e < E) {
+        const int64_t row = static_cast<int64_t>(seg_s[e]) + pre_s[e] + __popc(mask_s[e] & lt_mask);
+        if (row < o.max_rows) {
+          dest[r] = static_cast<int>(row);
+          o.row_of[my_tok * k + r] = static_cast<int32_t>(row);
+          o.token_of[row] = static_cast<int32_t>(my_tok);
+        } else {
+          raise_error(err, kErrRowOverflow);
+        }
+      }
+    }
+  }
+  uint4* xp = static_cast<uint4*>(o.x_perm);
+#pragma unroll
+  for (int t = 0; t < kFrontTokWarp; ++t) {
+#pragma unroll
+    for (int r = 0; r < S; ++r) {
+      const int row = __shfl_sync(0xffffffffu, dest[r], t);
+      if (r < k && row >= 0) {
+        uint4* dst = xp + static_cast<int64_t>(row) * nchunk;
+        const uint4* src = x_s + (ltok0 + t) * nchunk;
+#pragma unroll 4
+        for (int c = lane; c < nchunk; c += 32) dst[c] = src[c];
+      }
+    }
+  }
+  cluster_sync();  // no CTA leaves while another may still read its cnt_s
+}
+
+bool decode_front_supported(int dtype, int64_t n_tokens, int d, int E, int k) {
+  return (dtype == AGM_BF16 || dtype == AGM_F16) && n_tokens > 0 && n_tokens <= kDispatchBlock && d > 0 &&
+         d % 8 == 0 && d / 8 <= 32 * kFrontChunks && E >= 1 && E <= kMaxExperts && k >= 1 && k <= E;
+}
+
+template <typename T>
+static cudaError_t launch_front(const void* x, const void* w, int64_t n_tokens, int d, int E, int k, int tie_low_first,
+                                float* logits_out, int32_t* idx, void* gates, const FrontOut& o, int* err,
+                                cudaStream_t stream) {
+  const dim3 grid(kFrontCtas), block(32 * kFrontWarps);
+  const int n = static_cast<int>(n_tokens);
+  // the router weight in fp32 and the CTA's 16 token rows
+  const int smem = E * d * static_cast<int>(sizeof(float)) + kFrontTokCta * d * 2;
+  cudaError_t e = cudaSuccess;
+  switch (k) {
+    case 1: e = ensure_dynamic_smem(reinterpret_cast<const void*>(decode_front_kernel<T, 1>), smem); break;
+    case 2: e = ensure_dynamic_smem(reinterpret_cast<const void*>(decode_front_kernel<T, 2>), smem); break;
+    case 3: e = ensure_dynamic_smem(reinterpret_cast<const void*>(decode_front_kernel<T, 3>), smem); break;
+    case 4: e = ensure_dynamic_smem(reinterpret_cast<const void*>(decode_front_kernel<T, 4>), smem); break;
+    default: e = ensure_dynamic_smem(reinterpret_cast<const void*>(decode_front_kernel<T, 0>), smem); break;
+  }
+  if (e != cudaSuccess) return e;
+  T* g = static_cast<T*>(gates);
+  const T* xs = static_cast<const T*>(x);
+  const T* ws = static_cast<const T*>(w);
+  switch (k) {
+    case 1: return launch_cluster_kernel(decode_front_kernel<T, 1>, grid, block, kFrontCtas, smem, stream, xs, ws, n, d, E, k,
+                                         tie_low_first, logits_out, idx, g, o, err);
+    case 2: return launch_cluster_kernel(decode_front_kernel<T, 2>, grid, block, kFrontCtas, smem, stream, xs, ws, n, d, E, k,
+                                         tie_low_first, logits_out, idx, g, o, err);
+    case 3: return launch_cluster_kernel(decode_front_kernel<T, 3>, grid, block, kFrontCtas, smem, stream, xs, ws, n, d, E, k,
+                                         tie_low_first, logits_out, idx, g, o, err);
+    case 4: return launch_cluster_kernel(decode_front_kernel<T, 4>, grid, block, kFrontCtas, smem, stream, xs, ws, n, d, E, k,
+                                         tie_low_first, logits_out, idx, g, o, err);
+    default: return launch_cluster_kernel(decode_front_kernel<T, 0>, grid, block, kFrontCtas, smem, stream, xs, ws, n, d, E,
+                                          k, tie_low_first, logits_out, idx, g, o, err);
+  }
+}
+
+cudaError_t decode_front(int dtype, const void* x, const void* w, int64_t n_tokens, int d, int E, int k,
+                         int tie_low_first, float* logits_out, int32_t* idx, void* gates, const FrontOut& o, int* err,
+                         cudaStream_t stream) {
+  if (!decode_front_supported(dtype, n_tokens, d, E, k)) return cudaErrorInvalidValue;
+  if (o.seg_align != AGM_TILE_M && o.seg_align != 2 * AGM_TILE_M) return cudaErrorInvalidValue;
+  if (dtype == AGM_BF16)
+    return launch_front<__nv_bfloat16>(x, w, n_tokens, d, E, k, tie_low_first, logits_out, idx, gates, o, err, stream);
+  return launch_front<__half>(x, w, n_tokens, d, E, k, tie_low_first, logits_out, idx, gates, o, err, stream);
+}
+
 size_t router_smem_bytes(int d, int E) {
   return static_cast<size_t>(E) * d * sizeof(float) + static_cast<size_t>(kRouterWarps) * 32 * kMaxExperts * 4;
 }

@@ -263,7 +263,7 @@ def moe_forward(x: torch.Tensor, w_router: torch.Tensor, w1: torch.Tensor, b1: t
                 want: tuple = (), tie_low_first: bool = False, workspace: Optional[torch.Tensor] = None,
                 check_errors: bool = False, stage_events=None, logits_in: Optional[torch.Tensor] = None,
                 pair: bool = True, swap: bool = True, pdl: bool = True, fold: bool = True,
-                decode_tiles: bool = False):
+                decode_tiles: bool = False, front: bool = True):
     """Fused forward: x [N, d] -> out [N, d]. ``want`` may hold 'idx', 'gates', 'counts', 'logits'.
 
     Weights: w_router [E, d]; w1 [E, H, d]; b1 [E, H]; w2 [E, d, H]; b2 [E, d];
@@ -280,7 +280,10 @@ def moe_forward(x: torch.Tensor, w_router: torch.Tensor, w1: torch.Tensor, b1: t
     on CTA pairs, run the shared experts inside the routed FC1/FC2 launches
     (False: their own launches; the result is the same bit for bit).
     ``decode_tiles``: w1 and w2 are in the decode tile layout
-    (:func:`decode_tile_layout`); decode-sized batches only.
+    (:func:`decode_tile_layout`); decode-sized batches only. ``front``: let
+    batches of at most 128 tokens run router, dispatch plan and permute as
+    one cluster kernel (False: three kernels; the logits then come from the
+    tensor-core router, whose fp32 summation order differs).
     Returns out, or (out, extras dict) when ``want`` is not empty.
     """
     lib = load()
@@ -316,7 +319,7 @@ def moe_forward(x: torch.Tensor, w_router: torch.Tensor, w1: torch.Tensor, b1: t
         max(Hs, 1), ptr(ws1), ptr(sb1), ptr(ws2), ptr(sb2), ptr(out), ptr(workspace), workspace.numel(),
         _flags(tie_low_first) | (0 if pair else _lib.AGM_FLAG_NO_PAIR) | (0 if swap else _lib.AGM_FLAG_NO_SWAP)
         | (0 if pdl else _lib.AGM_FLAG_NO_PDL) | (0 if fold else _lib.AGM_FLAG_NO_FOLD)
-        | (_lib.AGM_FLAG_DECODE_TILES if decode_tiles else 0),
+        | (_lib.AGM_FLAG_DECODE_TILES if decode_tiles else 0) | (0 if front else _lib.AGM_FLAG_NO_FRONT),
         ptr(extras.get("idx")), ptr(extras.get("gates")), ptr(extras.get("counts")),
         ptr(extras.get("logits")), ptr(logits_in), None if ev_arr is None else ctypes.addressof(ev_arr),
         stream_handle(dev))

@@ -87,6 +87,10 @@ enum {
                                       128 x 64 weight tile one contiguous 16 KB block; only for
                                       decode-sized batches (top_k * n_tokens <= 32 * n_experts,
                                       16-bit dtypes, d and hidden multiples of 128) */
+#define AGM_FLAG_NO_FRONT 0x100    /* agm_moe_forward: router, dispatch plan and permute as three
+                                      kernels even for n_tokens <= 128 (default there: one cluster
+                                      kernel of 8 CTAs doing all three; 16-bit dtypes, d <= 2048,
+                                      logits computed by the library) */
 
 AGM_API const char* agm_last_error(void);
 AGM_API int agm_abi_version(void);
