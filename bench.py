@@ -365,6 +365,7 @@ def run_ours(args, world, rank, local):
         for j, s in enumerate(STAGES):
             stage_ms[s] += e[j].elapsed_time(e[j + 1])
     stage_ms = {s: v / n_ev for s, v in stage_ms.items()}
+    alone = stages_alone(x, wr) if rank == 0 else None
     clocks = clk.summary()
     value = N * world * args.steps / (ms_total / 1000.0)
     parity = None if args.skip_parity else parity_check(x, wr, w1, b1, w2, b2, out)
@@ -394,7 +395,7 @@ def run_ours(args, world, rank, local):
     skewed = None if args.skip_skewed else run_skewed_single(args, dev, stream)
     block_ffn = None if args.skip_block else run_block_ffn(args, dev, stream, x, (w1, b1, w2, b2, wr))
     report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e_value, x, decode, train, codec_leg,
-           parity=parity, skewed=skewed, block_ffn=block_ffn)
+           parity=parity, skewed=skewed, block_ffn=block_ffn, alone=alone)
 
 
 def run_block_ffn(args, dev, stream, x, weights):
@@ -1303,8 +1304,56 @@ def gemm_kernel_name(n_tokens):
     return "grouped_gemm_tc_kernel (FC1+FC2, tcgen05, one CTA per tile)"
 
 
+def stages_alone(x, wr, reps=20):
+    """Each memory-bound stage kernel launched `reps` times back to back
+    through its own C-ABI entry point (router: agm_router_topk; permute:
+    agm_permute; combine: agm_combine) on preallocated outputs, CUDA events
+    around the loop on the launching stream: the kernel's own duration plus
+    the gap between two launches. The per-stage pass of the forward puts an
+    event between kernels, so each of its stage times also holds a launch
+    latency and the kernel's prologue, which the forward itself hides by
+    letting each kernel start while the previous one finishes."""
+    from agillm41_b200 import _lib, ops
+
+    lib = ops.load()
+    dev = x.device
+    n, d = x.shape
+    st = torch.cuda.current_stream(dev).cuda_stream
+    idx, gates, hist, _ = ops.router_topk(x, wr, TOP_K)
+    plan = ops.dispatch_plan(hist, n, TOP_K)
+    x_perm, row_of = ops.permute(x, idx, plan, EXPERTS)
+    out = torch.empty_like(x)
+    bf16 = _lib.AGM_BF16
+    P = _lib.ptr
+
+    def router():
+        return lib.agm_router_topk(P(x), P(wr), bf16, n, d, EXPERTS, TOP_K, 0, None, None, P(idx), P(gates),
+                                   P(hist), None, st)
+
+    def permute():
+        return lib.agm_permute(P(x), bf16, n, d, EXPERTS, TOP_K, P(idx), P(plan["block_off"]), P(plan["seg_start"]),
+                               P(plan["counts"]), P(x_perm), P(row_of), P(plan["token_of"]), None, st)
+
+    def combine():
+        return lib.agm_combine(P(x_perm), P(row_of), P(gates), bf16, n, d, TOP_K, None, 0, 0, P(out), st)
+
+    res = {}
+    for name, fn in (("router", router), ("permute", permute), ("combine", combine)):
+        for _ in range(3):
+            assert fn() == 0, name
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        res[name] = e0.elapsed_time(e1) / reps
+    return res
+
+
 def report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e, x, decode=None, train=None, codec=None,
-           parity=None, skewed=None, block_ffn=None):
+           parity=None, skewed=None, block_ffn=None, alone=None):
     if rank != 0:
         return
     peaks = load_peaks()
@@ -1314,10 +1363,17 @@ def report(args, world, rank, N, ms_total, stage_ms, clocks, value, e2e, x, deco
     traffic_rec = load_traffic()
     traffic = traffic_rec.get("grouped_gemm_fc1_fc2_avg_bytes_per_launch")
 
+    alone = alone or {}
+
     def hbm(stage, per_tok):
         gbs = per_tok * N / (stage_ms[stage] / 1000.0) / 1e9
-        return {"ms": round(stage_ms[stage], 4), "achieved_gbs": round(gbs, 1), "frac": round(gbs / peaks["hbm"], 3),
-                "algorithmic_bytes": per_tok * N}
+        rec = {"ms": round(stage_ms[stage], 4), "achieved_gbs": round(gbs, 1), "frac": round(gbs / peaks["hbm"], 3),
+               "algorithmic_bytes": per_tok * N}
+        if stage in alone:
+            g2 = per_tok * N / (alone[stage] / 1000.0) / 1e9
+            rec["alone"] = {"ms": round(alone[stage], 4), "achieved_gbs": round(g2, 1),
+                            "frac": round(g2 / peaks["hbm"], 3)}
+        return rec
 
     cpu = None
     if world == 1 and not args.skip_cpu:
