@@ -589,6 +589,10 @@ AGM_API int agm_ep_dispatch(const void* x, int dtype, int64_t n_tokens, int d, i
   if ((e = mark(0)) != cudaSuccess) return ep_cuda(e, "event");
   e = cudaMemsetAsync(L.counts, 0, sizeof(int32_t) * n_experts, stream);
   if (e != cudaSuccess) return ep_cuda(e, "memset");
+  // Router, plan and permute may each start while the previous kernel
+  // finishes (each waits before reading its inputs); the flag kernels are
+  // plain launches, ordered after everything before them.
+  agm::PdlScope pdl(!(flags & AGM_FLAG_NO_PDL));
   if (n_tokens > 0) {
     e = agm::router_topk(dtype, x, w_router, n_tokens, d, n_experts, top_k, flags & AGM_FLAG_TIE_LOW_FIRST, nullptr,
                          nullptr, L.idx, L.gates, L.block_hist, L.err, sms, stream);
@@ -667,6 +671,11 @@ AGM_API int agm_ep_expert(int dtype, int64_t n_tokens, int d, int n_experts, int
   g1.tile_src = L.recv_tile_src;
   g1.src_signal = reinterpret_cast<const uint64_t*>(peer_comm[rank]);
   g1.src_epoch = epoch + 1;
+  // The tables come from the plan, three launches back, and the weights from
+  // before the forward: FC1 streams its first weight tiles while the kernel
+  // before it finishes, and FC2 while FC1 finishes.
+  g1.early_weights = true;
+  agm::PdlScope pdl(true);
   e = agm::grouped_gemm(dtype, recv, cap_rows, w1, g1, true, sms, stream, AGM_GEMM_PAIR);
   if (e != cudaSuccess) return ep_cuda(e, "grouped_gemm fc1");
   if ((e = mark(0)) != cudaSuccess) return ep_cuda(e, "event");
@@ -678,6 +687,7 @@ AGM_API int agm_ep_expert(int dtype, int64_t n_tokens, int d, int n_experts, int
   g2.k = hidden;
   g2.tile_dst = L.recv_tile_dst;
   g2.tile_src = nullptr;  // h is this rank's own
+  g2.early_weights = true;
   e = agm::grouped_gemm(dtype, L.h, cap_rows, w2, g2, false, sms, stream, AGM_GEMM_PAIR);
   if (e != cudaSuccess) return ep_cuda(e, "grouped_gemm fc2");
   if ((e = mark(1)) != cudaSuccess) return ep_cuda(e, "event");
