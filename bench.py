@@ -53,6 +53,7 @@ PERMUTE_BYTES = 2 * D + 4 * TOP_K + 2 * D * TOP_K + 4 * TOP_K + 4 * TOP_K  # x, 
 COMBINE_BYTES = 2 * D * TOP_K + 4 * TOP_K + 2 * TOP_K + 2 * D             # k rows, row_of, gates -> out row
 STAGES = ["router", "plan", "permute", "fc1", "fc2", "shared", "combine"]
 KERNELS_PER_STEP = 6   # router, plan, permute, fc1, fc2, combine
+DECODE_KERNELS_PER_LAYER = 4   # at most 128 tokens: decode front (router + plan + permute), fc1, fc2, combine
 TILE_ROWS = 128
 # Multi-GPU workload: each rank holds B x L tokens; router logits carry a
 # per-expert bias log(p_e) * ZIPF_SCALE with p Zipf(1.2) over a seeded
@@ -1291,7 +1292,8 @@ def run_decode(args, dev, stream):
             "steps": steps, "active_experts": active, "weight_bytes_per_step": wbytes,
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm"], "unit": "GB/s",
                          "frac": round(gbs / peaks["hbm"], 3), "peak_source": f"{peaks['src']} HBM copy"},
-            "gpu_launches_per_step": KERNELS_PER_STEP * DECODE_LAYERS + 2,
+            # per layer: the decode front (router + plan + permute in one cluster launch), FC1, FC2, combine
+            "gpu_launches_per_step": DECODE_KERNELS_PER_LAYER * DECODE_LAYERS,
             "residual": "perturbation added inside each layer's combine kernel (agm_moe_forward_residual)"}
 
 
