@@ -73,7 +73,8 @@ def run_case(ref, case, outdir):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference/agillm41.py")
+    ap.add_argument("--ref", default=os.environ.get("AGILLM41_REFERENCE", "/root/reference/agillm41.py"),
+                    help="the reference's agillm41.py (default: $AGILLM41_REFERENCE, else /root/reference/agillm41.py)")
     ap.add_argument("--only", default="")
     args = ap.parse_args()
     ref = load_reference(args.ref)
