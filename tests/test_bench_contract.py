@@ -1,0 +1,52 @@
+"""bench.py's reference arm on the host: one JSON line with the contract's keys
+(the metric of the benchmark definition, a CPU baseline describing the run, an
+e2e object with no host<->device bytes), and silence on ranks other than 0
+under a launcher. The reference arm times the oracle on the host cores, so
+this runs without a GPU."""
+import json
+import os
+import subprocess
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _run(extra_env=None):
+    env = dict(os.environ)
+    env.pop("RANK", None)
+    env.pop("WORLD_SIZE", None)
+    env.update(extra_env or {})
+    env["CUDA_VISIBLE_DEVICES"] = ""
+    return subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "2",
+                           "--warmup", "1", "--skip-reference-gpu"], cwd=ROOT, env=env, capture_output=True,
+                          text=True, timeout=600)
+
+
+def test_reference_arm_prints_one_contract_line():
+    p = _run()
+    assert p.returncode == 0, p.stderr[-2000:]
+    lines = [json.loads(l) for l in p.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1
+    line = lines[0]
+    with open(os.path.join(ROOT, "BASELINE.json")) as f:
+        metric = json.load(f)["metric"]
+    assert line["impl"] == "reference"
+    assert line["metric"] == metric
+    assert line["unit"] == "tokens/s" and line["higher_is_better"] is True
+    assert line["steps"] == 2 and line["warmup"] == 1 and line["n_gpus"] == 1
+    assert line["value"] > 0 and line["ms_per_step"] > 0
+    cb = line["cpu_baseline"]
+    assert cb["kind"] in ("port", "reference") and cb["cores"] >= 1 and cb["value"] == line["value"]
+    assert "tokens" in cb["sample"]
+    e2e = line["e2e"]
+    assert e2e["value"] == line["value"] and e2e["unit"] == line["unit"]
+    assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
+    cfg = line["config"]
+    assert cfg["tokens_per_gpu"] == 73728 and cfg["experts"] == 14 and cfg["top_k"] == 2
+    assert "sample" in cfg
+
+
+def test_reference_arm_other_ranks_exit_quietly():
+    p = _run({"RANK": "1", "WORLD_SIZE": "2"})
+    assert p.returncode == 0, p.stderr[-2000:]
+    assert not [l for l in p.stdout.splitlines() if l.startswith("{")]
