@@ -1,5 +1,5 @@
 """bench.py's reference arm on the host: one JSON line with the contract's keys
-(the metric of the benchmark definition, a CPU baseline describing the run, an
+(the same metric as the repository's own arm, a CPU baseline describing the run, an
 e2e object with no host<->device bytes), and silence on ranks other than 0
 under a launcher. The reference arm times the oracle on the host cores, so
 this runs without a GPU."""
@@ -28,10 +28,11 @@ def test_reference_arm_prints_one_contract_line():
     lines = [json.loads(l) for l in p.stdout.splitlines() if l.startswith("{")]
     assert len(lines) == 1
     line = lines[0]
-    with open(os.path.join(ROOT, "BASELINE.json")) as f:
-        metric = json.load(f)["metric"]
+    sys.path.insert(0, ROOT)
+    import bench
+
     assert line["impl"] == "reference"
-    assert line["metric"] == metric
+    assert line["metric"] == bench.METRIC  # the same metric as the repository's own arm
     assert line["unit"] == "tokens/s" and line["higher_is_better"] is True
     assert line["steps"] == 2 and line["warmup"] == 1 and line["n_gpus"] == 1
     assert line["value"] > 0 and line["ms_per_step"] > 0
