@@ -128,14 +128,20 @@ def test_update_reaches_the_moe_forward():
     assert torch.equal(y1, y2)
 
 
-def test_batch_matches_single_tensor_calls():
+@pytest.mark.parametrize("mode", ["lerp", "copy"])
+def test_batch_matches_single_tensor_calls(mode):
     """agm_codec_decode_batch (the path of decode/apply_tensor_state) against
     one agm_codec_decode call per tensor: 23 tensors of mixed pack kinds and
     target dtypes, 18 of one kind (two launches), rows of 8 elements (not
-    batchable), an unaligned target view (t5); bit for bit, in lerp mode."""
+    batchable), an unaligned target view (t5); bit for bit, in lerp and copy
+    mode. In copy mode a warp whose 32 groups lie in one tensor stores through
+    shared memory and a warp that straddles two tensors stores directly; the
+    1000 + i element tensors give both kinds of warp."""
     import ctypes
 
     from agillm41_b200 import _lib
+
+    apply_mode, alpha = {"lerp": (_lib.AGM_APPLY_LERP, 0.4), "copy": (_lib.AGM_APPLY_COPY, 1.0)}[mode]
 
     g = torch.Generator().manual_seed(96)
     specs = [(f"t{i}", "int8_symmetric", (1000 + i,), torch.float32) for i in range(18)]  # two launches of a kind
@@ -157,11 +163,11 @@ def test_batch_matches_single_tensor_calls():
         keep += [q, s]
         e = p.entry(q, s, single[p.key])
         rc = lib.agm_codec_decode(e.payload, e.kind, e.packed_dtype, e.n, e.cols, e.scale, e.row_scales,
-                                  e.scales_dtype, e.target, e.target_dtype, _lib.AGM_APPLY_LERP, 0.4, stream)
+                                  e.scales_dtype, e.target, e.target_dtype, apply_mode, alpha, stream)
         _lib.check(rc, "agm_codec_decode")
         rows.append(p.entry(q, s, view[p.key]))
     table = (_lib.AgmCodecTensor * len(rows))(*rows)
-    _lib.check(lib.agm_codec_decode_batch(ctypes.cast(table, ctypes.c_void_p), len(rows), _lib.AGM_APPLY_LERP, 0.4,
+    _lib.check(lib.agm_codec_decode_batch(ctypes.cast(table, ctypes.c_void_p), len(rows), apply_mode, alpha,
                                           stream), "agm_codec_decode_batch")
     torch.cuda.synchronize()
     for k in view:
